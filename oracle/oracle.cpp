@@ -1,0 +1,753 @@
+// oracle.cpp -- CPU restatement of Opure-VoxelEngine's decode path.
+//
+// TEST INFRASTRUCTURE ONLY: the parity checker for the CUDA path (see oracle.h for
+// who may load it and how it is pinned). Scalar, double accumulation, no SIMD
+// reordering of any sum, exactly as src/engine/Opure_CpuReference.cpp computes.
+#include "oracle.h"
+
+#include <cmath>
+#include <condition_variable>
+#include <functional>
+#include <mutex>
+#include <thread>
+#include <cstdlib>
+#include <cstring>
+#include <limits>
+#include <vector>
+
+namespace {
+
+// ---------------------------------------------------------------------------
+// fp16 <-> fp32 from the IEEE 754 binary16 definition.
+float f16_to_f32(uint16_t h) {
+    // Same case split as Opure_Streamer.cpp:49-84 (zero, subnormal, inf/NaN, normal),
+    // except the subnormal exponent: that file writes 127-15-e (:66), which halves
+    // every fp16 subnormal; the IEEE value needs 127-15-e+1 after e normalising shifts.
+    const uint32_t sign = uint32_t(h & 0x8000u) << 16;
+    const uint32_t exp = (h >> 10) & 0x1Fu;
+    uint32_t man = h & 0x3FFu;
+    uint32_t bits;
+    if (exp == 0) {
+        if (man == 0) {
+            bits = sign;
+        } else {
+            uint32_t e = 0;
+            while ((man & 0x400u) == 0) { man <<= 1; ++e; }
+            man &= 0x3FFu;
+            bits = sign | ((127u - 15u + 1u - e) << 23) | (man << 13);
+        }
+    } else if (exp == 0x1F) {
+        bits = sign | 0x7F800000u | (man << 13);
+    } else {
+        bits = sign | ((exp + 112u) << 23) | (man << 13);
+    }
+    float f;
+    std::memcpy(&f, &bits, 4);
+    return f;
+}
+
+uint16_t f32_to_f16(float f) {
+    uint32_t x;
+    std::memcpy(&x, &f, 4);
+    const uint32_t sign = (x >> 16) & 0x8000u;
+    const uint32_t exp = (x >> 23) & 0xFFu;
+    const uint32_t man = x & 0x7FFFFFu;
+    if (exp == 0xFF) return uint16_t(sign | (man ? 0x7E00u : 0x7C00u));
+    const int e = int(exp) - 112;  // rebias 127 -> 15
+    if (e >= 31) return uint16_t(sign | 0x7C00u);
+    if (e <= 0) {
+        // Result is subnormal (or zero): value = M * 2^(exp-150), unit 2^-24.
+        const int s = 14 - e;                 // bits to drop from the 24-bit significand
+        if (s > 24) return uint16_t(sign);
+        const uint32_t M = man | 0x800000u;
+        uint32_t q = M >> s;
+        const uint32_t rem = M & ((1u << s) - 1u);
+        const uint32_t half = 1u << (s - 1);
+        if (rem > half || (rem == half && (q & 1u))) ++q;
+        return uint16_t(sign | q);
+    }
+    uint32_t q = (uint32_t(e) << 10) | (man >> 13);
+    const uint32_t rem = man & 0x1FFFu;
+    if (rem > 0x1000u || (rem == 0x1000u && (q & 1u))) ++q;  // carry may reach inf: correct
+    return uint16_t(sign | q);
+}
+
+struct F16Lut {
+    float v[65536];
+    F16Lut() { for (uint32_t i = 0; i < 65536; ++i) v[i] = f16_to_f32(uint16_t(i)); }
+};
+const F16Lut &lut() {
+    static const F16Lut t;
+    return t;
+}
+
+float bf16_to_f32(uint16_t h) {
+    const uint32_t bits = uint32_t(h) << 16;
+    float f;
+    std::memcpy(&f, &bits, 4);
+    return f;
+}
+
+int g_threads = 1;
+
+// Persistent worker pool: run(n, fn) calls fn(i) for i in [0, n), split into
+// contiguous static chunks. Each index is computed by exactly one thread with the
+// same arithmetic as a serial loop, so results do not depend on the thread count.
+class Pool {
+public:
+    ~Pool() { resize(0); }
+    void resize(int n) {
+        {
+            std::unique_lock<std::mutex> lk(mu_);
+            stop_ = true;
+            ++gen_;
+        }
+        cv_.notify_all();
+        for (auto &t : workers_) t.join();
+        workers_.clear();
+        stop_ = false;
+        for (int i = 0; i < n; ++i) workers_.emplace_back([this, i] { loop(i); });
+    }
+    int size() const { return int(workers_.size()); }
+    void run(int64_t n, const std::function<void(int64_t)> &fn) {
+        const int nt = size() + 1;
+        if (nt == 1 || n < 2) {
+            for (int64_t i = 0; i < n; ++i) fn(i);
+            return;
+        }
+        {
+            std::unique_lock<std::mutex> lk(mu_);
+            fn_ = &fn;
+            n_ = n;
+            pending_ = size();
+            ++gen_;
+        }
+        cv_.notify_all();
+        chunk(0, nt, fn);
+        std::unique_lock<std::mutex> lk(mu_);
+        done_.wait(lk, [this] { return pending_ == 0; });
+        fn_ = nullptr;
+    }
+
+private:
+    void chunk(int who, int nt, const std::function<void(int64_t)> &fn) {
+        const int64_t b = n_ * who / nt, e = n_ * (who + 1) / nt;
+        for (int64_t i = b; i < e; ++i) fn(i);
+    }
+    void loop(int i) {
+        uint64_t seen;
+        {
+            std::unique_lock<std::mutex> lk(mu_);
+            seen = gen_;
+        }
+        for (;;) {
+            const std::function<void(int64_t)> *fn;
+            {
+                std::unique_lock<std::mutex> lk(mu_);
+                cv_.wait(lk, [&] { return gen_ != seen; });
+                seen = gen_;
+                if (stop_) return;
+                fn = fn_;
+            }
+            chunk(i + 1, size() + 1, *fn);
+            std::unique_lock<std::mutex> lk(mu_);
+            if (--pending_ == 0) done_.notify_one();
+        }
+    }
+    std::vector<std::thread> workers_;
+    std::mutex mu_;
+    std::condition_variable cv_, done_;
+    const std::function<void(int64_t)> *fn_ = nullptr;
+    int64_t n_ = 0;
+    int pending_ = 0;
+    uint64_t gen_ = 0;
+    bool stop_ = false;
+};
+
+Pool &pool() {
+    static Pool p;
+    return p;
+}
+
+// Runs fn over [0, n), in parallel when the work (n * cost) is large enough.
+void parallel_for(int64_t n, uint64_t cost, const std::function<void(int64_t)> &fn) {
+    if (g_threads > 1 && uint64_t(n) * cost > (1u << 16)) {
+        pool().run(n, fn);
+    } else {
+        for (int64_t i = 0; i < n; ++i) fn(i);
+    }
+}
+
+// Weight matrix in whichever storage the file had. Accumulation is identical.
+struct Matrix {
+    int dtype = -1;                 // ORC_F16 / ORC_F32 / ORC_I8 (BF16 is widened to F32)
+    uint32_t rows = 0, cols = 0;
+    std::vector<uint16_t> h;
+    std::vector<float> f;
+    std::vector<int8_t> q;
+    float scale = 1.0f;
+    bool present() const { return dtype >= 0; }
+};
+
+// y[o] = float(sum double(W[o][i]) * double(x[i])) -- Opure_CpuReference.cpp:151-161.
+void gemv_rows(const Matrix &W, const float *x, float *y) {
+    const uint32_t rows = W.rows, cols = W.cols;
+    std::vector<double> xd(cols);
+    for (uint32_t i = 0; i < cols; ++i) xd[i] = double(x[i]);
+    const float *L = lut().v;
+    parallel_for(rows, cols, [&](int64_t o) {
+        double acc = 0.0;
+        if (W.dtype == ORC_F16) {
+            const uint16_t *row = W.h.data() + size_t(o) * cols;
+            for (uint32_t i = 0; i < cols; ++i) acc += double(L[row[i]]) * xd[i];
+            y[o] = float(acc);
+        } else if (W.dtype == ORC_F32) {
+            const float *row = W.f.data() + size_t(o) * cols;
+            for (uint32_t i = 0; i < cols; ++i) acc += double(row[i]) * xd[i];
+            y[o] = float(acc);
+        } else {
+            const int8_t *row = W.q.data() + size_t(o) * cols;
+            for (uint32_t i = 0; i < cols; ++i) acc += double(row[i]) * xd[i];
+            // Opure_GEMV_Quant.usf:92 applies scaleW * scaleX (scaleX = 1, :206 of the
+            // engine) after the sum.
+            y[o] = float(acc * double(W.scale));
+        }
+    });
+}
+
+void rmsnorm(const float *x, const float *g, float *y, uint32_t d, float eps) {
+    // Opure_CpuReference.cpp:163-169.
+    double ss = 0.0;
+    for (uint32_t i = 0; i < d; ++i) ss += double(x[i]) * double(x[i]);
+    const double inv = 1.0 / std::sqrt(ss / d + eps);
+    for (uint32_t i = 0; i < d; ++i) y[i] = float(double(x[i]) * inv * double(g[i]));
+}
+
+void rope(float *vec, uint32_t nheads, uint32_t hd, uint32_t pos, double theta, int literal) {
+    // Structure of Opure_CpuReference.cpp:171-189. The exponent follows the shader
+    // (Opure_RoPE.usf:56, pair index) unless `literal` asks for the CPU file's
+    // element index.
+    for (uint32_t head = 0; head < nheads; ++head) {
+        float *row = vec + size_t(head) * hd;
+        for (uint32_t i = 0; i + 1 < hd; i += 2) {
+            const double ex = literal ? double(i) : double(i / 2);
+            const double freq = std::pow(theta, -2.0 * ex / double(hd));
+            const double t = double(pos) * freq;
+            const double ct = std::cos(t), st = std::sin(t);
+            const double e0 = row[i], e1 = row[i + 1];
+            row[i] = float(e0 * ct - e1 * st);
+            row[i + 1] = float(e0 * st + e1 * ct);
+        }
+    }
+}
+
+void swiglu(const float *g, const float *u, float *h, uint32_t n) {
+    // Opure_CpuReference.cpp:191-198 (float arithmetic, unbranched sigmoid).
+    for (uint32_t i = 0; i < n; ++i) {
+        const float s = 1.0f / (1.0f + std::exp(-g[i]));
+        h[i] = (g[i] * s) * u[i];
+    }
+}
+
+// One query head over `seq_len` keys: Opure_CpuReference.cpp:259-305.
+// krow(s)/vrow(s) return fp16 rows of hd elements.
+inline double widen(uint16_t h) { return double(lut().v[h]); }
+inline double widen(float f) { return double(f); }
+
+template <class KRow, class VRow>
+void attend_head(const float *qrow, uint32_t seq_len, uint32_t hd, float scale, KRow krow,
+                 VRow vrow, float *orow, std::vector<double> &scores) {
+    scores.resize(seq_len);
+    double m = -1e300;
+    for (uint32_t s = 0; s < seq_len; ++s) {
+        const auto *k = krow(s);
+        double sc = 0.0;
+        for (uint32_t d = 0; d < hd; ++d) sc += double(qrow[d]) * widen(k[d]);
+        sc *= double(scale);
+        scores[s] = sc;
+        if (sc > m) m = sc;
+    }
+    double sum = 0.0;
+    for (uint32_t s = 0; s < seq_len; ++s) {
+        const double e = std::exp(scores[s] - m);
+        scores[s] = e;
+        sum += e;
+    }
+    for (uint32_t d = 0; d < hd; ++d) orow[d] = 0.0f;
+    for (uint32_t s = 0; s < seq_len; ++s) {
+        const auto *v = vrow(s);
+        const double w = scores[s];
+        for (uint32_t d = 0; d < hd; ++d) orow[d] = float(double(orow[d]) + w * widen(v[d]));
+    }
+    const double inv = 1.0 / (sum > 0.0 ? sum : 1.0);
+    for (uint32_t d = 0; d < hd; ++d) orow[d] = float(double(orow[d]) * inv);
+}
+
+// Softmax probabilities in double, max-shifted.
+void softmax_d(const float *logits, uint32_t n, std::vector<double> &p) {
+    p.resize(n);
+    double mx = -std::numeric_limits<double>::infinity();
+    for (uint32_t i = 0; i < n; ++i) if (double(logits[i]) > mx) mx = logits[i];
+    double z = 0.0;
+    for (uint32_t i = 0; i < n; ++i) { p[i] = std::exp(double(logits[i]) - mx); z += p[i]; }
+    for (uint32_t i = 0; i < n; ++i) p[i] /= z;
+}
+
+uint32_t inverse_cdf(const std::vector<double> &w, double u) {
+    double z = 0.0;
+    for (double x : w) z += x;
+    const double thr = u * z;
+    double c = 0.0;
+    for (uint32_t i = 0; i < w.size(); ++i) {
+        c += w[i];
+        if (c > thr) return i;
+    }
+    // u*Z at the very top (rounding): the last index with non-zero weight.
+    for (uint32_t i = uint32_t(w.size()); i-- > 0;) if (w[i] > 0.0) return i;
+    return 0;
+}
+
+uint32_t argmax1(const float *x, uint32_t n, float *val) {
+    float best = -std::numeric_limits<float>::infinity();
+    uint32_t bi = 0;
+    bool any = false;
+    for (uint32_t i = 0; i < n; ++i) {
+        if (x[i] > best || (!any && x[i] == best)) { best = x[i]; bi = i; any = true; }
+    }
+    if (val) *val = best;
+    return bi;
+}
+
+}  // namespace
+
+// ===========================================================================
+extern "C" {
+
+void orc_rng_u32_stream(uint64_t seed, uint64_t n, uint32_t *out) {
+    uint64_t s = seed ? seed : 1;
+    for (uint64_t i = 0; i < n; ++i) {
+        s ^= s << 13; s ^= s >> 7; s ^= s << 17;
+        out[i] = uint32_t(s >> 32);
+    }
+}
+
+uint16_t orc_f32_to_f16(float f) { return f32_to_f16(f); }
+float orc_f16_to_f32(uint16_t h) { return f16_to_f32(h); }
+void orc_f32_to_f16_n(const float *src, uint16_t *dst, uint64_t n) {
+    for (uint64_t i = 0; i < n; ++i) dst[i] = f32_to_f16(src[i]);
+}
+void orc_f16_to_f32_n(const uint16_t *src, float *dst, uint64_t n) {
+    const float *L = lut().v;
+    for (uint64_t i = 0; i < n; ++i) dst[i] = L[src[i]];
+}
+
+void orc_gemv_f16(const uint16_t *w, const float *x, float *y, uint32_t rows, uint32_t cols,
+                  uint32_t nvec) {
+    Matrix M;
+    M.dtype = ORC_F16; M.rows = rows; M.cols = cols;
+    M.h.assign(w, w + size_t(rows) * cols);
+    for (uint32_t v = 0; v < nvec; ++v) gemv_rows(M, x + size_t(v) * cols, y + size_t(v) * rows);
+}
+
+void orc_gemv_f32(const float *w, const float *x, float *y, uint32_t rows, uint32_t cols,
+                  uint32_t nvec) {
+    Matrix M;
+    M.dtype = ORC_F32; M.rows = rows; M.cols = cols;
+    M.f.assign(w, w + size_t(rows) * cols);
+    for (uint32_t v = 0; v < nvec; ++v) gemv_rows(M, x + size_t(v) * cols, y + size_t(v) * rows);
+}
+
+void orc_gemv_q8(const int8_t *q, float scale_w, float scale_x, const float *x, float *y,
+                 uint32_t rows, uint32_t cols, uint32_t nvec) {
+    Matrix M;
+    M.dtype = ORC_I8; M.rows = rows; M.cols = cols;
+    M.q.assign(q, q + size_t(rows) * cols);
+    M.scale = 1.0f;
+    const double s = double(scale_w) * double(scale_x);
+    std::vector<float> tmp(rows);
+    for (uint32_t v = 0; v < nvec; ++v) {
+        // The unscaled sum, then the two scales in double (the shader applies them in
+        // float after its fp32 sum; the oracle keeps the CPU path's double).
+        const float *xv = x + size_t(v) * cols;
+        float *yv = y + size_t(v) * rows;
+        std::vector<double> xd(cols);
+        for (uint32_t i = 0; i < cols; ++i) xd[i] = xv[i];
+        parallel_for(rows, cols, [&](int64_t o) {
+            double acc = 0.0;
+            const int8_t *row = q + size_t(o) * cols;
+            for (uint32_t i = 0; i < cols; ++i) acc += double(row[i]) * xd[i];
+            yv[o] = float(acc * s);
+        });
+    }
+}
+
+void orc_quantize_q8(const uint16_t *w_f16, uint64_t n, int8_t *q, float *scale) {
+    const float *L = lut().v;
+    float amax = 0.0f;
+    for (uint64_t i = 0; i < n; ++i) amax = std::fmax(amax, std::fabs(L[w_f16[i]]));
+    const float s = amax > 0.0f ? amax / 127.0f : 1.0f;
+    for (uint64_t i = 0; i < n; ++i) {
+        const float r = std::nearbyint(L[w_f16[i]] / s);  // default rounding mode: half-even
+        q[i] = int8_t(r > 127.0f ? 127 : (r < -127.0f ? -127 : int(r)));
+    }
+    *scale = s;
+}
+
+void orc_rmsnorm(const float *x, const float *g, float *y, uint32_t d, float eps) {
+    rmsnorm(x, g, y, d, eps);
+}
+
+void orc_rope(float *vec, uint32_t nheads, uint32_t hd, uint32_t pos, double theta, int lit) {
+    rope(vec, nheads, hd, pos, theta, lit);
+}
+
+void orc_swiglu(const float *g, const float *u, float *h, uint32_t n) { swiglu(g, u, h, n); }
+
+void orc_argmax(const float *x, uint32_t n, uint32_t rows, uint32_t *idx, float *val) {
+    for (uint32_t r = 0; r < rows; ++r)
+        idx[r] = argmax1(x + size_t(r) * n, n, val ? val + r : nullptr);
+}
+
+void orc_attention_paged(const float *q, const uint16_t *pool, const int32_t *page_table,
+                         const uint32_t *seq_lens, uint32_t nseq, uint32_t nq,
+                         uint32_t max_pages, uint32_t P, uint32_t nH, uint32_t nKV,
+                         uint32_t hd, float scale, float *out) {
+    const uint32_t group = nH / nKV;
+    const int64_t jobs = int64_t(nseq) * nq * nH;
+    parallel_for(jobs, uint64_t(max_pages) * P * hd, [&](int64_t job) {
+        std::vector<double> scores;
+        {
+            const uint32_t h = uint32_t(job % nH);
+            const uint32_t j = uint32_t((job / nH) % nq);
+            const uint32_t b = uint32_t(job / (int64_t(nH) * nq));
+            const uint32_t g = h / group;
+            const int32_t *pt = page_table + size_t(b) * max_pages;
+            auto at = [&](uint32_t s, uint32_t kv) {
+                const size_t page = size_t(pt[s / P]);
+                return pool + ((page * 2 + kv) * nKV + g) * size_t(P) * hd + size_t(s % P) * hd;
+            };
+            const size_t qo = ((size_t(b) * nq + j) * nH + h) * hd;
+            attend_head(q + qo, seq_lens[b] + j, hd, scale,
+                        [&](uint32_t s) { return at(s, 0); },
+                        [&](uint32_t s) { return at(s, 1); }, out + qo, scores);
+        }
+    });
+}
+
+void orc_attention_f32(const float *q, const float *k_plane, const float *v_plane,
+                       uint32_t nH, uint32_t nKV, uint32_t hd, uint32_t max_seq,
+                       uint32_t seq_len, float scale, float *out) {
+    const uint32_t group = nH / nKV;
+    std::vector<double> scores;
+    for (uint32_t h = 0; h < nH; ++h) {
+        const size_t base = size_t(h / group) * max_seq * hd;
+        attend_head(q + size_t(h) * hd, seq_len, hd, scale,
+                    [&](uint32_t s) { return k_plane + base + size_t(s) * hd; },
+                    [&](uint32_t s) { return v_plane + base + size_t(s) * hd; },
+                    out + size_t(h) * hd, scores);
+    }
+}
+
+uint32_t orc_sample_softmax(const float *logits, uint32_t vocab, float u) {
+    std::vector<double> p;
+    softmax_d(logits, vocab, p);
+    return inverse_cdf(p, double(u));
+}
+
+int orc_spec_accept_greedy(const float *tl, const uint32_t *draft, uint32_t k, uint32_t V,
+                           uint32_t *out) {
+    uint32_t a = 0;
+    while (a < k && argmax1(tl + size_t(a) * V, V, nullptr) == draft[a]) {
+        out[a] = draft[a];
+        ++a;
+    }
+    out[a] = argmax1(tl + size_t(a) * V, V, nullptr);
+    return int(a);
+}
+
+int orc_spec_accept_rejection(const float *tl, const float *dl, const uint32_t *draft,
+                              const float *u_accept, float u_final, uint32_t k, uint32_t V,
+                              uint32_t *out) {
+    std::vector<double> p, q;
+    for (uint32_t i = 0; i < k; ++i) {
+        softmax_d(tl + size_t(i) * V, V, p);
+        softmax_d(dl + size_t(i) * V, V, q);
+        const uint32_t d = draft[i];
+        if (double(u_accept[i]) * q[d] <= p[d]) {
+            out[i] = d;
+            continue;
+        }
+        std::vector<double> r(V);
+        double z = 0.0;
+        for (uint32_t x = 0; x < V; ++x) { r[x] = p[x] > q[x] ? p[x] - q[x] : 0.0; z += r[x]; }
+        out[i] = inverse_cdf(z > 0.0 ? r : p, double(u_final));
+        return int(i);
+    }
+    softmax_d(tl + size_t(k) * V, V, p);
+    out[k] = inverse_cdf(p, double(u_final));
+    return int(k);
+}
+
+void orc_set_threads(int n) {
+    g_threads = n > 0 ? n : 1;
+    pool().resize(g_threads - 1);
+}
+int orc_get_threads(void) { return g_threads; }
+
+}  // extern "C"
+
+// ===========================================================================
+// Whole model
+// ===========================================================================
+struct orc_model {
+    orc_config c{};
+    Matrix embed, lm_head;
+    std::vector<float> final_norm;
+    struct Layer {
+        std::vector<float> in_norm, post_norm;
+        Matrix wq, wk, wv, wo, gate, up, down;
+    };
+    std::vector<Layer> layers;
+};
+
+struct orc_state {
+    uint32_t max_pos = 0, len = 0;
+    uint32_t L = 0, nKV = 0, hd = 0;
+    std::vector<uint16_t> kv;  // [L][2][nKV][max_pos][hd]
+    uint16_t *at(uint32_t l, uint32_t kvsel, uint32_t g, uint32_t pos) {
+        return kv.data() + ((((size_t(l) * 2 + kvsel) * nKV + g) * max_pos + pos) * hd);
+    }
+    const uint16_t *at(uint32_t l, uint32_t kvsel, uint32_t g, uint32_t pos) const {
+        return kv.data() + ((((size_t(l) * 2 + kvsel) * nKV + g) * max_pos + pos) * hd);
+    }
+};
+
+namespace {
+
+bool load_matrix(Matrix &M, int dtype, const void *data, uint64_t n, uint32_t rows,
+                 uint32_t cols, float scale) {
+    if (n != uint64_t(rows) * cols) return false;
+    M.rows = rows; M.cols = cols; M.scale = scale;
+    if (dtype == ORC_F16) {
+        M.dtype = ORC_F16;
+        M.h.assign(static_cast<const uint16_t *>(data), static_cast<const uint16_t *>(data) + n);
+    } else if (dtype == ORC_F32) {
+        M.dtype = ORC_F32;
+        M.f.assign(static_cast<const float *>(data), static_cast<const float *>(data) + n);
+    } else if (dtype == ORC_BF16) {
+        M.dtype = ORC_F32;
+        M.f.resize(n);
+        for (uint64_t i = 0; i < n; ++i) M.f[i] = bf16_to_f32(static_cast<const uint16_t *>(data)[i]);
+    } else if (dtype == ORC_I8) {
+        M.dtype = ORC_I8;
+        M.q.assign(static_cast<const int8_t *>(data), static_cast<const int8_t *>(data) + n);
+    } else {
+        return false;
+    }
+    return true;
+}
+
+bool load_vector(std::vector<float> &v, int dtype, const void *data, uint64_t n, uint32_t d) {
+    if (n != d) return false;
+    v.resize(n);
+    if (dtype == ORC_F16) {
+        orc_f16_to_f32_n(static_cast<const uint16_t *>(data), v.data(), n);
+    } else if (dtype == ORC_F32) {
+        std::memcpy(v.data(), data, n * 4);
+    } else if (dtype == ORC_BF16) {
+        for (uint64_t i = 0; i < n; ++i) v[i] = bf16_to_f32(static_cast<const uint16_t *>(data)[i]);
+    } else {
+        return false;
+    }
+    return true;
+}
+
+void embed_row(const Matrix &E, uint32_t tok, float *x) {
+    const size_t off = size_t(tok) * E.cols;
+    if (E.dtype == ORC_F16) {
+        const float *L = lut().v;
+        for (uint32_t i = 0; i < E.cols; ++i) x[i] = L[E.h[off + i]];
+    } else if (E.dtype == ORC_F32) {
+        std::memcpy(x, E.f.data() + off, size_t(E.cols) * 4);
+    } else {
+        for (uint32_t i = 0; i < E.cols; ++i) x[i] = float(E.q[off + i]) * E.scale;
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+orc_model *orc_model_create(const orc_config *cfg) {
+    if (!cfg || cfg->heads == 0 || cfg->kv_heads == 0 || cfg->heads % cfg->kv_heads != 0 ||
+        cfg->hidden % cfg->heads != 0)
+        return nullptr;
+    auto *m = new orc_model;
+    m->c = *cfg;
+    m->layers.resize(cfg->layers);
+    return m;
+}
+
+int orc_model_set_tensor(orc_model *m, int role, int layer, int dtype, const void *data,
+                         uint64_t n, float scale) {
+    if (!m || !data) return -1;
+    const orc_config &c = m->c;
+    const uint32_t h = c.hidden, ff = c.inter, kvh = c.kv_heads * (c.hidden / c.heads);
+    if (role >= ORC_IN_NORM && (layer < 0 || uint32_t(layer) >= c.layers)) return -1;
+    auto *Ly = role >= ORC_IN_NORM ? &m->layers[size_t(layer)] : nullptr;
+    bool ok = false;
+    switch (role) {
+        case ORC_EMBED: ok = load_matrix(m->embed, dtype, data, n, c.vocab, h, scale); break;
+        case ORC_LM_HEAD: ok = load_matrix(m->lm_head, dtype, data, n, c.vocab, h, scale); break;
+        case ORC_FINAL_NORM: ok = load_vector(m->final_norm, dtype, data, n, h); break;
+        case ORC_IN_NORM: ok = load_vector(Ly->in_norm, dtype, data, n, h); break;
+        case ORC_POST_NORM: ok = load_vector(Ly->post_norm, dtype, data, n, h); break;
+        case ORC_WQ: ok = load_matrix(Ly->wq, dtype, data, n, h, h, scale); break;
+        case ORC_WK: ok = load_matrix(Ly->wk, dtype, data, n, kvh, h, scale); break;
+        case ORC_WV: ok = load_matrix(Ly->wv, dtype, data, n, kvh, h, scale); break;
+        case ORC_WO: ok = load_matrix(Ly->wo, dtype, data, n, h, h, scale); break;
+        case ORC_GATE: ok = load_matrix(Ly->gate, dtype, data, n, ff, h, scale); break;
+        case ORC_UP: ok = load_matrix(Ly->up, dtype, data, n, ff, h, scale); break;
+        case ORC_DOWN: ok = load_matrix(Ly->down, dtype, data, n, h, ff, scale); break;
+        default: ok = false;
+    }
+    return ok ? 0 : -1;
+}
+
+int orc_model_ready(const orc_model *m) {
+    if (!m || !m->embed.present() || m->final_norm.empty()) return -1;
+    for (const auto &L : m->layers) {
+        if (L.in_norm.empty() || L.post_norm.empty() || !L.wq.present() || !L.wk.present() ||
+            !L.wv.present() || !L.wo.present() || !L.gate.present() || !L.up.present() ||
+            !L.down.present())
+            return -1;
+    }
+    return 0;
+}
+
+void orc_model_free(orc_model *m) { delete m; }
+
+orc_state *orc_state_create(const orc_model *m, uint32_t max_pos) {
+    if (!m || max_pos == 0) return nullptr;
+    auto *s = new orc_state;
+    s->max_pos = max_pos;
+    s->L = m->c.layers;
+    s->nKV = m->c.kv_heads;
+    s->hd = m->c.hidden / m->c.heads;
+    s->kv.assign(size_t(s->L) * 2 * s->nKV * max_pos * s->hd, 0);
+    return s;
+}
+
+void orc_state_free(orc_state *s) { delete s; }
+uint32_t orc_state_len(const orc_state *s) { return s ? s->len : 0; }
+void orc_state_truncate(orc_state *s, uint32_t len) {
+    if (s && len < s->len) s->len = len;
+}
+
+int orc_state_load_kv(orc_state *s, const uint16_t *kv, uint32_t len) {
+    if (!s || len > s->max_pos) return -1;
+    for (uint32_t l = 0; l < s->L; ++l)
+        for (uint32_t sel = 0; sel < 2; ++sel)
+            for (uint32_t g = 0; g < s->nKV; ++g) {
+                const uint16_t *src = kv + (((size_t(l) * 2 + sel) * s->nKV + g) * len) * s->hd;
+                std::memcpy(s->at(l, sel, g, 0), src, size_t(len) * s->hd * 2);
+            }
+    s->len = len;
+    return 0;
+}
+
+int orc_forward(const orc_model *m, orc_state *s, uint32_t tok, float *logits, float *trace) {
+    if (!m || !s) return -1;
+    const orc_config &c = m->c;
+    if (tok >= c.vocab || s->len >= s->max_pos) return -1;
+    const uint32_t h = c.hidden, ff = c.inter, hd = h / c.heads;
+    const uint32_t kvd = c.kv_heads * hd, group = c.heads / c.kv_heads;
+    const uint32_t t = s->len;
+
+    std::vector<float> x(h), normed(h), q(h), k(kvd), v(kvd), attn(h), proj(h), n2(h);
+    std::vector<float> g(ff), u(ff), hh(ff);
+    embed_row(m->embed, tok, x.data());
+
+    for (uint32_t Li = 0; Li < c.layers; ++Li) {
+        const orc_model::Layer &P = m->layers[Li];
+        rmsnorm(x.data(), P.in_norm.data(), normed.data(), h, c.eps);
+        gemv_rows(P.wq, normed.data(), q.data());
+        gemv_rows(P.wk, normed.data(), k.data());
+        gemv_rows(P.wv, normed.data(), v.data());
+        rope(q.data(), c.heads, hd, t, c.theta, c.rope_cpu_literal);
+        rope(k.data(), c.kv_heads, hd, t, c.theta, c.rope_cpu_literal);
+        // Append at position t ([kvHead][pos][dim], Opure_CpuReference.cpp:244-257),
+        // rounded to the fp16 the CUDA path's cache holds.
+        for (uint32_t g2 = 0; g2 < c.kv_heads; ++g2) {
+            uint16_t *kd = s->at(Li, 0, g2, t);
+            uint16_t *vd = s->at(Li, 1, g2, t);
+            for (uint32_t d = 0; d < hd; ++d) {
+                kd[d] = f32_to_f16(k[g2 * hd + d]);
+                vd[d] = f32_to_f16(v[g2 * hd + d]);
+            }
+        }
+        const uint32_t seq_len = t + 1;
+        parallel_for(c.heads, uint64_t(seq_len) * hd * 2, [&](int64_t hq) {
+            std::vector<double> scores;
+            {
+                const uint32_t kvh = uint32_t(hq) / group;
+                attend_head(q.data() + size_t(hq) * hd, seq_len, hd, c.attn_scale,
+                            [&](uint32_t sp) { return static_cast<const orc_state *>(s)->at(Li, 0, kvh, sp); },
+                            [&](uint32_t sp) { return static_cast<const orc_state *>(s)->at(Li, 1, kvh, sp); },
+                            attn.data() + size_t(hq) * hd, scores);
+            }
+        });
+        gemv_rows(P.wo, attn.data(), proj.data());
+        for (uint32_t i = 0; i < h; ++i) x[i] = x[i] + proj[i];
+
+        rmsnorm(x.data(), P.post_norm.data(), n2.data(), h, c.eps);
+        gemv_rows(P.gate, n2.data(), g.data());
+        gemv_rows(P.up, n2.data(), u.data());
+        swiglu(g.data(), u.data(), hh.data(), ff);
+        gemv_rows(P.down, hh.data(), proj.data());
+        for (uint32_t i = 0; i < h; ++i) x[i] = x[i] + proj[i];
+        if (trace) std::memcpy(trace + size_t(Li) * h, x.data(), size_t(h) * 4);
+    }
+    s->len = t + 1;
+    if (logits) {
+        // Final norm in place, then the (tied unless given) LM head, :338-345.
+        rmsnorm(x.data(), m->final_norm.data(), x.data(), h, c.eps);
+        gemv_rows(m->lm_head.present() ? m->lm_head : m->embed, x.data(), logits);
+    }
+    return 0;
+}
+
+int orc_generate(const orc_model *m, const uint32_t *prompt, uint32_t n_prompt,
+                 uint32_t budget, uint32_t max_pos, uint32_t *out, float *margins) {
+    if (!m || n_prompt == 0 || n_prompt > max_pos) return -1;
+    orc_state *s = orc_state_create(m, max_pos);
+    std::vector<float> logits(m->c.vocab);
+    auto top = [&](float *margin) {
+        float v1;
+        const uint32_t i1 = argmax1(logits.data(), m->c.vocab, &v1);
+        if (margin) {
+            float v2 = -std::numeric_limits<float>::infinity();
+            for (uint32_t i = 0; i < m->c.vocab; ++i)
+                if (i != i1 && logits[i] > v2) v2 = logits[i];
+            *margin = v1 - v2;
+        }
+        return i1;
+    };
+    for (uint32_t i = 0; i < n_prompt; ++i)
+        orc_forward(m, s, prompt[i], i + 1 == n_prompt ? logits.data() : nullptr, nullptr);
+    float mg = 0.0f;
+    uint32_t next = top(&mg);
+    int n = 0;
+    for (uint32_t i = 0; i < budget; ++i) {
+        out[n] = next;
+        if (margins) margins[n] = mg;
+        ++n;
+        if (s->len + 1 >= max_pos) break;
+        orc_forward(m, s, next, logits.data(), nullptr);
+        next = top(&mg);
+    }
+    orc_state_free(s);
+    return n;
+}
+
+}  // extern "C"
