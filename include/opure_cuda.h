@@ -1,0 +1,249 @@
+/*
+ * opure_cuda.h -- C ABI of libopure_cuda.so, the B200 (sm_100a) kernel layer.
+ *
+ * This library replaces the reference's GPU layers L1 + L2: the Direct3D 12
+ * device (src/core/Opure_Dx12.h:144-337: GpuBuffer, Device upload/readback,
+ * CommandScope::{SetPipeline,SetParams,Dispatch,Barrier}) and the HLSL kernel
+ * library (src/core/Opure_Shaders.h:23-128, the shaders/ directory). Where the reference
+ * addresses tensors as 32-bit word offsets into five bound buffers plus bank ids
+ * (shaders/Opure_Common.hlsl:35-96), this ABI takes plain device pointers,
+ * element counts and explicit dtypes.
+ *
+ * Conventions
+ *  - Every call returns an opure_status; nothing throws across the ABI.
+ *  - One opure_ctx per GPU, owning one CUDA stream. Kernel calls enqueue on that
+ *    stream and return immediately; opure_sync() waits with a deadline. A ctx is
+ *    not thread-safe: use one host thread per ctx.
+ *  - Buffers from opure_alloc are 256-byte aligned (as Opure_Dx12.cpp:113).
+ *  - Kernel calls allocate nothing (scratch is caller-provided), so a sequence
+ *    of them can be captured into a CUDA graph with opure_graph_begin/end.
+ *  - Device-side waits are bounded: a kernel that gives up records
+ *    OPURE_ERR_DEVICE_TIMEOUT in the ctx status word (opure_last_error) and
+ *    returns; no kernel traps.
+ */
+#ifndef OPURE_CUDA_H
+#define OPURE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum opure_status {
+    OPURE_OK = 0,
+    OPURE_ERR_INVALID_ARG = 1,    /* bad pointer, size or combination of options   */
+    OPURE_ERR_NO_DEVICE = 2,      /* no CUDA device, or not sm_100                  */
+    OPURE_ERR_CUDA = 3,           /* a CUDA runtime call failed                     */
+    OPURE_ERR_OUT_OF_MEMORY = 4,
+    OPURE_ERR_TIMEOUT = 5,        /* host-side bounded wait expired (opure_sync)    */
+    OPURE_ERR_DEVICE_TIMEOUT = 6, /* a device-side bounded wait gave up             */
+    OPURE_ERR_UNSUPPORTED = 7,    /* shape or option this build has no kernel for   */
+    OPURE_ERR_INJECTED = 8,       /* failure injected by opure_debug_inject_failure */
+    OPURE_ERR_DEVICE_BOUNDS = 9   /* a kernel's own bounds check refused an index   */
+} opure_status;
+
+typedef struct opure_ctx opure_ctx;
+typedef struct opure_graph opure_graph;
+typedef struct opure_event opure_event;
+
+typedef struct opure_device_info {
+    int32_t device;
+    int32_t sm_count;
+    int32_t cc_major, cc_minor;
+    uint64_t hbm_bytes;
+    uint64_t l2_bytes;
+    uint32_t smem_per_block_optin;
+    uint32_t clock_mhz_max;
+    char name[96];
+} opure_device_info;
+
+/* ---- lifetime (replaces dx12::Device::Initialize/Shutdown, Opure_Dx12.cpp:152-229) */
+opure_status opure_init(int device, opure_ctx **out);
+opure_status opure_shutdown(opure_ctx *ctx);
+opure_status opure_get_device_info(opure_ctx *ctx, opure_device_info *info);
+const char *opure_strerror(opure_status s);
+/* Reads and clears the device status word that kernels write on a bounds or
+ * timeout failure (the reference decodes device-removed reasons instead,
+ * Opure_Dx12.cpp:53-81). Synchronises the stream. */
+opure_status opure_last_error(opure_ctx *ctx);
+/* cudaStream_t of the ctx, for interop. */
+void *opure_stream(opure_ctx *ctx);
+
+/* ---- memory (replaces GpuBuffer + UploadToBuffer/ReadbackFromBuffer,
+ *      Opure_Dx12.h:144-173, Opure_Dx12.cpp:611-723) ------------------------- */
+opure_status opure_alloc(opure_ctx *ctx, size_t bytes, void **dptr);
+opure_status opure_free(opure_ctx *ctx, void *dptr);
+opure_status opure_alloc_host(opure_ctx *ctx, size_t bytes, void **hptr); /* pinned */
+opure_status opure_free_host(opure_ctx *ctx, void *hptr);
+opure_status opure_h2d(opure_ctx *ctx, void *dst, const void *src, size_t bytes);
+opure_status opure_d2h(opure_ctx *ctx, void *dst, const void *src, size_t bytes);
+opure_status opure_d2d(opure_ctx *ctx, void *dst, const void *src, size_t bytes);
+/* Byte fill, for poisoning (VoxelEngine::PoisonBanks, Opure_VoxelEngine.cpp:625-636). */
+opure_status opure_fill(opure_ctx *ctx, void *dst, uint8_t byte, size_t bytes);
+/* Waits for the ctx stream, polling with a deadline (the reference's 30 s fence
+ * wait, Opure_Dx12.cpp:459-492, returns OPURE_ERR_TIMEOUT here instead of throwing). */
+opure_status opure_sync(opure_ctx *ctx, uint32_t timeout_ms);
+
+/* ---- graphs and timing --------------------------------------------------- */
+opure_status opure_graph_begin(opure_ctx *ctx);
+opure_status opure_graph_end(opure_ctx *ctx, opure_graph **out);
+opure_status opure_graph_launch(opure_ctx *ctx, opure_graph *g);
+opure_status opure_graph_free(opure_graph *g);
+opure_status opure_event_create(opure_ctx *ctx, opure_event **out);
+opure_status opure_event_record(opure_ctx *ctx, opure_event *e);
+opure_status opure_event_elapsed_ms(opure_event *start, opure_event *stop, float *ms);
+opure_status opure_event_free(opure_event *e);
+
+/* ---- element-wise and reduction kernels ------------------------------------
+ * Each mirrors one reference shader; the fused decode path below folds them into
+ * GEMV prologues and epilogues, but they stay callable on their own. */
+
+/* out[t][i] = float(embed[tokens[t]][i]); embed fp16 [vocab][d].
+ * Replaces EmbeddingMain, shaders/Opure_Embedding.usf:21-35. */
+opure_status opure_embedding(opure_ctx *ctx, const uint16_t *embed_f16, uint32_t vocab,
+                             const int32_t *tokens, uint32_t n, uint32_t d, float *out);
+
+/* y[v] = x[v] * rsqrt(mean(x[v]^2) + eps) * g, per row of d; g fp16 or NULL (identity).
+ * Replaces RMSNormMain, shaders/Opure_RMSNorm.usf:31-79. */
+opure_status opure_rmsnorm(opure_ctx *ctx, const float *x, const uint16_t *gain_f16,
+                           float *y, uint32_t d, uint32_t rows, float eps);
+
+/* h = silu(g) * u, silu(g) = g * sigmoid(g). Replaces SwiGLUMain, Opure_SwiGLU.usf:19-40. */
+opure_status opure_swiglu(opure_ctx *ctx, const float *g, const float *u, float *h, uint32_t n);
+
+/* dst = a + b (dst may alias a or b). Replaces AddResMain, Opure_AddRes.usf:29-43,
+ * and AddMain, Opure_Add.usf:14-27. */
+opure_status opure_add(opure_ctx *ctx, const float *a, const float *b, float *dst, uint32_t n);
+
+/* Per row: lowest index of the largest value (NaN never wins). Writes the index and
+ * value of each of `rows` rows of n logits. Replaces ArgMaxMain, Opure_ArgMax.usf:33-85,
+ * with the lowest-index tie rule of the CPU checks (Opure_TestHarness.cpp:990-1002). */
+opure_status opure_argmax(opure_ctx *ctx, const float *logits, uint32_t n, uint32_t rows,
+                          uint32_t *out_idx, float *out_val);
+
+/* ---- paged KV cache ------------------------------------------------------ *
+ * One pool per layer, fp16, laid out [page][K|V][n_kv][page_size][head_dim]: the K
+ * (or V) block of one page and kv head is contiguous (page_size*head_dim*2 bytes).
+ * page_table is int32 [n_seq][max_pages] of physical page ids. The reference keeps
+ * one contiguous fp32 region per layer (Opure_Graph.cpp:396-400) and has no pages. */
+typedef struct opure_kv_layout {
+    uint16_t *pool;            /* this layer's page pool                          */
+    const int32_t *page_table; /* [n_seq][max_pages]                              */
+    uint32_t n_pages;          /* pages in the pool (bounds check)                */
+    uint32_t max_pages;        /* row length of page_table                        */
+    uint32_t page_size;        /* tokens per page: 16, 32, 64 or 128              */
+    uint32_t n_kv;             /* KV heads                                        */
+    uint32_t head_dim;         /* 64 or 128                                       */
+} opure_kv_layout;
+
+/* Rotates q [n][n_heads][hd] and k [n][n_kv][hd] in place with interleaved-pair RoPE at
+ * positions pos[i] (frequency theta^(-2*pair/hd), Opure_RoPE.usf:56; angle and sin/cos
+ * in double) and appends the rotated k and raw v [n][n_kv][hd] as fp16 to the paged cache
+ * of sequence seq[i] at pos[i]. Replaces RoPEMain, shaders/Opure_RoPE.usf:33-115. */
+opure_status opure_rope_kv_append(opure_ctx *ctx, float *q, float *k, const float *v,
+                                  const int32_t *seq, const int32_t *pos, uint32_t n,
+                                  uint32_t n_heads, double theta, const opure_kv_layout *kv);
+
+/* Split-K flash-decode attention over the paged fp16 cache, fp32 softmax.
+ * Query j of entry i (q is [n][n_q][n_heads][hd] fp32) belongs to sequence seq[i] and
+ * attends to keys [0, seq_len[i] + j) -- causal multi-query when n_q > 1 (speculative
+ * verify). GQA maps query head h to kv head h / (n_heads / n_kv). Scores are scaled by
+ * `scale` (the reference applies none: pass 1.0). Partial results of the key splits are
+ * merged inside the kernel by the last CTA of each (entry, kv head).
+ * Replaces AttentionMain{32..256}, shaders/Opure_FlashAttention_Decode.usf:58-179.
+ *
+ * scratch: opure_attention_scratch_bytes(...) bytes of device memory, caller-owned;
+ * its counter words must be zero before the first call (opure_fill) and are left
+ * zero by every call. */
+typedef struct opure_attn_args {
+    const float *q;
+    float *out;                /* [n][n_q][n_heads][hd] fp32                      */
+    const int32_t *seq;        /* [n] sequence index into page_table              */
+    const int32_t *seq_len;    /* [n] keys visible to query 0                     */
+    uint32_t n, n_q, n_heads;
+    float scale;
+    uint32_t max_ctx;          /* upper bound of seq_len + n_q - 1 (sizes the grid) */
+    uint32_t split_tokens;     /* keys per split; 0 = choose for this device       */
+    void *scratch;
+    size_t scratch_bytes;
+    opure_kv_layout kv;
+} opure_attn_args;
+size_t opure_attention_scratch_bytes(uint32_t n, uint32_t n_q, uint32_t n_heads,
+                                     uint32_t n_kv, uint32_t head_dim, uint32_t max_ctx,
+                                     uint32_t split_tokens);
+opure_status opure_attention(opure_ctx *ctx, const opure_attn_args *a);
+
+/* ---- weight-streaming GEMV --------------------------------------------------
+ * y[v][o] = epilogue( sum_i W[o][i] * prologue(x[v])[i] ), W row-major [rows][cols]
+ * (the safetensors layout), fp32 accumulation, for nvec in 1..9 input vectors.
+ * Replaces GEMVMain (shaders/Opure_GEMV.usf:40-88) and GEMVQuantMain
+ * (shaders/Opure_GEMV_Quant.usf:38-94). */
+enum {
+    OPURE_W_F16 = 0,   /* fp16 weights                                                */
+    OPURE_W_Q8 = 1     /* int8 weights, per-tensor scale: y = scale_w*scale_x*sum(q*x) */
+};
+enum {
+    OPURE_PRO_NONE = 0,
+    OPURE_PRO_RMSNORM = 1   /* x <- x * rsqrt(mean(x^2) + eps) * gain (fp16 gain)     */
+};
+enum {
+    OPURE_EPI_STORE = 0,    /* y = acc                                                */
+    OPURE_EPI_ADD = 1,      /* y = residual + acc (residual may alias y)              */
+    OPURE_EPI_SWIGLU = 2,   /* W is [2*rows][cols] = [gate; up]: y = silu(gate) * up  */
+    OPURE_EPI_ARGMAX = 3    /* y = acc (if y != NULL) and argmax per vector           */
+};
+typedef struct opure_gemv_args {
+    const void *w;
+    uint32_t w_dtype;          /* OPURE_W_F16 / OPURE_W_Q8                      */
+    float scale_w, scale_x;    /* OPURE_W_Q8 only                               */
+    uint32_t rows, cols, nvec;
+    const float *x;            /* [nvec][x_stride]                              */
+    uint32_t x_stride;
+    float *y;                  /* [nvec][y_stride]                              */
+    uint32_t y_stride;
+    uint32_t prologue;
+    const uint16_t *norm_gain; /* [cols] fp16, OPURE_PRO_RMSNORM                */
+    float eps;
+    uint32_t epilogue;
+    const float *residual;     /* OPURE_EPI_ADD: [nvec][y_stride]               */
+    /* OPURE_EPI_ARGMAX: packed (value, index) keys, one uint64 per vector, which the
+     * caller zeroes first; decode with opure_argmax_decode. */
+    unsigned long long *argmax_keys;
+} opure_gemv_args;
+opure_status opure_gemv(opure_ctx *ctx, const opure_gemv_args *a);
+/* Decodes OPURE_EPI_ARGMAX keys into (index, value) on the device. */
+opure_status opure_argmax_decode(opure_ctx *ctx, const unsigned long long *keys, uint32_t n,
+                                 uint32_t *out_idx, float *out_val);
+
+/* ---- speculative verify / accept (no reference counterpart: the reference's
+ *      SpeculativeVerify pipelines, Opure_SpeculativeDecode.usf:60-189, are never
+ *      dispatched and it has no accept logic) ------------------------------- */
+enum { OPURE_SPEC_GREEDY = 0, OPURE_SPEC_REJECTION = 1 };
+typedef struct opure_spec_args {
+    uint32_t mode;
+    uint32_t n_seq, k, vocab;
+    const float *target_logits; /* [n_seq][k+1][vocab]                          */
+    const float *draft_logits;  /* [n_seq][k][vocab]      (rejection only)      */
+    const int32_t *draft;       /* [n_seq][k]                                   */
+    const float *u_accept;      /* [n_seq][k]             (rejection only)      */
+    const float *u_final;       /* [n_seq]                (rejection only)      */
+    int32_t *out_tokens;        /* [n_seq][k+1]: accepted drafts + 1 new token  */
+    int32_t *out_accepted;      /* [n_seq]                                      */
+} opure_spec_args;
+opure_status opure_spec_accept(opure_ctx *ctx, const opure_spec_args *a);
+
+/* Inverse-CDF draw per row from softmax(logits) at temperature 1 with uniforms u[row]. */
+opure_status opure_sample_softmax(opure_ctx *ctx, const float *logits, uint32_t vocab,
+                                  uint32_t rows, const float *u, int32_t *out_tokens);
+
+/* ---- fault injection (host side; tests of the error paths) -----------------
+ * The next `count` ABI calls after `after_calls` more calls return OPURE_ERR_INJECTED
+ * without touching the GPU. count = 0 disarms. */
+opure_status opure_debug_inject_failure(opure_ctx *ctx, uint32_t after_calls, uint32_t count);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* OPURE_CUDA_H */

@@ -1,0 +1,233 @@
+// attention.cu -- split-K flash-decode attention over the paged fp16 KV cache.
+//
+// Replaces AttentionMain{32..256} (shaders/Opure_FlashAttention_Decode.usf:58-179): the
+// reference runs one 64-thread group per query head, serial over every key with two
+// barriers per key, and reads each KV head once per query head. Here one CTA owns a
+// (query entry, kv head, key split) triple and serves all G = n_heads / n_kv query heads
+// of that kv head from a single read of its keys and values.
+//
+// The per-lane online-softmax loop lives in attn_core.cuh. States are merged across
+// lane groups (shuffles), warps (shared memory) and finally across key splits: each CTA
+// writes its partial (m, l, acc) to caller-provided scratch and the last CTA of an
+// (entry, kv head) to finish -- found with an atomic ticket, no waiting -- merges them
+// and writes the output.
+#include <algorithm>
+
+#include "attn_core.cuh"
+#include "ctx.cuh"
+
+namespace opure {
+namespace {
+
+constexpr int kWarps = 4;
+
+template <int HD>
+constexpr uint32_t cta_block_tokens() { return AttnShape<HD>::TB * kWarps; }
+
+struct AttnParams {
+    const float *q;          // [entries][n_heads][HD] (entry = (i, j) flattened)
+    float *out;
+    const int32_t *seq;      // [n]
+    const int32_t *seq_len;  // [n]
+    uint32_t n, n_q, n_heads;
+    float scale_log2;        // scale * log2(e)
+    uint32_t split_tokens, n_splits;
+    float *partials;         // [entries * n_kv * n_splits][G][HD + 2]
+    uint32_t *counters;      // [entries * n_kv]
+    opure_kv_layout kv;
+    DeviceStatus *st;
+};
+
+template <int HD, int G>
+__global__ void __launch_bounds__(kWarps * 32) attn_kernel(AttnParams p) {
+    const uint32_t warp = threadIdx.x >> 5;
+    const uint32_t n_kv = p.kv.n_kv;
+    const uint32_t eg = blockIdx.x;              // (entry, kv head)
+    const uint32_t entry = eg / n_kv, g = eg % n_kv;
+    const uint32_t split = blockIdx.y;
+    const uint32_t i = entry / p.n_q, j = entry % p.n_q;
+
+    grid_dependency_wait();
+
+    const int32_t sidx = p.seq[i];
+    const int32_t len = p.seq_len[i] + int32_t(j);
+    const uint32_t t_begin = split * p.split_tokens;
+    const uint32_t t_end = min(uint32_t(max(len, 0)), t_begin + p.split_tokens);
+
+    float qv[G][AttnShape<HD>::E];
+    load_q_slice<HD, G>(p.q + size_t(entry) * p.n_heads * HD, g, p.scale_log2, qv);
+    AttnState<HD, G> st;
+    st.init();
+    KvView kv{reinterpret_cast<const __half *>(p.kv.pool),
+              p.kv.page_table + size_t(max(sidx, 0)) * p.kv.max_pages,
+              p.kv.max_pages, p.kv.n_pages, p.kv.page_size, n_kv, g, sidx >= 0};
+    attend_range<HD, G>(st, qv, kv, t_begin, t_end, warp, kWarps, p.st);
+    merge_lane_groups<HD, G>(st);
+
+    __shared__ WarpStates<HD, G, kWarps> ws;
+    store_warp_state<HD, G, kWarps>(st, ws, warp);
+    __syncthreads();
+
+    // CTA partial -> scratch; one thread per (head, dim) plus the (m, l) pair.
+    const uint32_t n_splits = p.n_splits;
+    float *part = p.partials + (size_t(eg) * n_splits + split) * G * (HD + 2);
+    for (uint32_t idx = threadIdx.x; idx < uint32_t(G) * HD; idx += blockDim.x) {
+        const uint32_t h = idx / HD, d = idx % HD;
+        float a, mn, ls;
+        merge_warps<HD, G, kWarps>(ws, h, d, a, mn, ls);
+        part[h * (HD + 2) + d] = a;
+        if (d == 0) {
+            part[h * (HD + 2) + HD] = mn;
+            part[h * (HD + 2) + HD + 1] = ls;
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    __shared__ uint32_t ticket;
+    if (threadIdx.x == 0) ticket = atomicAdd(p.counters + eg, 1u);
+    __syncthreads();
+    if (ticket != n_splits - 1) return;
+
+    // Last CTA of this (entry, kv head): merge every split.
+    __threadfence();
+    const float *parts = p.partials + size_t(eg) * n_splits * G * (HD + 2);
+    for (uint32_t idx = threadIdx.x; idx < uint32_t(G) * HD; idx += blockDim.x) {
+        const uint32_t h = idx / HD, d = idx % HD;
+        float mn = -INFINITY;
+        for (uint32_t sp = 0; sp < n_splits; ++sp)
+            mn = fmaxf(mn, __ldcg(parts + (size_t(sp) * G + h) * (HD + 2) + HD));
+        float a = 0.f, lsum = 0.f;
+        for (uint32_t sp = 0; sp < n_splits; ++sp) {
+            const float *pp = parts + (size_t(sp) * G + h) * (HD + 2);
+            const float ms = __ldcg(pp + HD);
+            const float f = (mn == -INFINITY || ms == -INFINITY) ? 0.f : fast_exp2(ms - mn);
+            a += __ldcg(pp + d) * f;
+            lsum += __ldcg(pp + HD + 1) * f;
+        }
+        // acc / max(sum, 1e-30) as the reference's epilogue
+        // (Opure_FlashAttention_Decode.usf:235-239).
+        p.out[(size_t(entry) * p.n_heads + g * G + h) * HD + d] = a / fmaxf(lsum, 1e-30f);
+    }
+    if (threadIdx.x == 0) p.counters[eg] = 0u;  // ready for the next call
+}
+
+using AttnKernel = void (*)(AttnParams);
+
+template <int HD>
+AttnKernel pick_g(uint32_t G) {
+    switch (G) {
+        case 1: return attn_kernel<HD, 1>;
+        case 2: return attn_kernel<HD, 2>;
+        case 3: return attn_kernel<HD, 3>;
+        case 4: return attn_kernel<HD, 4>;
+    }
+    return nullptr;
+}
+
+AttnKernel pick(uint32_t hd, uint32_t G) {
+    switch (hd) {
+        case 32: return pick_g<32>(G);
+        case 64: return pick_g<64>(G);
+        case 96: return pick_g<96>(G);
+        case 128: return pick_g<128>(G);
+        case 160: return pick_g<160>(G);
+        case 192: return pick_g<192>(G);
+        case 224: return pick_g<224>(G);
+        case 256: return pick_g<256>(G);
+    }
+    return nullptr;
+}
+
+uint32_t cta_tokens(uint32_t hd) {
+    switch (hd) {
+        case 32: return cta_block_tokens<32>();
+        case 64: return cta_block_tokens<64>();
+        case 96: return cta_block_tokens<96>();
+        case 128: return cta_block_tokens<128>();
+        case 160: return cta_block_tokens<160>();
+        case 192: return cta_block_tokens<192>();
+        case 224: return cta_block_tokens<224>();
+        case 256: return cta_block_tokens<256>();
+    }
+    return 0;
+}
+
+// Keys per split: a whole number of CTA blocks, with enough splits to put several
+// CTAs on every SM (sm_count 148 on B200) without splitting below one block.
+uint32_t choose_split(uint32_t entries, uint32_t n_kv, uint32_t hd, uint32_t max_ctx,
+                      uint32_t requested, int sm_count) {
+    const uint32_t unit = cta_tokens(hd);
+    if (requested) return ((requested + unit - 1) / unit) * unit;
+    const uint64_t pairs = uint64_t(entries) * n_kv;
+    const uint64_t target = uint64_t(sm_count > 0 ? sm_count : 148) * 4;
+    const uint64_t want_splits = std::max<uint64_t>(1, (target + pairs - 1) / pairs);
+    const uint64_t per = (uint64_t(std::max(max_ctx, 1u)) + want_splits - 1) / want_splits;
+    return uint32_t(std::max<uint64_t>(unit, ((per + unit - 1) / unit) * unit));
+}
+
+size_t scratch_layout(uint32_t entries, uint32_t n_kv, uint32_t G, uint32_t hd, uint32_t n_splits,
+                      size_t *counters_off) {
+    const size_t part = size_t(entries) * n_kv * n_splits * G * (hd + 2) * sizeof(float);
+    const size_t off = (part + 255) & ~size_t(255);
+    if (counters_off) *counters_off = off;
+    return off + size_t(entries) * n_kv * sizeof(uint32_t);
+}
+
+}  // namespace
+}  // namespace opure
+
+using namespace opure;
+
+extern "C" size_t opure_attention_scratch_bytes(uint32_t n, uint32_t n_q, uint32_t n_heads,
+                                                uint32_t n_kv, uint32_t hd, uint32_t max_ctx,
+                                                uint32_t split_tokens) {
+    if (!n || !n_q || !n_kv || !hd || n_heads % n_kv || !cta_tokens(hd)) return 0;
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const uint32_t entries = n * n_q;
+    const uint32_t st = choose_split(entries, n_kv, hd, max_ctx, split_tokens, sms);
+    const uint32_t n_splits = std::max(1u, (max_ctx + st - 1) / st);
+    return scratch_layout(entries, n_kv, n_heads / n_kv, hd, n_splits, nullptr);
+}
+
+extern "C" opure_status opure_attention(opure_ctx *ctx, const opure_attn_args *a) {
+    opure_status s = enter(ctx);
+    if (s) return s;
+    if (!a || !a->q || !a->out || !a->seq || !a->seq_len || !a->scratch) return OPURE_ERR_INVALID_ARG;
+    const opure_kv_layout &kv = a->kv;
+    if (!kv.pool || !kv.page_table || !kv.n_kv || !kv.page_size || !kv.max_pages)
+        return OPURE_ERR_INVALID_ARG;
+    if (a->n_heads % kv.n_kv) return OPURE_ERR_INVALID_ARG;
+    if (a->n == 0 || a->n_q == 0) return OPURE_OK;
+    const uint32_t G = a->n_heads / kv.n_kv;
+    AttnKernel k = pick(kv.head_dim, G);
+    if (!k) return OPURE_ERR_UNSUPPORTED;
+    if (reinterpret_cast<uintptr_t>(kv.pool) % 16) return OPURE_ERR_UNSUPPORTED;
+    const uint32_t entries = a->n * a->n_q;
+    const uint32_t st = choose_split(entries, kv.n_kv, kv.head_dim, a->max_ctx, a->split_tokens,
+                                     ctx->sm_count);
+    const uint32_t n_splits = std::max(1u, (a->max_ctx + st - 1) / st);
+    size_t counters_off = 0;
+    const size_t need = scratch_layout(entries, kv.n_kv, G, kv.head_dim, n_splits, &counters_off);
+    if (a->scratch_bytes < need || (reinterpret_cast<uintptr_t>(a->scratch) % 16))
+        return OPURE_ERR_INVALID_ARG;
+    if (uint64_t(entries) * kv.n_kv > 0x7fffffffu || n_splits > 65535) return OPURE_ERR_UNSUPPORTED;
+
+    AttnParams p{};
+    p.q = a->q;
+    p.out = a->out;
+    p.seq = a->seq;
+    p.seq_len = a->seq_len;
+    p.n = a->n;
+    p.n_q = a->n_q;
+    p.n_heads = a->n_heads;
+    p.scale_log2 = a->scale * 1.4426950408889634f;
+    p.split_tokens = st;
+    p.n_splits = n_splits;
+    p.partials = static_cast<float *>(a->scratch);
+    p.counters = reinterpret_cast<uint32_t *>(static_cast<char *>(a->scratch) + counters_off);
+    p.kv = kv;
+    p.st = ctx->status;
+    return launch(ctx, k, dim3(entries * kv.n_kv, n_splits), dim3(kWarps * 32), 0, true, p);
+}
