@@ -138,11 +138,14 @@ typedef struct opure_kv_layout {
     uint32_t head_dim;         /* 64 or 128                                       */
 } opure_kv_layout;
 
-/* Rotates q [n][n_heads][hd] and k [n][n_kv][hd] in place with interleaved-pair RoPE at
- * positions pos[i] (frequency theta^(-2*pair/hd), Opure_RoPE.usf:56; angle and sin/cos
- * in double) and appends the rotated k and raw v [n][n_kv][hd] as fp16 to the paged cache
- * of sequence seq[i] at pos[i]. Replaces RoPEMain, shaders/Opure_RoPE.usf:33-115. */
-opure_status opure_rope_kv_append(opure_ctx *ctx, float *q, float *k, const float *v,
+/* RoPE + KV append for n token vectors. Row i of `qkv` (row stride `stride` floats) holds
+ * [q: n_heads*hd | k: n_kv*hd | v: n_kv*hd], the layout of the fused q;k;v GEMV. q and k are
+ * rotated with interleaved-pair RoPE at position pos[i] (frequency theta^(-2*pair/hd) as
+ * Opure_RoPE.usf:56; angle, sin/cos and rotation in double as Opure_CpuReference.cpp:171-189);
+ * the rotated q goes to q_out [n][n_heads][hd] and the rotated k and raw v are appended as
+ * fp16 to the paged cache of sequence seq[i] at slot pos[i].
+ * Replaces RoPEMain, shaders/Opure_RoPE.usf:33-115. */
+opure_status opure_rope_kv_append(opure_ctx *ctx, const float *qkv, uint32_t stride, float *q_out,
                                   const int32_t *seq, const int32_t *pos, uint32_t n,
                                   uint32_t n_heads, double theta, const opure_kv_layout *kv);
 
@@ -198,6 +201,7 @@ typedef struct opure_gemv_args {
     const void *w;
     uint32_t w_dtype;          /* OPURE_W_F16 / OPURE_W_Q8                      */
     float scale_w, scale_x;    /* OPURE_W_Q8 only                               */
+    float scale_w2;            /* OPURE_W_Q8 + OPURE_EPI_SWIGLU: scale of the up half */
     uint32_t rows, cols, nvec;
     const float *x;            /* [nvec][x_stride]                              */
     uint32_t x_stride;
@@ -216,6 +220,35 @@ opure_status opure_gemv(opure_ctx *ctx, const opure_gemv_args *a);
 /* Decodes OPURE_EPI_ARGMAX keys into (index, value) on the device. */
 opure_status opure_argmax_decode(opure_ctx *ctx, const unsigned long long *keys, uint32_t n,
                                  uint32_t *out_idx, float *out_val);
+
+/* ---- decode-step bookkeeping ----------------------------------------------------
+ * A decode step computes one token vector per entry. opure_step_begin / opure_step_end
+ * bracket the per-layer kernels of a step so that a captured step graph replays with no
+ * host work: begin picks each vector's token (from the token history, or for a
+ * self-driving greedy vector past its known tokens, from the previous step's argmax key),
+ * records it, clears the key, publishes seq_len = pos + 1 and gathers the embedding row
+ * into the residual stream (EmbeddingMain, Opure_Embedding.usf:21-35); end advances the
+ * positions of self-driving vectors. This is the reference's DecodeStep/ArgMaxFrom loop
+ * (Opure_VoxelEngine.cpp:765-800, :962-988) without the per-token host round trip. */
+enum { OPURE_VEC_AUTO = 1 };
+typedef struct opure_step_io {
+    uint32_t nvec;
+    const int32_t *seq;        /* [nvec] sequence slot (page-table / token-history row) */
+    int32_t *pos;              /* [nvec] position computed by this step                  */
+    int32_t *seq_len;          /* [nvec] written by begin: pos + 1                       */
+    int32_t *known;            /* [nvec] tokens[seq][0, known) are valid                 */
+    const uint32_t *flags;     /* [nvec] OPURE_VEC_AUTO or 0 (token given by the host)   */
+    const int32_t *in_tokens;  /* [nvec] or NULL: token of each non-AUTO vector, recorded
+                                  into the history at pos (NULL: read the history)        */
+    int32_t *tokens;           /* [slots][max_len] token history                        */
+    uint32_t max_len;
+    unsigned long long *keys;  /* [nvec] argmax keys of the previous step's lm_head       */
+    const uint16_t *embed;     /* fp16 [vocab][hidden]                                   */
+    uint32_t vocab, hidden;
+    float *x;                  /* [nvec][hidden] residual stream, written by begin        */
+} opure_step_io;
+opure_status opure_step_begin(opure_ctx *ctx, const opure_step_io *io);
+opure_status opure_step_end(opure_ctx *ctx, const opure_step_io *io);
 
 /* ---- speculative verify / accept (no reference counterpart: the reference's
  *      SpeculativeVerify pipelines, Opure_SpeculativeDecode.usf:60-189, are never

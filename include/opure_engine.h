@@ -1,0 +1,128 @@
+/*
+ * opure_engine.h -- C ABI of libopure_engine.so, the C++20 host engine.
+ *
+ * Wraps engine::VoxelEngine (the reference's src/engine/Opure_VoxelEngine.h:114-335)
+ * for callers that bind C: the reference's HTTP server and harness call Generate,
+ * ForwardLogits and RunLayersTraced on the class directly (Opure_Server.cpp:305,
+ * Opure_TestHarness.cpp:624,956-987); these entry points expose the same operations
+ * with token ids in and out. C++ exceptions never cross the ABI: each call returns an
+ * opure_status and opure_engine_last_error() holds the message of the last failure.
+ *
+ * Also exported: the seeded synthetic-input generators that the benchmark
+ * configurations use in place of the reference's downloaded checkpoint.
+ */
+#ifndef OPURE_ENGINE_H
+#define OPURE_ENGINE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "opure_cuda.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct opure_engine opure_engine;
+
+/* EngineOptions (Opure_VoxelEngine.h:54-65) plus the B200 engine's own settings. */
+typedef struct opure_engine_options {
+    uint32_t max_new_tokens;  /* EngineOptions.maxNewTokens (0: 256)                   */
+    uint32_t max_batch;       /* independent sequences per step (0: 1)                 */
+    uint32_t max_len;         /* tokens per sequence incl. prompt (0: min(max_pos, 4096)) */
+    uint32_t page_size;       /* KV page size in tokens: 16/32/64/128 (0: 64)          */
+    uint64_t page_seed;       /* seeded shuffle of the KV free list (0: in order)      */
+    uint32_t use_graphs;      /* 1: capture each step into a CUDA graph                */
+    float attn_scale;         /* attention score scale (0: 1.0, the reference's)       */
+} opure_engine_options;
+
+typedef struct opure_engine_info {
+    uint32_t vocab, hidden, inter, layers, heads, kv_heads, head_dim, max_pos;
+    uint32_t max_len, max_batch, page_size, w_dtype;
+    uint64_t weight_bytes;        /* resident weight arena                              */
+    uint64_t stream_bytes;        /* weight bytes one decode step reads                 */
+    uint64_t kv_bytes_per_token;  /* fp16 K+V, all layers, one sequence                 */
+} opure_engine_info;
+
+typedef struct opure_generate_timing {
+    double prefill_ms;            /* device time of the prefill steps                   */
+    double decode_ms;             /* device time of the decode steps                    */
+    uint32_t prefill_steps, decode_steps;
+} opure_generate_timing;
+
+opure_status opure_engine_create(const char *model_dir, int device,
+                                 const opure_engine_options *opts, opure_engine **out);
+opure_status opure_engine_destroy(opure_engine *e);
+const char *opure_engine_last_error(opure_engine *e);
+opure_status opure_engine_get_info(opure_engine *e, opure_engine_info *info);
+opure_ctx *opure_engine_ctx(opure_engine *e);
+
+/* Generate (Opure_VoxelEngine.cpp:894-958) for n_seq independent prompts: prompts are
+ * concatenated in `prompts`, prompt_lens[n_seq] gives each length; each sequence gets
+ * `budget` greedy tokens in out_tokens[n_seq][budget]. Prefill and decode run on the
+ * device with no per-token host round trip. timing may be NULL. */
+opure_status opure_engine_generate(opure_engine *e, const int32_t *prompts, const uint32_t *prompt_lens,
+                                   uint32_t n_seq, uint32_t budget, int32_t *out_tokens,
+                                   opure_generate_timing *timing);
+
+/* Prefill of one sequence (slot 0) ahead of host-driven decode steps (:682-710); `next`
+ * (may be NULL) receives the argmax of the last prompt position (ArgMaxFrom, :962-988). */
+opure_status opure_engine_prefill(opure_engine *e, const int32_t *tokens, uint32_t n, int32_t *next);
+/* One host-driven step for sequences 0..n-1: tokens[i] at positions[i] in, next[i] out
+ * (DecodeStep, Opure_VoxelEngine.cpp:765-800: copy in, one step, 8-byte readback). */
+opure_status opure_engine_decode_step(opure_engine *e, const int32_t *tokens, const int32_t *positions,
+                                      uint32_t n, int32_t *next);
+
+/* Device-resident decoding after opure_engine_generate: enqueues `steps` replays of the
+ * step graph for sequences 0..n-1 (self-driving greedy, no host round trip) and returns
+ * without waiting; opure_engine_set_positions rewinds positions (tokens already in the
+ * history are then re-fed rather than re-chosen); opure_engine_sync waits for the stream
+ * and reports any device-side failure. */
+opure_status opure_engine_run_steps(opure_engine *e, uint32_t n, uint32_t steps);
+opure_status opure_engine_set_positions(opure_engine *e, const int32_t *positions, uint32_t n);
+opure_status opure_engine_sync(opure_engine *e);
+
+/* ForwardLogits / ForwardArgMax (Opure_VoxelEngine.cpp:803-821, :879-891). */
+opure_status opure_engine_forward_logits(opure_engine *e, const int32_t *tokens, uint32_t n, float *logits);
+opure_status opure_engine_forward_argmax(opure_engine *e, const int32_t *tokens, uint32_t n, int32_t *out);
+
+/* RunLayersTraced (Opure_VoxelEngine.cpp:546-587): residual after each of the first
+ * n_layers layers for `token` at position 0, into trace[n_layers][hidden]. */
+opure_status opure_engine_trace(opure_engine *e, int32_t token, uint32_t n_layers, float *trace);
+
+/* Fills the activation buffers with `value` (PoisonBanks, :625-636). */
+opure_status opure_engine_poison(opure_engine *e, float value);
+
+/* Loads precomputed fp16 K/V [layers][2][kv_heads][len][head_dim] into sequence slot `seq`
+ * (synthetic long contexts for the large-model configuration). */
+opure_status opure_engine_load_kv(opure_engine *e, uint32_t seq, const uint16_t *kv, uint32_t len);
+
+/* Parses config.json, maps model.safetensors, resolves tensor roles and plans the device
+ * layout without touching a GPU (the reference's opure_inspect tool, Opure_Inspect.cpp).
+ * On failure the reason is copied to err (err_len bytes, may be NULL). */
+opure_status opure_model_inspect(const char *model_dir, opure_engine_info *info, char *err, size_t err_len);
+
+/* ---- seeded synthetic inputs (the reference downloads a checkpoint instead,
+ *      scripts/fetch_model.ps1) ---------------------------------------------- */
+typedef struct opure_synth_spec {
+    uint32_t vocab, hidden, inter, layers, heads, kv_heads, max_pos;
+    float eps;
+    double theta;
+    uint32_t tied;            /* 1: lm_head is the embedding                          */
+    uint64_t seed;            /* weights N(0, std), xorshift64 + Box-Muller, fp16 RNE  */
+    float std;
+    uint32_t int8;            /* 1: matrices as per-tensor int8 + "scale" header key   */
+    uint64_t noise_seed;      /* draft models: + N(0, noise_std) per matrix element    */
+    float noise_std;
+} opure_synth_spec;
+
+opure_status opure_synth_model(const char *dir, const opure_synth_spec *spec);
+opure_status opure_synth_normal_f16(uint64_t seed, float stddev, uint64_t n, uint16_t *out);
+opure_status opure_synth_prompt(uint64_t seed, uint32_t vocab, uint32_t n, int32_t *out);
+opure_status opure_synth_permutation(uint64_t seed, uint32_t n, int32_t *out);
+opure_status opure_synth_uniforms(uint64_t seed, uint64_t n, float *out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* OPURE_ENGINE_H */

@@ -48,6 +48,7 @@ __global__ void __launch_bounds__(kWarps * 32) attn_kernel(AttnParams p) {
     const uint32_t i = entry / p.n_q, j = entry % p.n_q;
 
     grid_dependency_wait();
+    grid_dependents_launch();
 
     const int32_t sidx = p.seq[i];
     const int32_t len = p.seq_len[i] + int32_t(j);

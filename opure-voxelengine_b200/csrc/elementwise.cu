@@ -97,10 +97,12 @@ __global__ void argmax_decode_kernel(const unsigned long long *keys, uint32_t n,
 // RoPEMain, shaders/Opure_RoPE.usf:33-115: interleaved pairs, frequency
 // theta^(-2*pair/hd) (:56); the angle, sin/cos and rotation are computed in double as
 // the CPU path does (Opure_CpuReference.cpp:171-189). K (rotated) and V (raw) are
-// appended as fp16 into the paged cache.
-__global__ void rope_kv_kernel(float *q, float *k, const float *v, const int32_t *seq,
+// appended as fp16 into the paged cache; one thread per (q or k) pair.
+__global__ void rope_kv_kernel(const float *qkv, uint32_t stride, float *q_out, const int32_t *seq,
                                const int32_t *pos, uint32_t n_heads, double theta,
                                opure_kv_layout kv, DeviceStatus *st) {
+    grid_dependency_wait();
+    grid_dependents_launch();
     const uint32_t i = blockIdx.y;
     const uint32_t hd = kv.head_dim, half = hd / 2;
     const uint32_t nq = n_heads * half, nk = kv.n_kv * half;
@@ -113,12 +115,16 @@ __global__ void rope_kv_kernel(float *q, float *k, const float *v, const int32_t
     const double freq = pow(theta, -2.0 * double(pair) / double(hd));
     double sn, cs;
     sincos(double(p) * freq, &sn, &cs);
-    float *vec = is_q ? q + (size_t(i) * n_heads + head) * hd : k + (size_t(i) * kv.n_kv + head) * hd;
-    const double e0 = vec[2 * pair], e1 = vec[2 * pair + 1];
+    const float *row = qkv + size_t(i) * stride;
+    const float *src = is_q ? row + size_t(head) * hd : row + size_t(n_heads + head) * hd;
+    const double e0 = src[2 * pair], e1 = src[2 * pair + 1];
     const float r0 = float(e0 * cs - e1 * sn), r1 = float(e0 * sn + e1 * cs);
-    vec[2 * pair] = r0;
-    vec[2 * pair + 1] = r1;
-    if (is_q) return;
+    if (is_q) {
+        float *qd = q_out + (size_t(i) * n_heads + head) * hd;
+        qd[2 * pair] = r0;
+        qd[2 * pair + 1] = r1;
+        return;
+    }
     const uint32_t lp = uint32_t(p) / kv.page_size, slot = uint32_t(p) % kv.page_size;
     if (p < 0 || s < 0 || lp >= kv.max_pages) {
         report(st, OPURE_ERR_DEVICE_BOUNDS, 2, uint32_t(p));
@@ -132,7 +138,7 @@ __global__ void rope_kv_kernel(float *q, float *k, const float *v, const int32_t
     const size_t blk = size_t(kv.page_size) * hd;
     __half *kd = reinterpret_cast<__half *>(kv.pool) + (size_t(page) * 2 * kv.n_kv + head) * blk + size_t(slot) * hd;
     __half *vd = kd + size_t(kv.n_kv) * blk;
-    const float *vs = v + (size_t(i) * kv.n_kv + head) * hd;
+    const float *vs = row + size_t(n_heads + kv.n_kv + head) * hd;
     kd[2 * pair] = __float2half_rn(r0);
     kd[2 * pair + 1] = __float2half_rn(r1);
     vd[2 * pair] = __float2half_rn(vs[2 * pair]);
@@ -201,20 +207,21 @@ opure_status opure_argmax_decode(opure_ctx *ctx, const unsigned long long *keys,
                   n, idx, val);
 }
 
-opure_status opure_rope_kv_append(opure_ctx *ctx, float *q, float *k, const float *v,
+opure_status opure_rope_kv_append(opure_ctx *ctx, const float *qkv, uint32_t stride, float *q_out,
                                   const int32_t *seq, const int32_t *pos, uint32_t n,
                                   uint32_t n_heads, double theta, const opure_kv_layout *kv) {
     opure_status s = enter(ctx);
     if (s) return s;
-    if (!q || !k || !v || !seq || !pos || !kv || !kv->pool || !kv->page_table)
+    if (!qkv || !q_out || !seq || !pos || !kv || !kv->pool || !kv->page_table)
         return OPURE_ERR_INVALID_ARG;
     if (kv->head_dim == 0 || kv->head_dim % 2 || kv->n_kv == 0 || n_heads % kv->n_kv ||
         kv->page_size == 0)
         return OPURE_ERR_INVALID_ARG;
+    if (stride < (n_heads + 2 * kv->n_kv) * kv->head_dim) return OPURE_ERR_INVALID_ARG;
     if (n == 0) return OPURE_OK;
     const uint32_t pairs = (n_heads + kv->n_kv) * (kv->head_dim / 2);
-    return launch(ctx, rope_kv_kernel, dim3(ceil_div(pairs, 128), n), dim3(128), 0, false, q, k, v,
-                  seq, pos, n_heads, theta, *kv, ctx->status);
+    return launch(ctx, rope_kv_kernel, dim3(ceil_div(pairs, 128), n), dim3(128), 0, true, qkv, stride,
+                  q_out, seq, pos, n_heads, theta, *kv, ctx->status);
 }
 
 }  // extern "C"

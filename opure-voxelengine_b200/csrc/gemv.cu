@@ -18,6 +18,7 @@ struct GemvParams {
     size_t pitch;                 // bytes per weight row
     uint32_t rows, cols, nchunks;
     float scale;                  // scale_w * scale_x for int8, 1 for fp16
+    float scale2;                 // scale of the up half (SwiGLU), same convention
     const float *x;
     uint32_t x_stride;
     float *y;
@@ -35,25 +36,38 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(GemvParams p) {
     float *red = smem + NV * p.cols;
     __shared__ unsigned long long cta_best[kThreads / 32][NV];
 
-    grid_dependency_wait();
-    stage_vectors<NV>(p.x, p.x_stride, p.cols, PRO == OPURE_PRO_RMSNORM, p.gain, p.eps, xs, red);
-
     const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
     const uint32_t nwarps = gridDim.x * (kThreads / 32);
     const uint32_t groups = (p.rows + kRows - 1) / kRows;
+    const uint32_t g0 = blockIdx.x * (kThreads / 32) + warp;
+
+    // Weights do not depend on the previous kernel: start this warp's first row group
+    // before waiting on it.
+    RowPrefetch<kRows> pre, pre_up;
+    if (g0 < groups) {
+        const uint32_t valid0 = min(uint32_t(kRows), p.rows - g0 * kRows);
+        prefetch_rows(pre, p.w, p.pitch, g0 * kRows, valid0, p.nchunks);
+        if constexpr (EPI == OPURE_EPI_SWIGLU)
+            prefetch_rows(pre_up, p.w + size_t(p.rows) * p.pitch, p.pitch, g0 * kRows, valid0, p.nchunks);
+    }
+
+    grid_dependency_wait();
+    grid_dependents_launch();
+    stage_vectors<NV>(p.x, p.x_stride, p.cols, PRO == OPURE_PRO_RMSNORM, p.gain, p.eps, xs, red);
+
     unsigned long long best[NV];
 #pragma unroll
     for (int v = 0; v < NV; ++v) best[v] = 0ull;
 
-    for (uint32_t g = blockIdx.x * (kThreads / 32) + warp; g < groups; g += nwarps) {
+    for (uint32_t g = g0; g < groups; g += nwarps) {
         const uint32_t row0 = g * kRows;
         const uint32_t valid = min(uint32_t(kRows), p.rows - row0);
         float acc[kRows][NV];
-        dot_rows<WT, NV, kRows>(p.w, p.pitch, row0, valid, p.nchunks, xs, p.cols, acc);
+        dot_rows<WT, NV, kRows>(p.w, p.pitch, row0, valid, p.nchunks, xs, p.cols, acc, pre, g == g0);
         float acc_up[kRows][NV];
         if constexpr (EPI == OPURE_EPI_SWIGLU)
             dot_rows<WT, NV, kRows>(p.w + size_t(p.rows) * p.pitch, p.pitch, row0, valid, p.nchunks,
-                                    xs, p.cols, acc_up);
+                                    xs, p.cols, acc_up, pre_up, g == g0);
 #pragma unroll
         for (int r = 0; r < kRows; ++r) {
 #pragma unroll
@@ -71,7 +85,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(GemvParams p) {
                 } else if constexpr (EPI == OPURE_EPI_ADD) {
                     p.y[o] = p.residual[o] + val;
                 } else if constexpr (EPI == OPURE_EPI_SWIGLU) {
-                    const float u = acc_up[r][v] * p.scale;
+                    const float u = acc_up[r][v] * p.scale2;
                     const float s = 1.0f / (1.0f + expf(-val));
                     p.y[o] = (val * s) * u;
                 } else {
@@ -168,6 +182,7 @@ extern "C" opure_status opure_gemv(opure_ctx *ctx, const opure_gemv_args *a) {
     p.cols = a->cols;
     p.nchunks = uint32_t(p.pitch / 16);
     p.scale = a->w_dtype == OPURE_W_Q8 ? a->scale_w * a->scale_x : 1.0f;
+    p.scale2 = a->w_dtype == OPURE_W_Q8 ? (a->scale_w2 != 0.f ? a->scale_w2 : a->scale_w) * a->scale_x : 1.0f;
     p.x_stride = a->x_stride;
     p.y_stride = a->y_stride;
     p.gain = reinterpret_cast<const __half *>(a->norm_gain);

@@ -42,16 +42,44 @@ __device__ __forceinline__ void unpack_chunk(const uint4 &w, float *f) {
     }
 }
 
+constexpr int kBatch = 2;  // 16-byte chunks per lane and row loaded ahead of their FMAs
+
+// The first chunk batch of R rows, loaded into registers ahead of use: a kernel issues it
+// before waiting on its predecessor (weights never depend on the previous kernel), so the
+// DRAM latency overlaps the predecessor's tail.
+template <int R>
+struct RowPrefetch {
+    uint4 w[kBatch][R];
+};
+
+template <int R>
+__device__ __forceinline__ void prefetch_rows(RowPrefetch<R> &pf, const uint8_t *__restrict__ W,
+                                              size_t pitch, uint32_t row0, uint32_t rows_valid,
+                                              uint32_t nchunks) {
+    const uint32_t lane = threadIdx.x & 31u;
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+        const uint32_t c = lane + 32u * b;
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+            pf.w[b][r] = (c < nchunks && r < int(rows_valid)) ? ldg_nc(W + size_t(row0 + r) * pitch + size_t(c) * 16)
+                                                              : make_uint4(0, 0, 0, 0);
+    }
+}
+
 // Chunk-batched dot products of R rows (row0 .. row0+R-1, rows >= rows_valid are
 // skipped) against NV vectors xs[v * xs_stride + i] in shared memory.
 // Row r starts at W + (row0 + r) * pitch (bytes); a row has nchunks 16-byte chunks.
+// With use_pre, the first batch comes from `pre` (prefetch_rows of the same rows).
 // On return every lane holds the full sums in acc.
-template <int WT, int NV, int R, int BATCH = 2>
+template <int WT, int NV, int R>
 __device__ __forceinline__ void dot_rows(const uint8_t *__restrict__ W, size_t pitch,
                                          uint32_t row0, uint32_t rows_valid, uint32_t nchunks,
                                          const float *__restrict__ xs, uint32_t xs_stride,
-                                         float (&acc)[R][NV]) {
+                                         float (&acc)[R][NV], const RowPrefetch<R> &pre,
+                                         bool use_pre) {
     constexpr int E = WTraits<WT>::kElems;
+    constexpr int BATCH = kBatch;
     const uint32_t lane = threadIdx.x & 31u;
 #pragma unroll
     for (int r = 0; r < R; ++r)
@@ -64,13 +92,15 @@ __device__ __forceinline__ void dot_rows(const uint8_t *__restrict__ W, size_t p
 
     for (uint32_t c0 = lane; c0 < nchunks; c0 += 32u * BATCH) {
         uint4 w[BATCH][R];
+        const bool first = use_pre && c0 == lane;
 #pragma unroll
         for (int b = 0; b < BATCH; ++b) {
             const uint32_t c = c0 + 32u * b;
 #pragma unroll
             for (int r = 0; r < R; ++r)
-                w[b][r] = (c < nchunks && r < int(rows_valid)) ? ldg_nc(rowp[r] + size_t(c) * 16)
-                                                               : make_uint4(0, 0, 0, 0);
+                w[b][r] = first ? pre.w[b][r]
+                                : ((c < nchunks && r < int(rows_valid)) ? ldg_nc(rowp[r] + size_t(c) * 16)
+                                                                        : make_uint4(0, 0, 0, 0));
         }
 #pragma unroll
         for (int b = 0; b < BATCH; ++b) {

@@ -141,6 +141,7 @@ __global__ void __launch_bounds__(kThreads) spec_kernel(opure_spec_args a) {
     int32_t *out = a.out_tokens + size_t(s) * (k + 1);
 
     grid_dependency_wait();
+    grid_dependents_launch();
     if (a.mode == OPURE_SPEC_GREEDY) {
         uint32_t acc = 0;
         for (; acc < k; ++acc) {
@@ -214,6 +215,7 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(const float *logits, u
     __shared__ double dred[32];
     __shared__ uint32_t pick;
     grid_dependency_wait();
+    grid_dependents_launch();
     const float *p = logits + size_t(blockIdx.x) * V;
     const double pm = block_max_logit(p, V, red);
     double z = 0.0;

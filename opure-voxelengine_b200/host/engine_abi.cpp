@@ -1,0 +1,281 @@
+// engine_abi.cpp -- extern "C" surface of the host engine (include/opure_engine.h).
+#include <cstring>
+#include <exception>
+#include <new>
+#include <string>
+
+#include "opure_engine.h"
+#include "platform.h"
+#include "synth.h"
+#include "voxel_engine.h"
+
+struct opure_engine {
+    opure::engine::VoxelEngine eng;
+    std::string err;
+};
+
+namespace {
+
+thread_local std::string g_create_error;
+
+// Runs `fn`, turning exceptions into a status and a stored message.
+template <class F>
+opure_status Guard(opure_engine *e, F &&fn) {
+    try {
+        fn();
+        return OPURE_OK;
+    } catch (const opure::Error &x) {
+        if (e) e->err = x.what();
+        return x.status() != OPURE_OK ? x.status() : OPURE_ERR_INVALID_ARG;
+    } catch (const std::bad_alloc &) {
+        if (e) e->err = "host out of memory";
+        return OPURE_ERR_OUT_OF_MEMORY;
+    } catch (const std::exception &x) {
+        if (e) e->err = x.what();
+        return OPURE_ERR_INVALID_ARG;
+    }
+}
+
+std::vector<uint32_t> ToU32(const int32_t *t, uint32_t n) {
+    std::vector<uint32_t> v(n);
+    for (uint32_t i = 0; i < n; ++i) {
+        OPURE_CHECK(t[i] >= 0, "negative token id");
+        v[i] = uint32_t(t[i]);
+    }
+    return v;
+}
+
+}  // namespace
+
+extern "C" {
+
+opure_status opure_engine_create(const char *model_dir, int device, const opure_engine_options *o,
+                                 opure_engine **out) {
+    if (!model_dir || !out) return OPURE_ERR_INVALID_ARG;
+    *out = nullptr;
+    auto *e = new (std::nothrow) opure_engine;
+    if (!e) return OPURE_ERR_OUT_OF_MEMORY;
+    const opure_status s = Guard(e, [&] {
+        opure::engine::EngineOptions opts;
+        if (o) {
+            if (o->max_new_tokens) opts.maxNewTokens = o->max_new_tokens;
+            if (o->max_batch) opts.maxBatch = o->max_batch;
+            opts.maxLen = o->max_len;
+            if (o->page_size) opts.pageSize = o->page_size;
+            opts.pageSeed = o->page_seed;
+            opts.useGraphs = o->use_graphs != 0;
+            if (o->attn_scale != 0.f) opts.attnScale = o->attn_scale;
+        }
+        e->eng.Initialize(model_dir, opts, device);
+    });
+    if (s != OPURE_OK) {
+        g_create_error = e->err;
+        delete e;
+        return s;
+    }
+    *out = e;
+    return OPURE_OK;
+}
+
+opure_status opure_engine_destroy(opure_engine *e) {
+    if (!e) return OPURE_ERR_INVALID_ARG;
+    delete e;
+    return OPURE_OK;
+}
+
+const char *opure_engine_last_error(opure_engine *e) { return e ? e->err.c_str() : g_create_error.c_str(); }
+
+opure_ctx *opure_engine_ctx(opure_engine *e) { return e ? e->eng.Ctx() : nullptr; }
+
+namespace {
+
+void FillInfo(const opure::graph::Graph &g, opure_engine_info *info) {
+    const auto &c = g.Config();
+    const auto &p = g.Plan();
+    std::memset(info, 0, sizeof(*info));
+    info->vocab = c.vocabSize;
+    info->hidden = c.hiddenSize;
+    info->inter = c.intermediateSize;
+    info->layers = c.numLayers;
+    info->heads = c.numHeads;
+    info->kv_heads = c.numKvHeads;
+    info->head_dim = c.HeadDim();
+    info->max_pos = c.maxPositions;
+    info->w_dtype = p.wDtype;
+    info->weight_bytes = p.weightBytes;
+    const uint64_t eb = p.wDtype == OPURE_W_Q8 ? 1 : 2;
+    const uint64_t h = c.hiddenSize, ff = c.intermediateSize;
+    const uint64_t perLayer = (uint64_t(c.QkvRows()) * h + h * h + 3 * ff * h) * eb + 2 * h * 2;
+    info->stream_bytes = perLayer * c.numLayers + uint64_t(c.vocabSize) * h * (p.lmQuantized ? 1 : 2) + h * 2;
+    info->kv_bytes_per_token = c.KvBytesPerToken();
+}
+
+}  // namespace
+
+opure_status opure_engine_get_info(opure_engine *e, opure_engine_info *info) {
+    if (!e || !info) return OPURE_ERR_INVALID_ARG;
+    return Guard(e, [&] {
+        FillInfo(e->eng.GraphModel(), info);
+        info->max_len = e->eng.MaxLen();
+        info->max_batch = e->eng.Options().maxBatch;
+        info->page_size = e->eng.Options().pageSize;
+    });
+}
+
+opure_status opure_model_inspect(const char *model_dir, opure_engine_info *info, char *err, size_t err_len) {
+    if (!model_dir || !info) return OPURE_ERR_INVALID_ARG;
+    opure_engine scratch;
+    const opure_status s = Guard(&scratch, [&] {
+        opure::graph::Graph g;
+        g.LoadConfigOnly(model_dir);
+        FillInfo(g, info);
+    });
+    if (s != OPURE_OK && err && err_len) {
+        std::strncpy(err, scratch.err.c_str(), err_len - 1);
+        err[err_len - 1] = 0;
+    }
+    return s;
+}
+
+opure_status opure_engine_generate(opure_engine *e, const int32_t *prompts, const uint32_t *lens,
+                                   uint32_t n_seq, uint32_t budget, int32_t *out, opure_generate_timing *t) {
+    if (!e || !prompts || !lens || !out || n_seq == 0) return OPURE_ERR_INVALID_ARG;
+    return Guard(e, [&] {
+        std::vector<std::vector<uint32_t>> ps(n_seq);
+        size_t off = 0;
+        for (uint32_t i = 0; i < n_seq; ++i) {
+            ps[i] = ToU32(prompts + off, lens[i]);
+            off += lens[i];
+        }
+        opure::engine::StepTiming st;
+        const auto res = e->eng.GenerateBatch(ps, budget, &st);
+        for (uint32_t i = 0; i < n_seq; ++i)
+            for (uint32_t k = 0; k < budget; ++k) out[size_t(i) * budget + k] = int32_t(res[i].generated[k]);
+        if (t) {
+            t->prefill_ms = st.prefillMs;
+            t->decode_ms = st.decodeMs;
+            t->prefill_steps = st.prefillSteps;
+            t->decode_steps = st.decodeSteps;
+        }
+    });
+}
+
+opure_status opure_engine_prefill(opure_engine *e, const int32_t *tokens, uint32_t n, int32_t *next) {
+    if (!e || !tokens || n == 0) return OPURE_ERR_INVALID_ARG;
+    return Guard(e, [&] {
+        const uint32_t t = e->eng.Prefill(ToU32(tokens, n));
+        if (next) *next = int32_t(t);
+    });
+}
+
+opure_status opure_engine_decode_step(opure_engine *e, const int32_t *tokens, const int32_t *positions,
+                                      uint32_t n, int32_t *next) {
+    if (!e || !tokens || !positions || !next || n == 0) return OPURE_ERR_INVALID_ARG;
+    return Guard(e, [&] { e->eng.DecodeStepBatch(tokens, positions, n, next); });
+}
+
+opure_status opure_engine_run_steps(opure_engine *e, uint32_t n, uint32_t steps) {
+    if (!e) return OPURE_ERR_INVALID_ARG;
+    return Guard(e, [&] { e->eng.RunSteps(n, steps, false); });
+}
+
+opure_status opure_engine_set_positions(opure_engine *e, const int32_t *positions, uint32_t n) {
+    if (!e || !positions) return OPURE_ERR_INVALID_ARG;
+    return Guard(e, [&] { e->eng.SetPositions(positions, n); });
+}
+
+opure_status opure_engine_sync(opure_engine *e) {
+    if (!e) return OPURE_ERR_INVALID_ARG;
+    return Guard(e, [&] { e->eng.Sync(); });
+}
+
+opure_status opure_engine_forward_logits(opure_engine *e, const int32_t *tokens, uint32_t n, float *logits) {
+    if (!e || !tokens || !logits || n == 0) return OPURE_ERR_INVALID_ARG;
+    return Guard(e, [&] {
+        std::vector<float> l;
+        e->eng.ForwardLogits(ToU32(tokens, n), l);
+        std::memcpy(logits, l.data(), l.size() * 4);
+    });
+}
+
+opure_status opure_engine_forward_argmax(opure_engine *e, const int32_t *tokens, uint32_t n, int32_t *out) {
+    if (!e || !tokens || !out || n == 0) return OPURE_ERR_INVALID_ARG;
+    return Guard(e, [&] { *out = int32_t(e->eng.ForwardArgMax(ToU32(tokens, n))); });
+}
+
+opure_status opure_engine_trace(opure_engine *e, int32_t token, uint32_t n_layers, float *trace) {
+    if (!e || !trace || token < 0) return OPURE_ERR_INVALID_ARG;
+    return Guard(e, [&] {
+        std::vector<std::vector<float>> tr;
+        e->eng.RunLayersTraced(uint32_t(token), n_layers, tr);
+        for (size_t l = 0; l < tr.size(); ++l) std::memcpy(trace + l * tr[l].size(), tr[l].data(), tr[l].size() * 4);
+    });
+}
+
+opure_status opure_engine_poison(opure_engine *e, float value) {
+    if (!e) return OPURE_ERR_INVALID_ARG;
+    return Guard(e, [&] { e->eng.PoisonBanks(value); });
+}
+
+opure_status opure_engine_load_kv(opure_engine *e, uint32_t seq, const uint16_t *kv, uint32_t len) {
+    if (!e || !kv) return OPURE_ERR_INVALID_ARG;
+    return Guard(e, [&] { e->eng.LoadKv(seq, kv, len); });
+}
+
+// ---- synthetic inputs -------------------------------------------------------
+opure_status opure_synth_model(const char *dir, const opure_synth_spec *s) {
+    if (!dir || !s) return OPURE_ERR_INVALID_ARG;
+    return Guard(nullptr, [&] {
+        opure::synth::ModelSpec m;
+        m.vocab = s->vocab;
+        m.hidden = s->hidden;
+        m.inter = s->inter;
+        m.layers = s->layers;
+        m.heads = s->heads;
+        m.kv_heads = s->kv_heads;
+        m.max_pos = s->max_pos;
+        m.eps = s->eps;
+        m.theta = s->theta;
+        m.tied = s->tied != 0;
+        m.seed = s->seed;
+        m.std = s->std;
+        m.int8 = s->int8 != 0;
+        m.noise_seed = s->noise_seed;
+        m.noise_std = s->noise_std;
+        opure::synth::WriteModel(dir, m);
+    });
+}
+
+opure_status opure_synth_normal_f16(uint64_t seed, float stddev, uint64_t n, uint16_t *out) {
+    if (!out) return OPURE_ERR_INVALID_ARG;
+    return Guard(nullptr, [&] {
+        const auto v = opure::synth::NormalF16(seed, stddev, n);
+        std::memcpy(out, v.data(), n * 2);
+    });
+}
+
+opure_status opure_synth_prompt(uint64_t seed, uint32_t vocab, uint32_t n, int32_t *out) {
+    if (!out || vocab == 0) return OPURE_ERR_INVALID_ARG;
+    return Guard(nullptr, [&] {
+        const auto v = opure::synth::Prompt(seed, vocab, n);
+        std::memcpy(out, v.data(), size_t(n) * 4);
+    });
+}
+
+opure_status opure_synth_permutation(uint64_t seed, uint32_t n, int32_t *out) {
+    if (!out) return OPURE_ERR_INVALID_ARG;
+    return Guard(nullptr, [&] {
+        const auto v = opure::synth::Permutation(seed, n);
+        std::memcpy(out, v.data(), size_t(n) * 4);
+    });
+}
+
+opure_status opure_synth_uniforms(uint64_t seed, uint64_t n, float *out) {
+    if (!out) return OPURE_ERR_INVALID_ARG;
+    return Guard(nullptr, [&] {
+        const auto v = opure::synth::Uniforms(seed, n);
+        std::memcpy(out, v.data(), n * 4);
+    });
+}
+
+}  // extern "C"

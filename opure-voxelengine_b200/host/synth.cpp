@@ -1,0 +1,205 @@
+// synth.cpp -- seeded synthetic model and input generation.
+#include "synth.h"
+
+#include <sys/stat.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <sstream>
+
+#include "platform.h"
+#include "streamer.h"
+
+namespace opure::synth {
+
+double Normal::Next() {
+    if (has_) {
+        has_ = false;
+        return spare_;
+    }
+    const double u1 = rng_.NextOpen(), u2 = rng_.NextOpen();
+    const double r = std::sqrt(-2.0 * std::log(u1));
+    const double a = 2.0 * M_PI * u2;
+    spare_ = r * std::sin(a);
+    has_ = true;
+    return r * std::cos(a);
+}
+
+std::vector<uint16_t> NormalF16(uint64_t seed, float stddev, uint64_t n) {
+    Normal g(seed);
+    std::vector<uint16_t> out(n);
+    for (uint64_t i = 0; i < n; ++i) out[i] = safetensors::F32ToF16(float(g.Next() * stddev));
+    return out;
+}
+
+std::vector<int32_t> Prompt(uint64_t seed, uint32_t vocab, uint32_t n) {
+    Rng r(seed);
+    std::vector<int32_t> out(n);
+    for (uint32_t i = 0; i < n; ++i) out[i] = int32_t(r.NextU32() % vocab);
+    return out;
+}
+
+std::vector<int32_t> Permutation(uint64_t seed, uint32_t n) {
+    std::vector<int32_t> p(n);
+    for (uint32_t i = 0; i < n; ++i) p[i] = int32_t(i);
+    Rng r(seed);
+    for (uint32_t i = n; i > 1; --i) {
+        const uint32_t j = r.NextU32() % i;
+        std::swap(p[i - 1], p[j]);
+    }
+    return p;
+}
+
+std::vector<float> Uniforms(uint64_t seed, uint64_t n) {
+    Rng r(seed);
+    std::vector<float> out(n);
+    for (uint64_t i = 0; i < n; ++i) out[i] = float(double(r.NextU32()) / 4294967296.0);
+    return out;
+}
+
+namespace {
+
+struct Entry {
+    std::string name;
+    std::string dtype;
+    std::vector<uint64_t> shape;
+    std::vector<uint8_t> bytes;
+    float scale = 1.0f;
+    bool has_scale = false;
+};
+
+// Per-tensor symmetric int8: scale = absmax / 127, round half to even, clamp +-127.
+void Quantize(const std::vector<uint16_t> &w, std::vector<uint8_t> &q, float &scale) {
+    float amax = 0.f;
+    for (uint16_t h : w) amax = std::fmax(amax, std::fabs(safetensors::F16ToF32(h)));
+    scale = amax > 0.f ? amax / 127.0f : 1.0f;
+    q.resize(w.size());
+    for (size_t i = 0; i < w.size(); ++i) {
+        float r = std::nearbyint(safetensors::F16ToF32(w[i]) / scale);
+        r = std::fmin(127.f, std::fmax(-127.f, r));
+        q[i] = uint8_t(int8_t(r));
+    }
+}
+
+void MkDirs(const std::string &dir) {
+    std::string cur;
+    std::stringstream ss(dir);
+    std::string part;
+    if (!dir.empty() && dir[0] == '/') cur = "/";
+    while (std::getline(ss, part, '/')) {
+        if (part.empty()) continue;
+        cur += part + "/";
+        ::mkdir(cur.c_str(), 0755);
+    }
+}
+
+}  // namespace
+
+void WriteModel(const std::string &dir, const ModelSpec &s) {
+    OPURE_CHECK(s.heads && s.kv_heads && s.hidden % s.heads == 0 && s.heads % s.kv_heads == 0,
+                "synthetic model: inconsistent head counts");
+    MkDirs(dir);
+    const uint64_t h = s.hidden, ff = s.inter, hd = s.hidden / s.heads, kvh = uint64_t(s.kv_heads) * hd;
+    Normal g(s.seed);
+    Normal noise(s.noise_seed);
+    std::vector<Entry> entries;
+
+    auto matrix = [&](const std::string &name, uint64_t rows, uint64_t cols, bool quantizable) {
+        std::vector<uint16_t> w(rows * cols);
+        for (auto &x : w) {
+            float v = safetensors::F16ToF32(safetensors::F32ToF16(float(g.Next() * s.std)));
+            if (s.noise_std > 0.f) v = v + float(noise.Next() * s.noise_std);
+            x = safetensors::F32ToF16(v);
+        }
+        Entry e;
+        e.name = name;
+        e.shape = {rows, cols};
+        if (s.int8 && quantizable) {
+            e.dtype = "I8";
+            Quantize(w, e.bytes, e.scale);
+            e.has_scale = true;
+        } else {
+            e.dtype = "F16";
+            e.bytes.resize(w.size() * 2);
+            std::memcpy(e.bytes.data(), w.data(), e.bytes.size());
+        }
+        entries.push_back(std::move(e));
+    };
+    auto ones = [&](const std::string &name, uint64_t n) {
+        Entry e;
+        e.name = name;
+        e.dtype = "F16";
+        e.shape = {n};
+        std::vector<uint16_t> w(n, 0x3C00);  // 1.0
+        e.bytes.resize(n * 2);
+        std::memcpy(e.bytes.data(), w.data(), e.bytes.size());
+        entries.push_back(std::move(e));
+    };
+
+    matrix("model.embed_tokens.weight", s.vocab, h, false);
+    for (uint32_t l = 0; l < s.layers; ++l) {
+        const std::string p = "model.layers." + std::to_string(l) + ".";
+        ones(p + "input_layernorm.weight", h);
+        matrix(p + "self_attn.q_proj.weight", h, h, true);
+        matrix(p + "self_attn.k_proj.weight", kvh, h, true);
+        matrix(p + "self_attn.v_proj.weight", kvh, h, true);
+        matrix(p + "self_attn.o_proj.weight", h, h, true);
+        ones(p + "post_attention_layernorm.weight", h);
+        matrix(p + "mlp.gate_proj.weight", ff, h, true);
+        matrix(p + "mlp.up_proj.weight", ff, h, true);
+        matrix(p + "mlp.down_proj.weight", h, ff, true);
+    }
+    ones("model.norm.weight", h);
+    if (!s.tied) matrix("lm_head.weight", s.vocab, h, false);
+
+    // Header JSON with payload-relative offsets.
+    std::ostringstream hdr;
+    hdr << "{\"__metadata__\":{\"format\":\"pt\"}";
+    uint64_t off = 0;
+    for (const Entry &e : entries) {
+        hdr << ",\"" << e.name << "\":{\"dtype\":\"" << e.dtype << "\",\"shape\":[";
+        for (size_t i = 0; i < e.shape.size(); ++i) hdr << (i ? "," : "") << e.shape[i];
+        hdr << "],\"data_offsets\":[" << off << "," << off + e.bytes.size() << "]";
+        if (e.has_scale) {
+            char buf[64];
+            std::snprintf(buf, sizeof(buf), "%.9g", double(e.scale));
+            hdr << ",\"scale\":" << buf;
+        }
+        hdr << "}";
+        off += e.bytes.size();
+    }
+    hdr << "}";
+    std::string header = hdr.str();
+    while (header.size() % 8) header += ' ';  // payload 8-byte aligned
+
+    const std::string tmp = dir + "/model.safetensors.tmp";
+    {
+        std::ofstream f(tmp, std::ios::binary);
+        OPURE_CHECK(bool(f), "cannot write " + tmp);
+        const uint64_t hl = header.size();
+        f.write(reinterpret_cast<const char *>(&hl), 8);
+        f.write(header.data(), std::streamsize(header.size()));
+        for (const Entry &e : entries) f.write(reinterpret_cast<const char *>(e.bytes.data()), std::streamsize(e.bytes.size()));
+        OPURE_CHECK(bool(f), "short write to " + tmp);
+    }
+    OPURE_CHECK(std::rename(tmp.c_str(), (dir + "/model.safetensors").c_str()) == 0, "rename failed");
+
+    std::ostringstream cfg;
+    char eps[32], theta[32];
+    std::snprintf(eps, sizeof(eps), "%.9g", double(s.eps));
+    std::snprintf(theta, sizeof(theta), "%.17g", s.theta);
+    cfg << "{\n  \"architectures\": [\"LlamaForCausalLM\"],\n  \"model_type\": \"llama\",\n"
+        << "  \"hidden_act\": \"silu\",\n  \"vocab_size\": " << s.vocab << ",\n  \"hidden_size\": " << s.hidden
+        << ",\n  \"intermediate_size\": " << s.inter << ",\n  \"num_hidden_layers\": " << s.layers
+        << ",\n  \"num_attention_heads\": " << s.heads << ",\n  \"num_key_value_heads\": " << s.kv_heads
+        << ",\n  \"max_position_embeddings\": " << s.max_pos << ",\n  \"rms_norm_eps\": " << eps
+        << ",\n  \"rope_theta\": " << theta << ",\n  \"tie_word_embeddings\": " << (s.tied ? "true" : "false")
+        << ",\n  \"torch_dtype\": \"float16\"\n}\n";
+    std::ofstream c(dir + "/config.json");
+    c << cfg.str();
+    OPURE_CHECK(bool(c), "cannot write config.json");
+}
+
+}  // namespace opure::synth

@@ -1,0 +1,507 @@
+// voxel_engine.cpp -- decode engine on top of the C ABI (see voxel_engine.h).
+#include "voxel_engine.h"
+
+#include <algorithm>
+#include <cstring>
+
+#include "platform.h"
+
+namespace opure::engine {
+
+namespace {
+
+template <typename T>
+T *Alloc(opure_ctx *ctx, size_t count) {
+    void *p = nullptr;
+    OPURE_CUDA_CHECK(opure_alloc(ctx, std::max<size_t>(count * sizeof(T), 16), &p));
+    return static_cast<T *>(p);
+}
+
+const uint8_t *At(const void *base, uint64_t off) { return static_cast<const uint8_t *>(base) + off; }
+
+}  // namespace
+
+VoxelEngine::~VoxelEngine() { Shutdown(); }
+
+void VoxelEngine::Shutdown() {
+    if (!ctx_) return;
+    opure_sync(ctx_, 60000);
+    for (auto &kv : graphs_) opure_graph_free(kv.second);
+    graphs_.clear();
+    kv_.Destroy();
+    for (void *p : {static_cast<void *>(buf_.x), static_cast<void *>(buf_.qkv), static_cast<void *>(buf_.q),
+                    static_cast<void *>(buf_.attn), static_cast<void *>(buf_.h), static_cast<void *>(buf_.logits),
+                    static_cast<void *>(buf_.keys), static_cast<void *>(buf_.seq), static_cast<void *>(buf_.pos),
+                    static_cast<void *>(buf_.seqLen), static_cast<void *>(buf_.known), static_cast<void *>(buf_.flags),
+                    static_cast<void *>(buf_.inTokens), static_cast<void *>(buf_.tokens), weights_})
+        if (p) opure_free(ctx_, p);
+    for (auto &s : attnScratch_) opure_free(ctx_, s.second.first);
+    attnScratch_.clear();
+    if (hostIo_) opure_free_host(ctx_, hostIo_);
+    hostIo_ = nullptr;
+    buf_ = Buffers{};
+    weights_ = nullptr;
+    opure_shutdown(ctx_);
+    ctx_ = nullptr;
+    graph_.Release();
+    ready_ = false;
+}
+
+void VoxelEngine::Initialize(const std::string &modelDir, const EngineOptions &opts, int device) {
+    Shutdown();
+    OPURE_CHECK(!opts.enablePlasticity, "the SignSGD plasticity pass is not part of this engine");
+    OPURE_CHECK(opts.maxBatch >= 1, "maxBatch must be at least 1");
+    opts_ = opts;
+    OPURE_CUDA_CHECK(opure_init(device, &ctx_));
+    graph::LayoutOptions lo;
+    lo.fusedLayouts = false;
+    graph_.LoadConfigOnly(modelDir, lo);
+    const graph::ModelConfig &cfg = graph_.Config();
+    const graph::VramPlan &plan = graph_.Plan();
+
+    OPURE_CUDA_CHECK(opure_alloc(ctx_, plan.weightBytes, &weights_));
+    graph_.UploadWeights(ctx_, weights_);
+
+    maxLen_ = opts.maxLen ? std::min(opts.maxLen, cfg.maxPositions) : std::min(cfg.maxPositions, 4096u);
+    const uint32_t pagesPerSeq = (maxLen_ + opts.pageSize - 1) / opts.pageSize;
+    kv_.Create(ctx_, cfg, opts.pageSize, pagesPerSeq * opts.maxBatch, opts.maxBatch, pagesPerSeq, opts.pageSeed);
+    AllocBuffers();
+    seqLen_ = 0;
+    ready_ = true;
+}
+
+void VoxelEngine::AllocBuffers() {
+    const graph::ModelConfig &c = graph_.Config();
+    const uint32_t B = opts_.maxBatch;
+    buf_.x = Alloc<float>(ctx_, size_t(B) * c.hiddenSize);
+    buf_.qkv = Alloc<float>(ctx_, size_t(B) * c.QkvRows());
+    buf_.q = Alloc<float>(ctx_, size_t(B) * c.numHeads * c.HeadDim());
+    buf_.attn = Alloc<float>(ctx_, size_t(B) * c.hiddenSize);
+    buf_.h = Alloc<float>(ctx_, size_t(B) * c.intermediateSize);
+    buf_.logits = Alloc<float>(ctx_, size_t(B) * c.vocabSize);
+    buf_.keys = Alloc<unsigned long long>(ctx_, B);
+    buf_.seq = Alloc<int32_t>(ctx_, B);
+    buf_.pos = Alloc<int32_t>(ctx_, B);
+    buf_.seqLen = Alloc<int32_t>(ctx_, B);
+    buf_.known = Alloc<int32_t>(ctx_, B);
+    buf_.flags = Alloc<uint32_t>(ctx_, B);
+    buf_.inTokens = Alloc<int32_t>(ctx_, B);
+    buf_.tokens = Alloc<int32_t>(ctx_, size_t(B) * maxLen_);
+    OPURE_CUDA_CHECK(opure_fill(ctx_, buf_.keys, 0, sizeof(unsigned long long) * B));
+    OPURE_CUDA_CHECK(opure_fill(ctx_, buf_.tokens, 0, sizeof(int32_t) * size_t(B) * maxLen_));
+    // Pinned staging for the host-driven step: [in_tokens B][positions B][keys B (u64)].
+    OPURE_CUDA_CHECK(opure_alloc_host(ctx_, size_t(B) * 16, &hostIo_));
+    OPURE_CUDA_CHECK(opure_sync(ctx_, 60000));
+}
+
+void *VoxelEngine::AttnScratch(uint32_t n, size_t *bytes) {
+    auto it = attnScratch_.find(n);
+    if (it == attnScratch_.end()) {
+        const graph::ModelConfig &c = graph_.Config();
+        const size_t b = opure_attention_scratch_bytes(n, 1, c.numHeads, c.numKvHeads, c.HeadDim(), maxLen_, 0);
+        OPURE_CHECK(b > 0, "attention scratch size query failed");
+        void *p = nullptr;
+        OPURE_CUDA_CHECK(opure_alloc(ctx_, b, &p));
+        OPURE_CUDA_CHECK(opure_fill(ctx_, p, 0, b));  // split counters start at zero
+        it = attnScratch_.emplace(n, std::make_pair(p, b)).first;
+    }
+    *bytes = it->second.second;
+    return it->second.first;
+}
+
+opure_step_io VoxelEngine::StepIO(uint32_t n) const {
+    const graph::ModelConfig &c = graph_.Config();
+    opure_step_io io{};
+    io.nvec = n;
+    io.seq = buf_.seq;
+    io.pos = buf_.pos;
+    io.seq_len = buf_.seqLen;
+    io.known = buf_.known;
+    io.flags = buf_.flags;
+    io.in_tokens = buf_.inTokens;
+    io.tokens = buf_.tokens;
+    io.max_len = maxLen_;
+    io.keys = buf_.keys;
+    io.embed = reinterpret_cast<const uint16_t *>(At(weights_, graph_.Plan().embedTokens));
+    io.vocab = c.vocabSize;
+    io.hidden = c.hiddenSize;
+    io.x = buf_.x;
+    return io;
+}
+
+void VoxelEngine::RecordLayer(uint32_t L, uint32_t n) {
+    const graph::ModelConfig &c = graph_.Config();
+    const graph::VramPlan &plan = graph_.Plan();
+    const graph::VramPlan::LayerTensors &t = plan.layers[L];
+    const uint32_t h = c.hiddenSize, ff = c.intermediateSize, hd = c.HeadDim();
+    const uint32_t qkvRows = c.QkvRows();
+    const bool q8 = plan.wDtype == OPURE_W_Q8;
+    const uint64_t eb = q8 ? 1 : 2;
+
+    auto gemv = [&](const void *w, float scale, float scale2, uint32_t rows, uint32_t cols,
+                    const float *x, uint32_t xs, float *y, uint32_t ys, uint32_t pro,
+                    const void *gain, uint32_t epi, const float *res) {
+        opure_gemv_args a{};
+        a.w = w;
+        a.w_dtype = plan.wDtype;
+        a.scale_w = scale;
+        a.scale_x = 1.0f;  // activations stay fp32 (Opure_VoxelEngine.cpp:200-206)
+        a.scale_w2 = scale2;
+        a.rows = rows;
+        a.cols = cols;
+        a.nvec = n;
+        a.x = x;
+        a.x_stride = xs;
+        a.y = y;
+        a.y_stride = ys;
+        a.prologue = pro;
+        a.norm_gain = static_cast<const uint16_t *>(gain);
+        a.eps = c.rmsNormEps;
+        a.epilogue = epi;
+        a.residual = res;
+        OPURE_CUDA_CHECK(opure_gemv(ctx_, &a));
+    };
+    const void *inNorm = At(weights_, t.inputNorm), *postNorm = At(weights_, t.postAttNorm);
+
+    // q;k;v in one pass over the concatenated rows (three passes for int8, whose
+    // per-tensor scales differ).
+    if (!q8) {
+        gemv(At(weights_, t.wqkv), 1.f, 1.f, qkvRows, h, buf_.x, h, buf_.qkv, qkvRows, OPURE_PRO_RMSNORM,
+             inNorm, OPURE_EPI_STORE, nullptr);
+    } else {
+        const uint32_t qr = c.numHeads * hd, kr = c.numKvHeads * hd;
+        gemv(At(weights_, t.wqkv), t.sq, t.sq, qr, h, buf_.x, h, buf_.qkv, qkvRows, OPURE_PRO_RMSNORM,
+             inNorm, OPURE_EPI_STORE, nullptr);
+        gemv(At(weights_, t.wqkv + uint64_t(qr) * h * eb), t.sk, t.sk, kr, h, buf_.x, h, buf_.qkv + qr, qkvRows,
+             OPURE_PRO_RMSNORM, inNorm, OPURE_EPI_STORE, nullptr);
+        gemv(At(weights_, t.wqkv + uint64_t(qr + kr) * h * eb), t.sv, t.sv, kr, h, buf_.x, h, buf_.qkv + qr + kr,
+             qkvRows, OPURE_PRO_RMSNORM, inNorm, OPURE_EPI_STORE, nullptr);
+    }
+    const opure_kv_layout kv = kv_.Layout(L);
+    OPURE_CUDA_CHECK(opure_rope_kv_append(ctx_, buf_.qkv, qkvRows, buf_.q, buf_.seq, buf_.pos, n, c.numHeads,
+                                          c.ropeTheta, &kv));
+    opure_attn_args a{};
+    a.q = buf_.q;
+    a.out = buf_.attn;
+    a.seq = buf_.seq;
+    a.seq_len = buf_.seqLen;
+    a.n = n;
+    a.n_q = 1;
+    a.n_heads = c.numHeads;
+    a.scale = opts_.attnScale;
+    a.max_ctx = maxLen_;
+    a.split_tokens = 0;
+    a.scratch = AttnScratch(n, &a.scratch_bytes);
+    a.kv = kv;
+    OPURE_CUDA_CHECK(opure_attention(ctx_, &a));
+    // o_proj + residual, in place on the residual stream.
+    gemv(At(weights_, t.wo), t.so, t.so, h, h, buf_.attn, h, buf_.x, h, OPURE_PRO_NONE, nullptr, OPURE_EPI_ADD,
+         buf_.x);
+    // gate;up with the post-attention norm, SwiGLU epilogue.
+    gemv(At(weights_, t.wgu), t.sgate, t.sup, ff, h, buf_.x, h, buf_.h, ff, OPURE_PRO_RMSNORM, postNorm,
+         OPURE_EPI_SWIGLU, nullptr);
+    // down_proj + residual.
+    gemv(At(weights_, t.wdown), t.sdown, t.sdown, h, ff, buf_.h, ff, buf_.x, h, OPURE_PRO_NONE, nullptr,
+         OPURE_EPI_ADD, buf_.x);
+}
+
+void VoxelEngine::RecordStep(uint32_t n, bool logits) {
+    const graph::ModelConfig &c = graph_.Config();
+    const graph::VramPlan &plan = graph_.Plan();
+    const opure_step_io io = StepIO(n);
+    OPURE_CUDA_CHECK(opure_step_begin(ctx_, &io));
+    for (uint32_t L = 0; L < c.numLayers; ++L) RecordLayer(L, n);
+    // Final norm + (tied) LM head + argmax (Opure_VoxelEngine.cpp:514-532, ArgMax :783-791).
+    opure_gemv_args a{};
+    a.w = At(weights_, plan.lmHead);
+    a.w_dtype = plan.lmQuantized ? uint32_t(OPURE_W_Q8) : uint32_t(OPURE_W_F16);
+    a.scale_w = plan.slm;
+    a.scale_x = 1.0f;
+    a.rows = c.vocabSize;
+    a.cols = c.hiddenSize;
+    a.nvec = n;
+    a.x = buf_.x;
+    a.x_stride = c.hiddenSize;
+    a.y = logits ? buf_.logits : nullptr;
+    a.y_stride = c.vocabSize;
+    a.prologue = OPURE_PRO_RMSNORM;
+    a.norm_gain = reinterpret_cast<const uint16_t *>(At(weights_, plan.finalNorm));
+    a.eps = c.rmsNormEps;
+    a.epilogue = OPURE_EPI_ARGMAX;
+    a.argmax_keys = buf_.keys;
+    OPURE_CUDA_CHECK(opure_gemv(ctx_, &a));
+    OPURE_CUDA_CHECK(opure_step_end(ctx_, &io));
+}
+
+void VoxelEngine::RunSteps(uint32_t n, uint32_t steps, bool logits) {
+    OPURE_CHECK(ready_, "engine used before Initialize");
+    OPURE_CHECK(n >= 1 && n <= opts_.maxBatch, "batch exceeds maxBatch");
+    if (!opts_.useGraphs) {
+        for (uint32_t s = 0; s < steps; ++s) RecordStep(n, logits);
+        return;
+    }
+    const auto key = std::make_pair(n, logits);
+    auto it = graphs_.find(key);
+    if (it == graphs_.end()) {
+        size_t dummy = 0;
+        AttnScratch(n, &dummy);  // allocate outside the capture
+        OPURE_CUDA_CHECK(opure_sync(ctx_, 60000));
+        OPURE_CUDA_CHECK(opure_graph_begin(ctx_));
+        try {
+            RecordStep(n, logits);
+        } catch (...) {
+            opure_graph *g = nullptr;
+            opure_graph_end(ctx_, &g);
+            if (g) opure_graph_free(g);
+            throw;
+        }
+        opure_graph *g = nullptr;
+        OPURE_CUDA_CHECK(opure_graph_end(ctx_, &g));
+        it = graphs_.emplace(key, g).first;
+    }
+    for (uint32_t s = 0; s < steps; ++s) OPURE_CUDA_CHECK(opure_graph_launch(ctx_, it->second));
+}
+
+void VoxelEngine::SetPositions(const int32_t *positions, uint32_t n) {
+    OPURE_CHECK(n >= 1 && n <= opts_.maxBatch, "batch exceeds maxBatch");
+    for (uint32_t v = 0; v < n; ++v) {
+        OPURE_CHECK(positions[v] >= 0 && uint32_t(positions[v]) < maxLen_, "position exceeds maxLen");
+        OPURE_CHECK(uint32_t(positions[v]) < kv_.MappedPages(v) * kv_.PageSize(),
+                    "position beyond the sequence's reserved KV pages");
+    }
+    // Pageable source: the copy is staged before opure_h2d returns, so the caller's
+    // array may be reused immediately.
+    OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.pos, positions, n * 4));
+}
+
+void VoxelEngine::Sync() {
+    OPURE_CUDA_CHECK(opure_sync(ctx_, 600000));
+    const opure_status st = opure_last_error(ctx_);
+    if (st != OPURE_OK) ThrowError(std::string("device reported: ") + opure_strerror(st), st);
+}
+
+void VoxelEngine::ResetSequences(const std::vector<std::vector<uint32_t>> &prompts, uint32_t reserve,
+                                 bool automatic) {
+    const uint32_t n = uint32_t(prompts.size());
+    OPURE_CHECK(n >= 1 && n <= opts_.maxBatch, "batch exceeds maxBatch");
+    OPURE_CHECK(reserve <= maxLen_, "sequence exceeds the engine's maxLen");
+    const graph::ModelConfig &c = graph_.Config();
+    std::vector<int32_t> seq(n), pos(n, 0), known(n);
+    std::vector<uint32_t> flags(n, automatic ? OPURE_VEC_AUTO : 0u);
+    for (uint32_t v = 0; v < n; ++v) {
+        OPURE_CHECK(!prompts[v].empty(), "empty prompt");
+        OPURE_CHECK(prompts[v].size() <= reserve, "prompt exceeds the reserved length");
+        for (uint32_t t : prompts[v]) OPURE_CHECK(t < c.vocabSize, "token id out of vocabulary range");
+        seq[v] = int32_t(v);
+        known[v] = int32_t(prompts[v].size());
+        kv_.Release(v);
+        OPURE_CHECK(kv_.Reserve(v, reserve), "KV cache has no room for the sequence");
+        std::vector<int32_t> row(prompts[v].begin(), prompts[v].end());
+        OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.tokens + size_t(v) * maxLen_, row.data(), row.size() * 4));
+        OPURE_CUDA_CHECK(opure_sync(ctx_, 60000));
+    }
+    kv_.SyncTable();
+    OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.seq, seq.data(), n * 4));
+    OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.pos, pos.data(), n * 4));
+    OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.known, known.data(), n * 4));
+    OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.flags, flags.data(), n * 4));
+    hostDriven_ = !automatic;
+    OPURE_CUDA_CHECK(opure_fill(ctx_, buf_.keys, 0, n * 8));
+    OPURE_CUDA_CHECK(opure_sync(ctx_, 60000));
+}
+
+std::vector<GenerateResult> VoxelEngine::GenerateBatch(const std::vector<std::vector<uint32_t>> &prompts,
+                                                       uint32_t budget, StepTiming *timing) {
+    OPURE_CHECK(ready_, "engine used before Initialize");
+    const uint32_t n = uint32_t(prompts.size());
+    uint32_t maxP = 0;
+    for (const auto &p : prompts) maxP = std::max<uint32_t>(maxP, uint32_t(p.size()));
+    // The reference stops when seqLen + 1 >= maxPos (Opure_VoxelEngine.cpp:932).
+    OPURE_CHECK(maxP + budget < maxLen_, "prompt + budget exceeds the engine's maxLen");
+    ResetSequences(prompts, maxP + budget, true);
+
+    opure_event *e0 = nullptr, *e1 = nullptr, *e2 = nullptr;
+    OPURE_CUDA_CHECK(opure_event_create(ctx_, &e0));
+    OPURE_CUDA_CHECK(opure_event_create(ctx_, &e1));
+    OPURE_CUDA_CHECK(opure_event_create(ctx_, &e2));
+    OPURE_CUDA_CHECK(opure_event_record(ctx_, e0));
+    RunSteps(n, maxP, false);
+    OPURE_CUDA_CHECK(opure_event_record(ctx_, e1));
+    RunSteps(n, budget, false);
+    OPURE_CUDA_CHECK(opure_event_record(ctx_, e2));
+    Sync();
+    float pre = 0.f, dec = 0.f;
+    OPURE_CUDA_CHECK(opure_event_elapsed_ms(e0, e1, &pre));
+    OPURE_CUDA_CHECK(opure_event_elapsed_ms(e1, e2, &dec));
+    opure_event_free(e0);
+    opure_event_free(e1);
+    opure_event_free(e2);
+
+    std::vector<int32_t> rows(size_t(n) * maxLen_);
+    OPURE_CUDA_CHECK(opure_d2h(ctx_, rows.data(), buf_.tokens, rows.size() * 4));
+    OPURE_CUDA_CHECK(opure_sync(ctx_, 60000));
+    std::vector<GenerateResult> out(n);
+    for (uint32_t v = 0; v < n; ++v) {
+        GenerateResult &r = out[v];
+        r.promptTokens = prompts[v];
+        const size_t b = size_t(v) * maxLen_ + prompts[v].size();
+        r.generated.assign(rows.begin() + b, rows.begin() + b + budget);
+        r.msPerToken = budget ? double(dec) / budget : 0.0;
+        r.lastMs = r.msPerToken;
+    }
+    if (timing) {
+        timing->prefillMs = pre;
+        timing->decodeMs = dec;
+        timing->prefillSteps = maxP;
+        timing->decodeSteps = budget;
+    }
+    seqLen_ = maxP + budget;
+    lastTokenMs_ = budget ? double(dec) / budget : 0.0;
+    return out;
+}
+
+GenerateResult VoxelEngine::Generate(const std::vector<uint32_t> &tokens, const EngineOptions &opts) {
+    GenerateResult r;
+    r.promptTokens = tokens;
+    if (tokens.empty()) return r;
+    // No tokenizer is loaded (token-id workloads), so there is no <|endoftext|> id to stop on.
+    const uint32_t budget = std::min(opts.maxNewTokens, opts_.maxNewTokens);
+    return GenerateBatch({tokens}, budget).front();
+}
+
+uint32_t VoxelEngine::Prefill(const std::vector<uint32_t> &tokens) {
+    OPURE_CHECK(!tokens.empty(), "Prefill called with no tokens");
+    ResetSequences({tokens}, uint32_t(tokens.size()), true);
+    RunSteps(1, uint32_t(tokens.size()), false);
+    Sync();
+    unsigned long long key = 0;
+    OPURE_CUDA_CHECK(opure_d2h(ctx_, &key, buf_.keys, 8));
+    OPURE_CUDA_CHECK(opure_sync(ctx_, 60000));
+    seqLen_ = uint32_t(tokens.size());
+    return 0xffffffffu - uint32_t(key & 0xffffffffull);  // ArgMaxFrom (:962-988)
+}
+
+uint32_t VoxelEngine::ForwardArgMax(const std::vector<uint32_t> &tokens) {
+    OPURE_CHECK(!tokens.empty(), "ForwardArgMax called with no tokens");
+    ResetSequences({tokens}, uint32_t(tokens.size()), true);
+    RunSteps(1, uint32_t(tokens.size()), false);
+    Sync();
+    unsigned long long key = 0;
+    OPURE_CUDA_CHECK(opure_d2h(ctx_, &key, buf_.keys, 8));
+    OPURE_CUDA_CHECK(opure_sync(ctx_, 60000));
+    seqLen_ = uint32_t(tokens.size());
+    return 0xffffffffu - uint32_t(key & 0xffffffffull);
+}
+
+void VoxelEngine::ForwardLogits(const std::vector<uint32_t> &tokens, std::vector<float> &logitsOut) {
+    OPURE_CHECK(!tokens.empty(), "ForwardLogits called with no tokens");
+    ResetSequences({tokens}, uint32_t(tokens.size()), true);
+    RunSteps(1, uint32_t(tokens.size()), true);
+    Sync();
+    logitsOut.assign(graph_.Config().vocabSize, 0.f);
+    OPURE_CUDA_CHECK(opure_d2h(ctx_, logitsOut.data(), buf_.logits, logitsOut.size() * 4));
+    OPURE_CUDA_CHECK(opure_sync(ctx_, 60000));
+    seqLen_ = uint32_t(tokens.size());
+}
+
+void VoxelEngine::DecodeStepBatch(const int32_t *tokens, const int32_t *positions, uint32_t n, int32_t *next) {
+    OPURE_CHECK(n >= 1 && n <= opts_.maxBatch, "batch exceeds maxBatch");
+    auto *io = static_cast<int32_t *>(hostIo_);
+    for (uint32_t v = 0; v < n; ++v) {
+        OPURE_CHECK(positions[v] >= 0 && uint32_t(positions[v]) < maxLen_,
+                    "decode position exceeds the engine's maxLen");
+        OPURE_CHECK(tokens[v] >= 0 && uint32_t(tokens[v]) < graph_.Config().vocabSize,
+                    "token id out of vocabulary range");
+        OPURE_CHECK(kv_.Reserve(v, uint32_t(positions[v]) + 1), "KV cache has no room for the sequence");
+        io[v] = tokens[v];
+        io[opts_.maxBatch + v] = positions[v];
+    }
+    kv_.SyncTable();
+    if (!hostDriven_) {
+        // Token and position now come from the host: clear the self-driving flag.
+        const std::vector<uint32_t> zero(opts_.maxBatch, 0u);
+        OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.flags, zero.data(), zero.size() * 4));
+        hostDriven_ = true;
+    }
+    // One H2D each for tokens and positions (pinned), one step, one 8-byte-per-sequence
+    // readback: the reference's DecodeStep round trip (Opure_VoxelEngine.cpp:765-800).
+    OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.inTokens, io, n * 4));
+    OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.pos, io + opts_.maxBatch, n * 4));
+    RunSteps(n, 1, false);
+    auto *keys = reinterpret_cast<unsigned long long *>(io + 2 * opts_.maxBatch);
+    OPURE_CUDA_CHECK(opure_d2h(ctx_, keys, buf_.keys, n * 8));
+    OPURE_CUDA_CHECK(opure_sync(ctx_, 600000));
+    for (uint32_t v = 0; v < n; ++v) next[v] = int32_t(0xffffffffu - uint32_t(keys[v] & 0xffffffffull));
+}
+
+uint32_t VoxelEngine::DecodeStep(uint32_t tokenId, uint32_t position) {
+    OPURE_CHECK(position < graph_.Config().maxPositions, "decode position exceeds max_position_embeddings");
+    const int32_t t = int32_t(tokenId), p = int32_t(position);
+    int32_t next = 0;
+    DecodeStepBatch(&t, &p, 1, &next);
+    seqLen_ = position + 1;
+    return uint32_t(next);
+}
+
+void VoxelEngine::RunLayersTraced(uint32_t tokenId, uint32_t nLayers, std::vector<std::vector<float>> &trace) {
+    OPURE_CHECK(ready_, "engine used before Initialize");
+    const graph::ModelConfig &c = graph_.Config();
+    nLayers = std::min(nLayers, c.numLayers);
+    ResetSequences({{tokenId}}, 1, true);
+    const opure_step_io io = StepIO(1);
+    OPURE_CUDA_CHECK(opure_step_begin(ctx_, &io));
+    trace.assign(nLayers, std::vector<float>(c.hiddenSize));
+    for (uint32_t L = 0; L < nLayers; ++L) {
+        RecordLayer(L, 1);
+        OPURE_CUDA_CHECK(opure_d2h(ctx_, trace[L].data(), buf_.x, c.hiddenSize * 4));
+    }
+    Sync();
+}
+
+void VoxelEngine::PoisonBanks(float fill) {
+    const graph::ModelConfig &c = graph_.Config();
+    const uint32_t B = opts_.maxBatch;
+    auto poison = [&](float *p, size_t n) {
+        std::vector<float> pat(n, fill);
+        OPURE_CUDA_CHECK(opure_h2d(ctx_, p, pat.data(), n * 4));
+        OPURE_CUDA_CHECK(opure_sync(ctx_, 60000));
+    };
+    poison(buf_.x, size_t(B) * c.hiddenSize);
+    poison(buf_.qkv, size_t(B) * c.QkvRows());
+    poison(buf_.q, size_t(B) * c.numHeads * c.HeadDim());
+    poison(buf_.attn, size_t(B) * c.hiddenSize);
+    poison(buf_.h, size_t(B) * c.intermediateSize);
+    poison(buf_.logits, size_t(B) * c.vocabSize);
+}
+
+void VoxelEngine::LoadKv(uint32_t seq, const uint16_t *kvData, uint32_t len) {
+    const graph::ModelConfig &c = graph_.Config();
+    OPURE_CHECK(seq < opts_.maxBatch && len <= maxLen_, "LoadKv: sequence or length out of range");
+    OPURE_CHECK(kv_.Reserve(seq, std::max(len, 1u)), "KV cache has no room for the sequence");
+    kv_.SyncTable();
+    const uint32_t P = kv_.PageSize(), hd = c.HeadDim(), nkv = c.numKvHeads;
+    const std::vector<int32_t> &table = kv_.HostTable();
+    for (uint32_t L = 0; L < c.numLayers; ++L) {
+        uint8_t *pool = reinterpret_cast<uint8_t *>(kv_.Pool(L));
+        for (uint32_t sel = 0; sel < 2; ++sel)
+            for (uint32_t g = 0; g < nkv; ++g)
+                for (uint32_t lp = 0; lp * P < len; ++lp) {
+                    const uint32_t ntok = std::min(P, len - lp * P);
+                    const int32_t page = table[size_t(seq) * kv_.MaxPages() + lp];
+                    const uint16_t *src = kvData + ((((size_t(L) * 2 + sel) * nkv + g) * len) + size_t(lp) * P) * hd;
+                    uint8_t *dst = pool + ((size_t(page) * 2 + sel) * nkv + g) * size_t(P) * hd * 2;
+                    OPURE_CUDA_CHECK(opure_h2d(ctx_, dst, src, size_t(ntok) * hd * 2));
+                }
+        OPURE_CUDA_CHECK(opure_sync(ctx_, 600000));
+    }
+}
+
+VoxelEngine::MetricsSnapshot VoxelEngine::SnapshotMetrics() const {
+    MetricsSnapshot m;
+    if (kv_.NumPages()) m.kvOccupancy = 1.0f - float(kv_.FreePages()) / float(kv_.NumPages());
+    m.tokensPerSec = lastTokenMs_ > 0 ? float(1000.0 / lastTokenMs_) : 0.0f;
+    m.memoryPressure = 0.0f;
+    return m;
+}
+
+}  // namespace opure::engine

@@ -1,0 +1,160 @@
+// voxel_engine.h -- the decode engine: prefill, decode step and generate loop.
+//
+// Keeps the API of the reference's engine::VoxelEngine (src/engine/Opure_VoxelEngine.h:
+// EngineOptions :54-65, GenerateResult :99-109, Initialize, Generate, ForwardArgMax,
+// ForwardLogits, Prefill, DecodeStep, ArgMaxFrom-style readback, RunLayersTraced,
+// PoisonBanks, SnapshotMetrics, CurrentPosition), and adds batched generation over
+// independent sequences. All device work goes through the C ABI of libopure_cuda
+// (include/opure_cuda.h); nothing here computes on the CPU.
+//
+// One decode step runs, for every active token vector:
+//   step_begin (token pick + embedding gather)
+//   per layer: q;k;v GEMV with fused RMSNorm prologue -> RoPE + paged fp16 KV append
+//              -> split-K paged attention -> o_proj GEMV + residual
+//              -> gate;up GEMV with fused RMSNorm prologue and SwiGLU epilogue
+//              -> down_proj GEMV + residual
+//   lm_head GEMV with fused final RMSNorm and argmax epilogue, step_end.
+// The reference records the same graph as ~423 dispatches with a UAV barrier before each
+// (Opure_VoxelEngine.cpp:189-536) and waits on a fence every token; here the step is
+// captured once into a CUDA graph (kernels chained with programmatic dependent launch)
+// and replayed, and the token loop runs on the device without host round trips.
+#pragma once
+
+#include <cstdint>
+#include <map>
+#include <string>
+#include <utility>
+#include <vector>
+
+#include "graph.h"
+#include "kv_cache.h"
+#include "opure_cuda.h"
+
+namespace opure::engine {
+
+struct EngineOptions {
+    bool enablePlasticity = false;  // the SignSGD side feature is not part of this engine
+    uint32_t maxNewTokens = 256;
+    float temperature = 0.0f;       // 0 = greedy (the only mode Generate uses, as the reference)
+    // B200 engine options.
+    uint32_t maxBatch = 1;          // token vectors per step
+    uint32_t maxLen = 0;            // tokens per sequence (0: min(max_positions, 4096))
+    uint32_t pageSize = 64;         // KV page size in tokens
+    uint64_t pageSeed = 3;          // free-list shuffle (0: pages in order)
+    bool useGraphs = true;
+    float attnScale = 1.0f;         // 1.0 = the reference's unscaled scores
+};
+
+struct GenerateResult {
+    std::vector<uint32_t> promptTokens;
+    std::vector<uint32_t> generated;
+    uint32_t stopToken = 0;
+    bool hitStop = false;
+    double msPerToken = 0.0;
+    double lastMs = 0.0;
+};
+
+struct StepTiming {
+    double prefillMs = 0.0;   // device time of the prefill steps
+    double decodeMs = 0.0;    // device time of the decode steps
+    uint32_t prefillSteps = 0, decodeSteps = 0;
+};
+
+class VoxelEngine {
+public:
+    VoxelEngine() = default;
+    ~VoxelEngine();
+    VoxelEngine(const VoxelEngine &) = delete;
+    VoxelEngine &operator=(const VoxelEngine &) = delete;
+
+    // Loads the model onto `device`: layout plan, weight upload, KV pool, buffers.
+    void Initialize(const std::string &modelDir, const EngineOptions &opts, int device);
+    void Shutdown();
+    bool IsReady() const { return ready_; }
+
+    const graph::Graph &GraphModel() const { return graph_; }
+    const graph::ModelConfig &Model() const { return graph_.Config(); }
+    opure_ctx *Ctx() const { return ctx_; }
+    uint32_t MaxLen() const { return maxLen_; }
+    const EngineOptions &Options() const { return opts_; }
+
+    // Prefill `tokens`, then `opts.maxNewTokens` greedy steps (Opure_VoxelEngine.cpp:894-958).
+    GenerateResult Generate(const std::vector<uint32_t> &tokens, const EngineOptions &opts);
+    // Independent sequences, one per token vector (at most maxBatch), same budget each.
+    std::vector<GenerateResult> GenerateBatch(const std::vector<std::vector<uint32_t>> &prompts,
+                                              uint32_t budget, StepTiming *timing = nullptr);
+
+    uint32_t ForwardArgMax(const std::vector<uint32_t> &tokens);
+    void ForwardLogits(const std::vector<uint32_t> &tokens, std::vector<float> &logitsOut);
+
+    // Host-driven steps, the reference's Prefill + DecodeStep contract: each DecodeStep
+    // copies the token in, runs one step and reads the 8-byte argmax result back.
+    // Returns the argmax of the last prompt position (Prefill + ArgMaxFrom).
+    uint32_t Prefill(const std::vector<uint32_t> &tokens);
+    uint32_t DecodeStep(uint32_t tokenId, uint32_t position);
+    // The same for n sequences at once (slots 0..n-1): tokens/positions in, next tokens out.
+    void DecodeStepBatch(const int32_t *tokens, const int32_t *positions, uint32_t n, int32_t *next);
+
+    // Embedding + the first nLayers layers for one token at position 0; the residual
+    // after each layer (Opure_VoxelEngine.cpp:546-587).
+    void RunLayersTraced(uint32_t tokenId, uint32_t nLayers, std::vector<std::vector<float>> &trace);
+    // Fills the activation buffers with `fill` (Opure_VoxelEngine.cpp:625-636).
+    void PoisonBanks(float fill);
+
+    // Loads precomputed fp16 K/V [L][2][n_kv][len][hd] for sequence slot `seq` and marks
+    // `len` positions as cached (synthetic long contexts).
+    void LoadKv(uint32_t seq, const uint16_t *kv, uint32_t len);
+
+    struct MetricsSnapshot {
+        float kvOccupancy = 0.0f;
+        float tokensPerSec = 0.0f;
+        float memoryPressure = 0.0f;
+        float speculativeAcceptance = -1.0f;
+    };
+    MetricsSnapshot SnapshotMetrics() const;
+    uint32_t CurrentPosition() const { return seqLen_; }
+
+    // Enqueues `steps` decode steps for the first n vectors (graph replays when enabled).
+    void RunSteps(uint32_t n, uint32_t steps, bool logits);
+    // Rewinds the positions of vectors 0..n-1 (stream-ordered, no wait).
+    void SetPositions(const int32_t *positions, uint32_t n);
+    void Sync();
+
+    struct Buffers {
+        float *x = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr, *h = nullptr;
+        float *logits = nullptr;
+        unsigned long long *keys = nullptr;
+        int32_t *seq = nullptr, *pos = nullptr, *seqLen = nullptr, *known = nullptr;
+        uint32_t *flags = nullptr;
+        int32_t *inTokens = nullptr;
+        int32_t *tokens = nullptr;
+    };
+    const Buffers &Buf() const { return buf_; }
+
+private:
+    void AllocBuffers();
+    void RecordStep(uint32_t n, bool logits);
+    void RecordLayer(uint32_t layer, uint32_t n);
+    // Split-K attention scratch for batch n (one zeroed buffer per batch size, so its
+    // split counters always start at zero).
+    void *AttnScratch(uint32_t n, size_t *bytes);
+    void ResetSequences(const std::vector<std::vector<uint32_t>> &prompts, uint32_t reserve, bool automatic);
+    opure_step_io StepIO(uint32_t n) const;
+
+    opure_ctx *ctx_ = nullptr;
+    graph::Graph graph_;
+    kv::PagedKvCache kv_;
+    EngineOptions opts_{};
+    void *weights_ = nullptr;
+    Buffers buf_{};
+    uint32_t maxLen_ = 0;
+    bool ready_ = false;
+    uint32_t seqLen_ = 0;
+    double lastTokenMs_ = 0.0;
+    std::map<std::pair<uint32_t, bool>, opure_graph *> graphs_;
+    std::map<uint32_t, std::pair<void *, size_t>> attnScratch_;
+    void *hostIo_ = nullptr;  // pinned staging of the host-driven step
+    bool hostDriven_ = false; // step flags currently cleared for host-supplied tokens
+};
+
+}  // namespace opure::engine

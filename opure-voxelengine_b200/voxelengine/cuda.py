@@ -42,10 +42,18 @@ class AttnArgs(C.Structure):
 
 
 class GemvArgs(C.Structure):
-    _fields_ = [("w", P), ("w_dtype", u32), ("scale_w", f32), ("scale_x", f32), ("rows", u32),
+    _fields_ = [("w", P), ("w_dtype", u32), ("scale_w", f32), ("scale_x", f32),
+                ("scale_w2", f32), ("rows", u32),
                 ("cols", u32), ("nvec", u32), ("x", P), ("x_stride", u32), ("y", P),
                 ("y_stride", u32), ("prologue", u32), ("norm_gain", P), ("eps", f32),
                 ("epilogue", u32), ("residual", P), ("argmax_keys", P)]
+
+
+class StepIO(C.Structure):
+    _fields_ = [("nvec", u32), ("seq", P), ("pos", P), ("seq_len", P), ("known", P),
+                ("flags", P), ("in_tokens", P), ("tokens", P), ("max_len", u32), ("keys", P),
+                ("embed", P),
+                ("vocab", u32), ("hidden", u32), ("x", P)]
 
 
 class SpecArgs(C.Structure):
@@ -75,10 +83,11 @@ _SIGS = {
     "opure_rmsnorm": [P, P, P, P, u32, u32, f32],
     "opure_swiglu": [P, P, P, P, u32], "opure_add": [P, P, P, P, u32],
     "opure_argmax": [P, P, u32, u32, P, P],
-    "opure_rope_kv_append": [P, P, P, P, P, P, u32, u32, C.c_double, P],
+    "opure_rope_kv_append": [P, P, u32, P, P, P, u32, u32, C.c_double, P],
     "opure_attention": [P, P], "opure_gemv": [P, P], "opure_argmax_decode": [P, P, u32, P, P],
     "opure_spec_accept": [P, P], "opure_sample_softmax": [P, P, u32, u32, P, P],
     "opure_debug_inject_failure": [P, u32, u32],
+    "opure_step_begin": [P, P], "opure_step_end": [P, P],
 }
 
 

@@ -1,0 +1,239 @@
+"""ctypes binding of libopure_engine.so (include/opure_engine.h): the C++20 host engine
+and the seeded synthetic-input generators. No fallback: a missing library raises."""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+from . import cuda
+
+LIB_PATH = os.path.join(cuda.PKG, "libopure_engine.so")
+P, u32, u64, f32, i32, f64 = C.c_void_p, C.c_uint32, C.c_uint64, C.c_float, C.c_int32, C.c_double
+
+
+class EngineOptions(C.Structure):
+    _fields_ = [("max_new_tokens", u32), ("max_batch", u32), ("max_len", u32), ("page_size", u32),
+                ("page_seed", u64), ("use_graphs", u32), ("attn_scale", f32)]
+
+
+class EngineInfo(C.Structure):
+    _fields_ = [("vocab", u32), ("hidden", u32), ("inter", u32), ("layers", u32), ("heads", u32),
+                ("kv_heads", u32), ("head_dim", u32), ("max_pos", u32), ("max_len", u32),
+                ("max_batch", u32), ("page_size", u32), ("w_dtype", u32), ("weight_bytes", u64),
+                ("stream_bytes", u64), ("kv_bytes_per_token", u64)]
+
+
+class Timing(C.Structure):
+    _fields_ = [("prefill_ms", f64), ("decode_ms", f64), ("prefill_steps", u32),
+                ("decode_steps", u32)]
+
+
+class SynthSpec(C.Structure):
+    _fields_ = [("vocab", u32), ("hidden", u32), ("inter", u32), ("layers", u32), ("heads", u32),
+                ("kv_heads", u32), ("max_pos", u32), ("eps", f32), ("theta", f64), ("tied", u32),
+                ("seed", u64), ("std", f32), ("int8", u32), ("noise_seed", u64),
+                ("noise_std", f32)]
+
+
+# SmolLM-135M shape (BASELINE configs 0/2/3) and the 1.7B shape (config 4).
+SMOLLM_135M = dict(vocab=49152, hidden=576, inter=1536, layers=30, heads=9, kv_heads=3,
+                   max_pos=2048, eps=1e-5, theta=10000.0)
+LLAMA_1_7B = dict(vocab=49152, hidden=2048, inter=8192, layers=24, heads=32, kv_heads=32,
+                  max_pos=8192, eps=1e-5, theta=10000.0)
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        cuda.lib()  # libopure_cuda first (RTLD_GLOBAL)
+        if not os.path.exists(LIB_PATH):
+            raise OSError(f"{LIB_PATH} is not built: run __graft_entry__.build()")
+        L = C.CDLL(LIB_PATH, mode=C.RTLD_GLOBAL)
+        sigs = {
+            "opure_engine_create": [C.c_char_p, C.c_int, P, P],
+            "opure_engine_destroy": [P],
+            "opure_engine_get_info": [P, P],
+            "opure_engine_generate": [P, P, P, u32, u32, P, P],
+            "opure_engine_prefill": [P, P, u32, P],
+            "opure_engine_decode_step": [P, P, P, u32, P],
+            "opure_engine_forward_logits": [P, P, u32, P],
+            "opure_engine_run_steps": [P, u32, u32],
+            "opure_engine_set_positions": [P, P, u32],
+            "opure_engine_sync": [P],
+            "opure_engine_forward_argmax": [P, P, u32, P],
+            "opure_engine_trace": [P, i32, u32, P],
+            "opure_engine_poison": [P, f32],
+            "opure_engine_load_kv": [P, u32, P, u32],
+            "opure_model_inspect": [C.c_char_p, P, C.c_char_p, C.c_size_t],
+            "opure_synth_model": [C.c_char_p, P],
+            "opure_synth_normal_f16": [u64, f32, u64, P],
+            "opure_synth_prompt": [u64, u32, u32, P],
+            "opure_synth_permutation": [u64, u32, P],
+            "opure_synth_uniforms": [u64, u64, P],
+        }
+        for name, args in sigs.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = C.c_int
+        L.opure_engine_last_error.argtypes = [P]
+        L.opure_engine_last_error.restype = C.c_char_p
+        L.opure_engine_ctx.argtypes = [P]
+        L.opure_engine_ctx.restype = P
+        _lib = L
+    return _lib
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data_as(P)
+
+
+def _check(status, what, h=None):
+    if status != 0:
+        msg = lib().opure_engine_last_error(h) or b""
+        raise cuda.OpureError(status, f"{what}: {msg.decode(errors='replace')}")
+
+
+# ---- synthetic inputs ---------------------------------------------------------
+def synth_model(path: str, seed: int = 0, std: float = 0.02, int8: bool = False, tied: bool = True,
+                noise_seed: int = 0, noise_std: float = 0.0, **shape) -> str:
+    """Writes config.json + model.safetensors to `path` (skipped when already present with
+    the same spec, recorded in a marker file)."""
+    dims = dict(SMOLLM_135M)
+    dims.update(shape)
+    spec = SynthSpec(dims["vocab"], dims["hidden"], dims["inter"], dims["layers"], dims["heads"],
+                     dims["kv_heads"], dims["max_pos"], dims["eps"], dims["theta"], int(tied), seed,
+                     std, int(int8), noise_seed, noise_std)
+    marker = os.path.join(path, ".synth")
+    want = repr(sorted(dict(dims, seed=seed, std=std, int8=int8, tied=tied, noise_seed=noise_seed,
+                            noise_std=noise_std).items()))
+    if os.path.exists(marker) and open(marker).read() == want and \
+            os.path.exists(os.path.join(path, "model.safetensors")):
+        return path
+    _check(lib().opure_synth_model(path.encode(), C.byref(spec)), "opure_synth_model")
+    with open(marker, "w") as f:
+        f.write(want)
+    return path
+
+
+def normal_f16(seed: int, std: float, n: int) -> np.ndarray:
+    out = np.empty(n, np.uint16)
+    _check(lib().opure_synth_normal_f16(seed, std, n, _p(out)), "opure_synth_normal_f16")
+    return out
+
+
+def prompt(seed: int, vocab: int, n: int) -> np.ndarray:
+    out = np.empty(n, np.int32)
+    _check(lib().opure_synth_prompt(seed, vocab, n, _p(out)), "opure_synth_prompt")
+    return out
+
+
+def permutation(seed: int, n: int) -> np.ndarray:
+    out = np.empty(n, np.int32)
+    _check(lib().opure_synth_permutation(seed, n, _p(out)), "opure_synth_permutation")
+    return out
+
+
+def uniforms(seed: int, n: int) -> np.ndarray:
+    out = np.empty(n, np.float32)
+    _check(lib().opure_synth_uniforms(seed, n, _p(out)), "opure_synth_uniforms")
+    return out
+
+
+def inspect(model_dir: str) -> EngineInfo:
+    """Plans a model without a GPU; raises with the engine's reason on refusal."""
+    info = EngineInfo()
+    err = C.create_string_buffer(4096)
+    st = lib().opure_model_inspect(model_dir.encode(), C.byref(info), err, 4096)
+    if st != 0:
+        raise cuda.OpureError(st, "opure_model_inspect: " + err.value.decode(errors="replace"))
+    return info
+
+
+# ---- engine ----------------------------------------------------------------------
+class Engine:
+    """engine::VoxelEngine on one GPU."""
+
+    def __init__(self, model_dir: str, device: int = 0, max_batch: int = 1, max_len: int = 0,
+                 page_size: int = 64, page_seed: int = 3, use_graphs: bool = True,
+                 attn_scale: float = 1.0, max_new_tokens: int = 256):
+        o = EngineOptions(max_new_tokens, max_batch, max_len, page_size, page_seed,
+                          int(use_graphs), attn_scale)
+        h = C.c_void_p()
+        st = lib().opure_engine_create(model_dir.encode(), device, C.byref(o), C.byref(h))
+        _check(st, "opure_engine_create", None)
+        self.h = h
+        self.info = EngineInfo()
+        _check(lib().opure_engine_get_info(self.h, C.byref(self.info)), "get_info", self.h)
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().opure_engine_destroy(self.h)
+            self.h = None
+
+    __del__ = close
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    @property
+    def ctx(self):
+        return lib().opure_engine_ctx(self.h)
+
+    def generate(self, prompts, budget: int):
+        """prompts: list of token-id sequences; returns (tokens [n][budget], Timing)."""
+        ps = [np.asarray(p, np.int32) for p in prompts]
+        flat = np.ascontiguousarray(np.concatenate(ps), np.int32)
+        lens = np.array([p.size for p in ps], np.uint32)
+        out = np.zeros((len(ps), budget), np.int32)
+        t = Timing()
+        _check(lib().opure_engine_generate(self.h, _p(flat), _p(lens), len(ps), budget, _p(out),
+                                           C.byref(t)), "generate", self.h)
+        return out, t
+
+    def prefill(self, tokens) -> int:
+        """Prefill slot 0; returns the first generated token."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        nxt = C.c_int32()
+        _check(lib().opure_engine_prefill(self.h, _p(t), t.size, C.byref(nxt)), "prefill", self.h)
+        return int(nxt.value)
+
+    def decode_step(self, tokens, positions) -> np.ndarray:
+        t = np.ascontiguousarray(np.atleast_1d(tokens), np.int32)
+        p = np.ascontiguousarray(np.atleast_1d(positions), np.int32)
+        nxt = np.zeros(t.size, np.int32)
+        _check(lib().opure_engine_decode_step(self.h, _p(t), _p(p), t.size, _p(nxt)), "decode_step",
+               self.h)
+        return nxt
+
+    def forward_logits(self, tokens) -> np.ndarray:
+        t = np.ascontiguousarray(tokens, np.int32)
+        out = np.zeros(self.info.vocab, np.float32)
+        _check(lib().opure_engine_forward_logits(self.h, _p(t), t.size, _p(out)), "forward_logits",
+               self.h)
+        return out
+
+    def forward_argmax(self, tokens) -> int:
+        t = np.ascontiguousarray(tokens, np.int32)
+        out = C.c_int32()
+        _check(lib().opure_engine_forward_argmax(self.h, _p(t), t.size, C.byref(out)),
+               "forward_argmax", self.h)
+        return int(out.value)
+
+    def trace(self, token: int, n_layers: int) -> np.ndarray:
+        out = np.zeros((n_layers, self.info.hidden), np.float32)
+        _check(lib().opure_engine_trace(self.h, token, n_layers, _p(out)), "trace", self.h)
+        return out
+
+    def poison(self, value: float):
+        _check(lib().opure_engine_poison(self.h, value), "poison", self.h)
+
+    def load_kv(self, seq: int, kv: np.ndarray, length: int):
+        kv = np.ascontiguousarray(kv, np.uint16)
+        _check(lib().opure_engine_load_kv(self.h, seq, _p(kv), length), "load_kv", self.h)

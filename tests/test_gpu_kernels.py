@@ -313,20 +313,25 @@ def test_rope_kv_append(ctx, pos):
     maxp = pos // page + 1
     perm = rng.permutation(maxp + 2)[:maxp].astype(np.int32)
     pool = np.zeros((maxp + 2, 2, nkv, page, hd), np.uint16)
-    dq, dk, dv = ctx.to_device(q), ctx.to_device(k), ctx.to_device(v)
+    stride = (nh + 2 * nkv) * hd + 8          # padded row: the kernel honours the stride
+    qkv = np.zeros((1, stride), np.float32)
+    qkv[0, : nh * hd], qkv[0, nh * hd:(nh + nkv) * hd] = q[0], k[0]
+    qkv[0, (nh + nkv) * hd:(nh + 2 * nkv) * hd] = v[0]
+    dqkv, dq = ctx.to_device(qkv), ctx.buffer(nh * hd * 4).fill(0xFF)
     dpool, dpt = ctx.to_device(pool), ctx.to_device(perm[None])
     dseq, dpos = ctx.to_device(np.array([0], np.int32)), ctx.to_device(np.array([pos], np.int32))
     kv = cu.KvLayout(dpool.ptr, dpt.ptr, maxp + 2, maxp, page, nkv, hd)
-    ctx.call("opure_rope_kv_append", C.c_void_p(dq.ptr), C.c_void_p(dk.ptr), C.c_void_p(dv.ptr),
+    ctx.call("opure_rope_kv_append", C.c_void_p(dqkv.ptr), stride, C.c_void_p(dq.ptr),
              C.c_void_p(dseq.ptr), C.c_void_p(dpos.ptr), 1, nh, 10000.0, C.byref(kv))
-    gq = dq.download(np.float32, q.shape)[0]
-    gk = dk.download(np.float32, k.shape)[0]
+    gq = dq.download(np.float32, (nh * hd,))
     gpool = dpool.download(np.uint16, pool.shape)
     wq = oracle.rope(q[0], nh, hd, pos, 10000.0)
     wk = oracle.rope(k[0], nkv, hd, pos, 10000.0)
-    assert rel_err(gq, wq) < 1e-6 and rel_err(gk, wk) < 1e-6
+    assert rel_err(gq, wq) < 1e-6
     slot = gpool[perm[pos // page], :, :, pos % page]
-    assert np.array_equal(slot[0], f16(gk).reshape(nkv, hd))
+    # fp16 of the rotated key may differ by one ulp where fp32 rounding of the rotation
+    # straddles an fp16 tie; compare as fp16 values.
+    assert np.abs(oracle.f16_to_f32(slot[0]).ravel() - wk).max() <= 1e-3 * np.abs(wk).max()
     assert np.array_equal(slot[1], f16(v[0]).reshape(nkv, hd))
     assert ctx.last_error() == 0
 
@@ -336,11 +341,12 @@ def test_rope_kv_out_of_range_page_is_refused(ctx):
     # reported through the status word; nothing is written.
     nh, nkv, hd, page = 9, 3, 64, 16
     pool = np.zeros((2, 2, nkv, page, hd), np.uint16)
-    dq, dk, dv = ctx.buffer(nh * hd * 4).fill(0), ctx.buffer(nkv * hd * 4).fill(0), ctx.buffer(nkv * hd * 4).fill(0)
+    stride = (nh + 2 * nkv) * hd
+    dqkv, dq = ctx.buffer(stride * 4).fill(0), ctx.buffer(nh * hd * 4).fill(0)
     dpool, dpt = ctx.to_device(pool), ctx.to_device(np.array([[0, 1]], np.int32))
     dseq, dpos = ctx.to_device(np.array([0], np.int32)), ctx.to_device(np.array([40], np.int32))
     kv = cu.KvLayout(dpool.ptr, dpt.ptr, 2, 2, page, nkv, hd)
-    ctx.call("opure_rope_kv_append", C.c_void_p(dq.ptr), C.c_void_p(dk.ptr), C.c_void_p(dv.ptr),
+    ctx.call("opure_rope_kv_append", C.c_void_p(dqkv.ptr), stride, C.c_void_p(dq.ptr),
              C.c_void_p(dseq.ptr), C.c_void_p(dpos.ptr), 1, nh, 10000.0, C.byref(kv))
     assert ctx.last_error() == cu.ERR_DEVICE_BOUNDS
     assert ctx.last_error() == 0  # cleared by the read
