@@ -291,7 +291,10 @@ def run_ours(args, world, rank, local):
                "sample": f"{done} config-0 decode tokens of one sequence (positions 32..159 cyclic) "
                          f"on the CPU oracle after a {PROMPT_LEN}-token prefill"}
 
-    launches_per_step = 3 + info.layers * (6 if info.w_dtype == cu.W_F16 else 8)
+    # Kernel launches per step: step_begin + step_end + lm_head, plus per layer 3 on the
+    # fused path (B in {1,2,4,8}, fp16) or 6 (8 with int8's separate q/k/v GEMVs) per-op.
+    fused = info.w_dtype == cu.W_F16 and B in (1, 2, 4, 8)
+    launches_per_step = 3 + info.layers * (3 if fused else (6 if info.w_dtype == cu.W_F16 else 8))
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
@@ -330,6 +333,123 @@ def _events(ctx):
     return a, b
 
 
+# ---- kernel workloads: BASELINE configs 1 (attention sweep) and 2 (GEMV shapes) ----------
+def _time_events(ctx, fn, iters, warm=3):
+    """Average device ms of fn() over `iters` launches (CUDA events on the ctx stream)."""
+    import ctypes as C
+
+    from voxelengine import cuda as cu
+    L = cu.lib()
+    for _ in range(warm):
+        fn(0)
+    cu.check(L.opure_sync(ctx.h, 600000), "sync")
+    a, b = _events(ctx.h)
+    cu.check(L.opure_event_record(ctx.h, a), "event")
+    for i in range(iters):
+        fn(i)
+    cu.check(L.opure_event_record(ctx.h, b), "event")
+    ms = C.c_float()
+    cu.check(L.opure_event_elapsed_ms(a, b, C.byref(ms)), "elapsed")
+    L.opure_event_free(a)
+    L.opure_event_free(b)
+    return ms.value / iters
+
+
+def run_attention_sweep(args):
+    """Config 1: paged flash-decode, 9 q heads / 3 kv heads, hd 64, fp16 K/V, page table a
+    seeded permutation (seed 3). K/V values: fp16 N(0,1) from seed 2 (the first 16M draws,
+    tiled across larger pools; the data does not change the kernel's work)."""
+    from voxelengine import cuda as cu
+    from voxelengine import engine as ve
+    peak, kind = peaks()
+    nh, nkv, hd, P = 9, 3, 64, 64
+    base = ve.normal_f16(2, 1.0, 1 << 24)
+    out = []
+    with cu.Ctx(0) as ctx:
+        for B in (1, 8, 64):
+            for ctxlen in (512, 2048, 8192, 32768):
+                pages = B * (ctxlen // P)
+                pool_elems = pages * 2 * nkv * P * hd
+                pool = ctx.buffer(pool_elems * 2)
+                reps = -(-pool_elems // base.size)
+                for r in range(reps):
+                    n = min(base.size, pool_elems - r * base.size)
+                    pool.upload(base[:n], offset=r * base.size * 2)
+                perm = ve.permutation(3, pages).reshape(B, ctxlen // P)
+                q = oracle_free_f16_to_f32(ve.normal_f16(2, 1.0, B * nh * hd))
+                dq, dpt = ctx.to_device(q), ctx.to_device(perm.astype(np.int32))
+                dseq = ctx.to_device(np.arange(B, dtype=np.int32))
+                dlen = ctx.to_device(np.full(B, ctxlen, np.int32))
+                dout = ctx.buffer(B * nh * hd * 4)
+                sb = cu.attention_scratch_bytes(B, 1, nh, nkv, hd, ctxlen)
+                scratch = ctx.buffer(sb).fill(0)
+                a = cu.AttnArgs()
+                a.q, a.out, a.seq, a.seq_len = dq.ptr, dout.ptr, dseq.ptr, dlen.ptr
+                a.n, a.n_q, a.n_heads, a.scale, a.max_ctx = B, 1, nh, 1.0, ctxlen
+                a.scratch, a.scratch_bytes = scratch.ptr, sb
+                a.kv = cu.KvLayout(pool.ptr, dpt.ptr, pages, ctxlen // P, P, nkv, hd)
+                bytes_ = B * ctxlen * 2 * nkv * hd * 2 + B * nh * hd * 8 + B * (ctxlen // P) * 4
+                iters = max(5, min(200, int(2e9 / bytes_)))
+                ms = _time_events(ctx, lambda i: ctx.attention(a), iters)
+                gbs = bytes_ / (ms * 1e-3) / 1e9
+                out.append({"B": B, "ctx": ctxlen, "us": ms * 1e3, "bytes": bytes_, "GB/s": gbs,
+                            "frac": gbs / peak, "l2": "pool > L2" if bytes_ > 126e6 else "pool fits L2 (upper bound)"})
+                for b in (pool, dq, dpt, dseq, dlen, dout, scratch):
+                    b.free()
+    line = {"metric": "paged flash-decode attention HBM GB/s (config 1)", "unit": "GB/s",
+            "peak": peak, "peak_kind": kind, "points": out}
+    print(json.dumps(line), flush=True)
+
+
+def oracle_free_f16_to_f32(h):
+    return np.asarray(h, np.uint16).view(np.float16).astype(np.float32)
+
+
+def run_gemv_sweep(args):
+    """Config 2: GEMV at the projection shapes, fp16 and int8 (GEMV_Quant) weights derived
+    from N(0, 0.02) seed 4, x fp16 N(0,1), n = 1, 5, 9 vectors. Each timed launch reads a
+    different weight copy from a rotating set of >= 256 MB so the bytes come from HBM."""
+    from voxelengine import cuda as cu
+    from voxelengine import engine as ve
+    peak, kind = peaks()
+    out = []
+    with cu.Ctx(0) as ctx:
+        for rows, cols in ((576, 576), (192, 576), (1536, 576), (576, 1536), (49152, 576)):
+            w16 = ve.normal_f16(4, 0.02, rows * cols)
+            wf = oracle_free_f16_to_f32(w16)
+            amax = float(np.abs(wf).max())
+            sq = amax / 127.0
+            q8 = np.clip(np.rint(wf / sq), -127, 127).astype(np.int8)
+            for dtype, wh, eb, scale in ((cu.W_F16, w16, 2, 1.0), (cu.W_Q8, q8, 1, sq)):
+                wbytes = rows * cols * eb
+                copies = max(2, -(-256 * (1 << 20) // wbytes))
+                pool = ctx.buffer(copies * wbytes)
+                for c in range(copies):
+                    pool.upload(wh, offset=c * wbytes)
+                for n in (1, 5, 9):
+                    x = oracle_free_f16_to_f32(ve.normal_f16(4 + n, 1.0, n * cols))
+                    dx, dy = ctx.to_device(x), ctx.buffer(n * rows * 4)
+                    a = cu.GemvArgs()
+                    a.w_dtype, a.scale_w, a.scale_x = dtype, scale, 1.0
+                    a.rows, a.cols, a.nvec = rows, cols, n
+                    a.x, a.x_stride, a.y, a.y_stride = dx.ptr, cols, dy.ptr, rows
+
+                    def launch(i, a=a):
+                        a.w = pool.ptr + (i % copies) * wbytes
+                        ctx.gemv(a)
+                    iters = max(copies, 50)
+                    ms = _time_events(ctx, launch, iters)
+                    bytes_ = wbytes + n * cols * 2 + n * rows * 4 + (4 if dtype == cu.W_Q8 else 0)
+                    gbs = bytes_ / (ms * 1e-3) / 1e9
+                    out.append({"shape": f"{rows}x{cols}", "dtype": "f16" if dtype == cu.W_F16 else "q8",
+                                "n": n, "us": ms * 1e3, "bytes": bytes_, "GB/s": gbs, "frac": gbs / peak})
+                    dx.free()
+                    dy.free()
+                pool.free()
+    print(json.dumps({"metric": "weight-streaming GEMV HBM GB/s (config 2)", "unit": "GB/s", "peak": peak,
+                      "peak_kind": kind, "points": out}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -339,6 +459,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-steps", type=int, default=128)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--workload", choices=["decode", "attn", "gemv"], default="decode")
     ap.add_argument("--quick", action="store_true",
                     help="minimal run for profiler launch lists: no parity, e2e or CPU legs")
     args = ap.parse_args()
@@ -347,6 +468,10 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
+        elif args.workload == "attn":
+            run_attention_sweep(args)
+        elif args.workload == "gemv":
+            run_gemv_sweep(args)
         else:
             run_ours(args, world, rank, local)
     finally:

@@ -250,6 +250,50 @@ typedef struct opure_step_io {
 opure_status opure_step_begin(opure_ctx *ctx, const opure_step_io *io);
 opure_status opure_step_end(opure_ctx *ctx, const opure_step_io *io);
 
+/* ---- fused decode step (latency path, 1..8 token vectors, fp16 weights) ---------------
+ * Enqueues the whole per-layer graph of one decode step as three kernels per layer plus
+ * the lm_head (Opure_VoxelEngine.cpp:189-536 records 14 dispatches per layer):
+ *   A  RMSNorm + q;k;v GEMV + RoPE + fp16 paged-KV append      (one CTA per 8 q;k;v rows)
+ *   B  paged attention + o_proj partial sums into the residual (one CTA per kv head and
+ *      block of o_proj rows; o_proj stored grouped per kv head)
+ *   C  RMSNorm + gate;up GEMV + SwiGLU + down_proj partial sums (one CTA per block of the
+ *      intermediate dimension; down_proj stored transposed)
+ *   L  final RMSNorm + lm_head GEMV + argmax keys (+ logits when `logits` != NULL)
+ * Each kernel copies its whole weight slice into shared memory with a TMA bulk copy before
+ * waiting on its predecessor (programmatic dependent launch), so weight streaming overlaps
+ * the previous kernel. The residual stream is kept as fp32 base vectors plus 64-bit
+ * fixed-point (2^-32) deltas that the B and C partial sums are added to atomically, which
+ * makes the sums independent of arrival order; each kernel rebuilds x = base + delta.
+ * Input: `x` holds the step's embedding rows (opure_step_begin writes them).
+ * Requirements: head_dim 64 or 128, n_heads/n_kv <= 4, hidden % 8 == 0, nvec <= 8. */
+typedef struct opure_fused_layer {
+    const uint16_t *in_norm, *post_norm; /* fp16 [hidden]                                  */
+    const uint16_t *w_qkv;      /* fp16 [(n_heads + 2 n_kv) head_dim][hidden]: q, k, v rows */
+    const uint16_t *w_o_blk;    /* fp16 [n_kv][hidden][G head_dim]: (g, o, c) = Wo[o][g G hd + c] */
+    const uint16_t *w_gate_up;  /* fp16 [2 inter][hidden]: gate rows then up rows          */
+    const uint16_t *w_down_t;   /* fp16 [inter][hidden]: down_proj transposed              */
+    uint16_t *kv_pool;          /* this layer's page pool (layout of opure_kv_layout)      */
+} opure_fused_layer;
+
+typedef struct opure_fused_step {
+    uint32_t nvec, hidden, inter, n_heads, n_kv, head_dim, vocab, n_layers;
+    float eps, attn_scale;
+    double theta;
+    const opure_fused_layer *layers;   /* host array [n_layers], read during the call    */
+    const uint16_t *final_norm;        /* fp16 [hidden]                                  */
+    const uint16_t *lm_head;           /* fp16 [vocab][hidden]                           */
+    const int32_t *page_table;
+    uint32_t n_pages, max_pages, page_size;
+    const int32_t *seq, *pos;          /* [nvec] (pos = position computed by this step)  */
+    float *x;                          /* [nvec][hidden] embedding in, then base buffer 0 */
+    float *base1;                      /* [nvec][hidden]                                 */
+    long long *delta0, *delta1;        /* [nvec][hidden] fixed-point partial sums         */
+    float *q;                          /* [nvec][n_heads head_dim]                        */
+    float *logits;                     /* [nvec][vocab] or NULL                          */
+    unsigned long long *keys;          /* [nvec] argmax keys (zeroed by opure_step_begin) */
+} opure_fused_step;
+opure_status opure_decode_fused(opure_ctx *ctx, const opure_fused_step *s);
+
 /* ---- speculative verify / accept (no reference counterpart: the reference's
  *      SpeculativeVerify pipelines, Opure_SpeculativeDecode.usf:60-189, are never
  *      dispatched and it has no accept logic) ------------------------------- */

@@ -34,7 +34,14 @@ typedef struct opure_engine_options {
     uint64_t page_seed;       /* seeded shuffle of the KV free list (0: in order)      */
     uint32_t use_graphs;      /* 1: capture each step into a CUDA graph                */
     float attn_scale;         /* attention score scale (0: 1.0, the reference's)       */
+    uint32_t path;            /* OPURE_PATH_*: which step kernels to record            */
 } opure_engine_options;
+
+enum {
+    OPURE_PATH_AUTO = 0,      /* fused latency kernels when eligible, else per-op kernels */
+    OPURE_PATH_UNFUSED = 1,   /* per-op kernels: GEMV, RoPE+KV, attention, GEMV, ...      */
+    OPURE_PATH_FUSED = 2      /* opure_decode_fused; creation fails when not eligible     */
+};
 
 typedef struct opure_engine_info {
     uint32_t vocab, hidden, inter, layers, heads, kv_heads, head_dim, max_pos;

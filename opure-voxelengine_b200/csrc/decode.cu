@@ -1,0 +1,533 @@
+// decode.cu -- opure_decode_fused: the latency path of one decode step (1..8 token
+// vectors) as three fused kernels per layer plus the lm_head. See opure_cuda.h for the
+// phase split. Replaces the per-layer dispatch sequence of VoxelEngine::RecordForward
+// (src/engine/Opure_VoxelEngine.cpp:300-491): RMSNorm, GEMV q/k/v, RoPE, Attention,
+// GEMV o, AddRes, RMSNorm, GEMV gate/up, SwiGLU, GEMV down, AddRes.
+#include <algorithm>
+
+#include "attn_core.cuh"
+#include "ctx.cuh"
+#include "gemv.cuh"
+#include "tma.cuh"
+
+namespace opure {
+namespace {
+
+constexpr int kMaxVec = 8;
+
+struct KvParams {
+    uint16_t *pool;
+    const int32_t *page_table;
+    uint32_t n_pages, max_pages, page_size;
+};
+
+// x[v] = base[v] + delta[v] * 2^-32 (rounded to fp32 once, as the reference rounds its fp32
+// residual after every add), staged into xs and RMS-normalised with `gain` in place. The
+// designated CTA also writes the un-normalised x to base_out and zeroes delta_zero.
+template <int NV>
+__device__ __forceinline__ void stage_residual(const float *base, const long long *delta, uint32_t h,
+                                               const __half *gain, float eps, float *xs, float *red,
+                                               float *base_out, long long *delta_zero, bool designated) {
+    for (uint32_t i = threadIdx.x; i < NV * h; i += blockDim.x) {
+        float x = base[i];
+        if (delta) x = float(double(x) + double(__ldcg(delta + i)) * kFixInv);
+        xs[i] = x;
+        if (designated) {
+            if (base_out) base_out[i] = x;
+            if (delta_zero) delta_zero[i] = 0;
+        }
+    }
+    __syncthreads();
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u, nw = blockDim.x >> 5;
+    for (uint32_t v = 0; v < NV; ++v) {
+        float ss = 0.f;
+        for (uint32_t i = threadIdx.x; i < h; i += blockDim.x) ss = fmaf(xs[v * h + i], xs[v * h + i], ss);
+        ss = warp_sum(ss);
+        if (lane == 0) red[v * 32 + warp] = ss;
+    }
+    __syncthreads();
+    if (threadIdx.x < NV) {
+        float t = 0.f;
+        for (uint32_t w = 0; w < nw; ++w) t += red[threadIdx.x * 32 + w];
+        red[32 * NV + threadIdx.x] = float(1.0 / sqrt(double(t) / double(h) + double(eps)));
+    }
+    __syncthreads();
+    for (uint32_t i = threadIdx.x; i < NV * h; i += blockDim.x)
+        xs[i] = xs[i] * red[32 * NV + i / h] * __half2float(gain[i % h]);
+    __syncthreads();
+}
+
+// Dot products of R rows held in shared memory (row r at w + r * pitch bytes) with NV
+// vectors xs[v * h + i]; lanes stride the row's 16-byte chunks. Every lane gets the sums.
+template <int NV, int R>
+__device__ __forceinline__ void smem_dot(const uint8_t *w, uint32_t pitch, uint32_t nrows, uint32_t nchunks,
+                                         const float *xs, uint32_t h, float (&acc)[R][NV]) {
+    const uint32_t lane = threadIdx.x & 31u;
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int v = 0; v < NV; ++v) acc[r][v] = 0.f;
+    for (uint32_t c = lane; c < nchunks; c += 32) {
+        float xf[NV][8];
+#pragma unroll
+        for (int v = 0; v < NV; ++v) {
+            const float4 a = *reinterpret_cast<const float4 *>(xs + v * h + c * 8);
+            const float4 b = *reinterpret_cast<const float4 *>(xs + v * h + c * 8 + 4);
+            xf[v][0] = a.x; xf[v][1] = a.y; xf[v][2] = a.z; xf[v][3] = a.w;
+            xf[v][4] = b.x; xf[v][5] = b.y; xf[v][6] = b.z; xf[v][7] = b.w;
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            if (r >= int(nrows)) break;
+            float wf[8];
+            unpack8(*reinterpret_cast<const uint4 *>(w + size_t(r) * pitch + c * 16), wf);
+#pragma unroll
+            for (int v = 0; v < NV; ++v)
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc[r][v] = fmaf(wf[e], xf[v][e], acc[r][v]);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int v = 0; v < NV; ++v) acc[r][v] = warp_sum(acc[r][v]);
+}
+
+__device__ __forceinline__ __half *kv_slot(const KvParams &kv, uint32_t n_kv, uint32_t hd, int32_t seq,
+                                           int32_t pos, uint32_t sel, uint32_t head, DeviceStatus *st) {
+    const uint32_t lp = uint32_t(pos) / kv.page_size;
+    if (seq < 0 || pos < 0 || lp >= kv.max_pages) {
+        report(st, OPURE_ERR_DEVICE_BOUNDS, 30, uint32_t(pos));
+        return nullptr;
+    }
+    const int32_t page = kv.page_table[size_t(seq) * kv.max_pages + lp];
+    if (page < 0 || uint32_t(page) >= kv.n_pages) {
+        report(st, OPURE_ERR_DEVICE_BOUNDS, 31, uint32_t(page));
+        return nullptr;
+    }
+    const size_t blk = size_t(kv.page_size) * hd;
+    return reinterpret_cast<__half *>(kv.pool) + ((size_t(page) * 2 + sel) * n_kv + head) * blk +
+           size_t(uint32_t(pos) % kv.page_size) * hd;
+}
+
+// ---------------------------------------------------------------------------------------
+// A: RMSNorm + q;k;v GEMV + RoPE + paged KV append.
+constexpr uint32_t kARows = 8;      // rows per CTA: 4 warps x one RoPE pair
+constexpr uint32_t kAThreads = 128;
+
+struct QkvArgs {
+    const __half *w;
+    uint32_t rows, h, n_heads, n_kv, hd;
+    const __half *gain;
+    float eps;
+    double theta;
+    const float *base_in;
+    const long long *delta_in;   // NULL for layer 0 (x is the embedding)
+    float *base_out;
+    long long *delta_zero;
+    float *q_out;
+    KvParams kv;
+    const int32_t *seq, *pos;
+    DeviceStatus *st;
+};
+
+template <int NV>
+__global__ void __launch_bounds__(kAThreads) qkv_fused_kernel(QkvArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t bar;
+    const uint32_t pitch = a.h * 2;
+    const uint32_t row0 = blockIdx.x * kARows;
+    const uint32_t nrows = min(kARows, a.rows - row0);
+    uint8_t *wsm = smem;
+    float *xs = reinterpret_cast<float *>(smem + ((kARows * pitch + 127) & ~127u));
+    float *red = xs + NV * a.h;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        mbar_expect_tx(&bar, nrows * pitch);
+        bulk_load(wsm, reinterpret_cast<const uint8_t *>(a.w) + size_t(row0) * pitch, nrows * pitch, &bar);
+    }
+    grid_dependency_wait();
+    grid_dependents_launch();
+    stage_residual<NV>(a.base_in, a.delta_in, a.h, a.gain, a.eps, xs, red, a.base_out, a.delta_zero,
+                       blockIdx.x == 0);
+    if (!cta_wait_copy(&bar, a.st, 40)) return;
+
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t r = row0 + 2 * warp;  // this warp's RoPE pair (r, r + 1)
+    if (2 * warp >= nrows) return;
+    float acc[2][NV];
+    smem_dot<NV, 2>(wsm + size_t(2 * warp) * pitch, pitch, min(2u, nrows - 2 * warp), pitch / 16, xs, a.h, acc);
+    if (lane >= NV) return;
+    const uint32_t v = lane;
+    float e0 = 0.f, e1 = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+        if (k == int(v)) { e0 = acc[0][k]; e1 = acc[1][k]; }
+    const uint32_t qrows = a.n_heads * a.hd, krows = a.n_kv * a.hd;
+    const int32_t p = a.pos[v], s = a.seq[v];
+    if (r < qrows + krows) {
+        // RoPE, interleaved pairs, theta^(-2*pair/hd) (Opure_RoPE.usf:56), in double.
+        const uint32_t pair = (r % a.hd) / 2;
+        double sn, cs;
+        sincos(double(p) * pow(a.theta, -2.0 * double(pair) / double(a.hd)), &sn, &cs);
+        const float r0 = float(double(e0) * cs - double(e1) * sn);
+        const float r1 = float(double(e0) * sn + double(e1) * cs);
+        if (r < qrows) {
+            a.q_out[size_t(v) * qrows + r] = r0;
+            a.q_out[size_t(v) * qrows + r + 1] = r1;
+        } else {
+            const uint32_t head = (r - qrows) / a.hd;
+            __half *kd = kv_slot(a.kv, a.n_kv, a.hd, s, p, 0, head, a.st);
+            if (kd) {
+                kd[(r - qrows) % a.hd] = __float2half_rn(r0);
+                kd[(r - qrows) % a.hd + 1] = __float2half_rn(r1);
+            }
+        }
+    } else {
+        const uint32_t head = (r - qrows - krows) / a.hd;
+        __half *vd = kv_slot(a.kv, a.n_kv, a.hd, s, p, 1, head, a.st);
+        if (vd) {
+            vd[(r - qrows - krows) % a.hd] = __float2half_rn(e0);
+            vd[(r - qrows - krows) % a.hd + 1] = __float2half_rn(e1);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// B: attention for one kv head + o_proj partial over that head's input columns.
+constexpr uint32_t kBThreads = 256;
+constexpr int kBWarps = kBThreads / 32;
+
+struct AttnOArgs {
+    const __half *w_o_blk;
+    uint32_t h, n_heads, n_kv, rows_per_cta;
+    const float *q;
+    float scale_log2;
+    KvParams kv;
+    const int32_t *seq, *pos;
+    long long *delta_out;   // residual delta the partial sums are added to
+    long long *delta_zero;  // zeroed by the designated CTA for the next kernel
+    DeviceStatus *st;
+};
+
+template <int NV, int HD, int G>
+__global__ void __launch_bounds__(kBThreads) attn_oproj_kernel(AttnOArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ WarpStates<HD, G, kBWarps> ws;
+    __shared__ __align__(16) float attn[NV][G * HD];
+    constexpr uint32_t cols = G * HD, pitch = cols * 2;
+    const uint32_t g = blockIdx.x, rb = blockIdx.y;
+    const uint32_t row0 = rb * a.rows_per_cta;
+    const uint32_t nrows = min(a.rows_per_cta, a.h - row0);
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    uint8_t *wsm = smem;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        mbar_expect_tx(&bar, nrows * pitch);
+        bulk_load(wsm, reinterpret_cast<const uint8_t *>(a.w_o_blk) + (size_t(g) * a.h + row0) * pitch,
+                  nrows * pitch, &bar);
+    }
+    grid_dependency_wait();
+    grid_dependents_launch();
+    if (g == 0 && rb == 0)
+        for (uint32_t i = threadIdx.x; i < NV * a.h; i += blockDim.x) a.delta_zero[i] = 0;
+
+    for (int v = 0; v < NV; ++v) {
+        float qv[G][AttnShape<HD>::E];
+        load_q_slice<HD, G>(a.q + size_t(v) * a.n_heads * HD, g, a.scale_log2, qv);
+        AttnState<HD, G> st;
+        st.init();
+        const int32_t s = a.seq[v];
+        KvView kv{reinterpret_cast<const __half *>(a.kv.pool),
+                  a.kv.page_table + size_t(max(s, 0)) * a.kv.max_pages, a.kv.max_pages, a.kv.n_pages,
+                  a.kv.page_size, a.n_kv, g, s >= 0};
+        attend_range<HD, G>(st, qv, kv, 0, uint32_t(max(a.pos[v] + 1, 0)), warp, kBWarps, a.st);
+        merge_lane_groups<HD, G>(st);
+        store_warp_state<HD, G, kBWarps>(st, ws, warp);
+        __syncthreads();
+        for (uint32_t idx = threadIdx.x; idx < cols; idx += blockDim.x) {
+            float acc, m, l;
+            merge_warps<HD, G, kBWarps>(ws, idx / HD, idx % HD, acc, m, l);
+            attn[v][idx] = acc / fmaxf(l, 1e-30f);
+        }
+        __syncthreads();
+    }
+    if (!cta_wait_copy(&bar, a.st, 41)) return;
+    // o_proj partial: rows of this CTA x this kv head's G*HD input columns.
+    constexpr uint32_t nch = pitch / 16;
+    for (uint32_t rr = warp; rr < nrows; rr += kBWarps) {
+        float acc[NV];
+#pragma unroll
+        for (int v = 0; v < NV; ++v) acc[v] = 0.f;
+        for (uint32_t c = lane; c < nch; c += 32) {
+            float wf[8];
+            unpack8(*reinterpret_cast<const uint4 *>(wsm + size_t(rr) * pitch + c * 16), wf);
+#pragma unroll
+            for (int v = 0; v < NV; ++v)
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc[v] = fmaf(wf[e], attn[v][c * 8 + e], acc[v]);
+        }
+#pragma unroll
+        for (int v = 0; v < NV; ++v) {
+            const float t = warp_sum(acc[v]);
+            if (lane == uint32_t(v))
+                atomicAdd(reinterpret_cast<unsigned long long *>(a.delta_out + size_t(v) * a.h + row0 + rr),
+                          static_cast<unsigned long long>(to_fix(t)));
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// C: RMSNorm + gate;up GEMV + SwiGLU + down_proj partial over a block of F rows of the
+// intermediate dimension.
+constexpr uint32_t kCThreads = 128;
+
+struct MlpArgs {
+    const __half *w_gu, *w_down_t;
+    uint32_t h, ff, F;
+    const __half *gain;
+    float eps;
+    const float *base_in;
+    const long long *delta_in;
+    float *base_out;
+    long long *delta_out;
+    DeviceStatus *st;
+};
+
+template <int NV>
+__global__ void __launch_bounds__(kCThreads) mlp_fused_kernel(MlpArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t bar;
+    const uint32_t pitch = a.h * 2;
+    const uint32_t f0 = blockIdx.x * a.F;
+    const uint32_t nf = min(a.F, a.ff - f0);
+    const uint32_t blk = a.F * pitch;
+    uint8_t *wg = smem, *wu = smem + blk, *wd = smem + 2 * blk;
+    float *xs = reinterpret_cast<float *>(smem + 3 * blk);
+    float *red = xs + NV * a.h;
+    float *hs = red + 33 * NV;  // [F][NV]
+
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        mbar_expect_tx(&bar, 3 * nf * pitch);
+        const uint8_t *w = reinterpret_cast<const uint8_t *>(a.w_gu);
+        bulk_load(wg, w + size_t(f0) * pitch, nf * pitch, &bar);
+        bulk_load(wu, w + (size_t(a.ff) + f0) * pitch, nf * pitch, &bar);
+        bulk_load(wd, reinterpret_cast<const uint8_t *>(a.w_down_t) + size_t(f0) * pitch, nf * pitch, &bar);
+    }
+    grid_dependency_wait();
+    grid_dependents_launch();
+    stage_residual<NV>(a.base_in, a.delta_in, a.h, a.gain, a.eps, xs, red, a.base_out, nullptr,
+                       blockIdx.x == 0);
+    if (!cta_wait_copy(&bar, a.st, 42)) return;
+
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u, nw = kCThreads / 32;
+    for (uint32_t f = warp; f < nf; f += nw) {
+        float acc[1][NV], accu[1][NV];
+        smem_dot<NV, 1>(wg + size_t(f) * pitch, pitch, 1, pitch / 16, xs, a.h, acc);
+        smem_dot<NV, 1>(wu + size_t(f) * pitch, pitch, 1, pitch / 16, xs, a.h, accu);
+        if (lane == 0) {
+#pragma unroll
+            for (int v = 0; v < NV; ++v) {
+                const float gv = acc[0][v], uv = accu[0][v];
+                const float sg = 1.0f / (1.0f + expf(-gv));  // Opure_CpuReference.cpp:195
+                hs[f * NV + v] = (gv * sg) * uv;
+            }
+        }
+    }
+    __syncthreads();
+    // down_proj partial: out[o] = sum_f Wd^T[f][o] * h[f], every o of this block's f rows.
+    const __half *wdh = reinterpret_cast<const __half *>(wd);
+    for (uint32_t o = threadIdx.x; o < a.h; o += blockDim.x) {
+        float acc[NV];
+#pragma unroll
+        for (int v = 0; v < NV; ++v) acc[v] = 0.f;
+        for (uint32_t f = 0; f < nf; ++f) {
+            const float wv = __half2float(wdh[size_t(f) * a.h + o]);
+#pragma unroll
+            for (int v = 0; v < NV; ++v) acc[v] = fmaf(wv, hs[f * NV + v], acc[v]);
+        }
+#pragma unroll
+        for (int v = 0; v < NV; ++v)
+            atomicAdd(reinterpret_cast<unsigned long long *>(a.delta_out + size_t(v) * a.h + o),
+                      static_cast<unsigned long long>(to_fix(acc[v])));
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// L: final RMSNorm + lm_head GEMV + argmax keys (+ logits).
+constexpr int kLRows = 4;
+constexpr uint32_t kLThreads = 128;
+
+struct LmArgs {
+    const uint8_t *w;
+    uint32_t vocab, h;
+    const __half *gain;
+    float eps;
+    const float *base_in;
+    const long long *delta_in;
+    float *logits;
+    unsigned long long *keys;
+};
+
+template <int NV>
+__global__ void __launch_bounds__(kLThreads) lm_head_kernel(LmArgs a) {
+    extern __shared__ __align__(16) float lsm[];
+    float *xs = lsm;
+    float *red = lsm + NV * a.h;
+    __shared__ unsigned long long cta_best[kLThreads / 32][NV];
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    const uint32_t nwarps = gridDim.x * (kLThreads / 32);
+    const uint32_t groups = (a.vocab + kLRows - 1) / kLRows;
+    const uint32_t g0 = blockIdx.x * (kLThreads / 32) + warp;
+    const size_t pitch = size_t(a.h) * 2;
+    const uint32_t nchunks = uint32_t(pitch / 16);
+    RowPrefetch<kLRows> pre;
+    if (g0 < groups) prefetch_rows(pre, a.w, pitch, g0 * kLRows, min(uint32_t(kLRows), a.vocab - g0 * kLRows), nchunks);
+    grid_dependency_wait();
+    grid_dependents_launch();
+    stage_residual<NV>(a.base_in, a.delta_in, a.h, a.gain, a.eps, xs, red, nullptr, nullptr, false);
+    unsigned long long best[NV];
+#pragma unroll
+    for (int v = 0; v < NV; ++v) best[v] = 0ull;
+    for (uint32_t g = g0; g < groups; g += nwarps) {
+        const uint32_t row0 = g * kLRows;
+        const uint32_t valid = min(uint32_t(kLRows), a.vocab - row0);
+        float acc[kLRows][NV];
+        dot_rows<OPURE_W_F16, NV, kLRows>(a.w, pitch, row0, valid, nchunks, xs, a.h, acc, pre, g == g0);
+#pragma unroll
+        for (int r = 0; r < kLRows; ++r)
+#pragma unroll
+            for (int v = 0; v < NV; ++v) {
+                if (r >= int(valid)) continue;
+                const unsigned long long k = argmax_key(acc[r][v], row0 + r);
+                best[v] = k > best[v] ? k : best[v];
+                if (a.logits && lane == uint32_t((r * NV + v) & 31))
+                    a.logits[size_t(v) * a.vocab + row0 + r] = acc[r][v];
+            }
+    }
+    if (lane == 0)
+#pragma unroll
+        for (int v = 0; v < NV; ++v) cta_best[warp][v] = best[v];
+    __syncthreads();
+    if (threadIdx.x < NV) {
+        unsigned long long b = 0ull;
+        for (uint32_t w = 0; w < kLThreads / 32; ++w) b = cta_best[w][threadIdx.x] > b ? cta_best[w][threadIdx.x] : b;
+        if (b) atomicMax(a.keys + threadIdx.x, b);
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+template <typename K>
+opure_status allow_smem(K k, size_t bytes) {
+    if (bytes <= 48 * 1024) return OPURE_OK;
+    const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
+    return e == cudaSuccess ? OPURE_OK : cuda_status(e);
+}
+
+template <int NV, int HD, int G>
+opure_status run_step(opure_ctx *ctx, const opure_fused_step &s) {
+    const uint32_t h = s.hidden, hd = s.head_dim;
+    const uint32_t qkv_rows = (s.n_heads + 2 * s.n_kv) * hd;
+    const KvParams kvp0{nullptr, s.page_table, s.n_pages, s.max_pages, s.page_size};
+    const size_t a_smem = ((kARows * h * 2 + 127) & ~size_t(127)) + (NV * h + 33 * NV) * 4;
+    // B: about one CTA per SM over (kv head, o_proj row block).
+    const uint32_t rb_target = std::max<uint32_t>(1, uint32_t(ctx->sm_count) / s.n_kv);
+    const uint32_t rows_b = std::max<uint32_t>(1, (h + rb_target - 1) / rb_target);
+    const uint32_t rb = (h + rows_b - 1) / rows_b;
+    const size_t b_smem = size_t(rows_b) * G * HD * 2;
+    // C: blocks of F intermediate rows, F chosen so the three weight slices fit.
+    uint32_t F = 16;
+    while (F > 1 && 3ull * F * h * 2 > 160 * 1024) F /= 2;
+    const size_t c_smem = 3ull * F * h * 2 + (NV * h + 33 * NV + F * NV) * 4;
+    const size_t l_smem = (NV * h + 33 * NV) * 4;
+    opure_status st;
+    if ((st = allow_smem(qkv_fused_kernel<NV>, a_smem))) return st;
+    if ((st = allow_smem(attn_oproj_kernel<NV, HD, G>, b_smem))) return st;
+    if ((st = allow_smem(mlp_fused_kernel<NV>, c_smem))) return st;
+    if ((st = allow_smem(lm_head_kernel<NV>, l_smem))) return st;
+
+    float *base[2] = {s.x, s.base1};
+    long long *delta[2] = {s.delta0, s.delta1};
+    for (uint32_t L = 0; L < s.n_layers; ++L) {
+        const opure_fused_layer &ly = s.layers[L];
+        KvParams kvp = kvp0;
+        kvp.pool = ly.kv_pool;
+        // A: x = base0 + delta1 (layer 0: the embedding in base0) -> base1; zero delta0.
+        QkvArgs qa{reinterpret_cast<const __half *>(ly.w_qkv), qkv_rows, h, s.n_heads, s.n_kv, hd,
+                   reinterpret_cast<const __half *>(ly.in_norm), s.eps, s.theta, base[0],
+                   L == 0 ? nullptr : delta[1], base[1], delta[0], s.q, kvp, s.seq, s.pos, ctx->status};
+        if ((st = launch(ctx, qkv_fused_kernel<NV>, dim3((qkv_rows + kARows - 1) / kARows), dim3(kAThreads),
+                         a_smem, true, qa)))
+            return st;
+        // B: attention + o_proj partials into delta0; zero delta1.
+        AttnOArgs ba{reinterpret_cast<const __half *>(ly.w_o_blk), h, s.n_heads, s.n_kv, rows_b, s.q,
+                     s.attn_scale * 1.4426950408889634f, kvp, s.seq, s.pos, delta[0], delta[1], ctx->status};
+        if ((st = launch(ctx, attn_oproj_kernel<NV, HD, G>, dim3(s.n_kv, rb), dim3(kBThreads), b_smem, true, ba)))
+            return st;
+        // C: x = base1 + delta0 -> base0; MLP partials into delta1.
+        MlpArgs ca{reinterpret_cast<const __half *>(ly.w_gate_up), reinterpret_cast<const __half *>(ly.w_down_t),
+                   h, s.inter, F, reinterpret_cast<const __half *>(ly.post_norm), s.eps, base[1], delta[0],
+                   base[0], delta[1], ctx->status};
+        if ((st = launch(ctx, mlp_fused_kernel<NV>, dim3((s.inter + F - 1) / F), dim3(kCThreads), c_smem, true, ca)))
+            return st;
+    }
+    // L: x = base0 + delta1.
+    LmArgs la{reinterpret_cast<const uint8_t *>(s.lm_head), s.vocab, h,
+              reinterpret_cast<const __half *>(s.final_norm), s.eps, base[0], delta[1], s.logits, s.keys};
+    const uint32_t groups = (s.vocab + kLRows - 1) / kLRows;
+    const uint32_t ctas = std::min<uint32_t>((groups + 3) / 4, uint32_t(ctx->sm_count) * 8);
+    return launch(ctx, lm_head_kernel<NV>, dim3(ctas), dim3(kLThreads), l_smem, true, la);
+}
+
+template <int NV, int HD>
+opure_status pick_g(opure_ctx *ctx, const opure_fused_step &s, uint32_t G) {
+    switch (G) {
+        case 1: return run_step<NV, HD, 1>(ctx, s);
+        case 2: return run_step<NV, HD, 2>(ctx, s);
+        case 3: return run_step<NV, HD, 3>(ctx, s);
+        case 4: return run_step<NV, HD, 4>(ctx, s);
+    }
+    return OPURE_ERR_UNSUPPORTED;
+}
+
+template <int NV>
+opure_status pick_hd(opure_ctx *ctx, const opure_fused_step &s, uint32_t G) {
+    if (s.head_dim == 64) return pick_g<NV, 64>(ctx, s, G);
+    if (s.head_dim == 128) return pick_g<NV, 128>(ctx, s, G);
+    return OPURE_ERR_UNSUPPORTED;
+}
+
+}  // namespace
+}  // namespace opure
+
+using namespace opure;
+
+extern "C" opure_status opure_decode_fused(opure_ctx *ctx, const opure_fused_step *s) {
+    opure_status st = enter(ctx);
+    if (st) return st;
+    if (!s || !s->layers || !s->final_norm || !s->lm_head || !s->page_table || !s->seq || !s->pos || !s->x ||
+        !s->base1 || !s->delta0 || !s->delta1 || !s->q || !s->keys || !s->n_kv || !s->n_layers)
+        return OPURE_ERR_INVALID_ARG;
+    if (s->n_heads % s->n_kv || s->hidden % 8 || s->inter == 0) return OPURE_ERR_INVALID_ARG;
+    if (s->nvec == 0) return OPURE_OK;
+    const uint32_t G = s->n_heads / s->n_kv;
+    for (uint32_t L = 0; L < s->n_layers; ++L) {
+        const opure_fused_layer &l = s->layers[L];
+        if (!l.in_norm || !l.post_norm || !l.w_qkv || !l.w_o_blk || !l.w_gate_up || !l.w_down_t || !l.kv_pool)
+            return OPURE_ERR_INVALID_ARG;
+        for (const void *p : {static_cast<const void *>(l.w_qkv), static_cast<const void *>(l.w_o_blk),
+                              static_cast<const void *>(l.w_gate_up), static_cast<const void *>(l.w_down_t)})
+            if (reinterpret_cast<uintptr_t>(p) % 16) return OPURE_ERR_UNSUPPORTED;
+    }
+    switch (s->nvec) {
+        case 1: return pick_hd<1>(ctx, *s, G);
+        case 2: return pick_hd<2>(ctx, *s, G);
+        case 4: return pick_hd<4>(ctx, *s, G);
+        case 8: return pick_hd<8>(ctx, *s, G);
+    }
+    return OPURE_ERR_UNSUPPORTED;
+}

@@ -65,6 +65,7 @@ opure_status opure_engine_create(const char *model_dir, int device, const opure_
             opts.pageSeed = o->page_seed;
             opts.useGraphs = o->use_graphs != 0;
             if (o->attn_scale != 0.f) opts.attnScale = o->attn_scale;
+            opts.path = o->path;
         }
         e->eng.Initialize(model_dir, opts, device);
     });

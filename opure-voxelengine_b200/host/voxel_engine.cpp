@@ -33,7 +33,9 @@ void VoxelEngine::Shutdown() {
                     static_cast<void *>(buf_.attn), static_cast<void *>(buf_.h), static_cast<void *>(buf_.logits),
                     static_cast<void *>(buf_.keys), static_cast<void *>(buf_.seq), static_cast<void *>(buf_.pos),
                     static_cast<void *>(buf_.seqLen), static_cast<void *>(buf_.known), static_cast<void *>(buf_.flags),
-                    static_cast<void *>(buf_.inTokens), static_cast<void *>(buf_.tokens), weights_})
+                    static_cast<void *>(buf_.inTokens), static_cast<void *>(buf_.tokens),
+                    static_cast<void *>(buf_.base1), static_cast<void *>(buf_.delta0),
+                    static_cast<void *>(buf_.delta1), weights_})
         if (p) opure_free(ctx_, p);
     for (auto &s : attnScratch_) opure_free(ctx_, s.second.first);
     attnScratch_.clear();
@@ -54,7 +56,7 @@ void VoxelEngine::Initialize(const std::string &modelDir, const EngineOptions &o
     opts_ = opts;
     OPURE_CUDA_CHECK(opure_init(device, &ctx_));
     graph::LayoutOptions lo;
-    lo.fusedLayouts = false;
+    lo.fusedLayouts = opts.path != 1;  // grouped o_proj and transposed down_proj
     graph_.LoadConfigOnly(modelDir, lo);
     const graph::ModelConfig &cfg = graph_.Config();
     const graph::VramPlan &plan = graph_.Plan();
@@ -68,6 +70,17 @@ void VoxelEngine::Initialize(const std::string &modelDir, const EngineOptions &o
     AllocBuffers();
     seqLen_ = 0;
     ready_ = true;
+    if (opts.path == 2 && !UsesFused(opts.maxBatch))
+        ThrowError("the fused decode path does not support this model or batch size");
+}
+
+bool VoxelEngine::UsesFused(uint32_t n) const {
+    const graph::ModelConfig &c = graph_.Config();
+    const graph::VramPlan &p = graph_.Plan();
+    const uint32_t hd = c.HeadDim(), G = c.KvGroupSize();
+    return opts_.path != 1 && p.hasFused && p.wDtype == OPURE_W_F16 && !p.lmQuantized &&
+           (hd == 64 || hd == 128) && G >= 1 && G <= 4 && (n == 1 || n == 2 || n == 4 || n == 8) &&
+           3ull * c.hiddenSize * 2 <= 160 * 1024;
 }
 
 void VoxelEngine::AllocBuffers() {
@@ -87,6 +100,9 @@ void VoxelEngine::AllocBuffers() {
     buf_.flags = Alloc<uint32_t>(ctx_, B);
     buf_.inTokens = Alloc<int32_t>(ctx_, B);
     buf_.tokens = Alloc<int32_t>(ctx_, size_t(B) * maxLen_);
+    buf_.base1 = Alloc<float>(ctx_, size_t(B) * c.hiddenSize);
+    buf_.delta0 = Alloc<long long>(ctx_, size_t(B) * c.hiddenSize);
+    buf_.delta1 = Alloc<long long>(ctx_, size_t(B) * c.hiddenSize);
     OPURE_CUDA_CHECK(opure_fill(ctx_, buf_.keys, 0, sizeof(unsigned long long) * B));
     OPURE_CUDA_CHECK(opure_fill(ctx_, buf_.tokens, 0, sizeof(int32_t) * size_t(B) * maxLen_));
     // Pinned staging for the host-driven step: [in_tokens B][positions B][keys B (u64)].
@@ -210,6 +226,51 @@ void VoxelEngine::RecordStep(uint32_t n, bool logits) {
     const graph::VramPlan &plan = graph_.Plan();
     const opure_step_io io = StepIO(n);
     OPURE_CUDA_CHECK(opure_step_begin(ctx_, &io));
+    if (UsesFused(n)) {
+        std::vector<opure_fused_layer> layers(c.numLayers);
+        for (uint32_t L = 0; L < c.numLayers; ++L) {
+            const graph::VramPlan::LayerTensors &t = plan.layers[L];
+            opure_fused_layer &f = layers[L];
+            f.in_norm = reinterpret_cast<const uint16_t *>(At(weights_, t.inputNorm));
+            f.post_norm = reinterpret_cast<const uint16_t *>(At(weights_, t.postAttNorm));
+            f.w_qkv = reinterpret_cast<const uint16_t *>(At(weights_, t.wqkv));
+            f.w_o_blk = reinterpret_cast<const uint16_t *>(At(weights_, t.woBlk));
+            f.w_gate_up = reinterpret_cast<const uint16_t *>(At(weights_, t.wgu));
+            f.w_down_t = reinterpret_cast<const uint16_t *>(At(weights_, t.wdownT));
+            f.kv_pool = kv_.Pool(L);
+        }
+        opure_fused_step fs{};
+        fs.nvec = n;
+        fs.hidden = c.hiddenSize;
+        fs.inter = c.intermediateSize;
+        fs.n_heads = c.numHeads;
+        fs.n_kv = c.numKvHeads;
+        fs.head_dim = c.HeadDim();
+        fs.vocab = c.vocabSize;
+        fs.n_layers = c.numLayers;
+        fs.eps = c.rmsNormEps;
+        fs.attn_scale = opts_.attnScale;
+        fs.theta = c.ropeTheta;
+        fs.layers = layers.data();
+        fs.final_norm = reinterpret_cast<const uint16_t *>(At(weights_, plan.finalNorm));
+        fs.lm_head = reinterpret_cast<const uint16_t *>(At(weights_, plan.lmHead));
+        fs.page_table = kv_.DeviceTable();
+        fs.n_pages = kv_.NumPages();
+        fs.max_pages = kv_.MaxPages();
+        fs.page_size = kv_.PageSize();
+        fs.seq = buf_.seq;
+        fs.pos = buf_.pos;
+        fs.x = buf_.x;
+        fs.base1 = buf_.base1;
+        fs.delta0 = buf_.delta0;
+        fs.delta1 = buf_.delta1;
+        fs.q = buf_.q;
+        fs.logits = logits ? buf_.logits : nullptr;
+        fs.keys = buf_.keys;
+        OPURE_CUDA_CHECK(opure_decode_fused(ctx_, &fs));
+        OPURE_CUDA_CHECK(opure_step_end(ctx_, &io));
+        return;
+    }
     for (uint32_t L = 0; L < c.numLayers; ++L) RecordLayer(L, n);
     // Final norm + (tied) LM head + argmax (Opure_VoxelEngine.cpp:514-532, ArgMax :783-791).
     opure_gemv_args a{};

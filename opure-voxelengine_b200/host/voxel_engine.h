@@ -43,6 +43,7 @@ struct EngineOptions {
     uint64_t pageSeed = 3;          // free-list shuffle (0: pages in order)
     bool useGraphs = true;
     float attnScale = 1.0f;         // 1.0 = the reference's unscaled scores
+    uint32_t path = 0;              // 0 auto, 1 per-op kernels, 2 fused kernels required
 };
 
 struct GenerateResult {
@@ -128,7 +129,12 @@ public:
         uint32_t *flags = nullptr;
         int32_t *inTokens = nullptr;
         int32_t *tokens = nullptr;
+        // Fused path: second residual base and the two fixed-point delta buffers.
+        float *base1 = nullptr;
+        long long *delta0 = nullptr, *delta1 = nullptr;
     };
+    // True when steps of n vectors run on opure_decode_fused.
+    bool UsesFused(uint32_t n) const;
     const Buffers &Buf() const { return buf_; }
 
 private:

@@ -15,7 +15,10 @@ P, u32, u64, f32, i32, f64 = C.c_void_p, C.c_uint32, C.c_uint64, C.c_float, C.c_
 
 class EngineOptions(C.Structure):
     _fields_ = [("max_new_tokens", u32), ("max_batch", u32), ("max_len", u32), ("page_size", u32),
-                ("page_seed", u64), ("use_graphs", u32), ("attn_scale", f32)]
+                ("page_seed", u64), ("use_graphs", u32), ("attn_scale", f32), ("path", u32)]
+
+
+PATH_AUTO, PATH_UNFUSED, PATH_FUSED = 0, 1, 2
 
 
 class EngineInfo(C.Structure):
@@ -159,9 +162,9 @@ class Engine:
 
     def __init__(self, model_dir: str, device: int = 0, max_batch: int = 1, max_len: int = 0,
                  page_size: int = 64, page_seed: int = 3, use_graphs: bool = True,
-                 attn_scale: float = 1.0, max_new_tokens: int = 256):
+                 attn_scale: float = 1.0, max_new_tokens: int = 256, path: int = PATH_AUTO):
         o = EngineOptions(max_new_tokens, max_batch, max_len, page_size, page_seed,
-                          int(use_graphs), attn_scale)
+                          int(use_graphs), attn_scale, path)
         h = C.c_void_p()
         st = lib().opure_engine_create(model_dir.encode(), device, C.byref(o), C.byref(h))
         _check(st, "opure_engine_create", None)

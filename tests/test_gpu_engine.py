@@ -167,3 +167,52 @@ def test_config0_smollm_full_size(tmp_path_factory):
     want, margins = oracle.Model(d).generate(p, 128)
     print(f"cfg0: decode {t.decode_ms / 128 * 1e3:.1f} us/token, min oracle margin {margins.min():.3e}")
     assert_tokens(out[0], want, margins)
+
+
+# ---- the fused latency path (opure_decode_fused) ------------------------------------
+@pytest.mark.parametrize("batch", [1, 2, 4, 8])
+def test_fused_path_matches_oracle(models, small, batch):
+    prompts = [ve.prompt(40 + b, SMALL["vocab"], 6 + 2 * b) for b in range(batch)]
+    with ve.Engine(models["small"], max_batch=batch, max_len=96, path=ve.PATH_FUSED) as eng:
+        out, _ = eng.generate(prompts, 30)
+    for b in range(batch):
+        want, margins = small.generate(prompts[b], 30)
+        assert_tokens(out[b], want, margins)
+
+
+def test_fused_and_per_op_paths_agree(models, small):
+    p = ve.prompt(77, SMALL["vocab"], 17)
+    res = {}
+    for path in (ve.PATH_FUSED, ve.PATH_UNFUSED):
+        with ve.Engine(models["small"], max_len=64, path=path) as eng:
+            res[path] = (eng.generate([p], 20)[0][0], eng.forward_logits(p))
+    assert np.array_equal(res[ve.PATH_FUSED][0], res[ve.PATH_UNFUSED][0])
+    assert rel_err(res[ve.PATH_FUSED][1], res[ve.PATH_UNFUSED][1]) < 1e-4
+    st = small.state(64)
+    for i, t in enumerate(p):
+        lg, _ = st.forward(int(t), logits=(i == len(p) - 1))
+    assert rel_err(res[ve.PATH_FUSED][1], lg) < 1e-3
+
+
+def test_fused_head_dim_128(models):
+    m = oracle.Model(models["hd128"])
+    p = ve.prompt(3, HD128["vocab"], 9)
+    with ve.Engine(models["hd128"], max_len=64, path=ve.PATH_FUSED) as eng:
+        out, _ = eng.generate([p], 20)
+    want, margins = m.generate(p, 20)
+    assert_tokens(out[0], want, margins)
+
+
+def test_fused_host_driven_steps(models):
+    p = ve.prompt(6, SMALL["vocab"], 5)
+    with ve.Engine(models["small"], max_len=64, path=ve.PATH_FUSED) as eng:
+        ref, _ = eng.generate([p], 8)
+        toks = [eng.prefill(p)]
+        for i in range(7):
+            toks.append(int(eng.decode_step([toks[-1]], [len(p) + i])[0]))
+    assert toks == list(ref[0])
+
+
+def test_fused_path_refuses_int8(models):
+    with pytest.raises(Exception):
+        ve.Engine(models["q8"], max_len=32, path=ve.PATH_FUSED)
