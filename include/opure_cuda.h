@@ -178,6 +178,28 @@ size_t opure_attention_scratch_bytes(uint32_t n, uint32_t n_q, uint32_t n_heads,
                                      uint32_t split_tokens);
 opure_status opure_attention(opure_ctx *ctx, const opure_attn_args *a);
 
+/* Allocation-free attention. No counterpart in the reference (its attention has no scratch).
+ *
+ * Same computation and arguments as opure_attention, except that a->scratch and
+ * a->scratch_bytes are ignored: the split partials and counters live in a fixed buffer of
+ * OPURE_ATTN_STATIC_SCRATCH_BYTES inside this library, which every GPU that loads the
+ * library keeps until the process exits. It is for callers that are not allowed to
+ * allocate device memory themselves -- for example a plugin inside a host application
+ * (the reference plans an engine plugin) whose memory budget is owned by the host, or a
+ * real-time decode loop that must never stall on cudaMalloc/cudaFree, which synchronise
+ * the device. The call allocates nothing and calls no allocating library routine.
+ *
+ *  - Returns OPURE_ERR_UNSUPPORTED, without launching, when the call would need more than
+ *    OPURE_ATTN_STATIC_SCRATCH_BYTES (compare opure_attention_scratch_bytes for the same
+ *    shape against the limit).
+ *  - The first call on each device looks up the buffer's device address; make that first
+ *    call before capturing a stream into a CUDA graph.
+ *  - Every call shares the one buffer and clears the counters it needs on the ctx stream.
+ *    Calls that may run at the same time on the GPU (other streams or contexts on the same
+ *    device) race on the buffer: serialise them. */
+#define OPURE_ATTN_STATIC_SCRATCH_BYTES (8u << 20)
+opure_status opure_attention_static(opure_ctx *ctx, const opure_attn_args *a);
+
 /* ---- weight-streaming GEMV --------------------------------------------------
  * y[v][o] = epilogue( sum_i W[o][i] * prologue(x[v])[i] ), W row-major [rows][cols]
  * (the safetensors layout), fp32 accumulation, for nvec in 1..9 input vectors.

@@ -232,3 +232,78 @@ extern "C" opure_status opure_attention(opure_ctx *ctx, const opure_attn_args *a
     p.st = ctx->status;
     return launch(ctx, k, dim3(entries * kv.n_kv, n_splits), dim3(kWarps * 32), 0, true, p);
 }
+
+// ---- Allocation-free variant (opure_attention_static) ---------------------------------
+// For callers that may not allocate device memory (a plugin whose host owns the GPU memory
+// budget, or a real-time loop that cannot afford cudaMalloc's device synchronisation): the
+// split partials and counters live in this fixed array instead of caller scratch. Every
+// GPU that loads the library holds it until the process exits.
+static __device__ __align__(256) unsigned char g_attn_static_scratch[OPURE_ATTN_STATIC_SCRATCH_BYTES];
+
+#include <mutex>
+
+namespace {
+// Device address of g_attn_static_scratch per device, looked up once. In host code the
+// array's name is only a host-side stand-in, never a device pointer.
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mu;
+void *g_static_ptr[kMaxDevices] = {};
+
+opure_status static_scratch(int device, void **out) {
+    if (device < 0 || device >= kMaxDevices) return OPURE_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lk(g_static_mu);
+    if (!g_static_ptr[device]) {
+        void *p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_attn_static_scratch);  // device is current
+        if (e != cudaSuccess || !p) return cuda_status(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
+        g_static_ptr[device] = p;
+    }
+    *out = g_static_ptr[device];
+    return OPURE_OK;
+}
+}  // namespace
+
+extern "C" opure_status opure_attention_static(opure_ctx *ctx, const opure_attn_args *a) {
+    opure_status s = enter(ctx);
+    if (s) return s;
+    if (!a || !a->q || !a->out || !a->seq || !a->seq_len) return OPURE_ERR_INVALID_ARG;
+    const opure_kv_layout &kv = a->kv;
+    if (!kv.pool || !kv.page_table || !kv.n_kv || !kv.page_size || !kv.max_pages)
+        return OPURE_ERR_INVALID_ARG;
+    if (a->n_heads % kv.n_kv) return OPURE_ERR_INVALID_ARG;
+    if (a->n == 0 || a->n_q == 0) return OPURE_OK;
+    const uint32_t G = a->n_heads / kv.n_kv;
+    AttnKernel k = pick(kv.head_dim, G);
+    if (!k) return OPURE_ERR_UNSUPPORTED;
+    if (reinterpret_cast<uintptr_t>(kv.pool) % 16) return OPURE_ERR_UNSUPPORTED;
+    const uint32_t entries = a->n * a->n_q;
+    const uint32_t st = choose_split(entries, kv.n_kv, kv.head_dim, a->max_ctx, a->split_tokens,
+                                     ctx->sm_count);
+    const uint32_t n_splits = std::max(1u, (a->max_ctx + st - 1) / st);
+    size_t counters_off = 0;
+    const size_t need = scratch_layout(entries, kv.n_kv, G, kv.head_dim, n_splits, &counters_off);
+    if (need > OPURE_ATTN_STATIC_SCRATCH_BYTES) return OPURE_ERR_UNSUPPORTED;
+    if (uint64_t(entries) * kv.n_kv > 0x7fffffffu || n_splits > 65535) return OPURE_ERR_UNSUPPORTED;
+    void *scratch = nullptr;
+    if ((s = static_scratch(ctx->device, &scratch))) return s;
+    uint32_t *counters = reinterpret_cast<uint32_t *>(static_cast<char *>(scratch) + counters_off);
+    // The buffer keeps the previous call's bytes: the split counters must start at zero.
+    OPURE_CUDA_TRY(cudaMemsetAsync(counters, 0, size_t(entries) * kv.n_kv * sizeof(uint32_t), ctx->stream));
+
+    AttnParams p{};
+    p.q = a->q;
+    p.out = a->out;
+    p.seq = a->seq;
+    p.seq_len = a->seq_len;
+    p.n = a->n;
+    p.n_q = a->n_q;
+    p.n_heads = a->n_heads;
+    p.scale_log2 = a->scale * 1.4426950408889634f;
+    p.split_tokens = st;
+    p.n_splits = n_splits;
+    p.partials = static_cast<float *>(scratch);
+    p.counters = counters;
+    p.kv = kv;
+    p.st = ctx->status;
+    return launch(ctx, k, dim3(entries * kv.n_kv, n_splits), dim3(kWarps * 32), 0, true, p);
+}

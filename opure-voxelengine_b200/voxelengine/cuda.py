@@ -88,6 +88,7 @@ _SIGS = {
     "opure_spec_accept": [P, P], "opure_sample_softmax": [P, P, u32, u32, P, P],
     "opure_debug_inject_failure": [P, u32, u32],
     "opure_step_begin": [P, P], "opure_step_end": [P, P],
+    "opure_attention_static": [P, P],
 }
 
 
