@@ -24,17 +24,67 @@ struct KvParams {
 // x[v] = base[v] + delta[v] * 2^-32 (rounded to fp32 once, as the reference rounds its fp32
 // residual after every add), staged into xs and RMS-normalised with `gain` in place. The
 // designated CTA also writes the un-normalised x to base_out and zeroes delta_zero.
+// The fp16 norm gain a thread will need, fetched before the kernel waits on its
+// predecessor (gains are weights, never written by the previous kernel). Group g covers
+// elements 4g..4g+3 of the NV*h staged values.
+constexpr int kGainRegs = 4;
+struct GainPrefetch {
+    uint2 g[kGainRegs];
+};
+
+template <int NV>
+__device__ __forceinline__ void prefetch_gain(const __half *gain, uint32_t h, GainPrefetch &p) {
+    const uint32_t groups = NV * h / 4;
+#pragma unroll
+    for (int k = 0; k < kGainRegs; ++k) {
+        const uint32_t g = threadIdx.x + k * blockDim.x;
+        p.g[k] = g < groups ? __ldg(reinterpret_cast<const uint2 *>(gain + (4 * g) % h)) : make_uint2(0, 0);
+    }
+}
+
+// All of a thread's loads are issued before any is used (16-byte vectors, unrolled), so
+// staging costs one memory round trip rather than one per loop iteration. Requires
+// NV * h to be a multiple of 4 (h % 8 == 0 is checked at the ABI).
 template <int NV>
 __device__ __forceinline__ void stage_residual(const float *base, const long long *delta, uint32_t h,
-                                               const __half *gain, float eps, float *xs, float *red,
-                                               float *base_out, long long *delta_zero, bool designated) {
-    for (uint32_t i = threadIdx.x; i < NV * h; i += blockDim.x) {
-        float x = base[i];
-        if (delta) x = float(double(x) + double(__ldcg(delta + i)) * kFixInv);
-        xs[i] = x;
-        if (designated) {
-            if (base_out) base_out[i] = x;
-            if (delta_zero) delta_zero[i] = 0;
+                                               const GainPrefetch &gpre, const __half *gain, float eps,
+                                               float *xs, float *red, float *base_out, long long *delta_zero,
+                                               bool designated) {
+    constexpr int kLoads = 4;  // float4 groups per thread issued together
+    const uint32_t groups = NV * h / 4, step = blockDim.x;
+    for (uint32_t g0 = threadIdx.x; g0 < groups; g0 += kLoads * step) {
+        float4 b[kLoads];
+        longlong2 d[kLoads][2];
+#pragma unroll
+        for (int k = 0; k < kLoads; ++k) {
+            const uint32_t g = g0 + k * step;
+            if (g < groups) {
+                b[k] = __ldcg(reinterpret_cast<const float4 *>(base) + g);
+                if (delta) {
+                    d[k][0] = __ldcg(reinterpret_cast<const longlong2 *>(delta) + 2 * g);
+                    d[k][1] = __ldcg(reinterpret_cast<const longlong2 *>(delta) + 2 * g + 1);
+                }
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kLoads; ++k) {
+            const uint32_t g = g0 + k * step;
+            if (g >= groups) continue;
+            float4 x = b[k];
+            if (delta) {
+                x.x = float(double(x.x) + double(d[k][0].x) * kFixInv);
+                x.y = float(double(x.y) + double(d[k][0].y) * kFixInv);
+                x.z = float(double(x.z) + double(d[k][1].x) * kFixInv);
+                x.w = float(double(x.w) + double(d[k][1].y) * kFixInv);
+            }
+            reinterpret_cast<float4 *>(xs)[g] = x;
+            if (designated) {
+                if (base_out) reinterpret_cast<float4 *>(base_out)[g] = x;
+                if (delta_zero) {
+                    reinterpret_cast<longlong2 *>(delta_zero)[2 * g] = make_longlong2(0, 0);
+                    reinterpret_cast<longlong2 *>(delta_zero)[2 * g + 1] = make_longlong2(0, 0);
+                }
+            }
         }
     }
     __syncthreads();
@@ -52,8 +102,23 @@ __device__ __forceinline__ void stage_residual(const float *base, const long lon
         red[32 * NV + threadIdx.x] = float(1.0 / sqrt(double(t) / double(h) + double(eps)));
     }
     __syncthreads();
-    for (uint32_t i = threadIdx.x; i < NV * h; i += blockDim.x)
-        xs[i] = xs[i] * red[32 * NV + i / h] * __half2float(gain[i % h]);
+    auto scale = [&](uint32_t g, uint2 gw) {
+        const float2 g01 = h2f2(gw.x), g23 = h2f2(gw.y);
+        const float inv = red[32 * NV + (4 * g) / h];
+        float4 x = reinterpret_cast<float4 *>(xs)[g];
+        x.x = x.x * inv * g01.x;
+        x.y = x.y * inv * g01.y;
+        x.z = x.z * inv * g23.x;
+        x.w = x.w * inv * g23.y;
+        reinterpret_cast<float4 *>(xs)[g] = x;
+    };
+#pragma unroll
+    for (int k = 0; k < kGainRegs; ++k) {
+        const uint32_t g = threadIdx.x + k * step;
+        if (g < groups) scale(g, gpre.g[k]);
+    }
+    for (uint32_t g = threadIdx.x + kGainRegs * step; g < groups; g += step)
+        scale(g, __ldg(reinterpret_cast<const uint2 *>(gain + (4 * g) % h)));
     __syncthreads();
 }
 
@@ -147,50 +212,61 @@ __global__ void __launch_bounds__(kAThreads) qkv_fused_kernel(QkvArgs a) {
         mbar_expect_tx(&bar, nrows * pitch);
         bulk_load(wsm, reinterpret_cast<const uint8_t *>(a.w) + size_t(row0) * pitch, nrows * pitch, &bar);
     }
+    GainPrefetch gpre;
+    prefetch_gain<NV>(a.gain, a.h, gpre);
+
+    // Everything the epilogue needs besides the dot products depends only on the step's
+    // positions and the page table, which the previous kernel does not write: lane v of
+    // each warp resolves vector v's position, RoPE angle and KV slot before the wait.
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t r = row0 + 2 * warp;  // this warp's RoPE pair (r, r + 1)
+    const uint32_t qrows = a.n_heads * a.hd, krows = a.n_kv * a.hd;
+    const bool epi = 2 * warp < nrows && lane < NV;
+    double sn = 0.0, cs = 1.0;
+    __half *slot = nullptr;
+    if (epi) {
+        const int32_t p = a.pos[lane], s = a.seq[lane];
+        if (r < qrows + krows) {
+            // RoPE, interleaved pairs, theta^(-2*pair/hd) (Opure_RoPE.usf:56), in double.
+            const uint32_t pair = (r % a.hd) / 2;
+            sincos(double(p) * pow(a.theta, -2.0 * double(pair) / double(a.hd)), &sn, &cs);
+        }
+        if (r >= qrows) {
+            const bool is_k = r < qrows + krows;
+            const uint32_t rr = is_k ? r - qrows : r - qrows - krows;
+            slot = kv_slot(a.kv, a.n_kv, a.hd, s, p, is_k ? 0 : 1, rr / a.hd, a.st);
+            if (slot) slot += rr % a.hd;
+        }
+    }
+
     grid_dependency_wait();
     grid_dependents_launch();
-    stage_residual<NV>(a.base_in, a.delta_in, a.h, a.gain, a.eps, xs, red, a.base_out, a.delta_zero,
+    stage_residual<NV>(a.base_in, a.delta_in, a.h, gpre, a.gain, a.eps, xs, red, a.base_out, a.delta_zero,
                        blockIdx.x == 0);
     if (!cta_wait_copy(&bar, a.st, 40)) return;
 
-    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-    const uint32_t r = row0 + 2 * warp;  // this warp's RoPE pair (r, r + 1)
     if (2 * warp >= nrows) return;
     float acc[2][NV];
     smem_dot<NV, 2>(wsm + size_t(2 * warp) * pitch, pitch, min(2u, nrows - 2 * warp), pitch / 16, xs, a.h, acc);
-    if (lane >= NV) return;
+    if (!epi) return;
     const uint32_t v = lane;
     float e0 = 0.f, e1 = 0.f;
 #pragma unroll
     for (int k = 0; k < NV; ++k)
         if (k == int(v)) { e0 = acc[0][k]; e1 = acc[1][k]; }
-    const uint32_t qrows = a.n_heads * a.hd, krows = a.n_kv * a.hd;
-    const int32_t p = a.pos[v], s = a.seq[v];
     if (r < qrows + krows) {
-        // RoPE, interleaved pairs, theta^(-2*pair/hd) (Opure_RoPE.usf:56), in double.
-        const uint32_t pair = (r % a.hd) / 2;
-        double sn, cs;
-        sincos(double(p) * pow(a.theta, -2.0 * double(pair) / double(a.hd)), &sn, &cs);
         const float r0 = float(double(e0) * cs - double(e1) * sn);
         const float r1 = float(double(e0) * sn + double(e1) * cs);
         if (r < qrows) {
             a.q_out[size_t(v) * qrows + r] = r0;
             a.q_out[size_t(v) * qrows + r + 1] = r1;
-        } else {
-            const uint32_t head = (r - qrows) / a.hd;
-            __half *kd = kv_slot(a.kv, a.n_kv, a.hd, s, p, 0, head, a.st);
-            if (kd) {
-                kd[(r - qrows) % a.hd] = __float2half_rn(r0);
-                kd[(r - qrows) % a.hd + 1] = __float2half_rn(r1);
-            }
+        } else if (slot) {
+            slot[0] = __float2half_rn(r0);
+            slot[1] = __float2half_rn(r1);
         }
-    } else {
-        const uint32_t head = (r - qrows - krows) / a.hd;
-        __half *vd = kv_slot(a.kv, a.n_kv, a.hd, s, p, 1, head, a.st);
-        if (vd) {
-            vd[(r - qrows - krows) % a.hd] = __float2half_rn(e0);
-            vd[(r - qrows - krows) % a.hd + 1] = __float2half_rn(e1);
-        }
+    } else if (slot) {
+        slot[0] = __float2half_rn(e0);
+        slot[1] = __float2half_rn(e1);
     }
 }
 
@@ -230,21 +306,39 @@ __global__ void __launch_bounds__(kBThreads) attn_oproj_kernel(AttnOArgs a) {
         bulk_load(wsm, reinterpret_cast<const uint8_t *>(a.w_o_blk) + (size_t(g) * a.h + row0) * pitch,
                   nrows * pitch, &bar);
     }
+    // Positions, sequence slots and their page-table rows are not written by the previous
+    // kernel: stage them before waiting on it (page tables of up to kPtStage entries).
+    constexpr uint32_t kPtStage = 256;
+    __shared__ int32_t s_seq[NV], s_pos[NV];
+    __shared__ int32_t s_pt[NV][kPtStage];
+    const bool stage_pt = a.kv.max_pages <= kPtStage;
+    if (threadIdx.x < NV) {
+        s_seq[threadIdx.x] = a.seq[threadIdx.x];
+        s_pos[threadIdx.x] = a.pos[threadIdx.x];
+    }
+    __syncthreads();
+    if (stage_pt)
+        for (uint32_t i = threadIdx.x; i < NV * a.kv.max_pages; i += blockDim.x) {
+            const int32_t s = s_seq[i / a.kv.max_pages];
+            s_pt[i / a.kv.max_pages][i % a.kv.max_pages] =
+                s >= 0 ? a.kv.page_table[size_t(s) * a.kv.max_pages + i % a.kv.max_pages] : -1;
+        }
     grid_dependency_wait();
     grid_dependents_launch();
     if (g == 0 && rb == 0)
         for (uint32_t i = threadIdx.x; i < NV * a.h; i += blockDim.x) a.delta_zero[i] = 0;
+    __syncthreads();
 
     for (int v = 0; v < NV; ++v) {
         float qv[G][AttnShape<HD>::E];
         load_q_slice<HD, G>(a.q + size_t(v) * a.n_heads * HD, g, a.scale_log2, qv);
         AttnState<HD, G> st;
         st.init();
-        const int32_t s = a.seq[v];
+        const int32_t s = s_seq[v];
         KvView kv{reinterpret_cast<const __half *>(a.kv.pool),
-                  a.kv.page_table + size_t(max(s, 0)) * a.kv.max_pages, a.kv.max_pages, a.kv.n_pages,
-                  a.kv.page_size, a.n_kv, g, s >= 0};
-        attend_range<HD, G>(st, qv, kv, 0, uint32_t(max(a.pos[v] + 1, 0)), warp, kBWarps, a.st);
+                  stage_pt ? s_pt[v] : a.kv.page_table + size_t(max(s, 0)) * a.kv.max_pages,
+                  a.kv.max_pages, a.kv.n_pages, a.kv.page_size, a.n_kv, g, s >= 0};
+        attend_range<HD, G>(st, qv, kv, 0, uint32_t(max(s_pos[v] + 1, 0)), warp, kBWarps, a.st);
         merge_lane_groups<HD, G>(st);
         store_warp_state<HD, G, kBWarps>(st, ws, warp);
         __syncthreads();
@@ -318,9 +412,11 @@ __global__ void __launch_bounds__(kCThreads) mlp_fused_kernel(MlpArgs a) {
         bulk_load(wu, w + (size_t(a.ff) + f0) * pitch, nf * pitch, &bar);
         bulk_load(wd, reinterpret_cast<const uint8_t *>(a.w_down_t) + size_t(f0) * pitch, nf * pitch, &bar);
     }
+    GainPrefetch gpre;
+    prefetch_gain<NV>(a.gain, a.h, gpre);
     grid_dependency_wait();
     grid_dependents_launch();
-    stage_residual<NV>(a.base_in, a.delta_in, a.h, a.gain, a.eps, xs, red, a.base_out, nullptr,
+    stage_residual<NV>(a.base_in, a.delta_in, a.h, gpre, a.gain, a.eps, xs, red, a.base_out, nullptr,
                        blockIdx.x == 0);
     if (!cta_wait_copy(&bar, a.st, 42)) return;
 
@@ -387,9 +483,11 @@ __global__ void __launch_bounds__(kLThreads) lm_head_kernel(LmArgs a) {
     const uint32_t nchunks = uint32_t(pitch / 16);
     RowPrefetch<kLRows> pre;
     if (g0 < groups) prefetch_rows(pre, a.w, pitch, g0 * kLRows, min(uint32_t(kLRows), a.vocab - g0 * kLRows), nchunks);
+    GainPrefetch gpre;
+    prefetch_gain<NV>(a.gain, a.h, gpre);
     grid_dependency_wait();
     grid_dependents_launch();
-    stage_residual<NV>(a.base_in, a.delta_in, a.h, a.gain, a.eps, xs, red, nullptr, nullptr, false);
+    stage_residual<NV>(a.base_in, a.delta_in, a.h, gpre, a.gain, a.eps, xs, red, nullptr, nullptr, false);
     unsigned long long best[NV];
 #pragma unroll
     for (int v = 0; v < NV; ++v) best[v] = 0ull;
