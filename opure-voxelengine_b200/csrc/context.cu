@@ -57,8 +57,12 @@ opure_status opure_init(int device, opure_ctx **out) {
     cudaError_t e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaMalloc(&ctx->status, sizeof(opure::DeviceStatus));
     if (e == cudaSuccess) e = cudaMemset(ctx->status, 0, sizeof(opure::DeviceStatus));
+    if (e == cudaSuccess) e = cudaMalloc(&ctx->ws, opure::kTcWorkspaceBytes);
+    if (e == cudaSuccess) e = cudaMemset(ctx->ws, 0, opure::kTcWorkspaceBytes);
+    if (e == cudaSuccess) ctx->ws_bytes = opure::kTcWorkspaceBytes;
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
+        if (ctx->ws) cudaFree(ctx->ws);
         if (ctx->status) cudaFree(ctx->status);
         if (ctx->stream) cudaStreamDestroy(ctx->stream);
         delete ctx;
@@ -72,6 +76,7 @@ opure_status opure_shutdown(opure_ctx *ctx) {
     if (!ctx) return OPURE_ERR_INVALID_ARG;
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    if (ctx->ws) cudaFree(ctx->ws);
     if (ctx->status) cudaFree(ctx->status);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;

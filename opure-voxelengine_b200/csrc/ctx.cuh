@@ -3,6 +3,12 @@
 
 #include "common.cuh"
 
+namespace opure {
+// Tensor-core GEMV workspace: up to 256 vectors x 16384 columns packed as fp16 pairs
+// (16 MiB), their scales and split-K tickets, and 32 MiB of split-K partial sums.
+constexpr size_t kTcWorkspaceBytes = size_t(48) << 20;
+}  // namespace opure
+
 struct opure_ctx {
     int device = -1;
     cudaStream_t stream = nullptr;
@@ -14,6 +20,11 @@ struct opure_ctx {
     uint32_t inject_count = 0;
     // Programmatic dependent launch for kernels enqueued by this ctx.
     bool pdl = true;
+    // Device workspace of the tensor-core GEMV path (packed vectors, split-K partial sums
+    // and their tickets), allocated and zeroed once by opure_init so kernel calls allocate
+    // nothing; calls on one ctx are stream-ordered, so they share it safely.
+    void *ws = nullptr;
+    size_t ws_bytes = 0;
 };
 
 namespace opure {

@@ -1,0 +1,526 @@
+// gemm_tc.cu -- opure_gemv for 16..256 token vectors per pass on the tcgen05 tensor cores.
+//
+// With many vectors (batched decode, the k+1-position speculative verify pass) the GEMV
+// Y[v][row] = sum_k W[row][k] x[v][k] is a dense contraction: weights are streamed once
+// for all vectors and the products run on the 5th-generation tensor cores.
+//
+//   pack   one CTA per vector: optional RMSNorm (the GEMV prologue), then the vector is
+//          scaled by a power of two s_v and split into two fp16 halves
+//          x / s_v = hi + lo  (hi = fp16(x / s_v), lo = fp16(x / s_v - hi)),
+//          which keeps ~22 significant bits: W.x = s_v (W.hi + W.lo) with fp16 x fp16
+//          products accumulated in fp32, the accuracy of the fp32 CUDA-core GEMV.
+//   gemm   one CTA per (128-row tile, K split). Thread 0 streams 128x64 weight tiles and
+//          the matching 64-column slices of the packed vectors with TMA (128-byte
+//          swizzle) into a ring of shared-memory stages; thread 32 issues
+//          tcgen05.mma (M=128, N=vectors rounded up to 16, K=16, fp16 in, fp32 out) into
+//          a TMEM accumulator (two for the SwiGLU gate/up pair) and frees each stage with
+//          tcgen05.commit. The four warps then read the accumulator rows with tcgen05.ld
+//          (warp w owns TMEM lanes 32w..32w+31 = tile rows) and apply the epilogue:
+//          store, residual add, SwiGLU, or argmax keys (+ logits). With a K split every
+//          CTA stores fp32 partials and the last CTA of the tile (ticket counter) adds
+//          them in split order, so results do not depend on arrival order.
+// All waits are bounded (1 s); a timeout is reported in the ctx status word and the CTA
+// still releases its TMEM. No TMA multicast is used.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "gemm_tc.cuh"
+#include "tma.cuh"
+
+namespace opure {
+namespace {
+
+constexpr uint32_t kTileM = 128;   // weight rows per tile = TMEM lanes
+constexpr uint32_t kTileK = 64;    // 64 fp16 = one 128-byte swizzle row
+constexpr uint32_t kThreads = 128;
+constexpr uint32_t kMaxN = 256;    // vectors per pass (MMA N limit)
+constexpr uint32_t kMaxStages = 8;
+constexpr uint32_t kMaxTickets = 4096;
+// Workspace layout (ctx->ws).
+constexpr size_t kPackOff = 0;
+constexpr size_t kPackBytes = size_t(2) * kMaxN * kTcMaxCols * 2;
+constexpr size_t kScaleOff = kPackOff + kPackBytes;
+constexpr size_t kTicketOff = kScaleOff + kMaxN * 4;
+constexpr size_t kPartialOff = (kTicketOff + kMaxTickets * 4 + 255) & ~size_t(255);
+static_assert(kPartialOff < kTcWorkspaceBytes, "workspace layout");
+
+// ---- PTX wrappers -------------------------------------------------------------------
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint32_t x, uint32_t y,
+                                            uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t *dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major tile stored as 128-byte swizzled rows
+// (the layout TMA writes with CU_TENSOR_MAP_SWIZZLE_128B): 8-row groups 1024 bytes
+// apart, descriptor version 1, layout type 2 (128-byte swizzle).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+    return uint64_t((addr & 0x3FFFFu) >> 4) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) |
+           (uint64_t(1) << 46) | (uint64_t(2) << 61);
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16 (fp16 inputs, fp32 accumulate).
+__device__ __forceinline__ void mma_f16(uint32_t tmem, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem),
+        "l"(da), "l"(db), "r"(idesc), "r"(acc)
+        : "memory");
+}
+
+// Arrives on `bar` once every tcgen05.mma this thread issued before has completed.
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_addr(bar))
+                 : "memory");
+}
+
+// 16 consecutive fp32 accumulator columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+        "%14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+__device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long t = __shfl_xor_sync(0xffffffffu, v, o);
+        v = t > v ? t : v;
+    }
+    return v;
+}
+
+// ---- pack ---------------------------------------------------------------------------
+constexpr uint32_t kPackThreads = 256;
+
+struct PackParams {
+    const float *x;
+    uint32_t x_stride, K, npad;
+    uint32_t rmsnorm;
+    const __half *gain;
+    float eps;
+    __half *xp;      // [2 npad][K]: hi rows 0..npad-1, lo rows npad..2 npad-1
+    float *xscale;   // [npad]
+};
+
+__device__ float block_reduce(float v, bool is_max, float *red) {
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float t = __shfl_xor_sync(0xffffffffu, v, o);
+        v = is_max ? fmaxf(v, t) : v + t;
+    }
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float r = is_max ? 0.f : 0.f;
+    for (uint32_t w = 0; w < nw; ++w) r = is_max ? fmaxf(r, red[w]) : r + red[w];
+    return r;
+}
+
+__global__ void __launch_bounds__(kPackThreads) pack_kernel(PackParams p) {
+    extern __shared__ float row[];  // [K]
+    __shared__ float red[32];
+    grid_dependency_wait();
+    grid_dependents_launch();
+    const uint32_t v = blockIdx.x;
+    const float *x = p.x + size_t(v) * p.x_stride;
+    float ss = 0.f;
+    for (uint32_t i = threadIdx.x; i < p.K; i += blockDim.x) {
+        const float t = x[i];
+        row[i] = t;
+        ss = fmaf(t, t, ss);
+    }
+    float inv = 1.f;
+    if (p.rmsnorm) {
+        const float tot = block_reduce(ss, false, red);
+        // The GEMV prologue's RMSNorm (RMSNormMain, Opure_RMSNorm.usf:31-79).
+        inv = float(1.0 / sqrt(double(tot) / double(p.K) + double(p.eps)));
+    }
+    float amax = 0.f;
+    for (uint32_t i = threadIdx.x; i < p.K; i += blockDim.x) {
+        float t = row[i];
+        if (p.rmsnorm) t = t * inv * __half2float(p.gain[i]);
+        row[i] = t;
+        amax = fmaxf(amax, fabsf(t));
+    }
+    amax = block_reduce(amax, true, red);
+    // s = 2^(e - 14) with amax < 2^e, so |x / s| < 2^14 stays inside fp16's range.
+    int e = 0;
+    if (amax > 0.f && amax <= 3.0e38f) frexpf(amax, &e);
+    const float s = ldexpf(1.f, e - 14), rs = ldexpf(1.f, 14 - e);
+    if (threadIdx.x == 0) p.xscale[v] = s;
+    __half *hi = p.xp + size_t(v) * p.K;
+    __half *lo = p.xp + size_t(p.npad + v) * p.K;
+    for (uint32_t i = threadIdx.x; i < p.K; i += blockDim.x) {
+        const float t = row[i] * rs;
+        const __half h = __float2half_rn(t);
+        hi[i] = h;
+        lo[i] = __float2half_rn(t - __half2float(h));
+    }
+    // The GEMM reads these rows through TMA (the async proxy).
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// ---- GEMM ---------------------------------------------------------------------------
+struct TcParams {
+    uint32_t rows, n, npad, ktiles, kt_per_split, splits, stages;
+    float *y;
+    uint32_t y_stride;
+    const float *residual;
+    unsigned long long *keys;
+    const float *xscale;
+    float *partials;    // [tiles][splits][accumulators * npad][128]
+    uint32_t *tickets;  // [tiles]
+    DeviceStatus *st;
+};
+
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap, TcParams p) {
+    constexpr bool kSwiglu = EPI == OPURE_EPI_SWIGLU;
+    constexpr uint32_t kAcc = kSwiglu ? 2 : 1;
+    extern __shared__ uint8_t dsm[];
+    __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages], done;
+    __shared__ uint32_t tmem_base;
+    __shared__ int fail, last;
+    __shared__ uint32_t issued_s, consumed_s;
+
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t tile = blockIdx.x, split = blockIdx.y;
+    const uint32_t m0 = tile * kTileM;
+    const uint32_t kt0 = split * p.kt_per_split;
+    const uint32_t nk = min(p.ktiles, kt0 + p.kt_per_split) - kt0;
+    const uint32_t a_bytes = kTileM * 128, b_bytes = p.npad * 128;
+    const uint32_t stage_bytes = kAcc * a_bytes + 2 * b_bytes;
+    uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dsm) + 1023) & ~uintptr_t(1023));
+    auto a_tile = [&](uint32_t s, uint32_t j) { return base + size_t(s) * stage_bytes + j * a_bytes; };
+    auto b_tile = [&](uint32_t s, uint32_t j) { return base + size_t(s) * stage_bytes + kAcc * a_bytes + j * b_bytes; };
+    uint32_t ncols = 32;
+    while (ncols < kAcc * p.npad) ncols <<= 1;
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < p.stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(&done, 1);
+        fail = 0;
+        last = 0;
+        issued_s = 0;
+        consumed_s = 0;
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&wmap)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
+    }
+    if (warp == 2) tmem_alloc(&tmem_base, ncols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base;
+
+    if (threadIdx.x == 0) {
+        // Producer. Weight tiles do not depend on earlier kernels: the first stages are
+        // requested before waiting on them; the packed vectors only after.
+        const uint32_t pre = min(p.stages, nk);
+        for (uint32_t i = 0; i < pre; ++i) {
+            mbar_expect_tx(&full[i], stage_bytes);
+            tma_load_2d(a_tile(i, 0), &wmap, (kt0 + i) * kTileK, m0, &full[i]);
+            if (kSwiglu) tma_load_2d(a_tile(i, 1), &wmap, (kt0 + i) * kTileK, p.rows + m0, &full[i]);
+        }
+        grid_dependency_wait();
+        for (uint32_t i = 0; i < pre; ++i) {
+            tma_load_2d(b_tile(i, 0), &xmap, (kt0 + i) * kTileK, 0, &full[i]);
+            tma_load_2d(b_tile(i, 1), &xmap, (kt0 + i) * kTileK, p.npad, &full[i]);
+        }
+        uint32_t i = pre;
+        for (; i < nk; ++i) {
+            const uint32_t s = i % p.stages;
+            if (!mbar_wait(&empty[s], ((i / p.stages) & 1u) ^ 1u)) {
+                report(p.st, OPURE_ERR_DEVICE_TIMEOUT, 60, blockIdx.x);
+                fail = 1;
+                break;
+            }
+            mbar_expect_tx(&full[s], stage_bytes);
+            tma_load_2d(a_tile(s, 0), &wmap, (kt0 + i) * kTileK, m0, &full[s]);
+            if (kSwiglu) tma_load_2d(a_tile(s, 1), &wmap, (kt0 + i) * kTileK, p.rows + m0, &full[s]);
+            tma_load_2d(b_tile(s, 0), &xmap, (kt0 + i) * kTileK, 0, &full[s]);
+            tma_load_2d(b_tile(s, 1), &xmap, (kt0 + i) * kTileK, p.npad, &full[s]);
+        }
+        issued_s = i;
+    } else {
+        grid_dependency_wait();
+    }
+    grid_dependents_launch();
+
+    if (threadIdx.x == 32) {
+        // MMA issuer: per 64-wide K tile, four K=16 steps (32 bytes along the swizzled
+        // rows) of hi and lo products.
+        const uint32_t idesc = (1u << 4) | ((p.npad >> 3) << 17) | ((kTileM >> 4) << 24);
+        uint32_t i = 0;
+        for (; i < nk; ++i) {
+            const uint32_t s = i % p.stages;
+            if (!mbar_wait(&full[s], (i / p.stages) & 1u)) {
+                report(p.st, OPURE_ERR_DEVICE_TIMEOUT, 61, blockIdx.x);
+                fail = 1;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t a0 = smem_addr(a_tile(s, 0)), bh = smem_addr(b_tile(s, 0)), bl = smem_addr(b_tile(s, 1));
+#pragma unroll
+            for (uint32_t k = 0; k < kTileK / 16; ++k) {
+                const uint64_t dh = smem_desc(bh + 32 * k), dl = smem_desc(bl + 32 * k);
+                const uint64_t da = smem_desc(a0 + 32 * k);
+                mma_f16(tmem, da, dh, idesc, (i | k) != 0);
+                mma_f16(tmem, da, dl, idesc, 1);
+                if (kSwiglu) {
+                    const uint64_t du = smem_desc(smem_addr(a_tile(s, 1)) + 32 * k);
+                    mma_f16(tmem + p.npad, du, dh, idesc, (i | k) != 0);
+                    mma_f16(tmem + p.npad, du, dl, idesc, 1);
+                }
+            }
+            mma_commit(&empty[s]);
+        }
+        consumed_s = i;
+        mma_commit(&done);
+    }
+
+    // Epilogue: every thread owns one tile row (TMEM lane).
+    if (!mbar_wait(&done, 0)) report(p.st, OPURE_ERR_DEVICE_TIMEOUT, 62, blockIdx.x);
+    tc_fence_after();
+    __syncthreads();
+    __syncwarp();
+    if (fail) {
+        // Leave no copy in flight into this CTA's shared memory.
+        if (threadIdx.x == 0)
+            for (uint32_t i = consumed_s; i < issued_s; ++i) mbar_wait(&full[i % p.stages], (i / p.stages) & 1u);
+    } else {
+        const uint32_t lrow = warp * 32 + lane;
+        const uint32_t row = m0 + lrow;
+        const uint32_t taddr = tmem + ((warp * 32) << 16);
+        const uint32_t acc_cols = kAcc * p.npad;
+        bool run_epi = true;
+        float *part = nullptr;
+        if (p.splits > 1) {
+            // Partial sums of this split, column-major so a warp's stores are contiguous.
+            part = p.partials + size_t(tile) * p.splits * acc_cols * kTileM;
+            float *mine = part + size_t(split) * acc_cols * kTileM;
+            for (uint32_t c0 = 0; c0 < acc_cols; c0 += 16) {
+                float r[16];
+                tmem_ld16(taddr + c0, r);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) mine[size_t(c0 + j) * kTileM + lrow] = r[j];
+            }
+            __threadfence();
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                const uint32_t t = atomicAdd(&p.tickets[tile], 1u);
+                last = t == p.splits - 1;
+                if (last) p.tickets[tile] = 0;  // ready for the next call
+            }
+            __syncthreads();
+            run_epi = last;
+            __threadfence();
+        }
+        if (run_epi) {
+            auto column = [&](uint32_t c, float (&r)[16]) {
+                if (p.splits == 1) {
+                    tmem_ld16(taddr + c, r);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) r[j] = 0.f;
+                    for (uint32_t s = 0; s < p.splits; ++s) {
+                        const float *src = part + size_t(s) * acc_cols * kTileM;
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) r[j] += __ldcg(src + size_t(c + j) * kTileM + lrow);
+                    }
+                }
+            };
+            const bool in = row < p.rows;
+            for (uint32_t c0 = 0; c0 < p.npad; c0 += 16) {
+                float g[16], u[16];
+                column(c0, g);
+                if (kSwiglu) column(p.npad + c0, u);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const uint32_t v = c0 + j;
+                    if (v >= p.n) break;
+                    const float val = g[j] * p.xscale[v];
+                    const size_t o = size_t(v) * p.y_stride + row;
+                    if constexpr (EPI == OPURE_EPI_STORE) {
+                        if (in) p.y[o] = val;
+                    } else if constexpr (EPI == OPURE_EPI_ADD) {
+                        if (in) p.y[o] = p.residual[o] + val;
+                    } else if constexpr (EPI == OPURE_EPI_SWIGLU) {
+                        const float uv = u[j] * p.xscale[v];
+                        const float sg = 1.0f / (1.0f + expf(-val));
+                        if (in) p.y[o] = (val * sg) * uv;
+                    } else {
+                        if (in && p.y) p.y[o] = val;
+                        const unsigned long long k = warp_max_u64(in ? argmax_key(val, row) : 0ull);
+                        if (lane == 0 && k) atomicMax(p.keys + v, k);
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 2) tmem_dealloc(tmem, ncols);
+}
+
+// ---- host ---------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// Row-major fp16 [rows][K] matrix, boxes of 64 columns x box_rows rows, 128-byte swizzle.
+bool make_map(CUtensorMap *m, const void *ptr, uint32_t K, uint32_t rows, uint32_t box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {K, rows};
+    const cuuint64_t strides[1] = {cuuint64_t(K) * 2};
+    const cuuint32_t box[2] = {kTileK, box_rows};
+    const cuuint32_t es[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int EPI>
+opure_status launch_gemm(opure_ctx *ctx, const CUtensorMap &wm, const CUtensorMap &xm, const TcParams &p,
+                         uint32_t tiles, size_t smem) {
+    static_assert(EPI >= 0, "");
+    const cudaError_t e =
+        cudaFuncSetAttribute(gemm_tc_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return cuda_status(e);
+    return launch(ctx, gemm_tc_kernel<EPI>, dim3(tiles, p.splits), dim3(kThreads), smem, true, wm, xm, p);
+}
+
+}  // namespace
+
+bool gemv_tc_eligible(const opure_ctx *ctx, const opure_gemv_args *a) {
+    return ctx->ws && ctx->ws_bytes >= kTcWorkspaceBytes && a->w_dtype == OPURE_W_F16 && a->nvec >= kTcMinVec &&
+           a->cols % kTileK == 0 && a->cols <= kTcMaxCols && encode_fn() != nullptr;
+}
+
+opure_status gemv_tc(opure_ctx *ctx, const opure_gemv_args *a) {
+    const uint32_t K = a->cols, rows = a->rows;
+    const uint32_t epi = a->epilogue;
+    const uint32_t acc = epi == OPURE_EPI_SWIGLU ? 2 : 1;
+    uint8_t *ws = static_cast<uint8_t *>(ctx->ws);
+    __half *xp = reinterpret_cast<__half *>(ws + kPackOff);
+    float *xscale = reinterpret_cast<float *>(ws + kScaleOff);
+    uint32_t *tickets = reinterpret_cast<uint32_t *>(ws + kTicketOff);
+    float *partials = reinterpret_cast<float *>(ws + kPartialOff);
+    const size_t partial_cap = (ctx->ws_bytes - kPartialOff) / 4;
+
+    CUtensorMap wm;
+    if (!make_map(&wm, a->w, K, acc * rows, kTileM)) return OPURE_ERR_UNSUPPORTED;
+    const size_t pack_smem = size_t(K) * 4;
+    if (pack_smem > 48 * 1024) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(pack_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(pack_smem));
+        if (e != cudaSuccess) return cuda_status(e);
+    }
+    const uint32_t tiles = ceil_div(rows, kTileM);
+    const uint32_t ktiles = K / kTileK;
+    for (uint32_t v0 = 0; v0 < a->nvec; v0 += kMaxN) {
+        const uint32_t n = std::min(kMaxN, a->nvec - v0);
+        const uint32_t npad = (n + 15) & ~15u;
+        PackParams pp{a->x + size_t(v0) * a->x_stride, a->x_stride, K, npad, a->prologue == OPURE_PRO_RMSNORM,
+                      reinterpret_cast<const __half *>(a->norm_gain), a->eps, xp, xscale};
+        opure_status s = launch(ctx, pack_kernel, dim3(n), dim3(kPackThreads), pack_smem, true, pp);
+        if (s) return s;
+        CUtensorMap xm;
+        if (!make_map(&xm, xp, K, 2 * npad, npad)) return OPURE_ERR_UNSUPPORTED;
+
+        // K split: about one CTA per SM, partial sums must fit the workspace.
+        uint32_t splits = 1;
+        if (tiles < uint32_t(ctx->sm_count) && tiles <= kMaxTickets)
+            splits = std::max<uint32_t>(1, std::min<uint32_t>(ktiles, uint32_t(ctx->sm_count) / tiles));
+        while (splits > 1 && size_t(tiles) * splits * acc * npad * kTileM > partial_cap) --splits;
+        const uint32_t kt_per = ceil_div(ktiles, splits);
+        splits = ceil_div(ktiles, kt_per);
+
+        const uint32_t stage_bytes = acc * kTileM * 128 + 2 * npad * 128;
+        const size_t budget = std::min<size_t>(ctx->smem_optin, 227 * 1024) - 1024 - 256;
+        const uint32_t stages = std::min<uint32_t>({kMaxStages, uint32_t(budget / stage_bytes), kt_per});
+        if (stages < 1 || (stages < 2 && kt_per > 1)) return OPURE_ERR_UNSUPPORTED;
+
+        TcParams p{};
+        p.rows = rows;
+        p.n = n;
+        p.npad = npad;
+        p.ktiles = ktiles;
+        p.kt_per_split = kt_per;
+        p.splits = splits;
+        p.stages = stages;
+        p.y = a->y ? a->y + size_t(v0) * a->y_stride : nullptr;
+        p.y_stride = a->y_stride;
+        p.residual = a->residual ? a->residual + size_t(v0) * a->y_stride : nullptr;
+        p.keys = a->argmax_keys ? a->argmax_keys + v0 : nullptr;
+        p.xscale = xscale;
+        p.partials = partials;
+        p.tickets = tickets;
+        p.st = ctx->status;
+        // Request enough shared memory that no more CTAs fit on an SM than its 512 TMEM
+        // columns can serve, so tcgen05.alloc never waits on a co-resident CTA.
+        uint32_t ncols = 32;
+        while (ncols < acc * npad) ncols <<= 1;
+        const size_t per_sm = ctx->smem_optin + 1024;
+        const size_t smem = std::max<size_t>(size_t(stages) * stage_bytes + 1024, per_sm / (512 / ncols + 1) + 1);
+        if (smem > ctx->smem_optin) return OPURE_ERR_UNSUPPORTED;
+        switch (epi) {
+            case OPURE_EPI_STORE: s = launch_gemm<OPURE_EPI_STORE>(ctx, wm, xm, p, tiles, smem); break;
+            case OPURE_EPI_ADD: s = launch_gemm<OPURE_EPI_ADD>(ctx, wm, xm, p, tiles, smem); break;
+            case OPURE_EPI_SWIGLU: s = launch_gemm<OPURE_EPI_SWIGLU>(ctx, wm, xm, p, tiles, smem); break;
+            default: s = launch_gemm<OPURE_EPI_ARGMAX>(ctx, wm, xm, p, tiles, smem); break;
+        }
+        if (s) return s;
+    }
+    return OPURE_OK;
+}
+
+}  // namespace opure

@@ -4,6 +4,7 @@
 // with 4-byte loads; here a warp streams four rows with 16-byte loads and the vector is
 // shared by every row of the CTA from shared memory.
 #include "ctx.cuh"
+#include "gemm_tc.cuh"
 #include "gemv.cuh"
 
 namespace opure {
@@ -174,6 +175,8 @@ extern "C" opure_status opure_gemv(opure_ctx *ctx, const opure_gemv_args *a) {
     if ((uint64_t(a->cols) * eb) % 16 || reinterpret_cast<uintptr_t>(a->w) % 16) return OPURE_ERR_UNSUPPORTED;
     if (a->x_stride < a->cols || (a->y && a->y_stride < a->rows)) return OPURE_ERR_INVALID_ARG;
     if (a->x_stride % 4 || reinterpret_cast<uintptr_t>(a->x) % 16) return OPURE_ERR_UNSUPPORTED;
+    // Many vectors sharing the weights: a dense contraction for the tensor cores.
+    if (gemv_tc_eligible(ctx, a)) return gemv_tc(ctx, a);
 
     GemvParams p{};
     p.w = static_cast<const uint8_t *>(a->w);

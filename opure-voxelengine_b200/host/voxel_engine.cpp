@@ -348,7 +348,7 @@ void VoxelEngine::ResetSequences(const std::vector<std::vector<uint32_t>> &promp
     OPURE_CHECK(reserve <= maxLen_, "sequence exceeds the engine's maxLen");
     const graph::ModelConfig &c = graph_.Config();
     std::vector<int32_t> seq(n), pos(n, 0), known(n);
-    std::vector<uint32_t> flags(n, automatic ? OPURE_VEC_AUTO : 0u);
+    std::vector<uint32_t> flags(n, automatic ? uint32_t(OPURE_VEC_AUTO) : 0u);
     for (uint32_t v = 0; v < n; ++v) {
         OPURE_CHECK(!prompts[v].empty(), "empty prompt");
         OPURE_CHECK(prompts[v].size() <= reserve, "prompt exceeds the reserved length");
@@ -367,6 +367,7 @@ void VoxelEngine::ResetSequences(const std::vector<std::vector<uint32_t>> &promp
     OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.known, known.data(), n * 4));
     OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.flags, flags.data(), n * 4));
     hostDriven_ = !automatic;
+    seqIdentity_ = true;
     OPURE_CUDA_CHECK(opure_fill(ctx_, buf_.keys, 0, n * 8));
     OPURE_CUDA_CHECK(opure_sync(ctx_, 60000));
 }
@@ -419,6 +420,45 @@ std::vector<GenerateResult> VoxelEngine::GenerateBatch(const std::vector<std::ve
     seqLen_ = maxP + budget;
     lastTokenMs_ = budget ? double(dec) / budget : 0.0;
     return out;
+}
+
+std::vector<uint32_t> VoxelEngine::PrefillBatch(const std::vector<std::vector<uint32_t>> &prompts,
+                                                uint32_t reserve, bool logits) {
+    OPURE_CHECK(ready_, "engine used before Initialize");
+    const uint32_t n = uint32_t(prompts.size());
+    const size_t len = prompts.front().size();
+    for (const auto &p : prompts) OPURE_CHECK(p.size() == len, "PrefillBatch needs prompts of equal length");
+    ResetSequences(prompts, reserve, true);
+    RunSteps(n, uint32_t(len), logits);
+    Sync();
+    std::vector<unsigned long long> keys(n);
+    OPURE_CUDA_CHECK(opure_d2h(ctx_, keys.data(), buf_.keys, n * 8));
+    OPURE_CUDA_CHECK(opure_sync(ctx_, 60000));
+    std::vector<uint32_t> next(n);
+    for (uint32_t v = 0; v < n; ++v) next[v] = 0xffffffffu - uint32_t(keys[v] & 0xffffffffull);
+    return next;
+}
+
+void VoxelEngine::SetVectors(const int32_t *seq, const int32_t *pos, const int32_t *tok, uint32_t n) {
+    OPURE_CHECK(n >= 1 && n <= opts_.maxBatch, "more token vectors than maxBatch");
+    const uint32_t V = graph_.Config().vocabSize;
+    for (uint32_t v = 0; v < n; ++v) {
+        OPURE_CHECK(seq[v] >= 0 && uint32_t(seq[v]) < opts_.maxBatch, "sequence slot out of range");
+        OPURE_CHECK(pos[v] >= 0 && uint32_t(pos[v]) < maxLen_, "position exceeds the engine's maxLen");
+        OPURE_CHECK(tok[v] >= 0 && uint32_t(tok[v]) < V, "token id out of vocabulary range");
+        OPURE_CHECK(kv_.Reserve(uint32_t(seq[v]), uint32_t(pos[v]) + 1), "KV cache has no room for the sequence");
+    }
+    kv_.SyncTable();
+    // Pageable sources: staged before the calls return, so the arrays may be reused.
+    OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.seq, seq, n * 4));
+    OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.pos, pos, n * 4));
+    OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.inTokens, tok, n * 4));
+    seqIdentity_ = false;
+    if (!hostDriven_) {
+        const std::vector<uint32_t> zero(opts_.maxBatch, 0u);
+        OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.flags, zero.data(), zero.size() * 4));
+        hostDriven_ = true;
+    }
 }
 
 GenerateResult VoxelEngine::Generate(const std::vector<uint32_t> &tokens, const EngineOptions &opts) {
@@ -478,6 +518,13 @@ void VoxelEngine::DecodeStepBatch(const int32_t *tokens, const int32_t *position
         io[opts_.maxBatch + v] = positions[v];
     }
     kv_.SyncTable();
+    if (!seqIdentity_) {
+        // SetVectors may have pointed vectors at other slots; vector v is slot v here.
+        std::vector<int32_t> ident(opts_.maxBatch);
+        for (uint32_t v = 0; v < opts_.maxBatch; ++v) ident[v] = int32_t(v);
+        OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.seq, ident.data(), ident.size() * 4));
+        seqIdentity_ = true;
+    }
     if (!hostDriven_) {
         // Token and position now come from the host: clear the self-driving flag.
         const std::vector<uint32_t> zero(opts_.maxBatch, 0u);

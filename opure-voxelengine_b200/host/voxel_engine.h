@@ -117,6 +117,17 @@ public:
 
     // Enqueues `steps` decode steps for the first n vectors (graph replays when enabled).
     void RunSteps(uint32_t n, uint32_t steps, bool logits);
+
+    // Building blocks of multi-engine loops (speculative decoding):
+    // prefill independent prompts of equal length into slots 0..n-1 (reserving `reserve`
+    // positions each) and return the greedy next token of each;
+    std::vector<uint32_t> PrefillBatch(const std::vector<std::vector<uint32_t>> &prompts, uint32_t reserve,
+                                       bool logits);
+    // describe the next step's n token vectors: sequence slot, position and token of each
+    // (host-driven: no argmax feedback, positions not advanced);
+    void SetVectors(const int32_t *seq, const int32_t *pos, const int32_t *tok, uint32_t n);
+    float *DeviceLogits() const { return buf_.logits; }       // [maxBatch][vocab]
+    unsigned long long *DeviceKeys() const { return buf_.keys; }
     // Rewinds the positions of vectors 0..n-1 (stream-ordered, no wait).
     void SetPositions(const int32_t *positions, uint32_t n);
     void Sync();
@@ -161,6 +172,7 @@ private:
     std::map<uint32_t, std::pair<void *, size_t>> attnScratch_;
     void *hostIo_ = nullptr;  // pinned staging of the host-driven step
     bool hostDriven_ = false; // step flags currently cleared for host-supplied tokens
+    bool seqIdentity_ = true; // vector v currently maps to sequence slot v
 };
 
 }  // namespace opure::engine

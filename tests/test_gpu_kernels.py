@@ -302,6 +302,92 @@ def test_gemv_writes_every_output(ctx):
         assert not np.isnan(y).any()
 
 
+# ---- tensor-core path (16..256 vectors per pass: batched decode, verify pass) ----------
+# The vectors are split into fp16 hi + lo halves, so the result keeps fp32-GEMV accuracy:
+# besides the 1e-3 gate, the error must stay within TC_REL of the double-precision oracle.
+TC_REL = 2e-5
+
+
+@pytest.mark.parametrize("rows,cols,nvec", [(576, 576, 16), (960, 576, 64), (576, 1536, 64),
+                                            (192, 576, 144), (1000, 576, 300), (2048, 8192, 64)])
+def test_gemv_tc_store(ctx, rows, cols, nvec):
+    rng = np.random.default_rng(rows + cols + nvec)
+    w = f16(rng.standard_normal((rows, cols)).astype(np.float32) * 0.02)
+    x = rng.standard_normal((nvec, cols)).astype(np.float32) * np.float32(3.0)
+    y = gemv_gpu(ctx, w, x)
+    want = oracle.gemv_f16(w, x)
+    err = rel_err(y, want)
+    assert err < TC_REL, err
+
+
+def test_gemv_tc_rmsnorm_add(ctx):
+    rng = np.random.default_rng(31)
+    rows, cols, nvec = 576, 576, 64
+    w = f16(rng.standard_normal((rows, cols)).astype(np.float32) * 0.02)
+    x = rng.standard_normal((nvec, cols)).astype(np.float32)
+    x[3] *= 1e-4                                 # per-vector scales differ widely
+    x[5] *= 1e3
+    g = f16(1.0 + 0.1 * rng.standard_normal(cols).astype(np.float32))
+    res = rng.standard_normal((nvec, rows)).astype(np.float32)
+    y = gemv_gpu(ctx, w, x, pro=cu.PRO_RMSNORM, gain=g, epi=cu.EPI_ADD, residual=res)
+    xn = np.stack([oracle.rmsnorm(x[v], oracle.f16_to_f32(g), 1e-5) for v in range(nvec)])
+    want = res + oracle.gemv_f16(w, xn)
+    assert rel_err(y, want) < TC_REL
+
+
+def test_gemv_tc_unnormalised_scales(ctx):
+    # Without a norm the per-vector power-of-two scale carries vectors far outside
+    # fp16's range (and far below it) through the fp16 halves.
+    rng = np.random.default_rng(32)
+    rows, cols, nvec = 576, 1536, 32
+    w = f16(rng.standard_normal((rows, cols)).astype(np.float32) * 0.02)
+    x = rng.standard_normal((nvec, cols)).astype(np.float32)
+    x *= (10.0 ** rng.uniform(-6, 6, size=(nvec, 1))).astype(np.float32)
+    y = gemv_gpu(ctx, w, x)
+    want = oracle.gemv_f16(w, x)
+    for v in range(nvec):
+        assert rel_err(y[v], want[v]) < TC_REL, v
+
+
+@pytest.mark.parametrize("nvec", [16, 64, 80])
+def test_gemv_tc_swiglu(ctx, nvec):
+    rng = np.random.default_rng(40 + nvec)
+    ff, cols = 1536, 576
+    w = f16(rng.standard_normal((2 * ff, cols)).astype(np.float32) * 0.02)
+    x = rng.standard_normal((nvec, cols)).astype(np.float32)
+    g = f16(np.ones(cols, np.float32))
+    y = gemv_gpu(ctx, w, x, pro=cu.PRO_RMSNORM, gain=g, epi=cu.EPI_SWIGLU, rows=ff)
+    xn = np.stack([oracle.rmsnorm(x[v], np.ones(cols, np.float32), 1e-5) for v in range(nvec)])
+    gu = oracle.gemv_f16(w, xn)
+    want = np.stack([oracle.swiglu(gu[v, :ff], gu[v, ff:]) for v in range(nvec)])
+    assert rel_err(y, want) < TC_REL
+
+
+def test_gemv_tc_argmax_lm_head(ctx):
+    rng = np.random.default_rng(41)
+    rows, cols, nvec = 49152, 576, 64
+    w = f16(rng.standard_normal((rows, cols)).astype(np.float32) * 0.02)
+    x = rng.standard_normal((nvec, cols)).astype(np.float32)
+    g = f16(np.ones(cols, np.float32))
+    y, idx = gemv_gpu(ctx, w, x, pro=cu.PRO_RMSNORM, gain=g, epi=cu.EPI_ARGMAX)
+    xn = np.stack([oracle.rmsnorm(x[v], np.ones(cols, np.float32), 1e-5) for v in range(nvec)])
+    logits = oracle.gemv_f16(w, xn)
+    assert rel_err(y, logits) < TC_REL
+    want, _ = oracle.argmax(logits)
+    assert list(idx) == list(want)
+
+
+def test_gemv_tc_matches_cuda_core_path(ctx):
+    # 15 vectors run on the CUDA-core GEMV, 16 on the tensor cores: same results to
+    # within fp32 rounding.
+    rng = np.random.default_rng(42)
+    w = f16(rng.standard_normal((960, 576)).astype(np.float32) * 0.02)
+    x = rng.standard_normal((16, 576)).astype(np.float32)
+    y16 = gemv_gpu(ctx, w, x)
+    y15 = gemv_gpu(ctx, w, x[:15])
+    assert rel_err(y16[:15], y15) < TC_REL
+
+
 # ---- RoPE + KV append, embedding ------------------------------------------------------
 @pytest.mark.parametrize("pos", [0, 1, 157, 4095])
 def test_rope_kv_append(ctx, pos):
