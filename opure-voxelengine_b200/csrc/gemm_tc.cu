@@ -17,8 +17,9 @@
 //          tcgen05.commit. The four warps then read the accumulator rows with tcgen05.ld
 //          (warp w owns TMEM lanes 32w..32w+31 = tile rows) and apply the epilogue:
 //          store, residual add, SwiGLU, or argmax keys (+ logits). With a K split every
-//          CTA stores fp32 partials and the last CTA of the tile (ticket counter) adds
-//          them in split order, so results do not depend on arrival order.
+//          CTA adds its sums into a 64-bit fixed-point accumulator with integer atomics
+//          and the last CTA of the tile (ticket counter) converts them and runs the
+//          epilogue, so results do not depend on the order the splits finish in.
 // All waits are bounded (1 s); a timeout is reported in the ctx status word and the CTA
 // still releases its TMEM. No TMA multicast is used.
 #include <cuda.h>
@@ -203,7 +204,7 @@ struct TcParams {
     const float *residual;
     unsigned long long *keys;
     const float *xscale;
-    float *partials;    // [tiles][splits][accumulators * npad][128]
+    long long *accum;   // [tiles][accumulators * npad][128] fixed-point split-K sums
     uint32_t *tickets;  // [tiles]
     DeviceStatus *st;
 };
@@ -218,6 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __shared__ uint32_t tmem_base;
     __shared__ int fail, last;
     __shared__ uint32_t issued_s, consumed_s;
+    __shared__ float s_scale[kMaxN];
 
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t tile = blockIdx.x, split = blockIdx.y;
@@ -251,70 +253,78 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = tmem_base;
 
-    if (threadIdx.x == 0) {
-        // Producer. Weight tiles do not depend on earlier kernels: the first stages are
-        // requested before waiting on them; the packed vectors only after.
-        const uint32_t pre = min(p.stages, nk);
+    // Producer (warp 0, one lane). Weight tiles do not depend on earlier kernels: the
+    // first stages are requested before waiting on them; the packed vectors only after.
+    const uint32_t pre = min(p.stages, nk);
+    if (warp == 0 && lane == 0)
         for (uint32_t i = 0; i < pre; ++i) {
             mbar_expect_tx(&full[i], stage_bytes);
             tma_load_2d(a_tile(i, 0), &wmap, (kt0 + i) * kTileK, m0, &full[i]);
             if (kSwiglu) tma_load_2d(a_tile(i, 1), &wmap, (kt0 + i) * kTileK, p.rows + m0, &full[i]);
         }
-        grid_dependency_wait();
-        for (uint32_t i = 0; i < pre; ++i) {
-            tma_load_2d(b_tile(i, 0), &xmap, (kt0 + i) * kTileK, 0, &full[i]);
-            tma_load_2d(b_tile(i, 1), &xmap, (kt0 + i) * kTileK, p.npad, &full[i]);
-        }
-        uint32_t i = pre;
-        for (; i < nk; ++i) {
-            const uint32_t s = i % p.stages;
-            if (!mbar_wait(&empty[s], ((i / p.stages) & 1u) ^ 1u)) {
-                report(p.st, OPURE_ERR_DEVICE_TIMEOUT, 60, blockIdx.x);
-                fail = 1;
-                break;
-            }
-            mbar_expect_tx(&full[s], stage_bytes);
-            tma_load_2d(a_tile(s, 0), &wmap, (kt0 + i) * kTileK, m0, &full[s]);
-            if (kSwiglu) tma_load_2d(a_tile(s, 1), &wmap, (kt0 + i) * kTileK, p.rows + m0, &full[s]);
-            tma_load_2d(b_tile(s, 0), &xmap, (kt0 + i) * kTileK, 0, &full[s]);
-            tma_load_2d(b_tile(s, 1), &xmap, (kt0 + i) * kTileK, p.npad, &full[s]);
-        }
-        issued_s = i;
-    } else {
-        grid_dependency_wait();
-    }
+    grid_dependency_wait();
     grid_dependents_launch();
+    // Per-vector scales written by the pack kernel (read after the wait).
+    for (uint32_t v = threadIdx.x; v < p.npad; v += blockDim.x) s_scale[v] = v < p.n ? p.xscale[v] : 0.f;
 
-    if (threadIdx.x == 32) {
-        // MMA issuer: per 64-wide K tile, four K=16 steps (32 bytes along the swizzled
-        // rows) of hi and lo products.
-        const uint32_t idesc = (1u << 4) | ((p.npad >> 3) << 17) | ((kTileM >> 4) << 24);
-        uint32_t i = 0;
-        for (; i < nk; ++i) {
-            const uint32_t s = i % p.stages;
-            if (!mbar_wait(&full[s], (i / p.stages) & 1u)) {
-                report(p.st, OPURE_ERR_DEVICE_TIMEOUT, 61, blockIdx.x);
-                fail = 1;
-                break;
+    if (warp == 0) {
+        if (lane == 0) {
+            for (uint32_t i = 0; i < pre; ++i) {
+                tma_load_2d(b_tile(i, 0), &xmap, (kt0 + i) * kTileK, 0, &full[i]);
+                tma_load_2d(b_tile(i, 1), &xmap, (kt0 + i) * kTileK, p.npad, &full[i]);
             }
-            tc_fence_after();
-            const uint32_t a0 = smem_addr(a_tile(s, 0)), bh = smem_addr(b_tile(s, 0)), bl = smem_addr(b_tile(s, 1));
-#pragma unroll
-            for (uint32_t k = 0; k < kTileK / 16; ++k) {
-                const uint64_t dh = smem_desc(bh + 32 * k), dl = smem_desc(bl + 32 * k);
-                const uint64_t da = smem_desc(a0 + 32 * k);
-                mma_f16(tmem, da, dh, idesc, (i | k) != 0);
-                mma_f16(tmem, da, dl, idesc, 1);
-                if (kSwiglu) {
-                    const uint64_t du = smem_desc(smem_addr(a_tile(s, 1)) + 32 * k);
-                    mma_f16(tmem + p.npad, du, dh, idesc, (i | k) != 0);
-                    mma_f16(tmem + p.npad, du, dl, idesc, 1);
+            uint32_t i = pre;
+            for (; i < nk; ++i) {
+                const uint32_t s = i % p.stages;
+                if (!mbar_wait(&empty[s], ((i / p.stages) & 1u) ^ 1u)) {
+                    report(p.st, OPURE_ERR_DEVICE_TIMEOUT, 60, blockIdx.x);
+                    fail = 1;
+                    break;
                 }
+                mbar_expect_tx(&full[s], stage_bytes);
+                tma_load_2d(a_tile(s, 0), &wmap, (kt0 + i) * kTileK, m0, &full[s]);
+                if (kSwiglu) tma_load_2d(a_tile(s, 1), &wmap, (kt0 + i) * kTileK, p.rows + m0, &full[s]);
+                tma_load_2d(b_tile(s, 0), &xmap, (kt0 + i) * kTileK, 0, &full[s]);
+                tma_load_2d(b_tile(s, 1), &xmap, (kt0 + i) * kTileK, p.npad, &full[s]);
             }
-            mma_commit(&empty[s]);
+            issued_s = i;
         }
-        consumed_s = i;
-        mma_commit(&done);
+        // The other lanes park here rather than spinning beside the issuing lane.
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // MMA issuer: per 64-wide K tile, four K=16 steps (32 bytes along the swizzled
+            // rows) of hi and lo products.
+            const uint32_t idesc = (1u << 4) | ((p.npad >> 3) << 17) | ((kTileM >> 4) << 24);
+            uint32_t i = 0;
+            for (; i < nk; ++i) {
+                const uint32_t s = i % p.stages;
+                if (!mbar_wait(&full[s], (i / p.stages) & 1u)) {
+                    report(p.st, OPURE_ERR_DEVICE_TIMEOUT, 61, blockIdx.x);
+                    fail = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a0 = smem_addr(a_tile(s, 0)), bh = smem_addr(b_tile(s, 0));
+                const uint32_t bl = smem_addr(b_tile(s, 1));
+#pragma unroll
+                for (uint32_t k = 0; k < kTileK / 16; ++k) {
+                    const uint64_t dh = smem_desc(bh + 32 * k), dl = smem_desc(bl + 32 * k);
+                    const uint64_t da = smem_desc(a0 + 32 * k);
+                    mma_f16(tmem, da, dh, idesc, (i | k) != 0);
+                    mma_f16(tmem, da, dl, idesc, 1);
+                    if (kSwiglu) {
+                        const uint64_t du = smem_desc(smem_addr(a_tile(s, 1)) + 32 * k);
+                        mma_f16(tmem + p.npad, du, dh, idesc, (i | k) != 0);
+                        mma_f16(tmem + p.npad, du, dl, idesc, 1);
+                    }
+                }
+                mma_commit(&empty[s]);
+            }
+            consumed_s = i;
+            mma_commit(&done);
+        }
+        __syncwarp();
     }
 
     // Epilogue: every thread owns one tile row (TMEM lane).
@@ -332,16 +342,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t taddr = tmem + ((warp * 32) << 16);
         const uint32_t acc_cols = kAcc * p.npad;
         bool run_epi = true;
-        float *part = nullptr;
+        long long *acc64 = nullptr;
         if (p.splits > 1) {
-            // Partial sums of this split, column-major so a warp's stores are contiguous.
-            part = p.partials + size_t(tile) * p.splits * acc_cols * kTileM;
-            float *mine = part + size_t(split) * acc_cols * kTileM;
+            // K split: add this split's sums into the tile's 64-bit fixed-point (2^-32)
+            // accumulator; integer adds are associative, so the total does not depend on
+            // the order the splits arrive in. Column-major: a warp's adds are contiguous.
+            acc64 = p.accum + size_t(tile) * acc_cols * kTileM;
             for (uint32_t c0 = 0; c0 < acc_cols; c0 += 16) {
                 float r[16];
                 tmem_ld16(taddr + c0, r);
 #pragma unroll
-                for (int j = 0; j < 16; ++j) mine[size_t(c0 + j) * kTileM + lrow] = r[j];
+                for (int j = 0; j < 16; ++j)
+                    atomicAdd(reinterpret_cast<unsigned long long *>(acc64 + size_t(c0 + j) * kTileM + lrow),
+                              static_cast<unsigned long long>(to_fix(r[j])));
             }
             __threadfence();
             __syncthreads();
@@ -355,41 +368,53 @@ __global__ void __launch_bounds__(kThreads, 1)
             __threadfence();
         }
         if (run_epi) {
+            // Full sums of 16 columns of this thread's row (the last split also clears the
+            // accumulator for the next call).
             auto column = [&](uint32_t c, float (&r)[16]) {
                 if (p.splits == 1) {
                     tmem_ld16(taddr + c, r);
                 } else {
+                    long long a[16];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) r[j] = 0.f;
-                    for (uint32_t s = 0; s < p.splits; ++s) {
-                        const float *src = part + size_t(s) * acc_cols * kTileM;
+                    for (int j = 0; j < 16; ++j) a[j] = __ldcg(acc64 + size_t(c + j) * kTileM + lrow);
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) r[j] += __ldcg(src + size_t(c + j) * kTileM + lrow);
+                    for (int j = 0; j < 16; ++j) {
+                        acc64[size_t(c + j) * kTileM + lrow] = 0;
+                        r[j] = float(double(a[j]) * kFixInv);
                     }
                 }
             };
+            // Per 16 columns: every global load (the residual) is issued before any store,
+            // and the vector scales come from shared memory, so a thread pays one memory
+            // round trip per chunk rather than one per column.
             const bool in = row < p.rows;
             for (uint32_t c0 = 0; c0 < p.npad; c0 += 16) {
-                float g[16], u[16];
+                float g[16], u[16], res[16];
                 column(c0, g);
                 if (kSwiglu) column(p.npad + c0, u);
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
+                    res[j] = 0.f;
+                    if constexpr (EPI == OPURE_EPI_ADD)
+                        if (in && c0 + j < p.n) res[j] = p.residual[size_t(c0 + j) * p.y_stride + row];
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
                     const uint32_t v = c0 + j;
-                    if (v >= p.n) break;
-                    const float val = g[j] * p.xscale[v];
+                    const bool ok = in && v < p.n;
+                    const float val = g[j] * s_scale[v];
                     const size_t o = size_t(v) * p.y_stride + row;
                     if constexpr (EPI == OPURE_EPI_STORE) {
-                        if (in) p.y[o] = val;
+                        if (ok) p.y[o] = val;
                     } else if constexpr (EPI == OPURE_EPI_ADD) {
-                        if (in) p.y[o] = p.residual[o] + val;
+                        if (ok) p.y[o] = res[j] + val;
                     } else if constexpr (EPI == OPURE_EPI_SWIGLU) {
-                        const float uv = u[j] * p.xscale[v];
+                        const float uv = u[j] * s_scale[v];
                         const float sg = 1.0f / (1.0f + expf(-val));
-                        if (in) p.y[o] = (val * sg) * uv;
+                        if (ok) p.y[o] = (val * sg) * uv;
                     } else {
-                        if (in && p.y) p.y[o] = val;
-                        const unsigned long long k = warp_max_u64(in ? argmax_key(val, row) : 0ull);
+                        if (ok && p.y) p.y[o] = val;
+                        const unsigned long long k = warp_max_u64(ok ? argmax_key(val, row) : 0ull);
                         if (lane == 0 && k) atomicMax(p.keys + v, k);
                     }
                 }
@@ -453,8 +478,8 @@ opure_status gemv_tc(opure_ctx *ctx, const opure_gemv_args *a) {
     __half *xp = reinterpret_cast<__half *>(ws + kPackOff);
     float *xscale = reinterpret_cast<float *>(ws + kScaleOff);
     uint32_t *tickets = reinterpret_cast<uint32_t *>(ws + kTicketOff);
-    float *partials = reinterpret_cast<float *>(ws + kPartialOff);
-    const size_t partial_cap = (ctx->ws_bytes - kPartialOff) / 4;
+    long long *accum = reinterpret_cast<long long *>(ws + kPartialOff);
+    const size_t accum_cap = (ctx->ws_bytes - kPartialOff) / 8;
 
     CUtensorMap wm;
     if (!make_map(&wm, a->w, K, acc * rows, kTileM)) return OPURE_ERR_UNSUPPORTED;
@@ -480,7 +505,7 @@ opure_status gemv_tc(opure_ctx *ctx, const opure_gemv_args *a) {
         uint32_t splits = 1;
         if (tiles < uint32_t(ctx->sm_count) && tiles <= kMaxTickets)
             splits = std::max<uint32_t>(1, std::min<uint32_t>(ktiles, uint32_t(ctx->sm_count) / tiles));
-        while (splits > 1 && size_t(tiles) * splits * acc * npad * kTileM > partial_cap) --splits;
+        if (size_t(tiles) * acc * npad * kTileM > accum_cap) splits = 1;
         const uint32_t kt_per = ceil_div(ktiles, splits);
         splits = ceil_div(ktiles, kt_per);
 
@@ -502,7 +527,7 @@ opure_status gemv_tc(opure_ctx *ctx, const opure_gemv_args *a) {
         p.residual = a->residual ? a->residual + size_t(v0) * a->y_stride : nullptr;
         p.keys = a->argmax_keys ? a->argmax_keys + v0 : nullptr;
         p.xscale = xscale;
-        p.partials = partials;
+        p.accum = accum;
         p.tickets = tickets;
         p.st = ctx->status;
         // Request enough shared memory that no more CTAs fit on an SM than its 512 TMEM
