@@ -337,6 +337,23 @@ opure_status opure_spec_accept(opure_ctx *ctx, const opure_spec_args *a);
 opure_status opure_sample_softmax(opure_ctx *ctx, const float *logits, uint32_t vocab,
                                   uint32_t rows, const float *u, int32_t *out_tokens);
 
+/* The same draw, written as an argmax key into keys[row] so that the next self-driving
+ * decode step (OPURE_VEC_AUTO) takes the sampled token as its input: the draft model's
+ * sampling step of speculative decoding. With save != NULL row r is also copied to
+ * save + r * save_stride (the draft distribution the accept step needs). */
+opure_status opure_sample_keys(opure_ctx *ctx, const float *logits, uint32_t vocab, uint32_t rows,
+                               const float *u, unsigned long long *keys, float *save,
+                               size_t save_stride);
+
+/* Speculative round bookkeeping without a host round trip. For each sequence slot s whose
+ * round starts at position base[s]: the draft's proposals d_1..d_k are read from its
+ * token history hist[s][base+1 .. base+k-1] (the inputs of its later self-driving steps)
+ * and from keys[s] (the last step's result, d_k); writes the target's verify inputs
+ * verify_tokens[s][0..k] = (hist[s][base], d_1..d_k) and draft[s][0..k-1] = d_1..d_k. */
+opure_status opure_spec_gather(opure_ctx *ctx, const int32_t *hist, uint32_t max_len,
+                               const unsigned long long *keys, const int32_t *base, uint32_t n_seq,
+                               uint32_t k, int32_t *verify_tokens, int32_t *draft);
+
 /* ---- fault injection (host side; tests of the error paths) -----------------
  * The next `count` ABI calls after `after_calls` more calls return OPURE_ERR_INJECTED
  * without touching the GPU. count = 0 disarms. */

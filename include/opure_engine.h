@@ -104,6 +104,41 @@ opure_status opure_engine_poison(opure_engine *e, float value);
  * (synthetic long contexts for the large-model configuration). */
 opure_status opure_engine_load_kv(opure_engine *e, uint32_t seq, const uint16_t *kv, uint32_t len);
 
+/* ---- speculative decoding (no reference counterpart: the reference's verify shader,
+ *      Opure_SpeculativeDecode.usf:60-189, is never dispatched and it has no draft loop
+ *      or accept rule; speculativeAcceptance is fixed at -1, Opure_VoxelEngine.cpp:666) */
+
+/* An engine that enqueues on `share`'s ctx (stream) instead of its own, so a draft and a
+ * target engine can hand data to each other in stream order. `share` must outlive it. */
+opure_status opure_engine_create_shared(const char *model_dir, opure_engine *share,
+                                        const opure_engine_options *opts, opure_engine **out);
+
+typedef struct opure_spec_options {
+    uint32_t k;               /* draft tokens per round (1..64)                         */
+    uint32_t mode;            /* OPURE_SPEC_GREEDY or OPURE_SPEC_REJECTION (temperature 1) */
+    uint64_t seed;            /* sequence s draws uniforms from Rng(seed ^ s * 0x9E3779B97F4A7C15) */
+} opure_spec_options;
+
+typedef struct opure_spec_stats {
+    uint32_t rounds;
+    uint64_t drafted, accepted;   /* proposals to still-generating sequences, accepted   */
+    double draft_ms, verify_ms, total_ms;   /* device time of draft steps, verify + accept */
+} opure_spec_stats;
+
+/* Speculative decoding of n_seq prompts of length prompt_len (concatenated in `prompts`)
+ * into out_tokens[n_seq][budget]: per round the draft engine proposes k tokens per
+ * sequence, the target verifies the k+1 positions of all sequences in one batched step,
+ * and opure_spec_accept keeps the accepted prefix plus one target token. `draft` must be
+ * created with opure_engine_create_shared(…, target, …); target max_batch >= n_seq (k+1),
+ * draft max_batch >= n_seq, both max_len >= prompt_len + budget + k + 2. accept_log
+ * (may be NULL) receives up to accept_log_rounds rounds of n_seq accepted counts (-1 for
+ * a finished sequence); stats may be NULL. */
+opure_status opure_engine_spec_generate(opure_engine *target, opure_engine *draft, const int32_t *prompts,
+                                        uint32_t prompt_len, uint32_t n_seq, uint32_t budget,
+                                        const opure_spec_options *o, int32_t *out_tokens,
+                                        int32_t *accept_log, uint32_t accept_log_rounds,
+                                        opure_spec_stats *stats);
+
 /* Parses config.json, maps model.safetensors, resolves tensor roles and plans the device
  * layout without touching a GPU (the reference's opure_inspect tool, Opure_Inspect.cpp).
  * On failure the reason is copied to err (err_len bytes, may be NULL). */

@@ -209,20 +209,54 @@ __global__ void __launch_bounds__(kThreads) spec_kernel(opure_spec_args a) {
     }
 }
 
-__global__ void __launch_bounds__(kThreads) sample_kernel(const float *logits, uint32_t V,
-                                                          const float *u, int32_t *out) {
+// One row per CTA: inverse-CDF draw from softmax(logits[row]) with u[row]. The token
+// goes to out[row] and/or, as an argmax key, to keys[row] (where a self-driving decode
+// step picks up its next input); `save` receives a copy of the row when given.
+__global__ void __launch_bounds__(kThreads) sample_kernel(const float *logits, uint32_t V, const float *u,
+                                                          int32_t *out, unsigned long long *keys, float *save,
+                                                          size_t save_stride) {
     __shared__ unsigned long long red[32];
     __shared__ double dred[32];
     __shared__ uint32_t pick;
     grid_dependency_wait();
     grid_dependents_launch();
     const float *p = logits + size_t(blockIdx.x) * V;
+    if (save)
+        for (uint32_t x = threadIdx.x; x < V; x += blockDim.x) save[size_t(blockIdx.x) * save_stride + x] = p[x];
     const double pm = block_max_logit(p, V, red);
     double z = 0.0;
     for (uint32_t x = threadIdx.x; x < V; x += blockDim.x) z += exp(double(p[x]) - pm);
     z = block_sum_d(z, dred);
     const uint32_t t = block_inverse_cdf(V, double(u[blockIdx.x]), [&](uint32_t x) { return exp(double(p[x]) - pm) / z; }, dred, &pick);
-    if (threadIdx.x == 0) out[blockIdx.x] = int32_t(t);
+    if (threadIdx.x == 0) {
+        if (out) out[blockIdx.x] = int32_t(t);
+        if (keys) keys[blockIdx.x] = argmax_key(0.f, t);
+    }
+}
+
+// Per sequence s (one thread each): the draft's proposals d_1..d_k for the round that
+// starts at position base[s] are hist[s][base+1 .. base+k-1] (inputs of the draft's
+// later steps) and the last step's key (d_k). Writes the target's k+1 verify inputs
+// (hist[s][base], d_1..d_k) and the k drafts.
+__global__ void gather_kernel(const int32_t *hist, uint32_t max_len, const unsigned long long *keys,
+                              const int32_t *base, uint32_t n_seq, uint32_t k, int32_t *verify, int32_t *draft,
+                              DeviceStatus *st) {
+    grid_dependency_wait();
+    grid_dependents_launch();
+    const uint32_t s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= n_seq) return;
+    const int32_t b = base[s];
+    if (b < 0 || uint32_t(b) + k > max_len) {
+        report(st, OPURE_ERR_DEVICE_BOUNDS, 70, uint32_t(b));
+        return;
+    }
+    const int32_t *h = hist + size_t(s) * max_len;
+    verify[size_t(s) * (k + 1)] = h[b];
+    for (uint32_t j = 1; j <= k; ++j) {
+        const int32_t d = j < k ? h[b + j] : int32_t(argmax_key_index(keys[s]));
+        verify[size_t(s) * (k + 1) + j] = d;
+        draft[size_t(s) * k + j - 1] = d;
+    }
 }
 
 }  // namespace
@@ -248,5 +282,28 @@ extern "C" opure_status opure_sample_softmax(opure_ctx *ctx, const float *logits
     if (s) return s;
     if (!logits || !u || !out || !vocab) return OPURE_ERR_INVALID_ARG;
     if (rows == 0) return OPURE_OK;
-    return launch(ctx, sample_kernel, dim3(rows), dim3(kThreads), 0, true, logits, vocab, u, out);
+    return launch(ctx, sample_kernel, dim3(rows), dim3(kThreads), 0, true, logits, vocab, u, out,
+                  static_cast<unsigned long long *>(nullptr), static_cast<float *>(nullptr), size_t(0));
+}
+
+extern "C" opure_status opure_sample_keys(opure_ctx *ctx, const float *logits, uint32_t vocab, uint32_t rows,
+                                          const float *u, unsigned long long *keys, float *save,
+                                          size_t save_stride) {
+    opure_status s = enter(ctx);
+    if (s) return s;
+    if (!logits || !u || !keys || !vocab || (save && save_stride < vocab)) return OPURE_ERR_INVALID_ARG;
+    if (rows == 0) return OPURE_OK;
+    return launch(ctx, sample_kernel, dim3(rows), dim3(kThreads), 0, true, logits, vocab, u,
+                  static_cast<int32_t *>(nullptr), keys, save, save_stride);
+}
+
+extern "C" opure_status opure_spec_gather(opure_ctx *ctx, const int32_t *hist, uint32_t max_len,
+                                          const unsigned long long *keys, const int32_t *base, uint32_t n_seq,
+                                          uint32_t k, int32_t *verify_tokens, int32_t *draft) {
+    opure_status s = enter(ctx);
+    if (s) return s;
+    if (!hist || !keys || !base || !verify_tokens || !draft || k == 0 || max_len == 0) return OPURE_ERR_INVALID_ARG;
+    if (n_seq == 0) return OPURE_OK;
+    return launch(ctx, gather_kernel, dim3(ceil_div(n_seq, 128)), dim3(128), 0, true, hist, max_len, keys, base,
+                  n_seq, k, verify_tokens, draft, ctx->status);
 }

@@ -1,4 +1,5 @@
 // engine_abi.cpp -- extern "C" surface of the host engine (include/opure_engine.h).
+#include <algorithm>
 #include <cstring>
 #include <exception>
 #include <new>
@@ -6,6 +7,7 @@
 
 #include "opure_engine.h"
 #include "platform.h"
+#include "spec_decode.h"
 #include "synth.h"
 #include "voxel_engine.h"
 
@@ -49,26 +51,30 @@ std::vector<uint32_t> ToU32(const int32_t *t, uint32_t n) {
 
 extern "C" {
 
-opure_status opure_engine_create(const char *model_dir, int device, const opure_engine_options *o,
-                                 opure_engine **out) {
+namespace {
+
+opure::engine::EngineOptions ToOptions(const opure_engine_options *o) {
+    opure::engine::EngineOptions opts;
+    if (o) {
+        if (o->max_new_tokens) opts.maxNewTokens = o->max_new_tokens;
+        if (o->max_batch) opts.maxBatch = o->max_batch;
+        opts.maxLen = o->max_len;
+        if (o->page_size) opts.pageSize = o->page_size;
+        opts.pageSeed = o->page_seed;
+        opts.useGraphs = o->use_graphs != 0;
+        if (o->attn_scale != 0.f) opts.attnScale = o->attn_scale;
+        opts.path = o->path;
+    }
+    return opts;
+}
+
+opure_status Create(const char *model_dir, int device, opure_ctx *shared, const opure_engine_options *o,
+                    opure_engine **out) {
     if (!model_dir || !out) return OPURE_ERR_INVALID_ARG;
     *out = nullptr;
     auto *e = new (std::nothrow) opure_engine;
     if (!e) return OPURE_ERR_OUT_OF_MEMORY;
-    const opure_status s = Guard(e, [&] {
-        opure::engine::EngineOptions opts;
-        if (o) {
-            if (o->max_new_tokens) opts.maxNewTokens = o->max_new_tokens;
-            if (o->max_batch) opts.maxBatch = o->max_batch;
-            opts.maxLen = o->max_len;
-            if (o->page_size) opts.pageSize = o->page_size;
-            opts.pageSeed = o->page_seed;
-            opts.useGraphs = o->use_graphs != 0;
-            if (o->attn_scale != 0.f) opts.attnScale = o->attn_scale;
-            opts.path = o->path;
-        }
-        e->eng.Initialize(model_dir, opts, device);
-    });
+    const opure_status s = Guard(e, [&] { e->eng.Initialize(model_dir, ToOptions(o), device, shared); });
     if (s != OPURE_OK) {
         g_create_error = e->err;
         delete e;
@@ -76,6 +82,58 @@ opure_status opure_engine_create(const char *model_dir, int device, const opure_
     }
     *out = e;
     return OPURE_OK;
+}
+
+}  // namespace
+
+opure_status opure_engine_create(const char *model_dir, int device, const opure_engine_options *o,
+                                 opure_engine **out) {
+    return Create(model_dir, device, nullptr, o, out);
+}
+
+opure_status opure_engine_create_shared(const char *model_dir, opure_engine *share,
+                                        const opure_engine_options *o, opure_engine **out) {
+    if (!share || !share->eng.IsReady()) return OPURE_ERR_INVALID_ARG;
+    opure_device_info di{};
+    const opure_status s = opure_get_device_info(share->eng.Ctx(), &di);
+    if (s != OPURE_OK) return s;
+    return Create(model_dir, di.device, share->eng.Ctx(), o, out);
+}
+
+opure_status opure_engine_spec_generate(opure_engine *target, opure_engine *draft, const int32_t *prompts,
+                                        uint32_t prompt_len, uint32_t n_seq, uint32_t budget,
+                                        const opure_spec_options *o, int32_t *out_tokens,
+                                        int32_t *accept_log, uint32_t accept_log_rounds,
+                                        opure_spec_stats *stats) {
+    if (!target || !draft || !prompts || !o || !out_tokens || n_seq == 0 || prompt_len == 0 || budget == 0)
+        return OPURE_ERR_INVALID_ARG;
+    return Guard(target, [&] {
+        std::vector<std::vector<uint32_t>> ps(n_seq);
+        for (uint32_t s = 0; s < n_seq; ++s) ps[s] = ToU32(prompts + size_t(s) * prompt_len, prompt_len);
+        opure::engine::SpecOptions so;
+        so.k = o->k;
+        so.mode = o->mode;
+        so.seed = o->seed;
+        so.maxNew = budget;
+        opure::engine::SpecStats st;
+        std::vector<int32_t> log;
+        const auto res = opure::engine::SpecGenerate(target->eng, draft->eng, ps, so, &st, accept_log ? &log : nullptr);
+        for (uint32_t s = 0; s < n_seq; ++s)
+            for (uint32_t i = 0; i < budget; ++i) out_tokens[size_t(s) * budget + i] = int32_t(res[s][i]);
+        if (accept_log) {
+            const size_t m = std::min<size_t>(log.size(), size_t(accept_log_rounds) * n_seq);
+            std::copy_n(log.begin(), m, accept_log);
+            std::fill(accept_log + m, accept_log + size_t(accept_log_rounds) * n_seq, -2);
+        }
+        if (stats) {
+            stats->rounds = st.rounds;
+            stats->drafted = st.drafted;
+            stats->accepted = st.accepted;
+            stats->draft_ms = st.draftMs;
+            stats->verify_ms = st.verifyMs;
+            stats->total_ms = st.totalMs;
+        }
+    });
 }
 
 opure_status opure_engine_destroy(opure_engine *e) {

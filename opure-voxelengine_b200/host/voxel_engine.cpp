@@ -43,18 +43,26 @@ void VoxelEngine::Shutdown() {
     hostIo_ = nullptr;
     buf_ = Buffers{};
     weights_ = nullptr;
-    opure_shutdown(ctx_);
+    if (ownsCtx_) opure_shutdown(ctx_);
     ctx_ = nullptr;
+    ownsCtx_ = true;
     graph_.Release();
     ready_ = false;
 }
 
-void VoxelEngine::Initialize(const std::string &modelDir, const EngineOptions &opts, int device) {
+void VoxelEngine::Initialize(const std::string &modelDir, const EngineOptions &opts, int device,
+                             opure_ctx *shared) {
     Shutdown();
     OPURE_CHECK(!opts.enablePlasticity, "the SignSGD plasticity pass is not part of this engine");
     OPURE_CHECK(opts.maxBatch >= 1, "maxBatch must be at least 1");
     opts_ = opts;
-    OPURE_CUDA_CHECK(opure_init(device, &ctx_));
+    if (shared) {
+        ctx_ = shared;
+        ownsCtx_ = false;
+    } else {
+        OPURE_CUDA_CHECK(opure_init(device, &ctx_));
+        ownsCtx_ = true;
+    }
     graph::LayoutOptions lo;
     lo.fusedLayouts = opts.path != 1;  // grouped o_proj and transposed down_proj
     graph_.LoadConfigOnly(modelDir, lo);
@@ -445,20 +453,48 @@ void VoxelEngine::SetVectors(const int32_t *seq, const int32_t *pos, const int32
     for (uint32_t v = 0; v < n; ++v) {
         OPURE_CHECK(seq[v] >= 0 && uint32_t(seq[v]) < opts_.maxBatch, "sequence slot out of range");
         OPURE_CHECK(pos[v] >= 0 && uint32_t(pos[v]) < maxLen_, "position exceeds the engine's maxLen");
-        OPURE_CHECK(tok[v] >= 0 && uint32_t(tok[v]) < V, "token id out of vocabulary range");
+        OPURE_CHECK(!tok || (tok[v] >= 0 && uint32_t(tok[v]) < V), "token id out of vocabulary range");
         OPURE_CHECK(kv_.Reserve(uint32_t(seq[v]), uint32_t(pos[v]) + 1), "KV cache has no room for the sequence");
     }
     kv_.SyncTable();
     // Pageable sources: staged before the calls return, so the arrays may be reused.
     OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.seq, seq, n * 4));
     OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.pos, pos, n * 4));
-    OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.inTokens, tok, n * 4));
+    if (tok) OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.inTokens, tok, n * 4));
     seqIdentity_ = false;
     if (!hostDriven_) {
         const std::vector<uint32_t> zero(opts_.maxBatch, 0u);
         OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.flags, zero.data(), zero.size() * 4));
         hostDriven_ = true;
     }
+}
+
+void VoxelEngine::SetAutoVectors(const int32_t *pos, const int32_t *known, uint32_t n) {
+    OPURE_CHECK(ready_, "engine used before Initialize");
+    OPURE_CHECK(n >= 1 && n <= opts_.maxBatch, "more token vectors than maxBatch");
+    std::vector<int32_t> seq(n);
+    std::vector<uint32_t> flags(n, uint32_t(OPURE_VEC_AUTO));
+    for (uint32_t v = 0; v < n; ++v) {
+        OPURE_CHECK(pos[v] >= 0 && uint32_t(pos[v]) < maxLen_, "position exceeds the engine's maxLen");
+        OPURE_CHECK(known[v] >= 0 && uint32_t(known[v]) <= maxLen_, "known length exceeds the engine's maxLen");
+        OPURE_CHECK(uint32_t(pos[v]) < kv_.MappedPages(v) * kv_.PageSize(),
+                    "position beyond the sequence's reserved KV pages");
+        seq[v] = int32_t(v);
+    }
+    OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.seq, seq.data(), n * 4));
+    OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.pos, pos, n * 4));
+    OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.known, known, n * 4));
+    OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.flags, flags.data(), n * 4));
+    seqIdentity_ = true;
+    hostDriven_ = false;
+}
+
+void VoxelEngine::WriteHistory(uint32_t slot, uint32_t pos, const int32_t *tokens, uint32_t count) {
+    OPURE_CHECK(slot < opts_.maxBatch && uint64_t(pos) + count <= maxLen_, "history write out of range");
+    const uint32_t V = graph_.Config().vocabSize;
+    for (uint32_t i = 0; i < count; ++i)
+        OPURE_CHECK(tokens[i] >= 0 && uint32_t(tokens[i]) < V, "token id out of vocabulary range");
+    OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.tokens + size_t(slot) * maxLen_ + pos, tokens, size_t(count) * 4));
 }
 
 GenerateResult VoxelEngine::Generate(const std::vector<uint32_t> &tokens, const EngineOptions &opts) {

@@ -68,8 +68,12 @@ public:
     VoxelEngine(const VoxelEngine &) = delete;
     VoxelEngine &operator=(const VoxelEngine &) = delete;
 
-    // Loads the model onto `device`: layout plan, weight upload, KV pool, buffers.
-    void Initialize(const std::string &modelDir, const EngineOptions &opts, int device);
+    // Loads the model onto `device`: layout plan, weight upload, KV pool, buffers. With
+    // `shared`, the engine enqueues on that existing ctx (stream) instead of creating its
+    // own: engines that cooperate on one stream (speculative decoding's draft and target)
+    // then need no synchronisation between them. The owner of `shared` must outlive it.
+    void Initialize(const std::string &modelDir, const EngineOptions &opts, int device,
+                    opure_ctx *shared = nullptr);
     void Shutdown();
     bool IsReady() const { return ready_; }
 
@@ -124,8 +128,16 @@ public:
     std::vector<uint32_t> PrefillBatch(const std::vector<std::vector<uint32_t>> &prompts, uint32_t reserve,
                                        bool logits);
     // describe the next step's n token vectors: sequence slot, position and token of each
-    // (host-driven: no argmax feedback, positions not advanced);
+    // (host-driven: no argmax feedback, positions not advanced; tok == NULL leaves the
+    // tokens to a device producer writing DeviceInTokens());
     void SetVectors(const int32_t *seq, const int32_t *pos, const int32_t *tok, uint32_t n);
+    // or make vectors 0..n-1 self-driving on slots 0..n-1 from positions pos[v]: history
+    // tokens below known[v] are re-fed, later inputs are the previous step's result;
+    void SetAutoVectors(const int32_t *pos, const int32_t *known, uint32_t n);
+    // write `count` tokens into a slot's token history from position `pos`.
+    void WriteHistory(uint32_t slot, uint32_t pos, const int32_t *tokens, uint32_t count);
+    int32_t *DeviceHistory() const { return buf_.tokens; }      // [maxBatch][maxLen]
+    int32_t *DeviceInTokens() const { return buf_.inTokens; }   // [maxBatch]
     float *DeviceLogits() const { return buf_.logits; }       // [maxBatch][vocab]
     unsigned long long *DeviceKeys() const { return buf_.keys; }
     // Rewinds the positions of vectors 0..n-1 (stream-ordered, no wait).
@@ -173,6 +185,7 @@ private:
     void *hostIo_ = nullptr;  // pinned staging of the host-driven step
     bool hostDriven_ = false; // step flags currently cleared for host-supplied tokens
     bool seqIdentity_ = true; // vector v currently maps to sequence slot v
+    bool ownsCtx_ = true;
 };
 
 }  // namespace opure::engine

@@ -33,6 +33,18 @@ class Timing(C.Structure):
                 ("decode_steps", u32)]
 
 
+class SpecOptions(C.Structure):
+    _fields_ = [("k", u32), ("mode", u32), ("seed", u64)]
+
+
+class SpecStats(C.Structure):
+    _fields_ = [("rounds", u32), ("drafted", u64), ("accepted", u64), ("draft_ms", f64),
+                ("verify_ms", f64), ("total_ms", f64)]
+
+
+SPEC_GREEDY, SPEC_REJECTION = 0, 1
+
+
 class SynthSpec(C.Structure):
     _fields_ = [("vocab", u32), ("hidden", u32), ("inter", u32), ("layers", u32), ("heads", u32),
                 ("kv_heads", u32), ("max_pos", u32), ("eps", f32), ("theta", f64), ("tied", u32),
@@ -58,6 +70,8 @@ def lib() -> C.CDLL:
         L = C.CDLL(LIB_PATH, mode=C.RTLD_GLOBAL)
         sigs = {
             "opure_engine_create": [C.c_char_p, C.c_int, P, P],
+            "opure_engine_create_shared": [C.c_char_p, P, P, P],
+            "opure_engine_spec_generate": [P, P, P, u32, u32, u32, P, P, P, u32, P],
             "opure_engine_destroy": [P],
             "opure_engine_get_info": [P, P],
             "opure_engine_generate": [P, P, P, u32, u32, P, P],
@@ -162,12 +176,19 @@ class Engine:
 
     def __init__(self, model_dir: str, device: int = 0, max_batch: int = 1, max_len: int = 0,
                  page_size: int = 64, page_seed: int = 3, use_graphs: bool = True,
-                 attn_scale: float = 1.0, max_new_tokens: int = 256, path: int = PATH_AUTO):
+                 attn_scale: float = 1.0, max_new_tokens: int = 256, path: int = PATH_AUTO,
+                 share: "Engine | None" = None):
+        """With `share`, the engine runs on that engine's ctx (stream), as the draft of a
+        speculative pair must; it keeps a reference so the owner outlives it."""
         o = EngineOptions(max_new_tokens, max_batch, max_len, page_size, page_seed,
                           int(use_graphs), attn_scale, path)
         h = C.c_void_p()
-        st = lib().opure_engine_create(model_dir.encode(), device, C.byref(o), C.byref(h))
+        if share is None:
+            st = lib().opure_engine_create(model_dir.encode(), device, C.byref(o), C.byref(h))
+        else:
+            st = lib().opure_engine_create_shared(model_dir.encode(), share.h, C.byref(o), C.byref(h))
         _check(st, "opure_engine_create", None)
+        self.share = share
         self.h = h
         self.info = EngineInfo()
         _check(lib().opure_engine_get_info(self.h, C.byref(self.info)), "get_info", self.h)
@@ -176,6 +197,7 @@ class Engine:
         if getattr(self, "h", None):
             lib().opure_engine_destroy(self.h)
             self.h = None
+        self.share = None
 
     __del__ = close
 
@@ -199,6 +221,23 @@ class Engine:
         _check(lib().opure_engine_generate(self.h, _p(flat), _p(lens), len(ps), budget, _p(out),
                                            C.byref(t)), "generate", self.h)
         return out, t
+
+    def spec_generate(self, draft: "Engine", prompts, budget: int, k: int = 4, mode: int = SPEC_GREEDY,
+                      seed: int = 0, log_rounds: int = 0):
+        """Speculative decoding with `draft` (created with share=self). prompts: equal-length
+        sequences. Returns (tokens [n][budget], SpecStats, accept log [rounds][n] or None)."""
+        ps = np.ascontiguousarray(np.stack([np.asarray(p, np.int32) for p in prompts]), np.int32)
+        n, plen = ps.shape
+        out = np.zeros((n, budget), np.int32)
+        o = SpecOptions(k, mode, seed)
+        st = SpecStats()
+        log = np.zeros((log_rounds, n), np.int32) if log_rounds else None
+        _check(lib().opure_engine_spec_generate(self.h, draft.h, _p(ps), plen, n, budget, C.byref(o),
+                                                _p(out), _p(log), log_rounds, C.byref(st)),
+               "spec_generate", self.h)
+        if log is not None:
+            log = log[: min(log_rounds, st.rounds)]
+        return out, st, log
 
     def prefill(self, tokens) -> int:
         """Prefill slot 0; returns the first generated token."""

@@ -1,0 +1,82 @@
+"""CPU restatement of the speculative decoding loop (test infrastructure only).
+
+Follows the engine's SpecGenerate contract (opure-voxelengine_b200/host/spec_decode.h)
+sequence by sequence on the oracle's scalar forward: the draft proposes k tokens from
+position p (after recomputing position p-1), the target evaluates positions p..p+k, and
+oracle.spec_accept_* decides; both states are rolled back by truncation. Uniforms come
+from the harness Rng (Opure_TestHarness.cpp:36-47) seeded per sequence as
+seed ^ (s * 0x9E3779B97F4A7C15), drawn per round as u_draft[k], u_accept[k], u_final.
+"""
+import numpy as np
+
+import oracle
+
+GOLDEN = 0x9E3779B97F4A7C15
+MASK = (1 << 64) - 1
+
+
+class Rng:
+    def __init__(self, seed: int):
+        self.s = (seed & MASK) or 1
+
+    def u32(self) -> int:
+        s = self.s
+        s ^= (s << 13) & MASK
+        s ^= s >> 7
+        s ^= (s << 17) & MASK
+        self.s = s
+        return s >> 32
+
+    def uniform(self) -> float:
+        return float(np.float32(self.u32() / 4294967296.0))
+
+
+def argmax(logits) -> int:
+    return int(oracle.argmax(np.asarray(logits, np.float32)[None])[0][0])
+
+
+def spec_generate(target: oracle.Model, draft: oracle.Model, prompts, budget: int, k: int,
+                  rejection: bool, seed: int = 0):
+    """Returns (tokens [n][budget], accept counts per round [n][rounds])."""
+    outs, logs = [], []
+    for s, prompt in enumerate(prompts):
+        rng = Rng(seed ^ ((s * GOLDEN) & MASK))
+        p0 = len(prompt)
+        cap = p0 + budget + k + 2
+        ts, ds = target.state(cap), draft.state(cap)
+        lt = None
+        for i, tok in enumerate(prompt):
+            lt, _ = ts.forward(int(tok), logits=(i == p0 - 1))
+            ds.forward(int(tok), logits=False)
+        first = oracle.sample_softmax(lt, rng.uniform()) if rejection else argmax(lt)
+        out, log = [first], []
+        p, t, prev = p0, first, int(prompt[-1])
+        while len(out) < budget:
+            ud = [rng.uniform() for _ in range(k)] if rejection else None
+            ua = [rng.uniform() for _ in range(k)] if rejection else None
+            uf = rng.uniform() if rejection else None
+            ds.truncate(p - 1)
+            ds.forward(prev, logits=False)
+            drafts, dlog, cur = [], [], t
+            for j in range(k):
+                lq, _ = ds.forward(cur)
+                d = oracle.sample_softmax(lq, ud[j]) if rejection else argmax(lq)
+                drafts.append(d)
+                dlog.append(lq)
+                cur = d
+            ts.truncate(p)
+            tl = np.stack([ts.forward(tok)[0] for tok in [t] + drafts])
+            if rejection:
+                a, toks = oracle.spec_accept_rejection(tl, np.stack(dlog), np.array(drafts), np.array(ua, np.float32), uf)
+            else:
+                a, toks = oracle.spec_accept_greedy(tl, np.array(drafts))
+            log.append(int(a))
+            for i in range(a + 1):
+                if len(out) < budget:
+                    out.append(int(toks[i]))
+            prev = int(toks[a - 1]) if a > 0 else t
+            t = int(toks[a])
+            p += a + 1
+        outs.append(out)
+        logs.append(log)
+    return np.array(outs, np.int32), logs
