@@ -450,6 +450,60 @@ def run_gemv_sweep(args):
                       "peak_kind": kind, "points": out}), flush=True)
 
 
+def run_spec(args):
+    """Config 3: speculative decoding. Target = the config-0 model; draft = the same weights
+    plus seeded N(0, 0.004) noise on every matrix element (noise seed 6); k = 4 and 8;
+    batch 1 and 16 (prompt seeds 1..B); greedy and rejection sampling (temperature 1,
+    uniform seed 3); 256 generated tokens per sequence. Reports the acceptance rate,
+    generated tok/s (wall clock of the whole loop, host round trip per round included, and
+    device time) and the verify pass's algorithmic HBM GB/s (weights once + the KV rows of
+    the B(k+1) verify positions) over its device time (verify + accept)."""
+    from voxelengine import engine as ve
+    peak, kind = peaks()
+    tgt = model_dir()
+    root = os.environ.get("OPURE_BENCH_DIR", "/tmp/opure_bench")
+    drf = ve.synth_model(os.path.join(root, "smollm135m_seed0_draft6"), seed=0, noise_seed=6, noise_std=0.004)
+    budget = 256
+    points = []
+    for k in (4, 8):
+        for B in (1, 16):
+            max_len = PROMPT_LEN + budget + k + 8
+            t = ve.Engine(tgt, max_batch=B * (k + 1), max_len=max_len)
+            d = ve.Engine(drf, max_batch=B, max_len=max_len, share=t)
+            info = t.info
+            prompts = [ve.prompt(1 + b, 49152, PROMPT_LEN) for b in range(B)]
+            for mode, name in ((ve.SPEC_GREEDY, "greedy"), (ve.SPEC_REJECTION, "rejection")):
+                t.spec_generate(d, prompts, 16, k=k, mode=mode, seed=3)  # captures the step graphs
+                t0 = time.perf_counter()
+                _, st, _ = t.spec_generate(d, prompts, budget, k=k, mode=mode, seed=3)
+                wall = time.perf_counter() - t0
+                kv = info.kv_bytes_per_token
+                mean_p = PROMPT_LEN + budget / 2
+                vbytes = info.stream_bytes + B * (k + 1) * (kv * (mean_p + k / 2 + 1) + kv)
+                vgbs = vbytes * st.rounds / (st.verify_ms * 1e-3) / 1e9
+                points.append({"k": k, "B": B, "mode": name, "acceptance": st.accepted / max(st.drafted, 1),
+                               "rounds": st.rounds, "tok_s_wall": B * budget / wall,
+                               "tok_s_device": B * budget / (st.total_ms * 1e-3),
+                               "draft_ms": st.draft_ms, "verify_ms": st.verify_ms,
+                               "verify_GB_s": vgbs, "verify_frac": vgbs / peak})
+            d.close()
+            t.close()
+    line = {"metric": "speculative decode (config 3): generated tok/s and acceptance", "unit": "tok/s",
+            "peak": peak, "peak_kind": kind, "budget": budget, "points": points}
+    if not args.no_cpu:
+        import oracle
+        from oracle import spec
+        oracle.set_threads(os.cpu_count() or 1)
+        om_t, om_d = oracle.Model(tgt), oracle.Model(drf)
+        t0 = time.perf_counter()
+        spec.spec_generate(om_t, om_d, [ve.prompt(1, 49152, PROMPT_LEN)], 32, 4, rejection=False)
+        dt = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": 32 / dt, "unit": "tok/s", "cores": os.cpu_count() or 1, "kind": "port",
+                                "sample": "B=1, k=4, greedy: the first 32 generated tokens (prefill included) "
+                                          "of the oracle's speculative loop"}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -459,7 +513,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-steps", type=int, default=128)
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", choices=["decode", "attn", "gemv"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "attn", "gemv", "spec"], default="decode")
     ap.add_argument("--quick", action="store_true",
                     help="minimal run for profiler launch lists: no parity, e2e or CPU legs")
     args = ap.parse_args()
@@ -472,6 +526,8 @@ def main():
             run_attention_sweep(args)
         elif args.workload == "gemv":
             run_gemv_sweep(args)
+        elif args.workload == "spec":
+            run_spec(args)
         else:
             run_ours(args, world, rank, local)
     finally:

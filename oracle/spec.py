@@ -1,4 +1,5 @@
-"""CPU restatement of the speculative decoding loop (test infrastructure only).
+"""CPU restatement of the speculative decoding loop (test infrastructure: the checker of
+the GPU loop in tests/ and the CPU baseline of the config-3 bench; never product code).
 
 Follows the engine's SpecGenerate contract (opure-voxelengine_b200/host/spec_decode.h)
 sequence by sequence on the oracle's scalar forward: the draft proposes k tokens from

@@ -1,5 +1,5 @@
 """Speculative decoding on the GPU (draft + target engines on one stream) vs the CPU
-restatement of the same loop (tests/spec_oracle.py).
+restatement of the same loop (oracle/spec.py).
 
 the draft is the target with every weight perturbed by seeded
 N(0, 0.004) noise; k = 4 and 8; acceptance (a) greedy token match, (b) rejection sampling
@@ -13,7 +13,7 @@ import numpy as np
 import pytest
 
 import oracle
-import spec_oracle
+from oracle import spec as spec_oracle
 from voxelengine import engine as ve
 
 pytestmark = pytest.mark.gpu

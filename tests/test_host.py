@@ -44,6 +44,17 @@ def test_uniforms():
     assert np.array_equal(ve.uniforms(9, 100), want)
 
 
+def test_spec_uniform_streams():
+    # The speculative loop's per-sequence streams: the oracle's restatement and the
+    # engine's Rng draw the same uniforms from seed ^ s * 0x9E3779B97F4A7C15.
+    from oracle import spec
+    for seed, s in ((0, 0), (3, 1), (12, 15)):
+        derived = seed ^ ((s * spec.GOLDEN) & spec.MASK)
+        r = spec.Rng(derived)
+        assert np.array_equal(np.array([r.uniform() for _ in range(64)], np.float32),
+                              ve.uniforms(derived, 64))
+
+
 def test_normals_box_muller():
     r = Rng(5)
     want = []
