@@ -43,6 +43,10 @@ for p in (REPO, PKG):
 METRIC = "decode tok/s (bs1, bs64) at SmolLM-135M shape; GEMV+attn HBM GB/s as % of peak"
 PROMPT_LEN, DECODE_STEPS = 32, 128
 FALLBACK_PEAK = 6650.0  # GB/s, used only when MEASURED_PEAKS.json is absent
+# DRAM bytes (read + write) of one decode step, summed over its launches in an ncu capture
+# of `python bench.py --quick --no-cpu [--batch B] --steps 2 --warmup 3` (launch lists in
+# profiles/decode_bs1_fused_step.md and profiles/decode_bs64_tensor_core_step.md).
+NCU_STEP_TRAFFIC = {1: 275.0e6, 64: 483.7e6}
 
 
 def peaks():
@@ -291,10 +295,7 @@ def run_ours(args, world, rank, local):
                "sample": f"{done} config-0 decode tokens of one sequence (positions 32..159 cyclic) "
                          f"on the CPU oracle after a {PROMPT_LEN}-token prefill"}
 
-    # Kernel launches per step: step_begin + step_end + lm_head, plus per layer 3 on the
-    # fused path (B in {1,2,4,8}, fp16) or 6 (8 with int8's separate q/k/v GEMVs) per-op.
-    fused = info.w_dtype == cu.W_F16 and B in (1, 2, 4, 8)
-    launches_per_step = 3 + info.layers * (3 if fused else (6 if info.w_dtype == cu.W_F16 else 8))
+    line_launches = launches_per_step(info, B)
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
@@ -305,21 +306,38 @@ def run_ours(args, world, rank, local):
                    "parallelism": f"sequence-sharded x{world}",
                    "l2": "inputs larger than L2: every step streams 269 MB of weights (L2 126 MB)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": None,
+                     "frac": achieved / peak, "traffic": NCU_STEP_TRAFFIC.get(B),
                      "kernel": "whole decode step (GEMV dominant)", "peak_kind": peak_kind,
                      "bytes_per_step": sbytes},
         "e2e": e2e,
-        "gpu_launches": launches_per_step * args.steps,
+        "gpu_launches": line_launches * args.steps,
         "clocks": clocks,
         "parity": parity,
         "launches_before_timed": (PROMPT_LEN + (1 if args.quick else DECODE_STEPS) + args.warmup)
-        * launches_per_step,
+        * line_launches,
     }
     if cpu:
         line["cpu_baseline"] = cpu
     if rank == 0:
         print(json.dumps(line), flush=True)
     eng.close()
+
+
+def launches_per_step(info, B: int) -> int:
+    """Kernel launches of one decode step: step_begin + step_end, then
+    fused path (fp16, B in 1/2/4/8): 3 per layer + lm_head;
+    per-op path: per layer the q;k;v, o, gate;up and down GEMVs (+ RoPE/KV append and
+    attention), each GEMV one launch per 9-vector pass on the CUDA cores (int8 q;k;v as 3
+    GEMVs) or pack + tcgen05 GEMM per 256-vector pass from 16 vectors up, + the lm_head GEMV."""
+    from voxelengine import cuda as cu
+    if info.w_dtype == cu.W_F16 and B in (1, 2, 4, 8):
+        return 2 + 3 * info.layers + 1
+    if info.w_dtype == cu.W_F16 and B >= 16:
+        gemv = 2 * -(-B // 256)
+    else:
+        gemv = -(-B // 9)
+    qkv = gemv if info.w_dtype == cu.W_F16 else 3 * gemv
+    return 2 + info.layers * (qkv + 3 * gemv + 2) + gemv
 
 
 def _events(ctx):
