@@ -468,6 +468,73 @@ def run_gemv_sweep(args):
                       "peak_kind": kind, "points": out}), flush=True)
 
 
+def run_cfg4(args, world, rank, local):
+    """Config 4: 1.7B-shape batched decode (24 layers, hidden 2048, 32/32 heads, ff 8192,
+    vocab 49152, fp16 weights N(0, 0.02) seed 5, tied embeddings). 512 independent sequences
+    (--seqs) with 4096-token contexts each decode 64 tokens, sharded by sequence across the
+    ranks (no collective on the data path) and run in waves of at most --wave sequences per
+    GPU. Contexts are seeded synthetic KV values written on the device (opure_kv_synth,
+    seed 5 + wave index) instead of a 4096-step prefill; each sequence's first input token
+    is seeded. Device time of the 64 steps of every wave, summed, max over ranks."""
+    import ctypes as C
+
+    from voxelengine import cuda as cu
+    from voxelengine import engine as ve
+    root = os.environ.get("OPURE_BENCH_DIR", "/tmp/opure_bench")
+    path = os.path.join(root, "llama1p7b_seed5")
+    if rank == 0:
+        ve.synth_model(path, seed=5, **ve.LLAMA_1_7B)
+    barrier(world)
+    mp = ve.synth_model(path, seed=5, **ve.LLAMA_1_7B)
+    ctx_len, steps = 4096, 64
+    per_rank = -(-args.seqs // world)
+    wave = min(args.wave, per_rank)
+    eng = ve.Engine(mp, device=local, max_batch=wave, max_len=ctx_len + steps + 8, page_size=64, page_seed=3)
+    info = eng.info
+    L = cu.lib()
+    ev0, ev1 = _events(eng.ctx)
+    dev_ms, tokens, waves = 0.0, 0, 0
+    warm = 3  # graph capture + 2 replays; positions are rewound before the timed steps
+    for w0 in range(0, per_rank, wave):
+        n = min(wave, per_rank - w0)
+        first = ve.prompt(1000 + rank * per_rank + w0, info.vocab, n)
+        eng.synth_context(n, ctx_len, ctx_len + steps + 4, 5 + waves, first)
+        eng.run_steps(n, warm)                      # captures the step graph
+        eng.sync()
+        cu.check(ve.lib().opure_engine_set_positions(
+            eng.h, np.full(n, ctx_len, np.int32).ctypes.data_as(C.c_void_p), n), "set_positions")
+        cu.check(L.opure_event_record(eng.ctx, ev0), "event")
+        eng.run_steps(n, steps)
+        cu.check(L.opure_event_record(eng.ctx, ev1), "event")
+        eng.sync()
+        ms = C.c_float()
+        cu.check(L.opure_event_elapsed_ms(ev0, ev1, C.byref(ms)), "elapsed")
+        dev_ms += ms.value
+        tokens += n * steps
+        waves += 1
+    barrier(world)
+    dev_ms = allreduce_max(world, dev_ms)
+    kv = info.kv_bytes_per_token
+    step_bytes_ = info.stream_bytes + wave * (kv * (ctx_len + steps / 2 + 1) + kv)
+    step_ms = dev_ms / (waves * steps)
+    achieved = step_bytes_ / (step_ms * 1e-3) / 1e9
+    peak, peak_kind = peaks()
+    line = {"metric": "config-4 batched decode tok/s (1.7B shape, 4096-token contexts, 64 steps)",
+            "value": world * tokens / (dev_ms * 1e-3), "unit": "tok/s", "n_gpus": world, "steps": steps,
+            "warmup": warm, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "strong",
+            "dtype": "f16 weights/KV, f32 accumulate", "data": "synthetic",
+            "config": {"workload": f"cfg4: {args.seqs} sequences x 4096-token synthetic context, 64 decode "
+                                   f"steps, {per_rank} per GPU in waves of {wave}",
+                       "global_batch": args.seqs, "seq_len": ctx_len + steps,
+                       "parallelism": f"sequence-sharded x{world}"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
+                         "bytes_per_step": step_bytes_, "kernel": "whole decode step (attention dominant)"}}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    eng.close()
+
+
 def run_spec(args):
     """Config 3: speculative decoding. Target = the config-0 model; draft = the same weights
     plus seeded N(0, 0.004) noise on every matrix element (noise seed 6); k = 4 and 8;
@@ -531,7 +598,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-steps", type=int, default=128)
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", choices=["decode", "attn", "gemv", "spec"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "attn", "gemv", "spec", "cfg4"], default="decode")
+    ap.add_argument("--seqs", type=int, default=512, help="cfg4: total sequences over all ranks")
+    ap.add_argument("--wave", type=int, default=128, help="cfg4: sequences per GPU per wave")
     ap.add_argument("--quick", action="store_true",
                     help="minimal run for profiler launch lists: no parity, e2e or CPU legs")
     args = ap.parse_args()
@@ -546,6 +615,8 @@ def main():
             run_gemv_sweep(args)
         elif args.workload == "spec":
             run_spec(args)
+        elif args.workload == "cfg4":
+            run_cfg4(args, world, rank, local)
         else:
             run_ours(args, world, rank, local)
     finally:

@@ -68,6 +68,8 @@ const char *opure_strerror(opure_status s);
  * timeout failure (the reference decodes device-removed reasons instead,
  * Opure_Dx12.cpp:53-81). Synchronises the stream. */
 opure_status opure_last_error(opure_ctx *ctx);
+/* The same, also returning the failing kernel's site id and offending value (0 if none). */
+opure_status opure_last_error_detail(opure_ctx *ctx, uint32_t *where, uint32_t *detail);
 /* cudaStream_t of the ctx, for interop. */
 void *opure_stream(opure_ctx *ctx);
 
@@ -137,6 +139,15 @@ typedef struct opure_kv_layout {
     uint32_t n_kv;             /* KV heads                                        */
     uint32_t head_dim;         /* 64 or 128                                       */
 } opure_kv_layout;
+
+/* Seeded synthetic context: fills positions [0, len) of sequence slots slot0 ..
+ * slot0+n_slots-1 of one layer's pool (pages from page_table) with fp16 values
+ * v = fp16(4 u - 2), u = (splitmix64(seed ^ slot << 48 ^ i) >> 40) / 2^24, where
+ * i = (((layer * 2 + kv_sel) * n_kv + head) * 65536 + pos) * head_dim + d. Lets
+ * long-context decode (4096-token contexts) run without a prefill; opure_synth_kv in
+ * the engine library produces the same bits on the host. len <= 65536. */
+opure_status opure_kv_synth(opure_ctx *ctx, const opure_kv_layout *kv, uint32_t layer,
+                            uint32_t slot0, uint32_t n_slots, uint32_t len, uint64_t seed);
 
 /* RoPE + KV append for n token vectors. Row i of `qkv` (row stride `stride` floats) holds
  * [q: n_heads*hd | k: n_kv*hd | v: n_kv*hd], the layout of the fused q;k;v GEMV. q and k are

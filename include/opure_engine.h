@@ -104,6 +104,16 @@ opure_status opure_engine_poison(opure_engine *e, float value);
  * (synthetic long contexts for the large-model configuration). */
 opure_status opure_engine_load_kv(opure_engine *e, uint32_t seq, const uint16_t *kv, uint32_t len);
 
+/* Synthetic long contexts (config 4's 4096-token contexts without a prefill): slots
+ * 0..n-1 get `len` cached positions of seeded KV values (opure_kv_synth), `reserve`
+ * positions of KV pages, and continue self-driving (opure_engine_run_steps) from position
+ * len with first_tokens[v] as input. opure_engine_read_tokens copies `count` tokens of a
+ * slot's history from position `pos`. */
+opure_status opure_engine_synth_context(opure_engine *e, uint32_t n, uint32_t len, uint32_t reserve,
+                                        uint64_t seed, const int32_t *first_tokens);
+opure_status opure_engine_read_tokens(opure_engine *e, uint32_t slot, uint32_t pos, uint32_t count,
+                                      int32_t *out);
+
 /* ---- speculative decoding (no reference counterpart: the reference's verify shader,
  *      Opure_SpeculativeDecode.usf:60-189, is never dispatched and it has no draft loop
  *      or accept rule; speculativeAcceptance is fixed at -1, Opure_VoxelEngine.cpp:666) */
@@ -163,6 +173,9 @@ opure_status opure_synth_normal_f16(uint64_t seed, float stddev, uint64_t n, uin
 opure_status opure_synth_prompt(uint64_t seed, uint32_t vocab, uint32_t n, int32_t *out);
 opure_status opure_synth_permutation(uint64_t seed, uint32_t n, int32_t *out);
 opure_status opure_synth_uniforms(uint64_t seed, uint64_t n, float *out);
+/* Host form of opure_kv_synth for one slot: [layers][2][n_kv][len][head_dim] fp16. */
+opure_status opure_synth_kv(uint64_t seed, uint32_t slot, uint32_t layers, uint32_t n_kv, uint32_t len,
+                            uint32_t head_dim, uint16_t *out);
 
 #ifdef __cplusplus
 }

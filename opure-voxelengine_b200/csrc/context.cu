@@ -104,15 +104,19 @@ opure_status opure_get_device_info(opure_ctx *ctx, opure_device_info *info) {
 
 void *opure_stream(opure_ctx *ctx) { return ctx ? static_cast<void *>(ctx->stream) : nullptr; }
 
-opure_status opure_last_error(opure_ctx *ctx) {
+opure_status opure_last_error_detail(opure_ctx *ctx, uint32_t *where, uint32_t *detail) {
     opure_status s = enter(ctx);
     if (s) return s;
     OPURE_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
     opure::DeviceStatus st;
     OPURE_CUDA_TRY(cudaMemcpy(&st, ctx->status, sizeof(st), cudaMemcpyDeviceToHost));
     if (st.code) OPURE_CUDA_TRY(cudaMemset(ctx->status, 0, sizeof(st)));
+    if (where) *where = st.code ? st.where : 0;
+    if (detail) *detail = st.code ? st.detail : 0;
     return static_cast<opure_status>(st.code);
 }
+
+opure_status opure_last_error(opure_ctx *ctx) { return opure_last_error_detail(ctx, nullptr, nullptr); }
 
 // ---- memory ---------------------------------------------------------------
 opure_status opure_alloc(opure_ctx *ctx, size_t bytes, void **dptr) {

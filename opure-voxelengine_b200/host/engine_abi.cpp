@@ -100,6 +100,27 @@ opure_status opure_engine_create_shared(const char *model_dir, opure_engine *sha
     return Create(model_dir, di.device, share->eng.Ctx(), o, out);
 }
 
+opure_status opure_engine_synth_context(opure_engine *e, uint32_t n, uint32_t len, uint32_t reserve,
+                                        uint64_t seed, const int32_t *first_tokens) {
+    if (!e || !first_tokens) return OPURE_ERR_INVALID_ARG;
+    return Guard(e, [&] { e->eng.PrepareSynthetic(n, len, reserve, seed, first_tokens); });
+}
+
+opure_status opure_engine_read_tokens(opure_engine *e, uint32_t slot, uint32_t pos, uint32_t count,
+                                      int32_t *out) {
+    if (!e || !out) return OPURE_ERR_INVALID_ARG;
+    return Guard(e, [&] { e->eng.ReadHistory(slot, pos, count, out); });
+}
+
+opure_status opure_synth_kv(uint64_t seed, uint32_t slot, uint32_t layers, uint32_t n_kv, uint32_t len,
+                            uint32_t head_dim, uint16_t *out) {
+    if (!out || len > 65536) return OPURE_ERR_INVALID_ARG;
+    return Guard(nullptr, [&] {
+        const auto v = opure::synth::SynthKv(seed, slot, layers, n_kv, len, head_dim);
+        std::copy(v.begin(), v.end(), out);
+    });
+}
+
 opure_status opure_engine_spec_generate(opure_engine *target, opure_engine *draft, const int32_t *prompts,
                                         uint32_t prompt_len, uint32_t n_seq, uint32_t budget,
                                         const opure_spec_options *o, int32_t *out_tokens,

@@ -178,8 +178,7 @@ std::vector<std::vector<uint32_t>> SpecGenerate(VoxelEngine &target, VoxelEngine
         OPURE_CUDA_CHECK(opure_d2h(ctx, hOut.data(), dOut, hOut.size() * 4));
         OPURE_CUDA_CHECK(opure_d2h(ctx, hAcc.data(), dAcc, n * 4));
         OPURE_CUDA_CHECK(opure_sync(ctx, 60000));
-        const opure_status dev = opure_last_error(ctx);
-        if (dev != OPURE_OK) ThrowError(std::string("device reported: ") + opure_strerror(dev), dev);
+        CheckDevice(ctx);
         st.draftMs += Elapsed(ev[0], ev[1]);
         st.verifyMs += Elapsed(ev[1], ev[2]);
         ++st.rounds;

@@ -52,6 +52,29 @@ std::vector<int32_t> Permutation(uint64_t seed, uint32_t n) {
     return p;
 }
 
+uint16_t KvValue(uint64_t seed, uint32_t slot, uint64_t i) {
+    // SplitMix64 finaliser (Steele, Lea & Flood 2014).
+    uint64_t z = (seed ^ (uint64_t(slot) << 48) ^ i) + 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    z ^= z >> 31;
+    const float u = float(uint32_t(z >> 40)) * (1.0f / 16777216.0f);
+    return safetensors::F32ToF16(u * 4.0f - 2.0f);
+}
+
+std::vector<uint16_t> SynthKv(uint64_t seed, uint32_t slot, uint32_t layers, uint32_t n_kv, uint32_t len,
+                              uint32_t head_dim) {
+    std::vector<uint16_t> out(size_t(layers) * 2 * n_kv * len * head_dim);
+    size_t o = 0;
+    for (uint32_t L = 0; L < layers; ++L)
+        for (uint32_t sel = 0; sel < 2; ++sel)
+            for (uint32_t h = 0; h < n_kv; ++h)
+                for (uint32_t p = 0; p < len; ++p)
+                    for (uint32_t d = 0; d < head_dim; ++d)
+                        out[o++] = KvValue(seed, slot, (((uint64_t(L) * 2 + sel) * n_kv + h) * 65536 + p) * head_dim + d);
+    return out;
+}
+
 std::vector<float> Uniforms(uint64_t seed, uint64_t n) {
     Rng r(seed);
     std::vector<float> out(n);

@@ -60,4 +60,12 @@ std::vector<int32_t> Prompt(uint64_t seed, uint32_t vocab, uint32_t n);      // 
 std::vector<int32_t> Permutation(uint64_t seed, uint32_t n);                 // Fisher-Yates
 std::vector<float> Uniforms(uint64_t seed, uint64_t n);                      // NextU32() / 2^32
 
+// Synthetic KV context values (the host form of opure_kv_synth): element i of a slot is
+// fp16(4u - 2) with u = (splitmix64(seed ^ slot << 48 ^ i) >> 40) / 2^24 and
+// i = (((layer * 2 + kv_sel) * n_kv + head) * 65536 + pos) * head_dim + d.
+uint16_t KvValue(uint64_t seed, uint32_t slot, uint64_t i);
+// [layers][2][n_kv][len][head_dim] for one slot (the layout VoxelEngine::LoadKv takes).
+std::vector<uint16_t> SynthKv(uint64_t seed, uint32_t slot, uint32_t layers, uint32_t n_kv, uint32_t len,
+                              uint32_t head_dim);
+
 }  // namespace opure::synth

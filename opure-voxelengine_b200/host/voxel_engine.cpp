@@ -345,8 +345,16 @@ void VoxelEngine::SetPositions(const int32_t *positions, uint32_t n) {
 
 void VoxelEngine::Sync() {
     OPURE_CUDA_CHECK(opure_sync(ctx_, 600000));
-    const opure_status st = opure_last_error(ctx_);
-    if (st != OPURE_OK) ThrowError(std::string("device reported: ") + opure_strerror(st), st);
+    CheckDevice(ctx_);
+}
+
+void CheckDevice(opure_ctx *ctx) {
+    uint32_t where = 0, detail = 0;
+    const opure_status st = opure_last_error_detail(ctx, &where, &detail);
+    if (st != OPURE_OK)
+        ThrowError(std::string("device reported: ") + opure_strerror(st) + " (kernel site " + std::to_string(where) +
+                       ", value " + std::to_string(detail) + ")",
+                   st);
 }
 
 void VoxelEngine::ResetSequences(const std::vector<std::vector<uint32_t>> &prompts, uint32_t reserve,
@@ -638,6 +646,43 @@ void VoxelEngine::LoadKv(uint32_t seq, const uint16_t *kvData, uint32_t len) {
                 }
         OPURE_CUDA_CHECK(opure_sync(ctx_, 600000));
     }
+}
+
+void VoxelEngine::PrepareSynthetic(uint32_t n, uint32_t len, uint32_t reserve, uint64_t seed,
+                                   const int32_t *first) {
+    OPURE_CHECK(ready_, "engine used before Initialize");
+    OPURE_CHECK(n >= 1 && n <= opts_.maxBatch, "batch exceeds maxBatch");
+    OPURE_CHECK(len >= 1 && len < reserve && reserve <= maxLen_, "need 1 <= len < reserve <= maxLen");
+    const graph::ModelConfig &c = graph_.Config();
+    std::vector<int32_t> seq(n), pos(n, int32_t(len)), known(n, int32_t(len) + 1);
+    std::vector<uint32_t> flags(n, uint32_t(OPURE_VEC_AUTO));
+    for (uint32_t v = 0; v < n; ++v) {
+        OPURE_CHECK(first[v] >= 0 && uint32_t(first[v]) < c.vocabSize, "token id out of vocabulary range");
+        seq[v] = int32_t(v);
+        kv_.Release(v);
+        OPURE_CHECK(kv_.Reserve(v, reserve), "KV cache has no room for the sequence");
+    }
+    kv_.SyncTable();
+    for (uint32_t L = 0; L < c.numLayers; ++L) {
+        const opure_kv_layout l = kv_.Layout(L);
+        OPURE_CUDA_CHECK(opure_kv_synth(ctx_, &l, L, 0, n, len, seed));
+    }
+    for (uint32_t v = 0; v < n; ++v)
+        OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.tokens + size_t(v) * maxLen_ + len, first + v, 4));
+    OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.seq, seq.data(), n * 4));
+    OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.pos, pos.data(), n * 4));
+    OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.known, known.data(), n * 4));
+    OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.flags, flags.data(), n * 4));
+    OPURE_CUDA_CHECK(opure_fill(ctx_, buf_.keys, 0, size_t(n) * 8));
+    hostDriven_ = false;
+    seqIdentity_ = true;
+    Sync();
+}
+
+void VoxelEngine::ReadHistory(uint32_t slot, uint32_t pos, uint32_t count, int32_t *out) {
+    OPURE_CHECK(slot < opts_.maxBatch && uint64_t(pos) + count <= maxLen_, "history read out of range");
+    OPURE_CUDA_CHECK(opure_d2h(ctx_, out, buf_.tokens + size_t(slot) * maxLen_ + pos, size_t(count) * 4));
+    OPURE_CUDA_CHECK(opure_sync(ctx_, 60000));
 }
 
 VoxelEngine::MetricsSnapshot VoxelEngine::SnapshotMetrics() const {

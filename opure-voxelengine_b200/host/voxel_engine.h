@@ -61,6 +61,10 @@ struct StepTiming {
     uint32_t prefillSteps = 0, decodeSteps = 0;
 };
 
+// Reads the ctx's device status word; throws opure::Error naming the failing kernel site
+// and offending value when a kernel recorded a failure.
+void CheckDevice(opure_ctx *ctx);
+
 class VoxelEngine {
 public:
     VoxelEngine() = default;
@@ -109,6 +113,12 @@ public:
     // Loads precomputed fp16 K/V [L][2][n_kv][len][hd] for sequence slot `seq` and marks
     // `len` positions as cached (synthetic long contexts).
     void LoadKv(uint32_t seq, const uint16_t *kv, uint32_t len);
+    // Synthetic long contexts on the device: slots 0..n-1 get `len` cached positions of
+    // seeded KV values (opure_kv_synth), `reserve` positions of pages each, and continue
+    // self-driving from position len with first[v] as their next input.
+    void PrepareSynthetic(uint32_t n, uint32_t len, uint32_t reserve, uint64_t seed, const int32_t *first);
+    // Reads `count` tokens of a slot's token history from position `pos`.
+    void ReadHistory(uint32_t slot, uint32_t pos, uint32_t count, int32_t *out);
 
     struct MetricsSnapshot {
         float kvOccupancy = 0.0f;

@@ -85,6 +85,9 @@ def lib() -> C.CDLL:
             "opure_engine_trace": [P, i32, u32, P],
             "opure_engine_poison": [P, f32],
             "opure_engine_load_kv": [P, u32, P, u32],
+            "opure_engine_synth_context": [P, u32, u32, u32, u64, P],
+            "opure_engine_read_tokens": [P, u32, u32, u32, P],
+            "opure_synth_kv": [u64, u32, u32, u32, u32, u32, P],
             "opure_model_inspect": [C.c_char_p, P, C.c_char_p, C.c_size_t],
             "opure_synth_model": [C.c_char_p, P],
             "opure_synth_normal_f16": [u64, f32, u64, P],
@@ -157,6 +160,13 @@ def permutation(seed: int, n: int) -> np.ndarray:
 def uniforms(seed: int, n: int) -> np.ndarray:
     out = np.empty(n, np.float32)
     _check(lib().opure_synth_uniforms(seed, n, _p(out)), "opure_synth_uniforms")
+    return out
+
+
+def synth_kv(seed: int, slot: int, layers: int, n_kv: int, length: int, head_dim: int) -> np.ndarray:
+    """Host form of the device's synthetic KV context: [layers][2][n_kv][length][head_dim] fp16 bits."""
+    out = np.empty((layers, 2, n_kv, length, head_dim), np.uint16)
+    _check(lib().opure_synth_kv(seed, slot, layers, n_kv, length, head_dim, _p(out)), "opure_synth_kv")
     return out
 
 
@@ -275,6 +285,24 @@ class Engine:
 
     def poison(self, value: float):
         _check(lib().opure_engine_poison(self.h, value), "poison", self.h)
+
+    def synth_context(self, n: int, length: int, reserve: int, seed: int, first_tokens):
+        """Slots 0..n-1: `length` cached positions of seeded KV values, then self-driving
+        decode from position `length` with first_tokens[v] as input (run_steps)."""
+        f = np.ascontiguousarray(first_tokens, np.int32)
+        _check(lib().opure_engine_synth_context(self.h, n, length, reserve, seed, _p(f)), "synth_context",
+               self.h)
+
+    def run_steps(self, n: int, steps: int):
+        _check(lib().opure_engine_run_steps(self.h, n, steps), "run_steps", self.h)
+
+    def sync(self):
+        _check(lib().opure_engine_sync(self.h), "sync", self.h)
+
+    def read_tokens(self, slot: int, pos: int, count: int) -> np.ndarray:
+        out = np.zeros(count, np.int32)
+        _check(lib().opure_engine_read_tokens(self.h, slot, pos, count, _p(out)), "read_tokens", self.h)
+        return out
 
     def load_kv(self, seq: int, kv: np.ndarray, length: int):
         kv = np.ascontiguousarray(kv, np.uint16)

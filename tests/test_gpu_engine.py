@@ -216,3 +216,28 @@ def test_fused_host_driven_steps(models):
 def test_fused_path_refuses_int8(models):
     with pytest.raises(Exception):
         ve.Engine(models["q8"], max_len=32, path=ve.PATH_FUSED)
+
+
+@pytest.mark.parametrize("n,length", [(2, 200), (16, 130)])
+def test_synthetic_long_context_matches_oracle(models, small, n, length):
+    # Seeded KV contexts written on the device (opure_kv_synth) decode like the oracle
+    # given the same values through load_kv; n = 16 runs the tensor-core GEMV path.
+    c = SMALL
+    first = ve.prompt(77, c["vocab"], n)
+    with ve.Engine(models["small"], max_batch=n, max_len=length + 16) as eng:
+        eng.synth_context(n, length, length + 12, 9, first)
+        # A step's output enters the history as the next step's input: 9 steps leave 8.
+        eng.run_steps(n, 9)
+        eng.sync()
+        got = [eng.read_tokens(v, length + 1, 8) for v in range(n)]
+    for v in (0, n - 1):
+        st = small.state(length + 16)
+        st.load_kv(ve.synth_kv(9, v, c["layers"], c["kv_heads"], length, c["hidden"] // c["heads"]), length)
+        tok, want, margins = int(first[v]), [], []
+        for _ in range(8):
+            lg, _ = st.forward(tok)
+            tok = int(oracle.argmax(lg[None])[0][0])
+            want.append(tok)
+            top = np.sort(lg)[-2:]
+            margins.append(float(top[1] - top[0]))
+        assert_tokens(got[v], want, margins)

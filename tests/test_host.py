@@ -154,3 +154,25 @@ def test_truncated_safetensors_is_refused(tiny_dir, tmp_path):
     with pytest.raises(cu.OpureError) as e:
         ve.inspect(str(d))
     assert "past the end" in str(e.value)
+
+
+def test_synth_kv_matches_splitmix_restatement():
+    # The seeded long-context KV values (host form of opure_kv_synth) against an
+    # independent restatement of SplitMix64 + fp16(4u - 2).
+    M = (1 << 64) - 1
+
+    def splitmix(x):
+        z = (x + 0x9E3779B97F4A7C15) & M
+        z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & M
+        z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & M
+        return z ^ (z >> 31)
+
+    seed, slot, L, H, T, D = 5, 3, 2, 2, 9, 64
+    got = ve.synth_kv(seed, slot, L, H, T, D)
+    want = np.empty((L, 2, H, T, D), np.float16)
+    for idx in np.ndindex(L, 2, H, T, D):
+        l, s, h, t, d = idx
+        i = (((l * 2 + s) * H + h) * 65536 + t) * D + d
+        u = np.float32(splitmix(seed ^ (slot << 48) ^ i) >> 40) / np.float32(16777216.0)
+        want[idx] = np.float16(u * np.float32(4) - np.float32(2))
+    assert np.array_equal(got, want.view(np.uint16))
