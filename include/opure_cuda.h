@@ -365,6 +365,26 @@ opure_status opure_spec_gather(opure_ctx *ctx, const int32_t *hist, uint32_t max
                                const unsigned long long *keys, const int32_t *base, uint32_t n_seq,
                                uint32_t k, int32_t *verify_tokens, int32_t *draft);
 
+/* ---- tensor parallelism (the large-model configuration's 8-way TP at batch 1) --------
+ * NCCL communicators over NVLink/NVSwitch, loaded at run time from libnccl.so.2
+ * (OPURE_ERR_UNSUPPORTED when absent). One rank calls opure_comm_unique_id and sends the
+ * 128-byte id to the others out of band; every rank then calls opure_comm_init with its
+ * own ctx. Initialisation is non-blocking and bounded by timeout_ms (OPURE_ERR_TIMEOUT
+ * when a rank never joins). Collectives enqueue on the ctx stream (graph-capturable). */
+typedef struct opure_comm opure_comm;
+#define OPURE_COMM_ID_BYTES 128
+opure_status opure_comm_unique_id(uint8_t *id /* [OPURE_COMM_ID_BYTES] */);
+opure_status opure_comm_init(opure_ctx *ctx, uint32_t n_ranks, uint32_t rank, const uint8_t *id,
+                             uint32_t timeout_ms, opure_comm **out);
+opure_status opure_comm_destroy(opure_comm *c);
+opure_status opure_comm_info(const opure_comm *c, uint32_t *n_ranks, uint32_t *rank);
+/* In-place all-reduce over the communicator's ranks. */
+opure_status opure_allreduce_sum_f32(opure_ctx *ctx, opure_comm *c, float *buf, size_t n);
+opure_status opure_allreduce_max_u64(opure_ctx *ctx, opure_comm *c, unsigned long long *buf, size_t n);
+/* Argmax keys of a vocabulary shard whose first row is `offset`: rewrites each non-zero
+ * key's index to the global one (value bits unchanged), ready for a u64 max all-reduce. */
+opure_status opure_argmax_key_offset(opure_ctx *ctx, unsigned long long *keys, uint32_t n, uint32_t offset);
+
 /* ---- fault injection (host side; tests of the error paths) -----------------
  * The next `count` ABI calls after `after_calls` more calls return OPURE_ERR_INJECTED
  * without touching the GPU. count = 0 disarms. */

@@ -114,6 +114,16 @@ opure_status opure_engine_synth_context(opure_engine *e, uint32_t n, uint32_t le
 opure_status opure_engine_read_tokens(opure_engine *e, uint32_t slot, uint32_t pos, uint32_t count,
                                       int32_t *out);
 
+/* Tensor-parallel shard (the large-model configuration's 8-way TP at batch 1): the
+ * engine enqueues on `ctx` (which the caller created and keeps) and is rank r of n of
+ * `comm` (opure_comm_init on the same ctx). It holds q/k/v and gate/up rows, o_proj and
+ * down_proj columns and lm_head vocabulary rows of its shard, caches its KV heads, and
+ * each step all-reduces the o_proj and down_proj partial sums (fp32 sum) and the argmax
+ * keys (u64 max) over NCCL. Every rank must make the same calls in the same order.
+ * stream_bytes and kv_bytes_per_token of opure_engine_get_info are the shard's. */
+opure_status opure_engine_create_tp(const char *model_dir, opure_ctx *ctx, opure_comm *comm,
+                                    const opure_engine_options *opts, opure_engine **out);
+
 /* ---- speculative decoding (no reference counterpart: the reference's verify shader,
  *      Opure_SpeculativeDecode.usf:60-189, is never dispatched and it has no draft loop
  *      or accept rule; speculativeAcceptance is fixed at -1, Opure_VoxelEngine.cpp:666) */

@@ -1,6 +1,7 @@
 // context.cu -- lifetime, memory, synchronisation, graphs and timing of the C ABI.
 // Replaces the reference's D3D12 device layer (src/core/Opure_Dx12.{h,cpp}).
 #include <chrono>
+#include <cstdio>
 #include <cstring>
 #include <new>
 #include <thread>
@@ -98,7 +99,7 @@ opure_status opure_get_device_info(opure_ctx *ctx, opure_device_info *info) {
     int clk = 0;
     cudaDeviceGetAttribute(&clk, cudaDevAttrClockRate, ctx->device);
     info->clock_mhz_max = uint32_t(clk / 1000);
-    std::strncpy(info->name, prop.name, sizeof(info->name) - 1);
+    std::snprintf(info->name, sizeof(info->name), "%.95s", prop.name);
     return OPURE_OK;
 }
 

@@ -13,7 +13,6 @@
 namespace opure {
 namespace {
 
-constexpr int kMaxVec = 8;
 
 struct KvParams {
     uint16_t *pool;

@@ -69,12 +69,12 @@ opure::engine::EngineOptions ToOptions(const opure_engine_options *o) {
 }
 
 opure_status Create(const char *model_dir, int device, opure_ctx *shared, const opure_engine_options *o,
-                    opure_engine **out) {
+                    opure_engine **out, opure_comm *comm = nullptr) {
     if (!model_dir || !out) return OPURE_ERR_INVALID_ARG;
     *out = nullptr;
     auto *e = new (std::nothrow) opure_engine;
     if (!e) return OPURE_ERR_OUT_OF_MEMORY;
-    const opure_status s = Guard(e, [&] { e->eng.Initialize(model_dir, ToOptions(o), device, shared); });
+    const opure_status s = Guard(e, [&] { e->eng.Initialize(model_dir, ToOptions(o), device, shared, comm); });
     if (s != OPURE_OK) {
         g_create_error = e->err;
         delete e;
@@ -89,6 +89,15 @@ opure_status Create(const char *model_dir, int device, opure_ctx *shared, const 
 opure_status opure_engine_create(const char *model_dir, int device, const opure_engine_options *o,
                                  opure_engine **out) {
     return Create(model_dir, device, nullptr, o, out);
+}
+
+opure_status opure_engine_create_tp(const char *model_dir, opure_ctx *ctx, opure_comm *comm,
+                                    const opure_engine_options *o, opure_engine **out) {
+    if (!ctx || !comm) return OPURE_ERR_INVALID_ARG;
+    opure_device_info di{};
+    const opure_status s = opure_get_device_info(ctx, &di);
+    if (s != OPURE_OK) return s;
+    return Create(model_dir, di.device, ctx, o, out, comm);
 }
 
 opure_status opure_engine_create_shared(const char *model_dir, opure_engine *share,
@@ -183,11 +192,8 @@ void FillInfo(const opure::graph::Graph &g, opure_engine_info *info) {
     info->max_pos = c.maxPositions;
     info->w_dtype = p.wDtype;
     info->weight_bytes = p.weightBytes;
-    const uint64_t eb = p.wDtype == OPURE_W_Q8 ? 1 : 2;
-    const uint64_t h = c.hiddenSize, ff = c.intermediateSize;
-    const uint64_t perLayer = (uint64_t(c.QkvRows()) * h + h * h + 3 * ff * h) * eb + 2 * h * 2;
-    info->stream_bytes = perLayer * c.numLayers + uint64_t(c.vocabSize) * h * (p.lmQuantized ? 1 : 2) + h * 2;
-    info->kv_bytes_per_token = c.KvBytesPerToken();
+    info->stream_bytes = g.StreamBytes();
+    info->kv_bytes_per_token = c.KvBytesPerToken() / g.Local().tpSize;  // this shard's KV heads
 }
 
 }  // namespace

@@ -125,8 +125,25 @@ void Graph::LoadConfigOnly(const std::string &modelDir, const LayoutOptions &opt
 
 void Graph::PlanLayout(const LayoutOptions &opts) {
     plan_ = VramPlan{};
-    const uint64_t h = cfg_.hiddenSize, ff = cfg_.intermediateSize;
-    const uint64_t qkv = cfg_.QkvRows();
+    const uint32_t ts = opts.tpSize;
+    OPURE_CHECK(ts >= 1 && opts.tpRank < ts, "tensor-parallel rank out of range");
+    OPURE_CHECK(cfg_.numKvHeads % ts == 0, "num_key_value_heads must divide by the tensor-parallel size");
+    OPURE_CHECK(cfg_.intermediateSize % (16 * ts) == 0,
+                "intermediate_size / tensor-parallel size must be a multiple of 16");
+    OPURE_CHECK(cfg_.vocabSize % ts == 0, "vocab_size must divide by the tensor-parallel size");
+    local_ = LocalGeometry{};
+    local_.tpSize = ts;
+    local_.tpRank = opts.tpRank;
+    local_.heads = cfg_.numHeads / ts;
+    local_.kvHeads = cfg_.numKvHeads / ts;
+    local_.inter = cfg_.intermediateSize / ts;
+    local_.vocab = cfg_.vocabSize / ts;
+    local_.vocabOffset = local_.vocab * opts.tpRank;
+    OPURE_CHECK(ts == 1 || (uint64_t(local_.heads) * cfg_.HeadDim()) % 16 == 0,
+                "a shard's attention width must be a multiple of 16 elements");
+    const uint64_t h = cfg_.hiddenSize, ff = local_.inter;
+    const uint64_t qkv = local_.QkvRows(cfg_.HeadDim());
+    const uint64_t att = uint64_t(local_.heads) * cfg_.HeadDim();  // o_proj input columns
     // Matrices are all int8 or all floating point; mixing would need per-GEMV dtypes.
     bool anyQ = false, allQ = true;
     for (const BlockTensors &b : spec_.Blocks())
@@ -137,7 +154,7 @@ void Graph::PlanLayout(const LayoutOptions &opts) {
     OPURE_CHECK(!anyQ || allQ, "layer matrices mix int8 and floating point");
     plan_.wDtype = allQ ? OPURE_W_Q8 : OPURE_W_F16;
     const uint64_t eb = allQ ? 1 : 2;
-    plan_.hasFused = opts.fusedLayouts;
+    plan_.hasFused = opts.fusedLayouts && ts == 1;
 
     uint64_t cur = 0;
     auto place = [&](uint64_t bytes) {
@@ -151,9 +168,10 @@ void Graph::PlanLayout(const LayoutOptions &opts) {
     if (lm.Present() && !cfg_.tieWordEmbeddings) {
         plan_.lmQuantized = lm.IsQuantized();
         plan_.slm = lm.scale;
-        plan_.lmHead = place(uint64_t(cfg_.vocabSize) * h * (plan_.lmQuantized ? 1 : 2));
+        plan_.lmHead = place(uint64_t(local_.vocab) * h * (plan_.lmQuantized ? 1 : 2));
     } else {
-        plan_.lmHead = plan_.embedTokens;
+        // Tied: this shard's vocabulary rows of the (whole) embedding.
+        plan_.lmHead = plan_.embedTokens + uint64_t(local_.vocabOffset) * h * 2;
     }
     plan_.layers.resize(cfg_.numLayers);
     for (uint32_t l = 0; l < cfg_.numLayers; ++l) {
@@ -162,10 +180,10 @@ void Graph::PlanLayout(const LayoutOptions &opts) {
         t.inputNorm = place(h * 2);
         t.postAttNorm = place(h * 2);
         t.wqkv = place(qkv * h * eb);
-        t.wo = place(h * h * eb);
+        t.wo = place(h * att * eb);
         t.wgu = place(2 * ff * h * eb);
         t.wdown = place(h * ff * eb);
-        if (opts.fusedLayouts) {
+        if (plan_.hasFused) {
             t.woBlk = place(h * h * eb);
             t.wdownT = place(h * ff * eb);
         }
@@ -175,10 +193,19 @@ void Graph::PlanLayout(const LayoutOptions &opts) {
     plan_.weightBytes = cur;
 }
 
+uint64_t Graph::StreamBytes() const {
+    const uint64_t eb = plan_.wDtype == OPURE_W_Q8 ? 1 : 2;
+    const uint64_t h = cfg_.hiddenSize, ff = local_.inter, hd = cfg_.HeadDim();
+    const uint64_t perLayer = (uint64_t(local_.QkvRows(uint32_t(hd))) * h + h * local_.heads * hd + 3 * ff * h) * eb +
+                              2 * h * 2;
+    return perLayer * cfg_.numLayers + uint64_t(local_.vocab) * h * (plan_.lmQuantized ? 1 : 2) + h * 2;
+}
+
 void Graph::UploadWeights(opure_ctx *ctx, void *arena) {
     OPURE_CHECK(loaded_, "UploadWeights before LoadConfigOnly");
     auto *base = static_cast<uint8_t *>(arena);
     const uint64_t h = cfg_.hiddenSize, ff = cfg_.intermediateSize;
+    const uint32_t ts = local_.tpSize, tr = local_.tpRank;
     const uint32_t hd = cfg_.HeadDim(), G = cfg_.KvGroupSize(), nkv = cfg_.numKvHeads;
     const bool q8 = plan_.wDtype == OPURE_W_Q8;
     const uint64_t eb = q8 ? 1 : 2;
@@ -204,10 +231,30 @@ void Graph::UploadWeights(opure_ctx *ctx, void *arena) {
     put(plan_.embedTokens, stage);
     fetch(spec_.FinalNorm(), stage, false);
     put(plan_.finalNorm, stage);
-    if (plan_.lmHead != plan_.embedTokens) {
+    const uint64_t lmEb = plan_.lmQuantized ? 1 : 2;
+    if (!cfg_.tieWordEmbeddings && spec_.LmHead().Present()) {
         fetch(spec_.LmHead(), stage, true);
+        if (ts > 1) {  // this shard's vocabulary rows
+            const uint64_t rb = h * lmEb;
+            stage = std::vector<uint8_t>(stage.begin() + uint64_t(local_.vocabOffset) * rb,
+                                         stage.begin() + uint64_t(local_.vocabOffset + local_.vocab) * rb);
+        }
         put(plan_.lmHead, stage);
     }
+    // Row block [r0, r0 + nr) of a row-major matrix with `cols` columns.
+    auto rows = [&](std::vector<uint8_t> &m, uint64_t cols, uint64_t r0, uint64_t nr) {
+        if (ts == 1) return;
+        m = std::vector<uint8_t>(m.begin() + r0 * cols * eb, m.begin() + (r0 + nr) * cols * eb);
+    };
+    // Column block [c0, c0 + nc) of every row of a row-major [nrows][cols] matrix.
+    auto cols_of = [&](std::vector<uint8_t> &m, uint64_t nrows, uint64_t cols, uint64_t c0, uint64_t nc) {
+        if (ts == 1) return;
+        std::vector<uint8_t> out(nrows * nc * eb);
+        for (uint64_t r = 0; r < nrows; ++r)
+            std::copy_n(m.data() + (r * cols + c0) * eb, nc * eb, out.data() + r * nc * eb);
+        m.swap(out);
+    };
+    const uint64_t hq = uint64_t(local_.heads) * hd, hk = uint64_t(local_.kvHeads) * hd, ffl = local_.inter;
     std::vector<uint8_t> a, b2;
     for (uint32_t l = 0; l < cfg_.numLayers; ++l) {
         const BlockTensors &b = spec_.Blocks()[l];
@@ -220,10 +267,13 @@ void Graph::UploadWeights(opure_ctx *ctx, void *arena) {
         uint64_t off = t.wqkv;
         for (const TensorRef *r : {&b.wq, &b.wk, &b.wv}) {
             fetch(*r, stage, q8);
+            const uint64_t nr = r == &b.wq ? hq : hk;
+            rows(stage, h, uint64_t(tr) * nr, nr);  // this shard's heads
             put(off, stage);
             off += stage.size();
         }
         fetch(b.wo, a, q8);
+        cols_of(a, h, h, uint64_t(tr) * hq, hq);  // input columns of this shard's heads
         put(t.wo, a);
         if (plan_.hasFused) {
             // woBlk[g][o][c] = Wo[o][g*G*hd + c]: each kv head's input columns contiguous.
@@ -235,10 +285,13 @@ void Graph::UploadWeights(opure_ctx *ctx, void *arena) {
             put(t.woBlk, b2);
         }
         fetch(b.gate, stage, q8);
+        rows(stage, h, uint64_t(tr) * ffl, ffl);
         put(t.wgu, stage);
         fetch(b.up, stage, q8);
-        put(t.wgu + ff * h * eb, stage);
+        rows(stage, h, uint64_t(tr) * ffl, ffl);
+        put(t.wgu + ffl * h * eb, stage);
         fetch(b.down, a, q8);
+        cols_of(a, h, ff, uint64_t(tr) * ffl, ffl);
         put(t.wdown, a);
         if (plan_.hasFused) {
             b2.resize(a.size());

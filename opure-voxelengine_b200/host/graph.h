@@ -41,6 +41,17 @@ struct ModelConfig {
 
 struct LayoutOptions {
     bool fusedLayouts = true;  // also store o_proj grouped per kv head and down_proj^T
+    // Tensor parallelism: this device holds shard tpRank of tpSize. q/k/v and gate/up are
+    // split by rows (whole heads / intermediate rows), o_proj and down_proj by columns (the
+    // matching input slice), the lm_head by vocabulary rows; embeddings and norms are whole.
+    uint32_t tpSize = 1, tpRank = 0;
+};
+
+// The part of the model one tensor-parallel shard computes (the whole model at tpSize 1).
+struct LocalGeometry {
+    uint32_t heads = 0, kvHeads = 0, inter = 0, vocab = 0, vocabOffset = 0;
+    uint32_t tpSize = 1, tpRank = 0;
+    uint32_t QkvRows(uint32_t headDim) const { return (heads + 2 * kvHeads) * headDim; }
 };
 
 // Byte offsets into the weight arena.
@@ -78,6 +89,9 @@ public:
 
     const ModelConfig &Config() const { return cfg_; }
     const VramPlan &Plan() const { return plan_; }
+    const LocalGeometry &Local() const { return local_; }
+    // Weight bytes one decode step of this shard reads (matrices once, norms, lm_head rows).
+    uint64_t StreamBytes() const;
     const ModelSpec &Spec() const { return spec_; }
     bool IsLoaded() const { return loaded_; }
     bool IsQuantized() const { return plan_.wDtype == OPURE_W_Q8; }
@@ -87,6 +101,7 @@ private:
 
     ModelConfig cfg_;
     VramPlan plan_;
+    LocalGeometry local_;
     ModelSpec spec_;
     safetensors::WeightStreamer stream_;
     bool loaded_ = false;

@@ -35,7 +35,7 @@ void VoxelEngine::Shutdown() {
                     static_cast<void *>(buf_.seqLen), static_cast<void *>(buf_.known), static_cast<void *>(buf_.flags),
                     static_cast<void *>(buf_.inTokens), static_cast<void *>(buf_.tokens),
                     static_cast<void *>(buf_.base1), static_cast<void *>(buf_.delta0),
-                    static_cast<void *>(buf_.delta1), weights_})
+                    static_cast<void *>(buf_.delta1), static_cast<void *>(buf_.partial), weights_})
         if (p) opure_free(ctx_, p);
     for (auto &s : attnScratch_) opure_free(ctx_, s.second.first);
     attnScratch_.clear();
@@ -46,12 +46,13 @@ void VoxelEngine::Shutdown() {
     if (ownsCtx_) opure_shutdown(ctx_);
     ctx_ = nullptr;
     ownsCtx_ = true;
+    comm_ = nullptr;
     graph_.Release();
     ready_ = false;
 }
 
 void VoxelEngine::Initialize(const std::string &modelDir, const EngineOptions &opts, int device,
-                             opure_ctx *shared) {
+                             opure_ctx *shared, opure_comm *comm) {
     Shutdown();
     OPURE_CHECK(!opts.enablePlasticity, "the SignSGD plasticity pass is not part of this engine");
     OPURE_CHECK(opts.maxBatch >= 1, "maxBatch must be at least 1");
@@ -65,6 +66,12 @@ void VoxelEngine::Initialize(const std::string &modelDir, const EngineOptions &o
     }
     graph::LayoutOptions lo;
     lo.fusedLayouts = opts.path != 1;  // grouped o_proj and transposed down_proj
+    comm_ = comm;
+    if (comm) {
+        OPURE_CUDA_CHECK(opure_comm_info(comm, &lo.tpSize, &lo.tpRank));
+        lo.fusedLayouts = false;
+        OPURE_CHECK(opts.path != 2, "the fused decode path does not run tensor-parallel");
+    }
     graph_.LoadConfigOnly(modelDir, lo);
     const graph::ModelConfig &cfg = graph_.Config();
     const graph::VramPlan &plan = graph_.Plan();
@@ -74,7 +81,9 @@ void VoxelEngine::Initialize(const std::string &modelDir, const EngineOptions &o
 
     maxLen_ = opts.maxLen ? std::min(opts.maxLen, cfg.maxPositions) : std::min(cfg.maxPositions, 4096u);
     const uint32_t pagesPerSeq = (maxLen_ + opts.pageSize - 1) / opts.pageSize;
-    kv_.Create(ctx_, cfg, opts.pageSize, pagesPerSeq * opts.maxBatch, opts.maxBatch, pagesPerSeq, opts.pageSeed);
+    graph::ModelConfig kvCfg = cfg;
+    kvCfg.numKvHeads = graph_.Local().kvHeads;  // a shard caches only its own KV heads
+    kv_.Create(ctx_, kvCfg, opts.pageSize, pagesPerSeq * opts.maxBatch, opts.maxBatch, pagesPerSeq, opts.pageSeed);
     AllocBuffers();
     seqLen_ = 0;
     ready_ = true;
@@ -86,7 +95,7 @@ bool VoxelEngine::UsesFused(uint32_t n) const {
     const graph::ModelConfig &c = graph_.Config();
     const graph::VramPlan &p = graph_.Plan();
     const uint32_t hd = c.HeadDim(), G = c.KvGroupSize();
-    return opts_.path != 1 && p.hasFused && p.wDtype == OPURE_W_F16 && !p.lmQuantized &&
+    return opts_.path != 1 && !comm_ && p.hasFused && p.wDtype == OPURE_W_F16 && !p.lmQuantized &&
            (hd == 64 || hd == 128) && G >= 1 && G <= 4 && (n == 1 || n == 2 || n == 4 || n == 8) &&
            3ull * c.hiddenSize * 2 <= 160 * 1024;
 }
@@ -111,6 +120,7 @@ void VoxelEngine::AllocBuffers() {
     buf_.base1 = Alloc<float>(ctx_, size_t(B) * c.hiddenSize);
     buf_.delta0 = Alloc<long long>(ctx_, size_t(B) * c.hiddenSize);
     buf_.delta1 = Alloc<long long>(ctx_, size_t(B) * c.hiddenSize);
+    if (comm_) buf_.partial = Alloc<float>(ctx_, size_t(B) * c.hiddenSize);
     OPURE_CUDA_CHECK(opure_fill(ctx_, buf_.keys, 0, sizeof(unsigned long long) * B));
     OPURE_CUDA_CHECK(opure_fill(ctx_, buf_.tokens, 0, sizeof(int32_t) * size_t(B) * maxLen_));
     // Pinned staging for the host-driven step: [in_tokens B][positions B][keys B (u64)].
@@ -157,8 +167,9 @@ void VoxelEngine::RecordLayer(uint32_t L, uint32_t n) {
     const graph::ModelConfig &c = graph_.Config();
     const graph::VramPlan &plan = graph_.Plan();
     const graph::VramPlan::LayerTensors &t = plan.layers[L];
-    const uint32_t h = c.hiddenSize, ff = c.intermediateSize, hd = c.HeadDim();
-    const uint32_t qkvRows = c.QkvRows();
+    const graph::LocalGeometry &lg = graph_.Local();  // the whole model unless tensor-parallel
+    const uint32_t h = c.hiddenSize, ff = lg.inter, hd = c.HeadDim();
+    const uint32_t qkvRows = lg.QkvRows(hd), att = lg.heads * hd;
     const bool q8 = plan.wDtype == OPURE_W_Q8;
     const uint64_t eb = q8 ? 1 : 2;
 
@@ -193,7 +204,7 @@ void VoxelEngine::RecordLayer(uint32_t L, uint32_t n) {
         gemv(At(weights_, t.wqkv), 1.f, 1.f, qkvRows, h, buf_.x, h, buf_.qkv, qkvRows, OPURE_PRO_RMSNORM,
              inNorm, OPURE_EPI_STORE, nullptr);
     } else {
-        const uint32_t qr = c.numHeads * hd, kr = c.numKvHeads * hd;
+        const uint32_t qr = lg.heads * hd, kr = lg.kvHeads * hd;
         gemv(At(weights_, t.wqkv), t.sq, t.sq, qr, h, buf_.x, h, buf_.qkv, qkvRows, OPURE_PRO_RMSNORM,
              inNorm, OPURE_EPI_STORE, nullptr);
         gemv(At(weights_, t.wqkv + uint64_t(qr) * h * eb), t.sk, t.sk, kr, h, buf_.x, h, buf_.qkv + qr, qkvRows,
@@ -202,7 +213,7 @@ void VoxelEngine::RecordLayer(uint32_t L, uint32_t n) {
              qkvRows, OPURE_PRO_RMSNORM, inNorm, OPURE_EPI_STORE, nullptr);
     }
     const opure_kv_layout kv = kv_.Layout(L);
-    OPURE_CUDA_CHECK(opure_rope_kv_append(ctx_, buf_.qkv, qkvRows, buf_.q, buf_.seq, buf_.pos, n, c.numHeads,
+    OPURE_CUDA_CHECK(opure_rope_kv_append(ctx_, buf_.qkv, qkvRows, buf_.q, buf_.seq, buf_.pos, n, lg.heads,
                                           c.ropeTheta, &kv));
     opure_attn_args a{};
     a.q = buf_.q;
@@ -211,22 +222,38 @@ void VoxelEngine::RecordLayer(uint32_t L, uint32_t n) {
     a.seq_len = buf_.seqLen;
     a.n = n;
     a.n_q = 1;
-    a.n_heads = c.numHeads;
+    a.n_heads = lg.heads;
     a.scale = opts_.attnScale;
     a.max_ctx = maxLen_;
     a.split_tokens = 0;
     a.scratch = AttnScratch(n, &a.scratch_bytes);
     a.kv = kv;
     OPURE_CUDA_CHECK(opure_attention(ctx_, &a));
-    // o_proj + residual, in place on the residual stream.
-    gemv(At(weights_, t.wo), t.so, t.so, h, h, buf_.attn, h, buf_.x, h, OPURE_PRO_NONE, nullptr, OPURE_EPI_ADD,
-         buf_.x);
+    if (!comm_) {
+        // o_proj + residual, in place on the residual stream.
+        gemv(At(weights_, t.wo), t.so, t.so, h, h, buf_.attn, h, buf_.x, h, OPURE_PRO_NONE, nullptr, OPURE_EPI_ADD,
+             buf_.x);
+    } else {
+        // Tensor parallel: this shard's heads give a partial o_proj sum over their input
+        // columns; the shards' partials are summed over NCCL, then added to the residual.
+        gemv(At(weights_, t.wo), t.so, t.so, h, att, buf_.attn, h, buf_.partial, h, OPURE_PRO_NONE, nullptr,
+             OPURE_EPI_STORE, nullptr);
+        OPURE_CUDA_CHECK(opure_allreduce_sum_f32(ctx_, comm_, buf_.partial, size_t(n) * h));
+        OPURE_CUDA_CHECK(opure_add(ctx_, buf_.x, buf_.partial, buf_.x, n * h));
+    }
     // gate;up with the post-attention norm, SwiGLU epilogue.
     gemv(At(weights_, t.wgu), t.sgate, t.sup, ff, h, buf_.x, h, buf_.h, ff, OPURE_PRO_RMSNORM, postNorm,
          OPURE_EPI_SWIGLU, nullptr);
-    // down_proj + residual.
-    gemv(At(weights_, t.wdown), t.sdown, t.sdown, h, ff, buf_.h, ff, buf_.x, h, OPURE_PRO_NONE, nullptr,
-         OPURE_EPI_ADD, buf_.x);
+    if (!comm_) {
+        // down_proj + residual.
+        gemv(At(weights_, t.wdown), t.sdown, t.sdown, h, ff, buf_.h, ff, buf_.x, h, OPURE_PRO_NONE, nullptr,
+             OPURE_EPI_ADD, buf_.x);
+    } else {
+        gemv(At(weights_, t.wdown), t.sdown, t.sdown, h, ff, buf_.h, ff, buf_.partial, h, OPURE_PRO_NONE, nullptr,
+             OPURE_EPI_STORE, nullptr);
+        OPURE_CUDA_CHECK(opure_allreduce_sum_f32(ctx_, comm_, buf_.partial, size_t(n) * h));
+        OPURE_CUDA_CHECK(opure_add(ctx_, buf_.x, buf_.partial, buf_.x, n * h));
+    }
 }
 
 void VoxelEngine::RecordStep(uint32_t n, bool logits) {
@@ -286,19 +313,26 @@ void VoxelEngine::RecordStep(uint32_t n, bool logits) {
     a.w_dtype = plan.lmQuantized ? uint32_t(OPURE_W_Q8) : uint32_t(OPURE_W_F16);
     a.scale_w = plan.slm;
     a.scale_x = 1.0f;
-    a.rows = c.vocabSize;
+    const graph::LocalGeometry &lg = graph_.Local();
+    a.rows = lg.vocab;  // tensor parallel: this shard's vocabulary rows
     a.cols = c.hiddenSize;
     a.nvec = n;
     a.x = buf_.x;
     a.x_stride = c.hiddenSize;
     a.y = logits ? buf_.logits : nullptr;
-    a.y_stride = c.vocabSize;
+    a.y_stride = lg.vocab;
     a.prologue = OPURE_PRO_RMSNORM;
     a.norm_gain = reinterpret_cast<const uint16_t *>(At(weights_, plan.finalNorm));
     a.eps = c.rmsNormEps;
     a.epilogue = OPURE_EPI_ARGMAX;
     a.argmax_keys = buf_.keys;
     OPURE_CUDA_CHECK(opure_gemv(ctx_, &a));
+    if (comm_) {
+        // Vocabulary shards: global indices, then the largest key over all shards (ties
+        // keep the lowest global index, as in one unsplit argmax).
+        OPURE_CUDA_CHECK(opure_argmax_key_offset(ctx_, buf_.keys, n, lg.vocabOffset));
+        OPURE_CUDA_CHECK(opure_allreduce_max_u64(ctx_, comm_, buf_.keys, n));
+    }
     OPURE_CUDA_CHECK(opure_step_end(ctx_, &io));
 }
 
@@ -540,6 +574,7 @@ uint32_t VoxelEngine::ForwardArgMax(const std::vector<uint32_t> &tokens) {
 
 void VoxelEngine::ForwardLogits(const std::vector<uint32_t> &tokens, std::vector<float> &logitsOut) {
     OPURE_CHECK(!tokens.empty(), "ForwardLogits called with no tokens");
+    OPURE_CHECK(!comm_, "ForwardLogits is not available on a tensor-parallel shard (logits are split)");
     ResetSequences({tokens}, uint32_t(tokens.size()), true);
     RunSteps(1, uint32_t(tokens.size()), true);
     Sync();

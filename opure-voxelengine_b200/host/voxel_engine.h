@@ -76,8 +76,12 @@ public:
     // `shared`, the engine enqueues on that existing ctx (stream) instead of creating its
     // own: engines that cooperate on one stream (speculative decoding's draft and target)
     // then need no synchronisation between them. The owner of `shared` must outlive it.
+    // With `comm` (created on `shared`'s or this engine's device), the engine is shard
+    // rank-of-n of a tensor-parallel model: it holds its slice of the weights and KV heads,
+    // and every step all-reduces the o_proj and down_proj partial sums and the vocabulary
+    // shards' argmax keys over NCCL. All ranks must step in lockstep.
     void Initialize(const std::string &modelDir, const EngineOptions &opts, int device,
-                    opure_ctx *shared = nullptr);
+                    opure_ctx *shared = nullptr, opure_comm *comm = nullptr);
     void Shutdown();
     bool IsReady() const { return ready_; }
 
@@ -165,6 +169,7 @@ public:
         // Fused path: second residual base and the two fixed-point delta buffers.
         float *base1 = nullptr;
         long long *delta0 = nullptr, *delta1 = nullptr;
+        float *partial = nullptr;  // tensor parallelism: [maxBatch][hidden] shard partial sums
     };
     // True when steps of n vectors run on opure_decode_fused.
     bool UsesFused(uint32_t n) const;
@@ -196,6 +201,7 @@ private:
     bool hostDriven_ = false; // step flags currently cleared for host-supplied tokens
     bool seqIdentity_ = true; // vector v currently maps to sequence slot v
     bool ownsCtx_ = true;
+    opure_comm *comm_ = nullptr;  // tensor-parallel communicator (not owned)
 };
 
 }  // namespace opure::engine

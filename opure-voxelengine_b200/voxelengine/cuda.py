@@ -89,6 +89,14 @@ _SIGS = {
     "opure_debug_inject_failure": [P, u32, u32],
     "opure_step_begin": [P, P], "opure_step_end": [P, P],
     "opure_attention_static": [P, P],
+    "opure_last_error_detail": [P, P, P],
+    "opure_sample_keys": [P, P, u32, u32, P, P, P, sz],
+    "opure_spec_gather": [P, P, u32, P, P, u32, u32, P, P],
+    "opure_kv_synth": [P, P, u32, u32, u32, u32, u64],
+    "opure_comm_init": [P, u32, u32, P, u32, P], "opure_comm_destroy": [P],
+    "opure_comm_info": [P, P, P],
+    "opure_allreduce_sum_f32": [P, P, P, sz], "opure_allreduce_max_u64": [P, P, P, sz],
+    "opure_argmax_key_offset": [P, P, u32, u32],
 }
 
 
@@ -107,6 +115,8 @@ def lib() -> C.CDLL:
         L.opure_strerror.restype = C.c_char_p
         L.opure_stream.argtypes = [P]
         L.opure_stream.restype = P
+        L.opure_comm_unique_id.argtypes = [P]
+        L.opure_comm_unique_id.restype = C.c_int
         L.opure_attention_scratch_bytes.argtypes = [u32, u32, u32, u32, u32, u32, u32]
         L.opure_attention_scratch_bytes.restype = sz
         _lib = L
@@ -223,6 +233,37 @@ class Ctx:
 
     def call(self, name: str, *args):
         check(getattr(lib(), name)(self.h, *args), name)
+
+
+COMM_ID_BYTES = 128
+
+
+def comm_unique_id() -> bytes:
+    """NCCL unique id (created on one rank; send it to the others out of band)."""
+    buf = (C.c_uint8 * COMM_ID_BYTES)()
+    check(lib().opure_comm_unique_id(buf), "opure_comm_unique_id")
+    return bytes(buf)
+
+
+class Comm:
+    """Tensor-parallel communicator (opure_comm) of rank `rank` of `n_ranks` on `ctx`."""
+
+    def __init__(self, ctx: Ctx, n_ranks: int, rank: int, uid: bytes, timeout_ms: int = 60000):
+        idbuf = (C.c_uint8 * COMM_ID_BYTES).from_buffer_copy(uid)
+        h = C.c_void_p()
+        check(lib().opure_comm_init(ctx.h, n_ranks, rank, idbuf, timeout_ms, C.byref(h)), "opure_comm_init")
+        self.h, self.ctx, self.n_ranks, self.rank = h, ctx, n_ranks, rank
+
+    def allreduce_sum(self, buf: "DeviceBuffer", n: int):
+        check(lib().opure_allreduce_sum_f32(self.ctx.h, self.h, buf.ptr, n), "opure_allreduce_sum_f32")
+
+    def allreduce_max_u64(self, buf: "DeviceBuffer", n: int):
+        check(lib().opure_allreduce_max_u64(self.ctx.h, self.h, buf.ptr, n), "opure_allreduce_max_u64")
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().opure_comm_destroy(self.h)
+            self.h = None
 
 
 class Graph:

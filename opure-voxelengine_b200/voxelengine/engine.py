@@ -71,6 +71,7 @@ def lib() -> C.CDLL:
         sigs = {
             "opure_engine_create": [C.c_char_p, C.c_int, P, P],
             "opure_engine_create_shared": [C.c_char_p, P, P, P],
+            "opure_engine_create_tp": [C.c_char_p, P, P, P, P],
             "opure_engine_spec_generate": [P, P, P, u32, u32, u32, P, P, P, u32, P],
             "opure_engine_destroy": [P],
             "opure_engine_get_info": [P, P],
@@ -187,18 +188,22 @@ class Engine:
     def __init__(self, model_dir: str, device: int = 0, max_batch: int = 1, max_len: int = 0,
                  page_size: int = 64, page_seed: int = 3, use_graphs: bool = True,
                  attn_scale: float = 1.0, max_new_tokens: int = 256, path: int = PATH_AUTO,
-                 share: "Engine | None" = None):
+                 share: "Engine | None" = None, comm: "cuda.Comm | None" = None):
         """With `share`, the engine runs on that engine's ctx (stream), as the draft of a
-        speculative pair must; it keeps a reference so the owner outlives it."""
+        speculative pair must; it keeps a reference so the owner outlives it. With `comm`
+        it is that communicator's tensor-parallel shard, on the communicator's ctx."""
         o = EngineOptions(max_new_tokens, max_batch, max_len, page_size, page_seed,
                           int(use_graphs), attn_scale, path)
         h = C.c_void_p()
-        if share is None:
+        if comm is not None:
+            st = lib().opure_engine_create_tp(model_dir.encode(), comm.ctx.h, comm.h, C.byref(o), C.byref(h))
+        elif share is None:
             st = lib().opure_engine_create(model_dir.encode(), device, C.byref(o), C.byref(h))
         else:
             st = lib().opure_engine_create_shared(model_dir.encode(), share.h, C.byref(o), C.byref(h))
         _check(st, "opure_engine_create", None)
         self.share = share
+        self.comm = comm
         self.h = h
         self.info = EngineInfo()
         _check(lib().opure_engine_get_info(self.h, C.byref(self.info)), "get_info", self.h)
@@ -208,6 +213,7 @@ class Engine:
             lib().opure_engine_destroy(self.h)
             self.h = None
         self.share = None
+        self.comm = None
 
     __del__ = close
 
