@@ -535,6 +535,105 @@ def run_cfg4(args, world, rank, local):
     eng.close()
 
 
+def run_tp(args, world, rank, local):
+    """Config 4, second variant: batch-1 greedy decode of the 1.7B shape with world-way tensor
+    parallelism, one rank per GPU. Every step all-reduces (NCCL over NVLink) the o_proj and
+    down_proj partial sums of each layer (48 x 8 KB fp32 per token) and the vocabulary
+    shards' argmax keys (8 B). 32-token prompt (seed 1) prefilled, then device-resident steps
+    (graph replays, NCCL inside the graph) at positions 32..159 (cyclic). Device time, max
+    over ranks. `comm_us` is one 2048-float all-reduce timed on its own (100-call average)."""
+    import ctypes as C
+
+    import torch.distributed as dist
+
+    from voxelengine import cuda as cu
+    from voxelengine import engine as ve
+    root = os.environ.get("OPURE_BENCH_DIR", "/tmp/opure_bench")
+    path = os.path.join(root, "llama1p7b_seed5")
+    if rank == 0:
+        ve.synth_model(path, seed=5, **ve.LLAMA_1_7B)
+    barrier(world)
+    mp = ve.synth_model(path, seed=5, **ve.LLAMA_1_7B)
+    obj = [cu.comm_unique_id() if rank == 0 else None]
+    if world > 1:
+        dist.broadcast_object_list(obj, src=0)
+    ctx = cu.Ctx(local)
+    comm = cu.Comm(ctx, world, rank, obj[0], timeout_ms=120000)
+    eng = ve.Engine(mp, max_len=PROMPT_LEN + DECODE_STEPS + 8, comm=comm)
+    info = eng.info
+    L = cu.lib()
+    eng.generate([ve.prompt(1, info.vocab, PROMPT_LEN)], DECODE_STEPS)
+    pos_rewind = np.full(1, PROMPT_LEN, np.int32)
+
+    def rewind():
+        cu.check(ve.lib().opure_engine_set_positions(eng.h, pos_rewind.ctypes.data_as(C.c_void_p), 1),
+                 "set_positions")
+
+    def run(n_steps):
+        left = n_steps
+        while left:
+            chunk = min(left, run.remaining)
+            eng.run_steps(1, chunk)
+            run.remaining -= chunk
+            left -= chunk
+            if run.remaining == 0:
+                rewind()
+                run.remaining = DECODE_STEPS
+    run.remaining = DECODE_STEPS
+    rewind()
+    ev0, ev1 = _events(ctx.h)
+    run(args.warmup)
+    eng.sync()
+    barrier(world)
+    cu.check(L.opure_event_record(ctx.h, ev0), "event")
+    run(args.steps)
+    cu.check(L.opure_event_record(ctx.h, ev1), "event")
+    eng.sync()
+    ms = C.c_float()
+    cu.check(L.opure_event_elapsed_ms(ev0, ev1, C.byref(ms)), "elapsed")
+    barrier(world)
+    dev_ms = allreduce_max(world, float(ms.value))
+    # One o_proj-sized all-reduce on its own: 100 of them captured in a CUDA graph (as the
+    # decode step runs them), replayed and timed on the device.
+    buf = ctx.buffer(info.hidden * 4).fill(0)
+    g = cu.Graph(ctx)
+    with g:
+        for _ in range(100):
+            comm.allreduce_sum(buf, info.hidden)
+    for _ in range(3):
+        g.launch()
+    ctx.sync()
+    barrier(world)
+    cu.check(L.opure_event_record(ctx.h, ev0), "event")
+    g.launch()
+    cu.check(L.opure_event_record(ctx.h, ev1), "event")
+    ctx.sync()
+    g.free()
+    cu.check(L.opure_event_elapsed_ms(ev0, ev1, C.byref(ms)), "elapsed")
+    comm_us = allreduce_max(world, float(ms.value) * 10.0)
+    step_ms = dev_ms / args.steps
+    positions = [PROMPT_LEN + (i % DECODE_STEPS) for i in range(DECODE_STEPS)]
+    sbytes = step_bytes(info, 1, positions)   # this shard's weights and KV heads
+    achieved = sbytes / (step_ms * 1e-3) / 1e9
+    peak, peak_kind = peaks()
+    line = {"metric": "config-4 TP decode tok/s (1.7B shape, batch 1, tensor-parallel)",
+            "value": args.steps / (dev_ms * 1e-3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "strong",
+            "dtype": "f16 weights/KV, f32 accumulate", "data": "synthetic",
+            "config": {"workload": f"cfg4 TP-{world}: 1.7B shape, bs1, 32-token prompt, positions 32..159 cyclic",
+                       "global_batch": 1, "seq_len": PROMPT_LEN + DECODE_STEPS, "parallelism": f"tp{world}"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
+                         "bytes_per_step": sbytes, "kernel": "whole decode step, per GPU (its shard)"},
+            "comm": {"allreduce_us_2048_f32": comm_us, "allreduces_per_step": 2 * info.layers + 1,
+                     "est_ms_per_step": comm_us * (2 * info.layers + 1) / 1000.0}}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    eng.close()
+    comm.close()
+    ctx.close()
+
+
 def run_spec(args):
     """Config 3: speculative decoding. Target = the config-0 model; draft = the same weights
     plus seeded N(0, 0.004) noise on every matrix element (noise seed 6); k = 4 and 8;
@@ -598,7 +697,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-steps", type=int, default=128)
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", choices=["decode", "attn", "gemv", "spec", "cfg4"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "attn", "gemv", "spec", "cfg4", "tp"], default="decode")
     ap.add_argument("--seqs", type=int, default=512, help="cfg4: total sequences over all ranks")
     ap.add_argument("--wave", type=int, default=128, help="cfg4: sequences per GPU per wave")
     ap.add_argument("--quick", action="store_true",
@@ -617,6 +716,8 @@ def main():
             run_spec(args)
         elif args.workload == "cfg4":
             run_cfg4(args, world, rank, local)
+        elif args.workload == "tp":
+            run_tp(args, world, rank, local)
         else:
             run_ours(args, world, rank, local)
     finally:
