@@ -203,7 +203,8 @@ def run_ours(args, world, rank, local):
         mp = model_dir()
     B = args.batch
     max_len = PROMPT_LEN + DECODE_STEPS + 8
-    eng = ve.Engine(mp, device=local, max_batch=B, max_len=max_len, page_size=64, page_seed=3)
+    path = {"auto": ve.PATH_AUTO, "layers": ve.PATH_FUSED_LAYERS, "unfused": ve.PATH_UNFUSED}[args.path]
+    eng = ve.Engine(mp, device=local, max_batch=B, max_len=max_len, page_size=64, page_seed=3, path=path)
     info = eng.info
     L = cu.lib()
     ctx = eng.ctx
@@ -698,6 +699,9 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=128)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--workload", choices=["decode", "attn", "gemv", "spec", "cfg4", "tp"], default="decode")
+    ap.add_argument("--path", choices=["auto", "layers", "unfused"], default="auto",
+                    help="decode: step kernels (auto = one persistent kernel per step when eligible, "
+                         "layers = three fused kernels per layer, unfused = per-op kernels)")
     ap.add_argument("--seqs", type=int, default=512, help="cfg4: total sequences over all ranks")
     ap.add_argument("--wave", type=int, default=128, help="cfg4: sequences per GPU per wave")
     ap.add_argument("--quick", action="store_true",

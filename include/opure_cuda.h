@@ -324,7 +324,16 @@ typedef struct opure_fused_step {
     float *q;                          /* [nvec][n_heads head_dim]                        */
     float *logits;                     /* [nvec][vocab] or NULL                          */
     unsigned long long *keys;          /* [nvec] argmax keys (zeroed by opure_step_begin) */
+    uint32_t *sync;                    /* [3 n_layers + 1] device words for the persistent
+                                          kernel's grid barriers (reset by the call), or NULL */
+    uint32_t mode;                     /* OPURE_FUSED_AUTO or OPURE_FUSED_LAYER_KERNELS     */
 } opure_fused_step;
+/* AUTO: when the model fits (head_dim 64, <= 48 layers, each phase's work in one wave of
+ * CTAs, a layer's weight slices of one CTA double-buffered in shared memory) and `sync` is
+ * given, the whole step is ONE persistent cooperative kernel (one CTA per SM) whose layer
+ * phases meet at bounded grid-wide barriers; otherwise the three kernels per layer above.
+ * LAYER_KERNELS: always the three kernels per layer. */
+enum { OPURE_FUSED_AUTO = 0, OPURE_FUSED_LAYER_KERNELS = 1 };
 opure_status opure_decode_fused(opure_ctx *ctx, const opure_fused_step *s);
 
 /* ---- speculative verify / accept (no reference counterpart: the reference's

@@ -40,7 +40,9 @@ typedef struct opure_engine_options {
 enum {
     OPURE_PATH_AUTO = 0,      /* fused latency kernels when eligible, else per-op kernels */
     OPURE_PATH_UNFUSED = 1,   /* per-op kernels: GEMV, RoPE+KV, attention, GEMV, ...      */
-    OPURE_PATH_FUSED = 2      /* opure_decode_fused; creation fails when not eligible     */
+    OPURE_PATH_FUSED = 2,     /* opure_decode_fused; creation fails when not eligible     */
+    OPURE_PATH_FUSED_LAYERS = 3 /* opure_decode_fused as three kernels per layer (never the
+                                   persistent single-kernel step)                        */
 };
 
 typedef struct opure_engine_info {

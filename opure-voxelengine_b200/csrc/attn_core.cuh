@@ -74,8 +74,9 @@ __device__ __forceinline__ void load_q_slice(const float *q_heads /* [n_heads][H
 }
 
 // Accumulates keys [t_begin, t_end) into the lane state. The calling warp processes
-// blocks base = t_begin + warp_idx*TB, advancing by warp_count*TB.
-template <int HD, int G>
+// blocks base = t_begin + warp_idx*TB, advancing by warp_count*TB. COHERENT reads K/V
+// through L2 (for caches written earlier in the same kernel).
+template <int HD, int G, bool COHERENT = false>
 __device__ __forceinline__ void attend_range(AttnState<HD, G> &st, const float (&qv)[G][AttnShape<HD>::E],
                                              const KvView &kv, uint32_t t_begin, uint32_t t_end,
                                              uint32_t warp_idx, uint32_t warp_count,
@@ -107,8 +108,13 @@ __device__ __forceinline__ void attend_range(AttnState<HD, G> &st, const float (
             }
 #pragma unroll
             for (int c = 0; c < CH; ++c) {
-                kr[r][c] = valid[r] ? ldg_stream(kp + c * 8) : make_uint4(0, 0, 0, 0);
-                vr[r][c] = valid[r] ? ldg_stream(kp + size_t(kv.n_kv) * blk + c * 8) : make_uint4(0, 0, 0, 0);
+                if (COHERENT) {
+                    kr[r][c] = valid[r] ? ldcg_v4(kp + c * 8) : make_uint4(0, 0, 0, 0);
+                    vr[r][c] = valid[r] ? ldcg_v4(kp + size_t(kv.n_kv) * blk + c * 8) : make_uint4(0, 0, 0, 0);
+                } else {
+                    kr[r][c] = valid[r] ? ldg_stream(kp + c * 8) : make_uint4(0, 0, 0, 0);
+                    vr[r][c] = valid[r] ? ldg_stream(kp + size_t(kv.n_kv) * blk + c * 8) : make_uint4(0, 0, 0, 0);
+                }
             }
         }
         float s[R][G];

@@ -31,6 +31,24 @@ __device__ __forceinline__ void report(DeviceStatus *st, uint32_t code, uint32_t
 // ---------------------------------------------------------------------------
 // Memory access helpers.
 
+// 16-byte load from L2 (coherent across SMs within one kernel): for data other CTAs of the
+// same (persistent) kernel write, which the non-coherent path may serve stale.
+__device__ __forceinline__ uint4 ldcg_v4(const void *p) {
+    uint4 r;
+    asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+// L2 policy for weights: every byte is read once per step, so weights are marked
+// evict-first and the KV cache and activations (reused every step) stay resident in L2.
+__device__ __forceinline__ uint64_t l2_evict_first() {
+    uint64_t pol;
+    asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
 // 16-byte streaming load that bypasses L1 allocation: weights are read once per step.
 __device__ __forceinline__ uint4 ldg_stream(const void *p) {
     uint4 r;

@@ -121,6 +121,98 @@ __device__ __forceinline__ void stage_residual(const float *base, const long lon
     __syncthreads();
 }
 
+// stage_residual in one pass: each thread keeps the groups it loaded in registers, sums
+// their squares per vector, and after a single block reduction scales and stores them:
+// two barriers and no second trip through shared memory. A thread holds NV float4 groups,
+// so it needs NV*h/4 <= NV * blockDim.x, i.e. h <= 4 * blockDim.x (stage_residual_fits).
+template <int NV>
+__device__ __forceinline__ bool stage_residual_fits(uint32_t h) {
+    return h <= 4 * blockDim.x;
+}
+
+template <int NV>
+__device__ __forceinline__ void stage_residual_fast(const float *base, const long long *delta, uint32_t h,
+                                                    const GainPrefetch &gpre, const __half *gain, float eps,
+                                                    float *xs, float *red, float *base_out, long long *delta_zero,
+                                                    bool designated) {
+    constexpr int kFastSlots = NV;
+    const uint32_t groups = NV * h / 4, step = blockDim.x;
+    float4 xv[kFastSlots];
+    longlong2 d[kFastSlots][2];
+#pragma unroll
+    for (int k = 0; k < kFastSlots; ++k) {
+        const uint32_t g = threadIdx.x + k * step;
+        if (g < groups) {
+            xv[k] = __ldcg(reinterpret_cast<const float4 *>(base) + g);
+            if (delta) {
+                d[k][0] = __ldcg(reinterpret_cast<const longlong2 *>(delta) + 2 * g);
+                d[k][1] = __ldcg(reinterpret_cast<const longlong2 *>(delta) + 2 * g + 1);
+            }
+        }
+    }
+    float ss[NV];
+#pragma unroll
+    for (int v = 0; v < NV; ++v) ss[v] = 0.f;
+#pragma unroll
+    for (int k = 0; k < kFastSlots; ++k) {
+        const uint32_t g = threadIdx.x + k * step;
+        if (g >= groups) continue;
+        float4 x = xv[k];
+        if (delta) {
+            x.x = float(double(x.x) + double(d[k][0].x) * kFixInv);
+            x.y = float(double(x.y) + double(d[k][0].y) * kFixInv);
+            x.z = float(double(x.z) + double(d[k][1].x) * kFixInv);
+            x.w = float(double(x.w) + double(d[k][1].y) * kFixInv);
+        }
+        xv[k] = x;
+        if (designated) {
+            if (base_out) reinterpret_cast<float4 *>(base_out)[g] = x;
+            if (delta_zero) {
+                reinterpret_cast<longlong2 *>(delta_zero)[2 * g] = make_longlong2(0, 0);
+                reinterpret_cast<longlong2 *>(delta_zero)[2 * g + 1] = make_longlong2(0, 0);
+            }
+        }
+        const float s2 = fmaf(x.w, x.w, fmaf(x.z, x.z, fmaf(x.y, x.y, x.x * x.x)));
+        const uint32_t v = (4 * g) / h;
+#pragma unroll
+        for (int vv = 0; vv < NV; ++vv)
+            if (vv == int(v)) ss[vv] += s2;
+    }
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u, nw = blockDim.x >> 5;
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+        const float t = warp_sum(ss[v]);
+        if (lane == 0) red[v * 32 + warp] = t;
+    }
+    __syncthreads();
+    float inv[NV];
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+        float t = 0.f;
+        for (uint32_t w = 0; w < nw; ++w) t += red[v * 32 + w];
+        inv[v] = float(1.0 / sqrt(double(t) / double(h) + double(eps)));
+    }
+#pragma unroll
+    for (int k = 0; k < kFastSlots; ++k) {
+        const uint32_t g = threadIdx.x + k * step;
+        if (g >= groups) continue;
+        const uint32_t v = (4 * g) / h;
+        float iv = inv[0];
+#pragma unroll
+        for (int vv = 1; vv < NV; ++vv)
+            if (vv == int(v)) iv = inv[vv];
+        const uint2 gw = k < kGainRegs ? gpre.g[k] : __ldg(reinterpret_cast<const uint2 *>(gain + (4 * g) % h));
+        const float2 g01 = h2f2(gw.x), g23 = h2f2(gw.y);
+        float4 x = xv[k];
+        x.x = x.x * iv * g01.x;
+        x.y = x.y * iv * g01.y;
+        x.z = x.z * iv * g23.x;
+        x.w = x.w * iv * g23.y;
+        reinterpret_cast<float4 *>(xs)[g] = x;
+    }
+    __syncthreads();
+}
+
 // Dot products of R rows held in shared memory (row r at w + r * pitch bytes) with NV
 // vectors xs[v * h + i]; lanes stride the row's 16-byte chunks. Every lane gets the sums.
 template <int NV, int R>
@@ -157,21 +249,27 @@ __device__ __forceinline__ void smem_dot(const uint8_t *w, uint32_t pitch, uint3
         for (int v = 0; v < NV; ++v) acc[r][v] = warp_sum(acc[r][v]);
 }
 
-__device__ __forceinline__ __half *kv_slot(const KvParams &kv, uint32_t n_kv, uint32_t hd, int32_t seq,
-                                           int32_t pos, uint32_t sel, uint32_t head, DeviceStatus *st) {
+// Element offset of (seq, pos, K|V, kv head) row inside a layer's pool, or -1 (reported).
+__device__ __forceinline__ long long kv_offset(const KvParams &kv, uint32_t n_kv, uint32_t hd, int32_t seq,
+                                               int32_t pos, uint32_t sel, uint32_t head, DeviceStatus *st) {
     const uint32_t lp = uint32_t(pos) / kv.page_size;
     if (seq < 0 || pos < 0 || lp >= kv.max_pages) {
         report(st, OPURE_ERR_DEVICE_BOUNDS, 30, uint32_t(pos));
-        return nullptr;
+        return -1;
     }
     const int32_t page = kv.page_table[size_t(seq) * kv.max_pages + lp];
     if (page < 0 || uint32_t(page) >= kv.n_pages) {
         report(st, OPURE_ERR_DEVICE_BOUNDS, 31, uint32_t(page));
-        return nullptr;
+        return -1;
     }
     const size_t blk = size_t(kv.page_size) * hd;
-    return reinterpret_cast<__half *>(kv.pool) + ((size_t(page) * 2 + sel) * n_kv + head) * blk +
-           size_t(uint32_t(pos) % kv.page_size) * hd;
+    return (long long)(((size_t(page) * 2 + sel) * n_kv + head) * blk + size_t(uint32_t(pos) % kv.page_size) * hd);
+}
+
+__device__ __forceinline__ __half *kv_slot(const KvParams &kv, uint32_t n_kv, uint32_t hd, int32_t seq,
+                                           int32_t pos, uint32_t sel, uint32_t head, DeviceStatus *st) {
+    const long long off = kv_offset(kv, n_kv, hd, seq, pos, sel, head, st);
+    return off < 0 ? nullptr : reinterpret_cast<__half *>(kv.pool) + off;
 }
 
 // ---------------------------------------------------------------------------------------
@@ -518,6 +616,480 @@ __global__ void __launch_bounds__(kLThreads) lm_head_kernel(LmArgs a) {
 }
 
 // ---------------------------------------------------------------------------------------
+// P: the whole step as ONE persistent cooperative kernel, one CTA per SM. Each layer runs
+// the A, B and C phases above in turn, separated by grid-wide counters instead of kernel
+// boundaries; every CTA's weight slices of layer L+2 are copied (TMA bulk, double-buffered
+// per layer) while layers L+1 runs, and the lm_head follows the last layer. Data produced
+// inside the kernel by other CTAs (q, the appended KV rows, residual sums) is read through
+// L2 (ld.cg / atomics), never through the non-coherent path. Every wait is bounded (1 s):
+// a CTA that gives up records DEVICE_TIMEOUT, raises the grid's abort flag (so the others
+// leave their waits at once), waits for its own copies in flight and returns.
+constexpr uint32_t kPThreads = 256;
+constexpr int kPWarps = kPThreads / 32;
+constexpr uint32_t kPMaxLayers = 48;
+constexpr uint32_t kPtStageP = 256;
+constexpr uint32_t kLmBufs = 8;
+
+struct PLayer {
+    const uint8_t *w_qkv, *w_o_blk, *w_gu, *w_down_t;
+    const __half *in_norm, *post_norm;
+    uint16_t *kv_pool;
+};
+
+struct PersistArgs {
+    PLayer layers[kPMaxLayers];
+    uint32_t n_layers, h, inter, n_heads, n_kv, hd, vocab;
+    float eps, scale_log2;
+    double theta;
+    const __half *final_norm;
+    const uint8_t *lm_head;
+    const int32_t *page_table;
+    uint32_t n_pages, max_pages, page_size;
+    const int32_t *seq, *pos;
+    float *base0, *base1;
+    long long *delta0, *delta1;
+    float *q, *logits;
+    unsigned long long *keys;
+    uint32_t *sync;   // [3 n_layers] barrier counters, then the abort flag; zero at launch
+    DeviceStatus *st;
+    uint32_t qkv_rows, a_ctas;  // A: kARows q;k;v rows per CTA
+    uint32_t rows_b, rbs;       // B: CTA b < n_kv * rbs takes kv head b / rbs, o_proj row block b % rbs
+    uint32_t F, c_ctas;         // C: F intermediate rows per CTA
+    uint32_t slot_bytes, off_b, off_c;
+    uint32_t lm_rows, lm_chunk, lm_nbuf;  // lm_head: rows per CTA, rows per TMA chunk, chunk buffers
+};
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Grid-wide barrier k: every CTA arrives once; thread 0 waits (bounded) for all of them.
+__device__ bool grid_barrier(const PersistArgs &p, uint32_t k, int *s_ok) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t *ctr = p.sync + k;
+        const uint32_t *abort_flag = p.sync + 3 * p.n_layers;
+        __threadfence();
+        atomicAdd(ctr, 1u);
+        int ok = 1;
+        const uint64_t t0 = global_ns();
+        for (uint32_t i = 0;; ++i) {
+            if (ld_acquire_gpu(ctr) >= gridDim.x) break;
+            if ((i & 31u) == 31u) {
+                if (ld_acquire_gpu(abort_flag)) {
+                    ok = 0;
+                    break;
+                }
+                if (global_ns() - t0 > 1000000000ull) {
+                    report(p.st, OPURE_ERR_DEVICE_TIMEOUT, 50, k);
+                    atomicExch(p.sync + 3 * p.n_layers, 1u);
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+        *s_ok = ok;
+    }
+    __syncthreads();
+    return *s_ok != 0;
+}
+
+// This CTA's share of each phase (the same for every layer).
+struct PShare {
+    uint32_t na, a_row0;               // A rows
+    uint32_t nb, g, b_row0;            // B: kv head, o_proj rows
+    uint32_t nc, f0;                   // C intermediate rows
+};
+
+template <int HD, int G>
+__device__ __forceinline__ PShare p_share(const PersistArgs &p) {
+    PShare s{};
+    const uint32_t b = blockIdx.x;
+    if (b < p.a_ctas) {
+        s.a_row0 = b * kARows;
+        s.na = min(kARows, p.qkv_rows - s.a_row0);
+    }
+    if (b < p.n_kv * p.rbs) {
+        s.g = b / p.rbs;
+        s.b_row0 = (b % p.rbs) * p.rows_b;
+        s.nb = s.b_row0 < p.h ? min(p.rows_b, p.h - s.b_row0) : 0;
+    }
+    if (b < p.c_ctas) {
+        s.f0 = b * p.F;
+        s.nc = s.f0 < p.inter ? min(p.F, p.inter - s.f0) : 0;
+    }
+    return s;
+}
+
+template <int HD, int G>
+__device__ __forceinline__ uint32_t p_bytes(const PersistArgs &p, const PShare &s) {
+    return s.na * p.h * 2 + s.nb * G * HD * 2 + 3 * s.nc * p.h * 2;
+}
+
+// Thread 0: copy layer L's slices of this CTA into `slot`, completing on `bar`.
+template <int HD, int G>
+__device__ void p_issue(const PersistArgs &p, const PShare &s, uint32_t L, uint8_t *slot, uint64_t *bar) {
+    const uint32_t bytes = p_bytes<HD, G>(p, s);
+    if (!bytes) return;
+    const PLayer &ly = p.layers[L];
+    const uint32_t pitch = p.h * 2, bpitch = G * HD * 2;
+    // The slot was last read through the generic proxy; order that before the async writes.
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    mbar_expect_tx(bar, bytes);
+    if (s.na) bulk_load(slot, ly.w_qkv + size_t(s.a_row0) * pitch, s.na * pitch, bar);
+    if (s.nb)
+        bulk_load(slot + p.off_b, ly.w_o_blk + (size_t(s.g) * p.h + s.b_row0) * bpitch, s.nb * bpitch, bar);
+    if (s.nc) {
+        uint8_t *c = slot + p.off_c;
+        bulk_load(c, ly.w_gu + size_t(s.f0) * pitch, s.nc * pitch, bar);
+        bulk_load(c + p.F * pitch, ly.w_gu + (size_t(p.inter) + s.f0) * pitch, s.nc * pitch, bar);
+        bulk_load(c + 2 * p.F * pitch, ly.w_down_t + size_t(s.f0) * pitch, s.nc * pitch, bar);
+    }
+}
+
+// Whole-CTA bounded wait on `bar` reaching the end of phase `parity`.
+__device__ bool p_wait_slot(uint64_t *bar, uint32_t parity, const PersistArgs &p, int *s_ok) {
+    if (threadIdx.x == 0) {
+        *s_ok = 1;
+        if (!mbar_wait(bar, parity)) {
+            report(p.st, OPURE_ERR_DEVICE_TIMEOUT, 51, blockIdx.x);
+            atomicExch(p.sync + 3 * p.n_layers, 1u);  // the others leave their barrier waits
+            *s_ok = 0;
+        }
+    }
+    __syncthreads();
+    const bool ok = *s_ok != 0;
+    if (ok) mbar_wait(bar, parity);  // every thread observes the completed phase
+    return ok;
+}
+
+template <int NV, int HD, int G>
+__global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __grid_constant__ PersistArgs p) {
+    extern __shared__ __align__(1024) uint8_t psm[];
+    __shared__ __align__(8) uint64_t full[2];
+    __shared__ __align__(8) uint64_t lbar[kLmBufs];
+    __shared__ int s_ok;
+    __shared__ WarpStates<HD, G, kPWarps> ws;
+    __shared__ int32_t s_seq[NV], s_pos[NV];
+    __shared__ int32_t s_pt[NV][kPtStageP];
+    __shared__ unsigned long long cta_best[kPWarps][NV];
+    constexpr uint32_t cols_b = G * HD, bpitch = cols_b * 2;
+    const uint32_t pitch = p.h * 2;
+    uint8_t *slots[2] = {psm, psm + p.slot_bytes};
+    float *xs = reinterpret_cast<float *>(psm + 2 * size_t(p.slot_bytes));
+    float *red = xs + NV * p.h;
+    float *hs = red + 33 * NV;          // [F][NV]
+    float *attn = hs + ((p.F * NV + 3) & ~3u);  // [NV][G*HD], 16-byte aligned
+    const uint32_t b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const PShare sh = p_share<HD, G>(p);
+    const bool has_bytes = p_bytes<HD, G>(p, sh) != 0;
+    const bool stage_pt = p.max_pages <= kPtStageP;
+    const uint32_t qrows = p.n_heads * HD, krows = p.n_kv * HD;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&full[0], 1);
+        mbar_init(&full[1], 1);
+        for (uint32_t j = 0; j < kLmBufs; ++j) mbar_init(&lbar[j], 1);
+    }
+    // Sequences, positions and page tables are fixed for the step: stage them once.
+    if (threadIdx.x < NV) {
+        s_seq[threadIdx.x] = p.seq[threadIdx.x];
+        s_pos[threadIdx.x] = p.pos[threadIdx.x];
+    }
+    __syncthreads();
+    if (stage_pt)
+        for (uint32_t i = threadIdx.x; i < NV * p.max_pages; i += blockDim.x) {
+            const int32_t s = s_seq[i / p.max_pages];
+            s_pt[i / p.max_pages][i % p.max_pages] =
+                s >= 0 ? p.page_table[size_t(s) * p.max_pages + i % p.max_pages] : -1;
+        }
+    uint32_t issued = 0, waited = 0;
+    if (threadIdx.x == 0) {
+        for (uint32_t L = 0; L < 2 && L < p.n_layers; ++L) p_issue<HD, G>(p, sh, L, slots[L], &full[L]);
+    }
+    issued = min(2u, p.n_layers);
+    __syncthreads();
+
+    // RoPE angles and KV-row offsets depend only on the step's positions: resolved once
+    // for all layers (lane v < NV of each A warp owns vector v of its row pair).
+    const bool fast_stage = stage_residual_fits<NV>(p.h);
+    const uint32_t a_r = sh.a_row0 + 2 * warp;
+    const bool a_epi = sh.na && 2 * warp < sh.na && lane < NV;
+    double a_sn = 0.0, a_cs = 1.0;
+    long long a_kv = -1;  // element offset of this lane's K or V pair inside a layer pool
+    if (a_epi) {
+        const int32_t ps = s_pos[lane], sq = s_seq[lane];
+        if (a_r < qrows + krows)
+            sincos(double(ps) * pow(p.theta, -2.0 * double((a_r % HD) / 2) / double(HD)), &a_sn, &a_cs);
+        if (a_r >= qrows) {
+            const bool is_k = a_r < qrows + krows;
+            const uint32_t rr = is_k ? a_r - qrows : a_r - qrows - krows;
+            const KvParams k0{nullptr, p.page_table, p.n_pages, p.max_pages, p.page_size};
+            const long long off = kv_offset(k0, p.n_kv, HD, sq, ps, is_k ? 0 : 1, rr / HD, p.st);
+            if (off >= 0) a_kv = off + rr % HD;
+        }
+    }
+
+    // lm_head: this CTA's contiguous rows, streamed by TMA in chunks of lm_chunk rows
+    // through lm_nbuf buffers laid over the two (then free) layer slots.
+    const uint32_t lm_r0 = min(p.vocab, b * p.lm_rows), lm_r1 = min(p.vocab, lm_r0 + p.lm_rows);
+    const uint32_t lm_nchunks = (lm_r1 - lm_r0 + p.lm_chunk - 1) / p.lm_chunk;
+    const uint32_t lm_cbytes = p.lm_chunk * pitch;
+    uint32_t lm_issued = 0, lm_done = 0;
+    auto lm_issue = [&](uint32_t i) {  // thread 0
+        const uint32_t r0 = lm_r0 + i * p.lm_chunk, nr = min(p.lm_chunk, lm_r1 - r0);
+        uint64_t *bar = &lbar[i % p.lm_nbuf];
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_expect_tx(bar, nr * pitch);
+        bulk_load(psm + size_t(i % p.lm_nbuf) * lm_cbytes, p.lm_head + size_t(r0) * pitch, nr * pitch, bar);
+    };
+    // Chunk buffer j lies in the layer slot that is free during the last layer?
+    auto lm_in_free_slot = [&](uint32_t j) {
+        const uint32_t fs = p.n_layers & 1u;  // slot of layer n_layers - 2
+        const size_t lo = size_t(j) * lm_cbytes, hi = lo + lm_cbytes;
+        return p.n_layers >= 2 && lo >= size_t(fs) * p.slot_bytes && hi <= size_t(fs + 1) * p.slot_bytes;
+    };
+
+    for (uint32_t L = 0; L < p.n_layers; ++L) {
+        const PLayer &ly = p.layers[L];
+        uint8_t *sl = slots[L & 1];
+        if (has_bytes && !p_wait_slot(&full[L & 1], (L >> 1) & 1u, p, &s_ok)) goto abort;
+        ++waited;
+        if (L + 1 == p.n_layers) {
+            // The other slot is free for the rest of the step: start the lm_head chunks
+            // that live in it (in order, so chunk i always sits in buffer i % lm_nbuf).
+            while (lm_issued < lm_nchunks && lm_issued < p.lm_nbuf && lm_in_free_slot(lm_issued)) {
+                if (threadIdx.x == 0) lm_issue(lm_issued);
+                ++lm_issued;
+            }
+        }
+        const KvParams kvp{ly.kv_pool, p.page_table, p.n_pages, p.max_pages, p.page_size};
+
+        // ---- A: RMSNorm + q;k;v + RoPE + KV append ----------------------------------
+        if (sh.na) {
+            GainPrefetch gpre;
+            prefetch_gain<NV>(ly.in_norm, p.h, gpre);
+            if (fast_stage)
+                stage_residual_fast<NV>(p.base0, L == 0 ? nullptr : p.delta1, p.h, gpre, ly.in_norm, p.eps, xs, red,
+                                        b == 0 ? p.base1 : nullptr, b == 0 ? p.delta0 : nullptr, b == 0);
+            else
+                stage_residual<NV>(p.base0, L == 0 ? nullptr : p.delta1, p.h, gpre, ly.in_norm, p.eps, xs, red,
+                                   b == 0 ? p.base1 : nullptr, b == 0 ? p.delta0 : nullptr, b == 0);
+            if (2 * warp < sh.na) {
+                float acc[2][NV];
+                smem_dot<NV, 2>(sl + size_t(2 * warp) * pitch, pitch, min(2u, sh.na - 2 * warp), pitch / 16, xs,
+                                p.h, acc);
+                if (a_epi) {
+                    const uint32_t v = lane, r = a_r;
+                    float e0 = 0.f, e1 = 0.f;
+#pragma unroll
+                    for (int k = 0; k < NV; ++k)
+                        if (k == int(v)) {
+                            e0 = acc[0][k];
+                            e1 = acc[1][k];
+                        }
+                    __half *slot = a_kv >= 0 ? reinterpret_cast<__half *>(ly.kv_pool) + a_kv : nullptr;
+                    if (r < qrows + krows) {
+                        // RoPE, interleaved pairs, theta^(-2*pair/hd) (Opure_RoPE.usf:56), in double.
+                        const float r0 = float(double(e0) * a_cs - double(e1) * a_sn);
+                        const float r1 = float(double(e0) * a_sn + double(e1) * a_cs);
+                        if (r < qrows) {
+                            p.q[size_t(v) * qrows + r] = r0;
+                            p.q[size_t(v) * qrows + r + 1] = r1;
+                        } else if (slot) {
+                            slot[0] = __float2half_rn(r0);
+                            slot[1] = __float2half_rn(r1);
+                        }
+                    } else if (slot) {
+                        slot[0] = __float2half_rn(e0);
+                        slot[1] = __float2half_rn(e1);
+                    }
+                }
+            }
+        }
+        if (!grid_barrier(p, 3 * L, &s_ok)) goto abort;
+
+        // ---- B: attention of kv head g + o_proj partial sums ------------------------
+        if (b == 0)
+            for (uint32_t i = threadIdx.x; i < NV * p.h; i += blockDim.x) p.delta1[i] = 0;
+        if (sh.nb) {
+            for (int v = 0; v < NV; ++v) {
+                using S = AttnShape<HD>;
+                float qv[G][S::E];
+                const uint32_t sub = lane % S::LPT;
+#pragma unroll
+                for (int hh = 0; hh < G; ++hh) {
+                    const float4 *qr = reinterpret_cast<const float4 *>(
+                        p.q + size_t(v) * qrows + (size_t(sh.g) * G + hh) * HD + sub * S::E);
+#pragma unroll
+                    for (int e = 0; e < S::E / 4; ++e) {
+                        const float4 t = __ldcg(qr + e);
+                        qv[hh][4 * e] = t.x * p.scale_log2;
+                        qv[hh][4 * e + 1] = t.y * p.scale_log2;
+                        qv[hh][4 * e + 2] = t.z * p.scale_log2;
+                        qv[hh][4 * e + 3] = t.w * p.scale_log2;
+                    }
+                }
+                AttnState<HD, G> st;
+                st.init();
+                const int32_t s = s_seq[v];
+                KvView kv{reinterpret_cast<const __half *>(ly.kv_pool),
+                          stage_pt ? s_pt[v] : p.page_table + size_t(max(s, 0)) * p.max_pages,
+                          p.max_pages, p.n_pages, p.page_size, p.n_kv, sh.g, s >= 0};
+                attend_range<HD, G, true>(st, qv, kv, 0, uint32_t(max(s_pos[v] + 1, 0)), warp, kPWarps, p.st);
+                merge_lane_groups<HD, G>(st);
+                store_warp_state<HD, G, kPWarps>(st, ws, warp);
+                __syncthreads();
+                for (uint32_t idx = threadIdx.x; idx < cols_b; idx += blockDim.x) {
+                    float acc, m, l;
+                    merge_warps<HD, G, kPWarps>(ws, idx / HD, idx % HD, acc, m, l);
+                    attn[v * cols_b + idx] = acc / fmaxf(l, 1e-30f);
+                }
+                __syncthreads();
+            }
+            const uint8_t *wsm = sl + p.off_b;
+            constexpr uint32_t nch = bpitch / 16;
+            for (uint32_t rr = warp; rr < sh.nb; rr += kPWarps) {
+                float acc[NV];
+#pragma unroll
+                for (int v = 0; v < NV; ++v) acc[v] = 0.f;
+                for (uint32_t c = lane; c < nch; c += 32) {
+                    float wf[8];
+                    unpack8(*reinterpret_cast<const uint4 *>(wsm + size_t(rr) * bpitch + c * 16), wf);
+#pragma unroll
+                    for (int v = 0; v < NV; ++v)
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) acc[v] = fmaf(wf[e], attn[v * cols_b + c * 8 + e], acc[v]);
+                }
+#pragma unroll
+                for (int v = 0; v < NV; ++v) {
+                    const float t = warp_sum(acc[v]);
+                    if (lane == uint32_t(v))
+                        atomicAdd(reinterpret_cast<unsigned long long *>(p.delta0 + size_t(v) * p.h + sh.b_row0 + rr),
+                                  static_cast<unsigned long long>(to_fix(t)));
+                }
+            }
+        }
+        if (!grid_barrier(p, 3 * L + 1, &s_ok)) goto abort;
+
+        // ---- C: RMSNorm + gate;up + SwiGLU + down partial sums ----------------------
+        if (sh.nc) {
+            GainPrefetch gpre;
+            prefetch_gain<NV>(ly.post_norm, p.h, gpre);
+            if (fast_stage)
+                stage_residual_fast<NV>(p.base1, p.delta0, p.h, gpre, ly.post_norm, p.eps, xs, red,
+                                        b == 0 ? p.base0 : nullptr, nullptr, b == 0);
+            else
+                stage_residual<NV>(p.base1, p.delta0, p.h, gpre, ly.post_norm, p.eps, xs, red,
+                                   b == 0 ? p.base0 : nullptr, nullptr, b == 0);
+            const uint8_t *wg = sl + p.off_c, *wu = wg + p.F * pitch, *wd = wg + 2 * p.F * pitch;
+            for (uint32_t f = warp; f < sh.nc; f += kPWarps) {
+                float acc[1][NV], accu[1][NV];
+                smem_dot<NV, 1>(wg + size_t(f) * pitch, pitch, 1, pitch / 16, xs, p.h, acc);
+                smem_dot<NV, 1>(wu + size_t(f) * pitch, pitch, 1, pitch / 16, xs, p.h, accu);
+                if (lane == 0) {
+#pragma unroll
+                    for (int v = 0; v < NV; ++v) {
+                        const float gv = acc[0][v], uv = accu[0][v];
+                        const float sg = 1.0f / (1.0f + expf(-gv));  // Opure_CpuReference.cpp:195
+                        hs[f * NV + v] = (gv * sg) * uv;
+                    }
+                }
+            }
+            __syncthreads();
+            const __half *wdh = reinterpret_cast<const __half *>(wd);
+            for (uint32_t o = threadIdx.x; o < p.h; o += blockDim.x) {
+                float acc[NV];
+#pragma unroll
+                for (int v = 0; v < NV; ++v) acc[v] = 0.f;
+                for (uint32_t f = 0; f < sh.nc; ++f) {
+                    const float wv = __half2float(wdh[size_t(f) * p.h + o]);
+#pragma unroll
+                    for (int v = 0; v < NV; ++v) acc[v] = fmaf(wv, hs[f * NV + v], acc[v]);
+                }
+#pragma unroll
+                for (int v = 0; v < NV; ++v)
+                    atomicAdd(reinterpret_cast<unsigned long long *>(p.delta1 + size_t(v) * p.h + o),
+                              static_cast<unsigned long long>(to_fix(acc[v])));
+            }
+        }
+        __syncthreads();
+        // This slot's layer is done: start copying layer L+2 into it.
+        if (L + 2 < p.n_layers) {
+            if (threadIdx.x == 0) p_issue<HD, G>(p, sh, L + 2, sl, &full[L & 1]);
+            ++issued;
+        }
+        if (L + 1 == p.n_layers)
+            // Both slots are free now: the remaining first-round chunks.
+            while (lm_issued < lm_nchunks && lm_issued < p.lm_nbuf) {
+                if (threadIdx.x == 0) lm_issue(lm_issued);
+                ++lm_issued;
+            }
+        if (!grid_barrier(p, 3 * L + 2, &s_ok)) goto abort;
+    }
+
+    {
+        // ---- L: final RMSNorm + lm_head + argmax keys (+ logits) ---------------------
+        GainPrefetch gpre;
+        prefetch_gain<NV>(p.final_norm, p.h, gpre);
+        if (fast_stage)
+            stage_residual_fast<NV>(p.base0, p.delta1, p.h, gpre, p.final_norm, p.eps, xs, red, nullptr, nullptr,
+                                    false);
+        else
+            stage_residual<NV>(p.base0, p.delta1, p.h, gpre, p.final_norm, p.eps, xs, red, nullptr, nullptr, false);
+        unsigned long long best[NV];
+#pragma unroll
+        for (int v = 0; v < NV; ++v) best[v] = 0ull;
+        for (uint32_t i = 0; i < lm_nchunks; ++i) {
+            const uint32_t j = i % p.lm_nbuf;
+            if (!p_wait_slot(&lbar[j], (i / p.lm_nbuf) & 1u, p, &s_ok)) goto abort;
+            ++lm_done;
+            const uint32_t r0 = lm_r0 + i * p.lm_chunk, nr = min(p.lm_chunk, lm_r1 - r0);
+            const uint8_t *buf = psm + size_t(j) * lm_cbytes;
+            for (uint32_t rr = 2 * warp; rr < nr; rr += 2 * kPWarps) {
+                float acc[2][NV];
+                smem_dot<NV, 2>(buf + size_t(rr) * pitch, pitch, min(2u, nr - rr), pitch / 16, xs, p.h, acc);
+#pragma unroll
+                for (int r = 0; r < 2; ++r)
+#pragma unroll
+                    for (int v = 0; v < NV; ++v) {
+                        if (rr + r >= nr) continue;
+                        const unsigned long long k = argmax_key(acc[r][v], r0 + rr + r);
+                        best[v] = k > best[v] ? k : best[v];
+                        if (p.logits && lane == uint32_t((r * NV + v) & 31))
+                            p.logits[size_t(v) * p.vocab + r0 + rr + r] = acc[r][v];
+                    }
+            }
+            __syncthreads();  // buffer j read by every warp: refill it
+            if (lm_issued < lm_nchunks) {
+                if (threadIdx.x == 0) lm_issue(lm_issued);
+                ++lm_issued;
+            }
+        }
+        if (lane == 0)
+#pragma unroll
+            for (int v = 0; v < NV; ++v) cta_best[warp][v] = best[v];
+        __syncthreads();
+        if (threadIdx.x < NV) {
+            unsigned long long bb = 0ull;
+            for (uint32_t w = 0; w < kPWarps; ++w) bb = cta_best[w][threadIdx.x] > bb ? cta_best[w][threadIdx.x] : bb;
+            if (bb) atomicMax(p.keys + threadIdx.x, bb);
+        }
+    }
+    return;
+
+abort:
+    // Leave no copy in flight into this CTA's shared memory (bounded waits).
+    if (threadIdx.x == 0) {
+        if (has_bytes)
+            for (uint32_t L = waited; L < issued; ++L) mbar_wait(&full[L & 1], (L >> 1) & 1u);
+        for (uint32_t i = lm_done; i < lm_issued; ++i) mbar_wait(&lbar[i % p.lm_nbuf], (i / p.lm_nbuf) & 1u);
+    }
+}
+
+// ---------------------------------------------------------------------------------------
 template <typename K>
 opure_status allow_smem(K k, size_t bytes) {
     if (bytes <= 48 * 1024) return OPURE_OK;
@@ -580,8 +1152,113 @@ opure_status run_step(opure_ctx *ctx, const opure_fused_step &s) {
     return launch(ctx, lm_head_kernel<NV>, dim3(ctas), dim3(kLThreads), l_smem, true, la);
 }
 
+// The persistent kernel when this model and batch fit it: every phase's work in one wave
+// of CTAs (one per SM) and a layer's slices of one CTA, double-buffered, in shared memory.
+// Sets *ran; returns an error only for a failed launch.
+template <int NV, int HD, int G>
+opure_status run_persistent(opure_ctx *ctx, const opure_fused_step &s, bool *ran) {
+    *ran = false;
+    if (!s.sync || s.n_layers > kPMaxLayers || s.head_dim != HD) return OPURE_OK;
+    const uint32_t grid = uint32_t(ctx->sm_count);
+    const uint32_t h = s.hidden;
+    PersistArgs p{};
+    p.qkv_rows = (s.n_heads + 2 * s.n_kv) * HD;
+    p.a_ctas = (p.qkv_rows + kARows - 1) / kARows;
+    const uint32_t rb_target = std::max<uint32_t>(1, grid / s.n_kv);
+    p.rows_b = (h + rb_target - 1) / rb_target;
+    p.rbs = (h + p.rows_b - 1) / p.rows_b;
+    p.F = (s.inter + grid - 1) / grid;
+    p.c_ctas = (s.inter + p.F - 1) / p.F;
+    if (p.a_ctas > grid || s.n_kv * p.rbs > grid || p.c_ctas > grid) return OPURE_OK;
+    const uint32_t pitch = h * 2;
+    p.off_b = (kARows * pitch + 127) & ~127u;
+    p.off_c = (p.off_b + p.rows_b * G * HD * 2 + 127) & ~127u;
+    p.slot_bytes = (p.off_c + 3 * p.F * pitch + 1023) & ~1023u;
+    p.lm_rows = (s.vocab + grid - 1) / grid;
+    p.lm_chunk = 16;
+    p.lm_nbuf = std::min<uint32_t>(kLmBufs, (2 * p.slot_bytes) / (p.lm_chunk * pitch));
+    if (p.lm_nbuf < 2) return OPURE_OK;
+    const size_t scratch = (size_t(NV) * h + 33 * NV + ((p.F * NV + 3) & ~3u) + size_t(NV) * G * HD) * 4;
+    const size_t smem = 2 * size_t(p.slot_bytes) + scratch;
+    auto kern = persistent_step_kernel<NV, HD, G>;
+    cudaFuncAttributes fa{};
+    if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return OPURE_ERR_CUDA;
+    if (smem + fa.sharedSizeBytes + 1024 > ctx->smem_optin) return OPURE_OK;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+        return OPURE_ERR_CUDA;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kPThreads, smem) != cudaSuccess || per_sm < 1)
+        return OPURE_OK;
+
+    p.n_layers = s.n_layers;
+    p.h = h;
+    p.inter = s.inter;
+    p.n_heads = s.n_heads;
+    p.n_kv = s.n_kv;
+    p.hd = HD;
+    p.vocab = s.vocab;
+    p.eps = s.eps;
+    p.scale_log2 = s.attn_scale * 1.4426950408889634f;
+    p.theta = s.theta;
+    p.final_norm = reinterpret_cast<const __half *>(s.final_norm);
+    p.lm_head = reinterpret_cast<const uint8_t *>(s.lm_head);
+    p.page_table = s.page_table;
+    p.n_pages = s.n_pages;
+    p.max_pages = s.max_pages;
+    p.page_size = s.page_size;
+    p.seq = s.seq;
+    p.pos = s.pos;
+    p.base0 = s.x;
+    p.base1 = s.base1;
+    p.delta0 = s.delta0;
+    p.delta1 = s.delta1;
+    p.q = s.q;
+    p.logits = s.logits;
+    p.keys = s.keys;
+    p.sync = s.sync;
+    p.st = ctx->status;
+    for (uint32_t L = 0; L < s.n_layers; ++L) {
+        const opure_fused_layer &l = s.layers[L];
+        p.layers[L] = PLayer{reinterpret_cast<const uint8_t *>(l.w_qkv), reinterpret_cast<const uint8_t *>(l.w_o_blk),
+                             reinterpret_cast<const uint8_t *>(l.w_gate_up),
+                             reinterpret_cast<const uint8_t *>(l.w_down_t),
+                             reinterpret_cast<const __half *>(l.in_norm), reinterpret_cast<const __half *>(l.post_norm),
+                             l.kv_pool};
+    }
+    // Barrier counters and the abort flag start at zero (a memset node under capture).
+    if (cudaMemsetAsync(s.sync, 0, (3 * size_t(s.n_layers) + 1) * 4, ctx->stream) != cudaSuccess)
+        return OPURE_ERR_CUDA;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kPThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = ctx->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;  // all CTAs co-resident, or the launch fails
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
+    if (e != cudaSuccess) return cuda_status(e);
+    *ran = true;
+    return OPURE_OK;
+}
+
 template <int NV, int HD>
 opure_status pick_g(opure_ctx *ctx, const opure_fused_step &s, uint32_t G) {
+    if constexpr (HD == 64) {
+        bool ran = false;
+        opure_status st = OPURE_OK;
+        if (s.mode == OPURE_FUSED_AUTO) {
+            switch (G) {
+                case 1: st = run_persistent<NV, HD, 1>(ctx, s, &ran); break;
+                case 2: st = run_persistent<NV, HD, 2>(ctx, s, &ran); break;
+                case 3: st = run_persistent<NV, HD, 3>(ctx, s, &ran); break;
+                case 4: st = run_persistent<NV, HD, 4>(ctx, s, &ran); break;
+            }
+            if (st || ran) return st;
+        }
+    }
     switch (G) {
         case 1: return run_step<NV, HD, 1>(ctx, s);
         case 2: return run_step<NV, HD, 2>(ctx, s);

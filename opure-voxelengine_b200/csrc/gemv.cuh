@@ -24,12 +24,12 @@ struct WTraits<OPURE_W_Q8> {
 };
 
 // Plain (non-volatile) streaming load so the compiler may hoist it ahead of the FMAs of
-// the previous chunk batch.
+// the previous chunk batch; weights are evict-first in L2.
 __device__ __forceinline__ uint4 ldg_nc(const void *p) {
     uint4 r;
-    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+    asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
         : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-        : "l"(p));
+        : "l"(p), "l"(l2_evict_first()));
     return r;
 }
 

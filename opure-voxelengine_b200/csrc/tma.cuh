@@ -21,12 +21,13 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
 }
 
 // dst and src 16-byte aligned, bytes a multiple of 16; the mbarrier's transaction count
-// is limited to 2^20 - 1 bytes per phase.
+// is limited to 2^20 - 1 bytes per phase. Used for weights, which are read once per step:
+// the copy is marked evict-first in L2.
 __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
     asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-            smem_addr(dst)),
-        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
+        "%4;" ::"r"(smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(l2_evict_first())
         : "memory");
 }
 

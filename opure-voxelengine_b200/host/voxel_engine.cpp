@@ -35,7 +35,8 @@ void VoxelEngine::Shutdown() {
                     static_cast<void *>(buf_.seqLen), static_cast<void *>(buf_.known), static_cast<void *>(buf_.flags),
                     static_cast<void *>(buf_.inTokens), static_cast<void *>(buf_.tokens),
                     static_cast<void *>(buf_.base1), static_cast<void *>(buf_.delta0),
-                    static_cast<void *>(buf_.delta1), static_cast<void *>(buf_.partial), weights_})
+                    static_cast<void *>(buf_.delta1), static_cast<void *>(buf_.partial),
+                    static_cast<void *>(buf_.sync), weights_})
         if (p) opure_free(ctx_, p);
     for (auto &s : attnScratch_) opure_free(ctx_, s.second.first);
     attnScratch_.clear();
@@ -87,7 +88,7 @@ void VoxelEngine::Initialize(const std::string &modelDir, const EngineOptions &o
     AllocBuffers();
     seqLen_ = 0;
     ready_ = true;
-    if (opts.path == 2 && !UsesFused(opts.maxBatch))
+    if ((opts.path == 2 || opts.path == 3) && !UsesFused(opts.maxBatch))
         ThrowError("the fused decode path does not support this model or batch size");
 }
 
@@ -121,6 +122,7 @@ void VoxelEngine::AllocBuffers() {
     buf_.delta0 = Alloc<long long>(ctx_, size_t(B) * c.hiddenSize);
     buf_.delta1 = Alloc<long long>(ctx_, size_t(B) * c.hiddenSize);
     if (comm_) buf_.partial = Alloc<float>(ctx_, size_t(B) * c.hiddenSize);
+    buf_.sync = Alloc<uint32_t>(ctx_, 3 * size_t(c.numLayers) + 1);
     OPURE_CUDA_CHECK(opure_fill(ctx_, buf_.keys, 0, sizeof(unsigned long long) * B));
     OPURE_CUDA_CHECK(opure_fill(ctx_, buf_.tokens, 0, sizeof(int32_t) * size_t(B) * maxLen_));
     // Pinned staging for the host-driven step: [in_tokens B][positions B][keys B (u64)].
@@ -302,6 +304,8 @@ void VoxelEngine::RecordStep(uint32_t n, bool logits) {
         fs.q = buf_.q;
         fs.logits = logits ? buf_.logits : nullptr;
         fs.keys = buf_.keys;
+        fs.sync = buf_.sync;
+        fs.mode = opts_.path == 3 ? uint32_t(OPURE_FUSED_LAYER_KERNELS) : uint32_t(OPURE_FUSED_AUTO);
         OPURE_CUDA_CHECK(opure_decode_fused(ctx_, &fs));
         OPURE_CUDA_CHECK(opure_step_end(ctx_, &io));
         return;

@@ -43,7 +43,8 @@ struct EngineOptions {
     uint64_t pageSeed = 3;          // free-list shuffle (0: pages in order)
     bool useGraphs = true;
     float attnScale = 1.0f;         // 1.0 = the reference's unscaled scores
-    uint32_t path = 0;              // 0 auto, 1 per-op kernels, 2 fused kernels required
+    uint32_t path = 0;              // 0 auto, 1 per-op kernels, 2 fused required (persistent kernel
+                                    // when eligible), 3 fused as three kernels per layer
 };
 
 struct GenerateResult {
@@ -170,6 +171,7 @@ public:
         float *base1 = nullptr;
         long long *delta0 = nullptr, *delta1 = nullptr;
         float *partial = nullptr;  // tensor parallelism: [maxBatch][hidden] shard partial sums
+        uint32_t *sync = nullptr;  // grid-barrier words of the persistent decode kernel
     };
     // True when steps of n vectors run on opure_decode_fused.
     bool UsesFused(uint32_t n) const;

@@ -18,7 +18,7 @@ class EngineOptions(C.Structure):
                 ("page_seed", u64), ("use_graphs", u32), ("attn_scale", f32), ("path", u32)]
 
 
-PATH_AUTO, PATH_UNFUSED, PATH_FUSED = 0, 1, 2
+PATH_AUTO, PATH_UNFUSED, PATH_FUSED, PATH_FUSED_LAYERS = 0, 1, 2, 3
 
 
 class EngineInfo(C.Structure):

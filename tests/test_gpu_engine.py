@@ -194,6 +194,25 @@ def test_fused_and_per_op_paths_agree(models, small):
     assert rel_err(res[ve.PATH_FUSED][1], lg) < 1e-3
 
 
+@pytest.mark.parametrize("batch", [1, 4])
+def test_persistent_and_layer_kernels_agree(models, small, batch):
+    # The single persistent kernel per step (PATH_FUSED on this shape) against the same
+    # phases as three kernels per layer: identical tokens (the residual sums are
+    # fixed-point, so both are order-independent) and logits equal to fp32 rounding.
+    prompts = [ve.prompt(90 + b, SMALL["vocab"], 13) for b in range(batch)]
+    res = {}
+    for path in (ve.PATH_FUSED, ve.PATH_FUSED_LAYERS):
+        with ve.Engine(models["small"], max_batch=batch, max_len=64, path=path) as eng:
+            res[path] = eng.generate(prompts, 24)[0]
+            lg = eng.forward_logits(prompts[0]) if batch == 1 else None
+            res[(path, "lg")] = lg
+    assert np.array_equal(res[ve.PATH_FUSED], res[ve.PATH_FUSED_LAYERS])
+    if batch == 1:
+        assert rel_err(res[(ve.PATH_FUSED, "lg")], res[(ve.PATH_FUSED_LAYERS, "lg")]) < 1e-5
+    want, margins = small.generate(prompts[0], 24)
+    assert_tokens(res[ve.PATH_FUSED][0], want, margins)
+
+
 def test_fused_head_dim_128(models):
     m = oracle.Model(models["hd128"])
     p = ve.prompt(3, HD128["vocab"], 9)
