@@ -45,8 +45,8 @@ PROMPT_LEN, DECODE_STEPS = 32, 128
 FALLBACK_PEAK = 6650.0  # GB/s, used only when MEASURED_PEAKS.json is absent
 # DRAM bytes (read + write) of one decode step, summed over its launches in an ncu capture
 # of `python bench.py --quick --no-cpu [--batch B] --steps 2 --warmup 3` (launch lists in
-# profiles/decode_bs1_fused_step.md and profiles/decode_bs64_tensor_core_step.md).
-NCU_STEP_TRAFFIC = {1: 275.0e6, 64: 483.7e6}
+# profiles/decode_bs1_persistent_step.md and profiles/decode_bs64_tensor_core_step.md).
+NCU_STEP_TRAFFIC = {1: 271.9e6, 64: 483.7e6}
 
 
 def peaks():
@@ -191,38 +191,48 @@ def run_reference(args, world, rank):
 
 
 # ---- GPU side ---------------------------------------------------------------------------
-def run_ours(args, world, rank, local):
+def phase_stats(t: np.ndarray, n_layers: int) -> dict:
+    """Per-phase timing of one persistent decode step from its per-CTA stamps (ns):
+    work = a CTA's arrival at a barrier minus its release from the previous one; release =
+    first release minus last arrival (the barrier's own latency). Medians over layers of
+    the median / max over CTAs, in microseconds."""
+    t = t.astype(np.int64)
+    start = t[:, 3 * n_layers, 1]
+    end = t[:, 3 * n_layers + 1, 0]
+    t0 = start.min()
+    arrive = t[:, :3 * n_layers, 0] - t0
+    leave = t[:, :3 * n_layers, 1] - t0
+    prev = start - t0
+    rows = []
+    for k in range(3 * n_layers):
+        work = arrive[:, k] - prev
+        rows.append((np.median(work), work.max(), leave[:, k].min() - arrive[:, k].max()))
+        prev = leave[:, k]
+    rows = np.array(rows, np.float64) / 1e3
+    out = {"kernel_us": float((end.max() - t0) / 1e3), "lm_head_us": float((end.max() - t0) / 1e3 - leave[:, -1].min() / 1e3)}
+    for ph, name in enumerate(("qkv_rope_kv", "attention_oproj", "mlp")):
+        r = rows[ph::3]
+        out[name] = {"work_median_us": float(np.median(r[:, 0])), "work_max_us": float(np.median(r[:, 1])),
+                     "barrier_release_us": float(np.median(r[:, 2]))}
+    return out
+
+
+def device_steps(eng, B: int, steps: int, warmup: int, world: int, sample_clocks: bool):
+    """Times `steps` device-resident decode steps of sequences 0..B-1 (graph replays, no host
+    round trip; positions rewound to 32 every 128 steps, so every step has config-0 context
+    lengths) after `warmup` untimed ones. Returns (device ms, max over ranks; clock record)."""
     import ctypes as C
 
     from voxelengine import cuda as cu
     from voxelengine import engine as ve
-
-    mp = model_dir() if rank == 0 else None
-    barrier(world)
-    if mp is None:
-        mp = model_dir()
-    B = args.batch
-    max_len = PROMPT_LEN + DECODE_STEPS + 8
-    path = {"auto": ve.PATH_AUTO, "layers": ve.PATH_FUSED_LAYERS, "unfused": ve.PATH_UNFUSED}[args.path]
-    eng = ve.Engine(mp, device=local, max_batch=B, max_len=max_len, page_size=64, page_seed=3, path=path)
-    info = eng.info
     L = cu.lib()
     ctx = eng.ctx
-    prompts = [ve.prompt(1 + rank * B + b, 49152, PROMPT_LEN) for b in range(B)]
-
-    # Parity gate on this rank's first sequence: the engine's 128 config-0 tokens.
-    # (--quick, for profiler launch lists, generates one token: the launches before the
-    # timed region are then (PROMPT_LEN + 1 + warmup) * launches_per_step.)
-    gen, _ = eng.generate(prompts, 1 if args.quick else DECODE_STEPS)
-    parity = {"tokens_checked": 0}
-
-    # Device-resident steps: replay the step graph; positions wrap every 128 steps.
     eng_lib = ve.lib()
     pos_rewind = np.full(B, PROMPT_LEN, np.int32)
 
     def reset_positions():
         # pos := 32 for every sequence; tokens 32.. are already in the history from the
-        # generate above, so the replayed steps redo the same config-0 work.
+        # generate before, so the replayed steps redo the same config-0 work.
         cu.check(eng_lib.opure_engine_set_positions(eng.h, pos_rewind.ctypes.data_as(C.c_void_p), B),
                  "set_positions")
 
@@ -240,23 +250,81 @@ def run_ours(args, world, rank, local):
     reset_positions()
 
     ev0, ev1 = _events(ctx)
-    run(args.warmup)
+    run(warmup)
     cu.check(L.opure_sync(ctx, 600000), "sync")
-    sampler = ClockSampler() if rank == 0 else None
+    sampler = ClockSampler() if sample_clocks else None
     barrier(world)
     if sampler:
         sampler.start()
         time.sleep(0.2)
     cu.check(L.opure_event_record(ctx, ev0), "event")
-    run(args.steps)
+    run(steps)
     cu.check(L.opure_event_record(ctx, ev1), "event")
     cu.check(L.opure_sync(ctx, 600000), "sync")
     ms = C.c_float()
     cu.check(L.opure_event_elapsed_ms(ev0, ev1, C.byref(ms)), "elapsed")
     clocks = sampler.stop() if sampler else None
     barrier(world)
-    dev_ms = allreduce_max(world, float(ms.value))
+    L.opure_event_free(ev0)
+    L.opure_event_free(ev1)
+    return allreduce_max(world, float(ms.value)), clocks
+
+
+def measure_bs64(args, world, rank, local, mp):
+    """The metric's second batch size: 64 independent config-0 sequences per GPU (prompt
+    seeds 1..64), device-resident steps, same accounting as the bs1 line."""
+    from voxelengine import engine as ve
+    B = 64
+    eng = ve.Engine(mp, device=local, max_batch=B, max_len=PROMPT_LEN + DECODE_STEPS + 8, page_size=64,
+                    page_seed=3)
+    info = eng.info
+    eng.generate([ve.prompt(1 + rank * B + b, 49152, PROMPT_LEN) for b in range(B)], DECODE_STEPS)
+    dev_ms, _ = device_steps(eng, B, args.bs64_steps, 8, world, False)
+    eng.close()
+    positions = [PROMPT_LEN + (i % DECODE_STEPS) for i in range(DECODE_STEPS)]
+    sbytes = step_bytes(info, B, positions)
+    step_ms = dev_ms / args.bs64_steps
+    achieved = sbytes / (step_ms * 1e-3) / 1e9
+    peak, _ = peaks()
+    return {"value": world * B * args.bs64_steps / (dev_ms * 1e-3), "unit": "tok/s", "steps": args.bs64_steps,
+            "warmup": 8, "ms_per_step": step_ms, "global_batch": world * B,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": NCU_STEP_TRAFFIC.get(B), "bytes_per_step": sbytes},
+            "gpu_launches": launches_per_step(info, B) * args.bs64_steps}
+
+
+def run_ours(args, world, rank, local):
+    import ctypes as C
+
+    from voxelengine import cuda as cu
+    from voxelengine import engine as ve
+
+    mp = model_dir() if rank == 0 else None
+    barrier(world)
+    if mp is None:
+        mp = model_dir()
+    B = args.batch
+    max_len = PROMPT_LEN + DECODE_STEPS + 8
+    path = {"auto": ve.PATH_AUTO, "layers": ve.PATH_FUSED_LAYERS, "unfused": ve.PATH_UNFUSED}[args.path]
+    eng = ve.Engine(mp, device=local, max_batch=B, max_len=max_len, page_size=64, page_seed=3, path=path,
+                    phase_trace=args.phase_trace)
+    info = eng.info
+    L = cu.lib()
+    ctx = eng.ctx
+    prompts = [ve.prompt(1 + rank * B + b, 49152, PROMPT_LEN) for b in range(B)]
+
+    # Parity gate on this rank's first sequence: the engine's 128 config-0 tokens.
+    # (--quick, for profiler launch lists, generates one token: the launches before the
+    # timed region are then (PROMPT_LEN + 1 + warmup) * launches_per_step.)
+    gen, _ = eng.generate(prompts, 1 if args.quick else DECODE_STEPS)
+    parity = {"tokens_checked": 0}
+
+    dev_ms, clocks = device_steps(eng, B, args.steps, args.warmup, world, rank == 0)
     cu.check(L.opure_last_error(ctx), "device status")
+    phases = None
+    if args.phase_trace:
+        tr = eng.phase_trace()
+        phases = phase_stats(tr, info.layers) if tr.size else {"unavailable": "step is not the persistent kernel"}
 
     positions = [PROMPT_LEN + (i % DECODE_STEPS) for i in range(DECODE_STEPS)]
     sbytes = step_bytes(info, B, positions)
@@ -296,7 +364,7 @@ def run_ours(args, world, rank, local):
                "sample": f"{done} config-0 decode tokens of one sequence (positions 32..159 cyclic) "
                          f"on the CPU oracle after a {PROMPT_LEN}-token prefill"}
 
-    line_launches = launches_per_step(info, B)
+    line_launches = launches_per_step(info, B, args.path)
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
@@ -308,7 +376,9 @@ def run_ours(args, world, rank, local):
                    "l2": "inputs larger than L2: every step streams 269 MB of weights (L2 126 MB)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": NCU_STEP_TRAFFIC.get(B),
-                     "kernel": "whole decode step (GEMV dominant)", "peak_kind": peak_kind,
+                     "kernel": ("the persistent decode-step kernel (one launch per step)"
+                                if line_launches == 3 else "whole decode step (GEMV dominant)"),
+                     "peak_kind": peak_kind,
                      "bytes_per_step": sbytes},
         "e2e": e2e,
         "gpu_launches": line_launches * args.steps,
@@ -319,19 +389,26 @@ def run_ours(args, world, rank, local):
     }
     if cpu:
         line["cpu_baseline"] = cpu
+    if phases:
+        line["phases"] = phases
+    eng.close()
+    if B == 1 and args.bs64_steps > 0 and not args.quick:
+        line["bs64"] = measure_bs64(args, world, rank, local, mp)
     if rank == 0:
         print(json.dumps(line), flush=True)
-    eng.close()
 
 
-def launches_per_step(info, B: int) -> int:
+def launches_per_step(info, B: int, path: str = "auto") -> int:
     """Kernel launches of one decode step: step_begin + step_end, then
-    fused path (fp16, B in 1/2/4/8): 3 per layer + lm_head;
+    fused path (fp16, B in 1/2/4/8): one persistent kernel (path auto, head_dim 64, <= 48
+    layers) or 3 per layer + lm_head (path layers);
     per-op path: per layer the q;k;v, o, gate;up and down GEMVs (+ RoPE/KV append and
     attention), each GEMV one launch per 9-vector pass on the CUDA cores (int8 q;k;v as 3
     GEMVs) or pack + tcgen05 GEMM per 256-vector pass from 16 vectors up, + the lm_head GEMV."""
     from voxelengine import cuda as cu
-    if info.w_dtype == cu.W_F16 and B in (1, 2, 4, 8):
+    if info.w_dtype == cu.W_F16 and B in (1, 2, 4, 8) and path != "unfused":
+        if path == "auto" and info.head_dim == 64 and info.layers <= 48:
+            return 3
         return 2 + 3 * info.layers + 1
     if info.w_dtype == cu.W_F16 and B >= 16:
         gemv = 2 * -(-B // 256)
@@ -702,6 +779,12 @@ def main():
     ap.add_argument("--path", choices=["auto", "layers", "unfused"], default="auto",
                     help="decode: step kernels (auto = one persistent kernel per step when eligible, "
                          "layers = three fused kernels per layer, unfused = per-op kernels)")
+    ap.add_argument("--phase-trace", action="store_true",
+                    help="decode: record the persistent step's per-CTA phase stamps and report "
+                         "per-phase times (last timed step) under \"phases\"")
+    ap.add_argument("--bs64-steps", type=int, default=256,
+                    help="decode at --batch 1: also time this many bs64 steps (the metric's second "
+                         "batch size) and report them under \"bs64\"; 0 skips")
     ap.add_argument("--seqs", type=int, default=512, help="cfg4: total sequences over all ranks")
     ap.add_argument("--wave", type=int, default=128, help="cfg4: sequences per GPU per wave")
     ap.add_argument("--quick", action="store_true",

@@ -327,6 +327,11 @@ typedef struct opure_fused_step {
     uint32_t *sync;                    /* [3 n_layers + 1] device words for the persistent
                                           kernel's grid barriers (reset by the call), or NULL */
     uint32_t mode;                     /* OPURE_FUSED_AUTO or OPURE_FUSED_LAYER_KERNELS     */
+    unsigned long long *trace;         /* NULL, or [sm_count][3 n_layers + 2][2] words: the
+                                          persistent kernel's per-CTA %globaltimer stamps
+                                          (row k < 3 n_layers: arrival at / release from grid
+                                          barrier k; row 3 n_layers: [1] = kernel start; row
+                                          3 n_layers + 1: [0] = end), rewritten every step */
 } opure_fused_step;
 /* AUTO: when the model fits (head_dim 64, <= 48 layers, each phase's work in one wave of
  * CTAs, a layer's weight slices of one CTA double-buffered in shared memory) and `sync` is

@@ -35,6 +35,7 @@ typedef struct opure_engine_options {
     uint32_t use_graphs;      /* 1: capture each step into a CUDA graph                */
     float attn_scale;         /* attention score scale (0: 1.0, the reference's)       */
     uint32_t path;            /* OPURE_PATH_*: which step kernels to record            */
+    uint32_t phase_trace;     /* 1: the persistent step records per-CTA phase stamps   */
 } opure_engine_options;
 
 enum {
@@ -125,6 +126,11 @@ opure_status opure_engine_read_tokens(opure_engine *e, uint32_t slot, uint32_t p
  * stream_bytes and kv_bytes_per_token of opure_engine_get_info are the shard's. */
 opure_status opure_engine_create_tp(const char *model_dir, opure_ctx *ctx, opure_comm *comm,
                                     const opure_engine_options *opts, opure_engine **out);
+
+/* The last persistent decode step's per-CTA %globaltimer stamps (layout of
+ * opure_fused_step.trace: [sm_count][3 layers + 2][2]); needs options.phase_trace = 1.
+ * Copies at most `cap` words; *written gets the count (0 without tracing). */
+opure_status opure_engine_phase_trace(opure_engine *e, uint64_t *out, size_t cap, size_t *written);
 
 /* ---- speculative decoding (no reference counterpart: the reference's verify shader,
  *      Opure_SpeculativeDecode.usf:60-189, is never dispatched and it has no draft loop

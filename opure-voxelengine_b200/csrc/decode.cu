@@ -657,6 +657,7 @@ struct PersistArgs {
     uint32_t F, c_ctas;         // C: F intermediate rows per CTA
     uint32_t slot_bytes, off_b, off_c;
     uint32_t lm_rows, lm_chunk, lm_nbuf;  // lm_head: rows per CTA, rows per TMA chunk, chunk buffers
+    unsigned long long *trace;  // optional [grid][3 n_layers + 2][2] %globaltimer stamps, or NULL
 };
 
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
@@ -668,6 +669,9 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
 // Grid-wide barrier k: every CTA arrives once; thread 0 waits (bounded) for all of them.
 __device__ bool grid_barrier(const PersistArgs &p, uint32_t k, int *s_ok) {
     __syncthreads();
+    // Phase trace: [k][0] = this CTA's arrival at barrier k, [k][1] = its release.
+    unsigned long long *tr = p.trace ? p.trace + (size_t(blockIdx.x) * (3 * p.n_layers + 2) + k) * 2 : nullptr;
+    if (threadIdx.x == 0 && tr) tr[0] = global_ns();
     if (threadIdx.x == 0) {
         uint32_t *ctr = p.sync + k;
         const uint32_t *abort_flag = p.sync + 3 * p.n_layers;
@@ -691,6 +695,7 @@ __device__ bool grid_barrier(const PersistArgs &p, uint32_t k, int *s_ok) {
             }
         }
         *s_ok = ok;
+        if (tr) tr[1] = global_ns();
     }
     __syncthreads();
     return *s_ok != 0;
@@ -806,6 +811,9 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
                 s >= 0 ? p.page_table[size_t(s) * p.max_pages + i % p.max_pages] : -1;
         }
     uint32_t issued = 0, waited = 0;
+    // Trace rows 3 n_layers (kernel start, in [1]) and 3 n_layers + 1 (end, in [0]).
+    unsigned long long *trow = p.trace ? p.trace + size_t(blockIdx.x) * (3 * p.n_layers + 2) * 2 : nullptr;
+    if (threadIdx.x == 0 && trow) trow[3 * p.n_layers * 2 + 1] = global_ns();
     if (threadIdx.x == 0) {
         for (uint32_t L = 0; L < 2 && L < p.n_layers; ++L) p_issue<HD, G>(p, sh, L, slots[L], &full[L]);
     }
@@ -1077,6 +1085,7 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
             for (uint32_t w = 0; w < kPWarps; ++w) bb = cta_best[w][threadIdx.x] > bb ? cta_best[w][threadIdx.x] : bb;
             if (bb) atomicMax(p.keys + threadIdx.x, bb);
         }
+        if (threadIdx.x == 0 && trow) trow[(3 * p.n_layers + 1) * 2] = global_ns();
     }
     return;
 
@@ -1217,6 +1226,7 @@ opure_status run_persistent(opure_ctx *ctx, const opure_fused_step &s, bool *ran
     p.keys = s.keys;
     p.sync = s.sync;
     p.st = ctx->status;
+    p.trace = s.trace;
     for (uint32_t L = 0; L < s.n_layers; ++L) {
         const opure_fused_layer &l = s.layers[L];
         p.layers[L] = PLayer{reinterpret_cast<const uint8_t *>(l.w_qkv), reinterpret_cast<const uint8_t *>(l.w_o_blk),

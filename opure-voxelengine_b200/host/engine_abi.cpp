@@ -64,6 +64,7 @@ opure::engine::EngineOptions ToOptions(const opure_engine_options *o) {
         opts.useGraphs = o->use_graphs != 0;
         if (o->attn_scale != 0.f) opts.attnScale = o->attn_scale;
         opts.path = o->path;
+        opts.phaseTrace = o->phase_trace != 0;
     }
     return opts;
 }
@@ -107,6 +108,11 @@ opure_status opure_engine_create_shared(const char *model_dir, opure_engine *sha
     const opure_status s = opure_get_device_info(share->eng.Ctx(), &di);
     if (s != OPURE_OK) return s;
     return Create(model_dir, di.device, share->eng.Ctx(), o, out);
+}
+
+opure_status opure_engine_phase_trace(opure_engine *e, uint64_t *out, size_t cap, size_t *written) {
+    if (!e || !out || !written) return OPURE_ERR_INVALID_ARG;
+    return Guard(e, [&] { *written = e->eng.ReadPhaseTrace(reinterpret_cast<unsigned long long *>(out), cap); });
 }
 
 opure_status opure_engine_synth_context(opure_engine *e, uint32_t n, uint32_t len, uint32_t reserve,

@@ -36,7 +36,7 @@ void VoxelEngine::Shutdown() {
                     static_cast<void *>(buf_.inTokens), static_cast<void *>(buf_.tokens),
                     static_cast<void *>(buf_.base1), static_cast<void *>(buf_.delta0),
                     static_cast<void *>(buf_.delta1), static_cast<void *>(buf_.partial),
-                    static_cast<void *>(buf_.sync), weights_})
+                    static_cast<void *>(buf_.sync), static_cast<void *>(buf_.trace), weights_})
         if (p) opure_free(ctx_, p);
     for (auto &s : attnScratch_) opure_free(ctx_, s.second.first);
     attnScratch_.clear();
@@ -123,6 +123,13 @@ void VoxelEngine::AllocBuffers() {
     buf_.delta1 = Alloc<long long>(ctx_, size_t(B) * c.hiddenSize);
     if (comm_) buf_.partial = Alloc<float>(ctx_, size_t(B) * c.hiddenSize);
     buf_.sync = Alloc<uint32_t>(ctx_, 3 * size_t(c.numLayers) + 1);
+    if (opts_.phaseTrace) {
+        opure_device_info di{};
+        OPURE_CUDA_CHECK(opure_get_device_info(ctx_, &di));
+        traceWords_ = size_t(di.sm_count) * (3 * size_t(c.numLayers) + 2) * 2;
+        buf_.trace = Alloc<unsigned long long>(ctx_, traceWords_);
+        OPURE_CUDA_CHECK(opure_fill(ctx_, buf_.trace, 0, traceWords_ * 8));
+    }
     OPURE_CUDA_CHECK(opure_fill(ctx_, buf_.keys, 0, sizeof(unsigned long long) * B));
     OPURE_CUDA_CHECK(opure_fill(ctx_, buf_.tokens, 0, sizeof(int32_t) * size_t(B) * maxLen_));
     // Pinned staging for the host-driven step: [in_tokens B][positions B][keys B (u64)].
@@ -305,6 +312,7 @@ void VoxelEngine::RecordStep(uint32_t n, bool logits) {
         fs.logits = logits ? buf_.logits : nullptr;
         fs.keys = buf_.keys;
         fs.sync = buf_.sync;
+        fs.trace = buf_.trace;
         fs.mode = opts_.path == 3 ? uint32_t(OPURE_FUSED_LAYER_KERNELS) : uint32_t(OPURE_FUSED_AUTO);
         OPURE_CUDA_CHECK(opure_decode_fused(ctx_, &fs));
         OPURE_CUDA_CHECK(opure_step_end(ctx_, &io));
@@ -722,6 +730,14 @@ void VoxelEngine::ReadHistory(uint32_t slot, uint32_t pos, uint32_t count, int32
     OPURE_CHECK(slot < opts_.maxBatch && uint64_t(pos) + count <= maxLen_, "history read out of range");
     OPURE_CUDA_CHECK(opure_d2h(ctx_, out, buf_.tokens + size_t(slot) * maxLen_ + pos, size_t(count) * 4));
     OPURE_CUDA_CHECK(opure_sync(ctx_, 60000));
+}
+
+size_t VoxelEngine::ReadPhaseTrace(unsigned long long *out, size_t cap) {
+    if (!buf_.trace) return 0;
+    const size_t n = std::min(cap, traceWords_);
+    OPURE_CUDA_CHECK(opure_d2h(ctx_, out, buf_.trace, n * 8));
+    OPURE_CUDA_CHECK(opure_sync(ctx_, 60000));
+    return n;
 }
 
 VoxelEngine::MetricsSnapshot VoxelEngine::SnapshotMetrics() const {

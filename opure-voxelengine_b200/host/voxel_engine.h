@@ -45,6 +45,7 @@ struct EngineOptions {
     float attnScale = 1.0f;         // 1.0 = the reference's unscaled scores
     uint32_t path = 0;              // 0 auto, 1 per-op kernels, 2 fused required (persistent kernel
                                     // when eligible), 3 fused as three kernels per layer
+    bool phaseTrace = false;        // persistent kernel: record per-CTA phase timestamps
 };
 
 struct GenerateResult {
@@ -124,6 +125,9 @@ public:
     void PrepareSynthetic(uint32_t n, uint32_t len, uint32_t reserve, uint64_t seed, const int32_t *first);
     // Reads `count` tokens of a slot's token history from position `pos`.
     void ReadHistory(uint32_t slot, uint32_t pos, uint32_t count, int32_t *out);
+    // Copies the last persistent step's phase timestamps (layout of opure_fused_step.trace)
+    // to `out` (cap words); returns the words written (0 without phaseTrace).
+    size_t ReadPhaseTrace(unsigned long long *out, size_t cap);
 
     struct MetricsSnapshot {
         float kvOccupancy = 0.0f;
@@ -172,6 +176,7 @@ public:
         long long *delta0 = nullptr, *delta1 = nullptr;
         float *partial = nullptr;  // tensor parallelism: [maxBatch][hidden] shard partial sums
         uint32_t *sync = nullptr;  // grid-barrier words of the persistent decode kernel
+        unsigned long long *trace = nullptr;  // its phase timestamps (EngineOptions.phaseTrace)
     };
     // True when steps of n vectors run on opure_decode_fused.
     bool UsesFused(uint32_t n) const;
@@ -204,6 +209,7 @@ private:
     bool seqIdentity_ = true; // vector v currently maps to sequence slot v
     bool ownsCtx_ = true;
     opure_comm *comm_ = nullptr;  // tensor-parallel communicator (not owned)
+    size_t traceWords_ = 0;
 };
 
 }  // namespace opure::engine

@@ -15,7 +15,8 @@ P, u32, u64, f32, i32, f64 = C.c_void_p, C.c_uint32, C.c_uint64, C.c_float, C.c_
 
 class EngineOptions(C.Structure):
     _fields_ = [("max_new_tokens", u32), ("max_batch", u32), ("max_len", u32), ("page_size", u32),
-                ("page_seed", u64), ("use_graphs", u32), ("attn_scale", f32), ("path", u32)]
+                ("page_seed", u64), ("use_graphs", u32), ("attn_scale", f32), ("path", u32),
+                ("phase_trace", u32)]
 
 
 PATH_AUTO, PATH_UNFUSED, PATH_FUSED, PATH_FUSED_LAYERS = 0, 1, 2, 3
@@ -87,6 +88,7 @@ def lib() -> C.CDLL:
             "opure_engine_poison": [P, f32],
             "opure_engine_load_kv": [P, u32, P, u32],
             "opure_engine_synth_context": [P, u32, u32, u32, u64, P],
+            "opure_engine_phase_trace": [P, P, C.c_size_t, P],
             "opure_engine_read_tokens": [P, u32, u32, u32, P],
             "opure_synth_kv": [u64, u32, u32, u32, u32, u32, P],
             "opure_model_inspect": [C.c_char_p, P, C.c_char_p, C.c_size_t],
@@ -188,12 +190,13 @@ class Engine:
     def __init__(self, model_dir: str, device: int = 0, max_batch: int = 1, max_len: int = 0,
                  page_size: int = 64, page_seed: int = 3, use_graphs: bool = True,
                  attn_scale: float = 1.0, max_new_tokens: int = 256, path: int = PATH_AUTO,
-                 share: "Engine | None" = None, comm: "cuda.Comm | None" = None):
+                 share: "Engine | None" = None, comm: "cuda.Comm | None" = None,
+                 phase_trace: bool = False):
         """With `share`, the engine runs on that engine's ctx (stream), as the draft of a
         speculative pair must; it keeps a reference so the owner outlives it. With `comm`
         it is that communicator's tensor-parallel shard, on the communicator's ctx."""
         o = EngineOptions(max_new_tokens, max_batch, max_len, page_size, page_seed,
-                          int(use_graphs), attn_scale, path)
+                          int(use_graphs), attn_scale, path, int(phase_trace))
         h = C.c_void_p()
         if comm is not None:
             st = lib().opure_engine_create_tp(model_dir.encode(), comm.ctx.h, comm.h, C.byref(o), C.byref(h))
@@ -291,6 +294,15 @@ class Engine:
 
     def poison(self, value: float):
         _check(lib().opure_engine_poison(self.h, value), "poison", self.h)
+
+    def phase_trace(self) -> np.ndarray:
+        """The last persistent step's stamps [sm_count][3 layers + 2][2] (ns), or an empty array."""
+        cap = 4096 * (3 * self.info.layers + 2) * 2
+        out = np.zeros(cap, np.uint64)
+        n = C.c_size_t()
+        _check(lib().opure_engine_phase_trace(self.h, _p(out), cap, C.byref(n)), "phase_trace", self.h)
+        rows = 3 * self.info.layers + 2
+        return out[: n.value].reshape(-1, rows, 2) if n.value else out[:0]
 
     def synth_context(self, n: int, length: int, reserve: int, seed: int, first_tokens):
         """Slots 0..n-1: `length` cached positions of seeded KV values, then self-driving
