@@ -389,6 +389,15 @@ def run_ours(args, world, rank, local):
     }
     if cpu:
         line["cpu_baseline"] = cpu
+    if B == 1 and not args.quick:
+        # Time to first token: the 32-token prompt one token per step (the reference's way)
+        # against one chunked tensor-core step; best of 3 after a graph-capturing warm-up.
+        pre = {}
+        for name, chunk in (("per_token_steps", 0), ("chunked", PROMPT_LEN)):
+            with ve.Engine(mp, device=local, max_len=max_len, prefill_chunk=chunk) as e2:
+                e2.generate([prompts[0]], 1)
+                pre[name + "_ms"] = min(e2.generate([prompts[0]], 1)[1].prefill_ms for _ in range(3))
+        line["prefill"] = {"prompt_tokens": PROMPT_LEN, **pre}
     if phases:
         line["phases"] = phases
     eng.close()

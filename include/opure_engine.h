@@ -36,6 +36,9 @@ typedef struct opure_engine_options {
     float attn_scale;         /* attention score scale (0: 1.0, the reference's)       */
     uint32_t path;            /* OPURE_PATH_*: which step kernels to record            */
     uint32_t phase_trace;     /* 1: the persistent step records per-CTA phase stamps   */
+    uint32_t prefill_chunk;   /* >0: prefill prompts as steps of up to this many token
+                                 vectors (tensor-core GEMMs, causal within the step)
+                                 instead of one token per step (0: the reference's way) */
 } opure_engine_options;
 
 enum {

@@ -65,6 +65,7 @@ opure::engine::EngineOptions ToOptions(const opure_engine_options *o) {
         if (o->attn_scale != 0.f) opts.attnScale = o->attn_scale;
         opts.path = o->path;
         opts.phaseTrace = o->phase_trace != 0;
+        opts.prefillChunk = o->prefill_chunk;
     }
     return opts;
 }

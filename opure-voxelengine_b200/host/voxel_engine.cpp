@@ -36,7 +36,8 @@ void VoxelEngine::Shutdown() {
                     static_cast<void *>(buf_.inTokens), static_cast<void *>(buf_.tokens),
                     static_cast<void *>(buf_.base1), static_cast<void *>(buf_.delta0),
                     static_cast<void *>(buf_.delta1), static_cast<void *>(buf_.partial),
-                    static_cast<void *>(buf_.sync), static_cast<void *>(buf_.trace), weights_})
+                    static_cast<void *>(buf_.sync), static_cast<void *>(buf_.trace),
+                    static_cast<void *>(buf_.prefillKeys), weights_})
         if (p) opure_free(ctx_, p);
     for (auto &s : attnScratch_) opure_free(ctx_, s.second.first);
     attnScratch_.clear();
@@ -85,6 +86,7 @@ void VoxelEngine::Initialize(const std::string &modelDir, const EngineOptions &o
     graph::ModelConfig kvCfg = cfg;
     kvCfg.numKvHeads = graph_.Local().kvHeads;  // a shard caches only its own KV heads
     kv_.Create(ctx_, kvCfg, opts.pageSize, pagesPerSeq * opts.maxBatch, opts.maxBatch, pagesPerSeq, opts.pageSeed);
+    maxVec_ = std::max(opts.maxBatch, opts.prefillChunk);
     AllocBuffers();
     seqLen_ = 0;
     ready_ = true;
@@ -103,7 +105,7 @@ bool VoxelEngine::UsesFused(uint32_t n) const {
 
 void VoxelEngine::AllocBuffers() {
     const graph::ModelConfig &c = graph_.Config();
-    const uint32_t B = opts_.maxBatch;
+    const uint32_t B = maxVec_;  // token vectors per step (sequence slots: opts_.maxBatch)
     buf_.x = Alloc<float>(ctx_, size_t(B) * c.hiddenSize);
     buf_.qkv = Alloc<float>(ctx_, size_t(B) * c.QkvRows());
     buf_.q = Alloc<float>(ctx_, size_t(B) * c.numHeads * c.HeadDim());
@@ -117,7 +119,8 @@ void VoxelEngine::AllocBuffers() {
     buf_.known = Alloc<int32_t>(ctx_, B);
     buf_.flags = Alloc<uint32_t>(ctx_, B);
     buf_.inTokens = Alloc<int32_t>(ctx_, B);
-    buf_.tokens = Alloc<int32_t>(ctx_, size_t(B) * maxLen_);
+    buf_.tokens = Alloc<int32_t>(ctx_, size_t(opts_.maxBatch) * maxLen_);
+    buf_.prefillKeys = Alloc<unsigned long long>(ctx_, opts_.maxBatch);
     buf_.base1 = Alloc<float>(ctx_, size_t(B) * c.hiddenSize);
     buf_.delta0 = Alloc<long long>(ctx_, size_t(B) * c.hiddenSize);
     buf_.delta1 = Alloc<long long>(ctx_, size_t(B) * c.hiddenSize);
@@ -131,7 +134,7 @@ void VoxelEngine::AllocBuffers() {
         OPURE_CUDA_CHECK(opure_fill(ctx_, buf_.trace, 0, traceWords_ * 8));
     }
     OPURE_CUDA_CHECK(opure_fill(ctx_, buf_.keys, 0, sizeof(unsigned long long) * B));
-    OPURE_CUDA_CHECK(opure_fill(ctx_, buf_.tokens, 0, sizeof(int32_t) * size_t(B) * maxLen_));
+    OPURE_CUDA_CHECK(opure_fill(ctx_, buf_.tokens, 0, sizeof(int32_t) * size_t(opts_.maxBatch) * maxLen_));
     // Pinned staging for the host-driven step: [in_tokens B][positions B][keys B (u64)].
     OPURE_CUDA_CHECK(opure_alloc_host(ctx_, size_t(B) * 16, &hostIo_));
     OPURE_CUDA_CHECK(opure_sync(ctx_, 60000));
@@ -350,7 +353,7 @@ void VoxelEngine::RecordStep(uint32_t n, bool logits) {
 
 void VoxelEngine::RunSteps(uint32_t n, uint32_t steps, bool logits) {
     OPURE_CHECK(ready_, "engine used before Initialize");
-    OPURE_CHECK(n >= 1 && n <= opts_.maxBatch, "batch exceeds maxBatch");
+    OPURE_CHECK(n >= 1 && n <= maxVec_, "more token vectors than the engine's step capacity");
     if (!opts_.useGraphs) {
         for (uint32_t s = 0; s < steps; ++s) RecordStep(n, logits);
         return;
@@ -434,6 +437,41 @@ void VoxelEngine::ResetSequences(const std::vector<std::vector<uint32_t>> &promp
     OPURE_CUDA_CHECK(opure_sync(ctx_, 60000));
 }
 
+uint32_t VoxelEngine::PrefillChunks(const std::vector<std::vector<uint32_t>> &prompts) {
+    // Every prompt position of every sequence becomes one token vector; chunks of up to
+    // prefillChunk vectors run as single steps (each vector's attention covers exactly the
+    // KV rows before it, including the ones appended by the same step), so a chunk's
+    // projections run as tensor-core GEMMs over all its tokens at once.
+    const uint32_t n = uint32_t(prompts.size()), C = opts_.prefillChunk;
+    std::vector<int32_t> seq, pos, tok;
+    std::vector<int32_t> known(n), start(n);
+    for (uint32_t s = 0; s < n; ++s) {
+        for (uint32_t t = 0; t < prompts[s].size(); ++t) {
+            seq.push_back(int32_t(s));
+            pos.push_back(int32_t(t));
+            tok.push_back(int32_t(prompts[s][t]));
+        }
+        known[s] = start[s] = int32_t(prompts[s].size());
+    }
+    uint32_t steps = 0;
+    for (size_t i0 = 0; i0 < seq.size(); i0 += C) {
+        const uint32_t m = uint32_t(std::min<size_t>(C, seq.size() - i0));
+        SetVectors(seq.data() + i0, pos.data() + i0, tok.data() + i0, m);
+        RunSteps(m, 1, false);
+        ++steps;
+        // The argmax after each sequence's last prompt token: its first generated token.
+        for (uint32_t j = 0; j < m; ++j) {
+            const uint32_t s = uint32_t(seq[i0 + j]);
+            if (pos[i0 + j] + 1 == known[s])
+                OPURE_CUDA_CHECK(opure_d2d(ctx_, buf_.prefillKeys + s, buf_.keys + j, 8));
+        }
+    }
+    // Continue self-driving: vector s at position len_s takes the saved key as its input.
+    OPURE_CUDA_CHECK(opure_d2d(ctx_, buf_.keys, buf_.prefillKeys, size_t(n) * 8));
+    SetAutoVectors(start.data(), known.data(), n);
+    return steps;
+}
+
 std::vector<GenerateResult> VoxelEngine::GenerateBatch(const std::vector<std::vector<uint32_t>> &prompts,
                                                        uint32_t budget, StepTiming *timing) {
     OPURE_CHECK(ready_, "engine used before Initialize");
@@ -442,14 +480,19 @@ std::vector<GenerateResult> VoxelEngine::GenerateBatch(const std::vector<std::ve
     for (const auto &p : prompts) maxP = std::max<uint32_t>(maxP, uint32_t(p.size()));
     // The reference stops when seqLen + 1 >= maxPos (Opure_VoxelEngine.cpp:932).
     OPURE_CHECK(maxP + budget < maxLen_, "prompt + budget exceeds the engine's maxLen");
-    ResetSequences(prompts, maxP + budget, true);
+    const bool chunked = opts_.prefillChunk > 0;
+    ResetSequences(prompts, maxP + budget, !chunked);
 
     opure_event *e0 = nullptr, *e1 = nullptr, *e2 = nullptr;
     OPURE_CUDA_CHECK(opure_event_create(ctx_, &e0));
     OPURE_CUDA_CHECK(opure_event_create(ctx_, &e1));
     OPURE_CUDA_CHECK(opure_event_create(ctx_, &e2));
     OPURE_CUDA_CHECK(opure_event_record(ctx_, e0));
-    RunSteps(n, maxP, false);
+    uint32_t prefillSteps = maxP;
+    if (chunked)
+        prefillSteps = PrefillChunks(prompts);
+    else
+        RunSteps(n, maxP, false);
     OPURE_CUDA_CHECK(opure_event_record(ctx_, e1));
     RunSteps(n, budget, false);
     OPURE_CUDA_CHECK(opure_event_record(ctx_, e2));
@@ -476,7 +519,7 @@ std::vector<GenerateResult> VoxelEngine::GenerateBatch(const std::vector<std::ve
     if (timing) {
         timing->prefillMs = pre;
         timing->decodeMs = dec;
-        timing->prefillSteps = maxP;
+        timing->prefillSteps = prefillSteps;
         timing->decodeSteps = budget;
     }
     seqLen_ = maxP + budget;
@@ -502,7 +545,7 @@ std::vector<uint32_t> VoxelEngine::PrefillBatch(const std::vector<std::vector<ui
 }
 
 void VoxelEngine::SetVectors(const int32_t *seq, const int32_t *pos, const int32_t *tok, uint32_t n) {
-    OPURE_CHECK(n >= 1 && n <= opts_.maxBatch, "more token vectors than maxBatch");
+    OPURE_CHECK(n >= 1 && n <= maxVec_, "more token vectors than the engine's step capacity");
     const uint32_t V = graph_.Config().vocabSize;
     for (uint32_t v = 0; v < n; ++v) {
         OPURE_CHECK(seq[v] >= 0 && uint32_t(seq[v]) < opts_.maxBatch, "sequence slot out of range");
@@ -517,7 +560,7 @@ void VoxelEngine::SetVectors(const int32_t *seq, const int32_t *pos, const int32
     if (tok) OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.inTokens, tok, n * 4));
     seqIdentity_ = false;
     if (!hostDriven_) {
-        const std::vector<uint32_t> zero(opts_.maxBatch, 0u);
+        const std::vector<uint32_t> zero(maxVec_, 0u);
         OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.flags, zero.data(), zero.size() * 4));
         hostDriven_ = true;
     }
@@ -562,8 +605,12 @@ GenerateResult VoxelEngine::Generate(const std::vector<uint32_t> &tokens, const 
 
 uint32_t VoxelEngine::Prefill(const std::vector<uint32_t> &tokens) {
     OPURE_CHECK(!tokens.empty(), "Prefill called with no tokens");
-    ResetSequences({tokens}, uint32_t(tokens.size()), true);
-    RunSteps(1, uint32_t(tokens.size()), false);
+    const bool chunked = opts_.prefillChunk > 0;
+    ResetSequences({tokens}, uint32_t(tokens.size()), !chunked);
+    if (chunked)
+        PrefillChunks({tokens});
+    else
+        RunSteps(1, uint32_t(tokens.size()), false);
     Sync();
     unsigned long long key = 0;
     OPURE_CUDA_CHECK(opure_d2h(ctx_, &key, buf_.keys, 8));
@@ -659,7 +706,7 @@ void VoxelEngine::RunLayersTraced(uint32_t tokenId, uint32_t nLayers, std::vecto
 
 void VoxelEngine::PoisonBanks(float fill) {
     const graph::ModelConfig &c = graph_.Config();
-    const uint32_t B = opts_.maxBatch;
+    const uint32_t B = maxVec_;
     auto poison = [&](float *p, size_t n) {
         std::vector<float> pat(n, fill);
         OPURE_CUDA_CHECK(opure_h2d(ctx_, p, pat.data(), n * 4));

@@ -46,6 +46,8 @@ struct EngineOptions {
     uint32_t path = 0;              // 0 auto, 1 per-op kernels, 2 fused required (persistent kernel
                                     // when eligible), 3 fused as three kernels per layer
     bool phaseTrace = false;        // persistent kernel: record per-CTA phase timestamps
+    uint32_t prefillChunk = 0;      // >0: prompts prefilled as steps of up to this many token
+                                    // vectors (tensor-core GEMMs) instead of one token per step
 };
 
 struct GenerateResult {
@@ -177,6 +179,7 @@ public:
         float *partial = nullptr;  // tensor parallelism: [maxBatch][hidden] shard partial sums
         uint32_t *sync = nullptr;  // grid-barrier words of the persistent decode kernel
         unsigned long long *trace = nullptr;  // its phase timestamps (EngineOptions.phaseTrace)
+        unsigned long long *prefillKeys = nullptr;  // [maxBatch] chunked prefill's last-token keys
     };
     // True when steps of n vectors run on opure_decode_fused.
     bool UsesFused(uint32_t n) const;
@@ -190,6 +193,9 @@ private:
     // split counters always start at zero).
     void *AttnScratch(uint32_t n, size_t *bytes);
     void ResetSequences(const std::vector<std::vector<uint32_t>> &prompts, uint32_t reserve, bool automatic);
+    // Chunked prefill of slots 0..n-1 after ResetSequences(..., false); leaves them
+    // self-driving at their prompt lengths. Returns the number of steps it ran.
+    uint32_t PrefillChunks(const std::vector<std::vector<uint32_t>> &prompts);
     opure_step_io StepIO(uint32_t n) const;
 
     opure_ctx *ctx_ = nullptr;
@@ -210,6 +216,7 @@ private:
     bool ownsCtx_ = true;
     opure_comm *comm_ = nullptr;  // tensor-parallel communicator (not owned)
     size_t traceWords_ = 0;
+    uint32_t maxVec_ = 1;  // token vectors per step: max(maxBatch, prefillChunk)
 };
 
 }  // namespace opure::engine

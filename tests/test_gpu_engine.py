@@ -164,9 +164,13 @@ def test_config0_smollm_full_size(tmp_path_factory):
     p = ve.prompt(1, 49152, 32)
     with ve.Engine(d, max_len=256) as eng:
         out, t = eng.generate([p], 128)
+    with ve.Engine(d, max_len=256, prefill_chunk=32) as eng:
+        out_c, tc = eng.generate([p], 128)   # the 32-token prompt as one tensor-core step
     want, margins = oracle.Model(d).generate(p, 128)
-    print(f"cfg0: decode {t.decode_ms / 128 * 1e3:.1f} us/token, min oracle margin {margins.min():.3e}")
+    print(f"cfg0: decode {t.decode_ms / 128 * 1e3:.1f} us/token, prefill {t.prefill_ms:.2f} ms per-token "
+          f"vs {tc.prefill_ms:.2f} ms chunked, min oracle margin {margins.min():.3e}")
     assert_tokens(out[0], want, margins)
+    assert_tokens(out_c[0], want, margins)
 
 
 # ---- the fused latency path (opure_decode_fused) ------------------------------------
@@ -260,3 +264,31 @@ def test_synthetic_long_context_matches_oracle(models, small, n, length):
             top = np.sort(lg)[-2:]
             margins.append(float(top[1] - top[0]))
         assert_tokens(got[v], want, margins)
+
+
+@pytest.mark.parametrize("chunk", [16, 64])
+def test_chunked_prefill_matches_oracle(models, small, chunk):
+    # Prompts of different lengths prefilled as steps of up to `chunk` token vectors
+    # (several sequences per step, causal attention inside the step, tensor-core GEMMs
+    # from 16 vectors), then self-driving decode: the oracle's tokens for every sequence.
+    lens = (40, 17, 33)
+    prompts = [ve.prompt(60 + i, SMALL["vocab"], n) for i, n in enumerate(lens)]
+    with ve.Engine(models["small"], max_batch=3, max_len=96, prefill_chunk=chunk) as eng:
+        got, t = eng.generate(prompts, 12)
+    assert t.prefill_steps == -(-sum(lens) // chunk)
+    for i, p in enumerate(prompts):
+        want, margins = small.generate(p, 12)
+        assert_tokens(got[i], want, margins)
+
+
+def test_chunked_prefill_then_host_steps(models, small):
+    # Prefill (chunked) followed by the reference's host-driven DecodeStep loop.
+    p = ve.prompt(71, SMALL["vocab"], 21)
+    want, margins = small.generate(p, 6)
+    with ve.Engine(models["small"], max_len=64, prefill_chunk=16) as eng:
+        tok = eng.prefill(p)
+        got = [tok]
+        for i in range(5):
+            tok = int(eng.decode_step([tok], [len(p) + i])[0])
+            got.append(tok)
+    assert_tokens(got, want, margins)
