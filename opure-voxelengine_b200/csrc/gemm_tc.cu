@@ -199,13 +199,14 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(PackParams p) {
 // ---- GEMM ---------------------------------------------------------------------------
 struct TcParams {
     uint32_t rows, n, npad, ktiles, kt_per_split, splits, stages;
+    uint32_t nt;        // vectors per CTA (blockIdx.z selects vectors [z nt, z nt + nt))
     float *y;
     uint32_t y_stride;
     const float *residual;
     unsigned long long *keys;
     const float *xscale;
-    long long *accum;   // [tiles][accumulators * npad][128] fixed-point split-K sums
-    uint32_t *tickets;  // [tiles]
+    long long *accum;   // [tiles][npad / nt][accumulators * nt][128] fixed-point split-K sums
+    uint32_t *tickets;  // [tiles][npad / nt]
     DeviceStatus *st;
 };
 
@@ -224,15 +225,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t tile = blockIdx.x, split = blockIdx.y;
     const uint32_t m0 = tile * kTileM;
+    const uint32_t nt = p.nt, n0 = blockIdx.z * nt;        // this CTA's vectors
+    const uint32_t slice = tile * gridDim.z + blockIdx.z;  // (tile, vector slice) index
     const uint32_t kt0 = split * p.kt_per_split;
     const uint32_t nk = min(p.ktiles, kt0 + p.kt_per_split) - kt0;
-    const uint32_t a_bytes = kTileM * 128, b_bytes = p.npad * 128;
+    const uint32_t a_bytes = kTileM * 128, b_bytes = nt * 128;
     const uint32_t stage_bytes = kAcc * a_bytes + 2 * b_bytes;
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dsm) + 1023) & ~uintptr_t(1023));
     auto a_tile = [&](uint32_t s, uint32_t j) { return base + size_t(s) * stage_bytes + j * a_bytes; };
     auto b_tile = [&](uint32_t s, uint32_t j) { return base + size_t(s) * stage_bytes + kAcc * a_bytes + j * b_bytes; };
     uint32_t ncols = 32;
-    while (ncols < kAcc * p.npad) ncols <<= 1;
+    while (ncols < kAcc * nt) ncols <<= 1;
 
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < p.stages; ++s) {
@@ -270,8 +273,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0) {
         if (lane == 0) {
             for (uint32_t i = 0; i < pre; ++i) {
-                tma_load_2d(b_tile(i, 0), &xmap, (kt0 + i) * kTileK, 0, &full[i]);
-                tma_load_2d(b_tile(i, 1), &xmap, (kt0 + i) * kTileK, p.npad, &full[i]);
+                tma_load_2d(b_tile(i, 0), &xmap, (kt0 + i) * kTileK, n0, &full[i]);
+                tma_load_2d(b_tile(i, 1), &xmap, (kt0 + i) * kTileK, p.npad + n0, &full[i]);
             }
             uint32_t i = pre;
             for (; i < nk; ++i) {
@@ -284,8 +287,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_expect_tx(&full[s], stage_bytes);
                 tma_load_2d(a_tile(s, 0), &wmap, (kt0 + i) * kTileK, m0, &full[s]);
                 if (kSwiglu) tma_load_2d(a_tile(s, 1), &wmap, (kt0 + i) * kTileK, p.rows + m0, &full[s]);
-                tma_load_2d(b_tile(s, 0), &xmap, (kt0 + i) * kTileK, 0, &full[s]);
-                tma_load_2d(b_tile(s, 1), &xmap, (kt0 + i) * kTileK, p.npad, &full[s]);
+                tma_load_2d(b_tile(s, 0), &xmap, (kt0 + i) * kTileK, n0, &full[s]);
+                tma_load_2d(b_tile(s, 1), &xmap, (kt0 + i) * kTileK, p.npad + n0, &full[s]);
             }
             issued_s = i;
         }
@@ -295,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             // MMA issuer: per 64-wide K tile, four K=16 steps (32 bytes along the swizzled
             // rows) of hi and lo products.
-            const uint32_t idesc = (1u << 4) | ((p.npad >> 3) << 17) | ((kTileM >> 4) << 24);
+            const uint32_t idesc = (1u << 4) | ((nt >> 3) << 17) | ((kTileM >> 4) << 24);
             uint32_t i = 0;
             for (; i < nk; ++i) {
                 const uint32_t s = i % p.stages;
@@ -315,8 +318,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mma_f16(tmem, da, dl, idesc, 1);
                     if (kSwiglu) {
                         const uint64_t du = smem_desc(smem_addr(a_tile(s, 1)) + 32 * k);
-                        mma_f16(tmem + p.npad, du, dh, idesc, (i | k) != 0);
-                        mma_f16(tmem + p.npad, du, dl, idesc, 1);
+                        mma_f16(tmem + nt, du, dh, idesc, (i | k) != 0);
+                        mma_f16(tmem + nt, du, dl, idesc, 1);
                     }
                 }
                 mma_commit(&empty[s]);
@@ -340,14 +343,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t lrow = warp * 32 + lane;
         const uint32_t row = m0 + lrow;
         const uint32_t taddr = tmem + ((warp * 32) << 16);
-        const uint32_t acc_cols = kAcc * p.npad;
+        const uint32_t acc_cols = kAcc * nt;
         bool run_epi = true;
         long long *acc64 = nullptr;
         if (p.splits > 1) {
             // K split: add this split's sums into the tile's 64-bit fixed-point (2^-32)
             // accumulator; integer adds are associative, so the total does not depend on
             // the order the splits arrive in. Column-major: a warp's adds are contiguous.
-            acc64 = p.accum + size_t(tile) * acc_cols * kTileM;
+            acc64 = p.accum + size_t(slice) * acc_cols * kTileM;
             for (uint32_t c0 = 0; c0 < acc_cols; c0 += 16) {
                 float r[16];
                 tmem_ld16(taddr + c0, r);
@@ -359,9 +362,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             __threadfence();
             __syncthreads();
             if (threadIdx.x == 0) {
-                const uint32_t t = atomicAdd(&p.tickets[tile], 1u);
+                const uint32_t t = atomicAdd(&p.tickets[slice], 1u);
                 last = t == p.splits - 1;
-                if (last) p.tickets[tile] = 0;  // ready for the next call
+                if (last) p.tickets[slice] = 0;  // ready for the next call
             }
             __syncthreads();
             run_epi = last;
@@ -388,19 +391,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             // and the vector scales come from shared memory, so a thread pays one memory
             // round trip per chunk rather than one per column.
             const bool in = row < p.rows;
-            for (uint32_t c0 = 0; c0 < p.npad; c0 += 16) {
+            for (uint32_t c0 = 0; c0 < nt; c0 += 16) {
                 float g[16], u[16], res[16];
                 column(c0, g);
-                if (kSwiglu) column(p.npad + c0, u);
+                if (kSwiglu) column(nt + c0, u);
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     res[j] = 0.f;
                     if constexpr (EPI == OPURE_EPI_ADD)
-                        if (in && c0 + j < p.n) res[j] = p.residual[size_t(c0 + j) * p.y_stride + row];
+                        if (in && n0 + c0 + j < p.n) res[j] = p.residual[size_t(n0 + c0 + j) * p.y_stride + row];
                 }
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
-                    const uint32_t v = c0 + j;
+                    const uint32_t v = n0 + c0 + j;
                     const bool ok = in && v < p.n;
                     const float val = g[j] * s_scale[v];
                     const size_t o = size_t(v) * p.y_stride + row;
@@ -460,7 +463,7 @@ opure_status launch_gemm(opure_ctx *ctx, const CUtensorMap &wm, const CUtensorMa
     const cudaError_t e =
         cudaFuncSetAttribute(gemm_tc_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return cuda_status(e);
-    return launch(ctx, gemm_tc_kernel<EPI>, dim3(tiles, p.splits), dim3(kThreads), smem, true, wm, xm, p);
+    return launch(ctx, gemm_tc_kernel<EPI>, dim3(tiles, p.splits, p.npad / p.nt), dim3(kThreads), smem, true, wm, xm, p);
 }
 
 }  // namespace
@@ -498,18 +501,24 @@ opure_status gemv_tc(opure_ctx *ctx, const opure_gemv_args *a) {
                       reinterpret_cast<const __half *>(a->norm_gain), a->eps, xp, xscale};
         opure_status s = launch(ctx, pack_kernel, dim3(n), dim3(kPackThreads), pack_smem, true, pp);
         if (s) return s;
-        CUtensorMap xm;
-        if (!make_map(&xm, xp, K, 2 * npad, npad)) return OPURE_ERR_UNSUPPORTED;
-
-        // K split: about one CTA per SM, partial sums must fit the workspace.
+        // Work split, latency first. Vector slices (blockIdx.z) need no reduction: as many
+        // as fit one wave. A K split adds a fixed-point atomic reduction and a ticket, so it
+        // is used only for long K (more than 12 tiles of 64), about one CTA per SM at most.
+        const uint32_t sms = uint32_t(ctx->sm_count);
+        uint32_t nz = 1;
+        for (uint32_t c = 1; c <= npad / 16; ++c)
+            if ((npad / 16) % c == 0 && tiles * c <= sms) nz = c;
+        const uint32_t nt = npad / nz;
         uint32_t splits = 1;
-        if (tiles < uint32_t(ctx->sm_count) && tiles <= kMaxTickets)
-            splits = std::max<uint32_t>(1, std::min<uint32_t>(ktiles, uint32_t(ctx->sm_count) / tiles));
-        if (size_t(tiles) * acc * npad * kTileM > accum_cap) splits = 1;
+        if (ktiles > 12 && tiles * nz < sms && size_t(tiles) * nz <= kMaxTickets &&
+            size_t(tiles) * acc * npad * kTileM <= accum_cap)
+            splits = std::max<uint32_t>(1, std::min<uint32_t>(ceil_div(ktiles, 12), sms / (tiles * nz)));
         const uint32_t kt_per = ceil_div(ktiles, splits);
         splits = ceil_div(ktiles, kt_per);
+        CUtensorMap xm;
+        if (!make_map(&xm, xp, K, 2 * npad, nt)) return OPURE_ERR_UNSUPPORTED;
 
-        const uint32_t stage_bytes = acc * kTileM * 128 + 2 * npad * 128;
+        const uint32_t stage_bytes = acc * kTileM * 128 + 2 * nt * 128;
         const size_t budget = std::min<size_t>(ctx->smem_optin, 227 * 1024) - 1024 - 256;
         const uint32_t stages = std::min<uint32_t>({kMaxStages, uint32_t(budget / stage_bytes), kt_per});
         if (stages < 1 || (stages < 2 && kt_per > 1)) return OPURE_ERR_UNSUPPORTED;
@@ -518,6 +527,7 @@ opure_status gemv_tc(opure_ctx *ctx, const opure_gemv_args *a) {
         p.rows = rows;
         p.n = n;
         p.npad = npad;
+        p.nt = nt;
         p.ktiles = ktiles;
         p.kt_per_split = kt_per;
         p.splits = splits;
@@ -533,7 +543,7 @@ opure_status gemv_tc(opure_ctx *ctx, const opure_gemv_args *a) {
         // Request enough shared memory that no more CTAs fit on an SM than its 512 TMEM
         // columns can serve, so tcgen05.alloc never waits on a co-resident CTA.
         uint32_t ncols = 32;
-        while (ncols < acc * npad) ncols <<= 1;
+        while (ncols < acc * nt) ncols <<= 1;
         const size_t per_sm = ctx->smem_optin + 1024;
         const size_t smem = std::max<size_t>(size_t(stages) * stage_bytes + 1024, per_sm / (512 / ncols + 1) + 1);
         if (smem > ctx->smem_optin) return OPURE_ERR_UNSUPPORTED;
