@@ -519,7 +519,11 @@ opure_status gemv_tc(opure_ctx *ctx, const opure_gemv_args *a) {
         if (!make_map(&xm, xp, K, 2 * npad, nt)) return OPURE_ERR_UNSUPPORTED;
 
         const uint32_t stage_bytes = acc * kTileM * 128 + 2 * nt * 128;
-        const size_t budget = std::min<size_t>(ctx->smem_optin, 227 * 1024) - 1024 - 256;
+        // Dynamic shared memory left after the kernel's static arrays and the 1 KB used to
+        // align the stages.
+        cudaFuncAttributes fa{};
+        if (cudaFuncGetAttributes(&fa, gemm_tc_kernel<OPURE_EPI_SWIGLU>) != cudaSuccess) return OPURE_ERR_CUDA;
+        const size_t budget = std::min<size_t>(ctx->smem_optin, 227 * 1024) - fa.sharedSizeBytes - 1024 - 256;
         const uint32_t stages = std::min<uint32_t>({kMaxStages, uint32_t(budget / stage_bytes), kt_per});
         if (stages < 1 || (stages < 2 && kt_per > 1)) return OPURE_ERR_UNSUPPORTED;
 
@@ -546,7 +550,7 @@ opure_status gemv_tc(opure_ctx *ctx, const opure_gemv_args *a) {
         while (ncols < acc * nt) ncols <<= 1;
         const size_t per_sm = ctx->smem_optin + 1024;
         const size_t smem = std::max<size_t>(size_t(stages) * stage_bytes + 1024, per_sm / (512 / ncols + 1) + 1);
-        if (smem > ctx->smem_optin) return OPURE_ERR_UNSUPPORTED;
+        if (smem + fa.sharedSizeBytes > ctx->smem_optin) return OPURE_ERR_UNSUPPORTED;
         switch (epi) {
             case OPURE_EPI_STORE: s = launch_gemm<OPURE_EPI_STORE>(ctx, wm, xm, p, tiles, smem); break;
             case OPURE_EPI_ADD: s = launch_gemm<OPURE_EPI_ADD>(ctx, wm, xm, p, tiles, smem); break;
