@@ -159,9 +159,12 @@ uint32_t choose_split(uint32_t entries, uint32_t n_kv, uint32_t hd, uint32_t max
                       uint32_t requested, int sm_count) {
     const uint32_t unit = cta_tokens(hd);
     if (requested) return ((requested + unit - 1) / unit) * unit;
+    // About four CTAs per SM, but no split shorter than 128 tokens: a short context is one
+    // CTA's work, and each split adds a combine.
     const uint64_t pairs = uint64_t(entries) * n_kv;
     const uint64_t target = uint64_t(sm_count > 0 ? sm_count : 148) * 4;
-    const uint64_t want_splits = std::max<uint64_t>(1, (target + pairs - 1) / pairs);
+    const uint64_t want_splits = std::max<uint64_t>(
+        1, std::min<uint64_t>((target + pairs - 1) / pairs, std::max<uint64_t>(1, max_ctx / 128)));
     const uint64_t per = (uint64_t(std::max(max_ctx, 1u)) + want_splits - 1) / want_splits;
     return uint32_t(std::max<uint64_t>(unit, ((per + unit - 1) / unit) * unit));
 }
