@@ -74,9 +74,12 @@ __device__ __forceinline__ void load_q_slice(const float *q_heads /* [n_heads][H
 }
 
 // Accumulates keys [t_begin, t_end) into the lane state. The calling warp processes
-// blocks base = t_begin + warp_idx*TB, advancing by warp_count*TB. COHERENT reads K/V
-// through L2 (for caches written earlier in the same kernel).
-template <int HD, int G, bool COHERENT = false>
+// blocks base = t_begin + warp_idx*TB, advancing by warp_count*TB; STRIDED instead
+// interleaves the warps round by round (round r of warp w covers tokens base +
+// (r*warp_count + w)*TPW ..), so a context shorter than warp_count*TB still spreads over
+// every warp. Rounds past t_end are skipped (warp-uniform). COHERENT reads K/V through
+// L2 (for caches written earlier in the same kernel).
+template <int HD, int G, bool COHERENT = false, bool STRIDED = false>
 __device__ __forceinline__ void attend_range(AttnState<HD, G> &st, const float (&qv)[G][AttnShape<HD>::E],
                                              const KvView &kv, uint32_t t_begin, uint32_t t_end,
                                              uint32_t warp_idx, uint32_t warp_count,
@@ -87,12 +90,14 @@ __device__ __forceinline__ void attend_range(AttnState<HD, G> &st, const float (
     const uint32_t grp = lane / LPT, sub = lane % LPT;
     const size_t blk = size_t(kv.page_size) * HD;  // elements per page block
 
-    for (uint32_t base = t_begin + warp_idx * S::TB; base < t_end; base += warp_count * S::TB) {
+    for (uint32_t base = t_begin + (STRIDED ? 0u : warp_idx * S::TB); base < t_end; base += warp_count * S::TB) {
         uint4 kr[R][CH], vr[R][CH];
-        bool valid[R];
+        bool valid[R], live[R];
 #pragma unroll
         for (int r = 0; r < R; ++r) {
-            const uint32_t t = base + r * TPW + grp;
+            const uint32_t t0 = STRIDED ? base + (r * warp_count + warp_idx) * TPW : base + r * TPW;
+            live[r] = t0 < t_end;  // the same for every lane of the warp
+            const uint32_t t = t0 + grp;
             valid[r] = t < t_end && kv.ok;
             const __half *kp = nullptr;
             if (valid[r]) {
@@ -120,6 +125,11 @@ __device__ __forceinline__ void attend_range(AttnState<HD, G> &st, const float (
         float s[R][G];
 #pragma unroll
         for (int r = 0; r < R; ++r) {
+            if (!live[r]) {
+#pragma unroll
+                for (int h = 0; h < G; ++h) s[r][h] = -INFINITY;
+                continue;
+            }
             float kf[E];
 #pragma unroll
             for (int c = 0; c < CH; ++c) unpack8(kr[r][c], kf + 8 * c);
@@ -148,6 +158,7 @@ __device__ __forceinline__ void attend_range(AttnState<HD, G> &st, const float (
         }
 #pragma unroll
         for (int r = 0; r < R; ++r) {
+            if (!live[r]) continue;
             float vf[E];
 #pragma unroll
             for (int c = 0; c < CH; ++c) unpack8(vr[r][c], vf + 8 * c);

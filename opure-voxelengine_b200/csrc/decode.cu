@@ -249,6 +249,43 @@ __device__ __forceinline__ void smem_dot(const uint8_t *w, uint32_t pitch, uint3
         for (int v = 0; v < NV; ++v) acc[r][v] = warp_sum(acc[r][v]);
 }
 
+// smem_dot over R rows at arbitrary shared-memory addresses rows[r], r < nrows.
+template <int NV, int R>
+__device__ __forceinline__ void smem_dot_ptrs(const uint8_t *const (&rows)[R], uint32_t nrows, uint32_t nchunks,
+                                              const float *xs, uint32_t h, float (&acc)[R][NV]) {
+    const uint32_t lane = threadIdx.x & 31u;
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int v = 0; v < NV; ++v) acc[r][v] = 0.f;
+    for (uint32_t c = lane; c < nchunks; c += 32) {
+        float xf[NV][8];
+#pragma unroll
+        for (int v = 0; v < NV; ++v) {
+            const float4 a = *reinterpret_cast<const float4 *>(xs + v * h + c * 8);
+            const float4 b = *reinterpret_cast<const float4 *>(xs + v * h + c * 8 + 4);
+            xf[v][0] = a.x; xf[v][1] = a.y; xf[v][2] = a.z; xf[v][3] = a.w;
+            xf[v][4] = b.x; xf[v][5] = b.y; xf[v][6] = b.z; xf[v][7] = b.w;
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            if (r >= int(nrows)) break;
+            float wf[8];
+            unpack8(*reinterpret_cast<const uint4 *>(rows[r] + c * 16), wf);
+#pragma unroll
+            for (int v = 0; v < NV; ++v)
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc[r][v] = fmaf(wf[e], xf[v][e], acc[r][v]);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        if (r >= int(nrows)) break;
+#pragma unroll
+        for (int v = 0; v < NV; ++v) acc[r][v] = warp_sum(acc[r][v]);
+    }
+}
+
 // Element offset of (seq, pos, K|V, kv head) row inside a layer's pool, or -1 (reported).
 __device__ __forceinline__ long long kv_offset(const KvParams &kv, uint32_t n_kv, uint32_t hd, int32_t seq,
                                                int32_t pos, uint32_t sel, uint32_t head, DeviceStatus *st) {
@@ -435,7 +472,7 @@ __global__ void __launch_bounds__(kBThreads) attn_oproj_kernel(AttnOArgs a) {
         KvView kv{reinterpret_cast<const __half *>(a.kv.pool),
                   stage_pt ? s_pt[v] : a.kv.page_table + size_t(max(s, 0)) * a.kv.max_pages,
                   a.kv.max_pages, a.kv.n_pages, a.kv.page_size, a.n_kv, g, s >= 0};
-        attend_range<HD, G>(st, qv, kv, 0, uint32_t(max(s_pos[v] + 1, 0)), warp, kBWarps, a.st);
+        attend_range<HD, G, false, true>(st, qv, kv, 0, uint32_t(max(s_pos[v] + 1, 0)), warp, kBWarps, a.st);
         merge_lane_groups<HD, G>(st);
         store_warp_state<HD, G, kBWarps>(st, ws, warp);
         __syncthreads();
@@ -628,7 +665,7 @@ constexpr uint32_t kPThreads = 256;
 constexpr int kPWarps = kPThreads / 32;
 constexpr uint32_t kPMaxLayers = 48;
 constexpr uint32_t kPtStageP = 256;
-constexpr uint32_t kLmBufs = 8;
+constexpr uint32_t kLmBufs = 16;
 
 struct PLayer {
     const uint8_t *w_qkv, *w_o_blk, *w_gu, *w_down_t;
@@ -657,6 +694,8 @@ struct PersistArgs {
     uint32_t F, c_ctas;         // C: F intermediate rows per CTA
     uint32_t slot_bytes, off_b, off_c;
     uint32_t lm_rows, lm_chunk, lm_nbuf;  // lm_head: rows per CTA, rows per TMA chunk, chunk buffers
+    uint32_t lm_extra0;                   // first chunk buffer past the two layer slots (lm_nbuf: none)
+    uint32_t region_bytes;                // layer slots / chunk buffers; the scratch follows
     unsigned long long *trace;  // optional [grid][3 n_layers + 2][2] %globaltimer stamps, or NULL
 };
 
@@ -675,8 +714,9 @@ __device__ bool grid_barrier(const PersistArgs &p, uint32_t k, int *s_ok) {
     if (threadIdx.x == 0) {
         uint32_t *ctr = p.sync + k;
         const uint32_t *abort_flag = p.sync + 3 * p.n_layers;
-        __threadfence();
-        atomicAdd(ctr, 1u);
+        // Release arrival: the CTA's writes (ordered before thread 0 by the barrier above)
+        // are visible to every CTA that acquires the count; cheaper than a full fence.
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
         int ok = 1;
         const uint64_t t0 = global_ns();
         for (uint32_t i = 0;; ++i) {
@@ -783,10 +823,11 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
     constexpr uint32_t cols_b = G * HD, bpitch = cols_b * 2;
     const uint32_t pitch = p.h * 2;
     uint8_t *slots[2] = {psm, psm + p.slot_bytes};
-    float *xs = reinterpret_cast<float *>(psm + 2 * size_t(p.slot_bytes));
+    float *xs = reinterpret_cast<float *>(psm + p.region_bytes);
     float *red = xs + NV * p.h;
-    float *hs = red + 33 * NV;          // [F][NV]
+    float *hs = red + ((33 * NV + 3) & ~3u);  // [F][NV], 16-byte aligned like every buffer here
     float *attn = hs + ((p.F * NV + 3) & ~3u);  // [NV][G*HD], 16-byte aligned
+    float *gu = attn + NV * G * HD;             // [2F][NV] gate then up sums
     const uint32_t b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const PShare sh = p_share<HD, G>(p);
     const bool has_bytes = p_bytes<HD, G>(p, sh) != 0;
@@ -841,38 +882,50 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
     }
 
     // lm_head: this CTA's contiguous rows, streamed by TMA in chunks of lm_chunk rows
-    // through lm_nbuf buffers laid over the two (then free) layer slots.
+    // through lm_nbuf buffers. Buffers lm_extra0.. lie past the two layer slots and are
+    // filled at kernel start; the others overlay the slots and are filled once those are
+    // free. Chunks are issued and consumed in one order of positions q: buffer
+    // (q + lm_extra0) % lm_nbuf in round q / lm_nbuf (the early buffers come first), holding
+    // chunk buffer + round * lm_nbuf when that exists.
     const uint32_t lm_r0 = min(p.vocab, b * p.lm_rows), lm_r1 = min(p.vocab, lm_r0 + p.lm_rows);
     const uint32_t lm_nchunks = (lm_r1 - lm_r0 + p.lm_chunk - 1) / p.lm_chunk;
     const uint32_t lm_cbytes = p.lm_chunk * pitch;
-    uint32_t lm_issued = 0, lm_done = 0;
-    auto lm_issue = [&](uint32_t i) {  // thread 0
-        const uint32_t r0 = lm_r0 + i * p.lm_chunk, nr = min(p.lm_chunk, lm_r1 - r0);
-        uint64_t *bar = &lbar[i % p.lm_nbuf];
+    const uint32_t lm_rot = p.lm_extra0 % p.lm_nbuf;
+    const uint32_t lm_npos = (lm_nchunks + p.lm_nbuf - 1) / p.lm_nbuf * p.lm_nbuf;
+    uint32_t lm_issued = 0, lm_done = 0;  // positions
+    auto lm_buf = [&](uint32_t q) { return (q % p.lm_nbuf + lm_rot) % p.lm_nbuf; };
+    auto lm_chunk_at = [&](uint32_t q) { return lm_buf(q) + q / p.lm_nbuf * p.lm_nbuf; };
+    auto lm_issue = [&](uint32_t q) {  // thread 0; position q holds a chunk
+        const uint32_t j = lm_buf(q);
+        const uint32_t r0 = lm_r0 + lm_chunk_at(q) * p.lm_chunk, nr = min(p.lm_chunk, lm_r1 - r0);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        mbar_expect_tx(bar, nr * pitch);
-        bulk_load(psm + size_t(i % p.lm_nbuf) * lm_cbytes, p.lm_head + size_t(r0) * pitch, nr * pitch, bar);
+        mbar_expect_tx(&lbar[j], nr * pitch);
+        bulk_load(psm + size_t(j) * lm_cbytes, p.lm_head + size_t(r0) * pitch, nr * pitch, &lbar[j]);
     };
-    // Chunk buffer j lies in the layer slot that is free during the last layer?
-    auto lm_in_free_slot = [&](uint32_t j) {
-        const uint32_t fs = p.n_layers & 1u;  // slot of layer n_layers - 2
+    // May buffer j be filled now? stage 0: kernel start (past the slots only); 1: last
+    // layer (also the slot of layer n_layers - 2); 2: after the last layer (any).
+    auto lm_free = [&](uint32_t j, int stage) {
         const size_t lo = size_t(j) * lm_cbytes, hi = lo + lm_cbytes;
-        return p.n_layers >= 2 && lo >= size_t(fs) * p.slot_bytes && hi <= size_t(fs + 1) * p.slot_bytes;
+        if (stage == 2 || lo >= 2 * size_t(p.slot_bytes)) return true;
+        const uint32_t fs = p.n_layers & 1u;
+        return stage == 1 && p.n_layers >= 2 && lo >= size_t(fs) * p.slot_bytes && hi <= size_t(fs + 1) * p.slot_bytes;
     };
+    // Issues the next positions in order while each one's buffer is free: its previous
+    // position consumed and the stage allowing it. Every thread keeps the same counters.
+    auto lm_fill = [&](int stage) {
+        while (lm_issued < lm_npos && lm_issued < lm_done + p.lm_nbuf && lm_free(lm_buf(lm_issued), stage)) {
+            if (threadIdx.x == 0 && lm_chunk_at(lm_issued) < lm_nchunks) lm_issue(lm_issued);
+            ++lm_issued;
+        }
+    };
+    lm_fill(0);
 
     for (uint32_t L = 0; L < p.n_layers; ++L) {
         const PLayer &ly = p.layers[L];
         uint8_t *sl = slots[L & 1];
         if (has_bytes && !p_wait_slot(&full[L & 1], (L >> 1) & 1u, p, &s_ok)) goto abort;
         ++waited;
-        if (L + 1 == p.n_layers) {
-            // The other slot is free for the rest of the step: start the lm_head chunks
-            // that live in it (in order, so chunk i always sits in buffer i % lm_nbuf).
-            while (lm_issued < lm_nchunks && lm_issued < p.lm_nbuf && lm_in_free_slot(lm_issued)) {
-                if (threadIdx.x == 0) lm_issue(lm_issued);
-                ++lm_issued;
-            }
-        }
+        if (L + 1 == p.n_layers) lm_fill(1);  // the other slot is free for the rest of the step
         const KvParams kvp{ly.kv_pool, p.page_table, p.n_pages, p.max_pages, p.page_size};
 
         // ---- A: RMSNorm + q;k;v + RoPE + KV append ----------------------------------
@@ -946,7 +999,7 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
                 KvView kv{reinterpret_cast<const __half *>(ly.kv_pool),
                           stage_pt ? s_pt[v] : p.page_table + size_t(max(s, 0)) * p.max_pages,
                           p.max_pages, p.n_pages, p.page_size, p.n_kv, sh.g, s >= 0};
-                attend_range<HD, G, true>(st, qv, kv, 0, uint32_t(max(s_pos[v] + 1, 0)), warp, kPWarps, p.st);
+                attend_range<HD, G, true, true>(st, qv, kv, 0, uint32_t(max(s_pos[v] + 1, 0)), warp, kPWarps, p.st);
                 merge_lane_groups<HD, G>(st);
                 store_warp_state<HD, G, kPWarps>(st, ws, warp);
                 __syncthreads();
@@ -959,24 +1012,40 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
             }
             const uint8_t *wsm = sl + p.off_b;
             constexpr uint32_t nch = bpitch / 16;
-            for (uint32_t rr = warp; rr < sh.nb; rr += kPWarps) {
-                float acc[NV];
+            // Rows rr and rr + kPWarps of a warp in one pass (the attention chunk is read once).
+            for (uint32_t rr = warp; rr < sh.nb; rr += 2 * kPWarps) {
+                const bool two = rr + kPWarps < sh.nb;
+                float acc[2][NV];
 #pragma unroll
-                for (int v = 0; v < NV; ++v) acc[v] = 0.f;
+                for (int v = 0; v < NV; ++v) acc[0][v] = acc[1][v] = 0.f;
                 for (uint32_t c = lane; c < nch; c += 32) {
-                    float wf[8];
-                    unpack8(*reinterpret_cast<const uint4 *>(wsm + size_t(rr) * bpitch + c * 16), wf);
+                    float wf[2][8];
+                    unpack8(*reinterpret_cast<const uint4 *>(wsm + size_t(rr) * bpitch + c * 16), wf[0]);
+                    if (two)
+                        unpack8(*reinterpret_cast<const uint4 *>(wsm + size_t(rr + kPWarps) * bpitch + c * 16), wf[1]);
 #pragma unroll
-                    for (int v = 0; v < NV; ++v)
+                    for (int v = 0; v < NV; ++v) {
+                        const float4 a0 = *reinterpret_cast<const float4 *>(attn + v * cols_b + c * 8);
+                        const float4 a1 = *reinterpret_cast<const float4 *>(attn + v * cols_b + c * 8 + 4);
+                        const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
 #pragma unroll
-                        for (int e = 0; e < 8; ++e) acc[v] = fmaf(wf[e], attn[v * cols_b + c * 8 + e], acc[v]);
+                        for (int e = 0; e < 8; ++e) acc[0][v] = fmaf(wf[0][e], av[e], acc[0][v]);
+                        if (two)
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) acc[1][v] = fmaf(wf[1][e], av[e], acc[1][v]);
+                    }
                 }
 #pragma unroll
-                for (int v = 0; v < NV; ++v) {
-                    const float t = warp_sum(acc[v]);
-                    if (lane == uint32_t(v))
-                        atomicAdd(reinterpret_cast<unsigned long long *>(p.delta0 + size_t(v) * p.h + sh.b_row0 + rr),
-                                  static_cast<unsigned long long>(to_fix(t)));
+                for (int r = 0; r < 2; ++r) {
+                    if (r == 1 && !two) break;
+#pragma unroll
+                    for (int v = 0; v < NV; ++v) {
+                        const float t = warp_sum(acc[r][v]);
+                        if (lane == uint32_t(v))
+                            atomicAdd(reinterpret_cast<unsigned long long *>(p.delta0 + size_t(v) * p.h + sh.b_row0 +
+                                                                             rr + r * kPWarps),
+                                      static_cast<unsigned long long>(to_fix(t)));
+                    }
                 }
             }
         }
@@ -992,19 +1061,34 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
             else
                 stage_residual<NV>(p.base1, p.delta0, p.h, gpre, ly.post_norm, p.eps, xs, red,
                                    b == 0 ? p.base0 : nullptr, nullptr, b == 0);
-            const uint8_t *wg = sl + p.off_c, *wu = wg + p.F * pitch, *wd = wg + 2 * p.F * pitch;
-            for (uint32_t f = warp; f < sh.nc; f += kPWarps) {
-                float acc[1][NV], accu[1][NV];
-                smem_dot<NV, 1>(wg + size_t(f) * pitch, pitch, 1, pitch / 16, xs, p.h, acc);
-                smem_dot<NV, 1>(wu + size_t(f) * pitch, pitch, 1, pitch / 16, xs, p.h, accu);
-                if (lane == 0) {
+            const uint8_t *wg = sl + p.off_c, *wd = wg + 2 * p.F * pitch;
+            // The 2 nc dot products (gate rows f, then up rows f), three rows per warp and
+            // pass; SwiGLU once every warp's sums are in shared memory.
+            const uint32_t ngu = 2 * sh.nc;
+            for (uint32_t j0 = warp; j0 < ngu; j0 += 3 * kPWarps) {
+                const uint8_t *rows[3];
+                uint32_t nr = 0;
 #pragma unroll
-                    for (int v = 0; v < NV; ++v) {
-                        const float gv = acc[0][v], uv = accu[0][v];
-                        const float sg = 1.0f / (1.0f + expf(-gv));  // Opure_CpuReference.cpp:195
-                        hs[f * NV + v] = (gv * sg) * uv;
-                    }
+                for (int i = 0; i < 3; ++i) {
+                    const uint32_t j = j0 + i * kPWarps;
+                    rows[i] = wg + size_t(j < sh.nc ? j : p.F + (j - sh.nc)) * pitch;
+                    if (j < ngu) nr = i + 1;
                 }
+                float acc[3][NV];
+                smem_dot_ptrs<NV, 3>(rows, nr, pitch / 16, xs, p.h, acc);
+                if (lane == 0)
+#pragma unroll
+                    for (int i = 0; i < 3; ++i)
+                        if (i < int(nr))
+#pragma unroll
+                            for (int v = 0; v < NV; ++v) gu[(j0 + i * kPWarps) * NV + v] = acc[i][v];
+            }
+            __syncthreads();
+            for (uint32_t i = threadIdx.x; i < sh.nc * NV; i += blockDim.x) {
+                const uint32_t f = i / NV, v = i % NV;
+                const float gv = gu[f * NV + v], uv = gu[(sh.nc + f) * NV + v];
+                const float sg = 1.0f / (1.0f + expf(-gv));  // Opure_CpuReference.cpp:195
+                hs[f * NV + v] = (gv * sg) * uv;
             }
             __syncthreads();
             const __half *wdh = reinterpret_cast<const __half *>(wd);
@@ -1029,12 +1113,7 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
             if (threadIdx.x == 0) p_issue<HD, G>(p, sh, L + 2, sl, &full[L & 1]);
             ++issued;
         }
-        if (L + 1 == p.n_layers)
-            // Both slots are free now: the remaining first-round chunks.
-            while (lm_issued < lm_nchunks && lm_issued < p.lm_nbuf) {
-                if (threadIdx.x == 0) lm_issue(lm_issued);
-                ++lm_issued;
-            }
+        if (L + 1 == p.n_layers) lm_fill(2);  // both slots are free now
         if (!grid_barrier(p, 3 * L + 2, &s_ok)) goto abort;
     }
 
@@ -1050,11 +1129,15 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
         unsigned long long best[NV];
 #pragma unroll
         for (int v = 0; v < NV; ++v) best[v] = 0ull;
-        for (uint32_t i = 0; i < lm_nchunks; ++i) {
-            const uint32_t j = i % p.lm_nbuf;
-            if (!p_wait_slot(&lbar[j], (i / p.lm_nbuf) & 1u, p, &s_ok)) goto abort;
-            ++lm_done;
-            const uint32_t r0 = lm_r0 + i * p.lm_chunk, nr = min(p.lm_chunk, lm_r1 - r0);
+        for (uint32_t q = 0; q < lm_npos; ++q) {
+            const uint32_t j = lm_buf(q), c = lm_chunk_at(q);
+            if (c >= lm_nchunks) {  // no chunk at this position
+                ++lm_done;
+                lm_fill(2);
+                continue;
+            }
+            if (!p_wait_slot(&lbar[j], (q / p.lm_nbuf) & 1u, p, &s_ok)) goto abort;
+            const uint32_t r0 = lm_r0 + c * p.lm_chunk, nr = min(p.lm_chunk, lm_r1 - r0);
             const uint8_t *buf = psm + size_t(j) * lm_cbytes;
             for (uint32_t rr = 2 * warp; rr < nr; rr += 2 * kPWarps) {
                 float acc[2][NV];
@@ -1071,10 +1154,8 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
                     }
             }
             __syncthreads();  // buffer j read by every warp: refill it
-            if (lm_issued < lm_nchunks) {
-                if (threadIdx.x == 0) lm_issue(lm_issued);
-                ++lm_issued;
-            }
+            ++lm_done;
+            lm_fill(2);
         }
         if (lane == 0)
 #pragma unroll
@@ -1094,7 +1175,8 @@ abort:
     if (threadIdx.x == 0) {
         if (has_bytes)
             for (uint32_t L = waited; L < issued; ++L) mbar_wait(&full[L & 1], (L >> 1) & 1u);
-        for (uint32_t i = lm_done; i < lm_issued; ++i) mbar_wait(&lbar[i % p.lm_nbuf], (i / p.lm_nbuf) & 1u);
+        for (uint32_t q = lm_done; q < lm_issued; ++q)
+            if (lm_chunk_at(q) < lm_nchunks) mbar_wait(&lbar[lm_buf(q)], (q / p.lm_nbuf) & 1u);
     }
 }
 
@@ -1183,15 +1265,24 @@ opure_status run_persistent(opure_ctx *ctx, const opure_fused_step &s, bool *ran
     p.off_b = (kARows * pitch + 127) & ~127u;
     p.off_c = (p.off_b + p.rows_b * G * HD * 2 + 127) & ~127u;
     p.slot_bytes = (p.off_c + 3 * p.F * pitch + 1023) & ~1023u;
-    p.lm_rows = (s.vocab + grid - 1) / grid;
-    p.lm_chunk = 16;
-    p.lm_nbuf = std::min<uint32_t>(kLmBufs, (2 * p.slot_bytes) / (p.lm_chunk * pitch));
-    if (p.lm_nbuf < 2) return OPURE_OK;
-    const size_t scratch = (size_t(NV) * h + 33 * NV + ((p.F * NV + 3) & ~3u) + size_t(NV) * G * HD) * 4;
-    const size_t smem = 2 * size_t(p.slot_bytes) + scratch;
+    const size_t scratch =
+        (size_t(NV) * h + ((33 * NV + 3) & ~3u) + ((p.F * NV + 3) & ~3u) + size_t(NV) * G * HD + 2 * size_t(p.F) * NV) *
+        4;
     auto kern = persistent_step_kernel<NV, HD, G>;
     cudaFuncAttributes fa{};
     if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return OPURE_ERR_CUDA;
+    // Shared memory left for the slots / lm_head chunk buffers beside the scratch.
+    const size_t fixed = scratch + fa.sharedSizeBytes + 1024;
+    if (fixed + 2 * size_t(p.slot_bytes) > ctx->smem_optin) return OPURE_OK;
+    const size_t region_max = (ctx->smem_optin - fixed) & ~size_t(127);
+    p.lm_rows = (s.vocab + grid - 1) / grid;
+    p.lm_chunk = 16;
+    const uint32_t cbytes = p.lm_chunk * pitch;
+    p.lm_nbuf = uint32_t(std::min<size_t>(kLmBufs, region_max / cbytes));
+    if (p.lm_nbuf < 2) return OPURE_OK;
+    p.lm_extra0 = std::min<uint32_t>(p.lm_nbuf, (2 * p.slot_bytes + cbytes - 1) / cbytes);
+    p.region_bytes = uint32_t(std::max<size_t>(2 * size_t(p.slot_bytes), (size_t(p.lm_nbuf) * cbytes + 127) & ~size_t(127)));
+    const size_t smem = p.region_bytes + scratch;
     if (smem + fa.sharedSizeBytes + 1024 > ctx->smem_optin) return OPURE_OK;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
         return OPURE_ERR_CUDA;
