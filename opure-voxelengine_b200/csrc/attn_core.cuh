@@ -59,6 +59,13 @@ struct KvView {
     bool ok;                   // false: the sequence index was invalid
 };
 
+// Rows [0, n) of one sequence's keys and values for one kv head, copied into shared
+// memory ([n][HD] each); tokens from n on are read from the pool.
+struct KvStage {
+    const __half *k, *v;
+    uint32_t n;
+};
+
 // This lane's slice of the G query rows of kv head g, pre-scaled by scale*log2(e).
 template <int HD, int G>
 __device__ __forceinline__ void load_q_slice(const float *q_heads /* [n_heads][HD] */, uint32_t g,
@@ -78,12 +85,13 @@ __device__ __forceinline__ void load_q_slice(const float *q_heads /* [n_heads][H
 // interleaves the warps round by round (round r of warp w covers tokens base +
 // (r*warp_count + w)*TPW ..), so a context shorter than warp_count*TB still spreads over
 // every warp. Rounds past t_end are skipped (warp-uniform). COHERENT reads K/V through
-// L2 (for caches written earlier in the same kernel).
-template <int HD, int G, bool COHERENT = false, bool STRIDED = false>
+// L2 (for caches written earlier in the same kernel). STAGED reads tokens below stg.n
+// from shared memory.
+template <int HD, int G, bool COHERENT = false, bool STRIDED = false, bool STAGED = false>
 __device__ __forceinline__ void attend_range(AttnState<HD, G> &st, const float (&qv)[G][AttnShape<HD>::E],
                                              const KvView &kv, uint32_t t_begin, uint32_t t_end,
                                              uint32_t warp_idx, uint32_t warp_count,
-                                             DeviceStatus *status) {
+                                             DeviceStatus *status, const KvStage &stg = KvStage{nullptr, nullptr, 0}) {
     using S = AttnShape<HD>;
     constexpr int LPT = S::LPT, CH = S::CH, TPW = S::TPW, R = S::R, E = S::E;
     const uint32_t lane = threadIdx.x & 31u;
@@ -100,6 +108,15 @@ __device__ __forceinline__ void attend_range(AttnState<HD, G> &st, const float (
             const uint32_t t = t0 + grp;
             valid[r] = t < t_end && kv.ok;
             const __half *kp = nullptr;
+            if (STAGED && valid[r] && t < stg.n) {
+                const size_t o = size_t(t) * HD + sub * E;
+#pragma unroll
+                for (int c = 0; c < CH; ++c) {
+                    kr[r][c] = *reinterpret_cast<const uint4 *>(stg.k + o + c * 8);
+                    vr[r][c] = *reinterpret_cast<const uint4 *>(stg.v + o + c * 8);
+                }
+                continue;
+            }
             if (valid[r]) {
                 const uint32_t lp = t / kv.page_size;
                 const int32_t page = lp < kv.max_pages ? kv.pt[lp] : -1;

@@ -666,6 +666,7 @@ constexpr int kPWarps = kPThreads / 32;
 constexpr uint32_t kPMaxLayers = 48;
 constexpr uint32_t kPtStageP = 256;
 constexpr uint32_t kLmBufs = 16;
+constexpr uint32_t kKvStageTokens = 256;
 
 struct PLayer {
     const uint8_t *w_qkv, *w_o_blk, *w_gu, *w_down_t;
@@ -694,8 +695,10 @@ struct PersistArgs {
     uint32_t F, c_ctas;         // C: F intermediate rows per CTA
     uint32_t slot_bytes, off_b, off_c;
     uint32_t lm_rows, lm_chunk, lm_nbuf;  // lm_head: rows per CTA, rows per TMA chunk, chunk buffers
-    uint32_t lm_extra0;                   // first chunk buffer past the two layer slots (lm_nbuf: none)
-    uint32_t region_bytes;                // layer slots / chunk buffers; the scratch follows
+    uint32_t lm_extra0;                   // first chunk buffer past the slots and KV stage (lm_nbuf: none)
+    uint32_t lm_fixed;                    // bytes of the two layer slots + the KV stage
+    uint32_t region_bytes;                // layer slots, KV stage / chunk buffers; the scratch follows
+    uint32_t kv_cap, kv_off;              // KV stage: tokens per vector, byte offset (kv_cap 0: none)
     unsigned long long *trace;  // optional [grid][3 n_layers + 2][2] %globaltimer stamps, or NULL
 };
 
@@ -706,7 +709,10 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
 }
 
 // Grid-wide barrier k: every CTA arrives once; thread 0 waits (bounded) for all of them.
-__device__ bool grid_barrier(const PersistArgs &p, uint32_t k, int *s_ok) {
+// Thread 0 runs `after_arrive` between its arrival and its wait: every thread of the CTA
+// has finished the phase by then, so copies into shared memory read in that phase may start.
+template <typename Hook>
+__device__ bool grid_barrier(const PersistArgs &p, uint32_t k, int *s_ok, Hook &&after_arrive) {
     __syncthreads();
     // Phase trace: [k][0] = this CTA's arrival at barrier k, [k][1] = its release.
     unsigned long long *tr = p.trace ? p.trace + (size_t(blockIdx.x) * (3 * p.n_layers + 2) + k) * 2 : nullptr;
@@ -717,6 +723,7 @@ __device__ bool grid_barrier(const PersistArgs &p, uint32_t k, int *s_ok) {
         // Release arrival: the CTA's writes (ordered before thread 0 by the barrier above)
         // are visible to every CTA that acquires the count; cheaper than a full fence.
         asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
+        after_arrive();
         int ok = 1;
         const uint64_t t0 = global_ns();
         for (uint32_t i = 0;; ++i) {
@@ -739,6 +746,10 @@ __device__ bool grid_barrier(const PersistArgs &p, uint32_t k, int *s_ok) {
     }
     __syncthreads();
     return *s_ok != 0;
+}
+
+__device__ __forceinline__ bool grid_barrier(const PersistArgs &p, uint32_t k, int *s_ok) {
+    return grid_barrier(p, k, s_ok, [] {});
 }
 
 // This CTA's share of each phase (the same for every layer).
@@ -794,6 +805,28 @@ __device__ void p_issue(const PersistArgs &p, const PShare &s, uint32_t L, uint8
     }
 }
 
+// A position in the lm_head chunk order: q counts positions, m is q's index within its
+// round k of lm_nbuf positions (kept incrementally: no divisions in the loop).
+struct LmCursor {
+    uint32_t q, m, k;
+    __device__ __forceinline__ uint32_t buf(uint32_t rot, uint32_t nbuf) const {
+        const uint32_t j = m + rot;
+        return j >= nbuf ? j - nbuf : j;
+    }
+    __device__ __forceinline__ void next(uint32_t nbuf) {
+        ++q;
+        if (++m == nbuf) {
+            m = 0;
+            ++k;
+        }
+    }
+};
+
+// lm_head rows per warp and pass (chunk = kPWarps of them): four for one or two vectors,
+// two for more (registers).
+template <int NV>
+constexpr uint32_t kLmRowsPerWarp = NV <= 2 ? 4 : 2;
+
 // Whole-CTA bounded wait on `bar` reaching the end of phase `parity`.
 __device__ bool p_wait_slot(uint64_t *bar, uint32_t parity, const PersistArgs &p, int *s_ok) {
     if (threadIdx.x == 0) {
@@ -815,6 +848,8 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
     extern __shared__ __align__(1024) uint8_t psm[];
     __shared__ __align__(8) uint64_t full[2];
     __shared__ __align__(8) uint64_t lbar[kLmBufs];
+    __shared__ __align__(8) uint64_t kvbar;
+    __shared__ uint32_t s_nst[NV];
     __shared__ int s_ok;
     __shared__ WarpStates<HD, G, kPWarps> ws;
     __shared__ int32_t s_seq[NV], s_pos[NV];
@@ -838,6 +873,7 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
         mbar_init(&full[0], 1);
         mbar_init(&full[1], 1);
         for (uint32_t j = 0; j < kLmBufs; ++j) mbar_init(&lbar[j], 1);
+        mbar_init(&kvbar, 1);
     }
     // Sequences, positions and page tables are fixed for the step: stage them once.
     if (threadIdx.x < NV) {
@@ -851,6 +887,51 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
             s_pt[i / p.max_pages][i % p.max_pages] =
                 s >= 0 ? p.page_table[size_t(s) * p.max_pages + i % p.max_pages] : -1;
         }
+    __syncthreads();
+    // KV stage: the attention CTAs copy keys/values [0, s_nst[v]) of their kv head into
+    // shared memory one layer ahead. Only rows written before this step qualify (below the
+    // first position any vector of the sequence computes now), on pages that are valid.
+    if (threadIdx.x < NV) {
+        const int32_t sq = s_seq[threadIdx.x];
+        int32_t first = s_pos[threadIdx.x];
+        for (int u = 0; u < NV; ++u)
+            if (s_seq[u] == sq) first = min(first, s_pos[u]);
+        uint32_t n = (sq >= 0 && stage_pt && sh.nb && first > 0) ? min(uint32_t(first), p.kv_cap) : 0u;
+        for (uint32_t i = 0; i * p.page_size < n; ++i) {
+            const int32_t pg = i < p.max_pages ? s_pt[threadIdx.x][i] : -1;
+            if (pg < 0 || uint32_t(pg) >= p.n_pages) {
+                n = i * p.page_size;  // the pool path reports the bad page
+                break;
+            }
+        }
+        s_nst[threadIdx.x] = n;
+    }
+    __syncthreads();
+    uint32_t kv_total = 0;  // bytes per layer
+#pragma unroll
+    for (int v = 0; v < NV; ++v) kv_total += 2 * s_nst[v] * HD * 2;
+    const bool kv_on = kv_total != 0;
+    uint8_t *kvs = psm + p.kv_off;
+    const uint32_t kv_vbytes = p.kv_cap * HD * 2;  // one vector's K (then V) rows
+    auto kv_issue = [&](uint32_t L) {  // thread 0
+        const uint16_t *pool = p.layers[L].kv_pool;
+        const size_t blk = size_t(p.page_size) * HD;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_expect_tx(&kvbar, kv_total);
+        for (int v = 0; v < NV; ++v)
+            for (uint32_t t0 = 0; t0 < s_nst[v]; t0 += p.page_size) {
+                const uint32_t nr = min(p.page_size, s_nst[v] - t0);
+                const size_t kofs = (size_t(s_pt[v][t0 / p.page_size]) * 2 * p.n_kv + sh.g) * blk;
+                uint8_t *dk = kvs + size_t(v) * 2 * kv_vbytes + size_t(t0) * HD * 2;
+                bulk_load_keep(dk, pool + kofs, nr * HD * 2, &kvbar);
+                bulk_load_keep(dk + kv_vbytes, pool + kofs + size_t(p.n_kv) * blk, nr * HD * 2, &kvbar);
+            }
+    };
+    uint32_t kv_issued = 0, kv_waited = 0;  // layers
+    if (kv_on && p.n_layers) {
+        if (threadIdx.x == 0) kv_issue(0);
+        kv_issued = 1;
+    }
     uint32_t issued = 0, waited = 0;
     // Trace rows 3 n_layers (kernel start, in [1]) and 3 n_layers + 1 (end, in [0]).
     unsigned long long *trow = p.trace ? p.trace + size_t(blockIdx.x) * (3 * p.n_layers + 2) * 2 : nullptr;
@@ -882,9 +963,9 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
     }
 
     // lm_head: this CTA's contiguous rows, streamed by TMA in chunks of lm_chunk rows
-    // through lm_nbuf buffers. Buffers lm_extra0.. lie past the two layer slots and are
-    // filled at kernel start; the others overlay the slots and are filled once those are
-    // free. Chunks are issued and consumed in one order of positions q: buffer
+    // through lm_nbuf buffers. Buffers lm_extra0.. lie past the two layer slots and the KV
+    // stage and are filled at kernel start; the others overlay those and are filled once
+    // they are free. Chunks are issued and consumed in one order of positions q: buffer
     // (q + lm_extra0) % lm_nbuf in round q / lm_nbuf (the early buffers come first), holding
     // chunk buffer + round * lm_nbuf when that exists.
     const uint32_t lm_r0 = min(p.vocab, b * p.lm_rows), lm_r1 = min(p.vocab, lm_r0 + p.lm_rows);
@@ -892,30 +973,29 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
     const uint32_t lm_cbytes = p.lm_chunk * pitch;
     const uint32_t lm_rot = p.lm_extra0 % p.lm_nbuf;
     const uint32_t lm_npos = (lm_nchunks + p.lm_nbuf - 1) / p.lm_nbuf * p.lm_nbuf;
-    uint32_t lm_issued = 0, lm_done = 0;  // positions
-    auto lm_buf = [&](uint32_t q) { return (q % p.lm_nbuf + lm_rot) % p.lm_nbuf; };
-    auto lm_chunk_at = [&](uint32_t q) { return lm_buf(q) + q / p.lm_nbuf * p.lm_nbuf; };
-    auto lm_issue = [&](uint32_t q) {  // thread 0; position q holds a chunk
-        const uint32_t j = lm_buf(q);
-        const uint32_t r0 = lm_r0 + lm_chunk_at(q) * p.lm_chunk, nr = min(p.lm_chunk, lm_r1 - r0);
+    LmCursor lm_iss{}, lm_dn{};  // next position to issue / to consume
+    auto lm_issue = [&](uint32_t j, uint32_t c) {  // thread 0: chunk c into buffer j
+        const uint32_t r0 = lm_r0 + c * p.lm_chunk, nr = min(p.lm_chunk, lm_r1 - r0);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         mbar_expect_tx(&lbar[j], nr * pitch);
         bulk_load(psm + size_t(j) * lm_cbytes, p.lm_head + size_t(r0) * pitch, nr * pitch, &lbar[j]);
     };
-    // May buffer j be filled now? stage 0: kernel start (past the slots only); 1: last
-    // layer (also the slot of layer n_layers - 2); 2: after the last layer (any).
+    // May buffer j be filled now? stage 0: kernel start (past the slots and KV stage only);
+    // 1: last layer (also the slot of layer n_layers - 2); 2: after the last layer (any).
     auto lm_free = [&](uint32_t j, int stage) {
         const size_t lo = size_t(j) * lm_cbytes, hi = lo + lm_cbytes;
-        if (stage == 2 || lo >= 2 * size_t(p.slot_bytes)) return true;
+        if (stage == 2 || lo >= p.lm_fixed) return true;
         const uint32_t fs = p.n_layers & 1u;
         return stage == 1 && p.n_layers >= 2 && lo >= size_t(fs) * p.slot_bytes && hi <= size_t(fs + 1) * p.slot_bytes;
     };
     // Issues the next positions in order while each one's buffer is free: its previous
     // position consumed and the stage allowing it. Every thread keeps the same counters.
     auto lm_fill = [&](int stage) {
-        while (lm_issued < lm_npos && lm_issued < lm_done + p.lm_nbuf && lm_free(lm_buf(lm_issued), stage)) {
-            if (threadIdx.x == 0 && lm_chunk_at(lm_issued) < lm_nchunks) lm_issue(lm_issued);
-            ++lm_issued;
+        while (lm_iss.q < lm_npos && lm_iss.q < lm_dn.q + p.lm_nbuf) {
+            const uint32_t j = lm_iss.buf(lm_rot, p.lm_nbuf), c = j + lm_iss.k * p.lm_nbuf;
+            if (!lm_free(j, stage)) break;
+            if (threadIdx.x == 0 && c < lm_nchunks) lm_issue(j, c);
+            lm_iss.next(p.lm_nbuf);
         }
     };
     lm_fill(0);
@@ -976,6 +1056,10 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
         if (b == 0)
             for (uint32_t i = threadIdx.x; i < NV * p.h; i += blockDim.x) p.delta1[i] = 0;
         if (sh.nb) {
+            if (kv_on) {
+                if (!p_wait_slot(&kvbar, L & 1u, p, &s_ok)) goto abort;
+                ++kv_waited;
+            }
             for (int v = 0; v < NV; ++v) {
                 using S = AttnShape<HD>;
                 float qv[G][S::E];
@@ -999,7 +1083,11 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
                 KvView kv{reinterpret_cast<const __half *>(ly.kv_pool),
                           stage_pt ? s_pt[v] : p.page_table + size_t(max(s, 0)) * p.max_pages,
                           p.max_pages, p.n_pages, p.page_size, p.n_kv, sh.g, s >= 0};
-                attend_range<HD, G, true, true>(st, qv, kv, 0, uint32_t(max(s_pos[v] + 1, 0)), warp, kPWarps, p.st);
+                const KvStage stg{reinterpret_cast<const __half *>(kvs + size_t(v) * 2 * kv_vbytes),
+                                  reinterpret_cast<const __half *>(kvs + size_t(v) * 2 * kv_vbytes + kv_vbytes),
+                                  s_nst[v]};
+                attend_range<HD, G, true, true, true>(st, qv, kv, 0, uint32_t(max(s_pos[v] + 1, 0)), warp, kPWarps,
+                                                      p.st, stg);
                 merge_lane_groups<HD, G>(st);
                 store_warp_state<HD, G, kPWarps>(st, ws, warp);
                 __syncthreads();
@@ -1049,7 +1137,15 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
                 }
             }
         }
-        if (!grid_barrier(p, 3 * L + 1, &s_ok)) goto abort;
+        {
+            // Arrived: this CTA's KV stage is read; thread 0 starts the next layer's copy.
+            const bool next_kv = kv_on && L + 1 < p.n_layers;
+            const bool ok = grid_barrier(p, 3 * L + 1, &s_ok, [&] {
+                if (next_kv) kv_issue(L + 1);
+            });
+            kv_issued += next_kv ? 1u : 0u;
+            if (!ok) goto abort;
+        }
 
         // ---- C: RMSNorm + gate;up + SwiGLU + down partial sums ----------------------
         if (sh.nc) {
@@ -1107,14 +1203,19 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
                               static_cast<unsigned long long>(to_fix(acc[v])));
             }
         }
-        __syncthreads();
-        // This slot's layer is done: start copying layer L+2 into it.
-        if (L + 2 < p.n_layers) {
-            if (threadIdx.x == 0) p_issue<HD, G>(p, sh, L + 2, sl, &full[L & 1]);
-            ++issued;
+        if (L + 1 == p.n_layers) {
+            __syncthreads();
+            lm_fill(2);  // both slots are free now
         }
-        if (L + 1 == p.n_layers) lm_fill(2);  // both slots are free now
-        if (!grid_barrier(p, 3 * L + 2, &s_ok)) goto abort;
+        {
+            // Arrived: this slot's layer is done; thread 0 starts copying layer L+2 into it.
+            const bool refill = L + 2 < p.n_layers;
+            const bool ok = grid_barrier(p, 3 * L + 2, &s_ok, [&] {
+                if (refill) p_issue<HD, G>(p, sh, L + 2, sl, &full[L & 1]);
+            });
+            issued += refill ? 1u : 0u;
+            if (!ok) goto abort;
+        }
     }
 
     {
@@ -1129,32 +1230,30 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
         unsigned long long best[NV];
 #pragma unroll
         for (int v = 0; v < NV; ++v) best[v] = 0ull;
-        for (uint32_t q = 0; q < lm_npos; ++q) {
-            const uint32_t j = lm_buf(q), c = lm_chunk_at(q);
-            if (c >= lm_nchunks) {  // no chunk at this position
-                ++lm_done;
-                lm_fill(2);
-                continue;
-            }
-            if (!p_wait_slot(&lbar[j], (q / p.lm_nbuf) & 1u, p, &s_ok)) goto abort;
-            const uint32_t r0 = lm_r0 + c * p.lm_chunk, nr = min(p.lm_chunk, lm_r1 - r0);
-            const uint8_t *buf = psm + size_t(j) * lm_cbytes;
-            for (uint32_t rr = 2 * warp; rr < nr; rr += 2 * kPWarps) {
-                float acc[2][NV];
-                smem_dot<NV, 2>(buf + size_t(rr) * pitch, pitch, min(2u, nr - rr), pitch / 16, xs, p.h, acc);
+        constexpr uint32_t RW = kLmRowsPerWarp<NV>;
+        while (lm_dn.q < lm_npos) {
+            const uint32_t j = lm_dn.buf(lm_rot, p.lm_nbuf), c = j + lm_dn.k * p.lm_nbuf;
+            if (c < lm_nchunks) {
+                if (!p_wait_slot(&lbar[j], lm_dn.k & 1u, p, &s_ok)) goto abort;
+                const uint32_t r0 = lm_r0 + c * p.lm_chunk, nr = min(p.lm_chunk, lm_r1 - r0);
+                const uint8_t *buf = psm + size_t(j) * lm_cbytes;
+                for (uint32_t rr = RW * warp; rr < nr; rr += RW * kPWarps) {
+                    float acc[RW][NV];
+                    smem_dot<NV, RW>(buf + size_t(rr) * pitch, pitch, min(RW, nr - rr), pitch / 16, xs, p.h, acc);
 #pragma unroll
-                for (int r = 0; r < 2; ++r)
+                    for (int r = 0; r < int(RW); ++r)
 #pragma unroll
-                    for (int v = 0; v < NV; ++v) {
-                        if (rr + r >= nr) continue;
-                        const unsigned long long k = argmax_key(acc[r][v], r0 + rr + r);
-                        best[v] = k > best[v] ? k : best[v];
-                        if (p.logits && lane == uint32_t((r * NV + v) & 31))
-                            p.logits[size_t(v) * p.vocab + r0 + rr + r] = acc[r][v];
-                    }
+                        for (int v = 0; v < NV; ++v) {
+                            if (rr + r >= nr) continue;
+                            const unsigned long long k = argmax_key(acc[r][v], r0 + rr + r);
+                            best[v] = k > best[v] ? k : best[v];
+                            if (p.logits && lane == uint32_t((r * NV + v) & 31))
+                                p.logits[size_t(v) * p.vocab + r0 + rr + r] = acc[r][v];
+                        }
+                }
+                __syncthreads();  // buffer j read by every warp: refill it
             }
-            __syncthreads();  // buffer j read by every warp: refill it
-            ++lm_done;
+            lm_dn.next(p.lm_nbuf);
             lm_fill(2);
         }
         if (lane == 0)
@@ -1175,8 +1274,11 @@ abort:
     if (threadIdx.x == 0) {
         if (has_bytes)
             for (uint32_t L = waited; L < issued; ++L) mbar_wait(&full[L & 1], (L >> 1) & 1u);
-        for (uint32_t q = lm_done; q < lm_issued; ++q)
-            if (lm_chunk_at(q) < lm_nchunks) mbar_wait(&lbar[lm_buf(q)], (q / p.lm_nbuf) & 1u);
+        for (uint32_t l = kv_waited; l < kv_issued; ++l) mbar_wait(&kvbar, l & 1u);
+        for (LmCursor c = lm_dn; c.q < lm_iss.q; c.next(p.lm_nbuf)) {
+            const uint32_t j = c.buf(lm_rot, p.lm_nbuf);
+            if (j + c.k * p.lm_nbuf < lm_nchunks) mbar_wait(&lbar[j], c.k & 1u);
+        }
     }
 }
 
@@ -1275,13 +1377,18 @@ opure_status run_persistent(opure_ctx *ctx, const opure_fused_step &s, bool *ran
     const size_t fixed = scratch + fa.sharedSizeBytes + 1024;
     if (fixed + 2 * size_t(p.slot_bytes) > ctx->smem_optin) return OPURE_OK;
     const size_t region_max = (ctx->smem_optin - fixed) & ~size_t(127);
+    // KV stage: up to kKvStageTokens keys and values per vector, as far as they fit.
+    const size_t kv_tok = size_t(NV) * 2 * HD * 2;
+    p.kv_off = 2 * p.slot_bytes;
+    p.kv_cap = uint32_t(std::min<size_t>(kKvStageTokens, (region_max - 2 * size_t(p.slot_bytes)) / kv_tok)) & ~15u;
+    p.lm_fixed = uint32_t((2 * size_t(p.slot_bytes) + p.kv_cap * kv_tok + 127) & ~size_t(127));
     p.lm_rows = (s.vocab + grid - 1) / grid;
-    p.lm_chunk = 16;
+    p.lm_chunk = kLmRowsPerWarp<NV> * kPWarps;
     const uint32_t cbytes = p.lm_chunk * pitch;
     p.lm_nbuf = uint32_t(std::min<size_t>(kLmBufs, region_max / cbytes));
     if (p.lm_nbuf < 2) return OPURE_OK;
-    p.lm_extra0 = std::min<uint32_t>(p.lm_nbuf, (2 * p.slot_bytes + cbytes - 1) / cbytes);
-    p.region_bytes = uint32_t(std::max<size_t>(2 * size_t(p.slot_bytes), (size_t(p.lm_nbuf) * cbytes + 127) & ~size_t(127)));
+    p.lm_extra0 = std::min<uint32_t>(p.lm_nbuf, (p.lm_fixed + cbytes - 1) / cbytes);
+    p.region_bytes = uint32_t(std::max<size_t>(p.lm_fixed, (size_t(p.lm_nbuf) * cbytes + 127) & ~size_t(127)));
     const size_t smem = p.region_bytes + scratch;
     if (smem + fa.sharedSizeBytes + 1024 > ctx->smem_optin) return OPURE_OK;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)

@@ -31,6 +31,14 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
         : "memory");
 }
 
+// bulk_load with the default L2 policy, for data that is read again later (KV rows).
+__device__ __forceinline__ void bulk_load_keep(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_addr(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_addr(bar))
+                 : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t phase) {
     uint32_t ok;
     asm volatile(
