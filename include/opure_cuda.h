@@ -362,6 +362,41 @@ opure_status opure_spec_accept(opure_ctx *ctx, const opure_spec_args *a);
 opure_status opure_sample_softmax(opure_ctx *ctx, const float *logits, uint32_t vocab,
                                   uint32_t rows, const float *u, int32_t *out_tokens);
 
+/* Filtered sampling, one row of logits per sequence (the reference declares temperature,
+ * top_p, top_k and repetition_penalty in GenerationConfig, src/proto/opure.proto:35-46,
+ * without implementing them). Per row: logits of tokens in hist[seq[row]][0, hist_len[row])
+ * are penalised (l / r for l > 0, else l * r); temperature <= 0 or top_k == 1 is greedy
+ * (lowest index among the largest); otherwise z = l * (1 / T), top_k keeps the k largest
+ * (0: all; ties to the lower index), top_p < 1 keeps the shortest prefix of them, in the
+ * same order, whose mass reaches ceil(top_p * Z), and the token is the smallest index whose
+ * running kept mass exceeds floor(u[row] * Z_kept). Masses are exp(z - z_max) rounded to
+ * nearest in units of 2^-40 and summed as uint64. The token goes to out[row] and/or, as
+ * an argmax key, to keys[row] (the next self-driving step's input). vocab <= 2^18. */
+typedef struct opure_sample_args {
+    const float *logits;       /* [rows][stride]                                        */
+    uint32_t vocab, rows;
+    size_t stride;             /* floats between rows, >= vocab                         */
+    float temperature;
+    uint32_t top_k;            /* 0: off                                                */
+    float top_p;               /* (0, 1]; 1: off                                        */
+    float rep_penalty;         /* > 0; 1: off                                           */
+    const int32_t *hist;       /* [slots][max_len] token history, or NULL (no penalty)  */
+    uint32_t max_len;
+    const int32_t *seq;        /* [rows] history slot of each row, or NULL (slot = row) */
+    const int32_t *hist_len;   /* [rows] tokens of the history that count               */
+    const float *u;            /* [rows] uniforms in [0, 1) (not read when greedy)      */
+    int32_t *out;              /* [rows] or NULL                                        */
+    unsigned long long *keys;  /* [rows] or NULL                                        */
+} opure_sample_args;
+opure_status opure_sample_filtered(opure_ctx *ctx, const opure_sample_args *a);
+
+/* Per row of logits: out[row] = {max logit, L2 norm, softmax entropy (nats), log-sum-exp},
+ * as VoxelEngine::RefreshLogitStats (src/engine/Opure_VoxelEngine.cpp:832-876) computes
+ * the first three on the host: sqrt(sum l^2) in double; entropy with p = exp(double(l -
+ * max)) / sum, accumulated in double. */
+opure_status opure_logit_stats(opure_ctx *ctx, const float *logits, uint32_t vocab, uint32_t rows,
+                               size_t stride, float *out);
+
 /* The same draw, written as an argmax key into keys[row] so that the next self-driving
  * decode step (OPURE_VEC_AUTO) takes the sampled token as its input: the draft model's
  * sampling step of speculative decoding. With save != NULL row r is also copied to

@@ -170,6 +170,28 @@ opure_status opure_engine_spec_generate(opure_engine *target, opure_engine *draf
                                         int32_t *accept_log, uint32_t accept_log_rounds,
                                         opure_spec_stats *stats);
 
+typedef struct opure_sample_options {
+    float temperature;        /* <= 0: greedy                                           */
+    uint32_t top_k;           /* 0: off                                                 */
+    float top_p;              /* (0, 1]; 1: off                                         */
+    float rep_penalty;        /* > 0; 1: off                                            */
+    uint64_t seed;            /* sequence s draws uniforms from Rng(seed ^ s * 0x9E3779B97F4A7C15) */
+} opure_sample_options;
+
+/* Sampled generation of n_seq prompts of length prompt_len (concatenated in `prompts`) into
+ * out_tokens[n_seq][budget]: after the prompt, each token is drawn on the device by
+ * opure_sample_filtered (temperature, top-k, top-p, repetition penalty over the sequence so
+ * far; the reference declares these in GenerationConfig, src/proto/opure.proto:35-46,
+ * without implementing them) from its position's logits with the next uniform of the
+ * sequence's stream, and is the next step's input. stats (may be NULL) receives
+ * [n_seq][budget][4] opure_logit_stats of those logits: max, L2 norm, entropy (nats),
+ * log-sum-exp (the reference's RefreshLogitStats, Opure_VoxelEngine.cpp:832-876); logits
+ * (may be NULL; costly) the logits themselves, [n_seq][budget][vocab].
+ * max_batch >= n_seq, max_len >= prompt_len + budget + 1. */
+opure_status opure_engine_sample_generate(opure_engine *e, const int32_t *prompts, uint32_t prompt_len, uint32_t n_seq,
+                                          uint32_t budget, const opure_sample_options *o, int32_t *out_tokens,
+                                          float *stats, float *logits);
+
 /* Parses config.json, maps model.safetensors, resolves tensor roles and plans the device
  * layout without touching a GPU (the reference's opure_inspect tool, Opure_Inspect.cpp).
  * On failure the reason is copied to err (err_len bytes, may be NULL). */

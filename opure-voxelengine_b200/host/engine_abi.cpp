@@ -7,6 +7,7 @@
 
 #include "opure_engine.h"
 #include "platform.h"
+#include "sample_decode.h"
 #include "spec_decode.h"
 #include "synth.h"
 #include "voxel_engine.h"
@@ -170,6 +171,30 @@ opure_status opure_engine_spec_generate(opure_engine *target, opure_engine *draf
             stats->verify_ms = st.verifyMs;
             stats->total_ms = st.totalMs;
         }
+    });
+}
+
+opure_status opure_engine_sample_generate(opure_engine *e, const int32_t *prompts, uint32_t prompt_len, uint32_t n_seq,
+                                          uint32_t budget, const opure_sample_options *o, int32_t *out_tokens,
+                                          float *stats, float *logits) {
+    if (!e || !prompts || !o || !out_tokens || n_seq == 0 || prompt_len == 0 || budget == 0)
+        return OPURE_ERR_INVALID_ARG;
+    return Guard(e, [&] {
+        std::vector<std::vector<uint32_t>> ps(n_seq);
+        for (uint32_t s = 0; s < n_seq; ++s) ps[s] = ToU32(prompts + size_t(s) * prompt_len, prompt_len);
+        opure::engine::SampleOptions so;
+        so.temperature = o->temperature;
+        so.topK = o->top_k;
+        so.topP = o->top_p;
+        so.repPenalty = o->rep_penalty;
+        so.seed = o->seed;
+        so.maxNew = budget;
+        std::vector<float> st, lg;
+        const auto res = opure::engine::SampleGenerate(e->eng, ps, so, stats ? &st : nullptr, logits ? &lg : nullptr);
+        for (uint32_t s = 0; s < n_seq; ++s)
+            for (uint32_t i = 0; i < budget; ++i) out_tokens[size_t(s) * budget + i] = int32_t(res[s][i]);
+        if (stats) std::copy(st.begin(), st.end(), stats);
+        if (logits) std::copy(lg.begin(), lg.end(), logits);
     });
 }
 

@@ -161,6 +161,8 @@ public:
     int32_t *DeviceInTokens() const { return buf_.inTokens; }   // [maxBatch]
     float *DeviceLogits() const { return buf_.logits; }       // [maxBatch][vocab]
     unsigned long long *DeviceKeys() const { return buf_.keys; }
+    const int32_t *DeviceSeq() const { return buf_.seq; }      // [vectors] slot of each vector
+    const int32_t *DevicePos() const { return buf_.pos; }      // [vectors] next position of each
     // Rewinds the positions of vectors 0..n-1 (stream-ordered, no wait).
     void SetPositions(const int32_t *positions, uint32_t n);
     void Sync();

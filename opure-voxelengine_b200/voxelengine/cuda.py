@@ -62,6 +62,13 @@ class SpecArgs(C.Structure):
                 ("u_final", P), ("out_tokens", P), ("out_accepted", P)]
 
 
+class SampleArgs(C.Structure):
+    _fields_ = [("logits", P), ("vocab", u32), ("rows", u32), ("stride", sz),
+                ("temperature", f32), ("top_k", u32), ("top_p", f32), ("rep_penalty", f32),
+                ("hist", P), ("max_len", u32), ("seq", P), ("hist_len", P), ("u", P),
+                ("out", P), ("keys", P)]
+
+
 class DeviceInfo(C.Structure):
     _fields_ = [("device", i32), ("sm_count", i32), ("cc_major", i32), ("cc_minor", i32),
                 ("hbm_bytes", u64), ("l2_bytes", u64), ("smem_per_block_optin", u32),
@@ -97,6 +104,7 @@ _SIGS = {
     "opure_comm_info": [P, P, P],
     "opure_allreduce_sum_f32": [P, P, P, sz], "opure_allreduce_max_u64": [P, P, P, sz],
     "opure_argmax_key_offset": [P, P, u32, u32],
+    "opure_sample_filtered": [P, P], "opure_logit_stats": [P, P, u32, u32, sz, P],
 }
 
 
@@ -230,6 +238,9 @@ class Ctx:
 
     def spec_accept(self, args: SpecArgs):
         check(lib().opure_spec_accept(self.h, C.byref(args)), "opure_spec_accept")
+
+    def sample_filtered(self, args: SampleArgs):
+        check(lib().opure_sample_filtered(self.h, C.byref(args)), "opure_sample_filtered")
 
     def call(self, name: str, *args):
         check(getattr(lib(), name)(self.h, *args), name)

@@ -46,6 +46,11 @@ class SpecStats(C.Structure):
 SPEC_GREEDY, SPEC_REJECTION = 0, 1
 
 
+class SampleOptions(C.Structure):
+    _fields_ = [("temperature", f32), ("top_k", u32), ("top_p", f32), ("rep_penalty", f32),
+                ("seed", u64)]
+
+
 class SynthSpec(C.Structure):
     _fields_ = [("vocab", u32), ("hidden", u32), ("inter", u32), ("layers", u32), ("heads", u32),
                 ("kv_heads", u32), ("max_pos", u32), ("eps", f32), ("theta", f64), ("tied", u32),
@@ -74,6 +79,7 @@ def lib() -> C.CDLL:
             "opure_engine_create_shared": [C.c_char_p, P, P, P],
             "opure_engine_create_tp": [C.c_char_p, P, P, P, P],
             "opure_engine_spec_generate": [P, P, P, u32, u32, u32, P, P, P, u32, P],
+            "opure_engine_sample_generate": [P, P, u32, u32, u32, P, P, P, P],
             "opure_engine_destroy": [P],
             "opure_engine_get_info": [P, P],
             "opure_engine_generate": [P, P, P, u32, u32, P, P],
@@ -257,6 +263,24 @@ class Engine:
         if log is not None:
             log = log[: min(log_rounds, st.rounds)]
         return out, st, log
+
+    def sample_generate(self, prompts, budget: int, temperature: float = 1.0, top_k: int = 0,
+                        top_p: float = 1.0, rep_penalty: float = 1.0, seed: int = 0, stats: bool = False,
+                        logits: bool = False):
+        """Sampled generation (equal-length prompts). Returns tokens [n][budget], or a tuple
+        with, when asked for, the logit statistics [n][budget][4] (max, L2 norm, entropy,
+        log-sum-exp) and the logits [n][budget][vocab] each token was drawn from."""
+        ps = np.ascontiguousarray(np.stack([np.asarray(p, np.int32) for p in prompts]), np.int32)
+        n, plen = ps.shape
+        out = np.zeros((n, budget), np.int32)
+        st = np.zeros((n, budget, 4), np.float32) if stats else None
+        lg = np.zeros((n, budget, self.info.vocab), np.float32) if logits else None
+        o = SampleOptions(temperature, top_k, top_p, rep_penalty, seed)
+        _check(lib().opure_engine_sample_generate(self.h, _p(ps), plen, n, budget, C.byref(o), _p(out), _p(st),
+                                                  _p(lg)), "sample_generate", self.h)
+        if not stats and not logits:
+            return out
+        return (out,) + ((st,) if stats else ()) + ((lg,) if logits else ())
 
     def prefill(self, tokens) -> int:
         """Prefill slot 0; returns the first generated token."""

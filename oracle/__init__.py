@@ -59,6 +59,8 @@ def lib() -> C.CDLL:
             "orc_attention_paged": (None, [P, P, P, P, u32, u32, u32, u32, u32, u32, u32, f32, P]),
             "orc_attention_f32": (None, [P, P, P, u32, u32, u32, u32, u32, f32, P]),
             "orc_sample_softmax": (u32, [P, u32, f32]),
+            "orc_sample_filtered": (u32, [P, u32, f32, u32, f32, f32, P, u32, f32]),
+            "orc_logit_stats": (None, [P, u32, P]),
             "orc_spec_accept_greedy": (i32, [P, P, u32, u32, P]),
             "orc_spec_accept_rejection": (i32, [P, P, P, P, f32, u32, u32, P]),
             "orc_model_create": (P, [P]),
@@ -208,6 +210,22 @@ def attention_f32(q, k_plane, v_plane, n_heads, n_kv, hd, max_seq, seq_len, scal
 def sample_softmax(logits: np.ndarray, u: float) -> int:
     lg = np.ascontiguousarray(logits, np.float32)
     return int(lib().orc_sample_softmax(_p(lg), lg.size, u))
+
+
+def sample_filtered(logits: np.ndarray, u: float, temperature: float = 1.0, top_k: int = 0,
+                    top_p: float = 1.0, rep_penalty: float = 1.0, hist=None) -> int:
+    lg = np.ascontiguousarray(logits, np.float32)
+    h = None if hist is None else np.ascontiguousarray(hist, np.int32)
+    return int(lib().orc_sample_filtered(_p(lg), lg.size, temperature, top_k, top_p, rep_penalty, _p(h),
+                                         0 if h is None else h.size, u))
+
+
+def logit_stats(logits: np.ndarray) -> np.ndarray:
+    """{max, L2 norm, entropy (nats), log-sum-exp} of one row."""
+    lg = np.ascontiguousarray(logits, np.float32)
+    out = np.zeros(4, np.float32)
+    lib().orc_logit_stats(_p(lg), lg.size, _p(out))
+    return out
 
 
 def spec_accept_greedy(target_logits: np.ndarray, draft: np.ndarray):

@@ -5,6 +5,7 @@
 // reordering of any sum, exactly as src/engine/Opure_CpuReference.cpp computes.
 #include "oracle.h"
 
+#include <algorithm>
 #include <cmath>
 #include <condition_variable>
 #include <functional>
@@ -452,6 +453,103 @@ uint32_t orc_sample_softmax(const float *logits, uint32_t vocab, float u) {
     std::vector<double> p;
     softmax_d(logits, vocab, p);
     return inverse_cdf(p, double(u));
+}
+
+namespace {
+// Orderable key of (value, index): larger value first, then lower index; 0 for NaN.
+uint64_t sample_key(float v, uint32_t i) {
+    if (v != v) return 0;
+    uint32_t b;
+    std::memcpy(&b, &v, 4);
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return (uint64_t(b) << 32) | (0xffffffffu - i);
+}
+}  // namespace
+
+uint32_t orc_sample_filtered(const float *logits, uint32_t V, float T, uint32_t top_k, float top_p, float rep,
+                             const int32_t *hist, uint32_t hist_len, float u) {
+    std::vector<float> lp(logits, logits + V);
+    if (rep != 1.0f && hist) {
+        std::vector<char> seen(V, 0);
+        for (uint32_t i = 0; i < hist_len; ++i)
+            if (hist[i] >= 0 && uint32_t(hist[i]) < V) seen[hist[i]] = 1;
+        for (uint32_t i = 0; i < V; ++i)
+            if (seen[i]) lp[i] = lp[i] > 0.f ? lp[i] / rep : lp[i] * rep;
+    }
+    std::vector<uint32_t> order;
+    for (uint32_t i = 0; i < V; ++i)
+        if (sample_key(lp[i], i)) order.push_back(i);
+    if (order.empty()) return 0;
+    std::sort(order.begin(), order.end(),
+              [&](uint32_t a, uint32_t b) { return sample_key(lp[a], a) > sample_key(lp[b], b); });
+    if (!(T > 0.f) || top_k == 1) return order[0];
+    const double inv_t = 1.0 / double(T);
+    const double zmax = double(lp[order[0]]) * inv_t;
+    if (top_k > 1 && top_k < V && order.size() > top_k) order.resize(top_k);
+    std::vector<uint64_t> mass(V, 0);
+    for (uint32_t i : order) {
+        const double e = std::exp(double(lp[i]) * inv_t - zmax);
+        mass[i] = e > 0.0 ? uint64_t(std::nearbyint(e * 1099511627776.0)) : 0;  // NaN (inf - inf): 0
+    }
+    if (top_p < 1.0f) {
+        uint64_t z = 0;
+        for (uint32_t i : order) z += mass[i];
+        const double tgt = std::ceil(double(top_p) * double(z));
+        const uint64_t target = tgt < 1.0 ? 1 : uint64_t(tgt);
+        if (target < z) {
+            uint64_t cum = 0;
+            size_t keep = order.size();
+            for (size_t j = 0; j < order.size(); ++j) {
+                cum += mass[order[j]];
+                if (cum >= target) {
+                    keep = j + 1;
+                    break;
+                }
+            }
+            order.resize(keep);
+        }
+    }
+    std::vector<char> kept(V, 0);
+    uint64_t total = 0;
+    for (uint32_t i : order) {
+        kept[i] = 1;
+        total += mass[i];
+    }
+    if (total == 0) return order[0];  // no mass at all (an infinite logit): the greedy token
+    uint64_t thr = uint64_t(std::floor(double(u) * double(total)));
+    if (thr >= total) thr = total - 1;
+    uint64_t c = 0;
+    for (uint32_t i = 0; i < V; ++i) {
+        if (!kept[i]) continue;
+        c += mass[i];
+        if (c > thr) return i;
+    }
+    return order.back();
+}
+
+void orc_logit_stats(const float *l, uint32_t V, float *out) {
+    double ss = 0.0;
+    uint64_t best = 0;
+    for (uint32_t i = 0; i < V; ++i) {
+        ss += double(l[i]) * double(l[i]);
+        best = std::max(best, sample_key(l[i], i));
+    }
+    float mx = -std::numeric_limits<float>::infinity();
+    if (best) mx = l[0xffffffffu - uint32_t(best & 0xffffffffu)];
+    double se = 0.0;
+    for (uint32_t i = 0; i < V; ++i) se += std::exp(double(l[i] - mx));
+    double ent = 0.0;
+    if (se > 0.0) {
+        const double inv = 1.0 / se;
+        for (uint32_t i = 0; i < V; ++i) {
+            const double p = std::exp(double(l[i] - mx)) * inv;
+            if (p > 0.0) ent -= p * std::log(p);
+        }
+    }
+    out[0] = mx;
+    out[1] = float(std::sqrt(ss));
+    out[2] = float(ent);
+    out[3] = float(double(mx) + std::log(se));
 }
 
 int orc_spec_accept_greedy(const float *tl, const uint32_t *draft, uint32_t k, uint32_t V,

@@ -105,6 +105,22 @@ void orc_attention_f32(const float *q, const float *k_plane, const float *v_plan
  * smallest x with sum_{y<=x} exp(l_y - max) > u * Z, sums in double in index order. */
 uint32_t orc_sample_softmax(const float *logits, uint32_t vocab, float u);
 
+/* Filtered sampling (parity unpinned: the reference declares temperature, top_p, top_k
+ * and repetition_penalty in src/proto/opure.proto:35-46 but implements none of them).
+ * Restates, sequentially, the rules of opure_sample_filtered: penalty on tokens of
+ * hist[0, hist_len); greedy when T <= 0 or top_k == 1; keys sorted descending (value,
+ * then lower index); top-k prefix; masses round(exp(l/T - max) * 2^40) as uint64; top-p
+ * prefix reaching ceil(top_p * Z); draw = smallest index whose running kept mass exceeds
+ * floor(u * Z_kept). */
+uint32_t orc_sample_filtered(const float *logits, uint32_t vocab, float temperature, uint32_t top_k,
+                             float top_p, float rep_penalty, const int32_t *hist, uint32_t hist_len,
+                             float u);
+
+/* Logit statistics of VoxelEngine::RefreshLogitStats (src/engine/Opure_VoxelEngine.cpp:
+ * 832-876): out = {max, sqrt(sum l^2), entropy in nats, max + log(sum exp(l - max))};
+ * NaN logits are skipped for the max. */
+void orc_logit_stats(const float *logits, uint32_t vocab, float *out);
+
 /* Speculative accept/reject (the reference has none; parity unpinned).
  * Greedy: accepted = longest prefix with argmax(target_logits[i]) == draft[i]; the
  * token after it is argmax(target_logits[accepted]).
