@@ -46,7 +46,7 @@ FALLBACK_PEAK = 6650.0  # GB/s, used only when MEASURED_PEAKS.json is absent
 # DRAM bytes (read + write) of one decode step, summed over its launches in an ncu capture
 # of `python bench.py --quick --no-cpu [--batch B] --steps 2 --warmup 3` (launch lists in
 # profiles/decode_bs1_persistent_step.md and profiles/decode_bs64_tensor_core_step.md).
-NCU_STEP_TRAFFIC = {1: 271.9e6, 64: 411.0e6}
+NCU_STEP_TRAFFIC = {1: 271.8e6, 64: 411.0e6}
 
 
 def peaks():
@@ -775,6 +775,68 @@ def run_spec(args):
     print(json.dumps(line), flush=True)
 
 
+def run_sample(args):
+    """Sampling (SURVEY next-row 2): the opure_sample_filtered and opure_logit_stats kernels
+    on seeded N(0, 3) logits of the config-0 vocabulary (device time per call, CUDA events
+    over 50 calls after 5 warm-up ones), and sampled generation through the engine at the
+    reference chat defaults (temperature 0.8, top-k 50, top-p 0.95, Opure_Chat.cpp:69;
+    repetition penalty 1.1) against greedy generation of the same config-0 model: 128
+    tokens after the 32-token prompt, wall clock of the whole call (prefill included)."""
+    import ctypes as C
+
+    from voxelengine import cuda as cu
+    from voxelengine import engine as ve
+    V = 49152
+    points = []
+    ctx = cu.Ctx(0)
+    L = cu.lib()
+    rng = np.random.default_rng(5)
+    for rows in (1, 64):
+        lg = ctx.to_device((rng.standard_normal((rows, V)) * 3).astype(np.float32))
+        u = ctx.to_device(rng.random(rows).astype(np.float32))
+        out, st = ctx.buffer(rows * 4), ctx.buffer(rows * 16)
+        for name, T, k, p in (("top-k 50 + top-p 0.95", 0.8, 50, 0.95), ("top-p 0.9 (whole vocabulary)", 1.0, 0, 0.9),
+                              ("temperature only", 1.0, 0, 1.0), ("logit stats", None, 0, 1.0)):
+            a = cu.SampleArgs()
+            a.logits, a.vocab, a.rows, a.stride = lg.ptr, V, rows, V
+            a.temperature, a.top_k, a.top_p, a.rep_penalty = (T or 1.0), k, p, 1.0
+            a.u, a.out = u.ptr, out.ptr
+
+            def call():
+                if T is None:
+                    ctx.call("opure_logit_stats", C.c_void_p(lg.ptr), V, rows, V, C.c_void_p(st.ptr))
+                else:
+                    ctx.sample_filtered(a)
+            for _ in range(5):
+                call()
+            e0, e1 = cu.Event(ctx), cu.Event(ctx)
+            e0.record()
+            for _ in range(50):
+                call()
+            e1.record()
+            ctx.sync()
+            points.append({"rows": rows, "kernel": name, "us_per_call": e0.elapsed_ms(e1) * 1e3 / 50})
+            e0.free()
+            e1.free()
+    ctx.close()
+    mp = model_dir()
+    budget = 128
+    gen = {}
+    with ve.Engine(mp, max_batch=1, max_len=PROMPT_LEN + budget + 8) as eng:
+        prompts = [ve.prompt(1, V, PROMPT_LEN)]
+        eng.generate(prompts, 8)
+        eng.sample_generate(prompts, 8, temperature=0.8, top_k=50, top_p=0.95, rep_penalty=1.1, seed=1)
+        t0 = time.perf_counter()
+        eng.generate(prompts, budget)
+        gen["greedy_tok_s"] = budget / (time.perf_counter() - t0)
+        t0 = time.perf_counter()
+        eng.sample_generate(prompts, budget, temperature=0.8, top_k=50, top_p=0.95, rep_penalty=1.1, seed=1)
+        gen["sampled_tok_s"] = budget / (time.perf_counter() - t0)
+    line = {"metric": "sampling kernels (us per call) and sampled generation tok/s (bs1, config 0)",
+            "unit": "us", "points": points, "generate": gen}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -784,7 +846,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-steps", type=int, default=128)
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", choices=["decode", "attn", "gemv", "spec", "cfg4", "tp"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "attn", "gemv", "spec", "cfg4", "tp", "sample"], default="decode")
     ap.add_argument("--path", choices=["auto", "layers", "unfused"], default="auto",
                     help="decode: step kernels (auto = one persistent kernel per step when eligible, "
                          "layers = three fused kernels per layer, unfused = per-op kernels)")
@@ -810,6 +872,8 @@ def main():
             run_gemv_sweep(args)
         elif args.workload == "spec":
             run_spec(args)
+        elif args.workload == "sample":
+            run_sample(args)
         elif args.workload == "cfg4":
             run_cfg4(args, world, rank, local)
         elif args.workload == "tp":

@@ -77,7 +77,7 @@ struct SampleShared {
     uint32_t bits[kMaxVocab / 32];      // tokens in the history (repetition penalty)
     unsigned long long hist[256];       // radix-select bins
     unsigned long long red[32];
-    unsigned long long scan[kThreads];  // per-thread segment masses (draw)
+    unsigned long long scan[64 + kThreads];  // warp totals, warp offsets, per-thread offsets (draw)
     uint32_t pick;
     uint32_t digit;
 };
@@ -103,25 +103,69 @@ __device__ unsigned long long radix_select(uint32_t n, unsigned long long floor_
         const unsigned long long hi_mask = shift == 56 ? 0ull : ~0ull << (shift + 8);
         for (uint32_t b = threadIdx.x; b < 256; b += blockDim.x) sm.hist[b] = 0ull;
         __syncthreads();
-        for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
-            const unsigned long long k = keyf(i);
-            if (k < floor_key || (k & hi_mask) != prefix) continue;
-            const unsigned long long m = measf(i, k);
-            if (m) atomicAdd(&sm.hist[(k >> shift) & 255u], m);
+        // Warp-aggregated bins: one shared atomic per distinct bin of a warp's 32 keys
+        // (most keys of a row share their leading bytes, so per-key atomics would queue).
+        const uint32_t lane = threadIdx.x & 31u;
+        for (uint32_t base = threadIdx.x - lane; base < n; base += blockDim.x) {
+            const uint32_t i = base + lane;
+            uint32_t bin = 0;
+            unsigned long long m = 0ull;
+            if (i < n) {
+                const unsigned long long k = keyf(i);
+                if (k >= floor_key && (k & hi_mask) == prefix) {
+                    m = measf(i, k);
+                    bin = uint32_t(k >> shift) & 255u;
+                }
+            }
+            uint32_t rem = __ballot_sync(0xffffffffu, m != 0ull);
+            while (rem) {
+                const uint32_t lead = __ffs(rem) - 1;
+                const uint32_t b = __shfl_sync(0xffffffffu, bin, lead);
+                const bool mine = m != 0ull && bin == b;
+                unsigned long long v = mine ? m : 0ull;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                if (lane == lead) atomicAdd(&sm.hist[b], v);
+                rem &= ~__ballot_sync(0xffffffffu, mine);
+            }
         }
         __syncthreads();
-        if (threadIdx.x == 0) {
-            unsigned long long cum = above;
-            uint32_t d = 256;  // not reached
-            for (int b = 255; b >= 0; --b) {
-                if (cum + sm.hist[b] >= target) {
-                    d = uint32_t(b);
-                    break;
-                }
-                cum += sm.hist[b];
+        if (threadIdx.x < 32) {
+            // Warp 0 scans the bins from the top: lane j owns bins 255-8j .. 248-8j.
+            unsigned long long h[8], own = 0ull;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                h[q] = sm.hist[255 - 8 * lane - q];
+                own += h[q];
             }
-            sm.digit = d;
-            sm.red[0] = cum;
+            unsigned long long incl = own;  // inclusive prefix over lanes 0..lane
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const unsigned long long t = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= uint32_t(o)) incl += t;
+            }
+            unsigned long long cum = above + incl - own;  // measure above this lane's bins
+            uint32_t d = 256;
+            unsigned long long cum_d = 0ull;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                if (d == 256 && cum + h[q] >= target) {
+                    d = 255 - 8 * lane - q;
+                    cum_d = cum;
+                }
+                cum += h[q];
+            }
+            // The first lane (from the top) whose bins reach the target decides.
+            const uint32_t hit = __ballot_sync(0xffffffffu, d != 256);
+            if (hit) {
+                const uint32_t src = __ffs(hit) - 1;
+                d = __shfl_sync(0xffffffffu, d, src);
+                cum_d = __shfl_sync(0xffffffffu, cum_d, src);
+            }
+            if (lane == 0) {
+                sm.digit = hit ? d : 256u;
+                sm.red[0] = cum_d;
+            }
         }
         __syncthreads();
         if (sm.digit == 256) {
@@ -202,24 +246,37 @@ __global__ void __launch_bounds__(kThreads) sample_filtered_kernel(opure_sample_
         };
         unsigned long long local = 0ull;
         for (uint32_t i = b0; i < b1; ++i) local += kept_mass(i);
-        sm.scan[threadIdx.x] = local;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            unsigned long long run = 0ull;
-            for (uint32_t t = 0; t < blockDim.x; ++t) {
-                const unsigned long long v = sm.scan[t];
-                sm.scan[t] = run;
-                run += v;
-            }
-            sm.red[0] = run;
-            sm.pick = 0xffffffffu;
+        // Exclusive scan of the segment masses in thread order: within warps, then over
+        // the warp totals.
+        const uint32_t lane = threadIdx.x & 31u, wid = threadIdx.x >> 5;
+        unsigned long long incl = local;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned long long t = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= uint32_t(o)) incl += t;
         }
+        if (lane == 31) sm.scan[wid] = incl;
+        if (threadIdx.x == 0) sm.pick = 0xffffffffu;
+        __syncthreads();
+        if (wid == 0) {
+            const unsigned long long wt = lane < blockDim.x / 32 ? sm.scan[lane] : 0ull;
+            unsigned long long wi = wt;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const unsigned long long t = __shfl_up_sync(0xffffffffu, wi, o);
+                if (lane >= uint32_t(o)) wi += t;
+            }
+            sm.scan[32 + lane] = wi - wt;  // mass of the warps before this one
+            if (lane == 31) sm.red[0] = wi;
+        }
+        __syncthreads();
+        sm.scan[64 + threadIdx.x] = sm.scan[32 + wid] + incl - local;
         __syncthreads();
         const unsigned long long total = sm.red[0];
         const double uu = double(a.u[row]);
         unsigned long long thr = (unsigned long long)floor(uu * double(total));
         if (thr >= total) thr = total - 1;  // u in [0, 1): only reachable through rounding
-        unsigned long long c = sm.scan[threadIdx.x];
+        unsigned long long c = sm.scan[64 + threadIdx.x];
         if (total && c <= thr && c + local > thr) {
             for (uint32_t i = b0; i < b1; ++i) {
                 c += kept_mass(i);

@@ -99,6 +99,18 @@ def test_batch_beyond_one_gemv_pass(models, small):
         assert_tokens(out[b], want, margins)
 
 
+@pytest.mark.parametrize("n", [16, 40])
+def test_tensor_core_batch_matches_oracle(models, small, n):
+    # n >= 16 vectors take the per-layer kernels with the tensor-core GEMV path
+    # (pack + tcgen05 GEMM per projection), ragged prompts.
+    prompts = [ve.prompt(300 + s, SMALL["vocab"], 3 + s % 7) for s in range(n)]
+    with ve.Engine(models["small"], max_batch=n, max_len=40) as eng:
+        out, _ = eng.generate(prompts, 12)
+    for b in range(0, n, 3):
+        want, margins = small.generate(prompts[b], 12)
+        assert_tokens(out[b], want, margins)
+
+
 def test_host_driven_decode_steps(models):
     # Prefill + DecodeStep with the token/position copied in and the argmax read back
     # each step (Opure_VoxelEngine.cpp:765-800) equals the device-driven loop.
