@@ -138,6 +138,12 @@ typedef struct opure_kv_layout {
     uint32_t page_size;        /* tokens per page: 16, 32, 64 or 128              */
     uint32_t n_kv;             /* KV heads                                        */
     uint32_t head_dim;         /* 64 or 128                                       */
+    /* Sliding window (0: off). The first `ring` entries of a sequence's table row are used
+     * as a ring: position p lives in page page_table[seq][(p / page_size) % ring], and the
+     * attention of a query at position p covers positions [window_begin(p), p] with
+     * window_begin(p) = max(0, p / page_size - ring + 1) * page_size, i.e. the last
+     * ring - 1 whole pages and the current one; older pages are recycled in place. */
+    uint32_t ring;
 } opure_kv_layout;
 
 /* Seeded synthetic context: fills positions [0, len) of sequence slots slot0 ..
@@ -332,6 +338,7 @@ typedef struct opure_fused_step {
                                           (row k < 3 n_layers: arrival at / release from grid
                                           barrier k; row 3 n_layers: [1] = kernel start; row
                                           3 n_layers + 1: [0] = end), rewritten every step */
+    uint32_t kv_ring;                  /* sliding window of the cache (opure_kv_layout.ring) */
 } opure_fused_step;
 /* AUTO: when the model fits (head_dim 64, <= 48 layers, each phase's work in one wave of
  * CTAs, a layer's weight slices of one CTA double-buffered in shared memory) and `sync` is

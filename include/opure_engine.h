@@ -39,6 +39,11 @@ typedef struct opure_engine_options {
     uint32_t prefill_chunk;   /* >0: prefill prompts as steps of up to this many token
                                  vectors (tensor-core GEMMs, causal within the step)
                                  instead of one token per step (0: the reference's way) */
+    uint32_t kv_window;       /* >0: sliding-window KV cache of this many tokens, a multiple
+                                 of page_size (>= 2 pages): each sequence keeps that many
+                                 tokens of pages as a ring (opure_kv_layout.ring) and a
+                                 position attends to the last kv_window / page_size - 1 whole
+                                 pages and its own; 0: every position up to max_len */
 } opure_engine_options;
 
 enum {

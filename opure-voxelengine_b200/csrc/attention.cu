@@ -52,8 +52,9 @@ __global__ void __launch_bounds__(kWarps * 32) attn_kernel(AttnParams p) {
 
     const int32_t sidx = p.seq[i];
     const int32_t len = p.seq_len[i] + int32_t(j);
-    const uint32_t t_begin = split * p.split_tokens;
-    const uint32_t t_end = min(uint32_t(max(len, 0)), t_begin + p.split_tokens);
+    const uint32_t t_split = split * p.split_tokens;
+    const uint32_t t_end = min(uint32_t(max(len, 0)), t_split + p.split_tokens);
+    const uint32_t t_begin = max(t_split, window_begin(len - 1, p.kv.page_size, p.kv.ring));
 
     float qv[G][AttnShape<HD>::E];
     load_q_slice<HD, G>(p.q + size_t(entry) * p.n_heads * HD, g, p.scale_log2, qv);
@@ -61,7 +62,7 @@ __global__ void __launch_bounds__(kWarps * 32) attn_kernel(AttnParams p) {
     st.init();
     KvView kv{reinterpret_cast<const __half *>(p.kv.pool),
               p.kv.page_table + size_t(max(sidx, 0)) * p.kv.max_pages,
-              p.kv.max_pages, p.kv.n_pages, p.kv.page_size, n_kv, g, sidx >= 0};
+              p.kv.max_pages, p.kv.n_pages, p.kv.page_size, n_kv, g, sidx >= 0, p.kv.ring};
     attend_range<HD, G>(st, qv, kv, t_begin, t_end, warp, kWarps, p.st);
     merge_lane_groups<HD, G>(st);
 
@@ -200,7 +201,7 @@ extern "C" opure_status opure_attention(opure_ctx *ctx, const opure_attn_args *a
     if (s) return s;
     if (!a || !a->q || !a->out || !a->seq || !a->seq_len || !a->scratch) return OPURE_ERR_INVALID_ARG;
     const opure_kv_layout &kv = a->kv;
-    if (!kv.pool || !kv.page_table || !kv.n_kv || !kv.page_size || !kv.max_pages)
+    if (!kv.pool || !kv.page_table || !kv.n_kv || !kv.page_size || !kv.max_pages || kv.ring > kv.max_pages)
         return OPURE_ERR_INVALID_ARG;
     if (a->n_heads % kv.n_kv) return OPURE_ERR_INVALID_ARG;
     if (a->n == 0 || a->n_q == 0) return OPURE_OK;
@@ -271,7 +272,7 @@ extern "C" opure_status opure_attention_static(opure_ctx *ctx, const opure_attn_
     if (s) return s;
     if (!a || !a->q || !a->out || !a->seq || !a->seq_len) return OPURE_ERR_INVALID_ARG;
     const opure_kv_layout &kv = a->kv;
-    if (!kv.pool || !kv.page_table || !kv.n_kv || !kv.page_size || !kv.max_pages)
+    if (!kv.pool || !kv.page_table || !kv.n_kv || !kv.page_size || !kv.max_pages || kv.ring > kv.max_pages)
         return OPURE_ERR_INVALID_ARG;
     if (a->n_heads % kv.n_kv) return OPURE_ERR_INVALID_ARG;
     if (a->n == 0 || a->n_q == 0) return OPURE_OK;

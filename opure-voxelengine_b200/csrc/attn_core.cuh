@@ -57,7 +57,9 @@ struct KvView {
     const int32_t *pt;         // this sequence's page-table row
     uint32_t max_pages, n_pages, page_size, n_kv, g;
     bool ok;                   // false: the sequence index was invalid
+    uint32_t ring;             // sliding window: table entries used as a ring (0: off)
 };
+
 
 // Rows [0, n) of one sequence's keys and values for one kv head, copied into shared
 // memory ([n][HD] each); tokens from n on are read from the pool.
@@ -118,7 +120,7 @@ __device__ __forceinline__ void attend_range(AttnState<HD, G> &st, const float (
                 continue;
             }
             if (valid[r]) {
-                const uint32_t lp = t / kv.page_size;
+                const uint32_t lp = ring_slot(t / kv.page_size, kv.ring);
                 const int32_t page = lp < kv.max_pages ? kv.pt[lp] : -1;
                 if (page < 0 || uint32_t(page) >= kv.n_pages) {
                     report(status, OPURE_ERR_DEVICE_BOUNDS, 10, uint32_t(page));

@@ -138,6 +138,15 @@ __device__ __forceinline__ long long to_fix(float v) {
     return __double2ll_rn(double(v) * kFixScale);
 }
 
+// Sliding-window KV cache (opure_kv_layout.ring): the table entry of logical page lp, and
+// the first position a query at position p attends to.
+__device__ __forceinline__ uint32_t ring_slot(uint32_t lp, uint32_t ring) { return ring ? lp % ring : lp; }
+__device__ __forceinline__ uint32_t window_begin(int32_t p, uint32_t page_size, uint32_t ring) {
+    if (!ring || p < 0) return 0u;
+    const uint32_t lp = uint32_t(p) / page_size;
+    return lp + 1 > ring ? (lp + 1 - ring) * page_size : 0u;
+}
+
 }  // namespace opure
 
 // Host-side error propagation inside the ABI implementation.

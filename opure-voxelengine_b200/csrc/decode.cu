@@ -18,6 +18,7 @@ struct KvParams {
     uint16_t *pool;
     const int32_t *page_table;
     uint32_t n_pages, max_pages, page_size;
+    uint32_t ring;  // sliding window (opure_kv_layout.ring)
 };
 
 // x[v] = base[v] + delta[v] * 2^-32 (rounded to fp32 once, as the reference rounds its fp32
@@ -289,7 +290,7 @@ __device__ __forceinline__ void smem_dot_ptrs(const uint8_t *const (&rows)[R], u
 // Element offset of (seq, pos, K|V, kv head) row inside a layer's pool, or -1 (reported).
 __device__ __forceinline__ long long kv_offset(const KvParams &kv, uint32_t n_kv, uint32_t hd, int32_t seq,
                                                int32_t pos, uint32_t sel, uint32_t head, DeviceStatus *st) {
-    const uint32_t lp = uint32_t(pos) / kv.page_size;
+    const uint32_t lp = ring_slot(uint32_t(pos) / kv.page_size, kv.ring);
     if (seq < 0 || pos < 0 || lp >= kv.max_pages) {
         report(st, OPURE_ERR_DEVICE_BOUNDS, 30, uint32_t(pos));
         return -1;
@@ -471,8 +472,9 @@ __global__ void __launch_bounds__(kBThreads) attn_oproj_kernel(AttnOArgs a) {
         const int32_t s = s_seq[v];
         KvView kv{reinterpret_cast<const __half *>(a.kv.pool),
                   stage_pt ? s_pt[v] : a.kv.page_table + size_t(max(s, 0)) * a.kv.max_pages,
-                  a.kv.max_pages, a.kv.n_pages, a.kv.page_size, a.n_kv, g, s >= 0};
-        attend_range<HD, G, false, true>(st, qv, kv, 0, uint32_t(max(s_pos[v] + 1, 0)), warp, kBWarps, a.st);
+                  a.kv.max_pages, a.kv.n_pages, a.kv.page_size, a.n_kv, g, s >= 0, a.kv.ring};
+        attend_range<HD, G, false, true>(st, qv, kv, window_begin(s_pos[v], a.kv.page_size, a.kv.ring),
+                                         uint32_t(max(s_pos[v] + 1, 0)), warp, kBWarps, a.st);
         merge_lane_groups<HD, G>(st);
         store_warp_state<HD, G, kBWarps>(st, ws, warp);
         __syncthreads();
@@ -682,7 +684,7 @@ struct PersistArgs {
     const __half *final_norm;
     const uint8_t *lm_head;
     const int32_t *page_table;
-    uint32_t n_pages, max_pages, page_size;
+    uint32_t n_pages, max_pages, page_size, kv_ring;
     const int32_t *seq, *pos;
     float *base0, *base1;
     long long *delta0, *delta1;
@@ -896,7 +898,8 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
         int32_t first = s_pos[threadIdx.x];
         for (int u = 0; u < NV; ++u)
             if (s_seq[u] == sq) first = min(first, s_pos[u]);
-        uint32_t n = (sq >= 0 && stage_pt && sh.nb && first > 0) ? min(uint32_t(first), p.kv_cap) : 0u;
+        // (Not with a sliding window: the staged rows would start at the window.)
+        uint32_t n = (sq >= 0 && stage_pt && sh.nb && first > 0 && !p.kv_ring) ? min(uint32_t(first), p.kv_cap) : 0u;
         for (uint32_t i = 0; i * p.page_size < n; ++i) {
             const int32_t pg = i < p.max_pages ? s_pt[threadIdx.x][i] : -1;
             if (pg < 0 || uint32_t(pg) >= p.n_pages) {
@@ -956,7 +959,7 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
         if (a_r >= qrows) {
             const bool is_k = a_r < qrows + krows;
             const uint32_t rr = is_k ? a_r - qrows : a_r - qrows - krows;
-            const KvParams k0{nullptr, p.page_table, p.n_pages, p.max_pages, p.page_size};
+            const KvParams k0{nullptr, p.page_table, p.n_pages, p.max_pages, p.page_size, p.kv_ring};
             const long long off = kv_offset(k0, p.n_kv, HD, sq, ps, is_k ? 0 : 1, rr / HD, p.st);
             if (off >= 0) a_kv = off + rr % HD;
         }
@@ -1006,7 +1009,7 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
         if (has_bytes && !p_wait_slot(&full[L & 1], (L >> 1) & 1u, p, &s_ok)) goto abort;
         ++waited;
         if (L + 1 == p.n_layers) lm_fill(1);  // the other slot is free for the rest of the step
-        const KvParams kvp{ly.kv_pool, p.page_table, p.n_pages, p.max_pages, p.page_size};
+        const KvParams kvp{ly.kv_pool, p.page_table, p.n_pages, p.max_pages, p.page_size, p.kv_ring};
 
         // ---- A: RMSNorm + q;k;v + RoPE + KV append ----------------------------------
         if (sh.na) {
@@ -1082,12 +1085,12 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
                 const int32_t s = s_seq[v];
                 KvView kv{reinterpret_cast<const __half *>(ly.kv_pool),
                           stage_pt ? s_pt[v] : p.page_table + size_t(max(s, 0)) * p.max_pages,
-                          p.max_pages, p.n_pages, p.page_size, p.n_kv, sh.g, s >= 0};
+                          p.max_pages, p.n_pages, p.page_size, p.n_kv, sh.g, s >= 0, p.kv_ring};
                 const KvStage stg{reinterpret_cast<const __half *>(kvs + size_t(v) * 2 * kv_vbytes),
                                   reinterpret_cast<const __half *>(kvs + size_t(v) * 2 * kv_vbytes + kv_vbytes),
                                   s_nst[v]};
-                attend_range<HD, G, true, true, true>(st, qv, kv, 0, uint32_t(max(s_pos[v] + 1, 0)), warp, kPWarps,
-                                                      p.st, stg);
+                attend_range<HD, G, true, true, true>(st, qv, kv, window_begin(s_pos[v], p.page_size, p.kv_ring),
+                                                      uint32_t(max(s_pos[v] + 1, 0)), warp, kPWarps, p.st, stg);
                 merge_lane_groups<HD, G>(st);
                 store_warp_state<HD, G, kPWarps>(st, ws, warp);
                 __syncthreads();
@@ -1294,7 +1297,7 @@ template <int NV, int HD, int G>
 opure_status run_step(opure_ctx *ctx, const opure_fused_step &s) {
     const uint32_t h = s.hidden, hd = s.head_dim;
     const uint32_t qkv_rows = (s.n_heads + 2 * s.n_kv) * hd;
-    const KvParams kvp0{nullptr, s.page_table, s.n_pages, s.max_pages, s.page_size};
+    const KvParams kvp0{nullptr, s.page_table, s.n_pages, s.max_pages, s.page_size, s.kv_ring};
     const size_t a_smem = ((kARows * h * 2 + 127) & ~size_t(127)) + (NV * h + 33 * NV) * 4;
     // B: about one CTA per SM over (kv head, o_proj row block).
     const uint32_t rb_target = std::max<uint32_t>(1, uint32_t(ctx->sm_count) / s.n_kv);
@@ -1413,6 +1416,7 @@ opure_status run_persistent(opure_ctx *ctx, const opure_fused_step &s, bool *ran
     p.n_pages = s.n_pages;
     p.max_pages = s.max_pages;
     p.page_size = s.page_size;
+    p.kv_ring = s.kv_ring;
     p.seq = s.seq;
     p.pos = s.pos;
     p.base0 = s.x;
@@ -1494,7 +1498,8 @@ extern "C" opure_status opure_decode_fused(opure_ctx *ctx, const opure_fused_ste
     if (!s || !s->layers || !s->final_norm || !s->lm_head || !s->page_table || !s->seq || !s->pos || !s->x ||
         !s->base1 || !s->delta0 || !s->delta1 || !s->q || !s->keys || !s->n_kv || !s->n_layers)
         return OPURE_ERR_INVALID_ARG;
-    if (s->n_heads % s->n_kv || s->hidden % 8 || s->inter == 0) return OPURE_ERR_INVALID_ARG;
+    if (s->n_heads % s->n_kv || s->hidden % 8 || s->inter == 0 || s->kv_ring > s->max_pages)
+        return OPURE_ERR_INVALID_ARG;
     if (s->nvec == 0) return OPURE_OK;
     const uint32_t G = s->n_heads / s->n_kv;
     for (uint32_t L = 0; L < s->n_layers; ++L) {

@@ -125,7 +125,7 @@ __global__ void rope_kv_kernel(const float *qkv, uint32_t stride, float *q_out, 
         qd[2 * pair + 1] = r1;
         return;
     }
-    const uint32_t lp = uint32_t(p) / kv.page_size, slot = uint32_t(p) % kv.page_size;
+    const uint32_t lp = ring_slot(uint32_t(p) / kv.page_size, kv.ring), slot = uint32_t(p) % kv.page_size;
     if (p < 0 || s < 0 || lp >= kv.max_pages) {
         report(st, OPURE_ERR_DEVICE_BOUNDS, 2, uint32_t(p));
         return;

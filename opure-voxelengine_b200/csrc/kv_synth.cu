@@ -77,7 +77,8 @@ extern "C" opure_status opure_kv_synth(opure_ctx *ctx, const opure_kv_layout *kv
     if (s) return s;
     if (!kv || !kv->pool || !kv->page_table || !kv->page_size || !kv->n_kv || !kv->head_dim)
         return OPURE_ERR_INVALID_ARG;
-    if (kv->head_dim % 8 || len > 65536 || uint64_t(len) > uint64_t(kv->max_pages) * kv->page_size)
+    if (kv->head_dim % 8 || len > 65536 || uint64_t(len) > uint64_t(kv->max_pages) * kv->page_size ||
+        (kv->ring && uint64_t(len) > uint64_t(kv->ring) * kv->page_size))
         return OPURE_ERR_INVALID_ARG;
     if (n_slots == 0 || len == 0) return OPURE_OK;
     SynthParams p{kv->pool, kv->page_table, kv->n_pages, kv->max_pages, kv->page_size, kv->n_kv, kv->head_dim,

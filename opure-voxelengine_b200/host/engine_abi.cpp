@@ -67,6 +67,7 @@ opure::engine::EngineOptions ToOptions(const opure_engine_options *o) {
         opts.path = o->path;
         opts.phaseTrace = o->phase_trace != 0;
         opts.prefillChunk = o->prefill_chunk;
+        opts.kvWindow = o->kv_window;
     }
     return opts;
 }

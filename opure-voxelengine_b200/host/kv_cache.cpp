@@ -12,11 +12,12 @@ PagedKvCache::~PagedKvCache() { Destroy(); }
 
 void PagedKvCache::Create(opure_ctx *ctx, const graph::ModelConfig &cfg, uint32_t page_size,
                           uint32_t n_pages, uint32_t max_seqs, uint32_t max_pages_per_seq,
-                          uint64_t shuffle_seed) {
+                          uint64_t shuffle_seed, uint32_t ring) {
     Destroy();
     OPURE_CHECK(page_size == 16 || page_size == 32 || page_size == 64 || page_size == 128,
                 "KV page size must be 16, 32, 64 or 128 tokens");
     OPURE_CHECK(n_pages > 0 && max_seqs > 0 && max_pages_per_seq > 0, "empty KV cache");
+    OPURE_CHECK(ring <= max_pages_per_seq, "KV window longer than a table row");
     ctx_ = ctx;
     layers_ = cfg.numLayers;
     nKv_ = cfg.numKvHeads;
@@ -25,6 +26,7 @@ void PagedKvCache::Create(opure_ctx *ctx, const graph::ModelConfig &cfg, uint32_
     nPages_ = n_pages;
     maxSeqs_ = max_seqs;
     maxPages_ = max_pages_per_seq;
+    ring_ = ring;
     poolBytes_ = uint64_t(n_pages) * 2 * nKv_ * page_size * headDim_ * 2;
     OPURE_CUDA_CHECK(opure_alloc(ctx_, poolBytes_ * layers_, &pools_));
     OPURE_CUDA_CHECK(opure_fill(ctx_, pools_, 0, poolBytes_ * layers_));
@@ -60,7 +62,8 @@ void PagedKvCache::Destroy() {
 
 bool PagedKvCache::Reserve(uint32_t seq, uint32_t tokens) {
     OPURE_CHECK(seq < maxSeqs_, "KV sequence slot out of range");
-    const uint32_t need = (tokens + pageSize_ - 1) / pageSize_;
+    uint32_t need = (tokens + pageSize_ - 1) / pageSize_;
+    if (ring_) need = std::min(need, ring_);
     if (need > maxPages_) return false;
     if (need <= mapped_[seq]) return true;
     if (need - mapped_[seq] > free_.size()) return false;
@@ -88,6 +91,11 @@ void PagedKvCache::Release(uint32_t seq) { Truncate(seq, 0); }
 
 uint32_t PagedKvCache::MappedPages(uint32_t seq) const { return seq < maxSeqs_ ? mapped_[seq] : 0; }
 
+bool PagedKvCache::Covers(uint32_t seq, uint32_t pos) const {
+    if (seq >= maxSeqs_) return false;
+    return (ring_ && mapped_[seq] == ring_) || pos < mapped_[seq] * pageSize_;
+}
+
 void PagedKvCache::SyncTable() {
     if (!dirty_ || !ctx_) return;
     OPURE_CUDA_CHECK(opure_h2d(ctx_, dTable_, table_.data(), table_.size() * sizeof(int32_t)));
@@ -108,6 +116,7 @@ opure_kv_layout PagedKvCache::Layout(uint32_t layer) const {
     l.page_size = pageSize_;
     l.n_kv = nKv_;
     l.head_dim = headDim_;
+    l.ring = ring_;
     return l;
 }
 

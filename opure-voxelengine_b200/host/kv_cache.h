@@ -9,6 +9,12 @@
 // mapping logical page -> physical page. Pages come from a free list (optionally shuffled
 // with a seeded Fisher-Yates permutation, so tests exercise non-contiguous tables);
 // truncation (speculative rollback) and release return pages to it.
+//
+// Sliding window (ring > 0): a sequence holds at most `ring` pages, used as a ring (position
+// p in table entry (p / page_size) % ring, opure_kv_layout.ring); when it moves past them it
+// overwrites its own oldest page in place instead of mapping a new one. This replaces the
+// reference's eviction, which shifts the whole cache by one position with a memmove
+// dispatch per layer (EvictOldestKV, Opure_VoxelEngine.cpp:721-763; Opure_Memmove.usf).
 #pragma once
 
 #include <cstdint>
@@ -27,12 +33,16 @@ public:
     PagedKvCache &operator=(const PagedKvCache &) = delete;
 
     void Create(opure_ctx *ctx, const graph::ModelConfig &cfg, uint32_t page_size, uint32_t n_pages,
-                uint32_t max_seqs, uint32_t max_pages_per_seq, uint64_t shuffle_seed);
+                uint32_t max_seqs, uint32_t max_pages_per_seq, uint64_t shuffle_seed, uint32_t ring = 0);
     void Destroy();
 
-    // Maps pages for positions [0, tokens) of `seq`. Returns false (nothing changed) when
-    // the free list or the table row is too short.
+    // Maps pages for positions [0, tokens) of `seq` (with a window: at most `ring` pages,
+    // which then hold any position). Returns false (nothing changed) when the free list or
+    // the table row is too short.
     bool Reserve(uint32_t seq, uint32_t tokens);
+    // Whether position `pos` of `seq` has a mapped page.
+    bool Covers(uint32_t seq, uint32_t pos) const;
+    uint32_t Ring() const { return ring_; }
     void Truncate(uint32_t seq, uint32_t tokens);  // unmap pages wholly past `tokens`
     void Release(uint32_t seq);
     void SyncTable();                              // upload the table when it changed
@@ -51,7 +61,7 @@ public:
 private:
     opure_ctx *ctx_ = nullptr;
     uint32_t layers_ = 0, nKv_ = 0, headDim_ = 0;
-    uint32_t pageSize_ = 0, nPages_ = 0, maxSeqs_ = 0, maxPages_ = 0;
+    uint32_t pageSize_ = 0, nPages_ = 0, maxSeqs_ = 0, maxPages_ = 0, ring_ = 0;
     uint64_t poolBytes_ = 0;
     void *pools_ = nullptr;            // layers_ * poolBytes_
     int32_t *dTable_ = nullptr;        // [maxSeqs_][maxPages_]

@@ -51,6 +51,9 @@ std::vector<std::vector<uint32_t>> SpecGenerate(VoxelEngine &target, VoxelEngine
                                                 const SpecOptions &o, SpecStats *stats,
                                                 std::vector<int32_t> *acceptLog) {
     OPURE_CHECK(target.IsReady() && draft.IsReady(), "engine used before Initialize");
+    // A rolled-back position may need a page its ring has already recycled.
+    OPURE_CHECK(!target.Options().kvWindow && !draft.Options().kvWindow,
+                "speculative decoding does not run with a sliding-window KV cache");
     OPURE_CHECK(target.Ctx() == draft.Ctx(), "the draft engine must share the target engine's ctx");
     const uint32_t V = target.Model().vocabSize;
     OPURE_CHECK(draft.Model().vocabSize == V, "draft and target vocabularies differ");

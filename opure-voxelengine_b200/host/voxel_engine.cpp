@@ -82,10 +82,14 @@ void VoxelEngine::Initialize(const std::string &modelDir, const EngineOptions &o
     graph_.UploadWeights(ctx_, weights_);
 
     maxLen_ = opts.maxLen ? std::min(opts.maxLen, cfg.maxPositions) : std::min(cfg.maxPositions, 4096u);
-    const uint32_t pagesPerSeq = (maxLen_ + opts.pageSize - 1) / opts.pageSize;
+    OPURE_CHECK(opts.kvWindow % opts.pageSize == 0, "the KV window must be a multiple of the page size");
+    const uint32_t ring = opts.kvWindow / opts.pageSize;
+    OPURE_CHECK(ring == 0 || ring >= 2, "the KV window must span at least two pages");
+    const uint32_t pagesPerSeq = ring ? ring : (maxLen_ + opts.pageSize - 1) / opts.pageSize;
     graph::ModelConfig kvCfg = cfg;
     kvCfg.numKvHeads = graph_.Local().kvHeads;  // a shard caches only its own KV heads
-    kv_.Create(ctx_, kvCfg, opts.pageSize, pagesPerSeq * opts.maxBatch, opts.maxBatch, pagesPerSeq, opts.pageSeed);
+    kv_.Create(ctx_, kvCfg, opts.pageSize, pagesPerSeq * opts.maxBatch, opts.maxBatch, pagesPerSeq, opts.pageSeed,
+               ring);
     maxVec_ = std::max(opts.maxBatch, opts.prefillChunk);
     AllocBuffers();
     seqLen_ = 0;
@@ -305,6 +309,7 @@ void VoxelEngine::RecordStep(uint32_t n, bool logits) {
         fs.n_pages = kv_.NumPages();
         fs.max_pages = kv_.MaxPages();
         fs.page_size = kv_.PageSize();
+        fs.kv_ring = kv_.Ring();
         fs.seq = buf_.seq;
         fs.pos = buf_.pos;
         fs.x = buf_.x;
@@ -384,8 +389,7 @@ void VoxelEngine::SetPositions(const int32_t *positions, uint32_t n) {
     OPURE_CHECK(n >= 1 && n <= opts_.maxBatch, "batch exceeds maxBatch");
     for (uint32_t v = 0; v < n; ++v) {
         OPURE_CHECK(positions[v] >= 0 && uint32_t(positions[v]) < maxLen_, "position exceeds maxLen");
-        OPURE_CHECK(uint32_t(positions[v]) < kv_.MappedPages(v) * kv_.PageSize(),
-                    "position beyond the sequence's reserved KV pages");
+        OPURE_CHECK(kv_.Covers(v, uint32_t(positions[v])), "position beyond the sequence's reserved KV pages");
     }
     // Pageable source: the copy is staged before opure_h2d returns, so the caller's
     // array may be reused immediately.
@@ -446,6 +450,10 @@ uint32_t VoxelEngine::PrefillChunks(const std::vector<std::vector<uint32_t>> &pr
     std::vector<int32_t> seq, pos, tok;
     std::vector<int32_t> known(n), start(n);
     for (uint32_t s = 0; s < n; ++s) {
+        // With a KV window every prompt position must still have its own page: a step's
+        // later vectors would otherwise overwrite pages its earlier vectors attend to.
+        OPURE_CHECK(!kv_.Ring() || prompts[s].size() <= kv_.Ring() * kv_.PageSize(),
+                    "chunked prefill needs the prompt to fit the KV window");
         for (uint32_t t = 0; t < prompts[s].size(); ++t) {
             seq.push_back(int32_t(s));
             pos.push_back(int32_t(t));
@@ -574,8 +582,7 @@ void VoxelEngine::SetAutoVectors(const int32_t *pos, const int32_t *known, uint3
     for (uint32_t v = 0; v < n; ++v) {
         OPURE_CHECK(pos[v] >= 0 && uint32_t(pos[v]) < maxLen_, "position exceeds the engine's maxLen");
         OPURE_CHECK(known[v] >= 0 && uint32_t(known[v]) <= maxLen_, "known length exceeds the engine's maxLen");
-        OPURE_CHECK(uint32_t(pos[v]) < kv_.MappedPages(v) * kv_.PageSize(),
-                    "position beyond the sequence's reserved KV pages");
+        OPURE_CHECK(kv_.Covers(v, uint32_t(pos[v])), "position beyond the sequence's reserved KV pages");
         seq[v] = int32_t(v);
     }
     OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.seq, seq.data(), n * 4));
@@ -723,6 +730,7 @@ void VoxelEngine::PoisonBanks(float fill) {
 void VoxelEngine::LoadKv(uint32_t seq, const uint16_t *kvData, uint32_t len) {
     const graph::ModelConfig &c = graph_.Config();
     OPURE_CHECK(seq < opts_.maxBatch && len <= maxLen_, "LoadKv: sequence or length out of range");
+    OPURE_CHECK(!kv_.Ring() || len <= kv_.Ring() * kv_.PageSize(), "LoadKv: context longer than the KV window");
     OPURE_CHECK(kv_.Reserve(seq, std::max(len, 1u)), "KV cache has no room for the sequence");
     kv_.SyncTable();
     const uint32_t P = kv_.PageSize(), hd = c.HeadDim(), nkv = c.numKvHeads;

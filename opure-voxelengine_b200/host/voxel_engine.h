@@ -48,6 +48,10 @@ struct EngineOptions {
     bool phaseTrace = false;        // persistent kernel: record per-CTA phase timestamps
     uint32_t prefillChunk = 0;      // >0: prompts prefilled as steps of up to this many token
                                     // vectors (tensor-core GEMMs) instead of one token per step
+    uint32_t kvWindow = 0;          // >0: sliding-window KV cache of this many tokens (a multiple
+                                    // of pageSize): a sequence keeps kvWindow / pageSize pages as a
+                                    // ring, and a position attends to the last kvWindow / pageSize - 1
+                                    // whole pages and its own
 };
 
 struct GenerateResult {

@@ -32,7 +32,7 @@ class OpureError(RuntimeError):
 
 class KvLayout(C.Structure):
     _fields_ = [("pool", P), ("page_table", P), ("n_pages", u32), ("max_pages", u32),
-                ("page_size", u32), ("n_kv", u32), ("head_dim", u32)]
+                ("page_size", u32), ("n_kv", u32), ("head_dim", u32), ("ring", u32)]
 
 
 class AttnArgs(C.Structure):

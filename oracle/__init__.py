@@ -71,6 +71,7 @@ def lib() -> C.CDLL:
             "orc_state_free": (None, [P]),
             "orc_state_len": (u32, [P]),
             "orc_state_truncate": (None, [P, u32]),
+            "orc_state_set_window": (None, [P, u32, u32]),
             "orc_state_load_kv": (i32, [P, P, u32]),
             "orc_forward": (i32, [P, P, u32, P, P]),
             "orc_generate": (i32, [P, P, u32, u32, u32, P, P]),
@@ -347,6 +348,10 @@ class State:
 
     def truncate(self, n: int):
         lib().orc_state_truncate(self.h, n)
+
+    def set_window(self, page_size: int, ring: int):
+        """Sliding window of `ring` pages (orc_state_set_window); 0 turns it off."""
+        lib().orc_state_set_window(self.h, page_size, ring)
 
     def load_kv(self, kv: np.ndarray, length: int):
         kv = np.ascontiguousarray(kv, np.uint16)

@@ -610,6 +610,7 @@ struct orc_model {
 
 struct orc_state {
     uint32_t max_pos = 0, len = 0;
+    uint32_t win_page = 0, win_ring = 0;  // sliding window (orc_state_set_window)
     uint32_t L = 0, nKV = 0, hd = 0;
     std::vector<uint16_t> kv;  // [L][2][nKV][max_pos][hd]
     uint16_t *at(uint32_t l, uint32_t kvsel, uint32_t g, uint32_t pos) {
@@ -738,6 +739,11 @@ orc_state *orc_state_create(const orc_model *m, uint32_t max_pos) {
 
 void orc_state_free(orc_state *s) { delete s; }
 uint32_t orc_state_len(const orc_state *s) { return s ? s->len : 0; }
+void orc_state_set_window(orc_state *s, uint32_t page_size, uint32_t ring) {
+    if (!s) return;
+    s->win_page = ring ? page_size : 0;
+    s->win_ring = ring;
+}
 void orc_state_truncate(orc_state *s, uint32_t len) {
     if (s && len < s->len) s->len = len;
 }
@@ -784,14 +790,18 @@ int orc_forward(const orc_model *m, orc_state *s, uint32_t tok, float *logits, f
                 vd[d] = f32_to_f16(v[g2 * hd + d]);
             }
         }
-        const uint32_t seq_len = t + 1;
+        // Positions [w0, t]: all of them, or under a sliding window of win_ring pages of
+        // win_page tokens the last win_ring - 1 whole pages and the current one.
+        uint32_t w0 = 0;
+        if (s->win_ring && t / s->win_page + 1 > s->win_ring) w0 = (t / s->win_page + 1 - s->win_ring) * s->win_page;
+        const uint32_t seq_len = t + 1 - w0;
         parallel_for(c.heads, uint64_t(seq_len) * hd * 2, [&](int64_t hq) {
             std::vector<double> scores;
             {
                 const uint32_t kvh = uint32_t(hq) / group;
                 attend_head(q.data() + size_t(hq) * hd, seq_len, hd, c.attn_scale,
-                            [&](uint32_t sp) { return static_cast<const orc_state *>(s)->at(Li, 0, kvh, sp); },
-                            [&](uint32_t sp) { return static_cast<const orc_state *>(s)->at(Li, 1, kvh, sp); },
+                            [&](uint32_t sp) { return static_cast<const orc_state *>(s)->at(Li, 0, kvh, w0 + sp); },
+                            [&](uint32_t sp) { return static_cast<const orc_state *>(s)->at(Li, 1, kvh, w0 + sp); },
                             attn.data() + size_t(hq) * hd, scores);
             }
         });

@@ -175,6 +175,11 @@ orc_state *orc_state_create(const orc_model *m, uint32_t max_pos);
 void       orc_state_free(orc_state *s);
 uint32_t   orc_state_len(const orc_state *s);
 void       orc_state_truncate(orc_state *s, uint32_t len);
+/* Sliding window (parity unpinned: the reference's eviction, EvictOldestKV in
+ * Opure_VoxelEngine.cpp:721-763, shifts the cache by one token and is never reached):
+ * the token at position t attends to positions [w0, t], w0 = max(0, t / page_size -
+ * ring + 1) * page_size, as opure_kv_layout.ring. ring 0: off. */
+void       orc_state_set_window(orc_state *s, uint32_t page_size, uint32_t ring);
 /* Loads `len` positions of precomputed fp16 K/V, laid out [L][2][nKV][len][hd]. */
 int        orc_state_load_kv(orc_state *s, const uint16_t *kv, uint32_t len);
 

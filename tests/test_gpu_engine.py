@@ -304,3 +304,57 @@ def test_chunked_prefill_then_host_steps(models, small):
             tok = int(eng.decode_step([tok], [len(p) + i])[0])
             got.append(tok)
     assert_tokens(got, want, margins)
+
+
+# ---- sliding-window KV cache (pages recycled as a ring) ------------------------------
+def windowed_oracle(small, prompt, budget, page, ring):
+    """Greedy generation on the oracle with the same window (orc_state_set_window)."""
+    st = small.state(len(prompt) + budget + 2)
+    st.set_window(page, ring)
+    lg = None
+    for i, t in enumerate(prompt):
+        lg, _ = st.forward(int(t), logits=(i == len(prompt) - 1))
+    out, margins = [], []
+    for j in range(budget):
+        top = np.partition(lg, -2)[-2:]
+        tok = int(oracle.argmax(lg[None])[0][0])
+        out.append(tok)
+        margins.append(float(abs(top[1] - top[0])))
+        if j + 1 < budget:
+            lg, _ = st.forward(tok)
+    return np.array(out), np.array(margins)
+
+
+@pytest.mark.parametrize("path,n", [(ve.PATH_AUTO, 1), (ve.PATH_AUTO, 3), (ve.PATH_FUSED_LAYERS, 2),
+                                    (ve.PATH_UNFUSED, 2), (ve.PATH_AUTO, 17)])
+def test_sliding_window_matches_oracle(models, small, path, n):
+    # 16-token pages, a 3-page window: after 48 tokens every new page overwrites the
+    # sequence's oldest one and attention covers the last 2 whole pages + the current one.
+    # n = 1 / 3 run the persistent kernel, n = 17 the per-layer tensor-core path.
+    page, ring, budget = 16, 3, 70
+    prompts = [ve.prompt(500 + s, SMALL["vocab"], 9 + s % 4) for s in range(n)]
+    with ve.Engine(models["small"], max_batch=n, max_len=96, page_size=page, kv_window=page * ring,
+                   path=path) as eng:
+        out, _ = eng.generate(prompts, budget)
+    for b in sorted({0, n - 1}):
+        want, margins = windowed_oracle(small, prompts[b], budget, page, ring)
+        assert_tokens(out[b], want, margins)
+    # The window matters: without it the oracle's tokens differ after the first wrap.
+    full, _ = small.generate(prompts[0], budget)
+    want0, _ = windowed_oracle(small, prompts[0], budget, page, ring)
+    assert not np.array_equal(full, want0)
+
+
+def test_sliding_window_chunked_prefill_and_limits(models, small):
+    page, ring = 16, 3
+    p = ve.prompt(600, SMALL["vocab"], 40)
+    with ve.Engine(models["small"], max_len=128, page_size=page, kv_window=page * ring, prefill_chunk=16) as eng:
+        out, _ = eng.generate([p], 60)
+    want, margins = windowed_oracle(small, p, 60, page, ring)
+    assert_tokens(out[0], want, margins)
+    with pytest.raises(Exception):  # a prompt longer than the window cannot be chunk-prefilled
+        with ve.Engine(models["small"], max_len=128, page_size=page, kv_window=page * ring,
+                       prefill_chunk=16) as eng:
+            eng.generate([ve.prompt(601, SMALL["vocab"], 60)], 4)
+    with pytest.raises(Exception):  # not a multiple of the page size
+        ve.Engine(models["small"], max_len=128, page_size=page, kv_window=40)
