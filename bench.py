@@ -775,6 +775,28 @@ def run_spec(args):
     print(json.dumps(line), flush=True)
 
 
+def run_window(args):
+    """Sliding-window KV cache (SURVEY next-row 4): config-0 model, bs1, 1024 greedy tokens
+    after the 32-token prompt, with a 256-token window (4 pages of 64 as a ring) and without
+    one. Device time of the decode steps (the engine's Timing); with the window the KV held per
+    sequence stays at 4 pages and each step attends to at most 256 positions."""
+    from voxelengine import engine as ve
+    mp = model_dir()
+    budget, window = 1024, 256
+    points = []
+    for w in (0, window):
+        with ve.Engine(mp, max_batch=1, max_len=PROMPT_LEN + budget + 8, page_size=64, kv_window=w) as eng:
+            p = [ve.prompt(1, 49152, PROMPT_LEN)]
+            eng.generate(p, 16)
+            _, t = eng.generate(p, budget)
+            kvb = eng.info.kv_bytes_per_token
+        points.append({"kv_window": w, "tok_s_device": t.decode_steps / (t.decode_ms * 1e-3),
+                       "decode_ms": t.decode_ms, "kv_bytes_per_sequence": kvb * (w or PROMPT_LEN + budget)})
+    line = {"metric": "greedy decode tok/s over 1024 tokens with and without a sliding-window KV cache (bs1, config 0)",
+            "unit": "tok/s", "points": points}
+    print(json.dumps(line), flush=True)
+
+
 def run_sample(args):
     """Sampling (SURVEY next-row 2): the opure_sample_filtered and opure_logit_stats kernels
     on seeded N(0, 3) logits of the config-0 vocabulary (device time per call, CUDA events
@@ -846,7 +868,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-steps", type=int, default=128)
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", choices=["decode", "attn", "gemv", "spec", "cfg4", "tp", "sample"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "attn", "gemv", "spec", "cfg4", "tp", "sample", "window"], default="decode")
     ap.add_argument("--path", choices=["auto", "layers", "unfused"], default="auto",
                     help="decode: step kernels (auto = one persistent kernel per step when eligible, "
                          "layers = three fused kernels per layer, unfused = per-op kernels)")
@@ -874,6 +896,8 @@ def main():
             run_spec(args)
         elif args.workload == "sample":
             run_sample(args)
+        elif args.workload == "window":
+            run_window(args)
         elif args.workload == "cfg4":
             run_cfg4(args, world, rank, local)
         elif args.workload == "tp":
