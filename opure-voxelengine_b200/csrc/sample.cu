@@ -73,6 +73,10 @@ __device__ unsigned long long block_max_key(unsigned long long v, unsigned long 
     return r;
 }
 
+constexpr uint32_t kHistBins = 4096;  // top-k pre-select: the keys' leading 12 bits
+constexpr uint32_t kCand = 4096;      // candidate keys kept in shared memory
+constexpr uint32_t kKeptMax = 1024;   // kept tokens drawn from the candidate list
+
 struct SampleShared {
     uint32_t bits[kMaxVocab / 32];      // tokens in the history (repetition penalty)
     unsigned long long hist[256];       // radix-select bins
@@ -80,9 +84,13 @@ struct SampleShared {
     unsigned long long scan[64 + kThreads];  // warp totals, warp offsets, per-thread offsets (draw)
     uint32_t pick;
     uint32_t digit;
+    uint32_t n_cand, n_kept;
+    uint32_t hist12[kHistBins];         // top-k pre-select histogram
+    unsigned long long cand[kCand];     // keys at or above the pre-selected bin
+    unsigned long long cmass[kCand];    // their masses (0 below the top-k floor)
+    unsigned long long kept[kKeptMax];  // the kept keys, then their masses
+    unsigned long long kmass[kKeptMax];
 };
-
-static_assert(sizeof(SampleShared) <= 48 * 1024, "fits the default dynamic shared memory limit");
 
 // Penalised logit of token i.
 __device__ __forceinline__ float pen_logit(const float *l, uint32_t i, const SampleShared &sm, bool pen, float r) {
@@ -179,6 +187,67 @@ __device__ unsigned long long radix_select(uint32_t n, unsigned long long floor_
     return prefix;
 }
 
+// Top-k pre-select: a histogram of the keys' leading 12 bits finds the bin holding the k-th
+// largest key; every key at or above that bin goes to sm.cand. False (nothing usable) when
+// the list would overflow.
+template <class KeyF>
+__device__ bool compact_top_k(uint32_t n, uint32_t k, KeyF keyf, SampleShared &sm) {
+    for (uint32_t b = threadIdx.x; b < kHistBins; b += blockDim.x) sm.hist12[b] = 0u;
+    if (threadIdx.x == 0) sm.n_cand = 0u;
+    __syncthreads();
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+        const unsigned long long key = keyf(i);
+        if (key) atomicAdd(&sm.hist12[uint32_t(key >> 52)], 1u);
+    }
+    __syncthreads();
+    // Bins from the top: thread t owns bins 4095-4t .. 4092-4t; block-wide inclusive scan.
+    constexpr uint32_t kPer = kHistBins / kThreads;
+    uint32_t own = 0u;
+#pragma unroll
+    for (uint32_t q = 0; q < kPer; ++q) own += sm.hist12[kHistBins - 1 - kPer * threadIdx.x - q];
+    const uint32_t lane = threadIdx.x & 31u, wid = threadIdx.x >> 5;
+    uint32_t incl = own;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= uint32_t(o)) incl += t;
+    }
+    if (lane == 31) sm.scan[wid] = incl;
+    __syncthreads();
+    if (wid == 0) {
+        const unsigned long long wt = lane < blockDim.x / 32 ? sm.scan[lane] : 0ull;
+        unsigned long long wi = wt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned long long t = __shfl_up_sync(0xffffffffu, wi, o);
+            if (lane >= uint32_t(o)) wi += t;
+        }
+        sm.scan[32 + lane] = wi - wt;
+    }
+    if (threadIdx.x == 0) sm.digit = kHistBins;  // bin of the k-th key (none: fewer keys)
+    __syncthreads();
+    unsigned long long cum = sm.scan[32 + wid] + incl - own;  // keys above this thread's bins
+#pragma unroll
+    for (uint32_t q = 0; q < kPer; ++q) {
+        const uint32_t b = kHistBins - 1 - kPer * threadIdx.x - q;
+        const uint32_t h = sm.hist12[b];
+        if (cum < k && cum + h >= k) sm.digit = b;  // exactly one bin crosses
+        cum += h;
+    }
+    __syncthreads();
+    if (sm.digit == kHistBins) return false;
+    const unsigned long long floor_bin = (unsigned long long)sm.digit << 52;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+        const unsigned long long key = keyf(i);
+        if (key >= floor_bin) {
+            const uint32_t slot = atomicAdd(&sm.n_cand, 1u);
+            if (slot < kCand) sm.cand[slot] = key;
+        }
+    }
+    __syncthreads();
+    return sm.n_cand <= kCand;
+}
+
 __global__ void __launch_bounds__(kThreads) sample_filtered_kernel(opure_sample_args a) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     SampleShared &sm = *reinterpret_cast<SampleShared *>(smem_raw);
@@ -214,7 +283,69 @@ __global__ void __launch_bounds__(kThreads) sample_filtered_kernel(opure_sample_
     best = block_max_key(best, sm.red);
     uint32_t token = best ? argmax_key_index(best) : 0u;
 
-    if (a.temperature > 0.f && a.top_k != 1 && best) {
+    const bool compact = a.temperature > 0.f && a.top_k > 1 && a.top_k <= kKeptMax && a.top_k < V && best &&
+                         compact_top_k(V, a.top_k, keyf, sm);
+    if (compact) {
+        // Top-k survivors and the keys just below them sit in sm.cand: top-k, top-p and the
+        // draw run over that list instead of the whole row.
+        const double inv_t = 1.0 / double(a.temperature);
+        const double zmax = double(argmax_key_value(best)) * inv_t;
+        const uint32_t nc = sm.n_cand;
+        auto ckey = [&](uint32_t i) { return sm.cand[i]; };
+        const unsigned long long kfloor =
+            radix_select(nc, 1ull, a.top_k, ckey, [](uint32_t, unsigned long long) { return 1ull; }, sm);
+        unsigned long long z = 0ull;
+        for (uint32_t i = threadIdx.x; i < nc; i += blockDim.x) {
+            const unsigned long long k = sm.cand[i];
+            unsigned long long m = 0ull;
+            if (k >= kfloor) {
+                const double e = exp(double(argmax_key_value(k)) * inv_t - zmax);
+                m = e > 0.0 ? __double2ull_rn(e * kMassUnit) : 0ull;
+            }
+            sm.cmass[i] = m;
+            z += m;
+        }
+        z = block_sum(z, sm.red);  // (syncs: cmass complete)
+        unsigned long long floor_key = kfloor;
+        if (a.top_p < 1.0f) {
+            const double tgt = ceil(double(a.top_p) * double(z));
+            const unsigned long long target = tgt < 1.0 ? 1ull : (unsigned long long)tgt;
+            if (target < z)
+                floor_key = radix_select(nc, kfloor, target, ckey,
+                                         [&](uint32_t i, unsigned long long) { return sm.cmass[i]; }, sm);
+        }
+        // The kept keys (at most top_k), then the draw in index order: each kept token's
+        // running mass is the sum over the kept tokens with a lower index.
+        if (threadIdx.x == 0) {
+            sm.n_kept = 0;
+            sm.pick = 0xffffffffu;
+        }
+        __syncthreads();
+        for (uint32_t i = threadIdx.x; i < nc; i += blockDim.x)
+            if (sm.cand[i] >= floor_key) {
+                const uint32_t slot = atomicAdd(&sm.n_kept, 1u);
+                sm.kept[slot] = sm.cand[i];
+                sm.kmass[slot] = sm.cmass[i];
+            }
+        __syncthreads();
+        const uint32_t nk = sm.n_kept;
+        unsigned long long tot = 0ull;
+        for (uint32_t i = threadIdx.x; i < nk; i += blockDim.x) tot += sm.kmass[i];
+        tot = block_sum(tot, sm.red);
+        if (tot) {
+            unsigned long long thr = (unsigned long long)floor(double(a.u[row]) * double(tot));
+            if (thr >= tot) thr = tot - 1;
+            for (uint32_t i = threadIdx.x; i < nk; i += blockDim.x) {
+                const uint32_t idx = argmax_key_index(sm.kept[i]);
+                unsigned long long before = 0ull;
+                for (uint32_t j = 0; j < nk; ++j)
+                    if (argmax_key_index(sm.kept[j]) < idx) before += sm.kmass[j];
+                if (before <= thr && thr < before + sm.kmass[i]) sm.pick = idx;
+            }
+        }
+        __syncthreads();
+        if (tot) token = sm.pick;
+    } else if (a.temperature > 0.f && a.top_k != 1 && best) {
         const double inv_t = 1.0 / double(a.temperature);
         const double zmax = double(argmax_key_value(best)) * inv_t;
         // top-k: the k-th largest key (count measure).
@@ -347,6 +478,10 @@ extern "C" opure_status opure_sample_filtered(opure_ctx *ctx, const opure_sample
     if (a->temperature > 0.f && a->top_k != 1 && !a->u) return OPURE_ERR_INVALID_ARG;
     if (a->rep_penalty != 1.f && a->hist && (!a->hist_len || a->max_len == 0)) return OPURE_ERR_INVALID_ARG;
     if (a->rows == 0) return OPURE_OK;
+    static_assert(sizeof(SampleShared) <= 200 * 1024, "shared memory of the sampling CTA");
+    const cudaError_t e = cudaFuncSetAttribute(sample_filtered_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               int(sizeof(SampleShared)));
+    if (e != cudaSuccess) return cuda_status(e);
     return launch(ctx, sample_filtered_kernel, dim3(a->rows), dim3(kThreads), sizeof(SampleShared), true, *a);
 }
 
