@@ -15,6 +15,7 @@
 
 #include "attn_core.cuh"
 #include "ctx.cuh"
+#include "tma.cuh"
 
 namespace opure {
 namespace {
@@ -113,6 +114,240 @@ __global__ void __launch_bounds__(kWarps * 32) attn_kernel(AttnParams p) {
     if (threadIdx.x == 0) p.counters[eg] = 0u;  // ready for the next call
 }
 
+// ---- TMA-staged variant (head_dim 64 and 128) ----------------------------------------
+// The register-fed loop above issues one block of K/V loads per warp, then computes on it
+// before the next block's addresses (page-table entry, then the rows) are even known: two
+// dependent memory latencies per block and nothing in flight while it computes. Here a
+// producer warp walks the split's pages ahead of the consumers and copies each page's K
+// block and V block (page_size x HD fp16 each, contiguous in the pool) into a ring of
+// shared-memory stages with bulk copies that complete on an mbarrier; four consumer warps
+// run the same per-lane online softmax out of shared memory and release each stage with
+// one arrival per warp. The page-table entries are read 32 at a time by the producer warp.
+// All waits are bounded (1 s); a timed-out CTA records OPURE_ERR_DEVICE_TIMEOUT, and the
+// producer waits (bounded) for every copy it issued before the CTA exits.
+constexpr int kMaxStages = 8;
+constexpr uint32_t kStageBudget = 64 * 1024;  // bytes of K/V stages per CTA
+
+__host__ __device__ inline uint32_t stage_count(uint32_t page_bytes_kv) {
+    const uint32_t n = kStageBudget / page_bytes_kv;
+    return n < 2 ? 2u : (n > uint32_t(kMaxStages) ? uint32_t(kMaxStages) : n);
+}
+
+template <int HD, int G>
+__global__ void __launch_bounds__((kWarps + 1) * 32) attn_tma_kernel(AttnParams p) {
+    using S = AttnShape<HD>;
+    constexpr int LPT = S::LPT, CH = S::CH, TPW = S::TPW, E = S::E;
+    constexpr int R = 4;  // rounds per consumer block
+    extern __shared__ __align__(128) uint8_t stage_mem[];
+    __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages];
+    __shared__ int stage_ok[kMaxStages];
+    __shared__ WarpStates<HD, G, kWarps> ws;
+
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t n_kv = p.kv.n_kv;
+    const uint32_t eg = blockIdx.x;
+    const uint32_t entry = eg / n_kv, g = eg % n_kv;
+    const uint32_t split = blockIdx.y;
+    const uint32_t i = entry / p.n_q, j = entry % p.n_q;
+    const uint32_t P = p.kv.page_size;
+    const uint32_t page_elems = P * HD;
+    const uint32_t page_bytes = page_elems * 2;
+    const uint32_t n_stages = stage_count(2 * page_bytes);
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < n_stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kWarps);
+        }
+    }
+    __syncthreads();
+
+    grid_dependency_wait();
+    grid_dependents_launch();
+
+    const int32_t sidx = p.seq[i];
+    const int32_t len = p.seq_len[i] + int32_t(j);
+    const uint32_t t_split = split * p.split_tokens;
+    const uint32_t t_end = min(uint32_t(max(len, 0)), t_split + p.split_tokens);
+    const uint32_t t_begin = max(t_split, window_begin(len - 1, P, p.kv.ring));
+    const bool any = sidx >= 0 && t_end > t_begin;
+    const uint32_t pg_begin = t_begin / P;
+    const uint32_t n_pg = any ? (t_end + P - 1) / P - pg_begin : 0u;
+
+    AttnState<HD, G> st;
+    st.init();
+
+    if (warp == kWarps) {
+        // Producer warp: page-table entries 32 at a time, lane 0 issues the copies.
+        const int32_t *pt = p.kv.page_table + size_t(max(sidx, 0)) * p.kv.max_pages;
+        const __half *pool = reinterpret_cast<const __half *>(p.kv.pool);
+        bool ok = true;
+        uint32_t issued = 0;  // iterations whose stage was armed (lane 0)
+        for (uint32_t c0 = 0; c0 < n_pg && ok; c0 += 32) {
+            int32_t mine = -1;
+            if (c0 + lane < n_pg) {
+                const uint32_t lp = ring_slot(pg_begin + c0 + lane, p.kv.ring);
+                mine = lp < p.kv.max_pages ? pt[lp] : -1;
+            }
+            const uint32_t cnt = min(32u, n_pg - c0);
+            for (uint32_t k = 0; k < cnt; ++k) {
+                const int32_t page = __shfl_sync(0xffffffffu, mine, k);
+                if (lane == 0 && ok) {
+                    const uint32_t it = c0 + k, s = it % n_stages, use = it / n_stages;
+                    if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1u)) {
+                        report(p.st, OPURE_ERR_DEVICE_TIMEOUT, 12, blockIdx.x);
+                        ok = false;
+                    } else if (page < 0 || uint32_t(page) >= p.kv.n_pages) {
+                        report(p.st, OPURE_ERR_DEVICE_BOUNDS, 11, uint32_t(page));
+                        stage_ok[s] = 0;
+                        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&full[s])) : "memory");
+                        ++issued;
+                    } else {
+                        stage_ok[s] = 1;
+                        const __half *kp = pool + (size_t(page) * 2 * n_kv + g) * page_elems;
+                        uint8_t *dst = stage_mem + size_t(s) * 2 * page_bytes;
+                        mbar_expect_tx(&full[s], 2 * page_bytes);
+                        bulk_load_keep(dst, kp, page_bytes, &full[s]);
+                        bulk_load_keep(dst + page_bytes, kp + size_t(n_kv) * page_elems, page_bytes, &full[s]);
+                        ++issued;
+                    }
+                }
+                ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+                if (!ok) break;
+            }
+        }
+        // No copy may still be landing in shared memory when the CTA exits.
+        if (lane == 0) {
+            // The last use of each slot is the only phase that can still be pending.
+            for (uint32_t s = 0; s < n_stages && s < issued; ++s) {
+                const uint32_t last = issued - 1 - ((issued - 1 - s) % n_stages);  // last iteration on slot s
+                (void)mbar_wait(&full[s], (last / n_stages) & 1u);
+            }
+        }
+    } else {
+        float qv[G][E];
+        load_q_slice<HD, G>(p.q + size_t(entry) * p.n_heads * HD, g, p.scale_log2, qv);
+        const uint32_t grp = lane / LPT, sub = lane % LPT;
+        const uint32_t rounds = P / TPW;  // token rounds per page
+        for (uint32_t it = 0; it < n_pg; ++it) {
+            const uint32_t s = it % n_stages;
+            if (!mbar_wait(&full[s], (it / n_stages) & 1u)) {
+                if (lane == 0) report(p.st, OPURE_ERR_DEVICE_TIMEOUT, 13, blockIdx.x);
+                break;
+            }
+            const bool page_ok = stage_ok[s] != 0;
+            const __half *ks = reinterpret_cast<const __half *>(stage_mem + size_t(s) * 2 * page_bytes);
+            const __half *vs = ks + page_elems;
+            const uint32_t tok0 = (pg_begin + it) * P;
+            for (uint32_t r0 = warp; r0 < rounds; r0 += kWarps * R) {
+                uint4 kr[R][CH], vr[R][CH];
+                bool valid[R], live[R];
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    const uint32_t rr = r0 + r * kWarps;
+                    live[r] = rr < rounds;
+                    const uint32_t row = rr * TPW + grp;
+                    const uint32_t t = tok0 + row;
+                    valid[r] = live[r] && page_ok && t >= t_begin && t < t_end;
+#pragma unroll
+                    for (int c = 0; c < CH; ++c) {
+                        kr[r][c] = valid[r] ? *reinterpret_cast<const uint4 *>(ks + size_t(row) * HD + sub * E + c * 8)
+                                            : make_uint4(0, 0, 0, 0);
+                        vr[r][c] = valid[r] ? *reinterpret_cast<const uint4 *>(vs + size_t(row) * HD + sub * E + c * 8)
+                                            : make_uint4(0, 0, 0, 0);
+                    }
+                }
+                float sc[R][G];
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    float kf[E];
+#pragma unroll
+                    for (int c = 0; c < CH; ++c) unpack8(kr[r][c], kf + 8 * c);
+#pragma unroll
+                    for (int h = 0; h < G; ++h) {
+                        float d = 0.f;
+#pragma unroll
+                        for (int e = 0; e < E; ++e) d = fmaf(qv[h][e], kf[e], d);
+#pragma unroll
+                        for (int o = LPT / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+                        sc[r][h] = valid[r] ? d : -INFINITY;
+                    }
+                }
+#pragma unroll
+                for (int h = 0; h < G; ++h) {
+                    float mb = sc[0][h];
+#pragma unroll
+                    for (int r = 1; r < R; ++r) mb = fmaxf(mb, sc[r][h]);
+                    const float mn = fmaxf(st.m[h], mb);
+                    if (mn == -INFINITY) continue;
+                    const float corr = fast_exp2(st.m[h] - mn);
+                    st.l[h] *= corr;
+#pragma unroll
+                    for (int e = 0; e < E; ++e) st.acc[h][e] *= corr;
+                    st.m[h] = mn;
+                }
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    if (!valid[r]) continue;
+                    float vf[E];
+#pragma unroll
+                    for (int c = 0; c < CH; ++c) unpack8(vr[r][c], vf + 8 * c);
+#pragma unroll
+                    for (int h = 0; h < G; ++h) {
+                        const float pr = fast_exp2(sc[r][h] - st.m[h]);
+                        st.l[h] += pr;
+#pragma unroll
+                        for (int e = 0; e < E; ++e) st.acc[h][e] = fmaf(pr, vf[e], st.acc[h][e]);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&empty[s])) : "memory");
+        }
+        merge_lane_groups<HD, G>(st);
+        store_warp_state<HD, G, kWarps>(st, ws, warp);
+    }
+    __syncthreads();
+
+    const uint32_t n_splits = p.n_splits;
+    float *part = p.partials + (size_t(eg) * n_splits + split) * G * (HD + 2);
+    for (uint32_t idx = threadIdx.x; idx < uint32_t(G) * HD; idx += blockDim.x) {
+        const uint32_t h = idx / HD, d = idx % HD;
+        float a, mn, ls;
+        merge_warps<HD, G, kWarps>(ws, h, d, a, mn, ls);
+        part[h * (HD + 2) + d] = a;
+        if (d == 0) {
+            part[h * (HD + 2) + HD] = mn;
+            part[h * (HD + 2) + HD + 1] = ls;
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    __shared__ uint32_t ticket;
+    if (threadIdx.x == 0) ticket = atomicAdd(p.counters + eg, 1u);
+    __syncthreads();
+    if (ticket != n_splits - 1) return;
+
+    __threadfence();
+    const float *parts = p.partials + size_t(eg) * n_splits * G * (HD + 2);
+    for (uint32_t idx = threadIdx.x; idx < uint32_t(G) * HD; idx += blockDim.x) {
+        const uint32_t h = idx / HD, d = idx % HD;
+        float mn = -INFINITY;
+        for (uint32_t sp = 0; sp < n_splits; ++sp)
+            mn = fmaxf(mn, __ldcg(parts + (size_t(sp) * G + h) * (HD + 2) + HD));
+        float a = 0.f, lsum = 0.f;
+        for (uint32_t sp = 0; sp < n_splits; ++sp) {
+            const float *pp = parts + (size_t(sp) * G + h) * (HD + 2);
+            const float ms = __ldcg(pp + HD);
+            const float f = (mn == -INFINITY || ms == -INFINITY) ? 0.f : fast_exp2(ms - mn);
+            a += __ldcg(pp + d) * f;
+            lsum += __ldcg(pp + HD + 1) * f;
+        }
+        p.out[(size_t(entry) * p.n_heads + g * G + h) * HD + d] = a / fmaxf(lsum, 1e-30f);
+    }
+    if (threadIdx.x == 0) p.counters[eg] = 0u;
+}
+
 using AttnKernel = void (*)(AttnParams);
 
 template <int HD>
@@ -125,6 +360,20 @@ AttnKernel pick_g(uint32_t G) {
     }
     return nullptr;
 }
+
+template <int HD>
+AttnKernel pick_tma_g(uint32_t G) {
+    switch (G) {
+        case 1: return attn_tma_kernel<HD, 1>;
+        case 2: return attn_tma_kernel<HD, 2>;
+        case 3: return attn_tma_kernel<HD, 3>;
+        case 4: return attn_tma_kernel<HD, 4>;
+    }
+    return nullptr;
+}
+
+// Head dims served by the TMA-staged kernel.
+bool tma_path(uint32_t hd) { return hd == 64 || hd == 128; }
 
 AttnKernel pick(uint32_t hd, uint32_t G) {
     switch (hd) {
@@ -158,6 +407,19 @@ uint32_t cta_tokens(uint32_t hd) {
 // CTAs on every SM (sm_count 148 on B200) without splitting below one block.
 uint32_t choose_split(uint32_t entries, uint32_t n_kv, uint32_t hd, uint32_t max_ctx,
                       uint32_t requested, int sm_count) {
+    if (tma_path(hd)) {
+        // Splits are whole multiples of 128 tokens, so pages of 16..128 tokens never straddle
+        // two splits. About one wave of three CTAs per SM (rounded to the nearest whole split
+        // count, so a second, mostly empty wave is avoided).
+        const uint32_t unit = 128;
+        if (requested) return ((requested + unit - 1) / unit) * unit;
+        const uint64_t pairs = uint64_t(entries) * n_kv;
+        const uint64_t target = uint64_t(sm_count > 0 ? sm_count : 148) * 3;
+        const uint64_t near = std::max<uint64_t>(1, (target + pairs / 2) / pairs);
+        const uint64_t want = std::min<uint64_t>(near, std::max<uint64_t>(1, max_ctx / unit));
+        const uint64_t per = (uint64_t(std::max(max_ctx, 1u)) + want - 1) / want;
+        return uint32_t(std::max<uint64_t>(unit, ((per + unit - 1) / unit) * unit));
+    }
     const uint32_t unit = cta_tokens(hd);
     if (requested) return ((requested + unit - 1) / unit) * unit;
     // About four CTAs per SM, but no split shorter than 128 tokens: a short context is one
@@ -168,6 +430,24 @@ uint32_t choose_split(uint32_t entries, uint32_t n_kv, uint32_t hd, uint32_t max
         1, std::min<uint64_t>((target + pairs - 1) / pairs, std::max<uint64_t>(1, max_ctx / 128)));
     const uint64_t per = (uint64_t(std::max(max_ctx, 1u)) + want_splits - 1) / want_splits;
     return uint32_t(std::max<uint64_t>(unit, ((per + unit - 1) / unit) * unit));
+}
+
+opure_status launch_attention(opure_ctx *ctx, const AttnParams &p, uint32_t hd, uint32_t G, uint32_t pairs,
+                              uint32_t n_splits) {
+    if (tma_path(hd)) {
+        AttnKernel k = hd == 64 ? pick_tma_g<64>(G) : pick_tma_g<128>(G);
+        if (!k) return OPURE_ERR_UNSUPPORTED;
+        const uint32_t page_bytes = p.kv.page_size * hd * 2;
+        const size_t smem = size_t(stage_count(2 * page_bytes)) * 2 * page_bytes;
+        if (smem > 48 * 1024) {
+            const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+            if (e != cudaSuccess) return cuda_status(e);
+        }
+        return launch(ctx, k, dim3(pairs, n_splits), dim3((kWarps + 1) * 32), smem, true, p);
+    }
+    AttnKernel k = pick(hd, G);
+    if (!k) return OPURE_ERR_UNSUPPORTED;
+    return launch(ctx, k, dim3(pairs, n_splits), dim3(kWarps * 32), 0, true, p);
 }
 
 size_t scratch_layout(uint32_t entries, uint32_t n_kv, uint32_t G, uint32_t hd, uint32_t n_splits,
@@ -206,8 +486,7 @@ extern "C" opure_status opure_attention(opure_ctx *ctx, const opure_attn_args *a
     if (a->n_heads % kv.n_kv) return OPURE_ERR_INVALID_ARG;
     if (a->n == 0 || a->n_q == 0) return OPURE_OK;
     const uint32_t G = a->n_heads / kv.n_kv;
-    AttnKernel k = pick(kv.head_dim, G);
-    if (!k) return OPURE_ERR_UNSUPPORTED;
+    if (!pick(kv.head_dim, G)) return OPURE_ERR_UNSUPPORTED;
     if (reinterpret_cast<uintptr_t>(kv.pool) % 16) return OPURE_ERR_UNSUPPORTED;
     const uint32_t entries = a->n * a->n_q;
     const uint32_t st = choose_split(entries, kv.n_kv, kv.head_dim, a->max_ctx, a->split_tokens,
@@ -234,7 +513,7 @@ extern "C" opure_status opure_attention(opure_ctx *ctx, const opure_attn_args *a
     p.counters = reinterpret_cast<uint32_t *>(static_cast<char *>(a->scratch) + counters_off);
     p.kv = kv;
     p.st = ctx->status;
-    return launch(ctx, k, dim3(entries * kv.n_kv, n_splits), dim3(kWarps * 32), 0, true, p);
+    return launch_attention(ctx, p, kv.head_dim, G, entries * kv.n_kv, n_splits);
 }
 
 // ---- Allocation-free variant (opure_attention_static) ---------------------------------
@@ -277,8 +556,7 @@ extern "C" opure_status opure_attention_static(opure_ctx *ctx, const opure_attn_
     if (a->n_heads % kv.n_kv) return OPURE_ERR_INVALID_ARG;
     if (a->n == 0 || a->n_q == 0) return OPURE_OK;
     const uint32_t G = a->n_heads / kv.n_kv;
-    AttnKernel k = pick(kv.head_dim, G);
-    if (!k) return OPURE_ERR_UNSUPPORTED;
+    if (!pick(kv.head_dim, G)) return OPURE_ERR_UNSUPPORTED;
     if (reinterpret_cast<uintptr_t>(kv.pool) % 16) return OPURE_ERR_UNSUPPORTED;
     const uint32_t entries = a->n * a->n_q;
     const uint32_t st = choose_split(entries, kv.n_kv, kv.head_dim, a->max_ctx, a->split_tokens,
@@ -309,5 +587,5 @@ extern "C" opure_status opure_attention_static(opure_ctx *ctx, const opure_attn_
     p.counters = counters;
     p.kv = kv;
     p.st = ctx->status;
-    return launch(ctx, k, dim3(entries * kv.n_kv, n_splits), dim3(kWarps * 32), 0, true, p);
+    return launch_attention(ctx, p, kv.head_dim, G, entries * kv.n_kv, n_splits);
 }

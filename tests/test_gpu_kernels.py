@@ -201,6 +201,42 @@ def test_paged_attention_permuted(ctx, B, ctxlen, page):
     assert rel_err(got, want) < REL
 
 
+@pytest.mark.parametrize("page", [16, 64, 128])
+def test_attention_masks_poisoned_tail(ctx, page):
+    # Every pool byte outside the sequences' tokens is NaN (fp16 0xFFFF): whole pages are
+    # staged into shared memory, so masked rows must contribute nothing, not NaN * 0.
+    rng = np.random.default_rng(page)
+    B, nh, nkv, hd = 3, 9, 3, 64
+    lens = np.array([1, page + 3, 5 * page - 1], np.int32)
+    maxp = -(-int(lens.max()) // page)
+    npages = B * maxp + 2
+    perm = rng.permutation(npages)[: B * maxp].reshape(B, maxp).astype(np.int32)
+    pool = np.full((npages, 2, nkv, page, hd), 0xFFFF, np.uint16)
+    for b in range(B):
+        for t in range(int(lens[b])):
+            pg, r = perm[b, t // page], t % page
+            pool[pg, :, :, r] = f16(rng.standard_normal((2, nkv, hd)).astype(np.float32))
+    q = rng.standard_normal((B, 1, nh, hd)).astype(np.float32)
+    got = attention_gpu(ctx, q, pool, perm, lens, page, nh, nkv, hd)
+    want = oracle.attention_paged(q, pool, perm, lens, page, nh, nkv, hd)
+    assert not np.isnan(got).any()
+    assert rel_err(got, want) < REL
+
+
+def test_attention_large_batch_long_context(ctx):
+    # Config-1 shape at a size the oracle finishes quickly: 64 sequences, several splits.
+    rng = np.random.default_rng(77)
+    B, nh, nkv, hd, page, L = 64, 9, 3, 64, 64, 1024
+    maxp = L // page
+    perm = rng.permutation(B * maxp).reshape(B, maxp).astype(np.int32)
+    pool = f16(rng.standard_normal((B * maxp, 2, nkv, page, hd)).astype(np.float32))
+    q = rng.standard_normal((B, 1, nh, hd)).astype(np.float32)
+    lens = np.array([L - (b * 29) % 700 for b in range(B)], np.int32)
+    got = attention_gpu(ctx, q, pool, perm, lens, page, nh, nkv, hd)
+    want = oracle.attention_paged(q, pool, perm, lens, page, nh, nkv, hd)
+    assert rel_err(got, want) < REL
+
+
 def test_attention_multi_query_causal(ctx):
     # Speculative verify: 5 queries, query j sees seq_len + j keys.
     rng = np.random.default_rng(11)
