@@ -473,6 +473,8 @@ def run_attention_sweep(args):
     with cu.Ctx(0) as ctx:
         for B in (1, 8, 64):
             for ctxlen in (512, 2048, 8192, 32768):
+                if (args.attn_b and B != args.attn_b) or (args.attn_ctx and ctxlen != args.attn_ctx):
+                    continue
                 pages = B * (ctxlen // P)
                 pool_elems = pages * 2 * nkv * P * hd
                 pool = ctx.buffer(pool_elems * 2)
@@ -624,9 +626,10 @@ def run_cfg4(args, world, rank, local):
 
 def run_tp(args, world, rank, local):
     """Config 4, second variant: batch-1 greedy decode of the 1.7B shape with world-way tensor
-    parallelism, one rank per GPU. Every step all-reduces (NCCL over NVLink) the o_proj and
-    down_proj partial sums of each layer (48 x 8 KB fp32 per token) and the vocabulary
-    shards' argmax keys (8 B). 32-token prompt (seed 1) prefilled, then device-resident steps
+    parallelism, one rank per GPU. Every step all-reduces the o_proj and down_proj partial
+    sums of each layer (48 x 8 KB fp32 per token) and the vocabulary shards' argmax keys
+    (8 B): by default inside the producing kernels over NVLink peer memory
+    (opure_gemv_allreduce / opure_peer_argmax), with --tp-allreduce nccl as NCCL calls. 32-token prompt (seed 1) prefilled, then device-resident steps
     (graph replays, NCCL inside the graph) at positions 32..159 (cyclic). Device time, max
     over ranks. `comm_us` is one 2048-float all-reduce timed on its own (100-call average)."""
     import ctypes as C
@@ -646,7 +649,8 @@ def run_tp(args, world, rank, local):
         dist.broadcast_object_list(obj, src=0)
     ctx = cu.Ctx(local)
     comm = cu.Comm(ctx, world, rank, obj[0], timeout_ms=120000)
-    eng = ve.Engine(mp, max_len=PROMPT_LEN + DECODE_STEPS + 8, comm=comm)
+    tp_mode = ve.TP_NCCL if args.tp_allreduce == "nccl" else ve.TP_AUTO
+    eng = ve.Engine(mp, max_len=PROMPT_LEN + DECODE_STEPS + 8, comm=comm, tp_allreduce=tp_mode)
     info = eng.info
     L = cu.lib()
     eng.generate([ve.prompt(1, info.vocab, PROMPT_LEN)], DECODE_STEPS)
@@ -698,6 +702,36 @@ def run_tp(args, world, rank, local):
     g.free()
     cu.check(L.opure_event_elapsed_ms(ev0, ev1, C.byref(ms)), "elapsed")
     comm_us = allreduce_max(world, float(ms.value) * 10.0)
+    # The fused alternative: an o_proj-shaped peer GEMV all-reduce (this shard's 2048 x
+    # 2048/world fp16 block, partial sums exchanged over NVLink and added to the residual),
+    # 100 per graph. Every rank takes this path or none (the engine's flag is collective).
+    peer_us = None
+    if info.tp_peer:
+        peer = cu.Peer(comm, info.hidden)
+        cols = info.hidden // world
+        w = ctx.buffer(info.hidden * cols * 2).fill(0)
+        x = ctx.buffer(cols * 4).fill(0)
+        a = cu.GemvArgs()
+        a.w, a.w_dtype, a.rows, a.cols, a.nvec = w.ptr, cu.W_F16, info.hidden, cols, 1
+        a.x, a.x_stride, a.y, a.y_stride = x.ptr, cols, buf.ptr, info.hidden
+        a.epilogue, a.residual = cu.EPI_ADD, buf.ptr
+        g = cu.Graph(ctx)
+        with g:
+            for _ in range(100):
+                peer.gemv_allreduce(a)
+        for _ in range(3):
+            g.launch()
+        ctx.sync()
+        barrier(world)
+        cu.check(L.opure_event_record(ctx.h, ev0), "event")
+        g.launch()
+        cu.check(L.opure_event_record(ctx.h, ev1), "event")
+        ctx.sync()
+        g.free()
+        cu.check(L.opure_event_elapsed_ms(ev0, ev1, C.byref(ms)), "elapsed")
+        peer_us = allreduce_max(world, float(ms.value) * 10.0)
+        cu.check(ctx.last_error(), "peer all-reduce")
+        peer.close()
     step_ms = dev_ms / args.steps
     positions = [PROMPT_LEN + (i % DECODE_STEPS) for i in range(DECODE_STEPS)]
     sbytes = step_bytes(info, 1, positions)   # this shard's weights and KV heads
@@ -712,8 +746,10 @@ def run_tp(args, world, rank, local):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
                          "bytes_per_step": sbytes, "kernel": "whole decode step, per GPU (its shard)"},
-            "comm": {"allreduce_us_2048_f32": comm_us, "allreduces_per_step": 2 * info.layers + 1,
-                     "est_ms_per_step": comm_us * (2 * info.layers + 1) / 1000.0}}
+            "comm": {"path": "nvlink peer kernels" if info.tp_peer else "nccl",
+                     "allreduce_us_2048_f32": comm_us, "allreduces_per_step": 2 * info.layers + 1,
+                     "nccl_est_ms_per_step": comm_us * (2 * info.layers + 1) / 1000.0,
+                     "peer_gemv_allreduce_us": peer_us}}
     if rank == 0:
         print(json.dumps(line), flush=True)
     eng.close()
@@ -880,6 +916,10 @@ def main():
                          "batch size) and report them under \"bs64\"; 0 skips")
     ap.add_argument("--seqs", type=int, default=512, help="cfg4: total sequences over all ranks")
     ap.add_argument("--wave", type=int, default=128, help="cfg4: sequences per GPU per wave")
+    ap.add_argument("--attn-b", type=int, default=0, help="attn: only this batch size (1, 8 or 64)")
+    ap.add_argument("--attn-ctx", type=int, default=0, help="attn: only this context length")
+    ap.add_argument("--tp-allreduce", choices=["auto", "nccl"], default="auto",
+                    help="tp: NVLink peer kernels (auto, when every GPU pair maps each other's memory) or NCCL")
     ap.add_argument("--quick", action="store_true",
                     help="minimal run for profiler launch lists: no parity, e2e or CPU legs")
     args = ap.parse_args()

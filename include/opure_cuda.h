@@ -441,6 +441,38 @@ opure_status opure_allreduce_max_u64(opure_ctx *ctx, opure_comm *c, unsigned lon
  * key's index to the global one (value bits unchanged), ready for a u64 max all-reduce. */
 opure_status opure_argmax_key_offset(opure_ctx *ctx, unsigned long long *keys, uint32_t n, uint32_t offset);
 
+/* ---- NVLink peer all-reduce fused into the producing kernel (tensor parallelism) -------
+ * The reference has no multi-GPU path at all (one D3D12 device, Opure_Dx12.h:144-337); these
+ * replace, on the tensor-parallel step, the pair opure_allreduce_sum_f32 + opure_add after
+ * each o_proj / down_proj GEMV and the pair opure_argmax_key_offset + opure_allreduce_max_u64
+ * after the lm_head (the reference's serial AddRes / ArgMax dispatches,
+ * Opure_VoxelEngine.cpp:451-470,508-532).
+ *
+ * A peer group gives every rank of `comm` (one process per GPU) a mailbox in its own HBM
+ * that every other rank maps through CUDA IPC. Creation is collective over `comm` (same call
+ * on every rank, bounded by the communicator's timeout) and returns OPURE_ERR_UNSUPPORTED on
+ * every rank when any pair of GPUs cannot map each other's memory (then keep NCCL).
+ * `max_rows` bounds the GEMV rows of a collective; device-side waits give up after
+ * `timeout_ms` (0: 2000) with OPURE_ERR_DEVICE_TIMEOUT in the status word. Every rank must
+ * issue the same sequence of peer collectives with the same shapes. destroy is collective
+ * too (pass the communicator, or NULL if the other ranks are known to be done). */
+typedef struct opure_peer opure_peer;
+#define OPURE_PEER_MAX_RANKS 8
+#define OPURE_PEER_MAX_KEYS 256
+opure_status opure_peer_create(opure_ctx *ctx, opure_comm *comm, uint32_t max_rows, uint32_t timeout_ms,
+                               opure_peer **out);
+opure_status opure_peer_destroy(opure_ctx *ctx, opure_comm *comm, opure_peer *peer);
+opure_status opure_peer_info(const opure_peer *peer, uint32_t *n_ranks, uint32_t *rank, uint32_t *max_rows);
+/* GEMV (as opure_gemv, epilogue OPURE_EPI_STORE or OPURE_EPI_ADD, CUDA-core path for any
+ * nvec, in passes of up to 9 vectors) whose partial sums are all-reduced over the group
+ * inside the same kernel: y = (residual +) sum over ranks of W_rank x_rank, summed in rank
+ * order so every rank gets bit-identical results. One kernel per pass; no scratch. */
+opure_status opure_gemv_allreduce(opure_ctx *ctx, opure_peer *peer, const opure_gemv_args *a);
+/* In place: keys[i] <- the largest key over all ranks, after rewriting this rank's keys to
+ * global indices (its vocabulary shard starts at row `offset`); n <= OPURE_PEER_MAX_KEYS. */
+opure_status opure_peer_argmax(opure_ctx *ctx, opure_peer *peer, unsigned long long *keys, uint32_t n,
+                               uint32_t offset);
+
 /* ---- fault injection (host side; tests of the error paths) -----------------
  * The next `count` ABI calls after `after_calls` more calls return OPURE_ERR_INJECTED
  * without touching the GPU. count = 0 disarms. */

@@ -44,7 +44,15 @@ typedef struct opure_engine_options {
                                  tokens of pages as a ring (opure_kv_layout.ring) and a
                                  position attends to the last kv_window / page_size - 1 whole
                                  pages and its own; 0: every position up to max_len */
+    uint32_t tp_allreduce;    /* tensor parallel: OPURE_TP_* (0: peer kernels when every pair
+                                 of ranks can map each other's memory, else NCCL)        */
 } opure_engine_options;
+
+enum {
+    OPURE_TP_AUTO = 0,        /* opure_gemv_allreduce / opure_peer_argmax over NVLink peer
+                                 memory when available, else NCCL                         */
+    OPURE_TP_NCCL = 1         /* NCCL all-reduces between the per-op kernels             */
+};
 
 enum {
     OPURE_PATH_AUTO = 0,      /* fused latency kernels when eligible, else per-op kernels */
@@ -60,6 +68,8 @@ typedef struct opure_engine_info {
     uint64_t weight_bytes;        /* resident weight arena                              */
     uint64_t stream_bytes;        /* weight bytes one decode step reads                 */
     uint64_t kv_bytes_per_token;  /* fp16 K+V, all layers, one sequence                 */
+    uint32_t tp_ranks;            /* tensor-parallel ranks (1 without a communicator)     */
+    uint32_t tp_peer;             /* 1: collectives run as NVLink peer kernels, 0: NCCL   */
 } opure_engine_info;
 
 typedef struct opure_generate_timing {

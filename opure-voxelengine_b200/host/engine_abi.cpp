@@ -68,6 +68,7 @@ opure::engine::EngineOptions ToOptions(const opure_engine_options *o) {
         opts.phaseTrace = o->phase_trace != 0;
         opts.prefillChunk = o->prefill_chunk;
         opts.kvWindow = o->kv_window;
+        opts.tpAllreduce = o->tp_allreduce;
     }
     return opts;
 }
@@ -227,6 +228,7 @@ void FillInfo(const opure::graph::Graph &g, opure_engine_info *info) {
     info->weight_bytes = p.weightBytes;
     info->stream_bytes = g.StreamBytes();
     info->kv_bytes_per_token = c.KvBytesPerToken() / g.Local().tpSize;  // this shard's KV heads
+    info->tp_ranks = g.Local().tpSize;
 }
 
 }  // namespace
@@ -238,6 +240,7 @@ opure_status opure_engine_get_info(opure_engine *e, opure_engine_info *info) {
         info->max_len = e->eng.MaxLen();
         info->max_batch = e->eng.Options().maxBatch;
         info->page_size = e->eng.Options().pageSize;
+        info->tp_peer = e->eng.UsesPeer() ? 1 : 0;
     });
 }
 

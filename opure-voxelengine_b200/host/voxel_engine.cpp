@@ -28,6 +28,8 @@ void VoxelEngine::Shutdown() {
     opure_sync(ctx_, 60000);
     for (auto &kv : graphs_) opure_graph_free(kv.second);
     graphs_.clear();
+    if (peer_) opure_peer_destroy(ctx_, comm_, peer_);  // collective: every rank shuts down
+    peer_ = nullptr;
     kv_.Destroy();
     for (void *p : {static_cast<void *>(buf_.x), static_cast<void *>(buf_.qkv), static_cast<void *>(buf_.q),
                     static_cast<void *>(buf_.attn), static_cast<void *>(buf_.h), static_cast<void *>(buf_.logits),
@@ -92,6 +94,15 @@ void VoxelEngine::Initialize(const std::string &modelDir, const EngineOptions &o
                ring);
     maxVec_ = std::max(opts.maxBatch, opts.prefillChunk);
     AllocBuffers();
+    if (comm && opts.tpAllreduce == 0) {
+        // NVLink peer mailboxes for the fused all-reduces; every rank falls back to NCCL
+        // together when any pair of GPUs cannot map each other's memory.
+        const opure_status ps = opure_peer_create(ctx_, comm, cfg.hiddenSize, 2000, &peer_);
+        if (ps == OPURE_ERR_UNSUPPORTED)
+            peer_ = nullptr;
+        else
+            OPURE_CUDA_CHECK(ps);
+    }
     seqLen_ = 0;
     ready_ = true;
     if ((opts.path == 2 || opts.path == 3) && !UsesFused(opts.maxBatch))
@@ -249,6 +260,10 @@ void VoxelEngine::RecordLayer(uint32_t L, uint32_t n) {
         // o_proj + residual, in place on the residual stream.
         gemv(At(weights_, t.wo), t.so, t.so, h, h, buf_.attn, h, buf_.x, h, OPURE_PRO_NONE, nullptr, OPURE_EPI_ADD,
              buf_.x);
+    } else if (peer_) {
+        // Tensor parallel over NVLink peer memory: one kernel computes this shard's partial
+        // o_proj sum, exchanges it with every rank and adds the total to the residual.
+        TpGemvAllreduce(At(weights_, t.wo), t.so, h, att, buf_.attn, h, n);
     } else {
         // Tensor parallel: this shard's heads give a partial o_proj sum over their input
         // columns; the shards' partials are summed over NCCL, then added to the residual.
@@ -264,12 +279,37 @@ void VoxelEngine::RecordLayer(uint32_t L, uint32_t n) {
         // down_proj + residual.
         gemv(At(weights_, t.wdown), t.sdown, t.sdown, h, ff, buf_.h, ff, buf_.x, h, OPURE_PRO_NONE, nullptr,
              OPURE_EPI_ADD, buf_.x);
+    } else if (peer_) {
+        TpGemvAllreduce(At(weights_, t.wdown), t.sdown, h, ff, buf_.h, ff, n);
     } else {
         gemv(At(weights_, t.wdown), t.sdown, t.sdown, h, ff, buf_.h, ff, buf_.partial, h, OPURE_PRO_NONE, nullptr,
              OPURE_EPI_STORE, nullptr);
         OPURE_CUDA_CHECK(opure_allreduce_sum_f32(ctx_, comm_, buf_.partial, size_t(n) * h));
         OPURE_CUDA_CHECK(opure_add(ctx_, buf_.x, buf_.partial, buf_.x, n * h));
     }
+}
+
+// residual x += sum over the tensor-parallel ranks of W_rank . in_rank (o_proj / down_proj
+// shards, `cols` input columns each), reduced over NVLink inside the GEMV kernel.
+void VoxelEngine::TpGemvAllreduce(const void *w, float scale, uint32_t rows, uint32_t cols, const float *in,
+                                  uint32_t in_stride, uint32_t n) {
+    opure_gemv_args a{};
+    a.w = w;
+    a.w_dtype = graph_.Plan().wDtype;
+    a.scale_w = scale;
+    a.scale_x = 1.0f;
+    a.scale_w2 = scale;
+    a.rows = rows;
+    a.cols = cols;
+    a.nvec = n;
+    a.x = in;
+    a.x_stride = in_stride;
+    a.y = buf_.x;
+    a.y_stride = rows;
+    a.prologue = OPURE_PRO_NONE;
+    a.epilogue = OPURE_EPI_ADD;
+    a.residual = buf_.x;
+    OPURE_CUDA_CHECK(opure_gemv_allreduce(ctx_, peer_, &a));
 }
 
 void VoxelEngine::RecordStep(uint32_t n, bool logits) {
@@ -347,7 +387,11 @@ void VoxelEngine::RecordStep(uint32_t n, bool logits) {
     a.epilogue = OPURE_EPI_ARGMAX;
     a.argmax_keys = buf_.keys;
     OPURE_CUDA_CHECK(opure_gemv(ctx_, &a));
-    if (comm_) {
+    if (peer_ && n <= OPURE_PEER_MAX_KEYS) {
+        // Vocabulary shards: global indices and the largest key over all shards in one
+        // peer kernel (ties keep the lowest global index, as in one unsplit argmax).
+        OPURE_CUDA_CHECK(opure_peer_argmax(ctx_, peer_, buf_.keys, n, lg.vocabOffset));
+    } else if (comm_) {
         // Vocabulary shards: global indices, then the largest key over all shards (ties
         // keep the lowest global index, as in one unsplit argmax).
         OPURE_CUDA_CHECK(opure_argmax_key_offset(ctx_, buf_.keys, n, lg.vocabOffset));

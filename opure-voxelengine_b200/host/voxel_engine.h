@@ -52,6 +52,7 @@ struct EngineOptions {
                                     // of pageSize): a sequence keeps kvWindow / pageSize pages as a
                                     // ring, and a position attends to the last kvWindow / pageSize - 1
                                     // whole pages and its own
+    uint32_t tpAllreduce = 0;       // tensor parallel: 0 NVLink peer kernels when available, 1 NCCL
 };
 
 struct GenerateResult {
@@ -94,6 +95,7 @@ public:
     bool IsReady() const { return ready_; }
 
     const graph::Graph &GraphModel() const { return graph_; }
+    bool UsesPeer() const { return peer_ != nullptr; }
     const graph::ModelConfig &Model() const { return graph_.Config(); }
     opure_ctx *Ctx() const { return ctx_; }
     uint32_t MaxLen() const { return maxLen_; }
@@ -195,6 +197,8 @@ private:
     void AllocBuffers();
     void RecordStep(uint32_t n, bool logits);
     void RecordLayer(uint32_t layer, uint32_t n);
+    void TpGemvAllreduce(const void *w, float scale, uint32_t rows, uint32_t cols, const float *in,
+                         uint32_t in_stride, uint32_t n);
     // Split-K attention scratch for batch n (one zeroed buffer per batch size, so its
     // split counters always start at zero).
     void *AttnScratch(uint32_t n, size_t *bytes);
@@ -221,6 +225,7 @@ private:
     bool seqIdentity_ = true; // vector v currently maps to sequence slot v
     bool ownsCtx_ = true;
     opure_comm *comm_ = nullptr;  // tensor-parallel communicator (not owned)
+    opure_peer *peer_ = nullptr;  // NVLink peer mailboxes of the tensor-parallel group (owned)
     size_t traceWords_ = 0;
     uint32_t maxVec_ = 1;  // token vectors per step: max(maxBatch, prefillChunk)
 };

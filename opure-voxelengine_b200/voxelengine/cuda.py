@@ -105,6 +105,9 @@ _SIGS = {
     "opure_allreduce_sum_f32": [P, P, P, sz], "opure_allreduce_max_u64": [P, P, P, sz],
     "opure_argmax_key_offset": [P, P, u32, u32],
     "opure_sample_filtered": [P, P], "opure_logit_stats": [P, P, u32, u32, sz, P],
+    "opure_peer_create": [P, P, u32, u32, P], "opure_peer_destroy": [P, P, P],
+    "opure_peer_info": [P, P, P, P], "opure_gemv_allreduce": [P, P, P],
+    "opure_peer_argmax": [P, P, P, u32, u32],
 }
 
 
@@ -136,6 +139,17 @@ def _strerror(status: int) -> str:
         return lib().opure_strerror(status).decode()
     except OSError:
         return "library not loaded"
+
+
+def argmax_key(value: float, index: int) -> int:
+    """The kernels' packed argmax key: (orderable fp32 bits << 32) | (0xffffffff - index)."""
+    b = int(np.float32(value).view(np.uint32))
+    b = (~b & 0xFFFFFFFF) if b & 0x80000000 else (b | 0x80000000)
+    return (b << 32) | (0xFFFFFFFF - index)
+
+
+def argmax_key_index(key: int) -> int:
+    return 0xFFFFFFFF - (key & 0xFFFFFFFF)
 
 
 def check(status: int, what: str) -> None:
@@ -274,6 +288,28 @@ class Comm:
     def close(self):
         if getattr(self, "h", None):
             lib().opure_comm_destroy(self.h)
+            self.h = None
+
+
+class Peer:
+    """NVLink peer mailboxes of the ranks of `comm` (opure_peer): collective creation,
+    GEMVs all-reduced inside the kernel, and the argmax-key max over vocabulary shards."""
+
+    def __init__(self, comm: Comm, max_rows: int, timeout_ms: int = 2000):
+        h = C.c_void_p()
+        check(lib().opure_peer_create(comm.ctx.h, comm.h, max_rows, timeout_ms, C.byref(h)), "opure_peer_create")
+        self.h, self.comm, self.ctx = h, comm, comm.ctx
+
+    def gemv_allreduce(self, a: "GemvArgs"):
+        check(lib().opure_gemv_allreduce(self.ctx.h, self.h, C.byref(a)), "opure_gemv_allreduce")
+
+    def argmax(self, keys: "DeviceBuffer", n: int, offset: int):
+        check(lib().opure_peer_argmax(self.ctx.h, self.h, keys.ptr, n, offset), "opure_peer_argmax")
+
+    def close(self, collective: bool = True):
+        if getattr(self, "h", None):
+            check(lib().opure_peer_destroy(self.ctx.h, self.comm.h if collective else None, self.h),
+                  "opure_peer_destroy")
             self.h = None
 
 

@@ -16,17 +16,20 @@ P, u32, u64, f32, i32, f64 = C.c_void_p, C.c_uint32, C.c_uint64, C.c_float, C.c_
 class EngineOptions(C.Structure):
     _fields_ = [("max_new_tokens", u32), ("max_batch", u32), ("max_len", u32), ("page_size", u32),
                 ("page_seed", u64), ("use_graphs", u32), ("attn_scale", f32), ("path", u32),
-                ("phase_trace", u32), ("prefill_chunk", u32), ("kv_window", u32)]
+                ("phase_trace", u32), ("prefill_chunk", u32), ("kv_window", u32),
+                ("tp_allreduce", u32)]
 
 
 PATH_AUTO, PATH_UNFUSED, PATH_FUSED, PATH_FUSED_LAYERS = 0, 1, 2, 3
+TP_AUTO, TP_NCCL = 0, 1
 
 
 class EngineInfo(C.Structure):
     _fields_ = [("vocab", u32), ("hidden", u32), ("inter", u32), ("layers", u32), ("heads", u32),
                 ("kv_heads", u32), ("head_dim", u32), ("max_pos", u32), ("max_len", u32),
                 ("max_batch", u32), ("page_size", u32), ("w_dtype", u32), ("weight_bytes", u64),
-                ("stream_bytes", u64), ("kv_bytes_per_token", u64)]
+                ("stream_bytes", u64), ("kv_bytes_per_token", u64), ("tp_ranks", u32),
+                ("tp_peer", u32)]
 
 
 class Timing(C.Structure):
@@ -197,12 +200,16 @@ class Engine:
                  page_size: int = 64, page_seed: int = 3, use_graphs: bool = True,
                  attn_scale: float = 1.0, max_new_tokens: int = 256, path: int = PATH_AUTO,
                  share: "Engine | None" = None, comm: "cuda.Comm | None" = None,
-                 phase_trace: bool = False, prefill_chunk: int = 0, kv_window: int = 0):
+                 phase_trace: bool = False, prefill_chunk: int = 0, kv_window: int = 0,
+                 tp_allreduce: int = TP_AUTO):
         """With `share`, the engine runs on that engine's ctx (stream), as the draft of a
         speculative pair must; it keeps a reference so the owner outlives it. With `comm`
-        it is that communicator's tensor-parallel shard, on the communicator's ctx."""
+        it is that communicator's tensor-parallel shard, on the communicator's ctx, whose
+        all-reduces run as NVLink peer kernels (`tp_allreduce` TP_AUTO, when every pair of
+        GPUs can map each other's memory) or NCCL calls (TP_NCCL)."""
         o = EngineOptions(max_new_tokens, max_batch, max_len, page_size, page_seed,
-                          int(use_graphs), attn_scale, path, int(phase_trace), prefill_chunk, kv_window)
+                          int(use_graphs), attn_scale, path, int(phase_trace), prefill_chunk, kv_window,
+                          tp_allreduce)
         h = C.c_void_p()
         if comm is not None:
             st = lib().opure_engine_create_tp(model_dir.encode(), comm.ctx.h, comm.h, C.byref(o), C.byref(h))

@@ -3,8 +3,12 @@
 Each rank is a spawned process with its own GPU, ctx and NCCL communicator (the 128-byte
 id comes from the parent); every rank holds its shard of a small Llama-shaped model and
 the ranks all-reduce the o_proj / down_proj partial sums and the argmax keys each step.
-Gates: every rank generates the oracle's tokens exactly (the unsharded model on the CPU).
-Skipped with fewer than 2 GPUs.
+Gates: every rank generates the oracle's tokens exactly (the unsharded model on the CPU),
+on both all-reduce paths (NVLink peer kernels and NCCL). The peer kernels are also checked
+on their own: the all-reduced GEMV against the oracle's sum of the ranks' GEMVs (<= 1e-3
+relative, bit-identical on every rank), the argmax-key max, and a collective that one rank
+never joins, which must end in OPURE_ERR_DEVICE_TIMEOUT on the other rank (a bounded wait,
+no fault). Skipped with fewer than 2 GPUs.
 """
 import multiprocessing as mp
 import os
@@ -13,10 +17,14 @@ import numpy as np
 import pytest
 
 import oracle
+from common import rel_err
 from voxelengine import cuda as cu
 from voxelengine import engine as ve
 
 pytestmark = pytest.mark.gpu
+# The ranks are child processes; one test makes a rank skip a collective. NVLink SHARP
+# (multicast objects) stays off in NCCL, and the peer kernels use plain peer stores only.
+os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
 oracle.set_threads(os.cpu_count() or 1)
 
 MHA = dict(vocab=4096, hidden=512, inter=1024, layers=2, heads=8, kv_heads=8, max_pos=256)
@@ -34,7 +42,80 @@ def _gpus() -> int:
 needs2 = pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
 
 
-def _rank_main(rank, n, uid, model, prompt, budget, q):
+PEER_ROWS, PEER_COLS = 512, 256
+
+
+def peer_problem(rank, nvec, cols=PEER_COLS, rows=PEER_ROWS, seed=0):
+    """Rank `rank`'s shard of a row-split GEMV: W_r [rows, cols] fp16, x_r [nvec, cols],
+    and the residual [nvec, rows] every rank holds."""
+    g = np.random.default_rng(1000 * seed + rank)
+    w = oracle.f32_to_f16(g.standard_normal((rows, cols)).astype(np.float32) * 0.05)
+    x = g.standard_normal((nvec, cols)).astype(np.float32)
+    res = np.random.default_rng(seed).standard_normal((nvec, rows)).astype(np.float32)
+    return w, x, res
+
+
+PEER_CASES = [  # (nvec, epilogue add, rmsnorm prologue, int8 weights)
+    (1, True, False, False), (12, True, False, False), (3, False, True, False), (2, True, False, True)]
+
+
+def _peer_job(cu2, ctx, comm, rank, n, out):
+    peer = cu2.Peer(comm, PEER_ROWS)
+    keep = []
+    for i, (nvec, add, norm, q8) in enumerate(PEER_CASES):
+        w, x, res = peer_problem(rank, nvec, seed=i)
+        a = cu2.GemvArgs()
+        if q8:
+            q, sc = oracle.quantize_q8(w)
+            dw = ctx.to_device(q)
+            a.w, a.w_dtype, a.scale_w, a.scale_x = dw.ptr, cu2.W_Q8, sc, 1.0
+        else:
+            dw = ctx.to_device(w)
+            a.w, a.w_dtype = dw.ptr, cu2.W_F16
+        keep.append(dw)
+        dx, dy = ctx.to_device(x), ctx.to_device(res)
+        keep += [dx, dy]
+        a.rows, a.cols, a.nvec = PEER_ROWS, PEER_COLS, nvec
+        a.x, a.x_stride, a.y, a.y_stride = dx.ptr, PEER_COLS, dy.ptr, PEER_ROWS
+        a.epilogue = cu2.EPI_ADD if add else cu2.EPI_STORE
+        a.residual = dy.ptr if add else None
+        if norm:
+            gain = ctx.to_device(oracle.f32_to_f16(np.linspace(0.5, 1.5, PEER_COLS).astype(np.float32)))
+            keep.append(gain)
+            a.prologue, a.norm_gain, a.eps = cu2.PRO_RMSNORM, gain.ptr, 1e-5
+        peer.gemv_allreduce(a)
+        out[f"y{i}"] = dy.download(np.float32, (nvec, PEER_ROWS))
+    # Argmax keys: rank r's shard holds vocabulary rows [100 r, 100 r + 100); its local
+    # winners are (value 1 + r at row 7 r), (2.0 at row 3) and none (key 0) for the third.
+    vals = [(1.0 + rank, 7 * rank), (2.0, 3), None]
+    packed = np.array([0 if v is None else cu2.argmax_key(v[0], v[1]) for v in vals], np.uint64)
+    keys = ctx.to_device(packed)
+    peer.argmax(keys, 3, 100 * rank)
+    out["keys"] = keys.download(np.uint64, 3)
+    ctx.sync()
+    assert ctx.last_error() == 0
+    peer.close()
+
+
+def _peer_timeout_job(cu2, ctx, comm, rank, n, out):
+    import time
+    peer = cu2.Peer(comm, PEER_ROWS, timeout_ms=300)
+    if rank == 0:
+        w, x, res = peer_problem(rank, 1)
+        dw, dx, dy = ctx.to_device(w), ctx.to_device(x), ctx.to_device(res)
+        a = cu2.GemvArgs()
+        a.w, a.w_dtype, a.rows, a.cols, a.nvec = dw.ptr, cu2.W_F16, PEER_ROWS, PEER_COLS, 1
+        a.x, a.x_stride, a.y, a.y_stride = dx.ptr, PEER_COLS, dy.ptr, PEER_ROWS
+        a.epilogue = cu2.EPI_STORE
+        t0 = time.time()
+        peer.gemv_allreduce(a)   # rank 1 never joins this collective
+        ctx.sync()
+        out["wait_s"] = time.time() - t0
+        out["status"] = ctx.last_error()
+    peer.close()   # collective: rank 1 waits here until rank 0 is done with its mailbox
+
+
+def _rank_main(rank, n, uid, job, q):
     try:
         import sys
         repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -44,7 +125,8 @@ def _rank_main(rank, n, uid, model, prompt, budget, q):
         ctx = cu2.Ctx(rank)
         comm = cu2.Comm(ctx, n, rank, uid, timeout_ms=60000)
         out = {}
-        if model is None:
+        kind = job["kind"]
+        if kind == "allreduce":
             # All-reduce check: rank r contributes r + i; the sum is known.
             buf = ctx.to_device(np.arange(1000, dtype=np.float32) + rank)
             comm.allreduce_sum(buf, 1000)
@@ -53,11 +135,16 @@ def _rank_main(rank, n, uid, model, prompt, budget, q):
             ctx.sync()
             out["sum"] = buf.download(np.float32, 1000)
             out["max"] = keys.download(np.uint64, 2)
+        elif kind == "peer":
+            _peer_job(cu2, ctx, comm, rank, n, out)
+        elif kind == "peer_timeout":
+            _peer_timeout_job(cu2, ctx, comm, rank, n, out)
         else:
-            eng = ve2.Engine(model, max_len=64, comm=comm)
-            toks, _ = eng.generate([prompt], budget)
+            eng = ve2.Engine(job["model"], max_len=64, comm=comm, tp_allreduce=job["tp"])
+            toks, _ = eng.generate([job["prompt"]], job["budget"])
             out["tokens"] = toks[0]
             out["stream_bytes"] = eng.info.stream_bytes
+            out["tp_peer"] = eng.info.tp_peer
             eng.close()
         comm.close()
         ctx.close()
@@ -66,11 +153,11 @@ def _rank_main(rank, n, uid, model, prompt, budget, q):
         q.put((rank, {"error": repr(e)}))
 
 
-def _run(n, model=None, prompt=None, budget=0):
+def _run(n, job):
     uid = cu.comm_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank_main, args=(r, n, uid, model, prompt, budget, q)) for r in range(n)]
+    procs = [ctx.Process(target=_rank_main, args=(r, n, uid, job, q)) for r in range(n)]
     for p in procs:
         p.start()
     res = {}
@@ -88,19 +175,59 @@ def _run(n, model=None, prompt=None, budget=0):
 
 @needs2
 def test_allreduce_two_ranks():
-    res = _run(2)
+    res = _run(2, {"kind": "allreduce"})
     for r in range(2):
         assert np.array_equal(res[r]["sum"], 2 * np.arange(1000, dtype=np.float32) + 1)
         assert list(res[r]["max"]) == [2, 5]
 
 
 @needs2
+def test_peer_gemv_allreduce_matches_oracle():
+    res = _run(2, {"kind": "peer"})
+    for i, (nvec, add, norm, q8) in enumerate(PEER_CASES):
+        want = np.zeros((nvec, PEER_ROWS), np.float64)
+        for r in range(2):
+            w, x, resid = peer_problem(r, nvec, seed=i)
+            if norm:
+                g = oracle.f16_to_f32(oracle.f32_to_f16(np.linspace(0.5, 1.5, PEER_COLS).astype(np.float32)))
+                x = np.stack([oracle.rmsnorm(v, g, 1e-5) for v in x])
+            if q8:
+                qw, sc = oracle.quantize_q8(w)
+                want += oracle.gemv_q8(qw, sc, x)
+            else:
+                want += oracle.gemv_f16(w, x)
+        if add:
+            want += resid
+        for r in range(2):
+            assert rel_err(res[r][f"y{i}"], want) < 1e-3, (i, r)
+        # The replicated residual must stay identical on every rank.
+        assert np.array_equal(res[0][f"y{i}"].view(np.uint32), res[1][f"y{i}"].view(np.uint32)), i
+    # Largest value wins; ties (value 2.0 at global rows 3 and 103) keep the lowest index.
+    keys = res[0]["keys"]
+    assert np.array_equal(keys, res[1]["keys"])
+    assert cu.argmax_key_index(int(keys[0])) == 100 + 7   # rank 1: value 2.0 at 7, vs rank 0's 1.0
+    assert cu.argmax_key_index(int(keys[1])) == 3
+    assert int(keys[2]) == 0
+
+
+@needs2
+def test_peer_collective_times_out_when_a_rank_never_joins():
+    res = _run(2, {"kind": "peer_timeout"})
+    assert res[0]["status"] == cu.ERR_DEVICE_TIMEOUT
+    assert res[0]["wait_s"] < 30
+
+
+@needs2
+@pytest.mark.parametrize("tp", ["peer", "nccl"])
 @pytest.mark.parametrize("shape", ["mha", "gqa"])
-def test_tensor_parallel_generate_matches_oracle(tmp_path, shape):
+def test_tensor_parallel_generate_matches_oracle(tmp_path, shape, tp):
     spec = MHA if shape == "mha" else GQA
     model = ve.synth_model(str(tmp_path / shape), seed=31, **spec)
     prompt = ve.prompt(5, spec["vocab"], 10)
-    res = _run(2, model, prompt, 16)
+    job = {"kind": "generate", "model": model, "prompt": prompt, "budget": 16,
+           "tp": ve.TP_AUTO if tp == "peer" else ve.TP_NCCL}
+    res = _run(2, job)
+    assert res[0]["tp_peer"] == (1 if tp == "peer" else 0)
     want, margins = oracle.Model(model).generate(prompt, 16)
     for r in range(2):
         got = np.asarray(res[r]["tokens"])
