@@ -488,20 +488,25 @@ def run_attention_sweep(args):
                 dseq = ctx.to_device(np.arange(B, dtype=np.int32))
                 dlen = ctx.to_device(np.full(B, ctxlen, np.int32))
                 dout = ctx.buffer(B * nh * hd * 4)
-                sb = cu.attention_scratch_bytes(B, 1, nh, nkv, hd, ctxlen)
-                scratch = ctx.buffer(sb).fill(0)
-                a = cu.AttnArgs()
-                a.q, a.out, a.seq, a.seq_len = dq.ptr, dout.ptr, dseq.ptr, dlen.ptr
-                a.n, a.n_q, a.n_heads, a.scale, a.max_ctx = B, 1, nh, 1.0, ctxlen
-                a.scratch, a.scratch_bytes = scratch.ptr, sb
-                a.kv = cu.KvLayout(pool.ptr, dpt.ptr, pages, ctxlen // P, P, nkv, hd)
                 bytes_ = B * ctxlen * 2 * nkv * hd * 2 + B * nh * hd * 8 + B * (ctxlen // P) * 4
-                iters = max(5, min(200, int(2e9 / bytes_)))
-                ms = _time_events(ctx, lambda i: ctx.attention(a), iters)
-                gbs = bytes_ / (ms * 1e-3) / 1e9
-                out.append({"B": B, "ctx": ctxlen, "us": ms * 1e3, "bytes": bytes_, "GB/s": gbs,
-                            "frac": gbs / peak, "l2": "pool > L2" if bytes_ > 126e6 else "pool fits L2 (upper bound)"})
-                for b in (pool, dq, dpt, dseq, dlen, dout, scratch):
+                for split in args.attn_splits:
+                    sb = cu.attention_scratch_bytes(B, 1, nh, nkv, hd, ctxlen, split)
+                    scratch = ctx.buffer(sb).fill(0)
+                    a = cu.AttnArgs()
+                    a.q, a.out, a.seq, a.seq_len = dq.ptr, dout.ptr, dseq.ptr, dlen.ptr
+                    a.n, a.n_q, a.n_heads, a.scale, a.max_ctx = B, 1, nh, 1.0, ctxlen
+                    a.split_tokens, a.scratch, a.scratch_bytes = split, scratch.ptr, sb
+                    a.kv = cu.KvLayout(pool.ptr, dpt.ptr, pages, ctxlen // P, P, nkv, hd)
+                    iters = max(5, min(200, int(2e9 / bytes_)))
+                    ms = _time_events(ctx, lambda i: ctx.attention(a), iters)
+                    gbs = bytes_ / (ms * 1e-3) / 1e9
+                    pt = {"B": B, "ctx": ctxlen, "us": ms * 1e3, "bytes": bytes_, "GB/s": gbs, "frac": gbs / peak,
+                          "l2": "pool > L2" if bytes_ > 126e6 else "pool fits L2 (upper bound)"}
+                    if split:
+                        pt["split_tokens"] = split
+                    out.append(pt)
+                    scratch.free()
+                for b in (pool, dq, dpt, dseq, dlen, dout):
                     b.free()
     line = {"metric": "paged flash-decode attention HBM GB/s (config 1)", "unit": "GB/s",
             "peak": peak, "peak_kind": kind, "points": out}
@@ -918,6 +923,8 @@ def main():
     ap.add_argument("--wave", type=int, default=128, help="cfg4: sequences per GPU per wave")
     ap.add_argument("--attn-b", type=int, default=0, help="attn: only this batch size (1, 8 or 64)")
     ap.add_argument("--attn-ctx", type=int, default=0, help="attn: only this context length")
+    ap.add_argument("--attn-splits", type=lambda v: [int(x) for x in v.split(",")], default=[0],
+                    help="attn: comma-separated keys per split to time (0: the library's choice)")
     ap.add_argument("--tp-allreduce", choices=["auto", "nccl"], default="auto",
                     help="tp: NVLink peer kernels (auto, when every GPU pair maps each other's memory) or NCCL")
     ap.add_argument("--quick", action="store_true",

@@ -133,10 +133,99 @@ __host__ __device__ inline uint32_t stage_count(uint32_t page_bytes_kv) {
     return n < 2 ? 2u : (n > uint32_t(kMaxStages) ? uint32_t(kMaxStages) : n);
 }
 
+// One staged page through this warp's rounds (round rr covers page rows rr*TPW ..
+// rr*TPW + TPW-1; warp w takes rounds w, w + kWarps, ...), R rounds per softmax block.
+// CHECK masks rows outside [t_begin, t_end) (an empty range masks the whole page). The
+// running state is rescaled only when a block raises the running max (the factor would be
+// exactly 1 otherwise).
+template <int HD, int G, int R, bool CHECK>
+__device__ __forceinline__ void consume_page(AttnState<HD, G> &st, const float (&qv)[G][AttnShape<HD>::E],
+                                             const __half *ks, const __half *vs, uint32_t warp, uint32_t rounds,
+                                             uint32_t tok0, uint32_t t_begin, uint32_t t_end) {
+    using S = AttnShape<HD>;
+    constexpr int LPT = S::LPT, CH = S::CH, TPW = S::TPW, E = S::E;
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t grp = lane / LPT, sub = lane % LPT;
+    for (uint32_t r0 = warp; r0 < rounds; r0 += kWarps * R) {
+        uint4 kr[R][CH], vr[R][CH];
+        bool valid[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const uint32_t rr = r0 + r * kWarps;
+            const uint32_t row = rr * TPW + grp;
+            valid[r] = rr < rounds;
+            if (CHECK) valid[r] = valid[r] && tok0 + row >= t_begin && tok0 + row < t_end;
+#pragma unroll
+            for (int c = 0; c < CH; ++c) {
+                kr[r][c] = valid[r] ? *reinterpret_cast<const uint4 *>(ks + size_t(row) * HD + sub * E + c * 8)
+                                    : make_uint4(0, 0, 0, 0);
+                vr[r][c] = valid[r] ? *reinterpret_cast<const uint4 *>(vs + size_t(row) * HD + sub * E + c * 8)
+                                    : make_uint4(0, 0, 0, 0);
+            }
+        }
+        float sc[R][G];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            float kf[E];
+#pragma unroll
+            for (int c = 0; c < CH; ++c) unpack8(kr[r][c], kf + 8 * c);
+#pragma unroll
+            for (int h = 0; h < G; ++h) {
+                // Packed fp32x2 FMAs (sm_100): even and odd dims in two accumulators.
+                float2 d2 = make_float2(0.f, 0.f);
+#pragma unroll
+                for (int e = 0; e < E; e += 2)
+                    d2 = __ffma2_rn(make_float2(qv[h][e], qv[h][e + 1]), make_float2(kf[e], kf[e + 1]), d2);
+                float d = d2.x + d2.y;
+#pragma unroll
+                for (int o = LPT / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+                sc[r][h] = valid[r] ? d : -INFINITY;
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+            float mb = sc[0][h];
+#pragma unroll
+            for (int r = 1; r < R; ++r) mb = fmaxf(mb, sc[r][h]);
+            if (mb > st.m[h]) {  // also the first valid block (m = -inf)
+                const float corr = fast_exp2(st.m[h] - mb);
+                st.l[h] *= corr;
+                const float2 c2 = make_float2(corr, corr);
+#pragma unroll
+                for (int e = 0; e < E; e += 2) {
+                    const float2 a = __fmul2_rn(make_float2(st.acc[h][e], st.acc[h][e + 1]), c2);
+                    st.acc[h][e] = a.x;
+                    st.acc[h][e + 1] = a.y;
+                }
+                st.m[h] = mb;
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            if (!valid[r]) continue;
+            float vf[E];
+#pragma unroll
+            for (int c = 0; c < CH; ++c) unpack8(vr[r][c], vf + 8 * c);
+#pragma unroll
+            for (int h = 0; h < G; ++h) {
+                const float pr = fast_exp2(sc[r][h] - st.m[h]);
+                st.l[h] += pr;
+                const float2 p2 = make_float2(pr, pr);
+#pragma unroll
+                for (int e = 0; e < E; e += 2) {
+                    const float2 a = __ffma2_rn(p2, make_float2(vf[e], vf[e + 1]), make_float2(st.acc[h][e], st.acc[h][e + 1]));
+                    st.acc[h][e] = a.x;
+                    st.acc[h][e + 1] = a.y;
+                }
+            }
+        }
+    }
+}
+
 template <int HD, int G>
 __global__ void __launch_bounds__((kWarps + 1) * 32) attn_tma_kernel(AttnParams p) {
     using S = AttnShape<HD>;
-    constexpr int LPT = S::LPT, CH = S::CH, TPW = S::TPW, E = S::E;
+    constexpr int TPW = S::TPW, E = S::E;
     constexpr int R = 4;  // rounds per consumer block
     extern __shared__ __align__(128) uint8_t stage_mem[];
     __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages];
@@ -227,7 +316,6 @@ __global__ void __launch_bounds__((kWarps + 1) * 32) attn_tma_kernel(AttnParams 
     } else {
         float qv[G][E];
         load_q_slice<HD, G>(p.q + size_t(entry) * p.n_heads * HD, g, p.scale_log2, qv);
-        const uint32_t grp = lane / LPT, sub = lane % LPT;
         const uint32_t rounds = P / TPW;  // token rounds per page
         for (uint32_t it = 0; it < n_pg; ++it) {
             const uint32_t s = it % n_stages;
@@ -239,68 +327,11 @@ __global__ void __launch_bounds__((kWarps + 1) * 32) attn_tma_kernel(AttnParams 
             const __half *ks = reinterpret_cast<const __half *>(stage_mem + size_t(s) * 2 * page_bytes);
             const __half *vs = ks + page_elems;
             const uint32_t tok0 = (pg_begin + it) * P;
-            for (uint32_t r0 = warp; r0 < rounds; r0 += kWarps * R) {
-                uint4 kr[R][CH], vr[R][CH];
-                bool valid[R], live[R];
-#pragma unroll
-                for (int r = 0; r < R; ++r) {
-                    const uint32_t rr = r0 + r * kWarps;
-                    live[r] = rr < rounds;
-                    const uint32_t row = rr * TPW + grp;
-                    const uint32_t t = tok0 + row;
-                    valid[r] = live[r] && page_ok && t >= t_begin && t < t_end;
-#pragma unroll
-                    for (int c = 0; c < CH; ++c) {
-                        kr[r][c] = valid[r] ? *reinterpret_cast<const uint4 *>(ks + size_t(row) * HD + sub * E + c * 8)
-                                            : make_uint4(0, 0, 0, 0);
-                        vr[r][c] = valid[r] ? *reinterpret_cast<const uint4 *>(vs + size_t(row) * HD + sub * E + c * 8)
-                                            : make_uint4(0, 0, 0, 0);
-                    }
-                }
-                float sc[R][G];
-#pragma unroll
-                for (int r = 0; r < R; ++r) {
-                    float kf[E];
-#pragma unroll
-                    for (int c = 0; c < CH; ++c) unpack8(kr[r][c], kf + 8 * c);
-#pragma unroll
-                    for (int h = 0; h < G; ++h) {
-                        float d = 0.f;
-#pragma unroll
-                        for (int e = 0; e < E; ++e) d = fmaf(qv[h][e], kf[e], d);
-#pragma unroll
-                        for (int o = LPT / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-                        sc[r][h] = valid[r] ? d : -INFINITY;
-                    }
-                }
-#pragma unroll
-                for (int h = 0; h < G; ++h) {
-                    float mb = sc[0][h];
-#pragma unroll
-                    for (int r = 1; r < R; ++r) mb = fmaxf(mb, sc[r][h]);
-                    const float mn = fmaxf(st.m[h], mb);
-                    if (mn == -INFINITY) continue;
-                    const float corr = fast_exp2(st.m[h] - mn);
-                    st.l[h] *= corr;
-#pragma unroll
-                    for (int e = 0; e < E; ++e) st.acc[h][e] *= corr;
-                    st.m[h] = mn;
-                }
-#pragma unroll
-                for (int r = 0; r < R; ++r) {
-                    if (!valid[r]) continue;
-                    float vf[E];
-#pragma unroll
-                    for (int c = 0; c < CH; ++c) unpack8(vr[r][c], vf + 8 * c);
-#pragma unroll
-                    for (int h = 0; h < G; ++h) {
-                        const float pr = fast_exp2(sc[r][h] - st.m[h]);
-                        st.l[h] += pr;
-#pragma unroll
-                        for (int e = 0; e < E; ++e) st.acc[h][e] = fmaf(pr, vf[e], st.acc[h][e]);
-                    }
-                }
-            }
+            // Pages wholly inside the split skip the per-row range checks.
+            if (page_ok && tok0 >= t_begin && tok0 + P <= t_end)
+                consume_page<HD, G, R, false>(st, qv, ks, vs, warp, rounds, tok0, t_begin, t_end);
+            else
+                consume_page<HD, G, R, true>(st, qv, ks, vs, warp, rounds, tok0, page_ok ? t_begin : t_end, t_end);
             __syncwarp();
             if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&empty[s])) : "memory");
         }
@@ -333,9 +364,11 @@ __global__ void __launch_bounds__((kWarps + 1) * 32) attn_tma_kernel(AttnParams 
     for (uint32_t idx = threadIdx.x; idx < uint32_t(G) * HD; idx += blockDim.x) {
         const uint32_t h = idx / HD, d = idx % HD;
         float mn = -INFINITY;
+#pragma unroll 8  // independent loads: several splits in flight
         for (uint32_t sp = 0; sp < n_splits; ++sp)
             mn = fmaxf(mn, __ldcg(parts + (size_t(sp) * G + h) * (HD + 2) + HD));
         float a = 0.f, lsum = 0.f;
+#pragma unroll 8  // independent loads: several splits in flight
         for (uint32_t sp = 0; sp < n_splits; ++sp) {
             const float *pp = parts + (size_t(sp) * G + h) * (HD + 2);
             const float ms = __ldcg(pp + HD);
@@ -409,14 +442,21 @@ uint32_t choose_split(uint32_t entries, uint32_t n_kv, uint32_t hd, uint32_t max
                       uint32_t requested, int sm_count) {
     if (tma_path(hd)) {
         // Splits are whole multiples of 128 tokens, so pages of 16..128 tokens never straddle
-        // two splits. About one wave of three CTAs per SM (rounded to the nearest whole split
-        // count, so a second, mostly empty wave is avoided).
+        // two splits. Enough splits for about one wave of three CTAs per SM (at most 32: the
+        // last CTA of each (entry, kv head) merges every split). When that leaves fewer than
+        // three waves and splits of at most 3072 tokens would give three or more, those are
+        // taken instead: many mid-sized CTAs even out the SMs' shares of a large batch, while
+        // a grid between one and three waves loses more to its partial last wave than it
+        // gains. Measured on B200 over split sizes 256..16384 for 1, 8 and 64 sequences at
+        // 8192 and 32768 tokens, and on the 1.7B model's 2048 (sequence, kv head) pairs.
         const uint32_t unit = 128;
         if (requested) return ((requested + unit - 1) / unit) * unit;
         const uint64_t pairs = uint64_t(entries) * n_kv;
-        const uint64_t target = uint64_t(sm_count > 0 ? sm_count : 148) * 3;
-        const uint64_t near = std::max<uint64_t>(1, (target + pairs / 2) / pairs);
-        const uint64_t want = std::min<uint64_t>(near, std::max<uint64_t>(1, max_ctx / unit));
+        const uint64_t wave = uint64_t(sm_count > 0 ? sm_count : 148) * 3;
+        uint64_t want = std::min<uint64_t>(32, std::max<uint64_t>(1, (wave + pairs / 2) / pairs));
+        const uint64_t by_len = (uint64_t(max_ctx) + 3071) / 3072;
+        if (pairs * want < 3 * wave && pairs * by_len >= 3 * wave) want = by_len;
+        want = std::min<uint64_t>(want, std::max<uint64_t>(1, max_ctx / unit));
         const uint64_t per = (uint64_t(std::max(max_ctx, 1u)) + want - 1) / want;
         return uint32_t(std::max<uint64_t>(unit, ((per + unit - 1) / unit) * unit));
     }
