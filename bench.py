@@ -633,8 +633,9 @@ def run_tp(args, world, rank, local):
     """Config 4, second variant: batch-1 greedy decode of the 1.7B shape with world-way tensor
     parallelism, one rank per GPU. Every step all-reduces the o_proj and down_proj partial
     sums of each layer (48 x 8 KB fp32 per token) and the vocabulary shards' argmax keys
-    (8 B): by default inside the producing kernels over NVLink peer memory
-    (opure_gemv_allreduce / opure_peer_argmax), with --tp-allreduce nccl as NCCL calls. 32-token prompt (seed 1) prefilled, then device-resident steps
+    (8 B): as NCCL calls, or inside the producing kernels over NVLink peer memory
+    (opure_gemv_allreduce / opure_peer_argmax) with --tp-allreduce peer (auto: NCCL at 2
+    ranks, peer kernels from 4). 32-token prompt (seed 1) prefilled, then device-resident steps
     (graph replays, NCCL inside the graph) at positions 32..159 (cyclic). Device time, max
     over ranks. `comm_us` is one 2048-float all-reduce timed on its own (100-call average)."""
     import ctypes as C
@@ -654,7 +655,7 @@ def run_tp(args, world, rank, local):
         dist.broadcast_object_list(obj, src=0)
     ctx = cu.Ctx(local)
     comm = cu.Comm(ctx, world, rank, obj[0], timeout_ms=120000)
-    tp_mode = ve.TP_NCCL if args.tp_allreduce == "nccl" else ve.TP_AUTO
+    tp_mode = {"auto": ve.TP_AUTO, "nccl": ve.TP_NCCL, "peer": ve.TP_PEER}[args.tp_allreduce]
     eng = ve.Engine(mp, max_len=PROMPT_LEN + DECODE_STEPS + 8, comm=comm, tp_allreduce=tp_mode)
     info = eng.info
     L = cu.lib()
@@ -925,8 +926,8 @@ def main():
     ap.add_argument("--attn-ctx", type=int, default=0, help="attn: only this context length")
     ap.add_argument("--attn-splits", type=lambda v: [int(x) for x in v.split(",")], default=[0],
                     help="attn: comma-separated keys per split to time (0: the library's choice)")
-    ap.add_argument("--tp-allreduce", choices=["auto", "nccl"], default="auto",
-                    help="tp: NVLink peer kernels (auto, when every GPU pair maps each other's memory) or NCCL")
+    ap.add_argument("--tp-allreduce", choices=["auto", "nccl", "peer"], default="auto",
+                    help="tp: NCCL or NVLink peer kernels (auto: NCCL at 2 ranks, peer kernels from 4)")
     ap.add_argument("--quick", action="store_true",
                     help="minimal run for profiler launch lists: no parity, e2e or CPU legs")
     args = ap.parse_args()

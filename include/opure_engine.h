@@ -44,14 +44,16 @@ typedef struct opure_engine_options {
                                  tokens of pages as a ring (opure_kv_layout.ring) and a
                                  position attends to the last kv_window / page_size - 1 whole
                                  pages and its own; 0: every position up to max_len */
-    uint32_t tp_allreduce;    /* tensor parallel: OPURE_TP_* (0: peer kernels when every pair
-                                 of ranks can map each other's memory, else NCCL)        */
+    uint32_t tp_allreduce;    /* tensor parallel: OPURE_TP_* (0: OPURE_TP_AUTO)          */
 } opure_engine_options;
 
 enum {
-    OPURE_TP_AUTO = 0,        /* opure_gemv_allreduce / opure_peer_argmax over NVLink peer
-                                 memory when available, else NCCL                         */
-    OPURE_TP_NCCL = 1         /* NCCL all-reduces between the per-op kernels             */
+    OPURE_TP_AUTO = 0,        /* NCCL at 2 ranks (measured faster there); the peer kernels
+                                 from 4 ranks, when every pair of GPUs maps each other's
+                                 memory (else NCCL)                                        */
+    OPURE_TP_NCCL = 1,        /* NCCL all-reduces between the per-op kernels             */
+    OPURE_TP_PEER = 2         /* opure_gemv_allreduce / opure_peer_argmax over NVLink peer
+                                 memory at any rank count (NCCL if it cannot be mapped)    */
 };
 
 enum {

@@ -94,7 +94,13 @@ void VoxelEngine::Initialize(const std::string &modelDir, const EngineOptions &o
                ring);
     maxVec_ = std::max(opts.maxBatch, opts.prefillChunk);
     AllocBuffers();
-    if (comm && opts.tpAllreduce == 0) {
+    // At 2 ranks NCCL's 8 KB all-reduce inside the step graph took 9.3 us against 19 us for
+    // the fused GEMV + peer exchange (B200, 1.7B shape), so auto keeps NCCL there; from 4
+    // ranks (NCCL: 26 us per all-reduce at 8) it takes the peer kernels.
+    uint32_t tpRanks = 1;
+    if (comm) OPURE_CUDA_CHECK(opure_comm_info(comm, &tpRanks, nullptr));
+    const bool wantPeer = opts.tpAllreduce == 2 || (opts.tpAllreduce == 0 && tpRanks >= 4);
+    if (comm && wantPeer) {
         // NVLink peer mailboxes for the fused all-reduces; every rank falls back to NCCL
         // together when any pair of GPUs cannot map each other's memory.
         const opure_status ps = opure_peer_create(ctx_, comm, cfg.hiddenSize, 2000, &peer_);

@@ -21,7 +21,7 @@ class EngineOptions(C.Structure):
 
 
 PATH_AUTO, PATH_UNFUSED, PATH_FUSED, PATH_FUSED_LAYERS = 0, 1, 2, 3
-TP_AUTO, TP_NCCL = 0, 1
+TP_AUTO, TP_NCCL, TP_PEER = 0, 1, 2
 
 
 class EngineInfo(C.Structure):
@@ -205,8 +205,9 @@ class Engine:
         """With `share`, the engine runs on that engine's ctx (stream), as the draft of a
         speculative pair must; it keeps a reference so the owner outlives it. With `comm`
         it is that communicator's tensor-parallel shard, on the communicator's ctx, whose
-        all-reduces run as NVLink peer kernels (`tp_allreduce` TP_AUTO, when every pair of
-        GPUs can map each other's memory) or NCCL calls (TP_NCCL)."""
+        all-reduces run as NCCL calls (`tp_allreduce` TP_NCCL, and TP_AUTO at 2 ranks) or
+        as NVLink peer kernels (TP_PEER, and TP_AUTO from 4 ranks, when every pair of GPUs
+        can map each other's memory)."""
         o = EngineOptions(max_new_tokens, max_batch, max_len, page_size, page_seed,
                           int(use_graphs), attn_scale, path, int(phase_trace), prefill_chunk, kv_window,
                           tp_allreduce)

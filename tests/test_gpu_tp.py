@@ -225,7 +225,7 @@ def test_tensor_parallel_generate_matches_oracle(tmp_path, shape, tp):
     model = ve.synth_model(str(tmp_path / shape), seed=31, **spec)
     prompt = ve.prompt(5, spec["vocab"], 10)
     job = {"kind": "generate", "model": model, "prompt": prompt, "budget": 16,
-           "tp": ve.TP_AUTO if tp == "peer" else ve.TP_NCCL}
+           "tp": ve.TP_PEER if tp == "peer" else ve.TP_NCCL}
     res = _run(2, job)
     assert res[0]["tp_peer"] == (1 if tp == "peer" else 0)
     want, margins = oracle.Model(model).generate(prompt, 16)
