@@ -479,10 +479,10 @@ opure_status launch_attention(opure_ctx *ctx, const AttnParams &p, uint32_t hd, 
         if (!k) return OPURE_ERR_UNSUPPORTED;
         const uint32_t page_bytes = p.kv.page_size * hd * 2;
         const size_t smem = size_t(stage_count(2 * page_bytes)) * 2 * page_bytes;
-        if (smem > 48 * 1024) {
-            const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-            if (e != cudaSuccess) return cuda_status(e);
-        }
+        // Always: the dynamic stages plus the kernel's static shared memory may pass the
+        // default 48 KB per-block limit even when the stages alone do not.
+        const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        if (e != cudaSuccess) return cuda_status(e);
         return launch(ctx, k, dim3(pairs, n_splits), dim3((kWarps + 1) * 32), smem, true, p);
     }
     AttnKernel k = pick(hd, G);
