@@ -185,14 +185,22 @@ opure_status opure_fill(opure_ctx *ctx, void *dst, uint8_t byte, size_t n) {
 opure_status opure_sync(opure_ctx *ctx, uint32_t timeout_ms) {
     opure_status s = enter(ctx);
     if (s) return s;
-    // Poll instead of blocking so a wedged stream surfaces as a timeout.
-    const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(timeout_ms);
-    for (uint32_t spin = 0;; ++spin) {
+    // Poll instead of blocking so a wedged stream surfaces as a timeout. The first 2 ms
+    // poll without sleeping (a decode step is ~0.5 ms, and a sleep of a few microseconds
+    // wakes tens of microseconds late under the kernel's timer slack); longer waits sleep.
+    const auto t0 = std::chrono::steady_clock::now();
+    const auto deadline = t0 + std::chrono::milliseconds(timeout_ms);
+    const auto spin_until = t0 + std::chrono::milliseconds(2);
+    for (;;) {
         cudaError_t e = cudaStreamQuery(ctx->stream);
         if (e == cudaSuccess) return OPURE_OK;
         if (e != cudaErrorNotReady) return opure::cuda_status(e);
-        if (std::chrono::steady_clock::now() >= deadline) return OPURE_ERR_TIMEOUT;
-        if (spin > 64) std::this_thread::sleep_for(std::chrono::microseconds(20));
+        const auto now = std::chrono::steady_clock::now();
+        if (now >= deadline) return OPURE_ERR_TIMEOUT;
+        if (now < spin_until)
+            std::this_thread::yield();
+        else
+            std::this_thread::sleep_for(std::chrono::microseconds(20));
     }
 }
 
