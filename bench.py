@@ -45,8 +45,10 @@ PROMPT_LEN, DECODE_STEPS = 32, 128
 FALLBACK_PEAK = 6650.0  # GB/s, used only when MEASURED_PEAKS.json is absent
 # DRAM bytes (read + write) of one decode step, summed over its launches in an ncu capture
 # of `python bench.py --quick --no-cpu [--batch B] --steps 2 --warmup 3` (launch lists in
-# profiles/decode_bs1_persistent_step.md and profiles/decode_bs64_tensor_core_step.md).
-NCU_STEP_TRAFFIC = {1: 271.8e6, 64: 411.0e6}
+# profiles/decode_bs1_persistent_step.md and profiles/decode_bs64_tensor_core_step.md). The
+# batch-64 figure is the latest capture, taken while the attention kernel still copied whole
+# KV pages (it now copies only the rows below each split's end).
+NCU_STEP_TRAFFIC = {1: 271.8e6, 64: 452.3e6}
 
 
 def peaks():

@@ -295,9 +295,13 @@ __global__ void __launch_bounds__((kWarps + 1) * 32) attn_tma_kernel(AttnParams 
                         stage_ok[s] = 1;
                         const __half *kp = pool + (size_t(page) * 2 * n_kv + g) * page_elems;
                         uint8_t *dst = stage_mem + size_t(s) * 2 * page_bytes;
-                        mbar_expect_tx(&full[s], 2 * page_bytes);
-                        bulk_load_keep(dst, kp, page_bytes, &full[s]);
-                        bulk_load_keep(dst + page_bytes, kp + size_t(n_kv) * page_elems, page_bytes, &full[s]);
+                        // Only the page's rows below t_end (a prefix of the K and V blocks):
+                        // a sequence's last page is usually partly filled.
+                        const uint32_t rows = min(P, t_end - (pg_begin + it) * P);
+                        const uint32_t bytes = rows * HD * 2;
+                        mbar_expect_tx(&full[s], 2 * bytes);
+                        bulk_load_keep(dst, kp, bytes, &full[s]);
+                        bulk_load_keep(dst + page_bytes, kp + size_t(n_kv) * page_elems, bytes, &full[s]);
                         ++issued;
                     }
                 }
