@@ -43,11 +43,10 @@ for p in (REPO, PKG):
 METRIC = "decode tok/s (bs1, bs64) at SmolLM-135M shape; GEMV+attn HBM GB/s as % of peak"
 PROMPT_LEN, DECODE_STEPS = 32, 128
 FALLBACK_PEAK = 6650.0  # GB/s, used only when MEASURED_PEAKS.json is absent
-# DRAM bytes (read + write) of one decode step, summed over its launches in an ncu capture
-# of `python bench.py --quick --no-cpu [--batch B] --steps 2 --warmup 3` (launch lists in
-# profiles/decode_bs1_persistent_step.md and profiles/decode_bs64_tensor_core_step.md). The
-# batch-64 figure is the latest capture, taken while the attention kernel still copied whole
-# KV pages (it now copies only the rows below each split's end).
+# DRAM bytes (read + write) of one decode step from ncu captures of this build:
+# `ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum
+#  --clock-control none -k regex:<kernel> -c <n> python bench.py --quick --no-cpu [--batch B]
+#  --steps 2 --warmup 3`, per kernel over a few launches, summed over one step's launches.
 NCU_STEP_TRAFFIC = {1: 271.8e6, 64: 452.3e6}
 
 
@@ -74,43 +73,63 @@ def step_bytes(info, batch: int, positions) -> float:
     return info.stream_bytes + batch * (kv_row * mean_ctx + kv_row + info.hidden * 2)
 
 
+def smi_index(local: int) -> int:
+    """nvidia-smi's index of this rank's GPU (CUDA_VISIBLE_DEVICES maps CUDA ordinals)."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "").strip()
+    if vis:
+        parts = [v.strip() for v in vis.split(",")]
+        if local < len(parts) and parts[local].isdigit():
+            return int(parts[local])
+    return local
+
+
 class ClockSampler:
-    """nvidia-smi samples during the timed region (clocks, power, throttle reasons)."""
+    """nvidia-smi samples of ONE GPU (clocks, power, throttle reasons), each stamped on
+    arrival; stop() keeps only those inside the window marked by mark_begin/mark_end."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self):
-        self.rows, self.proc = [], None
+    def __init__(self, gpu_index: int):
+        self.rows, self.proc, self.gpu = [], None, gpu_index
+        self.t0 = self.t1 = None
 
     def start(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "20"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
         except OSError:
             self.proc = None
 
+    def mark_begin(self):
+        self.t0 = time.monotonic()
+
+    def mark_end(self):
+        self.t1 = time.monotonic()
+
     def _read(self):
         for line in self.proc.stdout:
-            self.rows.append([c.strip() for c in line.split(",")])
+            self.rows.append((time.monotonic(), [c.strip() for c in line.split(",")]))
 
-    def stop(self):
+    def stop(self, window: str):
         if not self.proc:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
         self.proc.wait()
         self.t.join(timeout=2)
-        sm = [float(r[1]) for r in self.rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
+        rows = [r for t, r in self.rows if len(r) >= 9 and r[0] == str(self.gpu)
+                and self.t0 is not None and self.t0 <= t <= (self.t1 or t)]
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows if len(r) >= 9
-                          for i, v in enumerate(r[5:9]) if v.lower() == "active"})
+        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[5:9]) if v.lower() == "active"})
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "samples": len(sm), "reasons": reasons}
+                "samples": len(sm), "gpu_index": self.gpu, "window": window, "reasons": reasons}
 
 
 def dist_init():
@@ -148,6 +167,16 @@ def allreduce_sum(world, x: float) -> float:
     return float(t.item())
 
 
+def gather_objects(world, obj):
+    """Every rank's `obj`, in rank order (a list of one at world 1)."""
+    if world == 1:
+        return [obj]
+    import torch.distributed as dist
+    out = [None] * world
+    dist.all_gather_object(out, obj)
+    return out
+
+
 def allreduce_max(world, x: float) -> float:
     if world == 1:
         return x
@@ -159,51 +188,114 @@ def allreduce_max(world, x: float) -> float:
 
 
 # ---- CPU side (the oracle: a port of the reference's scalar C++ forward) ----------------
-def cpu_decode(model_path: str, steps: int, warmup: int, batch: int, threads: int):
-    """Times `steps` decode tokens (after `warmup`) of config 0 on the CPU oracle, one
-    sequence at a time with the GEMV rows spread over `threads` host threads (rows are
-    independent; results equal the single-thread ones). Returns (tok/s, tokens, seconds)."""
+# Everything here uses the oracle alone (test infrastructure): its own seeded model and
+# prompts, byte-identical to the engine's, so the reference arm loads no product library.
+def cpu_model():
     import oracle
-    from voxelengine import engine as ve
+    return oracle.Model.synth(seed=0)
+
+
+def cpu_decode(m, steps: int, warmup: int, threads: int):
+    """Config 0 at batch 1 on the CPU oracle: the 32-token prompt (seed 1) prefilled, then
+    `steps` timed greedy tokens after `warmup` untimed ones at positions 32..159 (cyclic, as
+    the GPU arm), with the GEMV rows spread over `threads` host threads (rows are
+    independent; the results equal the one-thread ones). Returns (tok/s, tokens, seconds)."""
+    import oracle
     oracle.set_threads(threads)
-    m = oracle.Model(model_path)
     st = m.state(PROMPT_LEN + DECODE_STEPS + 1)
-    prompt = ve.prompt(1, 49152, PROMPT_LEN)
+    prompt = oracle.prompt(1, 49152, PROMPT_LEN)
     logits = None
     for i, t in enumerate(prompt):
         logits, _ = st.forward(int(t), logits=(i == PROMPT_LEN - 1))
     tok = int(np.argmax(logits))
-    done = 0
-    t0 = None
+    done, t0 = 0, None
     for s in range(warmup + steps):
         if s == warmup:
             t0 = time.perf_counter()
         if len(st) >= PROMPT_LEN + DECODE_STEPS:
-            st.truncate(PROMPT_LEN)  # cyclic positions 32..159, as the GPU arm
+            st.truncate(PROMPT_LEN)
         logits, _ = st.forward(tok)
         tok = int(np.argmax(logits))
-        if s >= warmup:
-            done += 1
+        done += s >= warmup
     dt = time.perf_counter() - t0
-    return batch * done / dt * 1.0 / batch, done, dt
+    return done / dt, done, dt
+
+
+def cpu_decode_sequences(m, n_seq: int, steps: int):
+    """The reference's CPU path as a server would run it on this host: `n_seq` independent
+    config-0 sequences (prompt seeds 1..n_seq), one per host thread, each computing
+    serially. All threads prefill, meet at a barrier, then time `steps` greedy tokens each.
+    Returns (aggregate tok/s, seconds)."""
+    import oracle
+    oracle.set_threads(1)
+    bar = threading.Barrier(n_seq + 1)
+    err = []
+
+    def worker(b):
+        try:
+            oracle.thread_serial(True)
+            st = m.state(PROMPT_LEN + steps + 2)
+            logits = None
+            for i, t in enumerate(oracle.prompt(1 + b, 49152, PROMPT_LEN)):
+                logits, _ = st.forward(int(t), logits=(i == PROMPT_LEN - 1))
+            tok = int(np.argmax(logits))
+            bar.wait()
+            for _ in range(steps):
+                logits, _ = st.forward(tok)
+                tok = int(np.argmax(logits))
+            bar.wait()
+        except Exception as e:  # keep the barrier from hanging the others
+            err.append(e)
+            bar.abort()
+
+    ts = [threading.Thread(target=worker, args=(b,)) for b in range(n_seq)]
+    for t in ts:
+        t.start()
+    bar.wait()
+    t0 = time.perf_counter()
+    bar.wait()
+    dt = time.perf_counter() - t0
+    for t in ts:
+        t.join()
+    if err:
+        raise err[0]
+    return n_seq * steps / dt, dt
+
+
+def cpu_baseline_record(m, steps: int, warmup: int):
+    """The CPU baseline of the config-0 line: batch 1 with the GEMV rows over every host
+    thread (the line's value), the same on one thread, and independent sequences, one per
+    host thread (the reference CPU path's throughput on this host)."""
+    threads = os.cpu_count() or 1
+    tps, done, dt = cpu_decode(m, steps, warmup, threads)
+    one, done1, _ = cpu_decode(m, max(4, min(steps, 8)), 1, 1)
+    seq_tps, _ = cpu_decode_sequences(m, threads, 4)
+    return {"value": tps, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{done} config-0 decode tokens of one sequence (positions 32..159 cyclic) after a "
+                      f"{PROMPT_LEN}-token prefill and {warmup} untimed tokens, GEMV rows over {threads} threads",
+            "one_thread": {"value": one, "unit": "tok/s", "cores": 1, "sample": f"{done1} tokens, batch 1"},
+            "independent_sequences": {"value": seq_tps, "unit": "tok/s", "cores": threads, "batch": threads,
+                                      "sample": f"{threads} config-0 sequences (prompt seeds 1..{threads}), one per "
+                                                "thread, 4 timed tokens each after their prefills"}}
 
 
 def run_reference(args, world, rank):
+    """The reference arm: the CPU oracle (a port of the reference's scalar C++ forward; its
+    own CPU reference includes <windows.h> and cannot be built here) on this host's cores,
+    same metric, unit and config-0 workload as the GPU arm, batch 1."""
     if rank != 0:
         return
-    mp = model_dir()
-    threads = os.cpu_count() or 1
-    tps, done, dt = cpu_decode(mp, args.steps, args.warmup, args.batch, threads)
+    m = cpu_model()
+    rec = cpu_baseline_record(m, args.steps, args.warmup)
+    tps = rec["value"]
     line = {
         "impl": "reference", "metric": METRIC, "value": tps, "unit": "tok/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / max(done, 1) * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / tps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64 accumulate, f16 weights/KV",
         "data": "synthetic",
-        "config": {"workload": "cfg0 decode, SmolLM-135M shape, bs1, positions 32..159 cyclic",
-                   "global_batch": 1, "seq_len": PROMPT_LEN + DECODE_STEPS},
-        "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": threads, "kind": "port",
-                         "sample": f"{done} decode tokens of one config-0 sequence after a "
-                                   f"{PROMPT_LEN}-token prefill and {args.warmup} warm-up tokens"},
+        "config": {"workload": "cfg0 greedy decode, SmolLM-135M shape, bs1, 32-token prompt, decode positions "
+                               "32..159 cyclic", "global_batch": 1, "seq_len": PROMPT_LEN + DECODE_STEPS},
+        "cpu_baseline": rec,
         "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -236,10 +328,14 @@ def phase_stats(t: np.ndarray, n_layers: int) -> dict:
     return out
 
 
-def device_steps(eng, B: int, steps: int, warmup: int, world: int, sample_clocks: bool):
+def device_steps(eng, B: int, steps: int, warmup: int, world: int, sample_clocks: bool, local: int = 0):
     """Times `steps` device-resident decode steps of sequences 0..B-1 (graph replays, no host
     round trip; positions rewound to 32 every 128 steps, so every step has config-0 context
-    lengths) after `warmup` untimed ones. Returns (device ms, max over ranks; clock record)."""
+    lengths) after `warmup` untimed ones. Returns (device ms, max over ranks; clock record).
+
+    The clock record holds the nvidia-smi samples of this GPU taken from the start of the
+    timed steps to the end of an untimed continuation of the same steps lasting at least
+    0.5 s: a short timed region (tens of steps of ~0.5 ms) ends before the next sample."""
     import ctypes as C
 
     from voxelengine import cuda as cu
@@ -271,18 +367,26 @@ def device_steps(eng, B: int, steps: int, warmup: int, world: int, sample_clocks
     ev0, ev1 = _events(ctx)
     run(warmup)
     cu.check(L.opure_sync(ctx, 600000), "sync")
-    sampler = ClockSampler() if sample_clocks else None
+    sampler = ClockSampler(smi_index(local)) if sample_clocks else None
     barrier(world)
     if sampler:
         sampler.start()
-        time.sleep(0.2)
+        time.sleep(0.3)  # nvidia-smi's first sample
+        sampler.mark_begin()
     cu.check(L.opure_event_record(ctx, ev0), "event")
     run(steps)
     cu.check(L.opure_event_record(ctx, ev1), "event")
+    if sampler:
+        # Keep the GPU on the same work, untimed, until the sampler has seen it.
+        t_soak = time.monotonic()
+        while time.monotonic() - t_soak < 0.5:
+            run(64)
+            cu.check(L.opure_sync(ctx, 600000), "sync")
+        sampler.mark_end()
     cu.check(L.opure_sync(ctx, 600000), "sync")
     ms = C.c_float()
     cu.check(L.opure_event_elapsed_ms(ev0, ev1, C.byref(ms)), "elapsed")
-    clocks = sampler.stop() if sampler else None
+    clocks = sampler.stop("timed steps + >= 0.5 s of the same steps right after") if sampler else None
     barrier(world)
     L.opure_event_free(ev0)
     L.opure_event_free(ev1)
@@ -338,7 +442,8 @@ def run_ours(args, world, rank, local):
     gen, _ = eng.generate(prompts, 1 if args.quick else DECODE_STEPS)
     parity = {"tokens_checked": 0}
 
-    dev_ms, clocks = device_steps(eng, B, args.steps, args.warmup, world, rank == 0)
+    dev_ms, clocks = device_steps(eng, B, args.steps, args.warmup, world, True, local)
+    clocks_per_rank = gather_objects(world, clocks)
     cu.check(L.opure_last_error(ctx), "device status")
     phases = None
     if args.phase_trace:
@@ -373,15 +478,12 @@ def run_ours(args, world, rank, local):
     cpu = None
     if rank == 0 and not args.no_cpu and not args.quick:
         import oracle
-        threads = os.cpu_count() or 1
-        oracle.set_threads(threads)
-        want, margins = oracle.Model(mp).generate(prompts[0], DECODE_STEPS)
+        oracle.set_threads(os.cpu_count() or 1)
+        m = oracle.Model(mp)
+        want, margins = m.generate(prompts[0], DECODE_STEPS)
         parity = {"tokens_checked": int(want.size), "tokens_equal": bool(np.array_equal(want, gen[0])),
                   "min_top2_margin": float(margins.min())}
-        tps, done, dt = cpu_decode(mp, args.cpu_steps, 4, 1, threads)
-        cpu = {"value": tps, "unit": "tok/s", "cores": threads, "kind": "port",
-               "sample": f"{done} config-0 decode tokens of one sequence (positions 32..159 cyclic) "
-                         f"on the CPU oracle after a {PROMPT_LEN}-token prefill"}
+        cpu = cpu_baseline_record(m, args.cpu_steps, 4)
 
     line_launches = launches_per_step(info, B, args.path)
     line = {
@@ -402,6 +504,7 @@ def run_ours(args, world, rank, local):
         "e2e": e2e,
         "gpu_launches": line_launches * args.steps,
         "clocks": clocks,
+        **({"clocks_per_rank": clocks_per_rank} if world > 1 else {}),
         "parity": parity,
         "launches_before_timed": (PROMPT_LEN + (1 if args.quick else DECODE_STEPS) + args.warmup)
         * line_launches,
@@ -480,14 +583,14 @@ def _time_events(ctx, fn, iters, warm=3):
 
 
 def run_attention_sweep(args):
-    """Config 1: paged flash-decode, 9 q heads / 3 kv heads, hd 64, fp16 K/V, page table a
-    seeded permutation (seed 3). K/V values: fp16 N(0,1) from seed 2 (the first 16M draws,
-    tiled across larger pools; the data does not change the kernel's work)."""
+    """Config 1: paged flash-decode, 9 q heads / 3 kv heads, hd 64, fp16 Q/K/V N(0, 1) from
+    seed 2 (stream order: the queries [B][9][64], then the page pool in memory order
+    [page][K|V][kv head][slot][dim]), page size 64, page table a seeded permutation (seed 3)
+    of the physical pages: the inputs the config-1 parity tests check."""
     from voxelengine import cuda as cu
     from voxelengine import engine as ve
     peak, kind = peaks()
     nh, nkv, hd, P = 9, 3, 64, 64
-    base = ve.normal_f16(2, 1.0, 1 << 24)
     out = []
     with cu.Ctx(0) as ctx:
         for B in (1, 8, 64):
@@ -496,13 +599,11 @@ def run_attention_sweep(args):
                     continue
                 pages = B * (ctxlen // P)
                 pool_elems = pages * 2 * nkv * P * hd
-                pool = ctx.buffer(pool_elems * 2)
-                reps = -(-pool_elems // base.size)
-                for r in range(reps):
-                    n = min(base.size, pool_elems - r * base.size)
-                    pool.upload(base[:n], offset=r * base.size * 2)
+                draws = ve.normal_f16(2, 1.0, B * nh * hd + pool_elems)
+                pool = ctx.to_device(draws[B * nh * hd:])
                 perm = ve.permutation(3, pages).reshape(B, ctxlen // P)
-                q = oracle_free_f16_to_f32(ve.normal_f16(2, 1.0, B * nh * hd))
+                q = oracle_free_f16_to_f32(draws[: B * nh * hd])
+                del draws
                 dq, dpt = ctx.to_device(q), ctx.to_device(perm.astype(np.int32))
                 dseq = ctx.to_device(np.arange(B, dtype=np.int32))
                 dlen = ctx.to_device(np.full(B, ctxlen, np.int32))
@@ -839,7 +940,7 @@ def run_spec(args):
 
 
 def run_window(args):
-    """Sliding-window KV cache (SURVEY next-row 4): config-0 model, bs1, 1024 greedy tokens
+    """Sliding-window KV cache (ring of pages): config-0 model, bs1, 1024 greedy tokens
     after the 32-token prompt, with a 256-token window (4 pages of 64 as a ring) and without
     one. Device time of the decode steps (the engine's Timing); with the window the KV held per
     sequence stays at 4 pages and each step attends to at most 256 positions."""
@@ -861,7 +962,7 @@ def run_window(args):
 
 
 def run_sample(args):
-    """Sampling (SURVEY next-row 2): the opure_sample_filtered and opure_logit_stats kernels
+    """Sampling: the opure_sample_filtered and opure_logit_stats kernels
     on seeded N(0, 3) logits of the config-0 vocabulary (device time per call, CUDA events
     over 50 calls after 5 warm-up ones), and sampled generation through the engine at the
     reference chat defaults (temperature 0.8, top-k 50, top-p 0.95, Opure_Chat.cpp:69;

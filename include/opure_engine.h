@@ -88,12 +88,22 @@ opure_status opure_engine_get_info(opure_engine *e, opure_engine_info *info);
 opure_ctx *opure_engine_ctx(opure_engine *e);
 
 /* Generate (Opure_VoxelEngine.cpp:894-958) for n_seq independent prompts: prompts are
- * concatenated in `prompts`, prompt_lens[n_seq] gives each length; each sequence gets
- * `budget` greedy tokens in out_tokens[n_seq][budget]. Prefill and decode run on the
- * device with no per-token host round trip. timing may be NULL. */
+ * concatenated in `prompts`, prompt_lens[n_seq] gives each length; each sequence gets up
+ * to `budget` greedy tokens in out_tokens[n_seq][budget]. Prefill and decode run on the
+ * device with no per-token host round trip. The reference's stop rules hold per sequence:
+ * generation ends after the stop id (config.json's eos_token_id; the reference uses its
+ * tokenizer's <|endoftext|>, :904,925-930), which is kept as the last token, or once
+ * prompt + generated tokens reach max_position_embeddings (:932); entries after a
+ * sequence's last token are -1. timing may be NULL. */
 opure_status opure_engine_generate(opure_engine *e, const int32_t *prompts, const uint32_t *prompt_lens,
                                    uint32_t n_seq, uint32_t budget, int32_t *out_tokens,
                                    opure_generate_timing *timing);
+/* opure_engine_generate that also reports each sequence's token count (counts[n_seq]) and
+ * whether the stop id ended it (hit_stop[n_seq]: GenerateResult.hitStop, :103-104); either
+ * may be NULL. */
+opure_status opure_engine_generate_stop(opure_engine *e, const int32_t *prompts, const uint32_t *prompt_lens,
+                                        uint32_t n_seq, uint32_t budget, int32_t *out_tokens, uint32_t *counts,
+                                        uint32_t *hit_stop, opure_generate_timing *timing);
 
 /* Prefill of one sequence (slot 0) ahead of host-driven decode steps (:682-710); `next`
  * (may be NULL) receives the argmax of the last prompt position (ArgMaxFrom, :962-988). */
@@ -146,6 +156,17 @@ opure_status opure_engine_read_tokens(opure_engine *e, uint32_t slot, uint32_t p
  * stream_bytes and kv_bytes_per_token of opure_engine_get_info are the shard's. */
 opure_status opure_engine_create_tp(const char *model_dir, opure_ctx *ctx, opure_comm *comm,
                                     const opure_engine_options *opts, opure_engine **out);
+
+/* VoxelEngine::SnapshotMetrics (Opure_VoxelEngine.h MetricsSnapshot, Opure_VoxelEngine.cpp:
+ * 640-670): KV page occupancy, tokens/s of the last generation's decode steps, memory
+ * pressure (0: the KV pool is fixed at creation), and the speculative acceptance rate of the
+ * last opure_engine_spec_generate this engine was the target of (-1 before any; the
+ * reference fixes it at -1, :666); `position` is CurrentPosition(). */
+typedef struct opure_engine_metrics {
+    float kv_occupancy, tokens_per_sec, memory_pressure, speculative_acceptance;
+    uint32_t position;
+} opure_engine_metrics;
+opure_status opure_engine_snapshot_metrics(opure_engine *e, opure_engine_metrics *m);
 
 /* The last persistent decode step's per-CTA %globaltimer stamps (layout of
  * opure_fused_step.trace: [sm_count][3 layers + 2][2]); needs options.phase_trace = 1.

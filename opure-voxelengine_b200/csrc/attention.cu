@@ -56,6 +56,9 @@ __global__ void __launch_bounds__(kWarps * 32) attn_kernel(AttnParams p) {
     const uint32_t t_split = split * p.split_tokens;
     const uint32_t t_end = min(uint32_t(max(len, 0)), t_split + p.split_tokens);
     const uint32_t t_begin = max(t_split, window_begin(len - 1, p.kv.page_size, p.kv.ring));
+    // Keys past the last split (a caller that understated max_ctx) would be dropped: refuse.
+    if (threadIdx.x == 0 && split + 1 == p.n_splits && len > 0 && uint32_t(len) > t_split + p.split_tokens)
+        report(p.st, OPURE_ERR_DEVICE_BOUNDS, 14, uint32_t(len));
 
     float qv[G][AttnShape<HD>::E];
     load_q_slice<HD, G>(p.q + size_t(entry) * p.n_heads * HD, g, p.scale_log2, qv);
@@ -259,6 +262,9 @@ __global__ void __launch_bounds__((kWarps + 1) * 32) attn_tma_kernel(AttnParams 
     const uint32_t t_split = split * p.split_tokens;
     const uint32_t t_end = min(uint32_t(max(len, 0)), t_split + p.split_tokens);
     const uint32_t t_begin = max(t_split, window_begin(len - 1, P, p.kv.ring));
+    // Keys past the last split (a caller that understated max_ctx) would be dropped: refuse.
+    if (threadIdx.x == 0 && split + 1 == p.n_splits && len > 0 && uint32_t(len) > t_split + p.split_tokens)
+        report(p.st, OPURE_ERR_DEVICE_BOUNDS, 14, uint32_t(len));
     const bool any = sidx >= 0 && t_end > t_begin;
     const uint32_t pg_begin = t_begin / P;
     const uint32_t n_pg = any ? (t_end + P - 1) / P - pg_begin : 0u;

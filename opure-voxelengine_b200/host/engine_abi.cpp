@@ -244,6 +244,18 @@ opure_status opure_engine_get_info(opure_engine *e, opure_engine_info *info) {
     });
 }
 
+opure_status opure_engine_snapshot_metrics(opure_engine *e, opure_engine_metrics *m) {
+    if (!e || !m) return OPURE_ERR_INVALID_ARG;
+    return Guard(e, [&] {
+        const auto s = e->eng.SnapshotMetrics();
+        m->kv_occupancy = s.kvOccupancy;
+        m->tokens_per_sec = s.tokensPerSec;
+        m->memory_pressure = s.memoryPressure;
+        m->speculative_acceptance = s.speculativeAcceptance;
+        m->position = e->eng.CurrentPosition();
+    });
+}
+
 opure_status opure_model_inspect(const char *model_dir, opure_engine_info *info, char *err, size_t err_len) {
     if (!model_dir || !info) return OPURE_ERR_INVALID_ARG;
     opure_engine scratch;
@@ -261,6 +273,12 @@ opure_status opure_model_inspect(const char *model_dir, opure_engine_info *info,
 
 opure_status opure_engine_generate(opure_engine *e, const int32_t *prompts, const uint32_t *lens,
                                    uint32_t n_seq, uint32_t budget, int32_t *out, opure_generate_timing *t) {
+    return opure_engine_generate_stop(e, prompts, lens, n_seq, budget, out, nullptr, nullptr, t);
+}
+
+opure_status opure_engine_generate_stop(opure_engine *e, const int32_t *prompts, const uint32_t *lens,
+                                        uint32_t n_seq, uint32_t budget, int32_t *out, uint32_t *counts,
+                                        uint32_t *hit_stop, opure_generate_timing *t) {
     if (!e || !prompts || !lens || !out || n_seq == 0) return OPURE_ERR_INVALID_ARG;
     return Guard(e, [&] {
         std::vector<std::vector<uint32_t>> ps(n_seq);
@@ -271,8 +289,12 @@ opure_status opure_engine_generate(opure_engine *e, const int32_t *prompts, cons
         }
         opure::engine::StepTiming st;
         const auto res = e->eng.GenerateBatch(ps, budget, &st);
-        for (uint32_t i = 0; i < n_seq; ++i)
-            for (uint32_t k = 0; k < budget; ++k) out[size_t(i) * budget + k] = int32_t(res[i].generated[k]);
+        for (uint32_t i = 0; i < n_seq; ++i) {
+            const size_t m = res[i].generated.size();
+            for (uint32_t k = 0; k < budget; ++k) out[size_t(i) * budget + k] = k < m ? int32_t(res[i].generated[k]) : -1;
+            if (counts) counts[i] = uint32_t(m);
+            if (hit_stop) hit_stop[i] = res[i].hitStop ? 1u : 0u;
+        }
         if (t) {
             t->prefill_ms = st.prefillMs;
             t->decode_ms = st.decodeMs;

@@ -63,6 +63,11 @@ ModelConfig ModelConfig::Parse(std::string_view text) {
     c.attentionBias = root.GetBool("attention_bias", false, ctx);
     c.mlpBias = root.GetBool("mlp_bias", false, ctx);
     if (const json::Value *t = root.Find("torch_dtype"); t && t->IsString()) c.torchDtype = t->str;
+    if (const json::Value *e = root.Find("eos_token_id")) {
+        const json::Value *id = e->IsArray() ? (e->arr.empty() ? nullptr : &e->arr[0]) : e;
+        if (id && id->IsNumber() && id->integral && id->inum >= 0 && id->inum < int64_t(c.vocabSize))
+            c.eosTokenId = id->inum;
+    }
     return c;
 }
 

@@ -29,6 +29,10 @@ struct ModelConfig {
     std::string torchDtype;
     std::string ropeScalingType = "none";
     double ropeScalingFactor = 1.0;
+    // Generation stop id: the reference takes the tokenizer's <|endoftext|> id
+    // (Opure_VoxelEngine.cpp:904); this engine loads no tokenizer and takes config.json's
+    // eos_token_id (the first entry when it is a list). -1: none.
+    int64_t eosTokenId = -1;
 
     uint32_t HeadDim() const { return numHeads ? hiddenSize / numHeads : 0; }
     uint32_t KvGroupSize() const { return numKvHeads ? numHeads / numKvHeads : 0; }

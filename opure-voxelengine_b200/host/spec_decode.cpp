@@ -204,6 +204,9 @@ std::vector<std::vector<uint32_t>> SpecGenerate(VoxelEngine &target, VoxelEngine
         }
     }
     st.totalMs = st.draftMs + st.verifyMs;
+    // MetricsSnapshot.speculativeAcceptance, which the reference fixes at -1
+    // (Opure_VoxelEngine.cpp:666): accepted / drafted over this call.
+    if (st.drafted) target.SetSpeculativeAcceptance(float(double(st.accepted) / double(st.drafted)));
     if (stats) *stats = st;
     return out;
 }

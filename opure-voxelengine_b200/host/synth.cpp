@@ -8,6 +8,7 @@
 #include <cstring>
 #include <fstream>
 #include <sstream>
+#include <thread>
 
 #include "platform.h"
 #include "streamer.h"
@@ -28,9 +29,31 @@ double Normal::Next() {
 }
 
 std::vector<uint16_t> NormalF16(uint64_t seed, float stddev, uint64_t n) {
-    Normal g(seed);
+    // Normals come in pairs from pairs of draws, so the stream splits into blocks of whole
+    // pairs: each block's generator state is found by stepping the xorshift alone, and the
+    // blocks (sqrt/log/sin/cos) run on host threads. The values equal the serial stream's.
+    constexpr uint64_t kBlock = uint64_t(1) << 17;  // normals per block (even)
     std::vector<uint16_t> out(n);
-    for (uint64_t i = 0; i < n; ++i) out[i] = safetensors::F32ToF16(float(g.Next() * stddev));
+    const uint64_t blocks = (n + kBlock - 1) / kBlock;
+    std::vector<uint64_t> starts(blocks);
+    Rng r(seed);
+    for (uint64_t b = 0; b < blocks; ++b) {
+        starts[b] = r.s;
+        for (uint64_t i = 0; i < kBlock; ++i) r.NextU32();
+    }
+    auto run = [&](uint64_t b0, uint64_t step) {
+        for (uint64_t b = b0; b < blocks; b += step) {
+            Normal g(1);
+            g.SetState(starts[b]);
+            const uint64_t i1 = std::min(n, (b + 1) * kBlock);
+            for (uint64_t i = b * kBlock; i < i1; ++i) out[i] = safetensors::F32ToF16(float(g.Next() * stddev));
+        }
+    };
+    const uint64_t nt = std::min<uint64_t>(blocks, std::max(1u, std::thread::hardware_concurrency()));
+    std::vector<std::thread> ts;
+    for (uint64_t t = 1; t < nt; ++t) ts.emplace_back(run, t, nt);
+    run(0, nt ? nt : 1);
+    for (auto &t : ts) t.join();
     return out;
 }
 

@@ -31,6 +31,11 @@ class Normal {
 public:
     explicit Normal(uint64_t seed) : rng_(seed) {}
     double Next();
+    // Continue from a raw xorshift state (at a pair boundary of the stream).
+    void SetState(uint64_t s) {
+        rng_.s = s;
+        has_ = false;
+    }
 
 private:
     Rng rng_;

@@ -534,12 +534,29 @@ std::vector<GenerateResult> VoxelEngine::GenerateBatch(const std::vector<std::ve
                                                        uint32_t budget, StepTiming *timing) {
     OPURE_CHECK(ready_, "engine used before Initialize");
     const uint32_t n = uint32_t(prompts.size());
+    const uint32_t maxPos = graph_.Config().maxPositions;
+    const int64_t eos = graph_.Config().eosTokenId;
     uint32_t maxP = 0;
     for (const auto &p : prompts) maxP = std::max<uint32_t>(maxP, uint32_t(p.size()));
-    // The reference stops when seqLen + 1 >= maxPos (Opure_VoxelEngine.cpp:932).
-    OPURE_CHECK(maxP + budget < maxLen_, "prompt + budget exceeds the engine's maxLen");
+    // The reference's stop rules (Opure_VoxelEngine.cpp:918-933): after pushing a token the
+    // loop ends when seqLen + 1 >= maxPos, so a prompt of length len gets at most
+    // maxPos - len tokens; and it ends on the stop id, kept as the last token.
+    // A step at position p writes the token of position p into the history (the previous
+    // step's argmax). After the prefill, vector v stands at start[v]: its prompt length
+    // (chunked prefill) or the longest prompt's (one token per step: shorter prompts
+    // generate meanwhile); after k decode steps its history holds positions < start + k.
     const bool chunked = opts_.prefillChunk > 0;
-    ResetSequences(prompts, maxP + budget, !chunked);
+    std::vector<uint32_t> limit(n), start(n);
+    uint32_t steps = 0;
+    for (uint32_t v = 0; v < n; ++v) {
+        const uint32_t len = uint32_t(prompts[v].size());
+        OPURE_CHECK(len < maxPos, "prompt reaches max_position_embeddings");
+        limit[v] = std::min(budget, maxPos - len);
+        start[v] = chunked ? len : maxP;
+        if (len + limit[v] > start[v]) steps = std::max(steps, len + limit[v] - start[v]);
+    }
+    OPURE_CHECK(maxP + steps <= maxLen_ && maxP + steps > 0, "prompt + budget exceeds the engine's maxLen");
+    ResetSequences(prompts, maxP + steps, !chunked);
 
     opure_event *e0 = nullptr, *e1 = nullptr, *e2 = nullptr;
     OPURE_CUDA_CHECK(opure_event_create(ctx_, &e0));
@@ -552,7 +569,42 @@ std::vector<GenerateResult> VoxelEngine::GenerateBatch(const std::vector<std::ve
     else
         RunSteps(n, maxP, false);
     OPURE_CUDA_CHECK(opure_event_record(ctx_, e1));
-    RunSteps(n, budget, false);
+    std::vector<int32_t> rows(size_t(n) * maxLen_);
+    // Index of each sequence's last token: limit - 1, or its first stop id.
+    std::vector<uint32_t> end(n);
+    auto scan = [&](uint32_t upto) {  // after `upto` decode steps
+        bool all = true;
+        for (uint32_t v = 0; v < n; ++v) {
+            const uint32_t len = uint32_t(prompts[v].size());
+            end[v] = limit[v] ? limit[v] - 1 : 0;
+            bool found = false;
+            for (uint32_t k = 0; eos >= 0 && k < limit[v] && len + k < start[v] + upto; ++k)
+                if (rows[size_t(v) * maxLen_ + len + k] == int32_t(eos)) {
+                    end[v] = k;
+                    found = true;
+                    break;
+                }
+            all = all && (found || len + limit[v] <= start[v] + upto);
+        }
+        return all;
+    };
+    uint32_t done = 0;
+    if (eos < 0) {
+        RunSteps(n, steps, false);
+        done = steps;
+    } else {
+        // With a stop id the steps run in chunks, and the loop ends early once every
+        // sequence has produced it (one token-row readback per chunk).
+        constexpr uint32_t kChunk = 16;
+        for (;;) {
+            OPURE_CUDA_CHECK(opure_d2h(ctx_, rows.data(), buf_.tokens, rows.size() * 4));
+            OPURE_CUDA_CHECK(opure_sync(ctx_, 600000));
+            if (scan(done) || done == steps) break;
+            const uint32_t c = std::min(kChunk, steps - done);
+            RunSteps(n, c, false);
+            done += c;
+        }
+    }
     OPURE_CUDA_CHECK(opure_event_record(ctx_, e2));
     Sync();
     float pre = 0.f, dec = 0.f;
@@ -562,26 +614,31 @@ std::vector<GenerateResult> VoxelEngine::GenerateBatch(const std::vector<std::ve
     opure_event_free(e1);
     opure_event_free(e2);
 
-    std::vector<int32_t> rows(size_t(n) * maxLen_);
     OPURE_CUDA_CHECK(opure_d2h(ctx_, rows.data(), buf_.tokens, rows.size() * 4));
     OPURE_CUDA_CHECK(opure_sync(ctx_, 60000));
+    scan(done);
     std::vector<GenerateResult> out(n);
     for (uint32_t v = 0; v < n; ++v) {
         GenerateResult &r = out[v];
         r.promptTokens = prompts[v];
+        const uint32_t count = limit[v] ? end[v] + 1 : 0;
         const size_t b = size_t(v) * maxLen_ + prompts[v].size();
-        r.generated.assign(rows.begin() + b, rows.begin() + b + budget);
-        r.msPerToken = budget ? double(dec) / budget : 0.0;
-        r.lastMs = r.msPerToken;
+        r.generated.assign(rows.begin() + b, rows.begin() + b + count);
+        if (count && eos >= 0 && r.generated.back() == uint32_t(eos)) {
+            r.hitStop = true;
+            r.stopToken = uint32_t(eos);
+        }
+        r.msPerToken = count ? double(dec) / count : 0.0;
+        r.lastMs = done ? double(dec) / done : 0.0;
     }
     if (timing) {
         timing->prefillMs = pre;
         timing->decodeMs = dec;
         timing->prefillSteps = prefillSteps;
-        timing->decodeSteps = budget;
+        timing->decodeSteps = done;
     }
-    seqLen_ = maxP + budget;
-    lastTokenMs_ = budget ? double(dec) / budget : 0.0;
+    seqLen_ = maxP + done;
+    lastTokenMs_ = done ? double(dec) / done : 0.0;
     return out;
 }
 
@@ -655,7 +712,7 @@ GenerateResult VoxelEngine::Generate(const std::vector<uint32_t> &tokens, const 
     GenerateResult r;
     r.promptTokens = tokens;
     if (tokens.empty()) return r;
-    // No tokenizer is loaded (token-id workloads), so there is no <|endoftext|> id to stop on.
+    // Stops on config.json's eos_token_id (no tokenizer is loaded) and at max_position_embeddings.
     const uint32_t budget = std::min(opts.maxNewTokens, opts_.maxNewTokens);
     return GenerateBatch({tokens}, budget).front();
 }
@@ -850,6 +907,7 @@ VoxelEngine::MetricsSnapshot VoxelEngine::SnapshotMetrics() const {
     if (kv_.NumPages()) m.kvOccupancy = 1.0f - float(kv_.FreePages()) / float(kv_.NumPages());
     m.tokensPerSec = lastTokenMs_ > 0 ? float(1000.0 / lastTokenMs_) : 0.0f;
     m.memoryPressure = 0.0f;
+    m.speculativeAcceptance = specAcceptance_;
     return m;
 }
 

@@ -144,6 +144,8 @@ public:
         float speculativeAcceptance = -1.0f;
     };
     MetricsSnapshot SnapshotMetrics() const;
+    // Acceptance rate of the last speculative generation this engine was the target of.
+    void SetSpeculativeAcceptance(float a) { specAcceptance_ = a; }
     uint32_t CurrentPosition() const { return seqLen_; }
 
     // Enqueues `steps` decode steps for the first n vectors (graph replays when enabled).
@@ -218,6 +220,7 @@ private:
     bool ready_ = false;
     uint32_t seqLen_ = 0;
     double lastTokenMs_ = 0.0;
+    float specAcceptance_ = -1.0f;
     std::map<std::pair<uint32_t, bool>, opure_graph *> graphs_;
     std::map<uint32_t, std::pair<void *, size_t>> attnScratch_;
     void *hostIo_ = nullptr;  // pinned staging of the host-driven step

@@ -37,6 +37,11 @@ class Timing(C.Structure):
                 ("decode_steps", u32)]
 
 
+class Metrics(C.Structure):
+    _fields_ = [("kv_occupancy", f32), ("tokens_per_sec", f32), ("memory_pressure", f32),
+                ("speculative_acceptance", f32), ("position", u32)]
+
+
 class SpecOptions(C.Structure):
     _fields_ = [("k", u32), ("mode", u32), ("seed", u64)]
 
@@ -86,6 +91,8 @@ def lib() -> C.CDLL:
             "opure_engine_destroy": [P],
             "opure_engine_get_info": [P, P],
             "opure_engine_generate": [P, P, P, u32, u32, P, P],
+            "opure_engine_generate_stop": [P, P, P, u32, u32, P, P, P, P],
+            "opure_engine_snapshot_metrics": [P, P],
             "opure_engine_prefill": [P, P, u32, P],
             "opure_engine_decode_step": [P, P, P, u32, P],
             "opure_engine_forward_logits": [P, P, u32, P],
@@ -254,6 +261,26 @@ class Engine:
         _check(lib().opure_engine_generate(self.h, _p(flat), _p(lens), len(ps), budget, _p(out),
                                            C.byref(t)), "generate", self.h)
         return out, t
+
+    def generate_stop(self, prompts, budget: int):
+        """generate with the per-sequence results of the reference's stop rules: returns
+        (tokens [n][budget] with -1 after each sequence's last token, counts [n],
+        hit_stop [n] bool, Timing)."""
+        ps = [np.asarray(p, np.int32) for p in prompts]
+        flat = np.ascontiguousarray(np.concatenate(ps), np.int32)
+        lens = np.array([p.size for p in ps], np.uint32)
+        out = np.zeros((len(ps), budget), np.int32)
+        counts = np.zeros(len(ps), np.uint32)
+        hit = np.zeros(len(ps), np.uint32)
+        t = Timing()
+        _check(lib().opure_engine_generate_stop(self.h, _p(flat), _p(lens), len(ps), budget, _p(out), _p(counts),
+                                                _p(hit), C.byref(t)), "generate_stop", self.h)
+        return out, counts, hit.astype(bool), t
+
+    def metrics(self) -> Metrics:
+        m = Metrics()
+        _check(lib().opure_engine_snapshot_metrics(self.h, C.byref(m)), "metrics", self.h)
+        return m
 
     def spec_generate(self, draft: "Engine", prompts, budget: int, k: int = 4, mode: int = SPEC_GREEDY,
                       seed: int = 0, log_rounds: int = 0):

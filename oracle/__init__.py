@@ -22,6 +22,16 @@ EMBED, FINAL_NORM, LM_HEAD, IN_NORM, POST_NORM = 0, 1, 2, 3, 4
 WQ, WK, WV, WO, GATE, UP, DOWN = 5, 6, 7, 8, 9, 10, 11
 
 
+class OrcSynth(C.Structure):
+    _fields_ = [("seed", C.c_uint64), ("std", C.c_float), ("tied", C.c_uint32), ("int8", C.c_uint32),
+                ("noise_seed", C.c_uint64), ("noise_std", C.c_float)]
+
+
+# SmolLM-135M shape (BASELINE configs 0/2/3).
+SMOLLM_135M = dict(vocab=49152, hidden=576, inter=1536, layers=30, heads=9, kv_heads=3,
+                   max_pos=2048, eps=1e-5, theta=10000.0)
+
+
 class OrcConfig(C.Structure):
     _fields_ = [
         ("vocab", C.c_uint32), ("hidden", C.c_uint32), ("inter", C.c_uint32),
@@ -77,6 +87,14 @@ def lib() -> C.CDLL:
             "orc_generate": (i32, [P, P, u32, u32, u32, P, P]),
             "orc_set_threads": (None, [i32]),
             "orc_get_threads": (i32, []),
+            "orc_thread_serial": (None, [i32]),
+            "orc_generate_stop": (i32, [P, P, u32, u32, u32, C.c_int64, P, P, P]),
+            "orc_generate_batch": (i32, [P, P, P, u32, u32, u32, C.c_int64, i32, P, P, P]),
+            "orc_synth_normal_f16": (None, [u64, f32, u64, P]),
+            "orc_synth_prompt": (None, [u64, u32, u32, P]),
+            "orc_synth_permutation": (None, [u64, u32, P]),
+            "orc_synth_uniforms": (None, [u64, u64, P]),
+            "orc_model_create_synth": (P, [P, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -112,6 +130,38 @@ def f16_to_f32(h: np.ndarray) -> np.ndarray:
     h = np.ascontiguousarray(h, np.uint16)
     out = np.empty(h.shape, np.float32)
     lib().orc_f16_to_f32_n(_p(h), _p(out), h.size)
+    return out
+
+
+def thread_serial(on: bool = True) -> None:
+    """The calling thread computes serially (never the shared worker pool): for callers
+    that run independent sequences on Python threads of their own (ctypes releases the
+    GIL during each call)."""
+    lib().orc_thread_serial(int(on))
+
+
+# ---- seeded synthetic inputs (the same bytes as the engine's generators) ----
+def normal_f16(seed: int, std: float, n: int) -> np.ndarray:
+    out = np.empty(n, np.uint16)
+    lib().orc_synth_normal_f16(seed, std, n, _p(out))
+    return out
+
+
+def prompt(seed: int, vocab: int, n: int) -> np.ndarray:
+    out = np.empty(n, np.int32)
+    lib().orc_synth_prompt(seed, vocab, n, _p(out))
+    return out
+
+
+def permutation(seed: int, n: int) -> np.ndarray:
+    out = np.empty(n, np.int32)
+    lib().orc_synth_permutation(seed, n, _p(out))
+    return out
+
+
+def uniforms(seed: int, n: int) -> np.ndarray:
+    out = np.empty(n, np.float32)
+    lib().orc_synth_uniforms(seed, n, _p(out))
     return out
 
 
@@ -269,25 +319,63 @@ def read_safetensors(path: str) -> dict:
     return out
 
 
+def _config_from(cfg: dict, attn_scale: float, rope_cpu_literal: bool) -> OrcConfig:
+    c = OrcConfig()
+    c.vocab = cfg["vocab_size"]
+    c.hidden = cfg["hidden_size"]
+    c.inter = cfg["intermediate_size"]
+    c.layers = cfg["num_hidden_layers"]
+    c.heads = cfg["num_attention_heads"]
+    c.kv_heads = cfg.get("num_key_value_heads", c.heads)
+    c.max_pos = cfg["max_position_embeddings"]
+    c.eps = cfg["rms_norm_eps"]
+    c.theta = cfg.get("rope_theta", 10000.0)
+    c.attn_scale = attn_scale
+    c.rope_cpu_literal = int(rope_cpu_literal)
+    return c
+
+
+def _eos_of(cfg: dict) -> int:
+    """The stop id: config.json's eos_token_id (the first when it is a list), -1 when absent."""
+    e = cfg.get("eos_token_id")
+    if isinstance(e, list):
+        e = e[0] if e else None
+    return int(e) if isinstance(e, int) and e >= 0 else -1
+
+
 class Model:
-    """A model directory (config.json + model.safetensors) loaded into the oracle."""
+    """A model directory (config.json + model.safetensors) loaded into the oracle, or
+    (Model.synth) a seeded random-init model built in memory."""
+
+    @classmethod
+    def synth(cls, seed: int = 0, std: float = 0.02, int8: bool = False, tied: bool = True,
+              noise_seed: int = 0, noise_std: float = 0.0, eos: int = -1, **shape) -> "Model":
+        """The model the engine's synth_model writes for the same arguments (same draw order,
+        same bytes), without touching the product's libraries or the file system."""
+        dims = dict(SMOLLM_135M)
+        dims.update(shape)
+        cfg = {"vocab_size": dims["vocab"], "hidden_size": dims["hidden"], "intermediate_size": dims["inter"],
+               "num_hidden_layers": dims["layers"], "num_attention_heads": dims["heads"],
+               "num_key_value_heads": dims["kv_heads"], "max_position_embeddings": dims["max_pos"],
+               "rms_norm_eps": dims["eps"], "rope_theta": dims["theta"], "tie_word_embeddings": bool(tied)}
+        if eos >= 0:
+            cfg["eos_token_id"] = int(eos)
+        self = cls.__new__(cls)
+        self.cfg = cfg
+        self.c = _config_from(cfg, 1.0, False)
+        self.eos = _eos_of(cfg)
+        sp = OrcSynth(seed, std, int(tied), int(int8), noise_seed, noise_std)
+        self.h = lib().orc_model_create_synth(C.byref(self.c), C.byref(sp))
+        if not self.h:
+            raise ValueError("oracle rejected the synthetic model")
+        return self
 
     def __init__(self, model_dir: str, attn_scale: float = 1.0, rope_cpu_literal: bool = False):
         cfg = json.load(open(os.path.join(model_dir, "config.json")))
         self.cfg = cfg
-        c = OrcConfig()
-        c.vocab = cfg["vocab_size"]
-        c.hidden = cfg["hidden_size"]
-        c.inter = cfg["intermediate_size"]
-        c.layers = cfg["num_hidden_layers"]
-        c.heads = cfg["num_attention_heads"]
-        c.kv_heads = cfg.get("num_key_value_heads", c.heads)
-        c.max_pos = cfg["max_position_embeddings"]
-        c.eps = cfg["rms_norm_eps"]
-        c.theta = cfg.get("rope_theta", 10000.0)
-        c.attn_scale = attn_scale
-        c.rope_cpu_literal = int(rope_cpu_literal)
+        c = _config_from(cfg, attn_scale, rope_cpu_literal)
         self.c = c
+        self.eos = _eos_of(cfg)
         self.h = lib().orc_model_create(C.byref(c))
         if not self.h:
             raise ValueError("oracle rejected the model configuration")
@@ -328,6 +416,39 @@ class Model:
         if n < 0:
             raise ValueError("oracle generate failed")
         return out[:n], margins[:n]
+
+    def generate_stop(self, prompt, budget: int, max_pos: int | None = None, eos: int | None = None):
+        """Generate with the reference's stop rules (stop id = config.json's eos_token_id
+        unless `eos` is given; -1: none). Returns (tokens, margins, hit_stop)."""
+        p = np.ascontiguousarray(prompt, np.uint32)
+        mp = max_pos or self.c.max_pos
+        out = np.zeros(budget, np.uint32)
+        margins = np.zeros(budget, np.float32)
+        hit = C.c_int(0)
+        n = lib().orc_generate_stop(self.h, _p(p), p.size, budget, mp, self.eos if eos is None else eos,
+                                    _p(out), _p(margins), C.byref(hit))
+        if n < 0:
+            raise ValueError("oracle generate failed")
+        return out[:n], margins[:n], bool(hit.value)
+
+    def generate_batch(self, prompts, budget: int, threads: int, max_pos: int | None = None,
+                       eos: int | None = None):
+        """Independent sequences on `threads` host threads (one sequence per thread at a
+        time, serial arithmetic inside). Returns (tokens [n][budget] (unused entries 0),
+        counts [n], margins [n][budget])."""
+        ps = [np.asarray(p, np.uint32) for p in prompts]
+        flat = np.ascontiguousarray(np.concatenate(ps), np.uint32)
+        lens = np.array([p.size for p in ps], np.uint32)
+        n = len(ps)
+        out = np.zeros((n, budget), np.uint32)
+        counts = np.zeros(n, np.uint32)
+        margins = np.zeros((n, budget), np.float32)
+        rc = lib().orc_generate_batch(self.h, _p(flat), _p(lens), n, budget, max_pos or self.c.max_pos,
+                                      self.eos if eos is None else eos, int(threads), _p(out), _p(counts),
+                                      _p(margins))
+        if rc != 0:
+            raise ValueError("oracle generate_batch failed")
+        return out, counts, margins
 
     def state(self, max_pos: int | None = None) -> "State":
         return State(self, max_pos or self.c.max_pos)

@@ -170,9 +170,13 @@ Pool &pool() {
     return p;
 }
 
+// Threads that run whole sequences of their own (orc_generate_batch workers, or callers
+// that asked with orc_thread_serial) compute serially and never touch the shared pool.
+thread_local bool t_serial = false;
+
 // Runs fn over [0, n), in parallel when the work (n * cost) is large enough.
 void parallel_for(int64_t n, uint64_t cost, const std::function<void(int64_t)> &fn) {
-    if (g_threads > 1 && uint64_t(n) * cost > (1u << 16)) {
+    if (!t_serial && g_threads > 1 && uint64_t(n) * cost > (1u << 16)) {
         pool().run(n, fn);
     } else {
         for (int64_t i = 0; i < n; ++i) fn(i);
@@ -856,6 +860,217 @@ int orc_generate(const orc_model *m, const uint32_t *prompt, uint32_t n_prompt,
     }
     orc_state_free(s);
     return n;
+}
+
+}  // extern "C"
+
+// ===========================================================================
+// Stop rules, independent sequences, seeded synthetic inputs
+// ===========================================================================
+namespace {
+
+// xorshift64 of Opure_TestHarness.cpp:36-47 (seed 0 behaves as seed 1).
+struct Xorshift {
+    uint64_t s;
+    explicit Xorshift(uint64_t seed) : s(seed ? seed : 1) {}
+    uint32_t next() {
+        s ^= s << 13; s ^= s >> 7; s ^= s << 17;
+        return uint32_t(s >> 32);
+    }
+    double open01() { return (double(next()) + 0.5) / 4294967296.0; }
+};
+
+// Standard normals by Box-Muller (Box & Muller 1958) on pairs of open uniforms u1, u2:
+// r = sqrt(-2 ln u1), a = 2 pi u2; r cos(a) first, then r sin(a).
+struct BoxMuller {
+    Xorshift r;
+    double spare = 0.0;
+    bool has = false;
+    explicit BoxMuller(uint64_t seed) : r(seed) {}
+    double next() {
+        if (has) {
+            has = false;
+            return spare;
+        }
+        const double u1 = r.open01(), u2 = r.open01();
+        const double rad = std::sqrt(-2.0 * std::log(u1)), a = 2.0 * M_PI * u2;
+        spare = rad * std::sin(a);
+        has = true;
+        return rad * std::cos(a);
+    }
+};
+
+uint16_t q8_round_store(float w, float scale) {
+    float r = std::nearbyint(w / scale);
+    r = std::fmin(127.f, std::fmax(-127.f, r));
+    return uint16_t(uint8_t(int8_t(r)));
+}
+
+// Greedy generation of one sequence with the reference's stop rules
+// (VoxelEngine::Generate, Opure_VoxelEngine.cpp:894-958): the token predicted from the last
+// prompt position is pushed first; after each push the loop ends when it was the stop id
+// (:925-930) or when seqLen + 1 >= maxPos (:932); otherwise one decode step follows.
+int generate_one(const orc_model *m, const uint32_t *prompt, uint32_t n_prompt, uint32_t budget,
+                 uint32_t max_pos, int64_t eos, uint32_t *out, float *margins, int *hit_stop) {
+    if (!m || n_prompt == 0 || n_prompt > max_pos) return -1;
+    orc_state *s = orc_state_create(m, max_pos);
+    std::vector<float> logits(m->c.vocab);
+    auto top = [&](float *margin) {
+        float v1;
+        const uint32_t i1 = argmax1(logits.data(), m->c.vocab, &v1);
+        if (margin) {
+            float v2 = -std::numeric_limits<float>::infinity();
+            for (uint32_t i = 0; i < m->c.vocab; ++i)
+                if (i != i1 && logits[i] > v2) v2 = logits[i];
+            *margin = v1 - v2;
+        }
+        return i1;
+    };
+    for (uint32_t i = 0; i < n_prompt; ++i)
+        orc_forward(m, s, prompt[i], i + 1 == n_prompt ? logits.data() : nullptr, nullptr);
+    float mg = 0.0f;
+    uint32_t next = top(&mg);
+    int n = 0;
+    if (hit_stop) *hit_stop = 0;
+    for (uint32_t i = 0; i < budget; ++i) {
+        out[n] = next;
+        if (margins) margins[n] = mg;
+        ++n;
+        if (eos >= 0 && next == uint32_t(eos)) {
+            if (hit_stop) *hit_stop = 1;
+            break;
+        }
+        if (s->len + 1 >= max_pos) break;
+        orc_forward(m, s, next, logits.data(), nullptr);
+        next = top(&mg);
+    }
+    orc_state_free(s);
+    return n;
+}
+
+}  // namespace
+
+extern "C" {
+
+void orc_thread_serial(int on) { t_serial = on != 0; }
+
+int orc_generate_stop(const orc_model *m, const uint32_t *prompt, uint32_t n_prompt, uint32_t budget,
+                      uint32_t max_pos, int64_t eos, uint32_t *out, float *margins, int *hit_stop) {
+    return generate_one(m, prompt, n_prompt, budget, max_pos, eos, out, margins, hit_stop);
+}
+
+int orc_generate_batch(const orc_model *m, const uint32_t *prompts, const uint32_t *prompt_lens,
+                       uint32_t n_seq, uint32_t budget, uint32_t max_pos, int64_t eos, int threads,
+                       uint32_t *out, uint32_t *counts, float *margins) {
+    if (!m || n_seq == 0) return -1;
+    std::vector<size_t> off(n_seq + 1, 0);
+    for (uint32_t i = 0; i < n_seq; ++i) off[i + 1] = off[i] + prompt_lens[i];
+    const uint32_t nt = uint32_t(std::max(1, std::min<int>(threads, int(n_seq))));
+    std::vector<int> rc(n_seq, 0);
+    auto work = [&](uint32_t who) {
+        t_serial = true;
+        for (uint32_t i = who; i < n_seq; i += nt) {
+            const int n = generate_one(m, prompts + off[i], prompt_lens[i], budget, max_pos, eos,
+                                       out + size_t(i) * budget, margins ? margins + size_t(i) * budget : nullptr,
+                                       nullptr);
+            rc[i] = n;
+            if (counts) counts[i] = n < 0 ? 0u : uint32_t(n);
+        }
+    };
+    std::vector<std::thread> ts;
+    for (uint32_t t = 1; t < nt; ++t) ts.emplace_back(work, t);
+    work(0);
+    for (auto &t : ts) t.join();
+    for (int r : rc)
+        if (r < 0) return -1;
+    return 0;
+}
+
+void orc_synth_normal_f16(uint64_t seed, float stddev, uint64_t n, uint16_t *out) {
+    // Pairs of normals come from pairs of draws, so the stream splits into chunks of whole
+    // pairs: the generator state at each chunk start is found by stepping the (cheap)
+    // xorshift alone, then the chunks (the costly transcendentals) run on the worker pool.
+    constexpr uint64_t kPairs = 1 << 16;
+    const uint64_t pairs = (n + 1) / 2, chunks = (pairs + kPairs - 1) / kPairs;
+    std::vector<uint64_t> starts(chunks);
+    Xorshift r(seed);
+    for (uint64_t c = 0; c < chunks; ++c) {
+        starts[c] = r.s;
+        for (uint64_t i = 0; i < 2 * kPairs; ++i) r.next();
+    }
+    parallel_for(int64_t(chunks), 2 * kPairs * 64, [&](int64_t c) {
+        BoxMuller g(1);
+        g.r.s = starts[size_t(c)];
+        const uint64_t i0 = uint64_t(c) * 2 * kPairs, i1 = std::min(n, i0 + 2 * kPairs);
+        for (uint64_t i = i0; i < i1; ++i) out[i] = f32_to_f16(float(g.next() * stddev));
+    });
+}
+
+void orc_synth_prompt(uint64_t seed, uint32_t vocab, uint32_t n, int32_t *out) {
+    Xorshift r(seed);
+    for (uint32_t i = 0; i < n; ++i) out[i] = int32_t(r.next() % vocab);
+}
+
+void orc_synth_permutation(uint64_t seed, uint32_t n, int32_t *out) {
+    for (uint32_t i = 0; i < n; ++i) out[i] = int32_t(i);
+    Xorshift r(seed);
+    for (uint32_t i = n; i > 1; --i) std::swap(out[i - 1], out[r.next() % i]);
+}
+
+void orc_synth_uniforms(uint64_t seed, uint64_t n, float *out) {
+    Xorshift r(seed);
+    for (uint64_t i = 0; i < n; ++i) out[i] = float(double(r.next()) / 4294967296.0);
+}
+
+orc_model *orc_model_create_synth(const orc_config *cfg, const orc_synth *sp) {
+    if (!sp) return nullptr;
+    orc_model *m = orc_model_create(cfg);
+    if (!m) return nullptr;
+    const orc_config &c = m->c;
+    const uint32_t h = c.hidden, ff = c.inter, kvh = c.kv_heads * (c.hidden / c.heads);
+    BoxMuller g(sp->seed), noise(sp->noise_seed);
+    std::vector<uint16_t> w;
+    std::vector<int8_t> q;
+    // One matrix in file order: fp16(N(0, std)), plus fp16-rounded N(0, noise_std) noise for
+    // draft models; int8 (absmax / 127, round half to even, clamp +-127) when asked.
+    auto matrix = [&](int role, int layer, uint32_t rows, uint32_t cols, bool quantizable) {
+        w.resize(size_t(rows) * cols);
+        for (auto &x : w) {
+            float v = f16_to_f32(f32_to_f16(float(g.next() * sp->std)));
+            if (sp->noise_std > 0.f) v = v + float(noise.next() * sp->noise_std);
+            x = f32_to_f16(v);
+        }
+        if (sp->int8 && quantizable) {
+            float amax = 0.f;
+            for (uint16_t x : w) amax = std::fmax(amax, std::fabs(f16_to_f32(x)));
+            const float scale = amax > 0.f ? amax / 127.0f : 1.0f;
+            q.resize(w.size());
+            for (size_t i = 0; i < w.size(); ++i) q[i] = int8_t(uint8_t(q8_round_store(f16_to_f32(w[i]), scale)));
+            return orc_model_set_tensor(m, role, layer, ORC_I8, q.data(), q.size(), scale);
+        }
+        return orc_model_set_tensor(m, role, layer, ORC_F16, w.data(), w.size(), 1.0f);
+    };
+    const std::vector<uint16_t> ones(h, 0x3C00);
+    int rc = matrix(ORC_EMBED, 0, c.vocab, h, false);
+    for (uint32_t l = 0; l < c.layers && rc == 0; ++l) {
+        const int L = int(l);
+        rc |= orc_model_set_tensor(m, ORC_IN_NORM, L, ORC_F16, ones.data(), h, 1.f);
+        rc |= matrix(ORC_WQ, L, h, h, true);
+        rc |= matrix(ORC_WK, L, kvh, h, true);
+        rc |= matrix(ORC_WV, L, kvh, h, true);
+        rc |= matrix(ORC_WO, L, h, h, true);
+        rc |= orc_model_set_tensor(m, ORC_POST_NORM, L, ORC_F16, ones.data(), h, 1.f);
+        rc |= matrix(ORC_GATE, L, ff, h, true);
+        rc |= matrix(ORC_UP, L, ff, h, true);
+        rc |= matrix(ORC_DOWN, L, h, ff, true);
+    }
+    rc |= orc_model_set_tensor(m, ORC_FINAL_NORM, 0, ORC_F16, ones.data(), h, 1.f);
+    if (!sp->tied) rc |= matrix(ORC_LM_HEAD, 0, c.vocab, h, false);
+    if (rc != 0 || orc_model_ready(m) != 0) {
+        orc_model_free(m);
+        return nullptr;
+    }
+    return m;
 }
 
 }  // extern "C"

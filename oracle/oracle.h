@@ -193,10 +193,56 @@ int orc_forward(const orc_model *m, orc_state *s, uint32_t token, float *logits,
 int orc_generate(const orc_model *m, const uint32_t *prompt, uint32_t n_prompt,
                  uint32_t budget, uint32_t max_pos, uint32_t *out, float *margins);
 
+/* Generate with both of the reference's stop rules (Opure_VoxelEngine.cpp:894-958): the
+ * token predicted from the last prompt position is pushed first; after each push the loop
+ * ends when that token is `eos` (:925-930; eos < 0: no stop id) or when seqLen + 1 >=
+ * max_pos (:932), else one decode step follows. Returns the tokens written (<= budget);
+ * *hit_stop (may be NULL) is 1 when the stop id ended it. */
+int orc_generate_stop(const orc_model *m, const uint32_t *prompt, uint32_t n_prompt, uint32_t budget,
+                      uint32_t max_pos, int64_t eos, uint32_t *out, float *margins, int *hit_stop);
+
+/* orc_generate_stop for n_seq independent sequences (prompts concatenated, prompt_lens
+ * each), one sequence per host thread at a time on `threads` threads, each computing
+ * serially: out [n_seq][budget], counts [n_seq] tokens each, margins (may be NULL)
+ * [n_seq][budget]. Results equal the one-at-a-time ones. 0 on success. */
+int orc_generate_batch(const orc_model *m, const uint32_t *prompts, const uint32_t *prompt_lens,
+                       uint32_t n_seq, uint32_t budget, uint32_t max_pos, int64_t eos, int threads,
+                       uint32_t *out, uint32_t *counts, float *margins);
+
 /* Worker threads for the row loops of GEMV and the head loop of attention. Rows are
  * independent, so results are identical for any thread count. */
 void orc_set_threads(int n);
 int  orc_get_threads(void);
+/* on = 1: the calling thread computes serially and never uses the worker pool (for
+ * callers that run independent sequences on threads of their own). */
+void orc_thread_serial(int on);
+
+/* ---- seeded synthetic inputs ------------------------------------------------
+ * The benchmark configurations' random-init models and inputs, generated here so the
+ * CPU side (parity checks, the reference arm of the benchmark) needs nothing of the
+ * product: the harness's xorshift64 Rng (Opure_TestHarness.cpp:36-47, seed 0 -> 1);
+ * normals by Box-Muller on pairs of open uniforms (NextU32() + 0.5) / 2^32, r cos(a)
+ * then r sin(a); fp16 by round-to-nearest-even. tests/ check these bytes against the
+ * engine's own generators. */
+void orc_synth_normal_f16(uint64_t seed, float stddev, uint64_t n, uint16_t *out);
+void orc_synth_prompt(uint64_t seed, uint32_t vocab, uint32_t n, int32_t *out);   /* NextU32() % vocab */
+void orc_synth_permutation(uint64_t seed, uint32_t n, int32_t *out);              /* Fisher-Yates */
+void orc_synth_uniforms(uint64_t seed, uint64_t n, float *out);                   /* NextU32() / 2^32 */
+
+typedef struct {
+    uint64_t seed;        /* matrices N(0, std) in file order                             */
+    float    std;
+    uint32_t tied;        /* 1: lm_head is the embedding                                   */
+    uint32_t int8;        /* 1: matrices (not the embedding / untied head) per-tensor int8 */
+    uint64_t noise_seed;  /* draft models: each element + N(0, noise_std), noise_std > 0   */
+    float    noise_std;
+} orc_synth;
+
+/* A random-init model built in memory: the embedding, then per layer q, k, v, o, gate,
+ * up, down (then the untied lm_head) drawn in that order from one normal stream, each
+ * element fp16(N(0, std)) (+ the noise stream's N(0, noise_std), re-rounded to fp16);
+ * norm gains 1.0. NULL on a bad configuration. */
+orc_model *orc_model_create_synth(const orc_config *cfg, const orc_synth *spec);
 
 #ifdef __cplusplus
 }

@@ -37,47 +37,60 @@ def argmax(logits) -> int:
 
 
 def spec_generate(target: oracle.Model, draft: oracle.Model, prompts, budget: int, k: int,
-                  rejection: bool, seed: int = 0):
-    """Returns (tokens [n][budget], accept counts per round [n][rounds])."""
-    outs, logs = [], []
-    for s, prompt in enumerate(prompts):
-        rng = Rng(seed ^ ((s * GOLDEN) & MASK))
-        p0 = len(prompt)
-        cap = p0 + budget + k + 2
-        ts, ds = target.state(cap), draft.state(cap)
-        lt = None
-        for i, tok in enumerate(prompt):
-            lt, _ = ts.forward(int(tok), logits=(i == p0 - 1))
-            ds.forward(int(tok), logits=False)
-        first = oracle.sample_softmax(lt, rng.uniform()) if rejection else argmax(lt)
-        out, log = [first], []
-        p, t, prev = p0, first, int(prompt[-1])
-        while len(out) < budget:
-            ud = [rng.uniform() for _ in range(k)] if rejection else None
-            ua = [rng.uniform() for _ in range(k)] if rejection else None
-            uf = rng.uniform() if rejection else None
-            ds.truncate(p - 1)
-            ds.forward(prev, logits=False)
-            drafts, dlog, cur = [], [], t
-            for j in range(k):
-                lq, _ = ds.forward(cur)
-                d = oracle.sample_softmax(lq, ud[j]) if rejection else argmax(lq)
-                drafts.append(d)
-                dlog.append(lq)
-                cur = d
-            ts.truncate(p)
-            tl = np.stack([ts.forward(tok)[0] for tok in [t] + drafts])
-            if rejection:
-                a, toks = oracle.spec_accept_rejection(tl, np.stack(dlog), np.array(drafts), np.array(ua, np.float32), uf)
-            else:
-                a, toks = oracle.spec_accept_greedy(tl, np.array(drafts))
-            log.append(int(a))
-            for i in range(a + 1):
-                if len(out) < budget:
-                    out.append(int(toks[i]))
-            prev = int(toks[a - 1]) if a > 0 else t
-            t = int(toks[a])
-            p += a + 1
-        outs.append(out)
-        logs.append(log)
-    return np.array(outs, np.int32), logs
+                  rejection: bool, seed: int = 0, threads: int = 1):
+    """Returns (tokens [n][budget], accept counts per round [n][rounds]). With threads > 1
+    the sequences run concurrently on host threads, each computing serially (the models
+    are only read; every sequence has its own states and uniform stream)."""
+    if threads > 1 and len(prompts) > 1:
+        from concurrent.futures import ThreadPoolExecutor
+
+        def one(s):
+            oracle.thread_serial(True)
+            return _spec_one(target, draft, s, prompts[s], budget, k, rejection, seed)
+        with ThreadPoolExecutor(max_workers=min(threads, len(prompts))) as ex:
+            res = list(ex.map(one, range(len(prompts))))
+    else:
+        res = [_spec_one(target, draft, s, p, budget, k, rejection, seed) for s, p in enumerate(prompts)]
+    return np.array([r[0] for r in res], np.int32), [r[1] for r in res]
+
+
+def _spec_one(target, draft, s, prompt, budget, k, rejection, seed):
+    """One sequence of the loop (sequence index s picks its uniform stream)."""
+    rng = Rng(seed ^ ((s * GOLDEN) & MASK))
+    p0 = len(prompt)
+    cap = p0 + budget + k + 2
+    ts, ds = target.state(cap), draft.state(cap)
+    lt = None
+    for i, tok in enumerate(prompt):
+        lt, _ = ts.forward(int(tok), logits=(i == p0 - 1))
+        ds.forward(int(tok), logits=False)
+    first = oracle.sample_softmax(lt, rng.uniform()) if rejection else argmax(lt)
+    out, log = [first], []
+    p, t, prev = p0, first, int(prompt[-1])
+    while len(out) < budget:
+        ud = [rng.uniform() for _ in range(k)] if rejection else None
+        ua = [rng.uniform() for _ in range(k)] if rejection else None
+        uf = rng.uniform() if rejection else None
+        ds.truncate(p - 1)
+        ds.forward(prev, logits=False)
+        drafts, dlog, cur = [], [], t
+        for j in range(k):
+            lq, _ = ds.forward(cur)
+            d = oracle.sample_softmax(lq, ud[j]) if rejection else argmax(lq)
+            drafts.append(d)
+            dlog.append(lq)
+            cur = d
+        ts.truncate(p)
+        tl = np.stack([ts.forward(tok)[0] for tok in [t] + drafts])
+        if rejection:
+            a, toks = oracle.spec_accept_rejection(tl, np.stack(dlog), np.array(drafts), np.array(ua, np.float32), uf)
+        else:
+            a, toks = oracle.spec_accept_greedy(tl, np.array(drafts))
+        log.append(int(a))
+        for i in range(a + 1):
+            if len(out) < budget:
+                out.append(int(toks[i]))
+        prev = int(toks[a - 1]) if a > 0 else t
+        t = int(toks[a])
+        p += a + 1
+    return out, log

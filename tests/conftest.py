@@ -28,3 +28,14 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if "gpu" in item.keywords:
             item.add_marker(skip)
+
+
+@pytest.fixture(scope="session")
+def smollm_dirs(tmp_path_factory):
+    """BASELINE config 0's model (SmolLM-135M shape, N(0, 0.02) seed 0, fp16) and config 3's
+    draft (the same weights + N(0, 0.004) noise, noise seed 6), written once per session."""
+    from voxelengine import engine as ve
+    root = tmp_path_factory.mktemp("smollm")
+    target = ve.synth_model(str(root / "target"), seed=0)
+    draft = ve.synth_model(str(root / "draft"), seed=0, noise_seed=6, noise_std=0.004)
+    return target, draft

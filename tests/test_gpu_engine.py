@@ -169,10 +169,10 @@ def test_poisoned_buffers_do_not_leak(models, small):
     assert_tokens(out[0], want, margins)
 
 
-def test_config0_smollm_full_size(tmp_path_factory):
+def test_config0_smollm_full_size(smollm_dirs):
     # SmolLM-135M shape, weights N(0, 0.02) seed 0, 32-token prompt
     # seed 1, prefill then 128 greedy decode steps, batch 1, paged fp16 KV.
-    d = ve.synth_model(str(tmp_path_factory.mktemp("cfg0")), seed=0)
+    d = smollm_dirs[0]
     p = ve.prompt(1, 49152, 32)
     with ve.Engine(d, max_len=256) as eng:
         out, t = eng.generate([p], 128)
@@ -358,3 +358,68 @@ def test_sliding_window_chunked_prefill_and_limits(models, small):
             eng.generate([ve.prompt(601, SMALL["vocab"], 60)], 4)
     with pytest.raises(Exception):  # not a multiple of the page size
         ve.Engine(models["small"], max_len=128, page_size=page, kv_window=40)
+
+
+# ---- Generate's stop rules (Opure_VoxelEngine.cpp:904,918-933) ------------------------
+def _with_config(src, dst, **edits):
+    """A model directory sharing src's weights with config.json edited."""
+    import json
+    os.makedirs(dst, exist_ok=True)
+    cfg = json.load(open(os.path.join(src, "config.json")))
+    cfg.update(edits)
+    with open(os.path.join(dst, "config.json"), "w") as f:
+        json.dump(cfg, f)
+    link = os.path.join(dst, "model.safetensors")
+    if not os.path.exists(link):
+        os.symlink(os.path.join(src, "model.safetensors"), link)
+    return dst
+
+
+@pytest.mark.parametrize("batch,chunk", [(1, 0), (3, 0), (3, 16)])
+def test_generate_stops_on_eos(models, small, tmp_path, batch, chunk):
+    # The stop id (config.json's eos_token_id) is the 10th token of sequence 0's free run:
+    # that sequence stops at its first occurrence, inclusive; the others stop wherever it
+    # first appears in theirs, or run the whole budget.
+    prompts = [ve.prompt(300 + s, SMALL["vocab"], 7 + 3 * s) for s in range(batch)]
+    eos = int(small.generate(prompts[0], 40)[0][9])
+    d = _with_config(models["small"], str(tmp_path / "eos"), eos_token_id=eos)
+    m = oracle.Model(d)
+    with ve.Engine(d, max_batch=batch, max_len=96, prefill_chunk=chunk) as eng:
+        out, counts, hit, _ = eng.generate_stop(prompts, 40)
+    for s, p in enumerate(prompts):
+        want, margins, want_hit = m.generate_stop(p, 40)
+        assert counts[s] == want.size and bool(hit[s]) == want_hit, (s, counts[s], want.size)
+        assert_tokens(out[s, : counts[s]], want, margins)
+        assert (out[s, counts[s]:] == -1).all()
+    assert hit[0] and counts[0] <= 10
+
+
+def test_generate_stops_at_max_positions(models, small, tmp_path):
+    # max_position_embeddings 48: a prompt of length n gets 48 - n tokens (seqLen + 1 >=
+    # maxPos ends the loop), whatever the budget.
+    d = _with_config(models["small"], str(tmp_path / "maxpos"), max_position_embeddings=48)
+    m = oracle.Model(d)
+    prompts = [ve.prompt(400 + s, SMALL["vocab"], 20 + 8 * s) for s in range(2)]
+    with ve.Engine(d, max_batch=2) as eng:
+        out, counts, hit, _ = eng.generate_stop(prompts, 64)
+    for s, p in enumerate(prompts):
+        want, margins, _ = m.generate_stop(p, 64)
+        assert want.size == 48 - p.size and counts[s] == want.size and not hit[s]
+        assert_tokens(out[s, : counts[s]], want, margins)
+
+
+# ---- BASELINE config 0 at batch 64 (the tensor-core path) ------------------------------
+def test_config0_bs64_full_size(smollm_dirs):
+    # All 64 config-0 sequences (prompt seeds 1..64, 32 tokens) decode 128 tokens in one
+    # batch on the tcgen05 GEMV path; every fourth sequence is checked against the oracle
+    # (16 sequences, run one per host thread).
+    d = smollm_dirs[0]
+    prompts = [ve.prompt(1 + b, 49152, 32) for b in range(64)]
+    with ve.Engine(d, max_batch=64, max_len=168) as eng:
+        out, _ = eng.generate(prompts, 128)
+    checked = list(range(0, 64, 4))
+    want, counts, margins = oracle.Model(d).generate_batch([prompts[b] for b in checked], 128,
+                                                           threads=os.cpu_count() or 1)
+    for i, b in enumerate(checked):
+        assert counts[i] == 128
+        assert_tokens(out[b], want[i], margins[i])

@@ -101,3 +101,37 @@ def test_spec_refuses_bad_pairings(pair):
         shared.close()
         other.close()
         t.close()
+
+
+# ---- BASELINE config 3 on its own pair: the config-0 model and its N(0, 0.004) draft -----
+@pytest.fixture(scope="module")
+def cfg3_oracles(smollm_dirs):
+    return oracle.Model(smollm_dirs[0]), oracle.Model(smollm_dirs[1])
+
+
+@pytest.mark.parametrize("k", [4, 8])
+@pytest.mark.parametrize("mode", [ve.SPEC_GREEDY, ve.SPEC_REJECTION])
+def test_config3_b16_matches_oracle(smollm_dirs, cfg3_oracles, k, mode):
+    # B = 16 sequences (prompt seeds 1..16, 32 tokens), 32 generated tokens each: the
+    # verify pass is B (k + 1) = 80 / 144 vectors on the tcgen05 GEMV. Accept counts per
+    # round and tokens bit-exact against the oracle's loop (sequences on host threads).
+    B, budget, seed = 16, 32, 3
+    prompts = [ve.prompt(1 + b, 49152, 32) for b in range(B)]
+    t = ve.Engine(smollm_dirs[0], max_batch=B * (k + 1), max_len=32 + budget + k + 8)
+    d = ve.Engine(smollm_dirs[1], max_batch=B, max_len=32 + budget + k + 8, share=t)
+    try:
+        got, st, log = t.spec_generate(d, prompts, budget, k=k, mode=mode, seed=seed, log_rounds=64)
+        acceptance = t.metrics().speculative_acceptance
+    finally:
+        close(t, d)
+    want, want_log = spec_oracle.spec_generate(*cfg3_oracles, prompts, budget, k,
+                                               rejection=(mode == ve.SPEC_REJECTION), seed=seed,
+                                               threads=os.cpu_count() or 1)
+    for s in range(B):
+        gpu_log = [int(a) for a in log[:, s] if a >= 0]
+        assert gpu_log == want_log[s], (s, gpu_log, want_log[s])
+    assert np.array_equal(got, want)
+    # The partial acceptance the noisy draft is meant to give, reported by the target's
+    # SnapshotMetrics (the reference fixes it at -1).
+    assert 0 < st.accepted < st.drafted
+    assert acceptance == pytest.approx(st.accepted / st.drafted, rel=1e-6)
