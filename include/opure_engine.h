@@ -235,6 +235,28 @@ opure_status opure_engine_sample_generate(opure_engine *e, const int32_t *prompt
  * On failure the reason is copied to err (err_len bytes, may be NULL). */
 opure_status opure_model_inspect(const char *model_dir, opure_engine_info *info, char *err, size_t err_len);
 
+/* ---- serving front end (the reference's HTTP server, src/app/Opure_Server.cpp) ---------
+ * GET /health, POST /generate, GET /metrics on 127.0.0.1:port (0: any free port), with one
+ * engine per listed device serving requests concurrently (the reference serves one at a
+ * time on its one device, :21-25). /generate takes {"tokens": [ids], "max_tokens": n
+ * (clamped to 1..2048), "temperature": t (> 0: sampled), "seed": s} and answers
+ * {"tokens": [...], "prompt_tokens", "generated_tokens", "ms_per_token", "total_ms",
+ * "hit_stop", "engine"}; there is no tokenizer, so a text "prompt" is refused with 400.
+ * Bodies over 1 MiB: 413; unknown routes 404; wrong methods 405; chunked bodies 400;
+ * /generate with no engine (n_devices 0): 503. */
+typedef struct opure_server opure_server;
+opure_status opure_server_start(const char *model_dir, const int *devices, uint32_t n_devices, uint16_t port,
+                                const opure_engine_options *opts, opure_server **out);
+uint16_t opure_server_port(const opure_server *s);
+/* Stops accepting, finishes the requests in hand, joins the workers, frees the engines. */
+opure_status opure_server_stop(opure_server *s);
+/* The /generate body parser on its own: token ids into tokens[cap] (n_tokens gets the
+ * count), the clamped max_tokens and temperature; on a malformed body returns
+ * OPURE_ERR_INVALID_ARG with the client-facing message in err. vocab 0: ids unchecked. */
+opure_status opure_server_parse_generate(const char *body, size_t len, uint32_t vocab, int32_t *tokens,
+                                         uint32_t cap, uint32_t *n_tokens, uint32_t *max_tokens,
+                                         float *temperature, char *err, size_t err_len);
+
 /* ---- seeded synthetic inputs (the reference downloads a checkpoint instead,
  *      scripts/fetch_model.ps1) ---------------------------------------------- */
 typedef struct opure_synth_spec {

@@ -88,19 +88,22 @@ __device__ __forceinline__ void load_q_slice(const float *q_heads /* [n_heads][H
 // (r*warp_count + w)*TPW ..), so a context shorter than warp_count*TB still spreads over
 // every warp. Rounds past t_end are skipped (warp-uniform). COHERENT reads K/V through
 // L2 (for caches written earlier in the same kernel). STAGED reads tokens below stg.n
-// from shared memory.
-template <int HD, int G, bool COHERENT = false, bool STRIDED = false, bool STAGED = false>
+// from shared memory. RB rounds per softmax block (default AttnShape's R): fewer keep
+// fewer K/V rows in registers, for callers whose keys mostly come from shared memory.
+template <int HD, int G, bool COHERENT = false, bool STRIDED = false, bool STAGED = false,
+          int RB = AttnShape<HD>::R>
 __device__ __forceinline__ void attend_range(AttnState<HD, G> &st, const float (&qv)[G][AttnShape<HD>::E],
                                              const KvView &kv, uint32_t t_begin, uint32_t t_end,
                                              uint32_t warp_idx, uint32_t warp_count,
                                              DeviceStatus *status, const KvStage &stg = KvStage{nullptr, nullptr, 0}) {
     using S = AttnShape<HD>;
-    constexpr int LPT = S::LPT, CH = S::CH, TPW = S::TPW, R = S::R, E = S::E;
+    constexpr int LPT = S::LPT, CH = S::CH, TPW = S::TPW, R = RB, E = S::E;
+    constexpr uint32_t TB = uint32_t(TPW) * R;  // tokens per warp block
     const uint32_t lane = threadIdx.x & 31u;
     const uint32_t grp = lane / LPT, sub = lane % LPT;
     const size_t blk = size_t(kv.page_size) * HD;  // elements per page block
 
-    for (uint32_t base = t_begin + (STRIDED ? 0u : warp_idx * S::TB); base < t_end; base += warp_count * S::TB) {
+    for (uint32_t base = t_begin + (STRIDED ? 0u : warp_idx * TB); base < t_end; base += warp_count * TB) {
         uint4 kr[R][CH], vr[R][CH];
         bool valid[R], live[R];
 #pragma unroll

@@ -8,6 +8,7 @@
 #include "opure_engine.h"
 #include "platform.h"
 #include "sample_decode.h"
+#include "server.h"
 #include "spec_decode.h"
 #include "synth.h"
 #include "voxel_engine.h"
@@ -420,6 +421,68 @@ opure_status opure_synth_uniforms(uint64_t seed, uint64_t n, float *out) {
         const auto v = opure::synth::Uniforms(seed, n);
         std::memcpy(out, v.data(), n * 4);
     });
+}
+
+}  // extern "C"
+
+// ---- serving front end (server.h) -----------------------------------------------------
+struct opure_server {
+    std::unique_ptr<opure::server::Server> srv;
+};
+
+extern "C" {
+
+opure_status opure_server_start(const char *model_dir, const int *devices, uint32_t n_devices, uint16_t port,
+                                const opure_engine_options *opts, opure_server **out) {
+    if (!out || (n_devices && (!model_dir || !devices))) return OPURE_ERR_INVALID_ARG;
+    *out = nullptr;
+    opure_engine scratch;
+    const opure_status s = Guard(&scratch, [&] {
+        std::vector<std::unique_ptr<opure::engine::VoxelEngine>> engines;
+        for (uint32_t i = 0; i < n_devices; ++i) {
+            auto e = std::make_unique<opure::engine::VoxelEngine>();
+            e->Initialize(model_dir, ToOptions(opts), devices[i]);
+            engines.push_back(std::move(e));
+        }
+        auto *h = new opure_server;
+        try {
+            h->srv = std::make_unique<opure::server::Server>(std::move(engines), port);
+        } catch (...) {
+            delete h;
+            throw;
+        }
+        *out = h;
+    });
+    if (s != OPURE_OK) g_create_error = scratch.err;
+    return s;
+}
+
+uint16_t opure_server_port(const opure_server *s) { return s && s->srv ? s->srv->Port() : 0; }
+
+opure_status opure_server_stop(opure_server *s) {
+    if (!s) return OPURE_ERR_INVALID_ARG;
+    delete s;  // stops the threads, then the engines are destroyed
+    return OPURE_OK;
+}
+
+opure_status opure_server_parse_generate(const char *body, size_t len, uint32_t vocab, int32_t *tokens,
+                                         uint32_t cap, uint32_t *n_tokens, uint32_t *max_tokens,
+                                         float *temperature, char *err, size_t err_len) {
+    if (!body || !n_tokens || !max_tokens || !temperature) return OPURE_ERR_INVALID_ARG;
+    opure::server::GenerateRequest r;
+    std::string e;
+    if (!opure::server::ParseGenerate(std::string_view(body, len), vocab, r, e)) {
+        if (err && err_len) {
+            std::strncpy(err, e.c_str(), err_len - 1);
+            err[err_len - 1] = 0;
+        }
+        return OPURE_ERR_INVALID_ARG;
+    }
+    *n_tokens = uint32_t(r.tokens.size());
+    for (uint32_t i = 0; i < std::min<uint32_t>(cap, *n_tokens); ++i) tokens[i] = int32_t(r.tokens[i]);
+    *max_tokens = r.maxTokens;
+    *temperature = r.temperature;
+    return OPURE_OK;
 }
 
 }  // extern "C"

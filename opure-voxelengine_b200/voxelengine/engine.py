@@ -107,6 +107,9 @@ def lib() -> C.CDLL:
             "opure_engine_phase_trace": [P, P, C.c_size_t, P],
             "opure_engine_read_tokens": [P, u32, u32, u32, P],
             "opure_synth_kv": [u64, u32, u32, u32, u32, u32, P],
+            "opure_server_start": [C.c_char_p, P, u32, C.c_uint16, P, P],
+            "opure_server_stop": [P],
+            "opure_server_parse_generate": [C.c_char_p, C.c_size_t, u32, P, u32, P, P, P, C.c_char_p, C.c_size_t],
             "opure_model_inspect": [C.c_char_p, P, C.c_char_p, C.c_size_t],
             "opure_synth_model": [C.c_char_p, P],
             "opure_synth_normal_f16": [u64, f32, u64, P],
@@ -122,6 +125,8 @@ def lib() -> C.CDLL:
         L.opure_engine_last_error.restype = C.c_char_p
         L.opure_engine_ctx.argtypes = [P]
         L.opure_engine_ctx.restype = P
+        L.opure_server_port.argtypes = [P]
+        L.opure_server_port.restype = C.c_uint16
         _lib = L
     return _lib
 
@@ -384,3 +389,46 @@ class Engine:
     def load_kv(self, seq: int, kv: np.ndarray, length: int):
         kv = np.ascontiguousarray(kv, np.uint16)
         _check(lib().opure_engine_load_kv(self.h, seq, _p(kv), length), "load_kv", self.h)
+
+
+# ---- serving front end -------------------------------------------------------------
+class Server:
+    """The HTTP front end (GET /health, POST /generate, GET /metrics) on 127.0.0.1 with one
+    engine per device in `devices` (none: the routes answer, /generate with 503)."""
+
+    def __init__(self, model_dir: str | None = None, devices=(), port: int = 0, **engine_opts):
+        devs = np.ascontiguousarray(list(devices), np.int32)
+        o = EngineOptions(engine_opts.get("max_new_tokens", 256), engine_opts.get("max_batch", 1),
+                          engine_opts.get("max_len", 0), engine_opts.get("page_size", 64),
+                          engine_opts.get("page_seed", 3), 1, 1.0, engine_opts.get("path", PATH_AUTO), 0, 0, 0, 0)
+        h = C.c_void_p()
+        _check(lib().opure_server_start(model_dir.encode() if model_dir else None, _p(devs) if devs.size else None,
+                                        int(devs.size), port, C.byref(o), C.byref(h)), "opure_server_start")
+        self.h = h
+        self.port = int(lib().opure_server_port(h))
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().opure_server_stop(self.h)
+            self.h = None
+
+    __del__ = close
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+
+def parse_generate(body: bytes, vocab: int = 0):
+    """The server's /generate body parser: (tokens, max_tokens, temperature), or raises
+    ValueError with the message a client would get."""
+    toks = np.zeros(4096, np.int32)
+    n, mt, t = C.c_uint32(), C.c_uint32(), C.c_float()
+    err = C.create_string_buffer(512)
+    st = lib().opure_server_parse_generate(body, len(body), vocab, _p(toks), toks.size, C.byref(n), C.byref(mt),
+                                           C.byref(t), err, 512)
+    if st != 0:
+        raise ValueError(err.value.decode(errors="replace"))
+    return toks[: n.value].tolist(), int(mt.value), float(t.value)

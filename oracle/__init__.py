@@ -89,7 +89,7 @@ def lib() -> C.CDLL:
             "orc_get_threads": (i32, []),
             "orc_thread_serial": (None, [i32]),
             "orc_generate_stop": (i32, [P, P, u32, u32, u32, C.c_int64, P, P, P]),
-            "orc_generate_batch": (i32, [P, P, P, u32, u32, u32, C.c_int64, i32, P, P, P]),
+            "orc_generate_batch": (i32, [P, P, P, u32, u32, u32, C.c_int64, i32, P, P, P, P]),
             "orc_synth_normal_f16": (None, [u64, f32, u64, P]),
             "orc_synth_prompt": (None, [u64, u32, u32, P]),
             "orc_synth_permutation": (None, [u64, u32, P]),
@@ -435,7 +435,7 @@ class Model:
                        eos: int | None = None):
         """Independent sequences on `threads` host threads (one sequence per thread at a
         time, serial arithmetic inside). Returns (tokens [n][budget] (unused entries 0),
-        counts [n], margins [n][budget])."""
+        counts [n], margins [n][budget], runner-up tokens [n][budget])."""
         ps = [np.asarray(p, np.uint32) for p in prompts]
         flat = np.ascontiguousarray(np.concatenate(ps), np.uint32)
         lens = np.array([p.size for p in ps], np.uint32)
@@ -443,12 +443,13 @@ class Model:
         out = np.zeros((n, budget), np.uint32)
         counts = np.zeros(n, np.uint32)
         margins = np.zeros((n, budget), np.float32)
+        second = np.zeros((n, budget), np.uint32)
         rc = lib().orc_generate_batch(self.h, _p(flat), _p(lens), n, budget, max_pos or self.c.max_pos,
                                       self.eos if eos is None else eos, int(threads), _p(out), _p(counts),
-                                      _p(margins))
+                                      _p(margins), _p(second))
         if rc != 0:
             raise ValueError("oracle generate_batch failed")
-        return out, counts, margins
+        return out, counts, margins, second
 
     def state(self, max_pos: int | None = None) -> "State":
         return State(self, max_pos or self.c.max_pos)

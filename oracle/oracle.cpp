@@ -911,19 +911,23 @@ uint16_t q8_round_store(float w, float scale) {
 // prompt position is pushed first; after each push the loop ends when it was the stop id
 // (:925-930) or when seqLen + 1 >= maxPos (:932); otherwise one decode step follows.
 int generate_one(const orc_model *m, const uint32_t *prompt, uint32_t n_prompt, uint32_t budget,
-                 uint32_t max_pos, int64_t eos, uint32_t *out, float *margins, int *hit_stop) {
+                 uint32_t max_pos, int64_t eos, uint32_t *out, float *margins, int *hit_stop,
+                 uint32_t *second = nullptr) {
     if (!m || n_prompt == 0 || n_prompt > max_pos) return -1;
     orc_state *s = orc_state_create(m, max_pos);
     std::vector<float> logits(m->c.vocab);
+    uint32_t i2 = 0;  // runner-up of the last top() (lowest index among equal values)
     auto top = [&](float *margin) {
         float v1;
         const uint32_t i1 = argmax1(logits.data(), m->c.vocab, &v1);
-        if (margin) {
-            float v2 = -std::numeric_limits<float>::infinity();
-            for (uint32_t i = 0; i < m->c.vocab; ++i)
-                if (i != i1 && logits[i] > v2) v2 = logits[i];
-            *margin = v1 - v2;
-        }
+        float v2 = -std::numeric_limits<float>::infinity();
+        i2 = i1;
+        for (uint32_t i = 0; i < m->c.vocab; ++i)
+            if (i != i1 && logits[i] > v2) {
+                v2 = logits[i];
+                i2 = i;
+            }
+        if (margin) *margin = v1 - v2;
         return i1;
     };
     for (uint32_t i = 0; i < n_prompt; ++i)
@@ -935,6 +939,7 @@ int generate_one(const orc_model *m, const uint32_t *prompt, uint32_t n_prompt, 
     for (uint32_t i = 0; i < budget; ++i) {
         out[n] = next;
         if (margins) margins[n] = mg;
+        if (second) second[n] = i2;
         ++n;
         if (eos >= 0 && next == uint32_t(eos)) {
             if (hit_stop) *hit_stop = 1;
@@ -961,7 +966,7 @@ int orc_generate_stop(const orc_model *m, const uint32_t *prompt, uint32_t n_pro
 
 int orc_generate_batch(const orc_model *m, const uint32_t *prompts, const uint32_t *prompt_lens,
                        uint32_t n_seq, uint32_t budget, uint32_t max_pos, int64_t eos, int threads,
-                       uint32_t *out, uint32_t *counts, float *margins) {
+                       uint32_t *out, uint32_t *counts, float *margins, uint32_t *second) {
     if (!m || n_seq == 0) return -1;
     std::vector<size_t> off(n_seq + 1, 0);
     for (uint32_t i = 0; i < n_seq; ++i) off[i + 1] = off[i] + prompt_lens[i];
@@ -972,7 +977,7 @@ int orc_generate_batch(const orc_model *m, const uint32_t *prompts, const uint32
         for (uint32_t i = who; i < n_seq; i += nt) {
             const int n = generate_one(m, prompts + off[i], prompt_lens[i], budget, max_pos, eos,
                                        out + size_t(i) * budget, margins ? margins + size_t(i) * budget : nullptr,
-                                       nullptr);
+                                       nullptr, second ? second + size_t(i) * budget : nullptr);
             rc[i] = n;
             if (counts) counts[i] = n < 0 ? 0u : uint32_t(n);
         }

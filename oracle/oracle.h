@@ -204,10 +204,12 @@ int orc_generate_stop(const orc_model *m, const uint32_t *prompt, uint32_t n_pro
 /* orc_generate_stop for n_seq independent sequences (prompts concatenated, prompt_lens
  * each), one sequence per host thread at a time on `threads` threads, each computing
  * serially: out [n_seq][budget], counts [n_seq] tokens each, margins (may be NULL)
- * [n_seq][budget]. Results equal the one-at-a-time ones. 0 on success. */
+ * [n_seq][budget] top-1 minus top-2 logit behind each token, second (may be NULL)
+ * [n_seq][budget] the top-2 token (lowest index among equal values). Results equal the
+ * one-at-a-time ones. 0 on success. */
 int orc_generate_batch(const orc_model *m, const uint32_t *prompts, const uint32_t *prompt_lens,
                        uint32_t n_seq, uint32_t budget, uint32_t max_pos, int64_t eos, int threads,
-                       uint32_t *out, uint32_t *counts, float *margins);
+                       uint32_t *out, uint32_t *counts, float *margins, uint32_t *second);
 
 /* Worker threads for the row loops of GEMV and the head loop of attention. Rows are
  * independent, so results are identical for any thread count. */

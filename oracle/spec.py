@@ -37,10 +37,13 @@ def argmax(logits) -> int:
 
 
 def spec_generate(target: oracle.Model, draft: oracle.Model, prompts, budget: int, k: int,
-                  rejection: bool, seed: int = 0, threads: int = 1):
-    """Returns (tokens [n][budget], accept counts per round [n][rounds]). With threads > 1
-    the sequences run concurrently on host threads, each computing serially (the models
-    are only read; every sequence has its own states and uniform stream)."""
+                  rejection: bool, seed: int = 0, threads: int = 1, records: bool = False):
+    """Returns (tokens [n][budget], accept counts per round [n][rounds]), and with
+    records=True also per sequence a list of per-round records: the drafted tokens, the
+    accepted count, the emitted tokens and (rejection) each draft's acceptance ratio
+    u_accept * q(d) / p(d) (accepted when <= 1). With threads > 1 the sequences run
+    concurrently on host threads, each computing serially (the models are only read;
+    every sequence has its own states and uniform stream)."""
     if threads > 1 and len(prompts) > 1:
         from concurrent.futures import ThreadPoolExecutor
 
@@ -51,7 +54,15 @@ def spec_generate(target: oracle.Model, draft: oracle.Model, prompts, budget: in
             res = list(ex.map(one, range(len(prompts))))
     else:
         res = [_spec_one(target, draft, s, p, budget, k, rejection, seed) for s, p in enumerate(prompts)]
-    return np.array([r[0] for r in res], np.int32), [r[1] for r in res]
+    out = (np.array([r[0] for r in res], np.int32), [r[1] for r in res])
+    return out + ([r[2] for r in res],) if records else out
+
+
+def _prob(logits, i: int) -> float:
+    """softmax(logits)[i] in double."""
+    z = np.asarray(logits, np.float64)
+    e = np.exp(z - z.max())
+    return float(e[i] / e.sum())
 
 
 def _spec_one(target, draft, s, prompt, budget, k, rejection, seed):
@@ -65,7 +76,7 @@ def _spec_one(target, draft, s, prompt, budget, k, rejection, seed):
         lt, _ = ts.forward(int(tok), logits=(i == p0 - 1))
         ds.forward(int(tok), logits=False)
     first = oracle.sample_softmax(lt, rng.uniform()) if rejection else argmax(lt)
-    out, log = [first], []
+    out, log, recs = [first], [], []
     p, t, prev = p0, first, int(prompt[-1])
     while len(out) < budget:
         ud = [rng.uniform() for _ in range(k)] if rejection else None
@@ -87,10 +98,15 @@ def _spec_one(target, draft, s, prompt, budget, k, rejection, seed):
         else:
             a, toks = oracle.spec_accept_greedy(tl, np.array(drafts))
         log.append(int(a))
+        rec = {"drafts": [int(d) for d in drafts], "a": int(a), "emitted": [int(x) for x in toks[: a + 1]]}
+        if rejection:
+            rec["ratios"] = [float(ua[j]) * _prob(dlog[j], drafts[j]) / max(_prob(tl[j], drafts[j]), 1e-300)
+                             for j in range(k)]
+        recs.append(rec)
         for i in range(a + 1):
             if len(out) < budget:
                 out.append(int(toks[i]))
         prev = int(toks[a - 1]) if a > 0 else t
         t = int(toks[a])
         p += a + 1
-    return out, log
+    return out, log, recs

@@ -61,8 +61,16 @@ def test_stop_rules():
 def test_batch_equals_one_at_a_time():
     m = oracle.Model.synth(seed=4, **TINY)
     prompts = [oracle.prompt(10 + s, TINY["vocab"], 3 + s % 4) for s in range(7)]
-    out, counts, margins = m.generate_batch(prompts, 9, threads=3)
+    out, counts, margins, second = m.generate_batch(prompts, 9, threads=3)
     for s, p in enumerate(prompts):
         want, mg = m.generate(p, 9)
         assert counts[s] == 9
         assert np.array_equal(out[s], want) and np.array_equal(margins[s], mg)
+    # The runner-up of each step: the best other token, its logit margin behind the winner.
+    st = m.state(32)
+    lg = None
+    for i, t in enumerate(prompts[0]):
+        lg, _ = st.forward(int(t))
+    order = np.argsort(-lg.astype(np.float64), kind="stable")
+    assert order[0] == out[0][0] and order[1] == second[0][0]
+    assert np.float32(lg[order[0]] - lg[order[1]]) == margins[0][0]
