@@ -117,8 +117,8 @@ __device__ __forceinline__ void attend_range(AttnState<HD, G> &st, const float (
                 const size_t o = size_t(t) * HD + sub * E;
 #pragma unroll
                 for (int c = 0; c < CH; ++c) {
-                    kr[r][c] = *reinterpret_cast<const uint4 *>(stg.k + o + c * 8);
-                    vr[r][c] = *reinterpret_cast<const uint4 *>(stg.v + o + c * 8);
+                    kr[r][c] = lds128(stg.k + o + c * 8);
+                    vr[r][c] = lds128(stg.v + o + c * 8);
                 }
                 continue;
             }

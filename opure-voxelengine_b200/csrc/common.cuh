@@ -58,6 +58,37 @@ __device__ __forceinline__ uint4 ldg_stream(const void *p) {
     return r;
 }
 
+// Shared-memory loads by explicit shared-window address. Pointers that reach a loop
+// through an array or a struct can lose their address space in the compiler's view, which
+// then emits slower generic loads; these always compile to ld.shared.
+__device__ __forceinline__ uint32_t shared_addr(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint4 lds128(const void *p) {
+    uint4 r;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "r"(shared_addr(p)));
+    return r;
+}
+__device__ __forceinline__ float4 lds_f4(const float *p) {
+    float4 r;
+    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+                 : "r"(shared_addr(p)));
+    return r;
+}
+__device__ __forceinline__ float lds_f32(const float *p) {
+    float r;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(r) : "r"(shared_addr(p)));
+    return r;
+}
+__device__ __forceinline__ float lds_h(const __half *p) {
+    unsigned short r;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(r) : "r"(shared_addr(p)));
+    return __half2float(__ushort_as_half(r));
+}
+
 __device__ __forceinline__ float2 h2f2(uint32_t u) {
     __half2 h = *reinterpret_cast<__half2 *>(&u);
     return __half22float2(h);

@@ -228,8 +228,8 @@ __device__ __forceinline__ void smem_dot(const uint8_t *w, uint32_t pitch, uint3
         float xf[NV][8];
 #pragma unroll
         for (int v = 0; v < NV; ++v) {
-            const float4 a = *reinterpret_cast<const float4 *>(xs + v * h + c * 8);
-            const float4 b = *reinterpret_cast<const float4 *>(xs + v * h + c * 8 + 4);
+            const float4 a = lds_f4(xs + v * h + c * 8);
+            const float4 b = lds_f4(xs + v * h + c * 8 + 4);
             xf[v][0] = a.x; xf[v][1] = a.y; xf[v][2] = a.z; xf[v][3] = a.w;
             xf[v][4] = b.x; xf[v][5] = b.y; xf[v][6] = b.z; xf[v][7] = b.w;
         }
@@ -237,7 +237,7 @@ __device__ __forceinline__ void smem_dot(const uint8_t *w, uint32_t pitch, uint3
         for (int r = 0; r < R; ++r) {
             if (r >= int(nrows)) break;
             float wf[8];
-            unpack8(*reinterpret_cast<const uint4 *>(w + size_t(r) * pitch + c * 16), wf);
+            unpack8(lds128(w + size_t(r) * pitch + c * 16), wf);
 #pragma unroll
             for (int v = 0; v < NV; ++v)
 #pragma unroll
@@ -263,8 +263,8 @@ __device__ __forceinline__ void smem_dot_ptrs(const uint8_t *const (&rows)[R], u
         float xf[NV][8];
 #pragma unroll
         for (int v = 0; v < NV; ++v) {
-            const float4 a = *reinterpret_cast<const float4 *>(xs + v * h + c * 8);
-            const float4 b = *reinterpret_cast<const float4 *>(xs + v * h + c * 8 + 4);
+            const float4 a = lds_f4(xs + v * h + c * 8);
+            const float4 b = lds_f4(xs + v * h + c * 8 + 4);
             xf[v][0] = a.x; xf[v][1] = a.y; xf[v][2] = a.z; xf[v][3] = a.w;
             xf[v][4] = b.x; xf[v][5] = b.y; xf[v][6] = b.z; xf[v][7] = b.w;
         }
@@ -272,7 +272,7 @@ __device__ __forceinline__ void smem_dot_ptrs(const uint8_t *const (&rows)[R], u
         for (int r = 0; r < R; ++r) {
             if (r >= int(nrows)) break;
             float wf[8];
-            unpack8(*reinterpret_cast<const uint4 *>(rows[r] + c * 16), wf);
+            unpack8(lds128(rows[r] + c * 16), wf);
 #pragma unroll
             for (int v = 0; v < NV; ++v)
 #pragma unroll
@@ -845,6 +845,133 @@ __device__ bool p_wait_slot(uint64_t *bar, uint32_t parity, const PersistArgs &p
     return ok;
 }
 
+// Exact two-pass attention of one query vector over keys [0, T) of kv head g, for contexts
+// that fit the shared-memory KV stage (T <= its capacity; hd 64). Rows [0, n_old) are
+// already staged (copied a layer ahead); rows [n_old, T) were written by phase A of this
+// layer and are fetched here first, in the same memory round trip as the query. Then the
+// whole CTA computes every score (8 lanes per key), each head's max and exp sums (one warp
+// per head), and the probability-weighted values (one thread per head and dimension pair,
+// the keys split in halves): no running rescale and no merging of per-lane or per-warp
+// states, which at decode lengths cost more than the arithmetic. Softmax in log2 units
+// (q pre-scaled by scale * log2 e), fp32, as attend_range. Writes out[h * 64 + d] =
+// sum_t p_t V[t][d] / max(sum_t p_t, 1e-30). sp: shared scratch of kTwoPassScratch floats.
+constexpr uint32_t kTwoPassKeys = kKvStageTokens;
+template <int G>
+constexpr uint32_t kTwoPassScratch = G * kTwoPassKeys + 4 + G * 64;
+
+template <int G>
+__device__ __forceinline__ void attend_two_pass(const float *q, float scale_log2, __half *sk, __half *sv,
+                                                uint32_t n_old, uint32_t T, const uint16_t *pool,
+                                                const int32_t *pt_row, uint32_t page_size, uint32_t n_kv,
+                                                uint32_t g, float *sp, float *out) {
+    constexpr uint32_t HD = 64;
+    const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+    const uint32_t sub = lane & 7u, grp = lane >> 3;
+    // (1) Loads first: the q slice of this lane, then this step's K/V rows.
+    float4 q4[G][2];
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+        q4[h][0] = __ldcg(reinterpret_cast<const float4 *>(q + h * HD + sub * 8));
+        q4[h][1] = __ldcg(reinterpret_cast<const float4 *>(q + h * HD + sub * 8 + 4));
+    }
+    const uint32_t items = (T - n_old) * 16;  // (row, K|V, 16-byte chunk)
+    const size_t blk = size_t(page_size) * HD;
+    for (uint32_t i0 = 0; i0 < items; i0 += kPThreads) {
+        const uint32_t i = i0 + tid;
+        if (i < items) {
+            const uint32_t t = n_old + i / 16, sel = (i / 8) & 1u, c = i % 8;
+            const int32_t page = pt_row[t / page_size];
+            const uint4 val = ldcg_v4(pool + ((size_t(page) * 2 + sel) * n_kv + g) * blk + size_t(t % page_size) * HD + c * 8);
+            *reinterpret_cast<uint4 *>((sel ? sv : sk) + size_t(t) * HD + c * 8) = val;
+        }
+    }
+    float qf[G][8];
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+        qf[h][0] = q4[h][0].x * scale_log2; qf[h][1] = q4[h][0].y * scale_log2;
+        qf[h][2] = q4[h][0].z * scale_log2; qf[h][3] = q4[h][0].w * scale_log2;
+        qf[h][4] = q4[h][1].x * scale_log2; qf[h][5] = q4[h][1].y * scale_log2;
+        qf[h][6] = q4[h][1].z * scale_log2; qf[h][7] = q4[h][1].w * scale_log2;
+    }
+    __syncthreads();
+    // (2) Scores: key t = (r * 8 + warp) * 4 + grp.
+    float *S = sp;  // [G][kTwoPassKeys]
+    for (uint32_t t0 = warp * 4; t0 < T; t0 += 32) {
+        const uint32_t t = t0 + grp;
+        const bool ok = t < T;
+        float kf[8];
+        unpack8(ok ? lds128(sk + size_t(t) * HD + sub * 8) : make_uint4(0, 0, 0, 0), kf);
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+            float2 d2 = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int e = 0; e < 8; e += 2)
+                d2 = __ffma2_rn(make_float2(qf[h][e], qf[h][e + 1]), make_float2(kf[e], kf[e + 1]), d2);
+            float d = d2.x + d2.y;
+            d += __shfl_xor_sync(0xffffffffu, d, 4);
+            d += __shfl_xor_sync(0xffffffffu, d, 2);
+            d += __shfl_xor_sync(0xffffffffu, d, 1);
+            if (sub == 0 && ok) S[h * kTwoPassKeys + t] = d;
+        }
+    }
+    __syncthreads();
+    // (3) Per head: max, probabilities in place, their sum.
+    if (warp < uint32_t(G)) {
+        float *Sh = S + warp * kTwoPassKeys;
+        float m = -INFINITY;
+        for (uint32_t t = lane; t < T; t += 32) m = fmaxf(m, Sh[t]);
+        m = warp_max(m);
+        float l = 0.f;
+        for (uint32_t t = lane; t < T; t += 32) {
+            const float pr = fast_exp2(Sh[t] - m);
+            Sh[t] = pr;
+            l += pr;
+        }
+        l = warp_sum(l);
+        if (lane == 0) sp[G * kTwoPassKeys + warp] = l;
+    }
+    __syncthreads();
+    // (4) Values: thread (half, head, dimension pair); each warp serves one head.
+    const uint32_t n_items = G * 32, half = tid / n_items, item = tid % n_items;
+    const uint32_t h = item / 32, dp = item % 32;
+    float2 acc = make_float2(0.f, 0.f);
+    if (half < 2) {
+        const float *P = S + h * kTwoPassKeys;
+        const uint32_t ta = half ? T / 2 : 0, tb = half ? T : T / 2;
+        float2 a1 = make_float2(0.f, 0.f);
+        uint32_t t = ta;
+        for (; t + 1 < tb; t += 2) {
+            const float p0 = P[t], p1 = P[t + 1];
+            const float2 v0 = h2f2(*reinterpret_cast<const uint32_t *>(sv + size_t(t) * HD + 2 * dp));
+            const float2 v1 = h2f2(*reinterpret_cast<const uint32_t *>(sv + size_t(t + 1) * HD + 2 * dp));
+            acc.x = fmaf(p0, v0.x, acc.x);
+            acc.y = fmaf(p0, v0.y, acc.y);
+            a1.x = fmaf(p1, v1.x, a1.x);
+            a1.y = fmaf(p1, v1.y, a1.y);
+        }
+        if (t < tb) {
+            const float p0 = P[t];
+            const float2 v0 = h2f2(*reinterpret_cast<const uint32_t *>(sv + size_t(t) * HD + 2 * dp));
+            acc.x = fmaf(p0, v0.x, acc.x);
+            acc.y = fmaf(p0, v0.y, acc.y);
+        }
+        acc.x += a1.x;
+        acc.y += a1.y;
+    }
+    float *part = sp + G * kTwoPassKeys + 4;  // [G * 32][2]: the second halves
+    if (half == 1) {
+        part[2 * item] = acc.x;
+        part[2 * item + 1] = acc.y;
+    }
+    __syncthreads();
+    if (half == 0) {
+        const float inv = 1.0f / fmaxf(sp[G * kTwoPassKeys + h], 1e-30f);
+        out[h * HD + 2 * dp] = (acc.x + part[2 * item]) * inv;
+        out[h * HD + 2 * dp + 1] = (acc.y + part[2 * item + 1]) * inv;
+    }
+    __syncthreads();
+}
+
 template <int NV, int HD, int G>
 __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __grid_constant__ PersistArgs p) {
     extern __shared__ __align__(1024) uint8_t psm[];
@@ -852,8 +979,10 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
     __shared__ __align__(8) uint64_t lbar[kLmBufs];
     __shared__ __align__(8) uint64_t kvbar;
     __shared__ uint32_t s_nst[NV];
+    __shared__ bool s_two[NV];  // this vector's attention runs attend_two_pass
     __shared__ int s_ok;
-    __shared__ WarpStates<HD, G, kPWarps> ws;
+    __shared__ WarpStates<HD, G, kPWarps> ws;  // also attend_two_pass's scratch
+    static_assert(sizeof(ws) >= kTwoPassScratch<G> * sizeof(float), "two-pass scratch does not fit");
     __shared__ int32_t s_seq[NV], s_pos[NV];
     __shared__ int32_t s_pt[NV][kPtStageP];
     __shared__ unsigned long long cta_best[kPWarps][NV];
@@ -908,6 +1037,15 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
             }
         }
         s_nst[threadIdx.x] = n;
+        // Two-pass attention when every key of the vector fits the stage on valid pages.
+        const uint32_t T = uint32_t(max(s_pos[threadIdx.x] + 1, 0));
+        bool two = HD == 64 && sq >= 0 && stage_pt && sh.nb && !p.kv_ring && T >= 1 && T <= p.kv_cap &&
+                   T <= kTwoPassKeys && uint32_t(first) >= n && uint32_t(first) <= T;
+        for (uint32_t i = 0; two && i * p.page_size < T; ++i) {
+            const int32_t pg = i < p.max_pages ? s_pt[threadIdx.x][i] : -1;
+            two = pg >= 0 && uint32_t(pg) < p.n_pages;
+        }
+        s_two[threadIdx.x] = two;
     }
     __syncthreads();
     uint32_t kv_total = 0;  // bytes per layer
@@ -1064,6 +1202,16 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
                 ++kv_waited;
             }
             for (int v = 0; v < NV; ++v) {
+                if constexpr (HD == 64) {
+                    if (s_two[v]) {
+                        attend_two_pass<G>(p.q + size_t(v) * qrows + size_t(sh.g) * G * HD, p.scale_log2,
+                                           reinterpret_cast<__half *>(kvs + size_t(v) * 2 * kv_vbytes),
+                                           reinterpret_cast<__half *>(kvs + size_t(v) * 2 * kv_vbytes + kv_vbytes),
+                                           s_nst[v], uint32_t(s_pos[v] + 1), ly.kv_pool, s_pt[v], p.page_size, p.n_kv,
+                                           sh.g, reinterpret_cast<float *>(&ws), attn + v * cols_b);
+                        continue;
+                    }
+                }
                 using S = AttnShape<HD>;
                 float qv[G][S::E];
                 const uint32_t sub = lane % S::LPT;
@@ -1089,7 +1237,9 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
                 const KvStage stg{reinterpret_cast<const __half *>(kvs + size_t(v) * 2 * kv_vbytes),
                                   reinterpret_cast<const __half *>(kvs + size_t(v) * 2 * kv_vbytes + kv_vbytes),
                                   s_nst[v]};
-                attend_range<HD, G, true, true, true>(st, qv, kv, window_begin(s_pos[v], p.page_size, p.kv_ring),
+                // Two rounds per softmax block: the keys come from shared memory (short
+                // latency), and fewer K/V rows in flight keep the kernel's registers from spilling.
+                attend_range<HD, G, true, true, true, 2>(st, qv, kv, window_begin(s_pos[v], p.page_size, p.kv_ring),
                                                       uint32_t(max(s_pos[v] + 1, 0)), warp, kPWarps, p.st, stg);
                 merge_lane_groups<HD, G>(st);
                 store_warp_state<HD, G, kPWarps>(st, ws, warp);
@@ -1111,13 +1261,13 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
                 for (int v = 0; v < NV; ++v) acc[0][v] = acc[1][v] = 0.f;
                 for (uint32_t c = lane; c < nch; c += 32) {
                     float wf[2][8];
-                    unpack8(*reinterpret_cast<const uint4 *>(wsm + size_t(rr) * bpitch + c * 16), wf[0]);
+                    unpack8(lds128(wsm + size_t(rr) * bpitch + c * 16), wf[0]);
                     if (two)
-                        unpack8(*reinterpret_cast<const uint4 *>(wsm + size_t(rr + kPWarps) * bpitch + c * 16), wf[1]);
+                        unpack8(lds128(wsm + size_t(rr + kPWarps) * bpitch + c * 16), wf[1]);
 #pragma unroll
                     for (int v = 0; v < NV; ++v) {
-                        const float4 a0 = *reinterpret_cast<const float4 *>(attn + v * cols_b + c * 8);
-                        const float4 a1 = *reinterpret_cast<const float4 *>(attn + v * cols_b + c * 8 + 4);
+                        const float4 a0 = lds_f4(attn + v * cols_b + c * 8);
+                        const float4 a1 = lds_f4(attn + v * cols_b + c * 8 + 4);
                         const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
 #pragma unroll
                         for (int e = 0; e < 8; ++e) acc[0][v] = fmaf(wf[0][e], av[e], acc[0][v]);
@@ -1196,9 +1346,9 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
 #pragma unroll
                 for (int v = 0; v < NV; ++v) acc[v] = 0.f;
                 for (uint32_t f = 0; f < sh.nc; ++f) {
-                    const float wv = __half2float(wdh[size_t(f) * p.h + o]);
+                    const float wv = lds_h(wdh + size_t(f) * p.h + o);
 #pragma unroll
-                    for (int v = 0; v < NV; ++v) acc[v] = fmaf(wv, hs[f * NV + v], acc[v]);
+                    for (int v = 0; v < NV; ++v) acc[v] = fmaf(wv, lds_f32(hs + f * NV + v), acc[v]);
                 }
 #pragma unroll
                 for (int v = 0; v < NV; ++v)
