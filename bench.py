@@ -192,6 +192,7 @@ def allreduce_max(world, x: float) -> float:
 # prompts, byte-identical to the engine's, so the reference arm loads no product library.
 def cpu_model():
     import oracle
+    oracle.set_threads(os.cpu_count() or 1)
     return oracle.Model.synth(seed=0)
 
 
@@ -416,6 +417,31 @@ def measure_bs64(args, world, rank, local, mp):
             "gpu_launches": launches_per_step(info, B) * args.bs64_steps}
 
 
+def measure_int8(args, world, rank, local):
+    """Config 0 at batch 1 with GEMV_Quant weights: the same model quantised per tensor to
+    int8 (absmax / 127; embedding and lm_head stay fp16), on the persistent step kernel.
+    Device-resident steps, same accounting as the bs1 line (algorithmic bytes from the
+    int8 weight stream)."""
+    from voxelengine import engine as ve
+    root = os.environ.get("OPURE_BENCH_DIR", "/tmp/opure_bench")
+    mp = ve.synth_model(os.path.join(root, "smollm135m_seed0_int8"), seed=0, int8=True)
+    eng = ve.Engine(mp, device=local, max_batch=1, max_len=PROMPT_LEN + DECODE_STEPS + 8, page_size=64, page_seed=3)
+    info = eng.info
+    eng.generate([ve.prompt(1 + rank, 49152, PROMPT_LEN)], DECODE_STEPS)
+    steps = args.steps
+    dev_ms, _ = device_steps(eng, 1, steps, args.warmup, world, False, local)
+    eng.close()
+    positions = [PROMPT_LEN + (i % DECODE_STEPS) for i in range(DECODE_STEPS)]
+    sbytes = step_bytes(info, 1, positions)
+    step_ms = dev_ms / steps
+    achieved = sbytes / (step_ms * 1e-3) / 1e9
+    peak, _ = peaks()
+    return {"value": world * steps / (dev_ms * 1e-3), "unit": "tok/s", "steps": steps, "ms_per_step": step_ms,
+            "weights": "int8 per-tensor (q/k/v/o/gate/up/down), fp16 embedding and lm_head",
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "bytes_per_step": sbytes}}
+
+
 def run_ours(args, world, rank, local):
     import ctypes as C
 
@@ -525,6 +551,8 @@ def run_ours(args, world, rank, local):
     eng.close()
     if B == 1 and args.bs64_steps > 0 and not args.quick:
         line["bs64"] = measure_bs64(args, world, rank, local, mp)
+    if B == 1 and args.int8 and not args.quick:
+        line["int8"] = measure_int8(args, world, rank, local)
     if rank == 0:
         print(json.dumps(line), flush=True)
 
@@ -1042,6 +1070,9 @@ def main():
     ap.add_argument("--bs64-steps", type=int, default=256,
                     help="decode at --batch 1: also time this many bs64 steps (the metric's second "
                          "batch size) and report them under \"bs64\"; 0 skips")
+    ap.add_argument("--int8", type=int, default=1,
+                    help="decode at --batch 1: also time the int8 (GEMV_Quant) config-0 model and report it "
+                         "under \"int8\"; 0 skips")
     ap.add_argument("--seqs", type=int, default=512, help="cfg4: total sequences over all ranks")
     ap.add_argument("--wave", type=int, default=128, help="cfg4: sequences per GPU per wave")
     ap.add_argument("--attn-b", type=int, default=0, help="attn: only this batch size (1, 8 or 64)")

@@ -307,11 +307,14 @@ opure_status opure_step_end(opure_ctx *ctx, const opure_step_io *io);
  * Requirements: head_dim 64 or 128, n_heads/n_kv <= 4, hidden % 8 == 0, nvec <= 8. */
 typedef struct opure_fused_layer {
     const uint16_t *in_norm, *post_norm; /* fp16 [hidden]                                  */
-    const uint16_t *w_qkv;      /* fp16 [(n_heads + 2 n_kv) head_dim][hidden]: q, k, v rows */
-    const uint16_t *w_o_blk;    /* fp16 [n_kv][hidden][G head_dim]: (g, o, c) = Wo[o][g G hd + c] */
-    const uint16_t *w_gate_up;  /* fp16 [2 inter][hidden]: gate rows then up rows          */
-    const uint16_t *w_down_t;   /* fp16 [inter][hidden]: down_proj transposed              */
+    const uint16_t *w_qkv;      /* [(n_heads + 2 n_kv) head_dim][hidden]: q, k, v rows     */
+    const uint16_t *w_o_blk;    /* [n_kv][hidden][G head_dim]: (g, o, c) = Wo[o][g G hd + c] */
+    const uint16_t *w_gate_up;  /* [2 inter][hidden]: gate rows then up rows               */
+    const uint16_t *w_down_t;   /* [inter][hidden]: down_proj transposed                   */
     uint16_t *kv_pool;          /* this layer's page pool (layout of opure_kv_layout)      */
+    /* Per-tensor scales of int8 matrices (opure_fused_step.w_dtype = OPURE_W_Q8; the
+     * matrices above then hold int8 in the same layouts): y = scale * sum(q * x). */
+    float s_q, s_k, s_v, s_o, s_gate, s_up, s_down;
 } opure_fused_layer;
 
 typedef struct opure_fused_step {
@@ -339,6 +342,11 @@ typedef struct opure_fused_step {
                                           barrier k; row 3 n_layers: [1] = kernel start; row
                                           3 n_layers + 1: [0] = end), rewritten every step */
     uint32_t kv_ring;                  /* sliding window of the cache (opure_kv_layout.ring) */
+    uint32_t w_dtype;                  /* layer matrices: OPURE_W_F16 (0) or OPURE_W_Q8 (int8
+                                          GEMV_Quant, persistent kernel only: head_dim 64,
+                                          hidden a multiple of 16, mode AUTO; otherwise
+                                          OPURE_ERR_UNSUPPORTED). Embedding, norms and the
+                                          lm_head are fp16 either way. */
 } opure_fused_step;
 /* AUTO: when the model fits (head_dim 64, <= 48 layers, each phase's work in one wave of
  * CTAs, a layer's weight slices of one CTA double-buffered in shared memory) and `sync` is

@@ -186,6 +186,10 @@ typedef struct opure_spec_options {
     uint32_t k;               /* draft tokens per round (1..64)                         */
     uint32_t mode;            /* OPURE_SPEC_GREEDY or OPURE_SPEC_REJECTION (temperature 1) */
     uint64_t seed;            /* sequence s draws uniforms from Rng(seed ^ s * 0x9E3779B97F4A7C15) */
+    int32_t *draft_log;       /* NULL, or [draft_log_rounds][n_seq][k]: each round's drafted
+                                 tokens d_1..d_k per sequence (-1 for a finished sequence;
+                                 rounds past the last are filled with -2)               */
+    uint32_t draft_log_rounds;
 } opure_spec_options;
 
 typedef struct opure_spec_stats {

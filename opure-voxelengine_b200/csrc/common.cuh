@@ -89,6 +89,12 @@ __device__ __forceinline__ float lds_h(const __half *p) {
     return __half2float(__ushort_as_half(r));
 }
 
+__device__ __forceinline__ float lds_s8(const void *p) {
+    int r;
+    asm volatile("ld.shared.s8 %0, [%1];" : "=r"(r) : "r"(shared_addr(p)));
+    return float(r);
+}
+
 __device__ __forceinline__ float2 h2f2(uint32_t u) {
     __half2 h = *reinterpret_cast<__half2 *>(&u);
     return __half22float2(h);

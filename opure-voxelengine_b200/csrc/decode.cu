@@ -214,69 +214,49 @@ __device__ __forceinline__ void stage_residual_fast(const float *base, const lon
     __syncthreads();
 }
 
-// Dot products of R rows held in shared memory (row r at w + r * pitch bytes) with NV
-// vectors xs[v * h + i]; lanes stride the row's 16-byte chunks. Every lane gets the sums.
-template <int NV, int R>
-__device__ __forceinline__ void smem_dot(const uint8_t *w, uint32_t pitch, uint32_t nrows, uint32_t nchunks,
-                                         const float *xs, uint32_t h, float (&acc)[R][NV]) {
-    const uint32_t lane = threadIdx.x & 31u;
-#pragma unroll
-    for (int r = 0; r < R; ++r)
-#pragma unroll
-        for (int v = 0; v < NV; ++v) acc[r][v] = 0.f;
-    for (uint32_t c = lane; c < nchunks; c += 32) {
-        float xf[NV][8];
-#pragma unroll
-        for (int v = 0; v < NV; ++v) {
-            const float4 a = lds_f4(xs + v * h + c * 8);
-            const float4 b = lds_f4(xs + v * h + c * 8 + 4);
-            xf[v][0] = a.x; xf[v][1] = a.y; xf[v][2] = a.z; xf[v][3] = a.w;
-            xf[v][4] = b.x; xf[v][5] = b.y; xf[v][6] = b.z; xf[v][7] = b.w;
-        }
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-            if (r >= int(nrows)) break;
-            float wf[8];
-            unpack8(lds128(w + size_t(r) * pitch + c * 16), wf);
-#pragma unroll
-            for (int v = 0; v < NV; ++v)
-#pragma unroll
-                for (int e = 0; e < 8; ++e) acc[r][v] = fmaf(wf[e], xf[v][e], acc[r][v]);
-        }
+// One 16-byte chunk of a weight row as fp32: 8 fp16, or (Q8) 16 int8 in the reference's
+// little-endian packing (Opure_GEMV_Quant.usf:52-93), unscaled.
+template <bool Q8>
+struct RowChunk {
+    static constexpr int E = Q8 ? 16 : 8;
+    __device__ __forceinline__ static void unpack(const uint4 &w, float *f) {
+        if constexpr (Q8)
+            unpack16_i8(w, f);
+        else
+            unpack8(w, f);
     }
-#pragma unroll
-    for (int r = 0; r < R; ++r)
-#pragma unroll
-        for (int v = 0; v < NV; ++v) acc[r][v] = warp_sum(acc[r][v]);
-}
+};
 
-// smem_dot over R rows at arbitrary shared-memory addresses rows[r], r < nrows.
-template <int NV, int R>
+// Dot products of R rows held in shared memory (row r at rows[r]; rows >= nrows skipped)
+// with NV vectors xs[v * h + i]; lanes stride the rows' 16-byte chunks (nchunks of them).
+// Every lane gets the sums. Q8 rows are int8: the caller applies the tensor's scale.
+template <int NV, int R, bool Q8 = false>
 __device__ __forceinline__ void smem_dot_ptrs(const uint8_t *const (&rows)[R], uint32_t nrows, uint32_t nchunks,
                                               const float *xs, uint32_t h, float (&acc)[R][NV]) {
+    constexpr int E = RowChunk<Q8>::E;
     const uint32_t lane = threadIdx.x & 31u;
 #pragma unroll
     for (int r = 0; r < R; ++r)
 #pragma unroll
         for (int v = 0; v < NV; ++v) acc[r][v] = 0.f;
     for (uint32_t c = lane; c < nchunks; c += 32) {
-        float xf[NV][8];
+        float xf[NV][E];
 #pragma unroll
-        for (int v = 0; v < NV; ++v) {
-            const float4 a = lds_f4(xs + v * h + c * 8);
-            const float4 b = lds_f4(xs + v * h + c * 8 + 4);
-            xf[v][0] = a.x; xf[v][1] = a.y; xf[v][2] = a.z; xf[v][3] = a.w;
-            xf[v][4] = b.x; xf[v][5] = b.y; xf[v][6] = b.z; xf[v][7] = b.w;
-        }
+        for (int v = 0; v < NV; ++v)
+#pragma unroll
+            for (int q = 0; q < E / 4; ++q) {
+                const float4 a = lds_f4(xs + v * h + c * E + 4 * q);
+                xf[v][4 * q] = a.x; xf[v][4 * q + 1] = a.y; xf[v][4 * q + 2] = a.z; xf[v][4 * q + 3] = a.w;
+            }
 #pragma unroll
         for (int r = 0; r < R; ++r) {
             if (r >= int(nrows)) break;
-            float wf[8];
-            unpack8(lds128(rows[r] + c * 16), wf);
+            float wf[E];
+            RowChunk<Q8>::unpack(lds128(rows[r] + c * 16), wf);
 #pragma unroll
             for (int v = 0; v < NV; ++v)
 #pragma unroll
-                for (int e = 0; e < 8; ++e) acc[r][v] = fmaf(wf[e], xf[v][e], acc[r][v]);
+                for (int e = 0; e < E; ++e) acc[r][v] = fmaf(wf[e], xf[v][e], acc[r][v]);
         }
     }
 #pragma unroll
@@ -285,6 +265,16 @@ __device__ __forceinline__ void smem_dot_ptrs(const uint8_t *const (&rows)[R], u
 #pragma unroll
         for (int v = 0; v < NV; ++v) acc[r][v] = warp_sum(acc[r][v]);
     }
+}
+
+// smem_dot_ptrs over R consecutive rows, row r at w + r * pitch bytes.
+template <int NV, int R, bool Q8 = false>
+__device__ __forceinline__ void smem_dot(const uint8_t *w, uint32_t pitch, uint32_t nrows, uint32_t nchunks,
+                                         const float *xs, uint32_t h, float (&acc)[R][NV]) {
+    const uint8_t *rows[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) rows[r] = w + size_t(r) * pitch;
+    smem_dot_ptrs<NV, R, Q8>(rows, nrows, nchunks, xs, h, acc);
 }
 
 // Element offset of (seq, pos, K|V, kv head) row inside a layer's pool, or -1 (reported).
@@ -674,6 +664,7 @@ struct PLayer {
     const uint8_t *w_qkv, *w_o_blk, *w_gu, *w_down_t;
     const __half *in_norm, *post_norm;
     uint16_t *kv_pool;
+    float s_q, s_k, s_v, s_o, s_gate, s_up, s_down;  // int8 tensor scales (1 for fp16)
 };
 
 struct PersistArgs {
@@ -781,18 +772,19 @@ __device__ __forceinline__ PShare p_share(const PersistArgs &p) {
     return s;
 }
 
-template <int HD, int G>
+// EB: bytes per weight element (2 fp16, 1 int8).
+template <int HD, int G, uint32_t EB>
 __device__ __forceinline__ uint32_t p_bytes(const PersistArgs &p, const PShare &s) {
-    return s.na * p.h * 2 + s.nb * G * HD * 2 + 3 * s.nc * p.h * 2;
+    return (s.na * p.h + s.nb * G * HD + 3 * s.nc * p.h) * EB;
 }
 
 // Thread 0: copy layer L's slices of this CTA into `slot`, completing on `bar`.
-template <int HD, int G>
+template <int HD, int G, uint32_t EB>
 __device__ void p_issue(const PersistArgs &p, const PShare &s, uint32_t L, uint8_t *slot, uint64_t *bar) {
-    const uint32_t bytes = p_bytes<HD, G>(p, s);
+    const uint32_t bytes = p_bytes<HD, G, EB>(p, s);
     if (!bytes) return;
     const PLayer &ly = p.layers[L];
-    const uint32_t pitch = p.h * 2, bpitch = G * HD * 2;
+    const uint32_t pitch = p.h * EB, bpitch = G * HD * EB;
     // The slot was last read through the generic proxy; order that before the async writes.
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     mbar_expect_tx(bar, bytes);
@@ -972,8 +964,12 @@ __device__ __forceinline__ void attend_two_pass(const float *q, float scale_log2
     __syncthreads();
 }
 
-template <int NV, int HD, int G>
+// Q8: the layer matrices are per-tensor int8 (GEMV_Quant, Opure_GEMV_Quant.usf:38-94): half
+// the bytes per slice, each dot product scaled by its tensor's scale; the embedding, norms
+// and lm_head stay fp16.
+template <int NV, int HD, int G, bool Q8 = false>
 __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __grid_constant__ PersistArgs p) {
+    constexpr uint32_t EB = Q8 ? 1u : 2u;  // bytes per layer-weight element
     extern __shared__ __align__(1024) uint8_t psm[];
     __shared__ __align__(8) uint64_t full[2];
     __shared__ __align__(8) uint64_t lbar[kLmBufs];
@@ -986,8 +982,9 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
     __shared__ int32_t s_seq[NV], s_pos[NV];
     __shared__ int32_t s_pt[NV][kPtStageP];
     __shared__ unsigned long long cta_best[kPWarps][NV];
-    constexpr uint32_t cols_b = G * HD, bpitch = cols_b * 2;
-    const uint32_t pitch = p.h * 2;
+    constexpr uint32_t cols_b = G * HD, bpitch = cols_b * EB;
+    const uint32_t pitch = p.h * 2;      // lm_head rows (fp16)
+    const uint32_t wpitch = p.h * EB;    // layer-weight rows of h elements
     uint8_t *slots[2] = {psm, psm + p.slot_bytes};
     float *xs = reinterpret_cast<float *>(psm + p.region_bytes);
     float *red = xs + NV * p.h;
@@ -996,7 +993,7 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
     float *gu = attn + NV * G * HD;             // [2F][NV] gate then up sums
     const uint32_t b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const PShare sh = p_share<HD, G>(p);
-    const bool has_bytes = p_bytes<HD, G>(p, sh) != 0;
+    const bool has_bytes = p_bytes<HD, G, EB>(p, sh) != 0;
     const bool stage_pt = p.max_pages <= kPtStageP;
     const uint32_t qrows = p.n_heads * HD, krows = p.n_kv * HD;
 
@@ -1078,7 +1075,7 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
     unsigned long long *trow = p.trace ? p.trace + size_t(blockIdx.x) * (3 * p.n_layers + 2) * 2 : nullptr;
     if (threadIdx.x == 0 && trow) trow[3 * p.n_layers * 2 + 1] = global_ns();
     if (threadIdx.x == 0) {
-        for (uint32_t L = 0; L < 2 && L < p.n_layers; ++L) p_issue<HD, G>(p, sh, L, slots[L], &full[L]);
+        for (uint32_t L = 0; L < 2 && L < p.n_layers; ++L) p_issue<HD, G, EB>(p, sh, L, slots[L], &full[L]);
     }
     issued = min(2u, p.n_layers);
     __syncthreads();
@@ -1161,16 +1158,18 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
                                    b == 0 ? p.base1 : nullptr, b == 0 ? p.delta0 : nullptr, b == 0);
             if (2 * warp < sh.na) {
                 float acc[2][NV];
-                smem_dot<NV, 2>(sl + size_t(2 * warp) * pitch, pitch, min(2u, sh.na - 2 * warp), pitch / 16, xs,
-                                p.h, acc);
+                smem_dot<NV, 2, Q8>(sl + size_t(2 * warp) * wpitch, wpitch, min(2u, sh.na - 2 * warp), wpitch / 16,
+                                    xs, p.h, acc);
                 if (a_epi) {
                     const uint32_t v = lane, r = a_r;
+                    // A RoPE pair never straddles the q | k | v boundaries (multiples of HD).
+                    const float sc = !Q8 ? 1.0f : (r < qrows ? ly.s_q : (r < qrows + krows ? ly.s_k : ly.s_v));
                     float e0 = 0.f, e1 = 0.f;
 #pragma unroll
                     for (int k = 0; k < NV; ++k)
                         if (k == int(v)) {
-                            e0 = acc[0][k];
-                            e1 = acc[1][k];
+                            e0 = acc[0][k] * sc;
+                            e1 = acc[1][k] * sc;
                         }
                     __half *slot = a_kv >= 0 ? reinterpret_cast<__half *>(ly.kv_pool) + a_kv : nullptr;
                     if (r < qrows + krows) {
@@ -1259,21 +1258,24 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
                 float acc[2][NV];
 #pragma unroll
                 for (int v = 0; v < NV; ++v) acc[0][v] = acc[1][v] = 0.f;
+                constexpr int E = RowChunk<Q8>::E;
                 for (uint32_t c = lane; c < nch; c += 32) {
-                    float wf[2][8];
-                    unpack8(lds128(wsm + size_t(rr) * bpitch + c * 16), wf[0]);
-                    if (two)
-                        unpack8(lds128(wsm + size_t(rr + kPWarps) * bpitch + c * 16), wf[1]);
+                    float wf[2][E];
+                    RowChunk<Q8>::unpack(lds128(wsm + size_t(rr) * bpitch + c * 16), wf[0]);
+                    if (two) RowChunk<Q8>::unpack(lds128(wsm + size_t(rr + kPWarps) * bpitch + c * 16), wf[1]);
 #pragma unroll
                     for (int v = 0; v < NV; ++v) {
-                        const float4 a0 = lds_f4(attn + v * cols_b + c * 8);
-                        const float4 a1 = lds_f4(attn + v * cols_b + c * 8 + 4);
-                        const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                        float av[E];
 #pragma unroll
-                        for (int e = 0; e < 8; ++e) acc[0][v] = fmaf(wf[0][e], av[e], acc[0][v]);
+                        for (int q = 0; q < E / 4; ++q) {
+                            const float4 a = lds_f4(attn + v * cols_b + c * E + 4 * q);
+                            av[4 * q] = a.x; av[4 * q + 1] = a.y; av[4 * q + 2] = a.z; av[4 * q + 3] = a.w;
+                        }
+#pragma unroll
+                        for (int e = 0; e < E; ++e) acc[0][v] = fmaf(wf[0][e], av[e], acc[0][v]);
                         if (two)
 #pragma unroll
-                            for (int e = 0; e < 8; ++e) acc[1][v] = fmaf(wf[1][e], av[e], acc[1][v]);
+                            for (int e = 0; e < E; ++e) acc[1][v] = fmaf(wf[1][e], av[e], acc[1][v]);
                     }
                 }
 #pragma unroll
@@ -1281,7 +1283,7 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
                     if (r == 1 && !two) break;
 #pragma unroll
                     for (int v = 0; v < NV; ++v) {
-                        const float t = warp_sum(acc[r][v]);
+                        const float t = warp_sum(acc[r][v]) * (Q8 ? ly.s_o : 1.0f);
                         if (lane == uint32_t(v))
                             atomicAdd(reinterpret_cast<unsigned long long *>(p.delta0 + size_t(v) * p.h + sh.b_row0 +
                                                                              rr + r * kPWarps),
@@ -1310,7 +1312,7 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
             else
                 stage_residual<NV>(p.base1, p.delta0, p.h, gpre, ly.post_norm, p.eps, xs, red,
                                    b == 0 ? p.base0 : nullptr, nullptr, b == 0);
-            const uint8_t *wg = sl + p.off_c, *wd = wg + 2 * p.F * pitch;
+            const uint8_t *wg = sl + p.off_c, *wd = wg + 2 * p.F * wpitch;
             // The 2 nc dot products (gate rows f, then up rows f), three rows per warp and
             // pass; SwiGLU once every warp's sums are in shared memory.
             const uint32_t ngu = 2 * sh.nc;
@@ -1320,17 +1322,20 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
 #pragma unroll
                 for (int i = 0; i < 3; ++i) {
                     const uint32_t j = j0 + i * kPWarps;
-                    rows[i] = wg + size_t(j < sh.nc ? j : p.F + (j - sh.nc)) * pitch;
+                    rows[i] = wg + size_t(j < sh.nc ? j : p.F + (j - sh.nc)) * wpitch;
                     if (j < ngu) nr = i + 1;
                 }
                 float acc[3][NV];
-                smem_dot_ptrs<NV, 3>(rows, nr, pitch / 16, xs, p.h, acc);
+                smem_dot_ptrs<NV, 3, Q8>(rows, nr, wpitch / 16, xs, p.h, acc);
                 if (lane == 0)
 #pragma unroll
                     for (int i = 0; i < 3; ++i)
-                        if (i < int(nr))
+                        if (i < int(nr)) {
+                            const uint32_t j = j0 + i * kPWarps;
+                            const float sc = !Q8 ? 1.0f : (j < sh.nc ? ly.s_gate : ly.s_up);
 #pragma unroll
-                            for (int v = 0; v < NV; ++v) gu[(j0 + i * kPWarps) * NV + v] = acc[i][v];
+                            for (int v = 0; v < NV; ++v) gu[j * NV + v] = acc[i][v] * sc;
+                        }
             }
             __syncthreads();
             for (uint32_t i = threadIdx.x; i < sh.nc * NV; i += blockDim.x) {
@@ -1346,14 +1351,14 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
 #pragma unroll
                 for (int v = 0; v < NV; ++v) acc[v] = 0.f;
                 for (uint32_t f = 0; f < sh.nc; ++f) {
-                    const float wv = lds_h(wdh + size_t(f) * p.h + o);
+                    const float wv = Q8 ? lds_s8(wd + size_t(f) * p.h + o) : lds_h(wdh + size_t(f) * p.h + o);
 #pragma unroll
                     for (int v = 0; v < NV; ++v) acc[v] = fmaf(wv, lds_f32(hs + f * NV + v), acc[v]);
                 }
 #pragma unroll
                 for (int v = 0; v < NV; ++v)
                     atomicAdd(reinterpret_cast<unsigned long long *>(p.delta1 + size_t(v) * p.h + o),
-                              static_cast<unsigned long long>(to_fix(acc[v])));
+                              static_cast<unsigned long long>(to_fix(acc[v] * (Q8 ? ly.s_down : 1.0f))));
             }
         }
         if (L + 1 == p.n_layers) {
@@ -1364,7 +1369,7 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
             // Arrived: this slot's layer is done; thread 0 starts copying layer L+2 into it.
             const bool refill = L + 2 < p.n_layers;
             const bool ok = grid_barrier(p, 3 * L + 2, &s_ok, [&] {
-                if (refill) p_issue<HD, G>(p, sh, L + 2, sl, &full[L & 1]);
+                if (refill) p_issue<HD, G, EB>(p, sh, L + 2, sl, &full[L & 1]);
             });
             issued += refill ? 1u : 0u;
             if (!ok) goto abort;
@@ -1501,7 +1506,7 @@ opure_status run_step(opure_ctx *ctx, const opure_fused_step &s) {
 // The persistent kernel when this model and batch fit it: every phase's work in one wave
 // of CTAs (one per SM) and a layer's slices of one CTA, double-buffered, in shared memory.
 // Sets *ran; returns an error only for a failed launch.
-template <int NV, int HD, int G>
+template <int NV, int HD, int G, bool Q8>
 opure_status run_persistent(opure_ctx *ctx, const opure_fused_step &s, bool *ran) {
     *ran = false;
     if (!s.sync || s.n_layers > kPMaxLayers || s.head_dim != HD) return OPURE_OK;
@@ -1516,14 +1521,15 @@ opure_status run_persistent(opure_ctx *ctx, const opure_fused_step &s, bool *ran
     p.F = (s.inter + grid - 1) / grid;
     p.c_ctas = (s.inter + p.F - 1) / p.F;
     if (p.a_ctas > grid || s.n_kv * p.rbs > grid || p.c_ctas > grid) return OPURE_OK;
-    const uint32_t pitch = h * 2;
-    p.off_b = (kARows * pitch + 127) & ~127u;
-    p.off_c = (p.off_b + p.rows_b * G * HD * 2 + 127) & ~127u;
-    p.slot_bytes = (p.off_c + 3 * p.F * pitch + 1023) & ~1023u;
+    const uint32_t pitch = h * 2;                 // lm_head rows (fp16)
+    const uint32_t eb = Q8 ? 1u : 2u, wpitch = h * eb;  // layer-weight rows
+    p.off_b = (kARows * wpitch + 127) & ~127u;
+    p.off_c = (p.off_b + p.rows_b * G * HD * eb + 127) & ~127u;
+    p.slot_bytes = (p.off_c + 3 * p.F * wpitch + 1023) & ~1023u;
     const size_t scratch =
         (size_t(NV) * h + ((33 * NV + 3) & ~3u) + ((p.F * NV + 3) & ~3u) + size_t(NV) * G * HD + 2 * size_t(p.F) * NV) *
         4;
-    auto kern = persistent_step_kernel<NV, HD, G>;
+    auto kern = persistent_step_kernel<NV, HD, G, Q8>;
     cudaFuncAttributes fa{};
     if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return OPURE_ERR_CUDA;
     // Shared memory left for the slots / lm_head chunk buffers beside the scratch.
@@ -1585,7 +1591,7 @@ opure_status run_persistent(opure_ctx *ctx, const opure_fused_step &s, bool *ran
                              reinterpret_cast<const uint8_t *>(l.w_gate_up),
                              reinterpret_cast<const uint8_t *>(l.w_down_t),
                              reinterpret_cast<const __half *>(l.in_norm), reinterpret_cast<const __half *>(l.post_norm),
-                             l.kv_pool};
+                             l.kv_pool, l.s_q, l.s_k, l.s_v, l.s_o, l.s_gate, l.s_up, l.s_down};
     }
     // Barrier counters and the abort flag start at zero (a memset node under capture).
     if (cudaMemsetAsync(s.sync, 0, (3 * size_t(s.n_layers) + 1) * 4, ctx->stream) != cudaSuccess)
@@ -1611,15 +1617,28 @@ opure_status pick_g(opure_ctx *ctx, const opure_fused_step &s, uint32_t G) {
     if constexpr (HD == 64) {
         bool ran = false;
         opure_status st = OPURE_OK;
+        if (s.w_dtype == OPURE_W_Q8) {
+            // int8 layer weights run on the persistent kernel only.
+            if (s.mode != OPURE_FUSED_AUTO) return OPURE_ERR_UNSUPPORTED;
+            switch (G) {
+                case 1: st = run_persistent<NV, HD, 1, true>(ctx, s, &ran); break;
+                case 2: st = run_persistent<NV, HD, 2, true>(ctx, s, &ran); break;
+                case 3: st = run_persistent<NV, HD, 3, true>(ctx, s, &ran); break;
+                case 4: st = run_persistent<NV, HD, 4, true>(ctx, s, &ran); break;
+            }
+            return st ? st : (ran ? OPURE_OK : OPURE_ERR_UNSUPPORTED);
+        }
         if (s.mode == OPURE_FUSED_AUTO) {
             switch (G) {
-                case 1: st = run_persistent<NV, HD, 1>(ctx, s, &ran); break;
-                case 2: st = run_persistent<NV, HD, 2>(ctx, s, &ran); break;
-                case 3: st = run_persistent<NV, HD, 3>(ctx, s, &ran); break;
-                case 4: st = run_persistent<NV, HD, 4>(ctx, s, &ran); break;
+                case 1: st = run_persistent<NV, HD, 1, false>(ctx, s, &ran); break;
+                case 2: st = run_persistent<NV, HD, 2, false>(ctx, s, &ran); break;
+                case 3: st = run_persistent<NV, HD, 3, false>(ctx, s, &ran); break;
+                case 4: st = run_persistent<NV, HD, 4, false>(ctx, s, &ran); break;
             }
             if (st || ran) return st;
         }
+    } else {
+        if (s.w_dtype == OPURE_W_Q8) return OPURE_ERR_UNSUPPORTED;
     }
     switch (G) {
         case 1: return run_step<NV, HD, 1>(ctx, s);
@@ -1650,6 +1669,9 @@ extern "C" opure_status opure_decode_fused(opure_ctx *ctx, const opure_fused_ste
         return OPURE_ERR_INVALID_ARG;
     if (s->n_heads % s->n_kv || s->hidden % 8 || s->inter == 0 || s->kv_ring > s->max_pages)
         return OPURE_ERR_INVALID_ARG;
+    if (s->w_dtype != OPURE_W_F16 && s->w_dtype != OPURE_W_Q8) return OPURE_ERR_INVALID_ARG;
+    if (s->w_dtype == OPURE_W_Q8 && (s->hidden % 16 || (s->n_heads / s->n_kv * s->head_dim) % 16))
+        return OPURE_ERR_UNSUPPORTED;  // whole 16-byte chunks of int8 per row
     if (s->nvec == 0) return OPURE_OK;
     const uint32_t G = s->n_heads / s->n_kv;
     for (uint32_t L = 0; L < s->n_layers; ++L) {

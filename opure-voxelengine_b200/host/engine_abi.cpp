@@ -157,8 +157,15 @@ opure_status opure_engine_spec_generate(opure_engine *target, opure_engine *draf
         so.seed = o->seed;
         so.maxNew = budget;
         opure::engine::SpecStats st;
-        std::vector<int32_t> log;
-        const auto res = opure::engine::SpecGenerate(target->eng, draft->eng, ps, so, &st, accept_log ? &log : nullptr);
+        std::vector<int32_t> log, dlog;
+        const auto res = opure::engine::SpecGenerate(target->eng, draft->eng, ps, so, &st, accept_log ? &log : nullptr,
+                                                     o->draft_log ? &dlog : nullptr);
+        if (o->draft_log) {
+            const size_t cap = size_t(o->draft_log_rounds) * n_seq * o->k;
+            const size_t m = std::min(dlog.size(), cap);
+            std::copy_n(dlog.begin(), m, o->draft_log);
+            std::fill(o->draft_log + m, o->draft_log + cap, -2);
+        }
         for (uint32_t s = 0; s < n_seq; ++s)
             for (uint32_t i = 0; i < budget; ++i) out_tokens[size_t(s) * budget + i] = int32_t(res[s][i]);
         if (accept_log) {

@@ -49,7 +49,7 @@ double Elapsed(opure_event *a, opure_event *b) {
 std::vector<std::vector<uint32_t>> SpecGenerate(VoxelEngine &target, VoxelEngine &draft,
                                                 const std::vector<std::vector<uint32_t>> &prompts,
                                                 const SpecOptions &o, SpecStats *stats,
-                                                std::vector<int32_t> *acceptLog) {
+                                                std::vector<int32_t> *acceptLog, std::vector<int32_t> *draftLog) {
     OPURE_CHECK(target.IsReady() && draft.IsReady(), "engine used before Initialize");
     // A rolled-back position may need a page its ring has already recycled.
     OPURE_CHECK(!target.Options().kvWindow && !draft.Options().kvWindow,
@@ -111,7 +111,7 @@ std::vector<std::vector<uint32_t>> SpecGenerate(VoxelEngine &target, VoxelEngine
     auto done = [&](uint32_t s) { return out[s].size() >= o.maxNew; };
 
     std::vector<int32_t> pos(n), known(n), seqv(size_t(n) * (k + 1)), posv(size_t(n) * (k + 1));
-    std::vector<int32_t> hOut(size_t(n) * (k + 1)), hAcc(n);
+    std::vector<int32_t> hOut(size_t(n) * (k + 1)), hAcc(n), hDraft(size_t(n) * k);
     std::vector<float> ud(size_t(k) * n), ua(size_t(n) * k), uf(n);
     SpecStats st;
     while (true) {
@@ -180,6 +180,7 @@ std::vector<std::vector<uint32_t>> SpecGenerate(VoxelEngine &target, VoxelEngine
         OPURE_CUDA_CHECK(opure_event_record(ctx, ev[2]));
         OPURE_CUDA_CHECK(opure_d2h(ctx, hOut.data(), dOut, hOut.size() * 4));
         OPURE_CUDA_CHECK(opure_d2h(ctx, hAcc.data(), dAcc, n * 4));
+        if (draftLog) OPURE_CUDA_CHECK(opure_d2h(ctx, hDraft.data(), dDraft, hDraft.size() * 4));
         OPURE_CUDA_CHECK(opure_sync(ctx, 60000));
         CheckDevice(ctx);
         st.draftMs += Elapsed(ev[0], ev[1]);
@@ -187,6 +188,8 @@ std::vector<std::vector<uint32_t>> SpecGenerate(VoxelEngine &target, VoxelEngine
         ++st.rounds;
 
         for (uint32_t s = 0; s < n; ++s) {
+            if (draftLog)
+                for (uint32_t j = 0; j < k; ++j) draftLog->push_back(done(s) ? -1 : hDraft[size_t(s) * k + j]);
             if (done(s)) {
                 if (acceptLog) acceptLog->push_back(-1);
                 continue;  // finished sequences keep their position: no KV growth

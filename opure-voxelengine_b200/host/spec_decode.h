@@ -51,10 +51,13 @@ struct SpecStats {
 // mode: a draw from its softmax with the sequence's first uniform). Uniform draws per
 // sequence and round are always u_draft[k], u_accept[k], u_final, in that order.
 // acceptLog, when given, receives per round n entries: the accepted count of each
-// sequence, or -1 once that sequence has all its tokens.
+// sequence, or -1 once that sequence has all its tokens. draftLog, when given, receives
+// per round n * k entries: the drafted tokens d_1..d_k of each sequence (-1 once it has
+// all its tokens).
 std::vector<std::vector<uint32_t>> SpecGenerate(VoxelEngine &target, VoxelEngine &draft,
                                                 const std::vector<std::vector<uint32_t>> &prompts,
                                                 const SpecOptions &o, SpecStats *stats = nullptr,
-                                                std::vector<int32_t> *acceptLog = nullptr);
+                                                std::vector<int32_t> *acceptLog = nullptr,
+                                                std::vector<int32_t> *draftLog = nullptr);
 
 }  // namespace opure::engine

@@ -123,19 +123,19 @@ void WeightStreamer::ParseHeader(const uint8_t *header, uint64_t len) {
         }
         const json::Value &off = v.At("data_offsets", name);
         OPURE_CHECK(off.IsArray() && off.arr.size() == 2,
-                    "tensor '" + name + "' must have exactly two data_offsets");
+                    "data_offsets of '" + name + "' is not a [begin, end] pair");
         const uint64_t b = uint64_t(off.arr[0].inum), e = uint64_t(off.arr[1].inum);
-        OPURE_CHECK(b <= e, "tensor '" + name + "' has data_offsets out of order");
-        OPURE_CHECK(e <= payloadBytes_, "tensor '" + name + "' runs past the end of the payload");
+        OPURE_CHECK(b <= e, "data_offsets of '" + name + "' end before they begin");
+        OPURE_CHECK(e <= payloadBytes_, "bytes of '" + name + "' extend beyond the file's data section");
         const uint64_t expect = StorageBytes(t.dtype, t.ElementCount());
-        OPURE_CHECK(e - b == expect, "tensor '" + name + "' declares " + std::to_string(e - b) +
-                                         " bytes but its shape and " + DtypeName(t.dtype) +
-                                         " dtype imply " + std::to_string(expect));
+        OPURE_CHECK(e - b == expect, "'" + name + "' spans " + std::to_string(e - b) + " bytes, but " +
+                                         std::to_string(t.ElementCount()) + " elements of " + DtypeName(t.dtype) +
+                                         " take " + std::to_string(expect));
         t.byteBegin = payloadBegin_ + b;
         t.byteEnd = payloadBegin_ + e;
         tensors_.push_back(std::move(t));
     }
-    OPURE_CHECK(!tensors_.empty(), "safetensors header declares no tensors");
+    OPURE_CHECK(!tensors_.empty(), "the safetensors header lists no tensor");
 }
 
 const Tensor *WeightStreamer::TryFind(std::string_view name) const {

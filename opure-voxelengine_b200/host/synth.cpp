@@ -28,6 +28,52 @@ double Normal::Next() {
     return r * std::cos(a);
 }
 
+namespace {
+// Runs fn(i) for i in [0, n) on the host's threads, in contiguous chunks of at least
+// `grain` indices.
+template <class F>
+void ParallelChunks(uint64_t n, uint64_t grain, F &&fn) {
+    const uint64_t nt = std::min<uint64_t>(std::max(1u, std::thread::hardware_concurrency()), (n + grain - 1) / grain);
+    if (nt <= 1) {
+        for (uint64_t i = 0; i < n; ++i) fn(i);
+        return;
+    }
+    std::vector<std::thread> ts;
+    for (uint64_t t = 0; t < nt; ++t)
+        ts.emplace_back([&, t] {
+            for (uint64_t i = n * t / nt; i < n * (t + 1) / nt; ++i) fn(i);
+        });
+    for (auto &th : ts) th.join();
+}
+}  // namespace
+
+void Normal::Fill(uint64_t n, double scale, float *out) {
+    uint64_t i = 0;
+    if (has_ && n) {  // the spare of a pair drawn earlier comes first
+        out[i++] = float(spare_ * scale);
+        has_ = false;
+    }
+    // Whole pairs: each block's generator state is found by stepping the xorshift alone,
+    // then the blocks (the transcendentals) run on host threads.
+    constexpr uint64_t kPairs = uint64_t(1) << 16;
+    const uint64_t pairs = (n - i) / 2, blocks = (pairs + kPairs - 1) / kPairs;
+    std::vector<uint64_t> starts(blocks);
+    for (uint64_t b = 0; b < blocks; ++b) {
+        starts[b] = rng_.s;
+        const uint64_t m = std::min(kPairs, pairs - b * kPairs);
+        for (uint64_t k = 0; k < 2 * m; ++k) rng_.NextU32();
+    }
+    float *o = out + i;
+    ParallelChunks(blocks, 1, [&](uint64_t b) {
+        Normal g(1);
+        g.rng_.s = starts[b];
+        const uint64_t m = std::min(kPairs, pairs - b * kPairs);
+        for (uint64_t k = 0; k < 2 * m; ++k) o[2 * b * kPairs + k] = float(g.Next() * scale);
+    });
+    i += 2 * pairs;
+    if (i < n) out[i] = float(Next() * scale);  // an odd count leaves the pair's spare
+}
+
 std::vector<uint16_t> NormalF16(uint64_t seed, float stddev, uint64_t n) {
     // Normals come in pairs from pairs of draws, so the stream splits into blocks of whole
     // pairs: each block's generator state is found by stepping the xorshift alone, and the
@@ -152,13 +198,22 @@ void WriteModel(const std::string &dir, const ModelSpec &s) {
     Normal noise(s.noise_seed);
     std::vector<Entry> entries;
 
+    std::vector<float> draws, noises;
     auto matrix = [&](const std::string &name, uint64_t rows, uint64_t cols, bool quantizable) {
-        std::vector<uint16_t> w(rows * cols);
-        for (auto &x : w) {
-            float v = safetensors::F16ToF32(safetensors::F32ToF16(float(g.Next() * s.std)));
-            if (s.noise_std > 0.f) v = v + float(noise.Next() * s.noise_std);
-            x = safetensors::F32ToF16(v);
+        // Element i: fp16(fp16(N_i * std) + noise_i * noise_std), both streams in element order.
+        const uint64_t n = rows * cols;
+        std::vector<uint16_t> w(n);
+        draws.resize(n);
+        g.Fill(n, double(s.std), draws.data());
+        if (s.noise_std > 0.f) {
+            noises.resize(n);
+            noise.Fill(n, double(s.noise_std), noises.data());
         }
+        ParallelChunks(n, 4096, [&](uint64_t i) {
+            float v = safetensors::F16ToF32(safetensors::F32ToF16(draws[i]));
+            if (s.noise_std > 0.f) v = v + noises[i];
+            w[i] = safetensors::F32ToF16(v);
+        });
         Entry e;
         e.name = name;
         e.shape = {rows, cols};

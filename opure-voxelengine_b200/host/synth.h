@@ -31,6 +31,9 @@ class Normal {
 public:
     explicit Normal(uint64_t seed) : rng_(seed) {}
     double Next();
+    // out[i] = float(Next() * scale) for the next n normals of the stream, on host threads
+    // when n is large: the same values and the same stream state afterwards as n calls.
+    void Fill(uint64_t n, double scale, float *out);
     // Continue from a raw xorshift state (at a pair boundary of the stream).
     void SetState(uint64_t s) {
         rng_.s = s;

@@ -119,9 +119,12 @@ bool VoxelEngine::UsesFused(uint32_t n) const {
     const graph::ModelConfig &c = graph_.Config();
     const graph::VramPlan &p = graph_.Plan();
     const uint32_t hd = c.HeadDim(), G = c.KvGroupSize();
-    return opts_.path != 1 && !comm_ && p.hasFused && p.wDtype == OPURE_W_F16 && !p.lmQuantized &&
-           (hd == 64 || hd == 128) && G >= 1 && G <= 4 && (n == 1 || n == 2 || n == 4 || n == 8) &&
-           3ull * c.hiddenSize * 2 <= 160 * 1024;
+    const bool shape = !comm_ && p.hasFused && !p.lmQuantized && G >= 1 && G <= 4 &&
+                       (n == 1 || n == 2 || n == 4 || n == 8) && 3ull * c.hiddenSize * 2 <= 160 * 1024;
+    if (p.wDtype == OPURE_W_Q8)  // GEMV_Quant weights: the persistent kernel only
+        return shape && opts_.path != 1 && opts_.path != 3 && hd == 64 && c.numLayers <= 48 &&
+               c.hiddenSize % 16 == 0 && (G * hd) % 16 == 0;
+    return shape && opts_.path != 1 && (hd == 64 || hd == 128);
 }
 
 void VoxelEngine::AllocBuffers() {
@@ -335,6 +338,13 @@ void VoxelEngine::RecordStep(uint32_t n, bool logits) {
             f.w_gate_up = reinterpret_cast<const uint16_t *>(At(weights_, t.wgu));
             f.w_down_t = reinterpret_cast<const uint16_t *>(At(weights_, t.wdownT));
             f.kv_pool = kv_.Pool(L);
+            f.s_q = t.sq;
+            f.s_k = t.sk;
+            f.s_v = t.sv;
+            f.s_o = t.so;
+            f.s_gate = t.sgate;
+            f.s_up = t.sup;
+            f.s_down = t.sdown;
         }
         opure_fused_step fs{};
         fs.nvec = n;
@@ -368,6 +378,7 @@ void VoxelEngine::RecordStep(uint32_t n, bool logits) {
         fs.sync = buf_.sync;
         fs.trace = buf_.trace;
         fs.mode = opts_.path == 3 ? uint32_t(OPURE_FUSED_LAYER_KERNELS) : uint32_t(OPURE_FUSED_AUTO);
+        fs.w_dtype = plan.wDtype;
         OPURE_CUDA_CHECK(opure_decode_fused(ctx_, &fs));
         OPURE_CUDA_CHECK(opure_step_end(ctx_, &io));
         return;

@@ -43,7 +43,7 @@ class Metrics(C.Structure):
 
 
 class SpecOptions(C.Structure):
-    _fields_ = [("k", u32), ("mode", u32), ("seed", u64)]
+    _fields_ = [("k", u32), ("mode", u32), ("seed", u64), ("draft_log", P), ("draft_log_rounds", u32)]
 
 
 class SpecStats(C.Structure):
@@ -288,13 +288,15 @@ class Engine:
         return m
 
     def spec_generate(self, draft: "Engine", prompts, budget: int, k: int = 4, mode: int = SPEC_GREEDY,
-                      seed: int = 0, log_rounds: int = 0):
+                      seed: int = 0, log_rounds: int = 0, draft_log: bool = False):
         """Speculative decoding with `draft` (created with share=self). prompts: equal-length
-        sequences. Returns (tokens [n][budget], SpecStats, accept log [rounds][n] or None)."""
+        sequences. Returns (tokens [n][budget], SpecStats, accept log [rounds][n] or None), and
+        with draft_log=True also the drafted tokens [rounds][n][k] (log_rounds rounds)."""
         ps = np.ascontiguousarray(np.stack([np.asarray(p, np.int32) for p in prompts]), np.int32)
         n, plen = ps.shape
         out = np.zeros((n, budget), np.int32)
-        o = SpecOptions(k, mode, seed)
+        dlog = np.zeros((log_rounds, n, k), np.int32) if draft_log else None
+        o = SpecOptions(k, mode, seed, _p(dlog) if dlog is not None else None, log_rounds if draft_log else 0)
         st = SpecStats()
         log = np.zeros((log_rounds, n), np.int32) if log_rounds else None
         _check(lib().opure_engine_spec_generate(self.h, draft.h, _p(ps), plen, n, budget, C.byref(o),
@@ -302,6 +304,8 @@ class Engine:
                "spec_generate", self.h)
         if log is not None:
             log = log[: min(log_rounds, st.rounds)]
+        if draft_log:
+            return out, st, log, dlog[: min(log_rounds, st.rounds)]
         return out, st, log
 
     def sample_generate(self, prompts, budget: int, temperature: float = 1.0, top_k: int = 0,

@@ -898,6 +898,32 @@ struct BoxMuller {
         has = true;
         return rad * std::cos(a);
     }
+    // out[i] = float(next() * scale) for the next n draws; whole pairs run in blocks on the
+    // worker pool, each block's xorshift state found by stepping the generator alone.
+    void fill(uint64_t n, double scale, float *out) {
+        uint64_t i = 0;
+        if (has && n) {
+            out[i++] = float(spare * scale);
+            has = false;
+        }
+        constexpr uint64_t kPairs = 1 << 16;
+        const uint64_t pairs = (n - i) / 2, blocks = (pairs + kPairs - 1) / kPairs;
+        std::vector<uint64_t> starts(blocks);
+        for (uint64_t b = 0; b < blocks; ++b) {
+            starts[b] = r.s;
+            const uint64_t m = std::min(kPairs, pairs - b * kPairs);
+            for (uint64_t k = 0; k < 2 * m; ++k) r.next();
+        }
+        float *o = out + i;
+        parallel_for(int64_t(blocks), 2 * kPairs * 64, [&](int64_t b) {
+            BoxMuller g(1);
+            g.r.s = starts[size_t(b)];
+            const uint64_t m = std::min(kPairs, pairs - uint64_t(b) * kPairs);
+            for (uint64_t k = 0; k < 2 * m; ++k) o[uint64_t(b) * 2 * kPairs + k] = float(g.next() * scale);
+        });
+        i += 2 * pairs;
+        if (i < n) out[i] = float(next() * scale);
+    }
 };
 
 uint16_t q8_round_store(float w, float scale) {
@@ -1038,12 +1064,20 @@ orc_model *orc_model_create_synth(const orc_config *cfg, const orc_synth *sp) {
     std::vector<int8_t> q;
     // One matrix in file order: fp16(N(0, std)), plus fp16-rounded N(0, noise_std) noise for
     // draft models; int8 (absmax / 127, round half to even, clamp +-127) when asked.
+    std::vector<float> draws, noises;
     auto matrix = [&](int role, int layer, uint32_t rows, uint32_t cols, bool quantizable) {
-        w.resize(size_t(rows) * cols);
-        for (auto &x : w) {
-            float v = f16_to_f32(f32_to_f16(float(g.next() * sp->std)));
-            if (sp->noise_std > 0.f) v = v + float(noise.next() * sp->noise_std);
-            x = f32_to_f16(v);
+        const uint64_t n = uint64_t(rows) * cols;
+        w.resize(n);
+        draws.resize(n);
+        g.fill(n, double(sp->std), draws.data());
+        if (sp->noise_std > 0.f) {
+            noises.resize(n);
+            noise.fill(n, double(sp->noise_std), noises.data());
+        }
+        for (uint64_t i = 0; i < n; ++i) {
+            float v = f16_to_f32(f32_to_f16(draws[i]));
+            if (sp->noise_std > 0.f) v = v + noises[i];
+            w[i] = f32_to_f16(v);
         }
         if (sp->int8 && quantizable) {
             float amax = 0.f;

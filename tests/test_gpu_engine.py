@@ -248,9 +248,40 @@ def test_fused_host_driven_steps(models):
     assert toks == list(ref[0])
 
 
-def test_fused_path_refuses_int8(models):
+@pytest.mark.parametrize("batch", [1, 2, 4])
+def test_int8_persistent_path_matches_oracle(models, batch):
+    # GEMV_Quant weights on the persistent step kernel (int8 slices streamed through the same
+    # shared-memory slots, each dot product scaled by its tensor's scale) against the oracle,
+    # and against the per-op int8 kernels.
+    m = oracle.Model(models["q8"])
+    prompts = [ve.prompt(500 + b, SMALL["vocab"], 9 + 3 * b) for b in range(batch)]
+    with ve.Engine(models["q8"], max_batch=batch, max_len=80, path=ve.PATH_FUSED) as eng:
+        out, _ = eng.generate(prompts, 24)
+    with ve.Engine(models["q8"], max_batch=batch, max_len=80, path=ve.PATH_UNFUSED) as eng:
+        per_op, _ = eng.generate(prompts, 24)
+    for b in range(batch):
+        want, margins = m.generate(prompts[b], 24)
+        assert_tokens(out[b], want, margins)
+    assert np.array_equal(out, per_op)
+
+
+def test_int8_layer_kernels_are_refused(models):
+    # int8 runs on the persistent kernel only; the three-kernels-per-layer path refuses it.
     with pytest.raises(Exception):
-        ve.Engine(models["q8"], max_len=32, path=ve.PATH_FUSED)
+        ve.Engine(models["q8"], max_len=32, path=ve.PATH_FUSED_LAYERS)
+
+
+def test_config0_int8_full_size(tmp_path_factory):
+    # The config-0 model quantised per tensor (absmax / 127) decodes its 128 tokens on the
+    # persistent kernel as the oracle does on the same int8 weights.
+    d = ve.synth_model(str(tmp_path_factory.mktemp("cfg0q8")), seed=0, int8=True)
+    p = ve.prompt(1, 49152, 32)
+    with ve.Engine(d, max_len=256) as eng:
+        out, _ = eng.generate([p], 128)
+    want, _, margins, second = oracle.Model(d).generate_batch([p], 128, threads=os.cpu_count() or 1)
+    n, note = greedy_tokens_agree(out[0], want[0], margins[0], second[0])
+    print(f"cfg0 int8: {note}")
+    assert n >= 64
 
 
 @pytest.mark.parametrize("n,length", [(2, 200), (16, 130)])

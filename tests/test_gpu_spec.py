@@ -109,7 +109,7 @@ DRAW_DRIFT = 64     # token ids: an inverse-CDF draw moved by cumulative-sum rou
 RATIO_MARGIN = 0.02  # |u q(d) / p(d) - 1| below this: an accept decision within logit noise
 
 
-def rejection_rounds_agree(got, gpu_log, want, recs, budget):
+def rejection_rounds_agree(got, gpu_log, want, recs, budget, gpu_drafts=None):
     """Rejection sampling at temperature 1 on a random-init model draws from nearly uniform
     distributions over 49152 ids (each id ~2e-5 of the mass): logits that differ by fp32
     rounding (~1e-5) move the cumulative sums, and with them an inverse-CDF draw, by a few
@@ -128,6 +128,19 @@ def rejection_rounds_agree(got, gpu_log, want, recs, budget):
         if pos >= budget:
             break
         ga = gpu_log[r] if r < len(gpu_log) else -1
+        if gpu_drafts is not None and r < len(gpu_drafts):
+            # The drafts both loops proposed this round: any difference is the draft's own
+            # inverse-CDF draw moving, which must stay within DRAW_DRIFT ids.
+            gd = [int(x) for x in gpu_drafts[r]]
+            for j, (a, b) in enumerate(zip(gd, rec["drafts"])):
+                if a != b:
+                    if abs(a - b) <= DRAW_DRIFT and (ga >= j or rec["a"] >= j):
+                        ok = all(x == y for x, y in zip(got[pos: pos + j], rec["emitted"][:j]))
+                        if ok:
+                            return pos + j, f"round {r}: draft draw {a} vs {b}"
+                    if abs(a - b) > DRAW_DRIFT:
+                        raise AssertionError(f"round {r}: drafts {gd} vs oracle {rec['drafts']}")
+                    break
         go = [int(x) for x in got[pos: pos + ga + 1]] if ga >= 0 else []
         wo = rec["emitted"][: budget - pos]
         if ga == rec["a"] and go == wo:
@@ -178,7 +191,8 @@ def test_config3_b16_matches_oracle(smollm_dirs, cfg3_oracles, cfg3_greedy, k, m
     t = ve.Engine(smollm_dirs[0], max_batch=B * (k + 1), max_len=32 + budget + k + 8)
     d = ve.Engine(smollm_dirs[1], max_batch=B, max_len=32 + budget + k + 8, share=t)
     try:
-        got, st, log = t.spec_generate(d, prompts, budget, k=k, mode=mode, seed=seed, log_rounds=64)
+        got, st, log, drafts = t.spec_generate(d, prompts, budget, k=k, mode=mode, seed=seed, log_rounds=64,
+                                               draft_log=True)
         acceptance = t.metrics().speculative_acceptance
     finally:
         close(t, d)
@@ -189,7 +203,8 @@ def test_config3_b16_matches_oracle(smollm_dirs, cfg3_oracles, cfg3_greedy, k, m
     for s in range(B):
         gpu_log = [int(a) for a in log[:, s] if a >= 0]
         if mode == ve.SPEC_REJECTION:
-            n, note = rejection_rounds_agree(got[s], gpu_log, want[s], recs[s], budget)
+            gpu_drafts = [drafts[r, s] for r in range(drafts.shape[0]) if log[r, s] >= 0]
+            n, note = rejection_rounds_agree(got[s], gpu_log, want[s], recs[s], budget, gpu_drafts)
             if note != "equal":
                 ties.append((s, n, note))
             continue

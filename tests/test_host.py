@@ -153,7 +153,7 @@ def test_truncated_safetensors_is_refused(tiny_dir, tmp_path):
     (d / "model.safetensors").write_bytes(raw[: len(raw) - 1000])
     with pytest.raises(cu.OpureError) as e:
         ve.inspect(str(d))
-    assert "past the end" in str(e.value)
+    assert "beyond the file" in str(e.value)
 
 
 def test_synth_kv_matches_splitmix_restatement():
