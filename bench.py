@@ -43,11 +43,34 @@ for p in (REPO, PKG):
 METRIC = "decode tok/s (bs1, bs64) at SmolLM-135M shape; GEMV+attn HBM GB/s as % of peak"
 PROMPT_LEN, DECODE_STEPS = 32, 128
 FALLBACK_PEAK = 6650.0  # GB/s, used only when MEASURED_PEAKS.json is absent
-# DRAM bytes (read + write) of one decode step from ncu captures of this build:
-# `ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum
-#  --clock-control none -k regex:<kernel> -c <n> python bench.py --quick --no-cpu [--batch B]
-#  --steps 2 --warmup 3`, per kernel over a few launches, summed over one step's launches.
-NCU_STEP_TRAFFIC = {1: 271.8e6, 64: 452.3e6}
+# DRAM bytes (read + write) of one decode step, from ncu captures of this build (cold caches:
+# ncu serialises launches). Batch 1, the persistent step kernel, mean of two launches:
+#   ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum
+#     --clock-control none -k regex:persistent_step -s 33 -c 2
+#     python bench.py --quick --no-cpu --steps 2 --warmup 3 --bs64-steps 0 --int8 0
+# -> 269.92 MB read + 1.0-3.5 MB written per launch.
+# Batch 64, the per-layer kernels over two layers at positions 32-33, times 30 layers, plus the
+# lm_head GEMM and the step's begin/end kernels:
+#   ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum
+#     --clock-control none -k "regex:gemm_tc_kernel|pack_kernel|attn_tma_kernel|rope_kv_kernel"
+#     -s 10872 -c 20 python bench.py --quick --no-cpu --batch 64 --steps 2 --warmup 3
+#     --bs64-steps 0 --int8 0
+# -> 11.80 MB per layer, 411.1 MB per step. ncu flushes the caches before every captured
+# launch, so at batch 64 each kernel's activation inputs count as DRAM reads too (an upper
+# bound; at batch 1 the step is one launch). Both captures ran at a mean context of about 37
+# positions; step_traffic() moves the K/V share to the timed steps' mean context.
+NCU_STEP_TRAFFIC = {1: 272.2e6, 64: 411.1e6}
+NCU_CAPTURE_CTX = 37.0
+
+
+def step_traffic(info, batch: int, positions):
+    """The captured DRAM bytes of one step, with the K/V reads moved from the capture's mean
+    context to the mean context of `positions`; None without a capture for this batch."""
+    t = NCU_STEP_TRAFFIC.get(batch)
+    if t is None:
+        return None
+    mean_ctx = float(np.mean([p + 1 for p in positions]))
+    return t + batch * info.kv_bytes_per_token * (mean_ctx - NCU_CAPTURE_CTX)
 
 
 def peaks():
@@ -413,7 +436,8 @@ def measure_bs64(args, world, rank, local, mp):
     return {"value": world * B * args.bs64_steps / (dev_ms * 1e-3), "unit": "tok/s", "steps": args.bs64_steps,
             "warmup": 8, "ms_per_step": step_ms, "global_batch": world * B,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": NCU_STEP_TRAFFIC.get(B), "bytes_per_step": sbytes},
+                         "frac": achieved / peak, "traffic": step_traffic(info, B, positions),
+                         "bytes_per_step": sbytes},
             "gpu_launches": launches_per_step(info, B) * args.bs64_steps}
 
 
@@ -468,7 +492,7 @@ def run_ours(args, world, rank, local):
     gen, _ = eng.generate(prompts, 1 if args.quick else DECODE_STEPS)
     parity = {"tokens_checked": 0}
 
-    dev_ms, clocks = device_steps(eng, B, args.steps, args.warmup, world, True, local)
+    dev_ms, clocks = device_steps(eng, B, args.steps, args.warmup, world, not args.quick, local)
     clocks_per_rank = gather_objects(world, clocks)
     cu.check(L.opure_last_error(ctx), "device status")
     phases = None
@@ -522,7 +546,7 @@ def run_ours(args, world, rank, local):
                    "parallelism": f"sequence-sharded x{world}",
                    "l2": "inputs larger than L2: every step streams 269 MB of weights (L2 126 MB)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": NCU_STEP_TRAFFIC.get(B),
+                     "frac": achieved / peak, "traffic": step_traffic(info, B, positions),
                      "kernel": ("the persistent decode-step kernel (one launch per step)"
                                 if line_launches == 3 else "whole decode step (GEMV dominant)"),
                      "peak_kind": peak_kind,
@@ -674,7 +698,7 @@ def run_gemv_sweep(args):
     peak, kind = peaks()
     out = []
     with cu.Ctx(0) as ctx:
-        for rows, cols in ((576, 576), (192, 576), (1536, 576), (576, 1536), (49152, 576)):
+        for rows, cols in args.gemv_shapes:
             w16 = ve.normal_f16(4, 0.02, rows * cols)
             wf = oracle_free_f16_to_f32(w16)
             amax = float(np.abs(wf).max())
@@ -686,7 +710,7 @@ def run_gemv_sweep(args):
                 pool = ctx.buffer(copies * wbytes)
                 for c in range(copies):
                     pool.upload(wh, offset=c * wbytes)
-                for n in (1, 5, 9):
+                for n in args.gemv_n:
                     x = oracle_free_f16_to_f32(ve.normal_f16(4 + n, 1.0, n * cols))
                     dx, dy = ctx.to_device(x), ctx.buffer(n * rows * 4)
                     a = cu.GemvArgs()
@@ -926,10 +950,10 @@ def run_spec(args):
     tgt = model_dir()
     root = os.environ.get("OPURE_BENCH_DIR", "/tmp/opure_bench")
     drf = ve.synth_model(os.path.join(root, "smollm135m_seed0_draft6"), seed=0, noise_seed=6, noise_std=0.004)
-    budget = 256
+    budget = args.spec_budget
     points = []
-    for k in (4, 8):
-        for B in (1, 16):
+    for k in args.spec_k:
+        for B in args.spec_b:
             max_len = PROMPT_LEN + budget + k + 8
             t = ve.Engine(tgt, max_batch=B * (k + 1), max_len=max_len)
             d = ve.Engine(drf, max_batch=B, max_len=max_len, share=t)
@@ -1073,6 +1097,16 @@ def main():
     ap.add_argument("--int8", type=int, default=1,
                     help="decode at --batch 1: also time the int8 (GEMV_Quant) config-0 model and report it "
                          "under \"int8\"; 0 skips")
+    ap.add_argument("--gemv-n", type=lambda v: [int(x) for x in v.split(",")], default=[1, 5, 9],
+                    help="gemv: comma-separated vector counts (16 and more run on the tensor cores)")
+    ap.add_argument("--gemv-shapes", type=lambda v: [tuple(int(d) for d in x.split("x")) for x in v.split(",")],
+                    default=[(576, 576), (192, 576), (1536, 576), (576, 1536), (49152, 576)],
+                    help="gemv: comma-separated ROWSxCOLS shapes")
+    ap.add_argument("--spec-k", type=lambda v: [int(x) for x in v.split(",")], default=[4, 8],
+                    help="spec: comma-separated draft lengths")
+    ap.add_argument("--spec-b", type=lambda v: [int(x) for x in v.split(",")], default=[1, 16],
+                    help="spec: comma-separated batch sizes")
+    ap.add_argument("--spec-budget", type=int, default=256, help="spec: generated tokens per sequence")
     ap.add_argument("--seqs", type=int, default=512, help="cfg4: total sequences over all ranks")
     ap.add_argument("--wave", type=int, default=128, help="cfg4: sequences per GPU per wave")
     ap.add_argument("--attn-b", type=int, default=0, help="attn: only this batch size (1, 8 or 64)")
