@@ -9,19 +9,24 @@
 //
 //  * Every rank owns a mailbox allocation that every other rank maps with CUDA IPC (one
 //    process per GPU, all GPUs on one NVSwitch). Layout (byte offsets):
-//      [kFlagsOff] u32 flags[src rank][CTA]     -- written by the sender CTA over NVLink
+//      [kFlagsOff] u32 flags[src rank][CTA]     -- argmax exchange: written by the sender
 //      [kCtlOff]   u32 seq, ticket, exchange    -- local only
 //      [kKeysOff]  u64 keys[parity][src][vec]   -- argmax keys
-//      [kRowsOff]  f32 rows[parity][src][vec][max_rows]
-//  * The GEMV CTA c computes its rows of this rank's partial, stores them with plain
-//    stores straight into slot `rank` of every rank's mailbox, then one thread per rank
-//    publishes flags[rank][c] = seq + 1 there with a system-scope release store. It then
-//    waits (acquire loads of its own mailbox, bounded by a deadline) until every rank's
-//    CTA c has published, and sums the n slots of its rows in rank order 0..n-1 -- the
-//    same order on every rank, so the replicated residual stays bit-identical everywhere --
-//    into y (optionally residual + sum). Every rank runs the same grid over the same rows,
-//    so CTA c only ever waits for the CTAs c of the other GPUs; the grid is at most one CTA
-//    per SM, so all of it is resident at once.
+//      [kRowsOff]  u64 rows[parity][src][vec][max_rows] -- (tag << 32) | fp32 bits
+//  * The GEMV CTA c computes its rows of this rank's partial and stores each value, with
+//    the collective's tag (seq + 1) in the upper half of the same 8-byte word, straight into
+//    slot `rank` of every rank's mailbox (relaxed system-scope 64-bit stores over NVLink).
+//    An aligned 64-bit access is single-copy atomic, so a reader that sees the tag also sees
+//    the value: no flag, no fence, one NVLink write latency per collective. The CTA then
+//    loads the n words of each of its rows from its own mailbox until every tag matches
+//    (bounded by a deadline) and sums the values in rank order 0..n-1 -- the same order on
+//    every rank, so the replicated residual stays bit-identical everywhere -- into y
+//    (optionally residual + sum). Every rank runs the same grid over the same rows, so CTA
+//    c only ever waits for the CTAs c of the other GPUs; the grid is at most one CTA per
+//    SM, so all of it is resident at once.
+//  * The argmax exchange (one CTA, 8-byte keys with no room for a tag) publishes per-rank
+//    flags with a system-scope release store after a CTA barrier, and waits on its own
+//    flags with acquire loads.
 //  * `seq` counts the collectives this rank has run. Every kernel reads it after its
 //    predecessor completes; the last CTA out (ticket) advances it. Data slots alternate by
 //    seq parity: a rank can be at most one collective ahead of any other (collective k+1 on
@@ -76,9 +81,10 @@ __device__ __forceinline__ uint32_t *flag_at(uint8_t *base, uint32_t src, uint32
     return reinterpret_cast<uint32_t *>(base + kFlagsOff) + size_t(src) * kMaxCtas + cta;
 }
 __device__ __forceinline__ uint32_t *ctl_at(uint8_t *base) { return reinterpret_cast<uint32_t *>(base + kCtlOff); }
-__device__ __forceinline__ float *row_slot(uint8_t *base, uint32_t par, uint32_t src, uint32_t v,
-                                           uint32_t max_rows) {
-    return reinterpret_cast<float *>(base + kRowsOff) + ((size_t(par) * kMaxRanks + src) * kPassVec + v) * max_rows;
+__device__ __forceinline__ unsigned long long *row_slot(uint8_t *base, uint32_t par, uint32_t src, uint32_t v,
+                                                        uint32_t max_rows) {
+    return reinterpret_cast<unsigned long long *>(base + kRowsOff) +
+           ((size_t(par) * kMaxRanks + src) * kPassVec + v) * max_rows;
 }
 __device__ __forceinline__ unsigned long long *key_slot(uint8_t *base, uint32_t par, uint32_t src) {
     return reinterpret_cast<unsigned long long *>(base + kKeysOff) + (size_t(par) * kMaxRanks + src) * kMaxKeys;
@@ -92,17 +98,28 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ unsigned long long tagged(float v, uint32_t tag) {
+    return (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
+}
 
 // Publishes this CTA's pushes to every rank and waits until the CTA of the same index on
-// every rank has published collective `want`. Whole CTA; the barrier at entry orders every
-// thread's pushes before the release stores, the one at exit orders the acquire loads before
-// any thread reads the mailbox. Returns false after a timeout (recorded in the status word).
+// every rank has published collective `want`. Whole CTA; the barrier at entry makes every
+// thread's pushes precede (in causality order) the release stores that thread 0..n-1 make at
+// system scope, the one at exit orders the acquire loads before any thread reads the
+// mailbox. Returns false after a timeout (recorded in the status word).
 __device__ bool exchange(const PeerView &pv, uint32_t want, DeviceStatus *st, uint32_t where) {
     __shared__ int failed;
     if (threadIdx.x == 0) failed = 0;
     __syncthreads();
     if (threadIdx.x < pv.n_ranks) {
-        __threadfence_system();
         st_release_sys(flag_at(pv.peer[threadIdx.x], pv.rank, blockIdx.x), want);
         const uint32_t *f = flag_at(pv.peer[pv.rank], threadIdx.x, blockIdx.x);
         if (int32_t(ld_acquire_sys(f) - want) < 0) {
@@ -158,7 +175,7 @@ __global__ void __launch_bounds__(kThreads) gemv_allreduce_kernel(ArParams p, Pe
     uint8_t *const local = pv.peer[pv.rank];
     if (threadIdx.x == 0) s_seq = *reinterpret_cast<volatile uint32_t *>(ctl_at(local));
     stage_vectors<NV>(p.x, p.x_stride, p.cols, PRO == OPURE_PRO_RMSNORM, p.gain, p.eps, xs, red);
-    const uint32_t seq = s_seq, par = seq & 1u;
+    const uint32_t seq = s_seq, par = seq & 1u, want = seq + 1u;
 
     // This rank's partial rows, pushed into slot `rank` of every mailbox.
     for (uint32_t g = g0; g < groups; g += nwarps) {
@@ -171,14 +188,14 @@ __global__ void __launch_bounds__(kThreads) gemv_allreduce_kernel(ArParams p, Pe
 #pragma unroll
             for (int v = 0; v < NV; ++v) {
                 if (r >= int(valid) || lane != uint32_t((r * NV + v) & 31)) continue;
-                const float val = acc[r][v] * p.scale;
-                for (uint32_t q = 0; q < pv.n_ranks; ++q) row_slot(pv.peer[q], par, pv.rank, v, pv.max_rows)[row0 + r] = val;
+                const unsigned long long word = tagged(acc[r][v] * p.scale, want);
+                for (uint32_t q = 0; q < pv.n_ranks; ++q)
+                    st_relaxed_sys_u64(row_slot(pv.peer[q], par, pv.rank, v, pv.max_rows) + row0 + r, word);
             }
     }
 
-    exchange(pv, seq + 1u, p.st, 90);
-
-    // Sum the ranks' slots of this CTA's rows in rank order.
+    // Sum the ranks' words of this CTA's rows in rank order, once every tag is this
+    // collective's. All n loads of a row are issued before any is checked.
     for (uint32_t g = g0; g < groups; g += nwarps) {
         const uint32_t row0 = g * kRows;
         const uint32_t valid = min(uint32_t(kRows), p.rows - row0);
@@ -187,12 +204,40 @@ __global__ void __launch_bounds__(kThreads) gemv_allreduce_kernel(ArParams p, Pe
 #pragma unroll
             for (int v = 0; v < NV; ++v) {
                 if (r >= int(valid) || lane != uint32_t((r * NV + v) & 31)) continue;
+                unsigned long long w[kMaxRanks];
+                uint32_t missing = 0;
+#pragma unroll
+                for (uint32_t q = 0; q < kMaxRanks; ++q)
+                    if (q < pv.n_ranks) {
+                        w[q] = ld_relaxed_sys_u64(row_slot(local, par, q, v, pv.max_rows) + row0 + r);
+                        if (uint32_t(w[q] >> 32) != want) missing |= 1u << q;
+                    }
+                if (missing) {
+                    const uint64_t t0 = global_ns();
+                    for (uint32_t i = 1; missing; ++i) {
+#pragma unroll
+                        for (uint32_t q = 0; q < kMaxRanks; ++q)
+                            if (missing & (1u << q)) {
+                                w[q] = ld_relaxed_sys_u64(row_slot(local, par, q, v, pv.max_rows) + row0 + r);
+                                if (uint32_t(w[q] >> 32) == want) missing &= ~(1u << q);
+                            }
+                        if (missing && (i & 63u) == 0 &&
+                            (global_ns() - t0 > pv.timeout_ns || *reinterpret_cast<volatile uint32_t *>(&p.st->code))) {
+                            report(p.st, OPURE_ERR_DEVICE_TIMEOUT, 90, __ffs(missing) - 1);
+                            break;
+                        }
+                    }
+                }
+                if (missing) continue;  // timed out: y keeps its old value, the status word says why
                 float s = 0.f;
-                for (uint32_t q = 0; q < pv.n_ranks; ++q) s += __ldcg(row_slot(local, par, q, v, pv.max_rows) + row0 + r);
+#pragma unroll
+                for (uint32_t q = 0; q < kMaxRanks; ++q)
+                    if (q < pv.n_ranks) s += __uint_as_float(uint32_t(w[q]));
                 const size_t o = size_t(v) * p.y_stride + row0 + r;
                 p.y[o] = ADD ? p.residual[o] + s : s;
             }
     }
+    __syncthreads();
 
     // The last CTA out advances the collective sequence (every CTA read it before its ticket).
     if (threadIdx.x == 0) {
@@ -341,7 +386,7 @@ opure_status opure_peer_create(opure_ctx *ctx, opure_comm *comm, uint32_t max_ro
     pr->rank = rank;
     pr->max_rows = max_rows;
     pr->timeout_ns = uint64_t(timeout_ms ? timeout_ms : 2000) * 1000000ull;
-    pr->bytes = (kRowsOff + size_t(2) * kMaxRanks * kPassVec * max_rows * 4 + 255) & ~size_t(255);
+    pr->bytes = (kRowsOff + size_t(2) * kMaxRanks * kPassVec * max_rows * 8 + 255) & ~size_t(255);
     void *mem = nullptr;
     cudaError_t e = cudaMalloc(&mem, pr->bytes);
     pr->local = e == cudaSuccess ? static_cast<uint8_t *>(mem) : nullptr;
