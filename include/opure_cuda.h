@@ -189,6 +189,10 @@ typedef struct opure_attn_args {
     void *scratch;
     size_t scratch_bytes;
     opure_kv_layout kv;
+    /* NULL, or a packed operand (see opure_gemv_args) of the n * n_q output vectors of
+     * length n_heads * head_dim, written besides `out`: the o_proj GEMV's x_packed.
+     * opure_attention only (opure_attention_static ignores it). */
+    uint16_t *out_packed;
 } opure_attn_args;
 size_t opure_attention_scratch_bytes(uint32_t n, uint32_t n_q, uint32_t n_heads,
                                      uint32_t n_kv, uint32_t head_dim, uint32_t max_ctx,
@@ -254,7 +258,26 @@ typedef struct opure_gemv_args {
     /* OPURE_EPI_ARGMAX: packed (value, index) keys, one uint64 per vector, which the
      * caller zeroes first; decode with opure_argmax_decode. */
     unsigned long long *argmax_keys;
+    /* Chained tensor-core operands (fp16 weights, 16..256 vectors, cols a multiple of 64;
+     * OPURE_ERR_UNSUPPORTED otherwise). A packed operand holds the nvec vectors of length
+     * L as fp16 pairs hi = fp16(v), lo = fp16((v - hi) * 2^11): [2][npad][L] halves, hi
+     * rows first, npad = nvec rounded up to 16 (opure_packed_bytes). Values must stay
+     * below 65504 in magnitude (a larger one is reported as OPURE_ERR_DEVICE_BOUNDS).
+     * Zero-initialise new packed buffers once: padding rows are read but never written. */
+    const uint16_t *x_packed;  /* non-NULL: the input vectors come from this packed operand
+                                  (x may then be NULL). With OPURE_PRO_RMSNORM the packed values
+                                  are gain * x, and x_sumsq supplies the norm               */
+    const float *x_sumsq;      /* x_packed + OPURE_PRO_RMSNORM: [ceil(cols / 128)][nvec] partial
+                                  sums of squares of x (a producer's y_sumsq)               */
+    uint16_t *y_packed;        /* non-NULL: also write the output vectors (STORE: y, ADD: the
+                                  new residual, SWIGLU: the activation) as a packed operand
+                                  [2][npad][rows], each value times y_pack_gain[row] if given */
+    const uint16_t *y_pack_gain; /* [rows] fp16 or NULL: the next GEMV's RMSNorm gain        */
+    float *y_sumsq;            /* [ceil(rows / 128)][nvec] or NULL: per 128-row block, the sum
+                                  of squares of the output vectors (before y_pack_gain)      */
 } opure_gemv_args;
+/* Bytes of a packed operand of nvec vectors of length len (see opure_gemv_args). */
+size_t opure_packed_bytes(uint32_t nvec, uint32_t len);
 opure_status opure_gemv(opure_ctx *ctx, const opure_gemv_args *a);
 /* Decodes OPURE_EPI_ARGMAX keys into (index, value) on the device. */
 opure_status opure_argmax_decode(opure_ctx *ctx, const unsigned long long *keys, uint32_t n,

@@ -37,7 +37,18 @@ struct AttnParams {
     uint32_t *counters;      // [entries * n_kv]
     opure_kv_layout kv;
     DeviceStatus *st;
+    __half *out_packed;      // null, or [2][pk_npad][n_heads * HD] (store_packed)
+    uint32_t pk_npad;
 };
+
+// Output element i (= head * HD + dim) of an entry: fp32, and with out_packed also the
+// scale-free fp16 pair of the next GEMV's packed operand.
+template <int HD>
+__device__ __forceinline__ void store_out(const AttnParams &p, uint32_t entry, uint32_t i, float v) {
+    const uint32_t len = p.n_heads * HD;
+    p.out[size_t(entry) * len + i] = v;
+    if (p.out_packed) store_packed(p.out_packed, p.pk_npad, len, entry, i, v, p.st, 15);
+}
 
 template <int HD, int G>
 __global__ void __launch_bounds__(kWarps * 32) attn_kernel(AttnParams p) {
@@ -112,8 +123,9 @@ __global__ void __launch_bounds__(kWarps * 32) attn_kernel(AttnParams p) {
         }
         // acc / max(sum, 1e-30) as the reference's epilogue
         // (Opure_FlashAttention_Decode.usf:235-239).
-        p.out[(size_t(entry) * p.n_heads + g * G + h) * HD + d] = a / fmaxf(lsum, 1e-30f);
+        store_out<HD>(p, entry, (g * G + h) * HD + d, a / fmaxf(lsum, 1e-30f));
     }
+    if (p.out_packed) asm volatile("fence.proxy.async.global;" ::: "memory");  // read by TMA next
     if (threadIdx.x == 0) p.counters[eg] = 0u;  // ready for the next call
 }
 
@@ -386,8 +398,9 @@ __global__ void __launch_bounds__((kWarps + 1) * 32) attn_tma_kernel(AttnParams 
             a += __ldcg(pp + d) * f;
             lsum += __ldcg(pp + HD + 1) * f;
         }
-        p.out[(size_t(entry) * p.n_heads + g * G + h) * HD + d] = a / fmaxf(lsum, 1e-30f);
+        store_out<HD>(p, entry, (g * G + h) * HD + d, a / fmaxf(lsum, 1e-30f));
     }
+    if (p.out_packed) asm volatile("fence.proxy.async.global;" ::: "memory");  // read by TMA next
     if (threadIdx.x == 0) p.counters[eg] = 0u;
 }
 
@@ -563,6 +576,8 @@ extern "C" opure_status opure_attention(opure_ctx *ctx, const opure_attn_args *a
     p.counters = reinterpret_cast<uint32_t *>(static_cast<char *>(a->scratch) + counters_off);
     p.kv = kv;
     p.st = ctx->status;
+    p.out_packed = reinterpret_cast<__half *>(a->out_packed);
+    p.pk_npad = (entries + 15) & ~15u;
     return launch_attention(ctx, p, kv.head_dim, G, entries * kv.n_kv, n_splits);
 }
 

@@ -29,6 +29,23 @@ __device__ __forceinline__ void report(DeviceStatus *st, uint32_t code, uint32_t
 }
 
 // ---------------------------------------------------------------------------
+// Chained tensor-core operand: vector `vec` of a [2][npad][len] fp16 buffer holds
+// hi = fp16(v) in row vec and lo = fp16((v - hi) * 2^11) in row npad + vec, so that
+// W.v = W.hi + 2^-11 W.lo keeps ~22 significant bits with fp16 x fp16 products (the
+// consumer accumulates the two halves separately). A value outside fp16's range is
+// reported at `site` and stored as 0.
+__device__ __forceinline__ void store_packed(__half *pk, uint32_t npad, uint32_t len, uint32_t vec, uint32_t i,
+                                             float v, DeviceStatus *st, uint32_t site) {
+    if (!(fabsf(v) < 65504.f)) {
+        report(st, OPURE_ERR_DEVICE_BOUNDS, site, i);
+        v = 0.f;
+    }
+    const __half hi = __float2half_rn(v);
+    pk[size_t(vec) * len + i] = hi;
+    pk[size_t(npad + vec) * len + i] = __float2half_rn((v - __half2float(hi)) * 2048.f);
+}
+
+// ---------------------------------------------------------------------------
 // Memory access helpers.
 
 // 16-byte load from L2 (coherent across SMs within one kernel): for data other CTAs of the

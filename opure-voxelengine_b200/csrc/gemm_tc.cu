@@ -9,17 +9,28 @@
 //          x / s_v = hi + lo  (hi = fp16(x / s_v), lo = fp16(x / s_v - hi)),
 //          which keeps ~22 significant bits: W.x = s_v (W.hi + W.lo) with fp16 x fp16
 //          products accumulated in fp32, the accuracy of the fp32 CUDA-core GEMV.
-//   gemm   one CTA per (128-row tile, K split). Thread 0 streams 128x64 weight tiles and
-//          the matching 64-column slices of the packed vectors with TMA (128-byte
-//          swizzle) into a ring of shared-memory stages; thread 32 issues
-//          tcgen05.mma (M=128, N=vectors rounded up to 16, K=16, fp16 in, fp32 out) into
-//          a TMEM accumulator (two for the SwiGLU gate/up pair) and frees each stage with
-//          tcgen05.commit. The four warps then read the accumulator rows with tcgen05.ld
+//   gemm   one CTA per (128-row tile, K split, vector slice of nt). Thread 0 streams
+//          128x64 weight tiles and the matching 64-column slices of the packed vectors with
+//          TMA (128-byte swizzle) into a ring of shared-memory stages, the slice's hi rows
+//          and lo rows side by side; thread 32 issues one tcgen05.mma per K=16 step with
+//          M=128 and N=2 nt (hi and lo vectors together, fp16 in, fp32 out), so each weight
+//          tile is read once for both halves, into a TMEM accumulator whose first nt
+//          columns hold W.hi and next nt W.lo (a second one for the SwiGLU up half), and
+//          frees each stage with tcgen05.commit. The four warps then read the accumulator rows with tcgen05.ld
 //          (warp w owns TMEM lanes 32w..32w+31 = tile rows) and apply the epilogue:
 //          store, residual add, SwiGLU, or argmax keys (+ logits). With a K split every
 //          CTA adds its sums into a 64-bit fixed-point accumulator with integer atomics
 //          and the last CTA of the tile (ticket counter) converts them and runs the
 //          epilogue, so results do not depend on the order the splits finish in.
+//   chained  consecutive GEMVs of a decode layer skip the pack kernel: the producer (a
+//          GEMM epilogue, or the attention kernel) writes its output vectors as scale-free
+//          fp16 pairs hi = fp16(v), lo = fp16((v - hi) 2^11) (store_packed), and the
+//          consumer accumulates W.hi and W.lo in two TMEM accumulators and adds them as
+//          D_hi + 2^-11 D_lo. The RMSNorm of a chained input moves into the consumer's
+//          epilogue: the producer multiplies the packed values by the norm gain and writes,
+//          per 128-row tile, the sum of squares of each vector (deterministic: one writer per
+//          tile and vector); the consumer adds the tiles' sums in tile order and scales its
+//          results by 1/rms. W.(g x / rms) = (W.(g x)) / rms.
 // All waits are bounded (1 s); a timeout is reported in the ctx status word and the CTA
 // still releases its TMEM. No TMA multicast is used.
 #include <cuda.h>
@@ -208,6 +219,14 @@ struct TcParams {
     long long *accum;   // [tiles][npad / nt][accumulators * nt][128] fixed-point split-K sums
     uint32_t *tickets;  // [tiles][npad / nt]
     DeviceStatus *st;
+    // Chained operands (see the file comment).
+    uint32_t chained;       // the B operand is a scale-free packed operand
+    uint32_t K;
+    const float *x_sumsq;   // chained RMSNorm: [ceil(K / 128)][n] partial sums of squares
+    float eps;
+    __half *y_packed;       // [2][npad][rows] or null
+    const __half *y_gain;   // [rows] or null
+    float *y_sumsq;         // [tiles][n] or null
 };
 
 template <int EPI>
@@ -221,6 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __shared__ int fail, last;
     __shared__ uint32_t issued_s, consumed_s;
     __shared__ float s_scale[kMaxN];
+    __shared__ float s_red[kThreads / 32][16];
 
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t tile = blockIdx.x, split = blockIdx.y;
@@ -234,8 +254,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dsm) + 1023) & ~uintptr_t(1023));
     auto a_tile = [&](uint32_t s, uint32_t j) { return base + size_t(s) * stage_bytes + j * a_bytes; };
     auto b_tile = [&](uint32_t s, uint32_t j) { return base + size_t(s) * stage_bytes + kAcc * a_bytes + j * b_bytes; };
+    // Accumulator a (gate / up) spans columns [2 nt a, 2 nt a + 2 nt): W.hi, then W.lo.
+    const float lo_scale = p.chained ? 1.0f / 2048.0f : 1.0f;
     uint32_t ncols = 32;
-    while (ncols < kAcc * nt) ncols <<= 1;
+    while (ncols < kAcc * 2 * nt) ncols <<= 1;
 
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < p.stages; ++s) {
@@ -267,8 +289,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     grid_dependency_wait();
     grid_dependents_launch();
-    // Per-vector scales written by the pack kernel (read after the wait).
-    for (uint32_t v = threadIdx.x; v < p.npad; v += blockDim.x) s_scale[v] = v < p.n ? p.xscale[v] : 0.f;
+    // Per-vector scales written by the pack kernel, or for a chained input 1 / rms from the
+    // producer's per-tile sums of squares (read after the wait).
+    for (uint32_t v = threadIdx.x; v < p.npad; v += blockDim.x) {
+        float sc = 0.f;
+        if (v < p.n) {
+            if (!p.chained) {
+                sc = p.xscale[v];
+            } else if (p.x_sumsq) {
+                double ss = 0.0;
+                for (uint32_t t = 0; t < (p.K + kTileM - 1) / kTileM; ++t) ss += double(__ldcg(p.x_sumsq + size_t(t) * p.n + v));
+                // The GEMV prologue's RMSNorm (RMSNormMain, Opure_RMSNorm.usf:31-79).
+                sc = float(1.0 / sqrt(ss / double(p.K) + double(p.eps)));
+            } else {
+                sc = 1.f;
+            }
+        }
+        s_scale[v] = sc;
+    }
 
     if (warp == 0) {
         if (lane == 0) {
@@ -298,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             // MMA issuer: per 64-wide K tile, four K=16 steps (32 bytes along the swizzled
             // rows) of hi and lo products.
-            const uint32_t idesc = (1u << 4) | ((nt >> 3) << 17) | ((kTileM >> 4) << 24);
+            const uint32_t idesc = (1u << 4) | (((2 * nt) >> 3) << 17) | ((kTileM >> 4) << 24);
             uint32_t i = 0;
             for (; i < nk; ++i) {
                 const uint32_t s = i % p.stages;
@@ -308,18 +346,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc_fence_after();
+                // b_tile(s, 1) follows b_tile(s, 0) directly: one K-major operand of 2 nt rows.
                 const uint32_t a0 = smem_addr(a_tile(s, 0)), bh = smem_addr(b_tile(s, 0));
-                const uint32_t bl = smem_addr(b_tile(s, 1));
 #pragma unroll
                 for (uint32_t k = 0; k < kTileK / 16; ++k) {
-                    const uint64_t dh = smem_desc(bh + 32 * k), dl = smem_desc(bl + 32 * k);
+                    const uint64_t db = smem_desc(bh + 32 * k);
                     const uint64_t da = smem_desc(a0 + 32 * k);
-                    mma_f16(tmem, da, dh, idesc, (i | k) != 0);
-                    mma_f16(tmem, da, dl, idesc, 1);
+                    const uint32_t accum = (i | k) != 0;
+                    mma_f16(tmem, da, db, idesc, accum);
                     if (kSwiglu) {
                         const uint64_t du = smem_desc(smem_addr(a_tile(s, 1)) + 32 * k);
-                        mma_f16(tmem + nt, du, dh, idesc, (i | k) != 0);
-                        mma_f16(tmem + nt, du, dl, idesc, 1);
+                        mma_f16(tmem + 2 * nt, du, db, idesc, accum);
                     }
                 }
                 mma_commit(&empty[s]);
@@ -344,6 +381,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t row = m0 + lrow;
         const uint32_t taddr = tmem + ((warp * 32) << 16);
         const uint32_t acc_cols = kAcc * nt;
+        // Result columns c .. c+15 (accumulator c / nt) of this thread's row: W.hi plus
+        // W.lo (scaled by 2^-11 for a chained operand).
+        auto tm_col = [&](uint32_t c, float (&r)[16]) {
+            const uint32_t col = (c / nt) * 2 * nt + c % nt;
+            float l[16];
+            tmem_ld16(taddr + col, r);
+            tmem_ld16(taddr + col + nt, l);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) r[j] = fmaf(l[j], lo_scale, r[j]);
+        };
         bool run_epi = true;
         long long *acc64 = nullptr;
         if (p.splits > 1) {
@@ -353,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             acc64 = p.accum + size_t(slice) * acc_cols * kTileM;
             for (uint32_t c0 = 0; c0 < acc_cols; c0 += 16) {
                 float r[16];
-                tmem_ld16(taddr + c0, r);
+                tm_col(c0, r);
 #pragma unroll
                 for (int j = 0; j < 16; ++j)
                     atomicAdd(reinterpret_cast<unsigned long long *>(acc64 + size_t(c0 + j) * kTileM + lrow),
@@ -375,7 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // accumulator for the next call).
             auto column = [&](uint32_t c, float (&r)[16]) {
                 if (p.splits == 1) {
-                    tmem_ld16(taddr + c, r);
+                    tm_col(c, r);
                 } else {
                     long long a[16];
 #pragma unroll
@@ -391,7 +438,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             // and the vector scales come from shared memory, so a thread pays one memory
             // round trip per chunk rather than one per column.
             const bool in = row < p.rows;
+            const float ygain = (p.y_packed && p.y_gain && in) ? __half2float(p.y_gain[row]) : 1.f;
             for (uint32_t c0 = 0; c0 < nt; c0 += 16) {
+                float outv[16];
                 float g[16], u[16], res[16];
                 column(c0, g);
                 if (kSwiglu) column(nt + c0, u);
@@ -407,21 +456,49 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const bool ok = in && v < p.n;
                     const float val = g[j] * s_scale[v];
                     const size_t o = size_t(v) * p.y_stride + row;
+                    outv[j] = 0.f;
                     if constexpr (EPI == OPURE_EPI_STORE) {
+                        outv[j] = val;
                         if (ok) p.y[o] = val;
                     } else if constexpr (EPI == OPURE_EPI_ADD) {
-                        if (ok) p.y[o] = res[j] + val;
+                        outv[j] = res[j] + val;
+                        if (ok) p.y[o] = outv[j];
                     } else if constexpr (EPI == OPURE_EPI_SWIGLU) {
                         const float uv = u[j] * s_scale[v];
                         const float sg = 1.0f / (1.0f + expf(-val));
-                        if (ok) p.y[o] = (val * sg) * uv;
+                        outv[j] = (val * sg) * uv;
+                        if (ok) p.y[o] = outv[j];
                     } else {
                         if (ok && p.y) p.y[o] = val;
                         const unsigned long long k = warp_max_u64(ok ? argmax_key(val, row) : 0ull);
                         if (lane == 0 && k) atomicMax(p.keys + v, k);
                     }
                 }
+                if constexpr (EPI != OPURE_EPI_ARGMAX) {
+                    // The next GEMV's packed operand, and this tile's sums of squares.
+                    if (p.y_packed)
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            if (in && n0 + c0 + j < p.n)
+                                store_packed(p.y_packed, p.npad, p.rows, n0 + c0 + j, row, outv[j] * ygain, p.st, 63);
+                    if (p.y_sumsq) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const float sq = warp_sum((in && n0 + c0 + j < p.n) ? outv[j] * outv[j] : 0.f);
+                            if (lane == 0) s_red[warp][j] = sq;
+                        }
+                        __syncthreads();
+                        if (threadIdx.x < 16 && n0 + c0 + threadIdx.x < p.n) {
+                            float t = 0.f;
+                            for (uint32_t w = 0; w < kThreads / 32; ++w) t += s_red[w][threadIdx.x];
+                            p.y_sumsq[size_t(tile) * p.n + n0 + c0 + threadIdx.x] = t;
+                        }
+                        __syncthreads();
+                    }
+                }
             }
+            // A packed output is read by the next kernel's TMA (the async proxy).
+            if (p.y_packed) asm volatile("fence.proxy.async.global;" ::: "memory");
         }
     }
     tc_fence_before();
@@ -473,10 +550,23 @@ bool gemv_tc_eligible(const opure_ctx *ctx, const opure_gemv_args *a) {
            a->cols % kTileK == 0 && a->cols <= kTcMaxCols && encode_fn() != nullptr;
 }
 
+size_t packed_bytes(uint32_t nvec, uint32_t len) {
+    return size_t(2) * ((nvec + 15) & ~15u) * len * 2;
+}
+
 opure_status gemv_tc(opure_ctx *ctx, const opure_gemv_args *a) {
     const uint32_t K = a->cols, rows = a->rows;
     const uint32_t epi = a->epilogue;
     const uint32_t acc = epi == OPURE_EPI_SWIGLU ? 2 : 1;
+    const bool chained_in = a->x_packed != nullptr;
+    const bool chained = chained_in || a->y_packed || a->y_sumsq;
+    if (chained) {
+        // One pass; the packed buffers hold all vectors.
+        if (a->nvec > kMaxN || epi == OPURE_EPI_ARGMAX && (a->y_packed || a->y_sumsq)) return OPURE_ERR_UNSUPPORTED;
+        if (chained_in && a->prologue == OPURE_PRO_RMSNORM && !a->x_sumsq) return OPURE_ERR_INVALID_ARG;
+        if (chained_in && reinterpret_cast<uintptr_t>(a->x_packed) % 16) return OPURE_ERR_UNSUPPORTED;
+        if (a->y_packed && (rows % 8 || reinterpret_cast<uintptr_t>(a->y_packed) % 16)) return OPURE_ERR_UNSUPPORTED;
+    }
     uint8_t *ws = static_cast<uint8_t *>(ctx->ws);
     __half *xp = reinterpret_cast<__half *>(ws + kPackOff);
     float *xscale = reinterpret_cast<float *>(ws + kScaleOff);
@@ -497,17 +587,27 @@ opure_status gemv_tc(opure_ctx *ctx, const opure_gemv_args *a) {
     for (uint32_t v0 = 0; v0 < a->nvec; v0 += kMaxN) {
         const uint32_t n = std::min(kMaxN, a->nvec - v0);
         const uint32_t npad = (n + 15) & ~15u;
-        PackParams pp{a->x + size_t(v0) * a->x_stride, a->x_stride, K, npad, a->prologue == OPURE_PRO_RMSNORM,
-                      reinterpret_cast<const __half *>(a->norm_gain), a->eps, xp, xscale};
-        opure_status s = launch(ctx, pack_kernel, dim3(n), dim3(kPackThreads), pack_smem, true, pp);
-        if (s) return s;
+        opure_status s = OPURE_OK;
+        if (!chained_in) {
+            PackParams pp{a->x + size_t(v0) * a->x_stride, a->x_stride, K, npad, a->prologue == OPURE_PRO_RMSNORM,
+                          reinterpret_cast<const __half *>(a->norm_gain), a->eps, xp, xscale};
+            s = launch(ctx, pack_kernel, dim3(n), dim3(kPackThreads), pack_smem, true, pp);
+            if (s) return s;
+        }
         // Work split, latency first. Vector slices (blockIdx.z) need no reduction: as many
         // as fit one wave. A K split adds a fixed-point atomic reduction and a ticket, so it
         // is used only for long K (more than 12 tiles of 64), about one CTA per SM at most.
         const uint32_t sms = uint32_t(ctx->sm_count);
+        // The MMA's N is 2 nt (hi and lo rows) <= 256, and the accumulators take
+        // acc * 2 nt of the SM's 512 TMEM columns.
         uint32_t nz = 1;
         for (uint32_t c = 1; c <= npad / 16; ++c)
             if ((npad / 16) % c == 0 && tiles * c <= sms) nz = c;
+        while (npad / nz > 128 || acc * 2 * (npad / nz) > 512) {
+            uint32_t c = nz + 1;
+            while ((npad / 16) % c) ++c;
+            nz = c;
+        }
         const uint32_t nt = npad / nz;
         uint32_t splits = 1;
         if (ktiles > 12 && tiles * nz < sms && size_t(tiles) * nz <= kMaxTickets &&
@@ -516,7 +616,8 @@ opure_status gemv_tc(opure_ctx *ctx, const opure_gemv_args *a) {
         const uint32_t kt_per = ceil_div(ktiles, splits);
         splits = ceil_div(ktiles, kt_per);
         CUtensorMap xm;
-        if (!make_map(&xm, xp, K, 2 * npad, nt)) return OPURE_ERR_UNSUPPORTED;
+        if (!make_map(&xm, chained_in ? static_cast<const void *>(a->x_packed) : xp, K, 2 * npad, nt))
+            return OPURE_ERR_UNSUPPORTED;
 
         const uint32_t stage_bytes = acc * kTileM * 128 + 2 * nt * 128;
         // Dynamic shared memory left after the kernel's static arrays and the 1 KB used to
@@ -544,10 +645,17 @@ opure_status gemv_tc(opure_ctx *ctx, const opure_gemv_args *a) {
         p.accum = accum;
         p.tickets = tickets;
         p.st = ctx->status;
+        p.chained = chained_in;
+        p.K = K;
+        p.x_sumsq = chained_in && a->prologue == OPURE_PRO_RMSNORM ? a->x_sumsq : nullptr;
+        p.eps = a->eps;
+        p.y_packed = reinterpret_cast<__half *>(a->y_packed);
+        p.y_gain = reinterpret_cast<const __half *>(a->y_pack_gain);
+        p.y_sumsq = a->y_sumsq;
         // Request enough shared memory that no more CTAs fit on an SM than its 512 TMEM
         // columns can serve, so tcgen05.alloc never waits on a co-resident CTA.
         uint32_t ncols = 32;
-        while (ncols < acc * nt) ncols <<= 1;
+        while (ncols < acc * 2 * nt) ncols <<= 1;
         const size_t per_sm = ctx->smem_optin + 1024;
         const size_t smem = std::max<size_t>(size_t(stages) * stage_bytes + 1024, per_sm / (512 / ncols + 1) + 1);
         if (smem + fa.sharedSizeBytes > ctx->smem_optin) return OPURE_ERR_UNSUPPORTED;

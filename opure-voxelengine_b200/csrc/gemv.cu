@@ -162,19 +162,27 @@ using namespace opure;
 extern "C" opure_status opure_gemv(opure_ctx *ctx, const opure_gemv_args *a) {
     opure_status s = enter(ctx);
     if (s) return s;
-    if (!a || !a->w || !a->x || a->rows == 0 || a->cols == 0) return OPURE_ERR_INVALID_ARG;
+    if (!a || !a->w || (!a->x && !a->x_packed) || a->rows == 0 || a->cols == 0) return OPURE_ERR_INVALID_ARG;
     if (a->nvec == 0) return OPURE_OK;
     if (a->w_dtype != OPURE_W_F16 && a->w_dtype != OPURE_W_Q8) return OPURE_ERR_INVALID_ARG;
     if (a->prologue > OPURE_PRO_RMSNORM || a->epilogue > OPURE_EPI_ARGMAX) return OPURE_ERR_INVALID_ARG;
-    if (a->prologue == OPURE_PRO_RMSNORM && !a->norm_gain) return OPURE_ERR_INVALID_ARG;
+    if (a->prologue == OPURE_PRO_RMSNORM && !a->norm_gain && !a->x_packed) return OPURE_ERR_INVALID_ARG;
     if (a->epilogue != OPURE_EPI_ARGMAX && !a->y) return OPURE_ERR_INVALID_ARG;
     if (a->epilogue == OPURE_EPI_ADD && !a->residual) return OPURE_ERR_INVALID_ARG;
     if (a->epilogue == OPURE_EPI_ARGMAX && !a->argmax_keys) return OPURE_ERR_INVALID_ARG;
     const uint32_t eb = a->w_dtype == OPURE_W_F16 ? 2u : 1u;
     // 16-byte chunks: each row must be a whole number of them and start aligned.
     if ((uint64_t(a->cols) * eb) % 16 || reinterpret_cast<uintptr_t>(a->w) % 16) return OPURE_ERR_UNSUPPORTED;
-    if (a->x_stride < a->cols || (a->y && a->y_stride < a->rows)) return OPURE_ERR_INVALID_ARG;
-    if (a->x_stride % 4 || reinterpret_cast<uintptr_t>(a->x) % 16) return OPURE_ERR_UNSUPPORTED;
+    if (a->y && a->y_stride < a->rows) return OPURE_ERR_INVALID_ARG;
+    if (!a->x_packed) {
+        if (a->x_stride < a->cols) return OPURE_ERR_INVALID_ARG;
+        if (a->x_stride % 4 || reinterpret_cast<uintptr_t>(a->x) % 16) return OPURE_ERR_UNSUPPORTED;
+    }
+    if (a->x_packed || a->y_packed || a->y_sumsq) {
+        // Chained operands exist only on the tensor-core path.
+        if (!gemv_tc_eligible(ctx, a)) return OPURE_ERR_UNSUPPORTED;
+        return gemv_tc(ctx, a);
+    }
     // Many vectors sharing the weights: a dense contraction for the tensor cores.
     if (gemv_tc_eligible(ctx, a)) return gemv_tc(ctx, a);
 
@@ -206,3 +214,5 @@ extern "C" opure_status opure_gemv(opure_ctx *ctx, const opure_gemv_args *a) {
     }
     return OPURE_OK;
 }
+
+extern "C" size_t opure_packed_bytes(uint32_t nvec, uint32_t len) { return packed_bytes(nvec, len); }

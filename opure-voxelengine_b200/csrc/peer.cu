@@ -482,6 +482,7 @@ opure_status opure_gemv_allreduce(opure_ctx *ctx, opure_peer *pr, const opure_ge
     opure_status s = enter(ctx);
     if (s) return s;
     if (!pr || !a || !a->w || !a->x || !a->y || a->rows == 0 || a->cols == 0) return OPURE_ERR_INVALID_ARG;
+    if (a->x_packed || a->y_packed || a->y_sumsq) return OPURE_ERR_UNSUPPORTED;
     if (ctx->device != pr->device) return OPURE_ERR_INVALID_ARG;
     if (a->nvec == 0) return OPURE_OK;
     if (a->w_dtype != OPURE_W_F16 && a->w_dtype != OPURE_W_Q8) return OPURE_ERR_INVALID_ARG;

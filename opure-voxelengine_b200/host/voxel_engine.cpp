@@ -2,6 +2,7 @@
 #include "voxel_engine.h"
 
 #include <algorithm>
+#include <cmath>
 #include <cstring>
 
 #include "platform.h"
@@ -127,6 +128,15 @@ bool VoxelEngine::UsesFused(uint32_t n) const {
     return shape && opts_.path != 1 && (hd == 64 || hd == 128);
 }
 
+bool VoxelEngine::Chained(uint32_t n) const {
+    const graph::ModelConfig &c = graph_.Config();
+    const graph::VramPlan &p = graph_.Plan();
+    const uint32_t att = c.numHeads * c.HeadDim();
+    return !comm_ && p.wDtype == OPURE_W_F16 && !p.lmQuantized && n >= 16 && n <= 256 && n <= maxVec_ &&
+           c.hiddenSize % 64 == 0 && c.intermediateSize % 64 == 0 && att % 64 == 0 && c.hiddenSize <= 16384 &&
+           c.intermediateSize <= 16384 && att <= 16384 && buf_.packRes != nullptr;
+}
+
 void VoxelEngine::AllocBuffers() {
     const graph::ModelConfig &c = graph_.Config();
     const uint32_t B = maxVec_;  // token vectors per step (sequence slots: opts_.maxBatch)
@@ -148,6 +158,21 @@ void VoxelEngine::AllocBuffers() {
     buf_.base1 = Alloc<float>(ctx_, size_t(B) * c.hiddenSize);
     buf_.delta0 = Alloc<long long>(ctx_, size_t(B) * c.hiddenSize);
     buf_.delta1 = Alloc<long long>(ctx_, size_t(B) * c.hiddenSize);
+    if (!comm_ && B >= 16) {
+        const uint32_t nv = std::min<uint32_t>(B, 256);
+        const uint32_t att = c.numHeads * c.HeadDim();
+        auto packed = [&](uint32_t len) {
+            const size_t bytes = opure_packed_bytes(nv, len);
+            void *ptr = nullptr;
+            OPURE_CUDA_CHECK(opure_alloc(ctx_, bytes, &ptr));
+            OPURE_CUDA_CHECK(opure_fill(ctx_, ptr, 0, bytes));  // padding rows stay zero
+            return static_cast<uint16_t *>(ptr);
+        };
+        buf_.packAttn = packed(att);
+        buf_.packRes = packed(c.hiddenSize);
+        buf_.packAct = packed(c.intermediateSize);
+        buf_.sumsq = Alloc<float>(ctx_, size_t((c.hiddenSize + 127) / 128) * nv);
+    }
     if (comm_) buf_.partial = Alloc<float>(ctx_, size_t(B) * c.hiddenSize);
     buf_.sync = Alloc<uint32_t>(ctx_, 3 * size_t(c.numLayers) + 1);
     if (opts_.phaseTrace) {
@@ -158,6 +183,9 @@ void VoxelEngine::AllocBuffers() {
         OPURE_CUDA_CHECK(opure_fill(ctx_, buf_.trace, 0, traceWords_ * 8));
     }
     OPURE_CUDA_CHECK(opure_fill(ctx_, buf_.keys, 0, sizeof(unsigned long long) * B));
+    // Per-vector step state starts defined (no self-driving vector, nothing known).
+    OPURE_CUDA_CHECK(opure_fill(ctx_, buf_.flags, 0, sizeof(uint32_t) * B));
+    OPURE_CUDA_CHECK(opure_fill(ctx_, buf_.known, 0, sizeof(int32_t) * B));
     OPURE_CUDA_CHECK(opure_fill(ctx_, buf_.tokens, 0, sizeof(int32_t) * size_t(opts_.maxBatch) * maxLen_));
     // Pinned staging for the host-driven step: [in_tokens B][positions B][keys B (u64)].
     OPURE_CUDA_CHECK(opure_alloc_host(ctx_, size_t(B) * 16, &hostIo_));
@@ -209,9 +237,20 @@ void VoxelEngine::RecordLayer(uint32_t L, uint32_t n) {
     const bool q8 = plan.wDtype == OPURE_W_Q8;
     const uint64_t eb = q8 ? 1 : 2;
 
+    // Chained tensor-core operands: each GEMV's epilogue (and the attention kernel) writes the
+    // next GEMV's packed fp16 input, and the residual's sums of squares for its RMSNorm, so
+    // no pack kernel runs between them (the first layer's q;k;v packs the embedding rows).
+    const bool ch = Chained(n);
+    struct Chain {
+        const uint16_t *in = nullptr;
+        const float *inSumsq = nullptr;
+        uint16_t *out = nullptr;
+        const void *outGain = nullptr;
+        float *outSumsq = nullptr;
+    };
     auto gemv = [&](const void *w, float scale, float scale2, uint32_t rows, uint32_t cols,
                     const float *x, uint32_t xs, float *y, uint32_t ys, uint32_t pro,
-                    const void *gain, uint32_t epi, const float *res) {
+                    const void *gain, uint32_t epi, const float *res, const Chain &chain = Chain{}) {
         opure_gemv_args a{};
         a.w = w;
         a.w_dtype = plan.wDtype;
@@ -230,15 +269,41 @@ void VoxelEngine::RecordLayer(uint32_t L, uint32_t n) {
         a.eps = c.rmsNormEps;
         a.epilogue = epi;
         a.residual = res;
+        a.x_packed = chain.in;
+        a.x_sumsq = chain.inSumsq;
+        a.y_packed = chain.out;
+        a.y_pack_gain = static_cast<const uint16_t *>(chain.outGain);
+        a.y_sumsq = chain.outSumsq;
         OPURE_CUDA_CHECK(opure_gemv(ctx_, &a));
     };
     const void *inNorm = At(weights_, t.inputNorm), *postNorm = At(weights_, t.postAttNorm);
+    // The gain of the RMSNorm after this layer: the next layer's input norm, or the final norm.
+    const void *nextNorm =
+        L + 1 < c.numLayers ? At(weights_, plan.layers[L + 1].inputNorm) : At(weights_, plan.finalNorm);
+    Chain qkvIn, oChain, guChain, downChain;
+    if (ch) {
+        if (L > 0) {
+            qkvIn.in = buf_.packRes;
+            qkvIn.inSumsq = buf_.sumsq;
+        }
+        oChain.in = buf_.packAttn;
+        oChain.out = buf_.packRes;
+        oChain.outGain = postNorm;
+        oChain.outSumsq = buf_.sumsq;
+        guChain.in = buf_.packRes;
+        guChain.inSumsq = buf_.sumsq;
+        guChain.out = buf_.packAct;
+        downChain.in = buf_.packAct;
+        downChain.out = buf_.packRes;
+        downChain.outGain = nextNorm;
+        downChain.outSumsq = buf_.sumsq;
+    }
 
     // q;k;v in one pass over the concatenated rows (three passes for int8, whose
     // per-tensor scales differ).
     if (!q8) {
         gemv(At(weights_, t.wqkv), 1.f, 1.f, qkvRows, h, buf_.x, h, buf_.qkv, qkvRows, OPURE_PRO_RMSNORM,
-             inNorm, OPURE_EPI_STORE, nullptr);
+             inNorm, OPURE_EPI_STORE, nullptr, qkvIn);
     } else {
         const uint32_t qr = lg.heads * hd, kr = lg.kvHeads * hd;
         gemv(At(weights_, t.wqkv), t.sq, t.sq, qr, h, buf_.x, h, buf_.qkv, qkvRows, OPURE_PRO_RMSNORM,
@@ -264,11 +329,12 @@ void VoxelEngine::RecordLayer(uint32_t L, uint32_t n) {
     a.split_tokens = 0;
     a.scratch = AttnScratch(n, &a.scratch_bytes);
     a.kv = kv;
+    a.out_packed = ch ? buf_.packAttn : nullptr;
     OPURE_CUDA_CHECK(opure_attention(ctx_, &a));
     if (!comm_) {
         // o_proj + residual, in place on the residual stream.
         gemv(At(weights_, t.wo), t.so, t.so, h, h, buf_.attn, h, buf_.x, h, OPURE_PRO_NONE, nullptr, OPURE_EPI_ADD,
-             buf_.x);
+             buf_.x, oChain);
     } else if (peer_) {
         // Tensor parallel over NVLink peer memory: one kernel computes this shard's partial
         // o_proj sum, exchanges it with every rank and adds the total to the residual.
@@ -283,11 +349,11 @@ void VoxelEngine::RecordLayer(uint32_t L, uint32_t n) {
     }
     // gate;up with the post-attention norm, SwiGLU epilogue.
     gemv(At(weights_, t.wgu), t.sgate, t.sup, ff, h, buf_.x, h, buf_.h, ff, OPURE_PRO_RMSNORM, postNorm,
-         OPURE_EPI_SWIGLU, nullptr);
+         OPURE_EPI_SWIGLU, nullptr, guChain);
     if (!comm_) {
         // down_proj + residual.
         gemv(At(weights_, t.wdown), t.sdown, t.sdown, h, ff, buf_.h, ff, buf_.x, h, OPURE_PRO_NONE, nullptr,
-             OPURE_EPI_ADD, buf_.x);
+             OPURE_EPI_ADD, buf_.x, downChain);
     } else if (peer_) {
         TpGemvAllreduce(At(weights_, t.wdown), t.sdown, h, ff, buf_.h, ff, n);
     } else {
@@ -403,6 +469,11 @@ void VoxelEngine::RecordStep(uint32_t n, bool logits) {
     a.eps = c.rmsNormEps;
     a.epilogue = OPURE_EPI_ARGMAX;
     a.argmax_keys = buf_.keys;
+    if (Chained(n)) {
+        // The last down_proj left the final-norm-gained residual packed.
+        a.x_packed = buf_.packRes;
+        a.x_sumsq = buf_.sumsq;
+    }
     OPURE_CUDA_CHECK(opure_gemv(ctx_, &a));
     if (peer_ && n <= OPURE_PEER_MAX_KEYS) {
         // Vocabulary shards: global indices and the largest key over all shards in one
@@ -478,7 +549,10 @@ void VoxelEngine::ResetSequences(const std::vector<std::vector<uint32_t>> &promp
     OPURE_CHECK(reserve <= maxLen_, "sequence exceeds the engine's maxLen");
     const graph::ModelConfig &c = graph_.Config();
     std::vector<int32_t> seq(n), pos(n, 0), known(n);
-    std::vector<uint32_t> flags(n, automatic ? uint32_t(OPURE_VEC_AUTO) : 0u);
+    // Flags of every vector slot: the n sequences' vectors self-drive or not, and no other
+    // slot self-drives (a chunked prefill step uses more vectors than there are sequences).
+    std::vector<uint32_t> flags(maxVec_, 0u);
+    std::fill(flags.begin(), flags.begin() + n, automatic ? uint32_t(OPURE_VEC_AUTO) : 0u);
     for (uint32_t v = 0; v < n; ++v) {
         OPURE_CHECK(!prompts[v].empty(), "empty prompt");
         OPURE_CHECK(prompts[v].size() <= reserve, "prompt exceeds the reserved length");
@@ -495,7 +569,7 @@ void VoxelEngine::ResetSequences(const std::vector<std::vector<uint32_t>> &promp
     OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.seq, seq.data(), n * 4));
     OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.pos, pos.data(), n * 4));
     OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.known, known.data(), n * 4));
-    OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.flags, flags.data(), n * 4));
+    OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.flags, flags.data(), flags.size() * 4));
     hostDriven_ = !automatic;
     seqIdentity_ = true;
     OPURE_CUDA_CHECK(opure_fill(ctx_, buf_.keys, 0, n * 8));
@@ -685,11 +759,11 @@ void VoxelEngine::SetVectors(const int32_t *seq, const int32_t *pos, const int32
     OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.pos, pos, n * 4));
     if (tok) OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.inTokens, tok, n * 4));
     seqIdentity_ = false;
-    if (!hostDriven_) {
-        const std::vector<uint32_t> zero(maxVec_, 0u);
-        OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.flags, zero.data(), zero.size() * 4));
-        hostDriven_ = true;
-    }
+    // Every vector of the step takes its token from the host: clear the self-driving flag of
+    // all n (earlier calls may have set flags for fewer vectors, e.g. one per prompt).
+    const std::vector<uint32_t> zero(n, 0u);
+    OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.flags, zero.data(), n * 4));
+    hostDriven_ = true;
 }
 
 void VoxelEngine::SetAutoVectors(const int32_t *pos, const int32_t *known, uint32_t n) {
@@ -843,6 +917,29 @@ void VoxelEngine::PoisonBanks(float fill) {
     poison(buf_.attn, size_t(B) * c.hiddenSize);
     poison(buf_.h, size_t(B) * c.intermediateSize);
     poison(buf_.logits, size_t(B) * c.vocabSize);
+    {
+        // Step state the host sets: every slot self-driving with nothing known, so a step
+        // whose vectors the host did not set up would take tokens from stale keys.
+        const std::vector<uint32_t> autoFlags(B, uint32_t(OPURE_VEC_AUTO));
+        const std::vector<int32_t> none(B, 0);
+        OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.flags, autoFlags.data(), B * 4));
+        OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.known, none.data(), B * 4));
+        OPURE_CUDA_CHECK(opure_sync(ctx_, 60000));
+    }
+    if (buf_.packRes) {
+        // Chained tensor-core operands: fp16 pairs (the fill's fp16 bits) and the sums of squares.
+        const uint32_t nv = std::min<uint32_t>(B, 256), att = c.numHeads * c.HeadDim();
+        const uint16_t h = std::isnan(fill) ? uint16_t(0x7e00) : uint16_t(0x3c00);  // NaN, or 1.0
+        auto poison16 = [&](uint16_t *p, size_t bytes) {
+            std::vector<uint16_t> pat(bytes / 2, h);
+            OPURE_CUDA_CHECK(opure_h2d(ctx_, p, pat.data(), bytes));
+            OPURE_CUDA_CHECK(opure_sync(ctx_, 60000));
+        };
+        poison16(buf_.packAttn, opure_packed_bytes(nv, att));
+        poison16(buf_.packRes, opure_packed_bytes(nv, c.hiddenSize));
+        poison16(buf_.packAct, opure_packed_bytes(nv, c.intermediateSize));
+        poison(buf_.sumsq, size_t((c.hiddenSize + 127) / 128) * nv);
+    }
 }
 
 void VoxelEngine::LoadKv(uint32_t seq, const uint16_t *kvData, uint32_t len) {

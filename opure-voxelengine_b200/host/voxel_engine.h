@@ -190,9 +190,17 @@ public:
         uint32_t *sync = nullptr;  // grid-barrier words of the persistent decode kernel
         unsigned long long *trace = nullptr;  // its phase timestamps (EngineOptions.phaseTrace)
         unsigned long long *prefillKeys = nullptr;  // [maxBatch] chunked prefill's last-token keys
+        // Chained tensor-core operands (steps of 16..256 vectors, fp16 weights): the packed
+        // inputs of the o_proj (attention output), gate;up / next q;k;v / lm_head (gained
+        // residual) and down_proj (SwiGLU activation), and the residual's per-tile sums of
+        // squares for the consumer's RMSNorm.
+        uint16_t *packAttn = nullptr, *packRes = nullptr, *packAct = nullptr;
+        float *sumsq = nullptr;
     };
     // True when steps of n vectors run on opure_decode_fused.
     bool UsesFused(uint32_t n) const;
+    // True when steps of n vectors run the per-op tensor-core GEMVs with chained operands.
+    bool Chained(uint32_t n) const;
     const Buffers &Buf() const { return buf_; }
 
 private:

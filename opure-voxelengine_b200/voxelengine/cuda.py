@@ -38,7 +38,7 @@ class KvLayout(C.Structure):
 class AttnArgs(C.Structure):
     _fields_ = [("q", P), ("out", P), ("seq", P), ("seq_len", P), ("n", u32), ("n_q", u32),
                 ("n_heads", u32), ("scale", f32), ("max_ctx", u32), ("split_tokens", u32),
-                ("scratch", P), ("scratch_bytes", sz), ("kv", KvLayout)]
+                ("scratch", P), ("scratch_bytes", sz), ("kv", KvLayout), ("out_packed", P)]
 
 
 class GemvArgs(C.Structure):
@@ -46,7 +46,8 @@ class GemvArgs(C.Structure):
                 ("scale_w2", f32), ("rows", u32),
                 ("cols", u32), ("nvec", u32), ("x", P), ("x_stride", u32), ("y", P),
                 ("y_stride", u32), ("prologue", u32), ("norm_gain", P), ("eps", f32),
-                ("epilogue", u32), ("residual", P), ("argmax_keys", P)]
+                ("epilogue", u32), ("residual", P), ("argmax_keys", P),
+                ("x_packed", P), ("x_sumsq", P), ("y_packed", P), ("y_pack_gain", P), ("y_sumsq", P)]
 
 
 class StepIO(C.Structure):
@@ -130,6 +131,8 @@ def lib() -> C.CDLL:
         L.opure_comm_unique_id.restype = C.c_int
         L.opure_attention_scratch_bytes.argtypes = [u32, u32, u32, u32, u32, u32, u32]
         L.opure_attention_scratch_bytes.restype = sz
+        L.opure_packed_bytes.argtypes = [u32, u32]
+        L.opure_packed_bytes.restype = sz
         _lib = L
     return _lib
 
@@ -160,6 +163,11 @@ def check(status: int, what: str) -> None:
 def attention_scratch_bytes(n, n_q, n_heads, n_kv, head_dim, max_ctx, split_tokens=0) -> int:
     return int(lib().opure_attention_scratch_bytes(n, n_q, n_heads, n_kv, head_dim, max_ctx,
                                                    split_tokens))
+
+
+def packed_bytes(nvec: int, length: int) -> int:
+    """Bytes of a chained tensor-core operand (fp16 hi/lo pairs of nvec vectors)."""
+    return int(lib().opure_packed_bytes(nvec, length))
 
 
 class DeviceBuffer:

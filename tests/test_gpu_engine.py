@@ -391,6 +391,22 @@ def test_sliding_window_chunked_prefill_and_limits(models, small):
         ve.Engine(models["small"], max_len=128, page_size=page, kv_window=40)
 
 
+@pytest.mark.parametrize("window", [0, 48])
+def test_chunked_prefill_with_poisoned_buffers(models, small, window):
+    # A chunked prefill step has more token vectors than there are sequences: every vector's
+    # step state (flags, known length) must be set by the host for that step, not left from
+    # earlier use of the slot. Poison-and-walk with every slot marked self-driving, NaN
+    # activations and NaN chained operands; one prompt in a two-sequence engine.
+    page = 16
+    p = ve.prompt(600, SMALL["vocab"], 40)
+    kw = dict(kv_window=window) if window else {}
+    with ve.Engine(models["small"], max_batch=2, max_len=128, page_size=page, prefill_chunk=16, **kw) as eng:
+        eng.poison(float("nan"))
+        out, _ = eng.generate([p], 12)
+    want, margins = windowed_oracle(small, p, 12, page, window // page) if window else small.generate(p, 12)
+    assert_tokens(out[0], want, margins)
+
+
 # ---- Generate's stop rules (Opure_VoxelEngine.cpp:904,918-933) ------------------------
 def _with_config(src, dst, **edits):
     """A model directory sharing src's weights with config.json edited."""

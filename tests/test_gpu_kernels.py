@@ -424,6 +424,106 @@ def test_gemv_tc_matches_cuda_core_path(ctx):
     assert rel_err(y16[:15], y15) < TC_REL
 
 
+def test_gemv_tc_chained_operands(ctx):
+    """A decode layer's GEMV chain on packed operands: o_proj-style ADD producing the gained
+    residual's packed form and per-tile sums of squares, gate;up with the RMSNorm applied from
+    those sums and a packed SwiGLU output, down_proj ADD producing the next packed residual,
+    and a normed STORE consumer. Each stage against the oracle on the previous stage's fp32
+    output (what its packed operand encodes)."""
+    rng = np.random.default_rng(43)
+    n, h, ff = 64, 576, 1536
+    w1 = f16(rng.standard_normal((h, h)).astype(np.float32) * 0.02)
+    w2 = f16(rng.standard_normal((2 * ff, h)).astype(np.float32) * 0.02)
+    w3 = f16(rng.standard_normal((h, ff)).astype(np.float32) * 0.02)
+    w4 = f16(rng.standard_normal((960, h)).astype(np.float32) * 0.02)
+    g2 = f16((0.5 + rng.random(h)).astype(np.float32))
+    g4 = f16((0.5 + rng.random(h)).astype(np.float32))
+    a = rng.standard_normal((n, h)).astype(np.float32)
+    r = rng.standard_normal((n, h)).astype(np.float32) * 3.0
+    tiles = (h + 127) // 128
+    pk_res = ctx.buffer(cu.packed_bytes(n, h)).fill(0)
+    pk_act = ctx.buffer(cu.packed_bytes(n, ff)).fill(0)
+    ss = ctx.buffer(4 * tiles * n).fill(0xFF)
+    dg2, dg4 = ctx.to_device(g2), ctx.to_device(g4)
+
+    def call(w, rows, cols, x=None, x_packed=None, sums=None, pro=cu.PRO_NONE, epi=cu.EPI_STORE,
+             residual=None, y_packed=None, y_gain=None, y_sumsq=None):
+        dw = ctx.to_device(w)
+        dy = ctx.buffer(n * rows * 4).fill(0xFF)
+        args = cu.GemvArgs()
+        args.w, args.w_dtype, args.rows, args.cols, args.nvec = dw.ptr, cu.W_F16, rows, cols, n
+        if x is not None:
+            dx = ctx.to_device(np.ascontiguousarray(x, np.float32))
+            args.x, args.x_stride = dx.ptr, cols
+        args.y, args.y_stride = dy.ptr, rows
+        args.prologue, args.epilogue, args.eps = pro, epi, 1e-5
+        if residual is not None:
+            args.residual = ctx.to_device(np.ascontiguousarray(residual, np.float32)).ptr
+        args.x_packed = x_packed.ptr if x_packed is not None else None
+        args.x_sumsq = sums.ptr if sums is not None else None
+        args.y_packed = y_packed.ptr if y_packed is not None else None
+        args.y_pack_gain = y_gain.ptr if y_gain is not None else None
+        args.y_sumsq = y_sumsq.ptr if y_sumsq is not None else None
+        ctx.gemv(args)
+        out = dy.download(np.float32, (n, rows))
+        assert ctx.last_error() == 0
+        return out
+
+    # o_proj + residual from fp32 inputs, emitting g2 * x packed and the sums of squares.
+    y1 = call(w1, h, h, x=a, epi=cu.EPI_ADD, residual=r, y_packed=pk_res, y_gain=dg2, y_sumsq=ss)
+    assert rel_err(y1, r + oracle.gemv_f16(w1, a)) < TC_REL
+    sums = ss.download(np.float32, (tiles, n)).sum(axis=0)
+    assert np.allclose(sums, (y1.astype(np.float64) ** 2).sum(axis=1), rtol=1e-5)
+    # gate;up + SwiGLU with the RMSNorm from the packed operand, emitting the activation.
+    y2 = call(w2, ff, h, x_packed=pk_res, sums=ss, pro=cu.PRO_RMSNORM, epi=cu.EPI_SWIGLU, y_packed=pk_act)
+    xn = np.stack([oracle.rmsnorm(y1[v], oracle.f16_to_f32(g2), 1e-5) for v in range(n)])
+    gu = oracle.gemv_f16(w2, xn)
+    want2 = np.stack([oracle.swiglu(gu[v, :ff], gu[v, ff:]) for v in range(n)])
+    assert rel_err(y2, want2) < TC_REL
+    # down_proj + residual from the packed activation, emitting g4 * x packed.
+    y3 = call(w3, h, ff, x_packed=pk_act, epi=cu.EPI_ADD, residual=y1, y_packed=pk_res, y_gain=dg4, y_sumsq=ss)
+    assert rel_err(y3, y1 + oracle.gemv_f16(w3, y2)) < TC_REL
+    # A normed consumer of that (the next q;k;v).
+    y4 = call(w4, 960, h, x_packed=pk_res, sums=ss, pro=cu.PRO_RMSNORM)
+    xn4 = np.stack([oracle.rmsnorm(y3[v], oracle.f16_to_f32(g4), 1e-5) for v in range(n)])
+    assert rel_err(y4, oracle.gemv_f16(w4, xn4)) < TC_REL
+
+
+def test_gemv_tc_chained_out_of_range_is_reported(ctx):
+    # A packed value beyond fp16's range cannot be represented: the kernel reports it in the
+    # status word instead of writing an infinity.
+    rng = np.random.default_rng(44)
+    n, h = 16, 576
+    w = f16(rng.standard_normal((h, h)).astype(np.float32) * 0.02)
+    x = rng.standard_normal((n, h)).astype(np.float32)
+    r = np.zeros((n, h), np.float32)
+    r[3, 100] = 1.0e5
+    pk = ctx.buffer(cu.packed_bytes(n, h)).fill(0)
+    dw, dx, dr = ctx.to_device(w), ctx.to_device(x), ctx.to_device(r)
+    dy = ctx.buffer(n * h * 4)
+    args = cu.GemvArgs()
+    args.w, args.w_dtype, args.rows, args.cols, args.nvec = dw.ptr, cu.W_F16, h, h, n
+    args.x, args.x_stride, args.y, args.y_stride = dx.ptr, h, dy.ptr, h
+    args.epilogue, args.residual, args.y_packed = cu.EPI_ADD, dr.ptr, pk.ptr
+    ctx.gemv(args)
+    ctx.sync()
+    assert ctx.last_error() == cu.ERR_DEVICE_BOUNDS
+
+
+def test_gemv_chained_needs_tensor_core_shape(ctx):
+    # Fewer than 16 vectors run on the CUDA cores, which have no packed operands.
+    n, h = 8, 576
+    w = np.zeros((h, h), np.float16)
+    pk = ctx.buffer(cu.packed_bytes(16, h)).fill(0)
+    dw, dy = ctx.to_device(w), ctx.buffer(n * h * 4)
+    args = cu.GemvArgs()
+    args.w, args.w_dtype, args.rows, args.cols, args.nvec = dw.ptr, cu.W_F16, h, h, n
+    args.x_packed, args.y, args.y_stride = pk.ptr, dy.ptr, h
+    with pytest.raises(cu.OpureError) as e:
+        ctx.gemv(args)
+    assert e.value.status == cu.ERR_UNSUPPORTED
+
+
 # ---- RoPE + KV append, embedding ------------------------------------------------------
 @pytest.mark.parametrize("pos", [0, 1, 157, 4095])
 def test_rope_kv_append(ctx, pos):
