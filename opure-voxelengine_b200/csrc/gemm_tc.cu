@@ -16,9 +16,10 @@
 //          M=128 and N=2 nt (hi and lo vectors together, fp16 in, fp32 out), so each weight
 //          tile is read once for both halves, into a TMEM accumulator whose first nt
 //          columns hold W.hi and next nt W.lo (a second one for the SwiGLU up half), and
-//          frees each stage with tcgen05.commit. The four warps then read the accumulator rows with tcgen05.ld
-//          (warp w owns TMEM lanes 32w..32w+31 = tile rows) and apply the epilogue:
-//          store, residual add, SwiGLU, or argmax keys (+ logits). With a K split every
+//          frees each stage with tcgen05.commit. The eight warps then read the accumulator
+//          rows with tcgen05.ld (warps w and w + 4 share TMEM lanes 32 (w % 4) .. = tile
+//          rows, each taking half of every 16-column chunk) and apply the epilogue: store,
+//          residual add, SwiGLU, or argmax keys (+ logits). With a K split every
 //          CTA adds its sums into a 64-bit fixed-point accumulator with integer atomics
 //          and the last CTA of the tile (ticket counter) converts them and runs the
 //          epilogue, so results do not depend on the order the splits finish in.
@@ -47,7 +48,8 @@ namespace {
 
 constexpr uint32_t kTileM = 128;   // weight rows per tile = TMEM lanes
 constexpr uint32_t kTileK = 64;    // 64 fp16 = one 128-byte swizzle row
-constexpr uint32_t kThreads = 128;
+constexpr uint32_t kThreads = 256;  // 8 warps: warp w reads TMEM lanes 32 (w % 4) .., columns half w / 4
+constexpr uint32_t kHalfCols = 8;   // epilogue columns per thread per 16-column chunk
 constexpr uint32_t kMaxN = 256;    // vectors per pass (MMA N limit)
 constexpr uint32_t kMaxStages = 8;
 constexpr uint32_t kMaxTickets = 4096;
@@ -111,20 +113,16 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
                  : "memory");
 }
 
-// 16 consecutive fp32 accumulator columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-    uint32_t r[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
-        "%14, %15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr)
-        : "memory");
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+// Issues the load of 8 consecutive fp32 accumulator columns of this thread's TMEM lane
+// into r (valid after tmem_wait_ld).
+__device__ __forceinline__ void tmem_ld8_issue(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr)
+                 : "memory");
 }
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v) {
 #pragma unroll
@@ -240,7 +238,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __shared__ int fail, last;
     __shared__ uint32_t issued_s, consumed_s;
     __shared__ float s_scale[kMaxN];
-    __shared__ float s_red[kThreads / 32][16];
+    __shared__ float s_red[4][16];
+    __shared__ __align__(16) __half s_pk[2][16][kTileM];  // packed output chunk, transposed
 
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t tile = blockIdx.x, split = blockIdx.y;
@@ -278,6 +277,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = tmem_base;
 
+    // The next norm's gain of this thread's epilogue row is a weight too: requested now,
+    // converted only in the epilogue.
+    const uint32_t erow = m0 + (warp & 3u) * 32 + lane;
+    __half gain_h = __float2half_rn(1.f);
+    if (p.y_packed && p.y_gain && erow < p.rows) gain_h = p.y_gain[erow];
     // Producer (warp 0, one lane). Weight tiles do not depend on earlier kernels: the
     // first stages are requested before waiting on them; the packed vectors only after.
     const uint32_t pre = min(p.stages, nk);
@@ -289,25 +293,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     grid_dependency_wait();
     grid_dependents_launch();
-    // Per-vector scales written by the pack kernel, or for a chained input 1 / rms from the
-    // producer's per-tile sums of squares (read after the wait).
-    for (uint32_t v = threadIdx.x; v < p.npad; v += blockDim.x) {
-        float sc = 0.f;
-        if (v < p.n) {
-            if (!p.chained) {
-                sc = p.xscale[v];
-            } else if (p.x_sumsq) {
-                double ss = 0.0;
-                for (uint32_t t = 0; t < (p.K + kTileM - 1) / kTileM; ++t) ss += double(__ldcg(p.x_sumsq + size_t(t) * p.n + v));
-                // The GEMV prologue's RMSNorm (RMSNormMain, Opure_RMSNorm.usf:31-79).
-                sc = float(1.0 / sqrt(ss / double(p.K) + double(p.eps)));
-            } else {
-                sc = 1.f;
-            }
-        }
-        s_scale[v] = sc;
-    }
-
     if (warp == 0) {
         if (lane == 0) {
             for (uint32_t i = 0; i < pre; ++i) {
@@ -332,7 +317,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // The other lanes park here rather than spinning beside the issuing lane.
         __syncwarp();
-    } else if (warp == 1) {
+    } else if (warp >= 2) {
+        // Per-vector scales written by the pack kernel, or for a chained input 1 / rms from
+        // the producer's per-tile sums of squares; used only by the epilogue.
+        for (uint32_t v = threadIdx.x - 64; v < p.npad; v += blockDim.x - 64) {
+            float sc = 0.f;
+            if (v < p.n) {
+                if (!p.chained) {
+                    sc = p.xscale[v];
+                } else if (p.x_sumsq) {
+                    double ss = 0.0;
+                    for (uint32_t t = 0; t < (p.K + kTileM - 1) / kTileM; ++t)
+                        ss += double(__ldcg(p.x_sumsq + size_t(t) * p.n + v));
+                    // The GEMV prologue's RMSNorm (RMSNormMain, Opure_RMSNorm.usf:31-79).
+                    sc = float(1.0 / sqrt(ss / double(p.K) + double(p.eps)));
+                } else {
+                    sc = 1.f;
+                }
+            }
+            s_scale[v] = sc;
+        }
+    }
+    if (warp == 1) {
         if (lane == 0) {
             // MMA issuer: per 64-wide K tile, four K=16 steps (32 bytes along the swizzled
             // rows) of hi and lo products.
@@ -377,19 +383,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (threadIdx.x == 0)
             for (uint32_t i = consumed_s; i < issued_s; ++i) mbar_wait(&full[i % p.stages], (i / p.stages) & 1u);
     } else {
-        const uint32_t lrow = warp * 32 + lane;
+        // Warps w and w + 4 share TMEM lanes 32 (w % 4) .. (tile rows); in each 16-column
+        // chunk warp w takes columns 0..7 and warp w + 4 columns 8..15.
+        const uint32_t quarter = warp & 3u, half = warp >> 2;
+        const uint32_t lrow = quarter * 32 + lane;
         const uint32_t row = m0 + lrow;
-        const uint32_t taddr = tmem + ((warp * 32) << 16);
+        const uint32_t taddr = tmem + ((quarter * 32) << 16);
         const uint32_t acc_cols = kAcc * nt;
-        // Result columns c .. c+15 (accumulator c / nt) of this thread's row: W.hi plus
-        // W.lo (scaled by 2^-11 for a chained operand).
-        auto tm_col = [&](uint32_t c, float (&r)[16]) {
+        // Result columns c .. c+7 (accumulator c / nt) of this thread's row: W.hi plus W.lo
+        // (scaled by 2^-11 for a chained operand).
+        auto tm_col = [&](uint32_t c, float (&r)[kHalfCols]) {
             const uint32_t col = (c / nt) * 2 * nt + c % nt;
-            float l[16];
-            tmem_ld16(taddr + col, r);
-            tmem_ld16(taddr + col + nt, l);
+            uint32_t h[kHalfCols], l[kHalfCols];
+            tmem_ld8_issue(taddr + col, h);
+            tmem_ld8_issue(taddr + col + nt, l);
+            tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 16; ++j) r[j] = fmaf(l[j], lo_scale, r[j]);
+            for (int j = 0; j < int(kHalfCols); ++j) r[j] = fmaf(__uint_as_float(l[j]), lo_scale, __uint_as_float(h[j]));
         };
         bool run_epi = true;
         long long *acc64 = nullptr;
@@ -398,11 +408,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             // accumulator; integer adds are associative, so the total does not depend on
             // the order the splits arrive in. Column-major: a warp's adds are contiguous.
             acc64 = p.accum + size_t(slice) * acc_cols * kTileM;
-            for (uint32_t c0 = 0; c0 < acc_cols; c0 += 16) {
-                float r[16];
+            for (uint32_t c0 = half * kHalfCols; c0 < acc_cols; c0 += 16) {
+                float r[kHalfCols];
                 tm_col(c0, r);
 #pragma unroll
-                for (int j = 0; j < 16; ++j)
+                for (int j = 0; j < int(kHalfCols); ++j)
                     atomicAdd(reinterpret_cast<unsigned long long *>(acc64 + size_t(c0 + j) * kTileM + lrow),
                               static_cast<unsigned long long>(to_fix(r[j])));
             }
@@ -418,40 +428,41 @@ __global__ void __launch_bounds__(kThreads, 1)
             __threadfence();
         }
         if (run_epi) {
-            // Full sums of 16 columns of this thread's row (the last split also clears the
+            // Full sums of this thread's 8 columns from c (the last split also clears the
             // accumulator for the next call).
-            auto column = [&](uint32_t c, float (&r)[16]) {
+            auto column = [&](uint32_t c, float (&r)[kHalfCols]) {
                 if (p.splits == 1) {
                     tm_col(c, r);
                 } else {
-                    long long a[16];
+                    long long a[kHalfCols];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) a[j] = __ldcg(acc64 + size_t(c + j) * kTileM + lrow);
+                    for (int j = 0; j < int(kHalfCols); ++j) a[j] = __ldcg(acc64 + size_t(c + j) * kTileM + lrow);
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
+                    for (int j = 0; j < int(kHalfCols); ++j) {
                         acc64[size_t(c + j) * kTileM + lrow] = 0;
                         r[j] = float(double(a[j]) * kFixInv);
                     }
                 }
             };
-            // Per 16 columns: every global load (the residual) is issued before any store,
-            // and the vector scales come from shared memory, so a thread pays one memory
-            // round trip per chunk rather than one per column.
+            // Per chunk: every global load (the residual) is issued before any store, and the
+            // vector scales come from shared memory, so a thread pays one memory round trip
+            // per chunk rather than one per column.
             const bool in = row < p.rows;
-            const float ygain = (p.y_packed && p.y_gain && in) ? __half2float(p.y_gain[row]) : 1.f;
-            for (uint32_t c0 = 0; c0 < nt; c0 += 16) {
-                float outv[16];
-                float g[16], u[16], res[16];
+            const float ygain = __half2float(gain_h);
+            for (uint32_t c16 = 0; c16 < nt; c16 += 16) {
+                const uint32_t c0 = c16 + half * kHalfCols;  // this thread's first column
+                float outv[kHalfCols];
+                float g[kHalfCols], u[kHalfCols], res[kHalfCols];
                 column(c0, g);
                 if (kSwiglu) column(nt + c0, u);
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
+                for (int j = 0; j < int(kHalfCols); ++j) {
                     res[j] = 0.f;
                     if constexpr (EPI == OPURE_EPI_ADD)
-                        if (in && n0 + c0 + j < p.n) res[j] = p.residual[size_t(n0 + c0 + j) * p.y_stride + row];
+                        if (in && n0 + c0 + j < p.n) res[j] = __ldcg(p.residual + size_t(n0 + c0 + j) * p.y_stride + row);
                 }
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
+                for (int j = 0; j < int(kHalfCols); ++j) {
                     const uint32_t v = n0 + c0 + j;
                     const bool ok = in && v < p.n;
                     const float val = g[j] * s_scale[v];
@@ -475,23 +486,42 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
                 if constexpr (EPI != OPURE_EPI_ARGMAX) {
-                    // The next GEMV's packed operand, and this tile's sums of squares.
-                    if (p.y_packed)
+                    // The next GEMV's packed operand: each thread's hi/lo halves go to shared
+                    // memory by vector, then every vector's 128-row slice leaves as 16-byte
+                    // stores (rows is a multiple of 8).
+                    if (p.y_packed) {
 #pragma unroll
-                        for (int j = 0; j < 16; ++j)
-                            if (in && n0 + c0 + j < p.n)
-                                store_packed(p.y_packed, p.npad, p.rows, n0 + c0 + j, row, outv[j] * ygain, p.st, 63);
-                    if (p.y_sumsq) {
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            const float sq = warp_sum((in && n0 + c0 + j < p.n) ? outv[j] * outv[j] : 0.f);
-                            if (lane == 0) s_red[warp][j] = sq;
+                        for (int j = 0; j < int(kHalfCols); ++j) {
+                            float v = outv[j] * ygain;
+                            if (!(fabsf(v) < 65504.f)) {
+                                if (in && n0 + c0 + j < p.n) report(p.st, OPURE_ERR_DEVICE_BOUNDS, 63, row);
+                                v = 0.f;
+                            }
+                            const __half hi = __float2half_rn(v);
+                            s_pk[0][half * kHalfCols + j][lrow] = hi;
+                            s_pk[1][half * kHalfCols + j][lrow] = __float2half_rn((v - __half2float(hi)) * 2048.f);
                         }
                         __syncthreads();
-                        if (threadIdx.x < 16 && n0 + c0 + threadIdx.x < p.n) {
+                        for (uint32_t idx = threadIdx.x; idx < 2 * 16 * (kTileM / 8); idx += blockDim.x) {
+                            const uint32_t r = idx / (kTileM / 8), c = idx % (kTileM / 8);
+                            const uint32_t h = r / 16, j = r % 16, v = n0 + c16 + j;
+                            if (v < p.n && m0 + c * 8 < p.rows)
+                                *reinterpret_cast<uint4 *>(p.y_packed + (size_t(h) * p.npad + v) * p.rows + m0 + c * 8) =
+                                    *reinterpret_cast<const uint4 *>(&s_pk[h][j][c * 8]);
+                        }
+                        __syncthreads();
+                    }
+                    if (p.y_sumsq) {
+#pragma unroll
+                        for (int j = 0; j < int(kHalfCols); ++j) {
+                            const float sq = warp_sum((in && n0 + c0 + j < p.n) ? outv[j] * outv[j] : 0.f);
+                            if (lane == 0) s_red[quarter][half * kHalfCols + j] = sq;
+                        }
+                        __syncthreads();
+                        if (threadIdx.x < 16 && n0 + c16 + threadIdx.x < p.n) {
                             float t = 0.f;
-                            for (uint32_t w = 0; w < kThreads / 32; ++w) t += s_red[w][threadIdx.x];
-                            p.y_sumsq[size_t(tile) * p.n + n0 + c0 + threadIdx.x] = t;
+                            for (uint32_t q = 0; q < 4; ++q) t += s_red[q][threadIdx.x];
+                            p.y_sumsq[size_t(tile) * p.n + n0 + c16 + threadIdx.x] = t;
                         }
                         __syncthreads();
                     }

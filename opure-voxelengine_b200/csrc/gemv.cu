@@ -54,7 +54,14 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(GemvParams p) {
 
     grid_dependency_wait();
     grid_dependents_launch();
-    stage_vectors<NV>(p.x, p.x_stride, p.cols, PRO == OPURE_PRO_RMSNORM, p.gain, p.eps, xs, red);
+    // int8 chunks span 16 elements: their vectors are staged chunk-interleaved (no bank
+    // conflicts on the 64-byte-per-lane reads); fp16 keeps the plain layout, measured faster.
+    constexpr bool kIL = WT == OPURE_W_Q8;
+    if constexpr (kIL)
+        stage_vectors_il<NV, WTraits<WT>::kElems>(p.x, p.x_stride, p.cols, PRO == OPURE_PRO_RMSNORM, p.gain, p.eps,
+                                                  xs, red);
+    else
+        stage_vectors<NV>(p.x, p.x_stride, p.cols, PRO == OPURE_PRO_RMSNORM, p.gain, p.eps, xs, red);
 
     unsigned long long best[NV];
 #pragma unroll
@@ -64,11 +71,11 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(GemvParams p) {
         const uint32_t row0 = g * kRows;
         const uint32_t valid = min(uint32_t(kRows), p.rows - row0);
         float acc[kRows][NV];
-        dot_rows<WT, NV, kRows>(p.w, p.pitch, row0, valid, p.nchunks, xs, p.cols, acc, pre, g == g0);
+        dot_rows<WT, NV, kRows, kIL>(p.w, p.pitch, row0, valid, p.nchunks, xs, p.cols, acc, pre, g == g0);
         float acc_up[kRows][NV];
         if constexpr (EPI == OPURE_EPI_SWIGLU)
-            dot_rows<WT, NV, kRows>(p.w + size_t(p.rows) * p.pitch, p.pitch, row0, valid, p.nchunks,
-                                    xs, p.cols, acc_up, pre_up, g == g0);
+            dot_rows<WT, NV, kRows, kIL>(p.w + size_t(p.rows) * p.pitch, p.pitch, row0, valid, p.nchunks,
+                                          xs, p.cols, acc_up, pre_up, g == g0);
 #pragma unroll
         for (int r = 0; r < kRows; ++r) {
 #pragma unroll

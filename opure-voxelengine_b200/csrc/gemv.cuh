@@ -68,11 +68,12 @@ __device__ __forceinline__ void prefetch_rows(RowPrefetch<R> &pf, const uint8_t 
 }
 
 // Chunk-batched dot products of R rows (row0 .. row0+R-1, rows >= rows_valid are
-// skipped) against NV vectors xs[v * xs_stride + i] in shared memory.
+// skipped) against NV vectors in shared memory: xs[v * xs_stride + i], or with IL the
+// chunk-interleaved layout of stage_vectors_il (xs_stride ignored).
 // Row r starts at W + (row0 + r) * pitch (bytes); a row has nchunks 16-byte chunks.
 // With use_pre, the first batch comes from `pre` (prefetch_rows of the same rows).
 // On return every lane holds the full sums in acc.
-template <int WT, int NV, int R>
+template <int WT, int NV, int R, bool IL = false>
 __device__ __forceinline__ void dot_rows(const uint8_t *__restrict__ W, size_t pitch,
                                          uint32_t row0, uint32_t rows_valid, uint32_t nchunks,
                                          const float *__restrict__ xs, uint32_t xs_stride,
@@ -111,12 +112,22 @@ __device__ __forceinline__ void dot_rows(const uint8_t *__restrict__ W, size_t p
             for (int r = 0; r < R; ++r) unpack_chunk<WT>(w[b][r], wf[r]);
 #pragma unroll
             for (int v = 0; v < NV; ++v) {
-                const float4 *xp = reinterpret_cast<const float4 *>(xs + size_t(v) * xs_stride + size_t(c) * E);
                 float xf[E];
+                if constexpr (IL) {
+                    // Lanes read consecutive float4s: no shared-memory bank conflicts.
+                    const float4 *xp = reinterpret_cast<const float4 *>(xs) + size_t(v) * (E / 4) * nchunks + c;
 #pragma unroll
-                for (int q = 0; q < E / 4; ++q) {
-                    const float4 t = xp[q];
-                    xf[4 * q] = t.x; xf[4 * q + 1] = t.y; xf[4 * q + 2] = t.z; xf[4 * q + 3] = t.w;
+                    for (int q = 0; q < E / 4; ++q) {
+                        const float4 t = xp[size_t(q) * nchunks];
+                        xf[4 * q] = t.x; xf[4 * q + 1] = t.y; xf[4 * q + 2] = t.z; xf[4 * q + 3] = t.w;
+                    }
+                } else {
+                    const float4 *xp = reinterpret_cast<const float4 *>(xs + size_t(v) * xs_stride + size_t(c) * E);
+#pragma unroll
+                    for (int q = 0; q < E / 4; ++q) {
+                        const float4 t = xp[q];
+                        xf[4 * q] = t.x; xf[4 * q + 1] = t.y; xf[4 * q + 2] = t.z; xf[4 * q + 3] = t.w;
+                    }
                 }
 #pragma unroll
                 for (int r = 0; r < R; ++r)
@@ -165,6 +176,48 @@ __device__ __forceinline__ void stage_vectors(const float *__restrict__ x, uint3
         const float inv = red[32 * NV + v];
         for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x)
             xs[v * cols + i] = xs[v * cols + i] * inv * __half2float(gain[i]);
+    }
+    __syncthreads();
+}
+
+// stage_vectors with a chunk-interleaved layout for dot_rows<..., IL = true>: element i
+// of vector v (chunk c = i / E of E elements per 16-byte weight chunk, quarter q = i % E / 4)
+// sits at float index ((v * E / 4 + q) * nchunks + c) * 4 + i % 4, so the lanes of a warp,
+// which work on consecutive chunks, read consecutive float4s. cols must be a multiple of E.
+// Same arithmetic as stage_vectors.
+template <int NV, int E>
+__device__ __forceinline__ void stage_vectors_il(const float *__restrict__ x, uint32_t x_stride,
+                                                 uint32_t cols, bool rmsnorm,
+                                                 const __half *__restrict__ gain, float eps,
+                                                 float *xs, float *red /* >= 33*NV floats */) {
+    const uint32_t nchunks = cols / E;
+    if (rmsnorm) {
+        const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u, nw = blockDim.x >> 5;
+        for (uint32_t v = 0; v < NV; ++v) {
+            float ss = 0.f;
+            for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) {
+                const float t = x[size_t(v) * x_stride + i];
+                ss = fmaf(t, t, ss);
+            }
+            ss = warp_sum(ss);
+            if (lane == 0) red[v * 32 + warp] = ss;
+        }
+        __syncthreads();
+        if (threadIdx.x < NV) {
+            float t = 0.f;
+            for (uint32_t w = 0; w < nw; ++w) t += red[threadIdx.x * 32 + w];
+            red[32 * NV + threadIdx.x] = float(1.0 / sqrt(double(t) / double(cols) + double(eps)));
+        }
+        __syncthreads();
+    }
+    for (uint32_t v = 0; v < NV; ++v) {
+        const float inv = rmsnorm ? red[32 * NV + v] : 1.f;
+        for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) {
+            float t = x[size_t(v) * x_stride + i];
+            if (rmsnorm) t = t * inv * __half2float(gain[i]);
+            const uint32_t c = i / E, q = (i % E) / 4;
+            xs[((size_t(v) * (E / 4) + q) * nchunks + c) * 4 + i % 4] = t;
+        }
     }
     __syncthreads();
 }

@@ -174,7 +174,14 @@ __global__ void __launch_bounds__(kThreads) gemv_allreduce_kernel(ArParams p, Pe
     grid_dependents_launch();
     uint8_t *const local = pv.peer[pv.rank];
     if (threadIdx.x == 0) s_seq = *reinterpret_cast<volatile uint32_t *>(ctl_at(local));
-    stage_vectors<NV>(p.x, p.x_stride, p.cols, PRO == OPURE_PRO_RMSNORM, p.gain, p.eps, xs, red);
+    // int8 chunks span 16 elements: their vectors are staged chunk-interleaved (no bank
+    // conflicts on the 64-byte-per-lane reads); fp16 keeps the plain layout, measured faster.
+    constexpr bool kIL = WT == OPURE_W_Q8;
+    if constexpr (kIL)
+        stage_vectors_il<NV, WTraits<WT>::kElems>(p.x, p.x_stride, p.cols, PRO == OPURE_PRO_RMSNORM, p.gain, p.eps,
+                                                  xs, red);
+    else
+        stage_vectors<NV>(p.x, p.x_stride, p.cols, PRO == OPURE_PRO_RMSNORM, p.gain, p.eps, xs, red);
     const uint32_t seq = s_seq, par = seq & 1u, want = seq + 1u;
 
     // This rank's partial rows, pushed into slot `rank` of every mailbox.
@@ -182,7 +189,7 @@ __global__ void __launch_bounds__(kThreads) gemv_allreduce_kernel(ArParams p, Pe
         const uint32_t row0 = g * kRows;
         const uint32_t valid = min(uint32_t(kRows), p.rows - row0);
         float acc[kRows][NV];
-        dot_rows<WT, NV, kRows>(p.w, p.pitch, row0, valid, p.nchunks, xs, p.cols, acc, pre, g == g0);
+        dot_rows<WT, NV, kRows, kIL>(p.w, p.pitch, row0, valid, p.nchunks, xs, p.cols, acc, pre, g == g0);
 #pragma unroll
         for (int r = 0; r < kRows; ++r)
 #pragma unroll
