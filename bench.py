@@ -808,8 +808,8 @@ def run_tp(args, world, rank, local):
     parallelism, one rank per GPU. Every step all-reduces the o_proj and down_proj partial
     sums of each layer (48 x 8 KB fp32 per token) and the vocabulary shards' argmax keys
     (8 B): as NCCL calls, or inside the producing kernels over NVLink peer memory
-    (opure_gemv_allreduce / opure_peer_argmax) with --tp-allreduce peer (auto: NCCL at 2
-    ranks, peer kernels from 4). 32-token prompt (seed 1) prefilled, then device-resident steps
+    (opure_gemv_allreduce / opure_peer_argmax) with --tp-allreduce peer (auto: the peer
+    kernels when every GPU pair maps each other's memory). 32-token prompt (seed 1) prefilled, then device-resident steps
     (graph replays, NCCL inside the graph) at positions 32..159 (cyclic). Device time, max
     over ranks. `comm_us` is one 2048-float all-reduce timed on its own (100-call average)."""
     import ctypes as C
@@ -1114,7 +1114,7 @@ def main():
     ap.add_argument("--attn-splits", type=lambda v: [int(x) for x in v.split(",")], default=[0],
                     help="attn: comma-separated keys per split to time (0: the library's choice)")
     ap.add_argument("--tp-allreduce", choices=["auto", "nccl", "peer"], default="auto",
-                    help="tp: NCCL or NVLink peer kernels (auto: NCCL at 2 ranks, peer kernels from 4)")
+                    help="tp: NCCL or NVLink peer kernels (auto: the peer kernels when every GPU pair maps)")
     ap.add_argument("--quick", action="store_true",
                     help="minimal run for profiler launch lists: no parity, e2e or CPU legs")
     args = ap.parse_args()

@@ -95,12 +95,13 @@ void VoxelEngine::Initialize(const std::string &modelDir, const EngineOptions &o
                ring);
     maxVec_ = std::max(opts.maxBatch, opts.prefillChunk);
     AllocBuffers();
-    // At 2 ranks NCCL's 8 KB all-reduce inside the step graph took 9.3 us against 19 us for
-    // the fused GEMV + peer exchange (B200, 1.7B shape), so auto keeps NCCL there; from 4
-    // ranks (NCCL: 26 us per all-reduce at 8) it takes the peer kernels.
+    // The fused GEMV + peer exchange (one kernel, tagged 8-byte words) took 9.0-9.1 us per
+    // o_proj-shaped call at 2 and 4 ranks against 9.3 / 14.9 us for NCCL's 8 KB all-reduce
+    // alone (B200, 1.7B shape; 535 vs 473 tok/s at TP-2, 616 vs 482 at TP-4), so auto takes
+    // the peer kernels at every rank count.
     uint32_t tpRanks = 1;
     if (comm) OPURE_CUDA_CHECK(opure_comm_info(comm, &tpRanks, nullptr));
-    const bool wantPeer = opts.tpAllreduce == 2 || (opts.tpAllreduce == 0 && tpRanks >= 4);
+    const bool wantPeer = opts.tpAllreduce == 2 || (opts.tpAllreduce == 0 && tpRanks >= 2);
     if (comm && wantPeer) {
         // NVLink peer mailboxes for the fused all-reduces; every rank falls back to NCCL
         // together when any pair of GPUs cannot map each other's memory.

@@ -52,7 +52,7 @@ struct EngineOptions {
                                     // of pageSize): a sequence keeps kvWindow / pageSize pages as a
                                     // ring, and a position attends to the last kvWindow / pageSize - 1
                                     // whole pages and its own
-    uint32_t tpAllreduce = 0;       // tensor parallel: 0 auto (peer kernels from 4 ranks), 1 NCCL, 2 peer
+    uint32_t tpAllreduce = 0;       // tensor parallel: 0 auto (peer kernels when mappable), 1 NCCL, 2 peer
 };
 
 struct GenerateResult {

@@ -218,7 +218,7 @@ class Engine:
         speculative pair must; it keeps a reference so the owner outlives it. With `comm`
         it is that communicator's tensor-parallel shard, on the communicator's ctx, whose
         all-reduces run as NCCL calls (`tp_allreduce` TP_NCCL, and TP_AUTO at 2 ranks) or
-        as NVLink peer kernels (TP_PEER, and TP_AUTO from 4 ranks, when every pair of GPUs
+        as NVLink peer kernels (TP_PEER, and TP_AUTO at any rank count, when every pair of GPUs
         can map each other's memory)."""
         o = EngineOptions(max_new_tokens, max_batch, max_len, page_size, page_seed,
                           int(use_graphs), attn_scale, path, int(phase_trace), prefill_chunk, kv_window,
