@@ -48,8 +48,8 @@ typedef struct opure_engine_options {
 } opure_engine_options;
 
 enum {
-    OPURE_TP_AUTO = 0,        /* the peer kernels (measured faster than NCCL at 2 and 4
-                                 ranks) when every pair of GPUs maps each other's memory,
+    OPURE_TP_AUTO = 0,        /* the peer kernels (measured faster than NCCL at 2, 4 and
+                                 8 ranks) when every pair of GPUs maps each other's memory,
                                  else NCCL                                                 */
     OPURE_TP_NCCL = 1,        /* NCCL all-reduces between the per-op kernels             */
     OPURE_TP_PEER = 2         /* opure_gemv_allreduce / opure_peer_argmax over NVLink peer

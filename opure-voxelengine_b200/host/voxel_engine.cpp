@@ -95,10 +95,10 @@ void VoxelEngine::Initialize(const std::string &modelDir, const EngineOptions &o
                ring);
     maxVec_ = std::max(opts.maxBatch, opts.prefillChunk);
     AllocBuffers();
-    // The fused GEMV + peer exchange (one kernel, tagged 8-byte words) took 9.0-9.1 us per
-    // o_proj-shaped call at 2 and 4 ranks against 9.3 / 14.9 us for NCCL's 8 KB all-reduce
-    // alone (B200, 1.7B shape; 535 vs 473 tok/s at TP-2, 616 vs 482 at TP-4), so auto takes
-    // the peer kernels at every rank count.
+    // The fused GEMV + peer exchange (one kernel, tagged 8-byte words) took 8.5-9.4 us per
+    // o_proj-shaped call at 2, 4 and 8 ranks against 9.3 / 14.9 / 24.9 us for NCCL's 8 KB
+    // all-reduce alone (B200, 1.7B shape; 535 vs 473 tok/s at TP-2, 616 vs 482 at TP-4, 664
+    // vs 421 at TP-8), so auto takes the peer kernels at every rank count.
     uint32_t tpRanks = 1;
     if (comm) OPURE_CUDA_CHECK(opure_comm_info(comm, &tpRanks, nullptr));
     const bool wantPeer = opts.tpAllreduce == 2 || (opts.tpAllreduce == 0 && tpRanks >= 2);
