@@ -489,7 +489,9 @@ def run_ours(args, world, rank, local):
     # Parity gate on this rank's first sequence: the engine's 128 config-0 tokens.
     # (--quick, for profiler launch lists, generates one token: the launches before the
     # timed region are then (PROMPT_LEN + 1 + warmup) * launches_per_step.)
-    gen, _ = eng.generate(prompts, 1 if args.quick else DECODE_STEPS)
+    # Quick runs generate only as far as their steps reach (each step needs its KV page
+    # reserved by the generate before).
+    gen, _ = eng.generate(prompts, min(DECODE_STEPS, args.steps + args.warmup + 2) if args.quick else DECODE_STEPS)
     parity = {"tokens_checked": 0}
 
     dev_ms, clocks = device_steps(eng, B, args.steps, args.warmup, world, not args.quick, local)
@@ -556,7 +558,8 @@ def run_ours(args, world, rank, local):
         "clocks": clocks,
         **({"clocks_per_rank": clocks_per_rank} if world > 1 else {}),
         "parity": parity,
-        "launches_before_timed": (PROMPT_LEN + (1 if args.quick else DECODE_STEPS) + args.warmup)
+        "launches_before_timed": (PROMPT_LEN + (min(DECODE_STEPS, args.steps + args.warmup + 2) if args.quick
+                                                else DECODE_STEPS) + args.warmup)
         * line_launches,
     }
     if cpu:

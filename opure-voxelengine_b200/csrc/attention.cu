@@ -10,8 +10,9 @@
 // lane groups (shuffles), warps (shared memory) and finally across key splits: each CTA
 // writes its partial (m, l, acc) to caller-provided scratch and the last CTA of an
 // (entry, kv head) to finish -- found with an atomic ticket, no waiting -- merges them
-// and writes the output.
+// and writes the output. With a single split the CTA writes its output directly.
 #include <algorithm>
+#include <type_traits>
 
 #include "attn_core.cuh"
 #include "ctx.cuh"
@@ -37,17 +38,25 @@ struct AttnParams {
     uint32_t *counters;      // [entries * n_kv]
     opure_kv_layout kv;
     DeviceStatus *st;
-    __half *out_packed;      // null, or [2][pk_npad][n_heads * HD] (store_packed)
-    uint32_t pk_npad;
 };
 
-// Output element i (= head * HD + dim) of an entry: fp32, and with out_packed also the
-// scale-free fp16 pair of the next GEMV's packed operand.
-template <int HD>
-__device__ __forceinline__ void store_out(const AttnParams &p, uint32_t entry, uint32_t i, float v) {
+// The TMA-staged kernel's parameters when it also writes the next GEMV's packed operand. A
+// separate type: two more fields in AttnParams itself made the kernel ~10% slower on long
+// contexts even with them unused (measured, B=64 x 8192 and 32768 tokens).
+struct AttnPackedParams : AttnParams {
+    __half *out_packed;      // [2][pk_npad][n_heads * HD] (store_packed)
+    uint32_t pk_npad;
+};
+template <bool PK>
+using AttnP = std::conditional_t<PK, AttnPackedParams, AttnParams>;
+
+// Output element i (= head * HD + dim) of an entry: fp32, and with PK also the scale-free
+// fp16 pair of the next GEMV's packed operand.
+template <int HD, bool PK>
+__device__ __forceinline__ void store_out(const AttnP<PK> &p, uint32_t entry, uint32_t i, float v) {
     const uint32_t len = p.n_heads * HD;
     p.out[size_t(entry) * len + i] = v;
-    if (p.out_packed) store_packed(p.out_packed, p.pk_npad, len, entry, i, v, p.st, 15);
+    if constexpr (PK) store_packed(p.out_packed, p.pk_npad, len, entry, i, v, p.st, 15);
 }
 
 template <int HD, int G>
@@ -87,6 +96,17 @@ __global__ void __launch_bounds__(kWarps * 32) attn_kernel(AttnParams p) {
 
     // CTA partial -> scratch; one thread per (head, dim) plus the (m, l) pair.
     const uint32_t n_splits = p.n_splits;
+    if (n_splits == 1) {
+        // One split: the CTA's merged state is the result (the split merge below would
+        // multiply it by exp2(0) = 1), so no partials, no ticket.
+        for (uint32_t idx = threadIdx.x; idx < uint32_t(G) * HD; idx += blockDim.x) {
+            const uint32_t h = idx / HD, d = idx % HD;
+            float a, mn, ls;
+            merge_warps<HD, G, kWarps>(ws, h, d, a, mn, ls);
+            p.out[(size_t(entry) * p.n_heads + g * G + h) * HD + d] = a / fmaxf(ls, 1e-30f);
+        }
+        return;
+    }
     float *part = p.partials + (size_t(eg) * n_splits + split) * G * (HD + 2);
     for (uint32_t idx = threadIdx.x; idx < uint32_t(G) * HD; idx += blockDim.x) {
         const uint32_t h = idx / HD, d = idx % HD;
@@ -123,9 +143,8 @@ __global__ void __launch_bounds__(kWarps * 32) attn_kernel(AttnParams p) {
         }
         // acc / max(sum, 1e-30) as the reference's epilogue
         // (Opure_FlashAttention_Decode.usf:235-239).
-        store_out<HD>(p, entry, (g * G + h) * HD + d, a / fmaxf(lsum, 1e-30f));
+        p.out[(size_t(entry) * p.n_heads + g * G + h) * HD + d] = a / fmaxf(lsum, 1e-30f);
     }
-    if (p.out_packed) asm volatile("fence.proxy.async.global;" ::: "memory");  // read by TMA next
     if (threadIdx.x == 0) p.counters[eg] = 0u;  // ready for the next call
 }
 
@@ -237,8 +256,8 @@ __device__ __forceinline__ void consume_page(AttnState<HD, G> &st, const float (
     }
 }
 
-template <int HD, int G>
-__global__ void __launch_bounds__((kWarps + 1) * 32) attn_tma_kernel(AttnParams p) {
+template <int HD, int G, bool PK>
+__global__ void __launch_bounds__((kWarps + 1) * 32) attn_tma_kernel(AttnP<PK> p) {
     using S = AttnShape<HD>;
     constexpr int TPW = S::TPW, E = S::E;
     constexpr int R = 4;  // rounds per consumer block
@@ -363,6 +382,18 @@ __global__ void __launch_bounds__((kWarps + 1) * 32) attn_tma_kernel(AttnParams 
     __syncthreads();
 
     const uint32_t n_splits = p.n_splits;
+    if (n_splits == 1) {
+        // One split: the CTA's merged state is the result (the split merge below would
+        // multiply it by exp2(0) = 1), so no partials, no ticket.
+        for (uint32_t idx = threadIdx.x; idx < uint32_t(G) * HD; idx += blockDim.x) {
+            const uint32_t h = idx / HD, d = idx % HD;
+            float a, mn, ls;
+            merge_warps<HD, G, kWarps>(ws, h, d, a, mn, ls);
+            store_out<HD, PK>(p, entry, (g * G + h) * HD + d, a / fmaxf(ls, 1e-30f));
+        }
+        if constexpr (PK) asm volatile("fence.proxy.async.global;" ::: "memory");  // read by TMA next
+        return;
+    }
     float *part = p.partials + (size_t(eg) * n_splits + split) * G * (HD + 2);
     for (uint32_t idx = threadIdx.x; idx < uint32_t(G) * HD; idx += blockDim.x) {
         const uint32_t h = idx / HD, d = idx % HD;
@@ -398,9 +429,9 @@ __global__ void __launch_bounds__((kWarps + 1) * 32) attn_tma_kernel(AttnParams 
             a += __ldcg(pp + d) * f;
             lsum += __ldcg(pp + HD + 1) * f;
         }
-        store_out<HD>(p, entry, (g * G + h) * HD + d, a / fmaxf(lsum, 1e-30f));
+        store_out<HD, PK>(p, entry, (g * G + h) * HD + d, a / fmaxf(lsum, 1e-30f));
     }
-    if (p.out_packed) asm volatile("fence.proxy.async.global;" ::: "memory");  // read by TMA next
+    if constexpr (PK) asm volatile("fence.proxy.async.global;" ::: "memory");  // read by TMA next
     if (threadIdx.x == 0) p.counters[eg] = 0u;
 }
 
@@ -417,13 +448,13 @@ AttnKernel pick_g(uint32_t G) {
     return nullptr;
 }
 
-template <int HD>
-AttnKernel pick_tma_g(uint32_t G) {
+template <int HD, bool PK>
+void (*pick_tma_g(uint32_t G))(AttnP<PK>) {
     switch (G) {
-        case 1: return attn_tma_kernel<HD, 1>;
-        case 2: return attn_tma_kernel<HD, 2>;
-        case 3: return attn_tma_kernel<HD, 3>;
-        case 4: return attn_tma_kernel<HD, 4>;
+        case 1: return attn_tma_kernel<HD, 1, PK>;
+        case 2: return attn_tma_kernel<HD, 2, PK>;
+        case 3: return attn_tma_kernel<HD, 3, PK>;
+        case 4: return attn_tma_kernel<HD, 4, PK>;
     }
     return nullptr;
 }
@@ -496,20 +527,29 @@ uint32_t choose_split(uint32_t entries, uint32_t n_kv, uint32_t hd, uint32_t max
 }
 
 opure_status launch_attention(opure_ctx *ctx, const AttnParams &p, uint32_t hd, uint32_t G, uint32_t pairs,
-                              uint32_t n_splits) {
+                              uint32_t n_splits, __half *out_packed = nullptr, uint32_t pk_npad = 0) {
     if (tma_path(hd)) {
-        AttnKernel k = hd == 64 ? pick_tma_g<64>(G) : pick_tma_g<128>(G);
-        if (!k) return OPURE_ERR_UNSUPPORTED;
         const uint32_t page_bytes = p.kv.page_size * hd * 2;
         const size_t smem = size_t(stage_count(2 * page_bytes)) * 2 * page_bytes;
         // Always: the dynamic stages plus the kernel's static shared memory may pass the
         // default 48 KB per-block limit even when the stages alone do not.
-        const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-        if (e != cudaSuccess) return cuda_status(e);
-        return launch(ctx, k, dim3(pairs, n_splits), dim3((kWarps + 1) * 32), smem, true, p);
+        auto go = [&](auto k, const auto &params) -> opure_status {
+            if (!k) return OPURE_ERR_UNSUPPORTED;
+            const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+            if (e != cudaSuccess) return cuda_status(e);
+            return launch(ctx, k, dim3(pairs, n_splits), dim3((kWarps + 1) * 32), smem, true, params);
+        };
+        if (out_packed) {
+            AttnPackedParams pp;
+            static_cast<AttnParams &>(pp) = p;
+            pp.out_packed = out_packed;
+            pp.pk_npad = pk_npad;
+            return go(hd == 64 ? pick_tma_g<64, true>(G) : pick_tma_g<128, true>(G), pp);
+        }
+        return go(hd == 64 ? pick_tma_g<64, false>(G) : pick_tma_g<128, false>(G), p);
     }
     AttnKernel k = pick(hd, G);
-    if (!k) return OPURE_ERR_UNSUPPORTED;
+    if (!k || out_packed) return OPURE_ERR_UNSUPPORTED;  // packed output: head_dim 64 / 128 only
     return launch(ctx, k, dim3(pairs, n_splits), dim3(kWarps * 32), 0, true, p);
 }
 
@@ -576,9 +616,8 @@ extern "C" opure_status opure_attention(opure_ctx *ctx, const opure_attn_args *a
     p.counters = reinterpret_cast<uint32_t *>(static_cast<char *>(a->scratch) + counters_off);
     p.kv = kv;
     p.st = ctx->status;
-    p.out_packed = reinterpret_cast<__half *>(a->out_packed);
-    p.pk_npad = (entries + 15) & ~15u;
-    return launch_attention(ctx, p, kv.head_dim, G, entries * kv.n_kv, n_splits);
+    return launch_attention(ctx, p, kv.head_dim, G, entries * kv.n_kv, n_splits,
+                            reinterpret_cast<__half *>(a->out_packed), (entries + 15) & ~15u);
 }
 
 // ---- Allocation-free variant (opure_attention_static) ---------------------------------

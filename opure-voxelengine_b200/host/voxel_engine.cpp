@@ -134,6 +134,7 @@ bool VoxelEngine::Chained(uint32_t n) const {
     const graph::VramPlan &p = graph_.Plan();
     const uint32_t att = c.numHeads * c.HeadDim();
     return !comm_ && p.wDtype == OPURE_W_F16 && !p.lmQuantized && n >= 16 && n <= 256 && n <= maxVec_ &&
+           (c.HeadDim() == 64 || c.HeadDim() == 128) &&  // the attention kernel with packed output
            c.hiddenSize % 64 == 0 && c.intermediateSize % 64 == 0 && att % 64 == 0 && c.hiddenSize <= 16384 &&
            c.intermediateSize <= 16384 && att <= 16384 && buf_.packRes != nullptr;
 }
