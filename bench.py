@@ -49,17 +49,19 @@ FALLBACK_PEAK = 6650.0  # GB/s, used only when MEASURED_PEAKS.json is absent
 #     --clock-control none -k regex:persistent_step -s 33 -c 2
 #     python bench.py --quick --no-cpu --steps 2 --warmup 3 --bs64-steps 0 --int8 0
 # -> 269.92 MB read + 1.0-3.5 MB written per launch.
-# Batch 64, the per-layer kernels over two layers at positions 32-33, times 30 layers, plus the
-# lm_head GEMM and the step's begin/end kernels:
+# Batch 64 (chained operands: six kernels per layer), layers 0 and 1 of one step, with layer
+# 1's kernels taken for every layer, plus layer 0's pack kernel and the lm_head GEMM:
 #   ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum
 #     --clock-control none -k "regex:gemm_tc_kernel|pack_kernel|attn_tma_kernel|rope_kv_kernel"
-#     -s 10872 -c 20 python bench.py --quick --no-cpu --batch 64 --steps 2 --warmup 3
+#     -s 6552 -c 13 python bench.py --quick --no-cpu --batch 64 --steps 2 --warmup 3
 #     --bs64-steps 0 --int8 0
-# -> 11.80 MB per layer, 411.1 MB per step. ncu flushes the caches before every captured
-# launch, so at batch 64 each kernel's activation inputs count as DRAM reads too (an upper
-# bound; at batch 1 the step is one launch). Both captures ran at a mean context of about 37
-# positions; step_traffic() moves the K/V share to the timed steps' mean context.
-NCU_STEP_TRAFFIC = {1: 272.2e6, 64: 411.1e6}
+# -> 11.03 MB per layer, 331.0 MB for 30 layers + 0.16 MB pack + 56.8 MB lm_head (the lm_head
+# GEMM's figure, its 56.6 MB of weights, from the capture of the build before the chained
+# operands) = 388.0 MB per step. ncu flushes the caches before every captured launch, so at
+# batch 64 each kernel's activation inputs count as DRAM reads too (an upper bound; at batch
+# 1 the step is one launch). Both captures ran at a mean context of about 37 positions;
+# step_traffic() moves the K/V share to the timed steps' mean context.
+NCU_STEP_TRAFFIC = {1: 272.2e6, 64: 388.0e6}
 NCU_CAPTURE_CTX = 37.0
 
 
@@ -590,12 +592,16 @@ def launches_per_step(info, B: int, path: str = "auto") -> int:
     layers) or 3 per layer + lm_head (path layers);
     per-op path: per layer the q;k;v, o, gate;up and down GEMVs (+ RoPE/KV append and
     attention), each GEMV one launch per 9-vector pass on the CUDA cores (int8 q;k;v as 3
-    GEMVs) or pack + tcgen05 GEMM per 256-vector pass from 16 vectors up, + the lm_head GEMV."""
+    GEMVs) or pack + tcgen05 GEMM per 256-vector pass from 16 vectors up, + the lm_head GEMV;
+    with chained operands (fp16, 16..256 vectors, head_dim 64 or 128) one tcgen05 GEMM per
+    projection and a single pack kernel (layer 0's q;k;v input)."""
     from voxelengine import cuda as cu
     if info.w_dtype == cu.W_F16 and B in (1, 2, 4, 8) and path != "unfused":
         if path == "auto" and info.head_dim == 64 and info.layers <= 48:
             return 3
         return 2 + 3 * info.layers + 1
+    if info.w_dtype == cu.W_F16 and 16 <= B <= 256 and info.head_dim in (64, 128):
+        return 2 + 1 + info.layers * 6 + 1
     if info.w_dtype == cu.W_F16 and B >= 16:
         gemv = 2 * -(-B // 256)
     else:
