@@ -34,13 +34,15 @@ void VoxelEngine::Shutdown() {
     kv_.Destroy();
     for (void *p : {static_cast<void *>(buf_.x), static_cast<void *>(buf_.qkv), static_cast<void *>(buf_.q),
                     static_cast<void *>(buf_.attn), static_cast<void *>(buf_.h), static_cast<void *>(buf_.logits),
-                    static_cast<void *>(buf_.keys), static_cast<void *>(buf_.seq), static_cast<void *>(buf_.pos),
+                    static_cast<void *>(buf_.keys), static_cast<void *>(buf_.seq),
                     static_cast<void *>(buf_.seqLen), static_cast<void *>(buf_.known), static_cast<void *>(buf_.flags),
                     static_cast<void *>(buf_.inTokens), static_cast<void *>(buf_.tokens),
                     static_cast<void *>(buf_.base1), static_cast<void *>(buf_.delta0),
                     static_cast<void *>(buf_.delta1), static_cast<void *>(buf_.partial),
                     static_cast<void *>(buf_.sync), static_cast<void *>(buf_.trace),
-                    static_cast<void *>(buf_.prefillKeys), weights_})
+                    static_cast<void *>(buf_.prefillKeys), static_cast<void *>(buf_.packAttn),
+                    static_cast<void *>(buf_.packRes), static_cast<void *>(buf_.packAct),
+                    static_cast<void *>(buf_.sumsq), weights_})
         if (p) opure_free(ctx_, p);
     for (auto &s : attnScratch_) opure_free(ctx_, s.second.first);
     attnScratch_.clear();
@@ -150,11 +152,13 @@ void VoxelEngine::AllocBuffers() {
     buf_.logits = Alloc<float>(ctx_, size_t(B) * c.vocabSize);
     buf_.keys = Alloc<unsigned long long>(ctx_, B);
     buf_.seq = Alloc<int32_t>(ctx_, B);
-    buf_.pos = Alloc<int32_t>(ctx_, B);
     buf_.seqLen = Alloc<int32_t>(ctx_, B);
     buf_.known = Alloc<int32_t>(ctx_, B);
     buf_.flags = Alloc<uint32_t>(ctx_, B);
-    buf_.inTokens = Alloc<int32_t>(ctx_, B);
+    // Host-given tokens and positions side by side, as in the pinned staging buffer, so the
+    // host-driven step copies both with one H2D (buf_.pos is not a separate allocation).
+    buf_.inTokens = Alloc<int32_t>(ctx_, 2 * size_t(B));
+    buf_.pos = buf_.inTokens + B;
     buf_.tokens = Alloc<int32_t>(ctx_, size_t(opts_.maxBatch) * maxLen_);
     buf_.prefillKeys = Alloc<unsigned long long>(ctx_, opts_.maxBatch);
     buf_.base1 = Alloc<float>(ctx_, size_t(B) * c.hiddenSize);
@@ -189,7 +193,8 @@ void VoxelEngine::AllocBuffers() {
     OPURE_CUDA_CHECK(opure_fill(ctx_, buf_.flags, 0, sizeof(uint32_t) * B));
     OPURE_CUDA_CHECK(opure_fill(ctx_, buf_.known, 0, sizeof(int32_t) * B));
     OPURE_CUDA_CHECK(opure_fill(ctx_, buf_.tokens, 0, sizeof(int32_t) * size_t(opts_.maxBatch) * maxLen_));
-    // Pinned staging for the host-driven step: [in_tokens B][positions B][keys B (u64)].
+    // Pinned staging for the host-driven step: [in_tokens B][positions B][keys B (u64)], B =
+    // token vectors per step (the device's inTokens / pos layout).
     OPURE_CUDA_CHECK(opure_alloc_host(ctx_, size_t(B) * 16, &hostIo_));
     OPURE_CUDA_CHECK(opure_sync(ctx_, 60000));
 }
@@ -854,7 +859,7 @@ void VoxelEngine::DecodeStepBatch(const int32_t *tokens, const int32_t *position
                     "token id out of vocabulary range");
         OPURE_CHECK(kv_.Reserve(v, uint32_t(positions[v]) + 1), "KV cache has no room for the sequence");
         io[v] = tokens[v];
-        io[opts_.maxBatch + v] = positions[v];
+        io[maxVec_ + v] = positions[v];
     }
     kv_.SyncTable();
     if (!seqIdentity_) {
@@ -870,12 +875,12 @@ void VoxelEngine::DecodeStepBatch(const int32_t *tokens, const int32_t *position
         OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.flags, zero.data(), zero.size() * 4));
         hostDriven_ = true;
     }
-    // One H2D each for tokens and positions (pinned), one step, one 8-byte-per-sequence
+    // One H2D of tokens and positions (pinned; the tokens of vectors n.. are unused by this
+    // step and rewritten before any step reads them), one step, one 8-byte-per-sequence
     // readback: the reference's DecodeStep round trip (Opure_VoxelEngine.cpp:765-800).
-    OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.inTokens, io, n * 4));
-    OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.pos, io + opts_.maxBatch, n * 4));
+    OPURE_CUDA_CHECK(opure_h2d(ctx_, buf_.inTokens, io, (size_t(maxVec_) + n) * 4));
     RunSteps(n, 1, false);
-    auto *keys = reinterpret_cast<unsigned long long *>(io + 2 * opts_.maxBatch);
+    auto *keys = reinterpret_cast<unsigned long long *>(io + 2 * size_t(maxVec_));
     OPURE_CUDA_CHECK(opure_d2h(ctx_, keys, buf_.keys, n * 8));
     OPURE_CUDA_CHECK(opure_sync(ctx_, 600000));
     for (uint32_t v = 0; v < n; ++v) next[v] = int32_t(0xffffffffu - uint32_t(keys[v] & 0xffffffffull));
