@@ -277,6 +277,62 @@ __device__ __forceinline__ void smem_dot(const uint8_t *w, uint32_t pitch, uint3
     smem_dot_ptrs<NV, R, Q8>(rows, nrows, nchunks, xs, h, acc);
 }
 
+// Eight fp16 rows (row r at w + r * pitch; rows >= nrows, 1 <= nrows, are not read) with
+// one vector xs, for the lm_head. The loads carry no per-row branch (a missing row reads
+// row nrows - 1 again) and the eight sums are reduced together: every level of the xor
+// butterfly halves the rows a lane keeps, so 4 + 2 + 1 + 1 + 1 shuffles replace 8 x 5.
+// Lane l returns the sum of row (l >> 2) & 7. Each level adds the same pairs of partial
+// sums as warp_sum, so every row's sum is bit-identical to smem_dot's.
+__device__ __forceinline__ float lm_dot8(const uint8_t *w, uint32_t pitch, uint32_t nrows, uint32_t nchunks,
+                                         const float *xs) {
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint8_t *rows[8];
+    float acc[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+        rows[r] = w + size_t(min(uint32_t(r), nrows - 1)) * pitch;
+        acc[r] = 0.f;
+    }
+    auto pass = [&](uint32_t c) {
+        uint4 raw[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) raw[r] = lds128(rows[r] + c * 16);
+        const float4 x0 = lds_f4(xs + c * 8), x1 = lds_f4(xs + c * 8 + 4);
+        const float xf[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+            float wf[8];
+            unpack8(raw[r], wf);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[r] = fmaf(wf[e], xf[e], acc[r]);
+        }
+    };
+    if (nchunks <= 96) {
+#pragma unroll
+        for (int i = 0; i < 3; ++i)
+            if (lane + 32u * i < nchunks) pass(lane + 32u * i);
+    } else {
+        for (uint32_t c = lane; c < nchunks; c += 32) pass(c);
+    }
+    // xor 16: keep rows 4 b4 + (0..3); xor 8: rows + 2 b3; xor 4: row + b2; then xor 2, 1.
+    const bool b4 = lane & 16u, b3 = lane & 8u, b2 = lane & 4u;
+    float u[4], t[2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float send = b4 ? acc[i] : acc[i + 4];
+        u[i] = (b4 ? acc[i + 4] : acc[i]) + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const float send = b3 ? u[i] : u[i + 2];
+        t[i] = (b3 ? u[i + 2] : u[i]) + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+    float x = (b2 ? t[1] : t[0]) + __shfl_xor_sync(0xffffffffu, b2 ? t[0] : t[1], 4);
+    x += __shfl_xor_sync(0xffffffffu, x, 2);
+    x += __shfl_xor_sync(0xffffffffu, x, 1);
+    return x;
+}
+
 // Element offset of (seq, pos, K|V, kv head) row inside a layer's pool, or -1 (reported).
 __device__ __forceinline__ long long kv_offset(const KvParams &kv, uint32_t n_kv, uint32_t hd, int32_t seq,
                                                int32_t pos, uint32_t sel, uint32_t head, DeviceStatus *st) {
@@ -1396,25 +1452,44 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_step_kernel(const __g
                 if (!p_wait_slot(&lbar[j], lm_dn.k & 1u, p, &s_ok)) goto abort;
                 const uint32_t r0 = lm_r0 + c * p.lm_chunk, nr = min(p.lm_chunk, lm_r1 - r0);
                 const uint8_t *buf = psm + size_t(j) * lm_cbytes;
-                for (uint32_t rr = RW * warp; rr < nr; rr += RW * kPWarps) {
-                    float acc[RW][NV];
-                    smem_dot<NV, RW>(buf + size_t(rr) * pitch, pitch, min(RW, nr - rr), pitch / 16, xs, p.h, acc);
-#pragma unroll
-                    for (int r = 0; r < int(RW); ++r)
-#pragma unroll
-                        for (int v = 0; v < NV; ++v) {
-                            if (rr + r >= nr) continue;
-                            const unsigned long long k = argmax_key(acc[r][v], r0 + rr + r);
-                            best[v] = k > best[v] ? k : best[v];
-                            if (p.logits && lane == uint32_t((r * NV + v) & 31))
-                                p.logits[size_t(v) * p.vocab + r0 + rr + r] = acc[r][v];
+                if constexpr (NV == 1) {
+                    static_assert(RW == 8, "lm_dot8 takes eight rows per warp");
+                    const uint32_t row = (lane >> 2) & 7u;
+                    for (uint32_t rr = RW * warp; rr < nr; rr += RW * kPWarps) {
+                        const float sum = lm_dot8(buf + size_t(rr) * pitch, pitch, min(RW, nr - rr), pitch / 16, xs);
+                        if (rr + row < nr) {
+                            const unsigned long long k = argmax_key(sum, r0 + rr + row);
+                            best[0] = k > best[0] ? k : best[0];
+                            if (p.logits && (lane & 3u) == 0) p.logits[r0 + rr + row] = sum;
                         }
+                    }
+                } else {
+                    for (uint32_t rr = RW * warp; rr < nr; rr += RW * kPWarps) {
+                        float acc[RW][NV];
+                        smem_dot<NV, RW>(buf + size_t(rr) * pitch, pitch, min(RW, nr - rr), pitch / 16, xs, p.h, acc);
+#pragma unroll
+                        for (int r = 0; r < int(RW); ++r)
+#pragma unroll
+                            for (int v = 0; v < NV; ++v) {
+                                if (rr + r >= nr) continue;
+                                const unsigned long long k = argmax_key(acc[r][v], r0 + rr + r);
+                                best[v] = k > best[v] ? k : best[v];
+                                if (p.logits && lane == uint32_t((r * NV + v) & 31))
+                                    p.logits[size_t(v) * p.vocab + r0 + rr + r] = acc[r][v];
+                            }
+                    }
                 }
                 __syncthreads();  // buffer j read by every warp: refill it
             }
             lm_dn.next(p.lm_nbuf);
             lm_fill(2);
         }
+        if constexpr (NV == 1)  // lm_dot8 leaves each lane the keys of its own rows
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long k = __shfl_xor_sync(0xffffffffu, best[0], o);
+                best[0] = k > best[0] ? k : best[0];
+            }
         if (lane == 0)
 #pragma unroll
             for (int v = 0; v < NV; ++v) cta_best[warp][v] = best[v];
